@@ -1,0 +1,162 @@
+/*
+ * rec_b200 — C ABI of the B200 decode hot path of rec (single-session,
+ * batch-1 decode of the Flint-style MoE transformer).
+ *
+ * Conventions
+ *   - Every pointer named *_dev is device memory owned by the caller (torch);
+ *     the library keeps non-owning views and allocates no device memory.
+ *   - Every call is stream-ordered and non-blocking unless stated otherwise;
+ *     `stream` is a cudaStream_t passed as void*.
+ *   - Return codes: 0 ok; < 0 argument error (the Python shim raises
+ *     ValueError); > 0 device status (a bounded device wait ran out or the
+ *     device rejected an input; the shim raises RuntimeError and marks the
+ *     session unusable).  Details: rec_last_error().
+ *   - bf16 / fp16 tensors are passed as uint16_t storage.
+ *
+ * Reference interfaces replaced (paths inside recursive-oss/rec):
+ *   engine/src/rec_mlx/kernels/megakernel.py:983-1337  FullModel (forward,
+ *       prefill_state, ensure_capacity), the `flint_decode` Metal kernel
+ *   engine/src/rec_mlx/kernels/sampling.py:17-169       ResidentSampler.block
+ *   engine/src/rec_mlx/kernels/masked_sampling.py:7-212 filtered sampling
+ *   engine/src/rec_mlx/kernels/resident_block.py:12-88   grid argmax packet
+ *   engine/src/rec_mlx/cache.py:6-46                     KV write kernels
+ *   engine/src/rec_mlx/model.py:40-139,216-254           native MLX ops
+ */
+#ifndef REC_B200_H
+#define REC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+#define REC_EXTERN extern "C"
+#else
+#define REC_EXTERN
+#endif
+#define REC_API REC_EXTERN __attribute__((visibility("default")))
+
+enum {
+  REC_OK = 0,
+  REC_EINVAL = -1,      /* bad argument / unsupported shape */
+  REC_ECUDA = -2,       /* CUDA runtime error at launch */
+  REC_ESTATE = -3,      /* session unusable or not configured */
+  REC_ELIMIT = -4,      /* context limit exhausted */
+  REC_DEV_BULK_TIMEOUT = 1,
+  REC_DEV_COUNTER_TIMEOUT = 2,
+  REC_DEV_BAD_TOKEN = 3,
+  REC_DEV_BAD_POSITION = 4,
+};
+
+/* Scale/bias storage type of quantized weights. */
+enum { REC_SCALE_FP16 = 0, REC_SCALE_BF16 = 1 };
+/* Router modes: softmax -> top-k -> renormalise; sigmoid + bias selection
+ * (reference model.py:245-254). */
+enum { REC_ROUTER_SOFTMAX = 0, REC_ROUTER_SIGMOID = 1 };
+/* Model flags. */
+enum { REC_FLAG_SINKS = 1, REC_FLAG_QK_NORM = 2 };
+
+/* Model shape (reference ModelArgs, engine/src/rec_mlx/model.py:14-37). */
+typedef struct RecModelDesc {
+  int32_t hidden;      /* H, multiple of 2048 */
+  int32_t n_layers;
+  int32_t n_q_heads;   /* 32 */
+  int32_t n_kv_heads;  /* 4 */
+  int32_t head_dim;    /* 128 */
+  int32_t n_experts;   /* E */
+  int32_t top_k;       /* k <= 8 */
+  int32_t moe_inter;   /* I: 256*n (n<=4) or a multiple of 2048 */
+  int32_t vocab;       /* V */
+  int32_t group_size;  /* 64 */
+  int32_t scale_dtype; /* REC_SCALE_* of the int4 weights */
+  int32_t kv_bits;     /* 4 or 8 (KV scales/biases are bf16) */
+  int32_t router_mode; /* REC_ROUTER_* */
+  int32_t flags;       /* REC_FLAG_* */
+  float rms_eps;
+  float rope_theta;
+} RecModelDesc;
+
+/* int4 g64 affine matrix in MLX layout: codes uint32[N, K/8], scales and
+ * biases [N, K/64] (reference megakernel.py:161-170). */
+typedef struct RecQMat {
+  const void* w;
+  const void* scales;
+  const void* biases;
+} RecQMat;
+
+typedef struct RecLayerWeights {
+  const void* input_norm; /* bf16 [H] */
+  const void* post_norm;  /* bf16 [H] */
+  RecQMat q, k, v, o;     /* [Hq*D, H], [Hkv*D, H] x2, [H, Hq*D] */
+  const void* router;     /* bf16 [E, H] */
+  const void* expert_bias;/* fp32 [E] (sigmoid router) or NULL */
+  RecQMat gate, up, down; /* [E*I, H], [E*I, H], [E*H, I] */
+  const void* sinks;      /* bf16 [Hq] or NULL */
+  const void* q_norm;     /* bf16 [D] or NULL */
+  const void* k_norm;     /* bf16 [D] or NULL */
+} RecLayerWeights;
+
+typedef struct RecGlobalWeights {
+  RecQMat embed;          /* int4 [V, H] */
+  const void* final_norm; /* bf16 [H] */
+  RecQMat lm_head;        /* int4 [V, H] */
+} RecGlobalWeights;
+
+/* One layer of quantized KV cache (reference MixedQuantizedKVCache,
+ * model.py:40-82): codes uint32[Hkv, C, D*bits/32], scales/biases bf16
+ * [Hkv, C, D/64]. */
+typedef struct RecKVLayer {
+  void* k_codes;
+  void* k_scales;
+  void* k_biases;
+  void* v_codes;
+  void* v_scales;
+  void* v_biases;
+} RecKVLayer;
+
+/* Sampling parameters of the sampling head. */
+typedef struct RecSampling {
+  float temperature;        /* 0 = greedy */
+  int32_t top_k;            /* 0 = off */
+  float top_p;              /* 1 = off */
+  float repetition_penalty; /* 1 = off */
+} RecSampling;
+
+typedef struct RecCtx RecCtx;
+
+/* ---- session ----------------------------------------------------------- */
+REC_API int rec_create(const RecModelDesc* desc, RecCtx** out);
+REC_API void rec_destroy(RecCtx* ctx);
+REC_API int rec_set_weights(RecCtx* ctx, const RecLayerWeights* layers, int32_t n_layers,
+                            const RecGlobalWeights* global);
+/* capacity: KV slots per layer (multiple of 256). */
+REC_API int rec_set_kv(RecCtx* ctx, const RecKVLayer* layers, int32_t n_layers, int32_t capacity);
+REC_API size_t rec_workspace_bytes(const RecCtx* ctx);
+REC_API int rec_set_workspace(RecCtx* ctx, void* workspace_dev, size_t bytes);
+/* One decode step: embeds `token` at `position`, runs every layer, writes
+ * bf16 logits[V] and (optional) the residual trace bf16[L+1, H].  Replaces
+ * FullModel.forward (megakernel.py:1224-1301). */
+REC_API int rec_decode_step(RecCtx* ctx, int32_t token, int32_t position, void* logits_dev,
+                            void* trace_dev, void* stream);
+/* Up to `count` greedy steps with the argmax fed back on the device; stops
+ * after an EOS id.  ids_dev int32[count] receives the produced ids, produced_dev
+ * int32[1] their number.  Replaces ResidentSampler.block for temperature 0
+ * (sampling.py:62-169, resident_block.py:12-88). */
+REC_API int rec_decode_greedy(RecCtx* ctx, int32_t token, int32_t position, int32_t count,
+                              const int32_t* eos, int32_t n_eos, int32_t* ids_dev,
+                              int32_t* produced_dev, void* stream);
+/* Reads the device status word (synchronises `stream`).  Non-zero marks the
+ * session unusable. */
+REC_API int rec_check_status(RecCtx* ctx, void* stream);
+REC_API int rec_last_error(char* buf, size_t len);
+
+/* ---- kernel entry points used by the unit tests -------------------------- */
+/* y = W x (int4 g64) with an optional fused RMSNorm prologue on x. */
+REC_API int rec_gemv_int4(const RecQMat* w, int32_t scale_dtype, int64_t n, int32_t k,
+                          const void* x_dev, const void* norm_weight_dev, float eps, void* y_dev,
+                          void* stream);
+/* MLX affine quantization of fp32 groups into codes + (bf16|fp16) scale/bias. */
+REC_API int rec_quantize_affine(const float* w_dev, int64_t n_groups, int32_t bits,
+                                int32_t scale_dtype, void* codes_dev, void* scales_dev,
+                                void* biases_dev, void* stream);
+
+#endif /* REC_B200_H */

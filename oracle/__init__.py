@@ -1,0 +1,187 @@
+"""CPU oracle of the rec decode hot path — TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py (cpu_baseline leg and
+--impl reference) may import this package.  It is the checker; the product
+path (rec_b200) never calls it.
+
+`rec_oracle.c` restates, in the canonical operation order of the CUDA
+kernels, the reference's algorithms (recursive-oss/rec,
+engine/src/rec_mlx/model.py and kernels/megakernel.py; see the C file header
+for line citations).  With identical inputs it matches the GPU bit for bit.
+`semantic.py` restates the reference's MLX formulas without any fixed order
+and is used for tolerance checks (rel-L2 2e-3 in bf16).
+
+Parity against MLX itself is unpinned: mlx 0.32.0 / mlx-lm 0.31.3 cannot be
+installed here and the reference holds no golden vectors; the reference's
+own kernel tests (engine/tests/test_kernel_routing.py,
+kernels/activation_optimization.py) are restated as known-answer tests.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "librec_oracle.so"
+_lib = None
+
+_u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+_u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        from . import build as _build
+
+        _build.build()
+        L = C.CDLL(str(LIB_PATH))
+        L.orc_exp.restype = C.c_float
+        L.orc_exp.argtypes = [C.c_float]
+        L.orc_exp_n.argtypes = [_f32p, _f32p, C.c_int64]
+        L.orc_quantize_affine.argtypes = [_f32p, C.c_int64, C.c_int, C.c_int, _u32p, _u16p, _u16p]
+        L.orc_gemv_int4.argtypes = [_u32p, _u16p, _u16p, C.c_int, C.c_int64, C.c_int, _u16p, _u16p]
+        L.orc_rmsnorm.argtypes = [_u16p, _u16p, C.c_int, C.c_float, _u16p]
+        L.orc_rope_table.argtypes = [C.c_float, C.c_int32, C.c_int32, _f32p]
+        L.orc_router_logits.argtypes = [_u16p, _u16p, C.c_int, C.c_int, _f32p]
+        L.orc_route.argtypes = [_f32p, C.c_int, C.c_int, C.c_int, C.c_void_p, _i32p, _f32p]
+        L.orc_swiglu.restype = C.c_uint16
+        L.orc_swiglu.argtypes = [C.c_uint16, C.c_uint16]
+        L.orc_argmax_bf16.restype = C.c_int32
+        L.orc_argmax_bf16.argtypes = [_u16p, C.c_int64]
+        L.orc_partial_bytes.restype = C.c_int
+        L.orc_sample.restype = C.c_int32
+        L.orc_to_bf.restype = C.c_uint16
+        L.orc_to_bf.argtypes = [C.c_float]
+        L.orc_to_hf.restype = C.c_uint16
+        L.orc_to_hf.argtypes = [C.c_float]
+        L.orc_hf.restype = C.c_float
+        L.orc_hf.argtypes = [C.c_uint16]
+        L.orc_decode_step.restype = C.c_int
+        _lib = L
+    return _lib
+
+
+# ---------------------------------------------------------------- bf16 / fp16
+def bf16_to_f32(u16: np.ndarray) -> np.ndarray:
+    return (np.asarray(u16, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16(f: np.ndarray) -> np.ndarray:
+    """Round to nearest even, NaN -> 0x7fff (same as the C oracle and CUDA)."""
+    u = np.ascontiguousarray(f, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = 0x7FFF
+    return r
+
+
+def fp16_to_f32(u16: np.ndarray) -> np.ndarray:
+    return np.asarray(u16, dtype=np.uint16).view(np.float16).astype(np.float32)
+
+
+def scale_to_f32(u16: np.ndarray, sd: int) -> np.ndarray:
+    return fp16_to_f32(u16) if sd == 0 else bf16_to_f32(u16)
+
+
+# ---------------------------------------------------------------- primitives
+def exp(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().orc_exp_n(x.ravel(), y.ravel(), x.size)
+    return y
+
+
+def quantize(w: np.ndarray, bits: int = 4, sd: int = 0):
+    """MLX affine quantization, group 64 along the last axis.  Returns codes
+    uint32[..., K*bits/32], scales and biases uint16[..., K/64]."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    *lead, k = w.shape
+    groups = w.size // 64
+    codes = np.zeros((*lead, k * bits // 32), np.uint32)
+    scales = np.zeros((*lead, k // 64), np.uint16)
+    biases = np.zeros_like(scales)
+    lib().orc_quantize_affine(w.reshape(-1), groups, bits, sd, codes.reshape(-1), scales.reshape(-1),
+                              biases.reshape(-1))
+    return codes, scales, biases
+
+
+def dequantize(codes, scales, biases, bits: int = 4, sd: int = 0) -> np.ndarray:
+    codes = np.asarray(codes, dtype=np.uint32)
+    per = 32 // bits
+    shifts = (np.arange(per, dtype=np.uint32) * bits)
+    q = ((codes[..., None] >> shifts) & ((1 << bits) - 1)).reshape(*codes.shape[:-1], -1).astype(np.float32)
+    s = np.repeat(scale_to_f32(scales, sd), 64, axis=-1)
+    b = np.repeat(scale_to_f32(biases, sd), 64, axis=-1)
+    return s * q + b
+
+
+def gemv(codes, scales, biases, x_bf16, sd: int = 0) -> np.ndarray:
+    codes = np.ascontiguousarray(codes, dtype=np.uint32)
+    n, k8 = codes.shape
+    y = np.zeros(n, np.uint16)
+    lib().orc_gemv_int4(codes.reshape(-1), np.ascontiguousarray(scales, np.uint16).reshape(-1),
+                        np.ascontiguousarray(biases, np.uint16).reshape(-1), sd, n, k8 * 8,
+                        np.ascontiguousarray(x_bf16, np.uint16), y)
+    return y
+
+
+def rmsnorm(h_bf16, w_bf16, eps: float = 1e-6) -> np.ndarray:
+    h = np.ascontiguousarray(h_bf16, np.uint16)
+    out = np.zeros_like(h)
+    lib().orc_rmsnorm(h, np.ascontiguousarray(w_bf16, np.uint16), h.size, eps, out)
+    return out
+
+
+def rope_table(theta: float, pos0: int, n: int) -> np.ndarray:
+    cs = np.zeros((n, 128), np.float32)
+    lib().orc_rope_table(theta, pos0, n, cs.reshape(-1))
+    return cs
+
+
+def router_logits(w_bf16, x_bf16) -> np.ndarray:
+    w = np.ascontiguousarray(w_bf16, np.uint16)
+    e, h = w.shape
+    out = np.zeros(e, np.float32)
+    lib().orc_router_logits(w.reshape(-1), np.ascontiguousarray(x_bf16, np.uint16), e, h, out)
+    return out
+
+
+def route(logits, k: int, mode: int = 0, bias=None):
+    logits = np.ascontiguousarray(logits, np.float32)
+    ids = np.zeros(k, np.int32)
+    w = np.zeros(k, np.float32)
+    bias_arr = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    lib().orc_route(logits, logits.size, k, mode, None if bias_arr is None else bias_arr.ctypes.data, ids, w)
+    return ids, w
+
+
+def select_topk(p, choice, k: int):
+    p = np.ascontiguousarray(p, np.float32)
+    choice = np.ascontiguousarray(choice, np.float32)
+    ids = np.zeros(k, np.int32)
+    w = np.zeros(k, np.float32)
+    lib().orc_select_topk(p.ctypes.data, choice.ctypes.data, p.size, k, ids.ctypes.data, w.ctypes.data)
+    return ids, w
+
+
+def mix(down_bf16, weights) -> np.ndarray:
+    d = np.ascontiguousarray(down_bf16, np.uint16)
+    k, h = d.shape
+    w = np.ascontiguousarray(weights, np.float32)
+    out = np.zeros(h, np.uint16)
+    lib().orc_mix(d.ctypes.data, h, w.ctypes.data, k, out.ctypes.data)
+    return out
+
+
+def swiglu(g_bf16: int, u_bf16: int) -> int:
+    return int(lib().orc_swiglu(int(g_bf16), int(u_bf16)))
+
+
+def argmax_bf16(x) -> int:
+    x = np.ascontiguousarray(x, np.uint16)
+    return int(lib().orc_argmax_bf16(x, x.size))

@@ -1,0 +1,799 @@
+/*
+ * rec_oracle.c — CPU restatement of the rec decode hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker for the CUDA path in
+ * rec_b200/csrc; only tests/, __graft_entry__.smoke() and bench.py's
+ * cpu_baseline / --impl reference legs load it.  Nothing in the product path
+ * links or calls it.
+ *
+ * What it restates (recursive-oss/rec, paths inside the project):
+ *   - MLX affine quantization used by nn.quantize and the quantized KV cache
+ *     (engine/src/rec_mlx/quantized.py:26-36, model.py:45-82); restated from
+ *     mlx 0.32.0's published affine_quantize algorithm (not vendored here).
+ *   - int4 g64 GEMV y = sum_g s_g*sum(x*q) + b_g*sum(x)  (megakernel.py:189-232)
+ *   - RMSNorm w*bf16(x*rsqrt(mean x^2+eps))               (megakernel.py:726-744)
+ *   - RoPE on pairs (i, i+64), theta_i = pos*base^(-i/64) (megakernel.py:248-266,
+ *     model.py:159-176)
+ *   - quantize-on-append of K/V, group 64 along head_dim   (model.py:45-82)
+ *   - GQA decode attention over the quantized cache, split-KV partials and a
+ *     log-sum-exp merge                                    (megakernel.py:276-318,
+ *     619-693; scores/sink semantics model.py:108-139)
+ *   - router: softmax -> top-k -> renormalise, or sigmoid + bias selection
+ *                                                          (model.py:245-254,
+ *     megakernel.py:406-435,696-725, rank_routing.py:12-32)
+ *   - SwiGLU experts with the reference's bf16 rounding points and the
+ *     sequential bf16 expert mix                           (megakernel.py:747-798,
+ *     944-969, mixed_bits.py:32-54)
+ *   - lm_head GEMV + argmax with lowest-index ties        (resident_block.py:12-59)
+ *   - penalty / temperature / top-k / top-p sampler with an injected uniform.
+ *
+ * Every floating-point operation is written out with its rounding, in the
+ * canonical order the CUDA kernels use (compile with -ffp-contract=off and
+ * FMA hardware: fmaf() is the IEEE fused multiply-add).  With identical
+ * inputs the CUDA path and this file agree bit for bit.
+ *
+ * Parity against MLX itself is unpinned: mlx/mlx-lm are not installable in
+ * this environment and the reference ships no golden vectors.
+ */
+#include <float.h>
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "../include/rec_b200.h"
+
+#define ORC_API __attribute__((visibility("default")))
+
+/* ------------------------------------------------------------------ types */
+static inline float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+
+static inline float bf(uint16_t v) { return u2f((uint32_t)v << 16); }
+static inline uint16_t to_bf(float f) {
+  uint32_t u = f2u(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fff; /* canonical NaN */
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+static inline float rbf(float f) { return bf(to_bf(f)); }
+
+static inline float hf(uint16_t h) {
+  uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1fu, man = h & 0x3ffu;
+  if (exp == 0) {
+    if (man == 0) return u2f(sign);
+    float v = (float)man * 5.9604644775390625e-8f; /* 2^-24, exact */
+    return sign ? -v : v;
+  }
+  if (exp == 31) return u2f(sign | 0x7f800000u | (man << 13));
+  return u2f(sign | ((exp + 112u) << 23) | (man << 13));
+}
+static inline uint16_t to_hf(float f) {
+  /* round to nearest even */
+  uint32_t u = f2u(f), sign = (u >> 16) & 0x8000u;
+  uint32_t a = u & 0x7fffffffu;
+  if (a > 0x7f800000u) return (uint16_t)(sign | 0x7e00u);
+  if (a >= 0x477ff000u) return (uint16_t)(sign | 0x7c00u); /* overflow -> inf */
+  if (a < 0x38800000u) {                                    /* subnormal half */
+    float v = u2f(a) * 16777216.0f;                          /* * 2^24, exact */
+    uint32_t m = (uint32_t)rintf(v);
+    return (uint16_t)(sign | m);
+  }
+  uint32_t exp = (a >> 23) - 112u, man = a & 0x7fffffu;
+  uint32_t h = (exp << 10) | (man >> 13);
+  uint32_t rem = man & 0x1fffu;
+  if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h += 1;
+  return (uint16_t)(sign | h);
+}
+static inline float sbv(uint16_t v, int sd) { return sd == REC_SCALE_FP16 ? hf(v) : bf(v); }
+static inline uint16_t to_sb(float f, int sd) { return sd == REC_SCALE_FP16 ? to_hf(f) : to_bf(f); }
+
+ORC_API uint16_t orc_to_bf(float f) { return to_bf(f); }
+ORC_API uint16_t orc_to_hf(float f) { return to_hf(f); }
+ORC_API float orc_hf(uint16_t h) { return hf(h); }
+
+/* -------------------------------------------------------------- exp */
+/* Cody-Waite reduction with a 16-bit head of ln2, degree-7 Taylor polynomial
+ * in Horner form with fused multiply-adds, 2^n applied in two halves. */
+ORC_API float orc_exp(float x) {
+  if (!(x > -104.0f)) return (x != x) ? x : 0.0f;
+  if (x > 88.8f) return u2f(0x7f800000u);
+  const float log2e = 1.44269504088896341f;
+  const float ln2_hi = 0.693145751953125f;
+  const float ln2_lo = 1.42860682030941723e-6f;
+  float n = rintf(x * log2e);
+  float r = fmaf(-n, ln2_hi, x);
+  r = fmaf(-n, ln2_lo, r);
+  float p = 1.98412698412698413e-4f;
+  p = fmaf(p, r, 1.38888888888888889e-3f);
+  p = fmaf(p, r, 8.33333333333333333e-3f);
+  p = fmaf(p, r, 4.16666666666666667e-2f);
+  p = fmaf(p, r, 1.66666666666666667e-1f);
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  int e = (int)n;
+  int e1 = e / 2, e2 = e - e1;
+  p = p * u2f((uint32_t)(e1 + 127) << 23);
+  return p * u2f((uint32_t)(e2 + 127) << 23);
+}
+static inline float rexp(float x) { return orc_exp(x); }
+ORC_API void orc_exp_n(const float* x, float* y, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) y[i] = orc_exp(x[i]);
+}
+static inline float rsigmoid(float g) {
+  float tail = 1.0f / (1.0f + rexp(fabsf(g)));
+  return g < 0.0f ? tail : 1.0f - tail;
+}
+
+/* Butterfly sum over w lanes: v[l] += v[l^off] for off = w/2..1. */
+static void bfly(float* v, int w) {
+  float t[32];
+  for (int off = w / 2; off >= 1; off >>= 1) {
+    for (int l = 0; l < w; ++l) t[l] = v[l] + v[l ^ off];
+    memcpy(v, t, sizeof(float) * w);
+  }
+}
+
+/* ------------------------------------------------- affine quantization */
+/* mx.quantize(w, group_size=64, bits, mode="affine") for one group of fp32
+ * values; codes packed little-endian into uint32 words. */
+static void quant_group(const float* w, int bits, int sd, uint32_t* codes, uint16_t* s_out,
+                        uint16_t* b_out) {
+  const int G = 64;
+  float wmax = w[0], wmin = w[0];
+  for (int i = 1; i < G; ++i) {
+    wmax = w[i] > wmax ? w[i] : wmax;
+    wmin = w[i] < wmin ? w[i] : wmin;
+  }
+  const float n_bins = (float)((1 << bits) - 1);
+  float scale = (wmax - wmin) / n_bins;
+  scale = scale > 1e-7f ? scale : 1e-7f;
+  int side = fabsf(wmin) > fabsf(wmax);
+  scale = side ? scale : -scale;
+  float edge = side ? wmin : wmax;
+  float q0 = rintf(edge / scale);
+  float bias = 0.0f;
+  if (q0 != 0.0f) {
+    scale = edge / q0;
+    bias = edge;
+  }
+  int per = 32 / bits;
+  for (int i = 0; i < G / per; ++i) codes[i] = 0;
+  for (int i = 0; i < G; ++i) {
+    float q = rintf((w[i] - bias) / scale);
+    q = q < 0.0f ? 0.0f : (q > n_bins ? n_bins : q);
+    codes[i / per] |= (uint32_t)q << (bits * (i % per));
+  }
+  *s_out = to_sb(scale, sd);
+  *b_out = to_sb(bias, sd);
+}
+
+ORC_API void orc_quantize_affine(const float* w, int64_t n_groups, int bits, int sd, uint32_t* codes,
+                                 uint16_t* scales, uint16_t* biases) {
+  int words = 64 * bits / 32;
+#pragma omp parallel for schedule(static)
+  for (int64_t g = 0; g < n_groups; ++g)
+    quant_group(w + g * 64, bits, sd, codes + g * words, scales + g, biases + g);
+}
+
+/* ------------------------------------------------------------ RMSNorm */
+/* Sum of squares: H/8 chunks of 8 (sequential), groups of 32 chunks by
+ * butterfly, group sums in order.  inv = 1/sqrt(ss/H + eps). */
+static float rms_inv(const uint16_t* h, int H, float eps) {
+  int groups = H / 256;
+  float total = 0.0f;
+  for (int g = 0; g < groups; ++g) {
+    float v[32];
+    for (int l = 0; l < 32; ++l) {
+      float a = 0.0f;
+      for (int i = 0; i < 8; ++i) {
+        float x = bf(h[(g * 32 + l) * 8 + i]);
+        a = fmaf(x, x, a);
+      }
+      v[l] = a;
+    }
+    bfly(v, 32);
+    total = total + v[0];
+  }
+  float mean = total / (float)H;
+  return 1.0f / sqrtf(mean + eps);
+}
+static void rmsnorm(const uint16_t* h, const uint16_t* w, int H, float eps, uint16_t* out) {
+  float inv = rms_inv(h, H, eps);
+  for (int i = 0; i < H; ++i) out[i] = to_bf(bf(w[i]) * rbf(bf(h[i]) * inv));
+}
+ORC_API void orc_rmsnorm(const uint16_t* h, const uint16_t* w, int H, float eps, uint16_t* out) {
+  rmsnorm(h, w, H, eps, out);
+}
+
+/* ---------------------------------------------------------- int4 GEMV */
+typedef struct {
+  float p[4][4][2];
+  float X;
+} ChunkX;
+
+static void prep_chunk(const uint16_t* x32, ChunkX* cx) {
+  static const float lo_scale[4] = {1.0f, 0.0625f, 0.00390625f, 0.000244140625f};
+  static const float hi_scale[4] = {1.52587890625e-05f, 0.00390625f, 0.000244140625f,
+                                    1.52587890625e-05f};
+  float xl = 0.0f, xh = 0.0f;
+  for (int k = 0; k < 4; ++k)
+    for (int i = 0; i < 4; ++i) {
+      float a = bf(x32[8 * k + i]), b = bf(x32[8 * k + 4 + i]);
+      cx->p[k][i][0] = a * lo_scale[i];
+      cx->p[k][i][1] = b * hi_scale[i];
+      xl = xl + a;
+      xh = xh + b;
+    }
+  cx->X = xl + xh;
+}
+
+static float chunk_dot(const uint32_t* w4, const ChunkX* cx) {
+  const uint32_t M = 0x4B000000u;
+  float lo = 0.0f, hi = 0.0f;
+  for (int k = 0; k < 4; ++k) {
+    uint32_t a = w4[k], a12 = a >> 12;
+    float fl[4] = {u2f((a & 0xFu) | M), u2f((a & 0xF0u) | M), u2f((a & 0xF00u) | M),
+                   u2f((a & 0xF000u) | M)};
+    float fh[4] = {u2f((a & 0xF0000u) | M), u2f((a12 & 0xF00u) | M), u2f((a12 & 0xF000u) | M),
+                   u2f((a12 & 0xF0000u) | M)};
+    for (int i = 0; i < 4; ++i) {
+      fl[i] = fl[i] - 8388608.0f;
+      fh[i] = fh[i] - 8388608.0f;
+    }
+    for (int i = 0; i < 4; ++i) {
+      lo = fmaf(cx->p[k][i][0], fl[i], lo);
+      hi = fmaf(cx->p[k][i][1], fh[i], hi);
+    }
+  }
+  return lo + hi;
+}
+
+/* One row of y = W x in the canonical lane order.  cx: prepared chunks of x. */
+static float rowdot(const uint32_t* wrow, const uint16_t* srow, const uint16_t* brow, int sd, int K,
+                    const ChunkX* cx) {
+  int wide = (K % 2048) == 0;
+  int T = wide ? 32 : 8, SEG = wide ? K / 2048 : 1, CH = wide ? 2 : K / 256;
+  float total = 0.0f;
+  for (int seg = 0; seg < SEG; ++seg) {
+    float v[32];
+    for (int l = 0; l < T; ++l) {
+      float acc = 0.0f;
+      for (int m = 0; m < CH; ++m) {
+        int c = wide ? seg * 64 + l + 32 * m : l + 8 * m;
+        float d = chunk_dot(wrow + c * 4, &cx[c]);
+        float s = sbv(srow[c >> 1], sd), b = sbv(brow[c >> 1], sd);
+        acc = fmaf(s, d, acc);
+        acc = fmaf(b, cx[c].X, acc);
+      }
+      v[l] = acc;
+    }
+    bfly(v, T);
+    total = seg == 0 ? v[0] : total + v[0];
+  }
+  return total;
+}
+
+static ChunkX* prep_x(const uint16_t* x, int K) {
+  ChunkX* cx = (ChunkX*)malloc(sizeof(ChunkX) * (K / 32));
+  for (int c = 0; c < K / 32; ++c) prep_chunk(x + c * 32, &cx[c]);
+  return cx;
+}
+
+static void gemv(const RecQMat* m, int sd, int64_t row0, int64_t n, int K, const uint16_t* x,
+                 float* yf, uint16_t* y) {
+  ChunkX* cx = prep_x(x, K);
+  const uint32_t* W = (const uint32_t*)m->w;
+  const uint16_t* S = (const uint16_t*)m->scales;
+  const uint16_t* B = (const uint16_t*)m->biases;
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < n; ++r) {
+    int64_t row = row0 + r;
+    float v = rowdot(W + row * (K / 8), S + row * (K / 64), B + row * (K / 64), sd, K, cx);
+    if (yf) yf[r] = v;
+    if (y) y[r] = to_bf(v);
+  }
+  free(cx);
+}
+
+ORC_API void orc_gemv_int4(const uint32_t* w, const uint16_t* s, const uint16_t* b, int sd,
+                           int64_t n, int K, const uint16_t* x, uint16_t* y) {
+  RecQMat m = {w, s, b};
+  gemv(&m, sd, 0, n, K, x, NULL, y);
+}
+
+/* --------------------------------------------------------- embedding */
+static void embed(const RecQMat* m, int sd, int H, int token, uint16_t* h) {
+  const uint32_t* W = (const uint32_t*)m->w + (int64_t)token * (H / 8);
+  const uint16_t* S = (const uint16_t*)m->scales + (int64_t)token * (H / 64);
+  const uint16_t* B = (const uint16_t*)m->biases + (int64_t)token * (H / 64);
+  for (int i = 0; i < H; ++i) {
+    float q = (float)((W[i / 8] >> (4 * (i % 8))) & 15u);
+    h[i] = to_bf(fmaf(sbv(S[i / 64], sd), q, sbv(B[i / 64], sd)));
+  }
+}
+
+/* ------------------------------------------------------------- RoPE */
+/* cos/sin of pos*base^(-i/64), computed in double and rounded to float. */
+ORC_API void orc_rope_table(float theta, int32_t pos0, int32_t n, float* cs) {
+  for (int p = 0; p < n; ++p)
+    for (int i = 0; i < 64; ++i) {
+      double inv = pow((double)theta, -(double)i / 64.0);
+      double a = (double)(pos0 + p) * inv;
+      cs[(int64_t)p * 128 + i] = (float)cos(a);
+      cs[(int64_t)p * 128 + 64 + i] = (float)sin(a);
+    }
+}
+static void rope_head(uint16_t* x, const float* cs) {
+  for (int i = 0; i < 64; ++i) {
+    float a = bf(x[i]), b = bf(x[i + 64]), c = cs[i], s = cs[64 + i];
+    float lo = fmaf(a, c, -(b * s));
+    float hi = fmaf(a, s, b * c);
+    x[i] = to_bf(lo);
+    x[i + 64] = to_bf(hi);
+  }
+}
+/* per-head RMSNorm over 128 (q_norm/k_norm): lane l holds dims 4l..4l+3,
+ * sequential squares, butterfly, inv = 1/sqrt(ss/128 + eps). */
+static void head_norm(uint16_t* x, const uint16_t* w, float eps) {
+  float v[32];
+  for (int l = 0; l < 32; ++l) {
+    float a = 0.0f;
+    for (int j = 0; j < 4; ++j) {
+      float t = bf(x[4 * l + j]);
+      a = fmaf(t, t, a);
+    }
+    v[l] = a;
+  }
+  bfly(v, 32);
+  float inv = 1.0f / sqrtf(v[0] / 128.0f + eps);
+  for (int d = 0; d < 128; ++d) x[d] = to_bf(bf(w[d]) * rbf(bf(x[d]) * inv));
+}
+
+/* ------------------------------------------------- KV quantized append */
+static void kv_store(const RecKVLayer* kv, int Hkv, int C, int bits, int pos, const uint16_t* k,
+                     const uint16_t* v) {
+  int words = 128 * bits / 32;
+  for (int g = 0; g < Hkv; ++g)
+    for (int half = 0; half < 2; ++half) {
+      int64_t slot = (int64_t)g * C + pos;
+      float wk[64], wv[64];
+      for (int i = 0; i < 64; ++i) {
+        wk[i] = bf(k[g * 128 + half * 64 + i]);
+        wv[i] = bf(v[g * 128 + half * 64 + i]);
+      }
+      quant_group(wk, bits, REC_SCALE_BF16, (uint32_t*)kv->k_codes + slot * words + half * (words / 2),
+                  (uint16_t*)kv->k_scales + slot * 2 + half, (uint16_t*)kv->k_biases + slot * 2 + half);
+      quant_group(wv, bits, REC_SCALE_BF16, (uint32_t*)kv->v_codes + slot * words + half * (words / 2),
+                  (uint16_t*)kv->v_scales + slot * 2 + half, (uint16_t*)kv->v_biases + slot * 2 + half);
+    }
+}
+ORC_API void orc_kv_store(const RecKVLayer* kv, int Hkv, int C, int bits, int pos, const uint16_t* k,
+                          const uint16_t* v) {
+  kv_store(kv, Hkv, C, bits, pos, k, v);
+}
+
+/* ---------------------------------------------------------- attention */
+#define ATT_BLOCK 256
+#define ATT_TILE 32
+#define ATT_WARPS 4
+#define ATT_SUPER 64 /* blocks per super-chunk */
+#define NEG_INF (-INFINITY)
+
+typedef struct {
+  float m, l;
+  float acc[128];
+} Partial;
+
+static void p_empty(Partial* p) {
+  p->m = NEG_INF;
+  p->l = 0.0f;
+  memset(p->acc, 0, sizeof(p->acc));
+}
+/* a <- merge(a, b) */
+static void p_merge(Partial* a, const Partial* b) {
+  if (b->m == NEG_INF) return;
+  if (a->m == NEG_INF) {
+    *a = *b;
+    return;
+  }
+  float m = a->m > b->m ? a->m : b->m;
+  float a1 = rexp(a->m - m), a2 = rexp(b->m - m);
+  a->l = fmaf(a->l, a1, b->l * a2);
+  for (int d = 0; d < 128; ++d) a->acc[d] = fmaf(a->acc[d], a1, b->acc[d] * a2);
+  a->m = m;
+}
+
+static inline uint32_t kv_code(const uint32_t* row, int bits, int d) {
+  return bits == 4 ? (row[d >> 3] >> (4 * (d & 7))) & 15u : (row[d >> 2] >> (8 * (d & 3))) & 255u;
+}
+
+/* qs: scaled bf16 query of one head as floats[128]; QS[2]: group sums. */
+static float att_score(const float* qs, const float* QS, const uint32_t* krow, const uint16_t* ks,
+                       const uint16_t* kb, int bits) {
+  float t = 0.0f;
+  for (int g = 0; g < 2; ++g) {
+    float a[4] = {0, 0, 0, 0};
+    for (int d = 64 * g; d < 64 * g + 64; ++d) a[d & 3] = fmaf(qs[d], (float)kv_code(krow, bits, d), a[d & 3]);
+    float A = (a[0] + a[1]) + (a[2] + a[3]);
+    float s = bf(ks[g]), b = bf(kb[g]);
+    t = g == 0 ? fmaf(b, QS[0], s * A) : fmaf(b, QS[1], fmaf(s, A, t));
+  }
+  return rbf(t);
+}
+
+/* Partial of q head h over tokens [t0, t1) in the canonical tile/warp order
+ * (block-local). */
+static void att_block(const float* qs, const float* QS, const RecKVLayer* kv, int g, int C, int bits,
+                      int b, int T, Partial* out) {
+  int words = 128 * bits / 32;
+  const uint32_t* KC = (const uint32_t*)kv->k_codes;
+  const uint32_t* VC = (const uint32_t*)kv->v_codes;
+  const uint16_t *KS = (const uint16_t*)kv->k_scales, *KB = (const uint16_t*)kv->k_biases;
+  const uint16_t *VS = (const uint16_t*)kv->v_scales, *VB = (const uint16_t*)kv->v_biases;
+  Partial warp[ATT_WARPS];
+  for (int w = 0; w < ATT_WARPS; ++w) {
+    Partial* P = &warp[w];
+    p_empty(P);
+    for (int j = w; j < ATT_BLOCK / ATT_TILE; j += ATT_WARPS) {
+      int base = b * ATT_BLOCK + j * ATT_TILE;
+      if (base >= T) break;
+      float s[ATT_TILE], p[ATT_TILE];
+      float tmax = NEG_INF;
+      for (int t = 0; t < ATT_TILE; ++t) {
+        int tok = base + t;
+        if (tok < T) {
+          int64_t slot = (int64_t)g * C + tok;
+          s[t] = att_score(qs, QS, KC + slot * words, KS + slot * 2, KB + slot * 2, bits);
+          tmax = s[t] > tmax ? s[t] : tmax;
+        }
+      }
+      float mnew = P->m > tmax ? P->m : tmax;
+      float alpha = rexp(P->m - mnew);
+      for (int t = 0; t < ATT_TILE; ++t) p[t] = (base + t < T) ? rexp(s[t] - mnew) : 0.0f;
+      float v[32];
+      memcpy(v, p, sizeof(v));
+      bfly(v, 32);
+      P->l = fmaf(P->l, alpha, v[0]);
+      for (int d = 0; d < 128; ++d) P->acc[d] = P->acc[d] * alpha;
+      for (int t = 0; t < ATT_TILE; ++t) {
+        int tok = base + t;
+        if (tok >= T) break;
+        int64_t slot = (int64_t)g * C + tok;
+        const uint32_t* vrow = VC + slot * words;
+        for (int d = 0; d < 128; ++d) {
+          float val = fmaf(bf(VS[slot * 2 + d / 64]), (float)kv_code(vrow, bits, d), bf(VB[slot * 2 + d / 64]));
+          P->acc[d] = fmaf(p[t], val, P->acc[d]);
+        }
+      }
+      P->m = mnew;
+    }
+  }
+  p_empty(out);
+  for (int w = 0; w < ATT_WARPS; ++w) p_merge(out, &warp[w]);
+}
+
+static void prep_query(const uint16_t* q, float* qs, float* QS) {
+  for (int d = 0; d < 128; ++d) qs[d] = rbf(bf(q[d]) * 0.0883883476483184405f);
+  for (int g = 0; g < 2; ++g) {
+    float a[4] = {0, 0, 0, 0};
+    for (int d = 64 * g; d < 64 * g + 64; ++d) a[d & 3] = a[d & 3] + qs[d];
+    QS[g] = (a[0] + a[1]) + (a[2] + a[3]);
+  }
+}
+
+/* Super-chunk partials of every q head: supers[h * n_super + s].  Tokens
+ * [0, T) of one layer's cache. */
+ORC_API void orc_attention_supers(const uint16_t* q, const RecKVLayer* kv, int Hq, int Hkv, int C,
+                                  int bits, int T, Partial* supers, int n_super) {
+  int nblocks = (T + ATT_BLOCK - 1) / ATT_BLOCK;
+#pragma omp parallel for schedule(dynamic)
+  for (int h = 0; h < Hq; ++h) {
+    float qs[128], QS[2];
+    prep_query(q + h * 128, qs, QS);
+    int g = h / (Hq / Hkv);
+    for (int s = 0; s < n_super; ++s) {
+      Partial* S = &supers[h * n_super + s];
+      p_empty(S);
+      for (int b = s * ATT_SUPER; b < (s + 1) * ATT_SUPER && b < nblocks; ++b) {
+        Partial P;
+        att_block(qs, QS, kv, g, C, bits, b, T, &P);
+        p_merge(S, &P);
+      }
+    }
+  }
+}
+
+ORC_API void orc_attention_final(const Partial* supers, int Hq, int n_super, const uint16_t* sinks,
+                                 uint16_t* out) {
+  for (int h = 0; h < Hq; ++h) {
+    Partial F;
+    p_empty(&F);
+    if (sinks) {
+      F.m = bf(sinks[h]);
+      F.l = 1.0f;
+    }
+    for (int s = 0; s < n_super; ++s) p_merge(&F, &supers[h * n_super + s]);
+    for (int d = 0; d < 128; ++d) out[h * 128 + d] = to_bf(F.acc[d] / F.l);
+  }
+}
+
+ORC_API int orc_partial_bytes(void) { return (int)sizeof(Partial); }
+
+/* -------------------------------------------------------------- router */
+/* bf16 router logits: lane l owns 8-element chunks l, l+32, ...; sequential
+ * fused multiply-adds, butterfly, round to bf16. */
+static float router_logit(const uint16_t* wrow, const uint16_t* x, int H) {
+  float v[32];
+  for (int l = 0; l < 32; ++l) {
+    float a = 0.0f;
+    for (int c = l; c < H / 8; c += 32)
+      for (int i = 0; i < 8; ++i) a = fmaf(bf(wrow[c * 8 + i]), bf(x[c * 8 + i]), a);
+    v[l] = a;
+  }
+  bfly(v, 32);
+  return rbf(v[0]);
+}
+
+/* Selection + weights.  Softmax: p = exp(l - max) / sum (lane l sums experts
+ * l, l+32, ... in order, then butterfly).  Sigmoid: p = sigmoid(l), choice
+ * = p + bias.  top-k by choice, ties -> lower index; weights
+ * = p_sel / (sum_sel + 1e-20) with the sum taken in rank order. */
+/* top-k of `choice` (ties -> lower index), weights = p_sel/(sum + 1e-20) with
+ * the sum taken in rank order (rank_routing.py:12-32, megakernel.py:696-725). */
+ORC_API void orc_select_topk(const float* p, const float* choice, int E, int k, int32_t* ids,
+                             float* weights) {
+  int taken[1024] = {0};
+  for (int r = 0; r < k; ++r) {
+    int best = -1;
+    for (int e = 0; e < E; ++e)
+      if (!taken[e] && (best < 0 || choice[e] > choice[best])) best = e;
+    taken[best] = 1;
+    ids[r] = best;
+  }
+  float sum = 0.0f;
+  for (int r = 0; r < k; ++r) sum = sum + p[ids[r]];
+  sum = sum + 1e-20f;
+  for (int r = 0; r < k; ++r) weights[r] = p[ids[r]] / sum;
+}
+
+/* bf16 expert mix of H elements: out[i] = mix over r of down[r*H + i]. */
+ORC_API void orc_mix(const uint16_t* down, int H, const float* w, int k, uint16_t* out);
+
+ORC_API void orc_route(const float* logits, int E, int k, int mode, const float* bias, int32_t* ids,
+                       float* weights) {
+  float p[1024], choice[1024];
+  if (mode == REC_ROUTER_SOFTMAX) {
+    float mx = NEG_INF;
+    for (int e = 0; e < E; ++e) mx = logits[e] > mx ? logits[e] : mx;
+    float v[32];
+    for (int l = 0; l < 32; ++l) {
+      float a = 0.0f;
+      for (int e = l; e < E; e += 32) a = a + rexp(logits[e] - mx);
+      v[l] = a;
+    }
+    bfly(v, 32);
+    for (int e = 0; e < E; ++e) {
+      p[e] = rexp(logits[e] - mx) / v[0];
+      choice[e] = p[e];
+    }
+  } else {
+    for (int e = 0; e < E; ++e) {
+      p[e] = rsigmoid(logits[e]);
+      choice[e] = p[e] + bias[e];
+    }
+  }
+  orc_select_topk(p, choice, E, k, ids, weights);
+}
+
+ORC_API void orc_router_logits(const uint16_t* W, const uint16_t* x, int E, int H, float* logits) {
+  for (int e = 0; e < E; ++e) logits[e] = router_logit(W + (int64_t)e * H, x, H);
+}
+
+/* SwiGLU: sig = bf16(sigmoid(g)), act = bf16(bf16(g*sig)*u) (megakernel.py:770-774). */
+static inline uint16_t swiglu(float g, float u) {
+  float sig = rbf(rsigmoid(g));
+  return to_bf(rbf(g * sig) * u);
+}
+ORC_API uint16_t orc_swiglu(uint16_t g, uint16_t u) { return swiglu(bf(g), bf(u)); }
+
+/* Expert mix for one element: m = bf16(d_0*bf16(w_0)) + 0, then for r >= 1
+ * m = bf16(bf16(d_r*bf16(w_r)) + 0 + m) (mixed_bits.py:42-54). */
+static inline float mix_elem(const uint16_t* d, int stride, const float* w, int k) {
+  float m = 0.0f;
+  for (int r = 0; r < k; ++r) {
+    float t = rbf(bf(d[r * stride]) * rbf(w[r])) + 0.0f;
+    m = r == 0 ? t : rbf(t + m);
+  }
+  return m;
+}
+
+ORC_API void orc_mix(const uint16_t* down, int H, const float* w, int k, uint16_t* out) {
+  for (int i = 0; i < H; ++i) out[i] = to_bf(mix_elem(down + i, H, w, k));
+}
+
+/* MoE FFN on normalised x: writes the bf16 mix (without residual). */
+static void moe_ffn(const RecModelDesc* md, const RecLayerWeights* L, const uint16_t* xn,
+                    const int32_t* ids, const float* w, uint16_t* mix, uint16_t* act_out,
+                    uint16_t* down_out) {
+  int H = md->hidden, I = md->moe_inter, k = md->top_k, sd = md->scale_dtype;
+  uint16_t* act = (uint16_t*)malloc(sizeof(uint16_t) * k * I);
+  uint16_t* dn = (uint16_t*)malloc(sizeof(uint16_t) * k * H);
+  uint16_t* g = (uint16_t*)malloc(sizeof(uint16_t) * I);
+  uint16_t* u = (uint16_t*)malloc(sizeof(uint16_t) * I);
+  for (int r = 0; r < k; ++r) {
+    gemv(&L->gate, sd, (int64_t)ids[r] * I, I, H, xn, NULL, g);
+    gemv(&L->up, sd, (int64_t)ids[r] * I, I, H, xn, NULL, u);
+    for (int i = 0; i < I; ++i) act[r * I + i] = swiglu(bf(g[i]), bf(u[i]));
+    gemv(&L->down, sd, (int64_t)ids[r] * H, H, I, act + r * I, NULL, dn + r * H);
+  }
+  for (int i = 0; i < H; ++i) mix[i] = to_bf(mix_elem(dn + i, H, w, k));
+  if (act_out) memcpy(act_out, act, sizeof(uint16_t) * k * I);
+  if (down_out) memcpy(down_out, dn, sizeof(uint16_t) * k * H);
+  free(act);
+  free(dn);
+  free(g);
+  free(u);
+}
+
+ORC_API void orc_moe(const RecModelDesc* md, const RecLayerWeights* L, const uint16_t* h,
+                     int32_t* ids, float* w, uint16_t* act, uint16_t* down, uint16_t* h_out) {
+  int H = md->hidden, E = md->n_experts;
+  uint16_t* xn = (uint16_t*)malloc(sizeof(uint16_t) * H);
+  float* logits = (float*)malloc(sizeof(float) * E);
+  uint16_t* mix = (uint16_t*)malloc(sizeof(uint16_t) * H);
+  rmsnorm(h, (const uint16_t*)L->post_norm, H, md->rms_eps, xn);
+  orc_router_logits((const uint16_t*)L->router, xn, E, H, logits);
+  orc_route(logits, E, md->top_k, md->router_mode, (const float*)L->expert_bias, ids, w);
+  moe_ffn(md, L, xn, ids, w, mix, act, down);
+  for (int i = 0; i < H; ++i) h_out[i] = to_bf(bf(h[i]) + bf(mix[i]));
+  free(xn);
+  free(logits);
+  free(mix);
+}
+
+/* ------------------------------------------------------- argmax / head */
+static int32_t argmax_bf16(const uint16_t* x, int64_t n) {
+  float best = NEG_INF;
+  int32_t idx = -1;
+  for (int64_t i = 0; i < n; ++i) {
+    float v = bf(x[i]);
+    if (v > best || idx < 0) {
+      if (v != v) continue;
+      best = v;
+      idx = (int32_t)i;
+    }
+  }
+  return idx;
+}
+ORC_API int32_t orc_argmax_bf16(const uint16_t* x, int64_t n) { return argmax_bf16(x, n); }
+
+/* Sampler: z = penalised(logit)/T; keep the top_k by z (ties -> lower
+ * index) in descending order; e_i = exp(z_i - z_0); S = sum e_i; p_i = e_i/S;
+ * keep the shortest prefix whose cumulative p reaches top_p; draw with the
+ * uniform u as the first i with cumsum(e)_i > u * sum(e over kept).
+ * Penalty (repetition): for ids present in history, l > 0 ? l/pen : l*pen. */
+ORC_API int32_t orc_sample(const uint16_t* logits, int64_t V, const int32_t* hist, int n_hist,
+                           const RecSampling* sp, float u) {
+  if (sp->temperature == 0.0f) return argmax_bf16(logits, V);
+  uint8_t* seen = (uint8_t*)calloc((size_t)V, 1);
+  for (int i = 0; i < n_hist; ++i)
+    if (hist[i] >= 0 && hist[i] < V) seen[hist[i]] = 1;
+  int K = sp->top_k > 0 ? sp->top_k : (int)V;
+  if (K > V) K = (int)V;
+  float* z = (float*)malloc(sizeof(float) * V);
+  for (int64_t v = 0; v < V; ++v) {
+    float l = bf(logits[v]);
+    if (seen[v] && sp->repetition_penalty != 1.0f)
+      l = l > 0.0f ? l / sp->repetition_penalty : l * sp->repetition_penalty;
+    z[v] = l / sp->temperature;
+  }
+  /* top-K selection by repeated max (ties -> lower index) */
+  int32_t* sel = (int32_t*)malloc(sizeof(int32_t) * K);
+  uint8_t* used = (uint8_t*)calloc((size_t)V, 1);
+  for (int r = 0; r < K; ++r) {
+    int64_t best = -1;
+    for (int64_t v = 0; v < V; ++v)
+      if (!used[v] && (best < 0 || z[v] > z[best])) best = v;
+    used[best] = 1;
+    sel[r] = (int32_t)best;
+  }
+  float* e = (float*)malloc(sizeof(float) * K);
+  float S = 0.0f;
+  for (int r = 0; r < K; ++r) {
+    e[r] = rexp(z[sel[r]] - z[sel[0]]);
+    S = S + e[r];
+  }
+  int n = K;
+  if (sp->top_p < 1.0f) {
+    float c = 0.0f;
+    for (int r = 0; r < K; ++r) {
+      c = c + e[r] / S;
+      if (c >= sp->top_p) {
+        n = r + 1;
+        break;
+      }
+    }
+  }
+  float Sn = 0.0f;
+  for (int r = 0; r < n; ++r) Sn = Sn + e[r];
+  float target = u * Sn;
+  float c = 0.0f;
+  int32_t out = sel[n - 1];
+  for (int r = 0; r < n; ++r) {
+    c = c + e[r];
+    if (c > target) {
+      out = sel[r];
+      break;
+    }
+  }
+  free(seen);
+  free(z);
+  free(sel);
+  free(used);
+  free(e);
+  return out;
+}
+
+/* --------------------------------------------------------- decode step */
+/* One full decode step.  kv: n_layers layer caches of capacity C; h_trace
+ * (optional) bf16[L+1, H]; logits bf16[V]. */
+ORC_API int orc_decode_step(const RecModelDesc* md, const RecLayerWeights* layers,
+                            const RecGlobalWeights* gw, const RecKVLayer* kv, int C, int token,
+                            int pos, uint16_t* logits, uint16_t* trace) {
+  int H = md->hidden, Hq = md->n_q_heads, Hkv = md->n_kv_heads, D = 128;
+  int sd = md->scale_dtype;
+  if (token < 0 || token >= md->vocab || pos < 0 || pos >= C) return -1;
+  uint16_t* h = (uint16_t*)malloc(sizeof(uint16_t) * H);
+  uint16_t* xn = (uint16_t*)malloc(sizeof(uint16_t) * H);
+  uint16_t* qkv = (uint16_t*)malloc(sizeof(uint16_t) * (Hq + 2 * Hkv) * D);
+  uint16_t* att = (uint16_t*)malloc(sizeof(uint16_t) * Hq * D);
+  uint16_t* o = (uint16_t*)malloc(sizeof(uint16_t) * H);
+  float cs[128];
+  orc_rope_table(md->rope_theta, pos, 1, cs);
+  int T = pos + 1;
+  int n_super = (T + ATT_BLOCK * ATT_SUPER - 1) / (ATT_BLOCK * ATT_SUPER);
+  Partial* supers = (Partial*)malloc(sizeof(Partial) * Hq * n_super);
+
+  embed(&gw->embed, sd, H, token, h);
+  if (trace) memcpy(trace, h, sizeof(uint16_t) * H);
+  for (int li = 0; li < md->n_layers; ++li) {
+    const RecLayerWeights* L = &layers[li];
+    rmsnorm(h, (const uint16_t*)L->input_norm, H, md->rms_eps, xn);
+    gemv(&L->q, sd, 0, Hq * D, H, xn, NULL, qkv);
+    gemv(&L->k, sd, 0, Hkv * D, H, xn, NULL, qkv + Hq * D);
+    gemv(&L->v, sd, 0, Hkv * D, H, xn, NULL, qkv + (Hq + Hkv) * D);
+    uint16_t* q = qkv;
+    uint16_t* k = qkv + Hq * D;
+    uint16_t* v = qkv + (Hq + Hkv) * D;
+    for (int hh = 0; hh < Hq; ++hh) {
+      if ((md->flags & REC_FLAG_QK_NORM) && L->q_norm) head_norm(q + hh * D, (const uint16_t*)L->q_norm, md->rms_eps);
+      rope_head(q + hh * D, cs);
+    }
+    for (int g = 0; g < Hkv; ++g) {
+      if ((md->flags & REC_FLAG_QK_NORM) && L->k_norm) head_norm(k + g * D, (const uint16_t*)L->k_norm, md->rms_eps);
+      rope_head(k + g * D, cs);
+    }
+    kv_store(&kv[li], Hkv, C, md->kv_bits, pos, k, v);
+    orc_attention_supers(q, &kv[li], Hq, Hkv, C, md->kv_bits, T, supers, n_super);
+    orc_attention_final(supers, Hq, n_super,
+                        (md->flags & REC_FLAG_SINKS) ? (const uint16_t*)L->sinks : NULL, att);
+    gemv(&L->o, sd, 0, H, Hq * D, att, NULL, o);
+    for (int i = 0; i < H; ++i) h[i] = to_bf(bf(h[i]) + bf(o[i]));
+    int32_t ids[8];
+    float w[8];
+    orc_moe(md, L, h, ids, w, NULL, NULL, h);
+    if (trace) memcpy(trace + (int64_t)(li + 1) * H, h, sizeof(uint16_t) * H);
+  }
+  rmsnorm(h, (const uint16_t*)gw->final_norm, H, md->rms_eps, xn);
+  gemv(&gw->lm_head, sd, 0, md->vocab, H, xn, NULL, logits);
+  free(h);
+  free(xn);
+  free(qkv);
+  free(att);
+  free(o);
+  free(supers);
+  return 0;
+}

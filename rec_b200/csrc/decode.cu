@@ -1,0 +1,625 @@
+// Decode session: workspace layout, the per-token launch sequence (captured
+// once into a CUDA graph) and the session entry points of the C ABI.
+//
+// Replaces FullModel.forward / ResidentSampler.block of the reference
+// (engine/src/rec_mlx/kernels/megakernel.py:1224-1301, sampling.py:62-169):
+// one persistent Metal dispatch with ~390 software grid barriers per token
+// becomes a graph of ~7 kernels per layer chained with programmatic
+// dependent launch, so each kernel streams its weights while the previous one
+// finishes.
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <vector>
+
+#include "attn.cuh"
+#include "capi_common.h"
+#include "moe.cuh"
+
+namespace rec {
+
+// --- control block (device ints) ---------------------------------------------
+enum Ctrl : int {
+  kCtlStatus = 0,
+  kCtlToken = 1,
+  kCtlPosition = 2,
+  kCtlActive = 3,
+  kCtlProduced = 4,
+  kCtlStep = 5,
+  kCtlNEos = 6,
+  kCtlArgmax = 7,
+  kCtlEos = 8,       // 8 slots
+  kCtlRecorded = 16, // 64 slots: ids produced by the current packet
+  kCtlInts = 80,
+};
+constexpr int kMaxPacket = 64;
+constexpr int kMaxEos = 8;
+
+__global__ void k_set_step(int* ctl, int token, int position, int n_eos, const int4 eos_lo, const int4 eos_hi) {
+  if (threadIdx.x == 0) {
+    ctl[kCtlToken] = token;
+    ctl[kCtlPosition] = position;
+    ctl[kCtlActive] = 1;
+    ctl[kCtlProduced] = 0;
+    ctl[kCtlStep] = 0;
+    ctl[kCtlNEos] = n_eos;
+    const int e[8] = {eos_lo.x, eos_lo.y, eos_lo.z, eos_lo.w, eos_hi.x, eos_hi.y, eos_hi.z, eos_hi.w};
+    for (int i = 0; i < kMaxEos; ++i) ctl[kCtlEos + i] = e[i];
+  }
+}
+
+// Embedding row (int4 g64): h = bf16(fma(scale, q, bias)).  Also the first
+// trace row.  Reference megakernel.py:850-860.
+template <int SD>
+__global__ void __launch_bounds__(256) k_embed(int* ctl, QMatDev emb, int H, int V, int capacity, int token_base,
+                                               uint16_t* h, uint16_t* trace) {
+  int tok = ctl[kCtlToken];
+  const int pos = ctl[kCtlPosition];
+  if (tok < 0 || tok >= V) {
+    if (threadIdx.x == 0) report(ctl + kCtlStatus, kStatusBadToken);
+    tok = 0;
+  }
+  if ((pos < 0 || pos - token_base >= capacity) && threadIdx.x == 0) report(ctl + kCtlStatus, kStatusBadPosition);
+  grid_launch_dependents();
+  const uint32_t* w = emb.w + size_t(tok) * (H / 8);
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float q = float((w[i >> 3] >> (4 * (i & 7))) & 15u);
+    const float s = sb<SD>(emb.s[size_t(tok) * (H / 64) + (i >> 6)]);
+    const float b = sb<SD>(emb.b[size_t(tok) * (H / 64) + (i >> 6)]);
+    const uint16_t v = to_bf(__fmaf_rn(s, q, b));
+    h[i] = v;
+    trace[i] = v;
+  }
+}
+
+// End of a step: record the argmax, stop after EOS, advance the position.
+__global__ void k_step_end(int* ctl) {
+  grid_wait();
+  if (threadIdx.x == 0) {
+    const int t = ctl[kCtlArgmax];
+    const int step = ctl[kCtlStep];
+    if (ctl[kCtlActive]) {
+      if (step < kMaxPacket) ctl[kCtlRecorded + step] = t;
+      ctl[kCtlProduced] += 1;
+      for (int i = 0; i < ctl[kCtlNEos]; ++i)
+        if (ctl[kCtlEos + i] == t) ctl[kCtlActive] = 0;
+    }
+    ctl[kCtlToken] = t;
+    ctl[kCtlPosition] += 1;
+    ctl[kCtlStep] = step + 1;
+  }
+}
+
+// --- launch helper ----------------------------------------------------------------
+template <typename Kern, typename... Args>
+cudaError_t launch(Kern kern, int grid, int block, size_t smem, cudaStream_t st, bool pdl, Args... args) {
+  static std::mutex mu;
+  static std::set<const void*> configured;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    const void* key = reinterpret_cast<const void*>(kern);
+    if (smem > 48 * 1024 && !configured.count(key)) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+      if (e != cudaSuccess) return e;
+      configured.insert(key);
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+}  // namespace rec
+
+// ------------------------------------------------------------------------------
+// Session
+// ------------------------------------------------------------------------------
+using namespace rec;
+
+struct RecCtx {
+  RecModelDesc d;
+  std::vector<RecLayerWeights> layers;
+  RecGlobalWeights g = {};
+  bool has_weights = false;
+  std::vector<RecKVLayer> kv;
+  int capacity = 0;
+  int token_base = 0;       // split-KV: first position held by this rank
+  int block_begin = 0, block_end = 1 << 30;
+  uint8_t* ws = nullptr;
+  size_t ws_bytes = 0;
+  bool usable = true;
+  // workspace views
+  int* ctl = nullptr;
+  unsigned* counters = nullptr;
+  uint16_t *h = nullptr, *qkv = nullptr, *attn = nullptr, *xn = nullptr, *act = nullptr, *logits = nullptr,
+           *trace = nullptr;
+  float *router_logits = nullptr, *wts = nullptr, *cand_val = nullptr, *partials = nullptr, *supers = nullptr,
+        *rope = nullptr;
+  int *ids = nullptr, *cand_idx = nullptr;
+  int n_super_max = 0;
+  int grid = 148;
+  cudaStream_t cap_stream = nullptr;
+  cudaGraphExec_t step_exec = nullptr;
+};
+
+namespace {
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct Layout {
+  size_t off[24];
+  size_t total;
+};
+
+enum Region {
+  rCtl, rCounters, rH, rQkv, rAttn, rXn, rAct, rLogits, rTrace, rRouter, rIds, rWts, rCandV, rCandI, rPartials,
+  rSupers, rRope, rCount
+};
+
+Layout layout_of(const RecCtx* c) {
+  const RecModelDesc& d = c->d;
+  const int grid = c->grid;
+  const int nblk = c->capacity / kAttBlock;
+  const int nsup = (nblk + kAttSuper - 1) / kAttSuper;
+  size_t sz[rCount];
+  sz[rCtl] = kCtlInts * 4;
+  sz[rCounters] = (64 + d.n_q_heads) * 4;
+  sz[rH] = size_t(d.hidden) * 2;
+  sz[rQkv] = size_t(d.n_q_heads + 2 * d.n_kv_heads) * 128 * 2;
+  sz[rAttn] = size_t(d.n_q_heads) * 128 * 2;
+  sz[rXn] = size_t(d.hidden) * 2;
+  sz[rAct] = size_t(d.top_k) * d.moe_inter * 2;
+  sz[rLogits] = size_t(d.vocab) * 2;
+  sz[rTrace] = size_t(d.n_layers + 1) * d.hidden * 2;
+  sz[rRouter] = size_t(d.n_experts) * 4;
+  sz[rIds] = kMaxTopK * 4;
+  sz[rWts] = kMaxTopK * 4;
+  sz[rCandV] = size_t(grid) * 4;
+  sz[rCandI] = size_t(grid) * 4;
+  sz[rPartials] = size_t(d.n_q_heads) * nblk * kPartialFloats * 4;
+  sz[rSupers] = size_t(d.n_q_heads) * nsup * kPartialFloats * 4;
+  sz[rRope] = size_t(c->capacity) * 128 * 4;
+  Layout L;
+  size_t o = 0;
+  for (int i = 0; i < rCount; ++i) {
+    L.off[i] = o;
+    o = align_up(o + sz[i], 256);
+  }
+  L.total = o;
+  return L;
+}
+
+template <int SD>
+cudaError_t enqueue_step_sd(RecCtx* c, cudaStream_t st) {
+  const RecModelDesc& d = c->d;
+  const int H = d.hidden;
+  const int grid = c->grid;
+  cudaError_t e;
+  e = launch(k_embed<SD>, 1, 256, 0, st, false, c->ctl, QMatDev{(const uint32_t*)c->g.embed.w,
+             (const uint16_t*)c->g.embed.scales, (const uint16_t*)c->g.embed.biases}, H, d.vocab, c->capacity,
+             c->token_base, c->h, c->trace);
+  if (e != cudaSuccess) return e;
+  int* status = c->ctl + kCtlStatus;
+  for (int li = 0; li < d.n_layers; ++li) {
+    const RecLayerWeights& L = c->layers[li];
+    const RecKVLayer& kv = c->kv[li];
+    // 1. RMSNorm + QKV projection
+    {
+      GemvArgs a = {};
+      a.mat[0] = {(const uint32_t*)L.q.w, (const uint16_t*)L.q.scales, (const uint16_t*)L.q.biases};
+      a.mat[1] = {(const uint32_t*)L.k.w, (const uint16_t*)L.k.scales, (const uint16_t*)L.k.biases};
+      a.mat[2] = {(const uint32_t*)L.v.w, (const uint16_t*)L.v.scales, (const uint16_t*)L.v.biases};
+      a.rows[0] = d.n_q_heads * 128;
+      a.rows[1] = d.n_kv_heads * 128;
+      a.rows[2] = d.n_kv_heads * 128;
+      a.total_rows = a.rows[0] + a.rows[1] + a.rows[2];
+      a.x = c->h;
+      a.norm_w = (const uint16_t*)L.input_norm;
+      a.eps = d.rms_eps;
+      a.out = c->qkv;
+      a.status = status;
+      a.pdl = 1;
+      using Kq = GemvSmem<2048, gemv_rs<2048>(), 3>;
+      e = launch(k_gemv<2048, SD, gemv_rs<2048>(), 3, kEpiStore>, grid, kThreads, sizeof(Kq), st, true, a);
+      if (e != cudaSuccess) return e;
+    }
+    // 2. attention partials (+ RoPE, quantize-on-append) and combine
+    {
+      AttnArgs a = {};
+      a.qkv = c->qkv;
+      a.k_codes = (uint32_t*)kv.k_codes;
+      a.k_scales = (uint16_t*)kv.k_scales;
+      a.k_biases = (uint16_t*)kv.k_biases;
+      a.v_codes = (uint32_t*)kv.v_codes;
+      a.v_scales = (uint16_t*)kv.v_scales;
+      a.v_biases = (uint16_t*)kv.v_biases;
+      a.capacity = c->capacity;
+      a.hq = d.n_q_heads;
+      a.hkv = d.n_kv_heads;
+      a.rope = c->rope;
+      a.q_norm = (d.flags & REC_FLAG_QK_NORM) ? (const uint16_t*)L.q_norm : nullptr;
+      a.k_norm = (d.flags & REC_FLAG_QK_NORM) ? (const uint16_t*)L.k_norm : nullptr;
+      a.eps = d.rms_eps;
+      a.position = c->ctl + kCtlPosition;
+      a.token_base = c->token_base;
+      a.block_begin = c->block_begin;
+      a.block_end = c->block_end;
+      a.partials = c->partials;
+      a.supers = c->supers;
+      a.head_counters = c->counters + 2;
+      a.out = c->attn;
+      a.sinks = (d.flags & REC_FLAG_SINKS) ? (const uint16_t*)L.sinks : nullptr;
+      a.n_super_max = c->n_super_max;
+      a.final_merge = 1;
+      a.status = status;
+      a.pdl = 1;
+      const int agrid = 2 * sm_count();
+      if (d.kv_bits == 4)
+        e = launch(k_attn_partial<4>, agrid, 128, sizeof(AttnSmem<4>), st, true, a);
+      else
+        e = launch(k_attn_partial<8>, agrid, 128, sizeof(AttnSmem<8>), st, true, a);
+      if (e != cudaSuccess) return e;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(d.n_q_heads, std::max(1, c->n_super_max));
+      cfg.blockDim = dim3(32);
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      e = cudaLaunchKernelEx(&cfg, k_attn_combine, a);
+      if (e != cudaSuccess) return e;
+    }
+    // 3. O projection + residual
+    {
+      GemvArgs a = {};
+      a.mat[0] = {(const uint32_t*)L.o.w, (const uint16_t*)L.o.scales, (const uint16_t*)L.o.biases};
+      a.rows[0] = H;
+      a.total_rows = H;
+      a.x = c->attn;
+      a.resid = c->h;
+      a.status = status;
+      a.pdl = 1;
+      if (d.n_q_heads * 128 == 4096) {
+        using Ko = GemvSmem<4096, gemv_rs<4096>(), 3>;
+        e = launch(k_gemv<4096, SD, gemv_rs<4096>(), 3, kEpiResidual>, grid, kThreads, sizeof(Ko), st, true, a);
+      } else {
+        using Ko = GemvSmem<2048, gemv_rs<2048>(), 3>;
+        e = launch(k_gemv<2048, SD, gemv_rs<2048>(), 3, kEpiResidual>, grid, kThreads, sizeof(Ko), st, true, a);
+      }
+      if (e != cudaSuccess) return e;
+    }
+    // 4. router
+    {
+      RouterArgs a = {};
+      a.h = c->h;
+      a.norm_w = (const uint16_t*)L.post_norm;
+      a.eps = d.rms_eps;
+      a.w = (const uint16_t*)L.router;
+      a.expert_bias = (const float*)L.expert_bias;
+      a.E = d.n_experts;
+      a.k = d.top_k;
+      a.mode = d.router_mode;
+      a.logits = c->router_logits;
+      a.xn_out = c->xn;
+      a.ids = c->ids;
+      a.wts = c->wts;
+      a.counter = c->counters + 1;
+      a.status = status;
+      a.pdl = 1;
+      e = launch(k_router<2048>, (d.n_experts + kWarps - 1) / kWarps, kThreads, sizeof(RouterSmem<2048>), st, true, a);
+      if (e != cudaSuccess) return e;
+    }
+    // 5. experts gate/up + SwiGLU
+    {
+      GateUpArgs a = {};
+      a.gate = {(const uint32_t*)L.gate.w, (const uint16_t*)L.gate.scales, (const uint16_t*)L.gate.biases};
+      a.up = {(const uint32_t*)L.up.w, (const uint16_t*)L.up.scales, (const uint16_t*)L.up.biases};
+      a.xn = c->xn;
+      a.ids = c->ids;
+      a.k = d.top_k;
+      a.I = d.moe_inter;
+      a.expert_lo = 0;
+      a.expert_hi = d.n_experts;
+      a.act = c->act;
+      a.status = status;
+      a.pdl = 1;
+      constexpr int RSP = 16;
+      e = launch(k_gateup<SD, RSP, 3>, grid, kThreads, sizeof(GateUpSmem<RSP, 3>), st, true, a);
+      if (e != cudaSuccess) return e;
+    }
+    // 6. experts down + bf16 mix + residual
+    {
+      DownArgs a = {};
+      a.down = {(const uint32_t*)L.down.w, (const uint16_t*)L.down.scales, (const uint16_t*)L.down.biases};
+      a.act = c->act;
+      a.ids = c->ids;
+      a.wts = c->wts;
+      a.k = d.top_k;
+      a.H = H;
+      a.expert_lo = 0;
+      a.expert_hi = d.n_experts;
+      a.h = c->h;
+      a.trace_row = c->trace + size_t(li + 1) * H;
+      a.status = status;
+      a.pdl = 1;
+      const int dgrid = std::max(grid, H / (2 * DownSmem<768>::RMAX / 2));
+      switch (d.moe_inter) {
+        case 256: e = launch(k_down<256, SD>, dgrid, kThreads, sizeof(DownSmem<256>), st, true, a); break;
+        case 512: e = launch(k_down<512, SD>, dgrid, kThreads, sizeof(DownSmem<512>), st, true, a); break;
+        case 768: e = launch(k_down<768, SD>, dgrid, kThreads, sizeof(DownSmem<768>), st, true, a); break;
+        case 1024: e = launch(k_down<1024, SD>, dgrid, kThreads, sizeof(DownSmem<1024>), st, true, a); break;
+        default: return cudaErrorInvalidValue;
+      }
+      if (e != cudaSuccess) return e;
+    }
+  }
+  // final norm + lm_head + argmax
+  {
+    GemvArgs a = {};
+    a.mat[0] = {(const uint32_t*)c->g.lm_head.w, (const uint16_t*)c->g.lm_head.scales,
+                (const uint16_t*)c->g.lm_head.biases};
+    a.rows[0] = d.vocab;
+    a.total_rows = d.vocab;
+    a.x = c->h;
+    a.norm_w = (const uint16_t*)c->g.final_norm;
+    a.eps = d.rms_eps;
+    a.out = c->logits;
+    a.cand_val = c->cand_val;
+    a.cand_idx = c->cand_idx;
+    a.counter = c->counters + 0;
+    a.token_out = c->ctl + kCtlArgmax;
+    a.status = status;
+    a.pdl = 1;
+    using Kh = GemvSmem<2048, gemv_rs<2048>(), 3>;
+    e = launch(k_gemv<2048, SD, gemv_rs<2048>(), 3, kEpiArgmax>, grid, kThreads, sizeof(Kh), st, true, a);
+    if (e != cudaSuccess) return e;
+  }
+  return launch(k_step_end, 1, 32, 0, st, true, c->ctl);
+}
+
+cudaError_t enqueue_step(RecCtx* c, cudaStream_t st) {
+  return c->d.scale_dtype == REC_SCALE_FP16 ? enqueue_step_sd<0>(c, st) : enqueue_step_sd<1>(c, st);
+}
+
+int ensure_graph(RecCtx* c) {
+  if (c->step_exec) return REC_OK;
+  if (!c->cap_stream) REC_CHECK_CUDA(cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking));
+  cudaGraph_t graph = nullptr;
+  REC_CHECK_CUDA(cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal));
+  cudaError_t e = enqueue_step(c, c->cap_stream);
+  cudaError_t e2 = cudaStreamEndCapture(c->cap_stream, &graph);
+  if (e != cudaSuccess || e2 != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    set_error("step capture failed: %s", cudaGetErrorString(e != cudaSuccess ? e : e2));
+    return REC_ECUDA;
+  }
+  e = cudaGraphInstantiate(&c->step_exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) {
+    c->step_exec = nullptr;
+    set_error("graph instantiate failed: %s", cudaGetErrorString(e));
+    return REC_ECUDA;
+  }
+  return REC_OK;
+}
+
+void drop_graph(RecCtx* c) {
+  if (c->step_exec) cudaGraphExecDestroy(c->step_exec);
+  c->step_exec = nullptr;
+}
+
+bool valid_qmat(const RecQMat& m) {
+  return m.w && m.scales && m.biases && aligned16(m.w) && aligned16(m.scales) && aligned16(m.biases);
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------
+// C ABI
+// ------------------------------------------------------------------------------
+REC_API int rec_create(const RecModelDesc* desc, RecCtx** out) {
+  REC_CHECK_ARG(desc && out, "rec_create: null argument");
+  const RecModelDesc& d = *desc;
+  REC_CHECK_ARG(d.hidden == 2048, "hidden must be 2048 (got %d)", d.hidden);
+  REC_CHECK_ARG(d.head_dim == 128, "head_dim must be 128");
+  REC_CHECK_ARG(d.n_kv_heads > 0 && d.n_q_heads == 8 * d.n_kv_heads, "need 8 query heads per KV head");
+  REC_CHECK_ARG(d.n_q_heads * 128 == 2048 || d.n_q_heads * 128 == 4096, "n_q_heads must be 16 or 32");
+  REC_CHECK_ARG(d.n_experts > 0 && d.n_experts <= kMaxExperts, "n_experts must be in 1..%d", kMaxExperts);
+  REC_CHECK_ARG(d.top_k >= 1 && d.top_k <= kMaxTopK && d.top_k <= d.n_experts, "top_k must be in 1..8");
+  REC_CHECK_ARG(d.moe_inter == 256 || d.moe_inter == 512 || d.moe_inter == 768 || d.moe_inter == 1024,
+                "moe_inter must be 256, 512, 768 or 1024");
+  REC_CHECK_ARG(d.vocab > 0 && d.vocab % 2 == 0, "vocab must be even");
+  REC_CHECK_ARG(d.group_size == 64, "group_size must be 64");
+  REC_CHECK_ARG(d.scale_dtype == REC_SCALE_FP16 || d.scale_dtype == REC_SCALE_BF16, "bad scale dtype");
+  REC_CHECK_ARG(d.kv_bits == 4 || d.kv_bits == 8, "kv_bits must be 4 or 8");
+  REC_CHECK_ARG(d.router_mode == REC_ROUTER_SOFTMAX || d.router_mode == REC_ROUTER_SIGMOID, "bad router mode");
+  REC_CHECK_ARG(d.n_layers >= 1, "need at least one layer");
+  RecCtx* c = new RecCtx();
+  c->d = d;
+  c->grid = sm_count();
+  *out = c;
+  return REC_OK;
+}
+
+REC_API void rec_destroy(RecCtx* ctx) {
+  if (!ctx) return;
+  drop_graph(ctx);
+  if (ctx->cap_stream) cudaStreamDestroy(ctx->cap_stream);
+  delete ctx;
+}
+
+REC_API int rec_set_weights(RecCtx* c, const RecLayerWeights* layers, int32_t n_layers, const RecGlobalWeights* g) {
+  REC_CHECK_ARG(c && layers && g, "rec_set_weights: null argument");
+  REC_CHECK_ARG(n_layers == c->d.n_layers, "expected %d layers, got %d", c->d.n_layers, n_layers);
+  for (int i = 0; i < n_layers; ++i) {
+    const RecLayerWeights& L = layers[i];
+    REC_CHECK_ARG(L.input_norm && L.post_norm && L.router, "layer %d: missing norm/router weights", i);
+    REC_CHECK_ARG(valid_qmat(L.q) && valid_qmat(L.k) && valid_qmat(L.v) && valid_qmat(L.o) && valid_qmat(L.gate) &&
+                      valid_qmat(L.up) && valid_qmat(L.down),
+                  "layer %d: quantized matrices must be non-null and 16-byte aligned", i);
+    REC_CHECK_ARG(aligned16(L.router), "layer %d: router must be 16-byte aligned", i);
+    REC_CHECK_ARG(c->d.router_mode != REC_ROUTER_SIGMOID || L.expert_bias, "layer %d: sigmoid router needs a bias", i);
+    REC_CHECK_ARG(!(c->d.flags & REC_FLAG_SINKS) || L.sinks, "layer %d: sinks enabled but missing", i);
+    REC_CHECK_ARG(!(c->d.flags & REC_FLAG_QK_NORM) || (L.q_norm && L.k_norm), "layer %d: qk norm missing", i);
+  }
+  REC_CHECK_ARG(valid_qmat(g->embed) && valid_qmat(g->lm_head) && g->final_norm, "global weights incomplete");
+  c->layers.assign(layers, layers + n_layers);
+  c->g = *g;
+  c->has_weights = true;
+  drop_graph(c);
+  return REC_OK;
+}
+
+REC_API int rec_set_kv(RecCtx* c, const RecKVLayer* layers, int32_t n_layers, int32_t capacity) {
+  REC_CHECK_ARG(c && layers, "rec_set_kv: null argument");
+  REC_CHECK_ARG(n_layers == c->d.n_layers, "expected %d KV layers", c->d.n_layers);
+  REC_CHECK_ARG(capacity > 0 && capacity % kAttBlock == 0, "capacity must be a positive multiple of %d", kAttBlock);
+  for (int i = 0; i < n_layers; ++i) {
+    const RecKVLayer& k = layers[i];
+    REC_CHECK_ARG(k.k_codes && k.k_scales && k.k_biases && k.v_codes && k.v_scales && k.v_biases &&
+                      aligned16(k.k_codes) && aligned16(k.v_codes) && aligned16(k.k_scales) &&
+                      aligned16(k.k_biases) && aligned16(k.v_scales) && aligned16(k.v_biases),
+                  "KV layer %d: buffers must be non-null and 16-byte aligned", i);
+  }
+  const bool grow = capacity != c->capacity;
+  c->kv.assign(layers, layers + n_layers);
+  c->capacity = capacity;
+  const int nblk = capacity / kAttBlock;
+  c->n_super_max = (nblk + kAttSuper - 1) / kAttSuper;
+  if (grow) {
+    c->ws = nullptr;  // workspace must be re-sized
+    c->ws_bytes = 0;
+  }
+  drop_graph(c);
+  return REC_OK;
+}
+
+REC_API size_t rec_workspace_bytes(const RecCtx* c) {
+  if (!c || c->capacity <= 0) return 0;
+  return layout_of(c).total;
+}
+
+REC_API int rec_set_workspace(RecCtx* c, void* ws, size_t bytes) {
+  REC_CHECK_ARG(c && ws, "rec_set_workspace: null argument");
+  REC_CHECK_ARG(c->capacity > 0, "call rec_set_kv before rec_set_workspace");
+  const Layout L = layout_of(c);
+  REC_CHECK_ARG(bytes >= L.total, "workspace too small: %zu < %zu", bytes, L.total);
+  REC_CHECK_ARG((reinterpret_cast<uintptr_t>(ws) & 255u) == 0, "workspace must be 256-byte aligned");
+  uint8_t* b = static_cast<uint8_t*>(ws);
+  c->ws = b;
+  c->ws_bytes = bytes;
+  c->ctl = reinterpret_cast<int*>(b + L.off[rCtl]);
+  c->counters = reinterpret_cast<unsigned*>(b + L.off[rCounters]);
+  c->h = reinterpret_cast<uint16_t*>(b + L.off[rH]);
+  c->qkv = reinterpret_cast<uint16_t*>(b + L.off[rQkv]);
+  c->attn = reinterpret_cast<uint16_t*>(b + L.off[rAttn]);
+  c->xn = reinterpret_cast<uint16_t*>(b + L.off[rXn]);
+  c->act = reinterpret_cast<uint16_t*>(b + L.off[rAct]);
+  c->logits = reinterpret_cast<uint16_t*>(b + L.off[rLogits]);
+  c->trace = reinterpret_cast<uint16_t*>(b + L.off[rTrace]);
+  c->router_logits = reinterpret_cast<float*>(b + L.off[rRouter]);
+  c->ids = reinterpret_cast<int*>(b + L.off[rIds]);
+  c->wts = reinterpret_cast<float*>(b + L.off[rWts]);
+  c->cand_val = reinterpret_cast<float*>(b + L.off[rCandV]);
+  c->cand_idx = reinterpret_cast<int*>(b + L.off[rCandI]);
+  c->partials = reinterpret_cast<float*>(b + L.off[rPartials]);
+  c->supers = reinterpret_cast<float*>(b + L.off[rSupers]);
+  c->rope = reinterpret_cast<float*>(b + L.off[rRope]);
+  // control block and counters start at zero
+  REC_CHECK_CUDA(cudaMemset(b, 0, L.off[rH]));
+  // RoPE table: cos/sin of pos * theta^(-i/64) in double, rounded to float
+  std::vector<float> cs(size_t(c->capacity) * 128);
+  for (int p = 0; p < c->capacity; ++p)
+    for (int i = 0; i < 64; ++i) {
+      const double inv = std::pow(double(c->d.rope_theta), -double(i) / 64.0);
+      const double ang = double(c->token_base + p) * inv;
+      cs[size_t(p) * 128 + i] = float(std::cos(ang));
+      cs[size_t(p) * 128 + 64 + i] = float(std::sin(ang));
+    }
+  REC_CHECK_CUDA(cudaMemcpy(c->rope, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+  c->usable = true;
+  drop_graph(c);
+  return REC_OK;
+}
+
+static int check_ready(RecCtx* c) {
+  REC_CHECK_ARG(c, "null context");
+  if (!c->usable) {
+    set_error("Session was invalidated by a GPU synchronization failure");
+    return REC_ESTATE;
+  }
+  if (!c->has_weights || !c->ws || c->kv.empty()) {
+    set_error("session not configured (weights, KV and workspace are required)");
+    return REC_ESTATE;
+  }
+  return ensure_graph(c);
+}
+
+REC_API int rec_decode_step(RecCtx* c, int32_t token, int32_t position, void* logits_dev, void* trace_dev,
+                            void* stream) {
+  int rc = check_ready(c);
+  if (rc) return rc;
+  if (position < c->token_base || position - c->token_base >= c->capacity) {
+    set_error("position %d outside the KV capacity", position);
+    return REC_ELIMIT;
+  }
+  REC_CHECK_ARG(token >= 0 && token < c->d.vocab, "token %d outside the vocabulary", token);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  k_set_step<<<1, 32, 0, st>>>(c->ctl, token, position, 0, make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0));
+  REC_CHECK_CUDA(cudaGetLastError());
+  REC_CHECK_CUDA(cudaGraphLaunch(c->step_exec, st));
+  if (logits_dev)
+    REC_CHECK_CUDA(cudaMemcpyAsync(logits_dev, c->logits, size_t(c->d.vocab) * 2, cudaMemcpyDeviceToDevice, st));
+  if (trace_dev)
+    REC_CHECK_CUDA(cudaMemcpyAsync(trace_dev, c->trace, size_t(c->d.n_layers + 1) * c->d.hidden * 2,
+                                   cudaMemcpyDeviceToDevice, st));
+  return REC_OK;
+}
+
+REC_API int rec_decode_greedy(RecCtx* c, int32_t token, int32_t position, int32_t count, const int32_t* eos,
+                              int32_t n_eos, int32_t* ids_dev, int32_t* produced_dev, void* stream) {
+  int rc = check_ready(c);
+  if (rc) return rc;
+  REC_CHECK_ARG(count >= 1 && count <= kMaxPacket, "packet must contain between 1 and %d tokens", kMaxPacket);
+  REC_CHECK_ARG(n_eos >= 0 && n_eos <= kMaxEos && (n_eos == 0 || eos), "between 0 and %d EOS ids", kMaxEos);
+  REC_CHECK_ARG(token >= 0 && token < c->d.vocab, "token %d outside the vocabulary", token);
+  if (position < c->token_base || position + count - c->token_base > c->capacity) {
+    set_error("Decode context limit exhausted");
+    return REC_ELIMIT;
+  }
+  int e8[8] = {-1, -1, -1, -1, -1, -1, -1, -1};
+  for (int i = 0; i < n_eos; ++i) e8[i] = eos[i];
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  k_set_step<<<1, 32, 0, st>>>(c->ctl, token, position, n_eos, make_int4(e8[0], e8[1], e8[2], e8[3]),
+                               make_int4(e8[4], e8[5], e8[6], e8[7]));
+  REC_CHECK_CUDA(cudaGetLastError());
+  for (int i = 0; i < count; ++i) REC_CHECK_CUDA(cudaGraphLaunch(c->step_exec, st));
+  if (ids_dev)
+    REC_CHECK_CUDA(cudaMemcpyAsync(ids_dev, c->ctl + kCtlRecorded, size_t(count) * 4, cudaMemcpyDeviceToDevice, st));
+  if (produced_dev)
+    REC_CHECK_CUDA(cudaMemcpyAsync(produced_dev, c->ctl + kCtlProduced, 4, cudaMemcpyDeviceToDevice, st));
+  return REC_OK;
+}
+
+REC_API int rec_check_status(RecCtx* c, void* stream) {
+  REC_CHECK_ARG(c && c->ctl, "rec_check_status: session not configured");
+  int s = 0;
+  REC_CHECK_CUDA(cudaMemcpyAsync(&s, c->ctl + kCtlStatus, 4, cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream)));
+  REC_CHECK_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  if (s != 0) {
+    c->usable = false;
+    set_error("GPU synchronization failed: device status %d", s);
+  }
+  return s;
+}

@@ -1,0 +1,248 @@
+"""Model configurations, synthetic weights and KV storage for the decode path.
+
+The layout of every tensor is the reference's MLX layout
+(engine/src/rec_mlx/quantized.py:26-36, megakernel.py:161-170):
+int4 g64 affine weights as uint32 codes [N, K/8] (stored as int32 tensors)
+with scales/biases [N, K/64]; expert weights stacked [E*N, K]; the quantized
+KV cache as codes [Hkv, C, 128*bits/32] with bf16 scales/biases [Hkv, C, 2]
+(model.py:40-82).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field, replace
+
+import torch
+
+from . import abi
+
+
+@dataclass(frozen=True)
+class ModelConfig:
+    """Shape of the decoder (reference ModelArgs, model.py:14-37)."""
+    name: str = "custom"
+    hidden: int = 2048
+    n_layers: int = 48
+    n_q_heads: int = 32
+    n_kv_heads: int = 4
+    head_dim: int = 128
+    n_experts: int = 128
+    top_k: int = 8
+    moe_inter: int = 768
+    vocab: int = 151936
+    scale_dtype: torch.dtype = torch.float16
+    kv_bits: int = 8
+    router_mode: int = abi.REC_ROUTER_SOFTMAX
+    flags: int = 0
+    rms_eps: float = 1e-6
+    rope_theta: float = 1e6
+
+    def desc(self) -> abi.RecModelDesc:
+        return abi.RecModelDesc(
+            hidden=self.hidden, n_layers=self.n_layers, n_q_heads=self.n_q_heads, n_kv_heads=self.n_kv_heads,
+            head_dim=self.head_dim, n_experts=self.n_experts, top_k=self.top_k, moe_inter=self.moe_inter,
+            vocab=self.vocab, group_size=64,
+            scale_dtype=abi.REC_SCALE_FP16 if self.scale_dtype == torch.float16 else abi.REC_SCALE_BF16,
+            kv_bits=self.kv_bits, router_mode=self.router_mode, flags=self.flags, rms_eps=self.rms_eps,
+            rope_theta=self.rope_theta)
+
+    def weight_bytes_per_token(self) -> int:
+        """Algorithmic bytes streamed per decode step (weights only)."""
+        g = 0.5 + 4 / 64  # int4 codes + fp16/bf16 scale and bias per 64
+        h, d = self.hidden, self.head_dim
+        attn = (self.n_q_heads + 2 * self.n_kv_heads) * d * h + h * self.n_q_heads * d
+        experts = self.top_k * 3 * self.moe_inter * h
+        per_layer = (attn + experts) * g + self.n_experts * h * 2 + 2 * h * 2
+        return int(self.n_layers * per_layer + self.vocab * h * g + h * 2 + h * g)
+
+    def kv_bytes_per_token(self, context: int) -> int:
+        per = 2 * self.n_kv_heads * (self.head_dim * self.kv_bits // 8 + 2 * 2 * self.head_dim // 64)
+        return self.n_layers * per * context
+
+
+# BASELINE.json configurations
+CONFIG1_LAYER = ModelConfig(name="config1_layer", n_layers=1, n_experts=64, vocab=4096, kv_bits=8)
+CONFIG3 = ModelConfig(name="config3_flint_shaped_48L_128E", n_layers=48, n_experts=128, kv_bits=8)
+CONFIG4 = replace(CONFIG3, name="config4_252k_4bit_kv", kv_bits=4)
+# small shapes for parity tests (same kernels, fewer layers/experts/vocab)
+TINY = ModelConfig(name="tiny", n_layers=2, n_experts=16, top_k=4, vocab=4096, kv_bits=8)
+
+
+def _quantize(w: torch.Tensor, bits: int, scale_dtype: torch.dtype):
+    if w.is_cuda:
+        from .ops import quantize_affine
+
+        return quantize_affine(w.float().contiguous(), bits, scale_dtype)
+    raise ValueError("synthetic weights are quantized on the GPU; pass a CUDA device")
+
+
+def _normal(gen: torch.Generator, shape, std: float, device) -> torch.Tensor:
+    x = torch.randn(*shape, generator=gen, device=device, dtype=torch.float32) * std
+    return x.to(torch.bfloat16).float()  # weights exist as bf16 before quantization
+
+
+def _norm_weight(gen, h, device) -> torch.Tensor:
+    return (1.0 + 0.1 * torch.randn(h, generator=gen, device=device)).to(torch.bfloat16)
+
+
+@dataclass
+class QTensor:
+    w: torch.Tensor  # int32 [N, K/8]
+    s: torch.Tensor  # fp16/bf16 [N, K/64]
+    b: torch.Tensor
+
+    def rec(self) -> abi.RecQMat:
+        return abi.RecQMat(self.w.data_ptr(), self.s.data_ptr(), self.b.data_ptr())
+
+    def nbytes(self) -> int:
+        return self.w.numel() * 4 + self.s.numel() * 2 + self.b.numel() * 2
+
+
+@dataclass
+class LayerWeights:
+    input_norm: torch.Tensor
+    post_norm: torch.Tensor
+    q: QTensor
+    k: QTensor
+    v: QTensor
+    o: QTensor
+    router: torch.Tensor
+    gate: QTensor
+    up: QTensor
+    down: QTensor
+    expert_bias: torch.Tensor | None = None
+    sinks: torch.Tensor | None = None
+    q_norm: torch.Tensor | None = None
+    k_norm: torch.Tensor | None = None
+
+    def rec(self) -> abi.RecLayerWeights:
+        def p(t):
+            return None if t is None else t.data_ptr()
+
+        return abi.RecLayerWeights(
+            input_norm=p(self.input_norm), post_norm=p(self.post_norm), q=self.q.rec(), k=self.k.rec(),
+            v=self.v.rec(), o=self.o.rec(), router=p(self.router), expert_bias=p(self.expert_bias),
+            gate=self.gate.rec(), up=self.up.rec(), down=self.down.rec(), sinks=p(self.sinks),
+            q_norm=p(self.q_norm), k_norm=p(self.k_norm))
+
+
+@dataclass
+class ModelWeights:
+    cfg: ModelConfig
+    layers: list[LayerWeights]
+    embed: QTensor
+    final_norm: torch.Tensor
+    lm_head: QTensor
+    expert_range: tuple[int, int] = (0, 0)  # experts held (expert parallelism)
+    _keep: list = field(default_factory=list)
+
+    def rec_layers(self):
+        arr = (abi.RecLayerWeights * len(self.layers))(*[L.rec() for L in self.layers])
+        self._keep.append(arr)
+        return arr
+
+    def rec_global(self) -> abi.RecGlobalWeights:
+        g = abi.RecGlobalWeights(embed=self.embed.rec(), final_norm=self.final_norm.data_ptr(),
+                                 lm_head=self.lm_head.rec())
+        self._keep.append(g)
+        return g
+
+
+def generate_weights(cfg: ModelConfig, seed: int = 0, device: str | torch.device = "cuda",
+                     expert_range: tuple[int, int] | None = None) -> ModelWeights:
+    """Random-init weights of the configuration: linear weights ~N(0, 0.02)
+    rounded to bf16, then int4 g64 affine-quantized; router bf16 ~N(0, 0.02);
+    embedding rows ~N(0, 1).  With expert_range=(lo, hi) only experts
+    [lo, hi) are materialised (expert parallelism); the rest are still drawn so
+    that every rank sees the same values."""
+    device = torch.device(device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    h, d, sd = cfg.hidden, cfg.head_dim, cfg.scale_dtype
+    lo, hi = expert_range if expert_range is not None else (0, cfg.n_experts)
+
+    def qmat(n, k, std=0.02):
+        return QTensor(*_quantize(_normal(gen, (n, k), std, device), 4, sd))
+
+    def experts(n, k):
+        parts = []
+        for e in range(cfg.n_experts):
+            w = _normal(gen, (n, k), 0.02, device)
+            if lo <= e < hi:
+                parts.append(_quantize(w, 4, sd))
+        return QTensor(*(torch.cat([p[i] for p in parts]) for i in range(3)))
+
+    layers = []
+    for _ in range(cfg.n_layers):
+        L = LayerWeights(
+            input_norm=_norm_weight(gen, h, device),
+            post_norm=_norm_weight(gen, h, device),
+            q=qmat(cfg.n_q_heads * d, h), k=qmat(cfg.n_kv_heads * d, h), v=qmat(cfg.n_kv_heads * d, h),
+            o=qmat(h, cfg.n_q_heads * d),
+            router=_normal(gen, (cfg.n_experts, h), 0.02, device).to(torch.bfloat16),
+            gate=experts(cfg.moe_inter, h), up=experts(cfg.moe_inter, h), down=experts(h, cfg.moe_inter))
+        if cfg.router_mode == abi.REC_ROUTER_SIGMOID:
+            L.expert_bias = (0.05 * torch.randn(cfg.n_experts, generator=gen, device=device)).float()
+        if cfg.flags & abi.REC_FLAG_SINKS:
+            L.sinks = torch.randn(cfg.n_q_heads, generator=gen, device=device).to(torch.bfloat16)
+        if cfg.flags & abi.REC_FLAG_QK_NORM:
+            L.q_norm = _norm_weight(gen, d, device)
+            L.k_norm = _norm_weight(gen, d, device)
+        layers.append(L)
+    embed = qmat(cfg.vocab, h, std=1.0)
+    final_norm = _norm_weight(gen, h, device)
+    lm_head = qmat(cfg.vocab, h)
+    return ModelWeights(cfg, layers, embed, final_norm, lm_head, expert_range=(lo, hi))
+
+
+@dataclass
+class KVCache:
+    """Quantized KV storage for every layer, capacity C (multiple of 256)."""
+    cfg: ModelConfig
+    capacity: int
+    layers: list[dict]
+
+    @classmethod
+    def allocate(cls, cfg: ModelConfig, capacity: int, device="cuda") -> "KVCache":
+        if capacity % 256:
+            raise ValueError("KV capacity must be a multiple of 256")
+        words = 128 * cfg.kv_bits // 32
+        layers = []
+        for _ in range(cfg.n_layers):
+            L = {}
+            for kv in ("k", "v"):
+                L[f"{kv}_codes"] = torch.zeros(cfg.n_kv_heads, capacity, words, dtype=torch.int32, device=device)
+                L[f"{kv}_scales"] = torch.zeros(cfg.n_kv_heads, capacity, 2, dtype=torch.bfloat16, device=device)
+                L[f"{kv}_biases"] = torch.zeros(cfg.n_kv_heads, capacity, 2, dtype=torch.bfloat16, device=device)
+            layers.append(L)
+        return cls(cfg, capacity, layers)
+
+    def rec(self):
+        arr = (abi.RecKVLayer * len(self.layers))(*[
+            abi.RecKVLayer(*(L[n].data_ptr() for n in ("k_codes", "k_scales", "k_biases", "v_codes", "v_scales",
+                                                       "v_biases"))) for L in self.layers])
+        return arr
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for L in self.layers for t in L.values())
+
+    def fill_random(self, upto: int, seed: int = 0, start: int = 0) -> None:
+        """Fills positions [start, upto) by quantizing synthetic K, V ~ N(0, 1)
+        (group 64 along head_dim) — the long-context caches of BASELINE.json
+        configs 2 and 4 are built this way instead of by prefill."""
+        from .ops import quantize_affine
+
+        gen = torch.Generator(device=self.layers[0]["k_codes"].device)
+        gen.manual_seed(seed)
+        dev = self.layers[0]["k_codes"].device
+        chunk = 16384
+        for L in self.layers:
+            for kv in ("k", "v"):
+                for p0 in range(start, upto, chunk):
+                    p1 = min(upto, p0 + chunk)
+                    x = torch.randn(self.cfg.n_kv_heads, p1 - p0, 128, generator=gen, device=dev)
+                    x = x.to(torch.bfloat16).float()
+                    c, s, b = quantize_affine(x, self.cfg.kv_bits, torch.bfloat16)
+                    L[f"{kv}_codes"][:, p0:p1] = c
+                    L[f"{kv}_scales"][:, p0:p1] = s
+                    L[f"{kv}_biases"][:, p0:p1] = b

@@ -1,0 +1,86 @@
+"""A decode session on one GPU: the C-ABI context with its weights, KV cache
+and workspace (all device memory owned by torch)."""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from ._lib import RecError, check, lib
+from .model import KVCache, ModelWeights
+
+
+class DecodeSession:
+    def __init__(self, weights: ModelWeights, kv: KVCache):
+        self.weights = weights
+        self.kv = kv
+        self.cfg = weights.cfg
+        self._desc = self.cfg.desc()
+        handle = C.c_void_p()
+        check(lib().rec_create(C.byref(self._desc), C.byref(handle)), "rec_create")
+        self.ctx = handle
+        self._layers = weights.rec_layers()
+        self._global = weights.rec_global()
+        check(lib().rec_set_weights(self.ctx, self._layers, len(weights.layers), C.byref(self._global)),
+              "rec_set_weights")
+        self._kv = kv.rec()
+        check(lib().rec_set_kv(self.ctx, self._kv, len(kv.layers), kv.capacity), "rec_set_kv")
+        nbytes = lib().rec_workspace_bytes(self.ctx)
+        self.workspace = torch.empty(nbytes + 256, dtype=torch.uint8, device=kv.layers[0]["k_codes"].device)
+        base = self.workspace.data_ptr()
+        aligned = (base + 255) // 256 * 256
+        check(lib().rec_set_workspace(self.ctx, C.c_void_p(aligned), nbytes), "rec_set_workspace")
+        dev = self.workspace.device
+        self.logits = torch.empty(self.cfg.vocab, dtype=torch.bfloat16, device=dev)
+        self.trace = torch.empty(self.cfg.n_layers + 1, self.cfg.hidden, dtype=torch.bfloat16, device=dev)
+        self.ids = torch.zeros(64, dtype=torch.int32, device=dev)
+        self.produced = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.usable = True
+
+    def __del__(self):
+        ctx = getattr(self, "ctx", None)
+        if ctx:
+            try:
+                lib().rec_destroy(ctx)
+            except Exception:
+                pass
+            self.ctx = None
+
+    @staticmethod
+    def _stream():
+        return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def step(self, token: int, position: int, want_trace: bool = False):
+        """One decode step; returns (logits bf16[V], trace bf16[L+1, H] or None)."""
+        check(lib().rec_decode_step(self.ctx, int(token), int(position), C.c_void_p(self.logits.data_ptr()),
+                                    C.c_void_p(self.trace.data_ptr()) if want_trace else None, self._stream()),
+              "rec_decode_step")
+        return self.logits, (self.trace if want_trace else None)
+
+    def greedy(self, token: int, position: int, count: int, eos=()):
+        """Up to `count` greedy tokens with device-side feedback; stops after
+        an EOS id.  Returns the produced ids (host list)."""
+        eos = list(eos)
+        arr = (C.c_int32 * max(1, len(eos)))(*eos) if eos else None
+        check(lib().rec_decode_greedy(self.ctx, int(token), int(position), int(count), arr, len(eos),
+                                      C.c_void_p(self.ids.data_ptr()), C.c_void_p(self.produced.data_ptr()),
+                                      self._stream()), "rec_decode_greedy")
+        self.check_status()
+        n = int(self.produced.item())
+        return self.ids[:n].tolist()
+
+    def greedy_async(self, token: int, position: int, count: int, eos=()) -> None:
+        """Enqueues a greedy packet without synchronising (ids stay on device)."""
+        eos = list(eos)
+        arr = (C.c_int32 * max(1, len(eos)))(*eos) if eos else None
+        check(lib().rec_decode_greedy(self.ctx, int(token), int(position), int(count), arr, len(eos),
+                                      C.c_void_p(self.ids.data_ptr()), C.c_void_p(self.produced.data_ptr()),
+                                      self._stream()), "rec_decode_greedy")
+
+    def check_status(self) -> None:
+        s = lib().rec_check_status(self.ctx, self._stream())
+        if s > 0:
+            self.usable = False
+            raise RecError(f"GPU synchronization failed: device status {s}")
+        if s < 0:
+            check(s, "rec_check_status")
