@@ -1,0 +1,399 @@
+#!/usr/bin/env python
+"""Decode throughput of the rec hot path on B200 (BASELINE.json metric).
+
+Workload (the Flint-shaped MoE model): 48 layers,
+hidden 2048, GQA 32/4 x 128, 128 experts top-8 with SwiGLU intermediate 768,
+vocab 151,936, all linear weights int4 g64 (fp16 scale/bias) from N(0, 0.02),
+8-bit quantized KV cache.  The prompt (1,024 ids uniform over the vocabulary,
+seed 1) is prefilled by running it through the decode step, then greedy
+tokens are decoded.  One bench step = one decoded token.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl rec|reference]
+
+Rank 0 prints one JSON line.  Multi-GPU runs (torchrun) currently run one
+independent session per GPU (replicas).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tokens/s at batch 1 vs context 1K-252K; achieved HBM GB/s per kernel"
+UNIT = "tokens/s"
+KERNEL_NAMES = ["embed", "qkv", "attn_partial", "attn_combine", "o_proj", "router", "experts_gate_up",
+                "experts_down_mix", "lm_head_argmax", "step_end"]
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=512)
+    p.add_argument("--warmup", type=int, default=16)
+    p.add_argument("--impl", choices=["rec", "reference"], default="rec")
+    p.add_argument("--context", type=int, default=1024)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--profile-phases", action="store_true",
+                   help="also record the persistent kernel's phase timeline (printed to stderr)")
+    return p.parse_args()
+
+
+def measured_peaks():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------- clocks
+class Clocks:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.file.flush()
+        rows = [r.split(",") for r in Path(self.file.name).read_text().strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------- rec arm
+def run_rec(args):
+    import torch
+    import torch.distributed as dist
+
+    from rec_b200 import abi
+    from rec_b200._lib import check, lib
+    from rec_b200.engine import FullModel, KVStorage, ResidentSampler
+    from rec_b200.model import CONFIG3, KVCache, generate_weights
+    from rec_b200.session import DecodeSession
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    cfg = CONFIG3
+    W, K = max(3, args.warmup), args.steps
+    ctx0 = args.context
+    capacity = (ctx0 + W + 2 * K + 64 + 255) // 256 * 256
+    weights = generate_weights(cfg, seed=0, device="cuda")
+    kv = KVCache.allocate(cfg, capacity)
+    sess = DecodeSession(weights, kv)
+    g = torch.Generator().manual_seed(1)
+    prompt = torch.randint(0, cfg.vocab, (ctx0,), generator=g).tolist()
+    # prefill: the prompt through the decode step
+    sess.prefill(prompt[:-1])
+    first = sess.greedy(prompt[-1], ctx0 - 1, 1)[0]
+    pos = ctx0
+
+    stream = torch.cuda.current_stream()
+    ids_dev, prod_dev = sess.ids, sess.produced
+
+    def decode(n, token, position):
+        """n greedy steps; token < 0 continues from the device state."""
+        done = 0
+        while done < n:
+            c = min(64, n - done)
+            check(lib().rec_decode_greedy(sess.ctx, token if done == 0 else -1, position + done, c, None, 0,
+                                          ids_dev.data_ptr(), prod_dev.data_ptr(), stream.cuda_stream))
+            done += c
+        return (n + 63) // 64
+
+    decode(W, first, pos)
+    pos += W
+    barrier()
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    packets = decode(K, -1, pos)
+    e1.record(stream)
+    barrier()
+    clk = clocks.stop()
+    sess.check_status()
+    pos += K
+    t_local = e0.elapsed_time(e1) / 1e3
+    t = torch.tensor([t_local], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    t_max = float(t.item())
+    kernels_per_step = 1 + cfg.n_layers * 7 + 2
+    value = K * world / t_max
+
+    phases = None
+    if args.profile_phases:
+        from rec_b200 import phases as ph
+
+        stamps = ph.capture(sess, -1, pos, steps=2)
+        pos += 2
+        phases = ph.summarize(stamps, cfg.n_layers)
+        print(json.dumps({"phases_us": phases}), file=sys.stderr, flush=True)
+
+    # ---- per-kernel times (standalone launches on this stream, CUDA events)
+    peak, peak_kind = measured_peaks()
+    per_kernel = {}
+    H, I, k = cfg.hidden, cfg.moe_inter, cfg.top_k
+    g64 = 0.5 + 4 / 64
+    kernel_bytes = {
+        "qkv": (cfg.n_q_heads + 2 * cfg.n_kv_heads) * 128 * H * g64 + H * 2 * 2,
+        "attn_partial": kv.nbytes() / cfg.n_layers * pos / capacity,
+        "o_proj": H * cfg.n_q_heads * 128 * g64 + H * 2 * 2,
+        "router": cfg.n_experts * H * 2 + H * 2 * 2,
+        "experts_gate_up": k * 2 * I * H * g64 + H * 2 + k * I * 2,
+        "experts_down_mix": k * H * I * g64 + k * I * 2 + H * 2 * 2,
+        "lm_head_argmax": cfg.vocab * H * g64 + cfg.vocab * 2 + H * 2,
+    }
+    # Each kernel is captured `reps` times into a CUDA graph (no host launch
+    # overhead between launches) and the replay is timed with CUDA events on
+    # the stream it runs on; launches are back to back, without PDL overlap.
+    reps = 50
+    for kind, name in enumerate(KERNEL_NAMES):
+        if name in ("embed", "step_end"):
+            continue
+        for _ in range(3):
+            check(lib().rec_launch_kernel(sess.ctx, kind, 0, stream.cuda_stream))
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            cs = torch.cuda.current_stream()
+            for _ in range(reps):
+                check(lib().rec_launch_kernel(sess.ctx, kind, 0, cs.cuda_stream))
+        graph.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        graph.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        del graph
+        us = a.elapsed_time(b) / reps * 1e3
+        entry = {"us": round(us, 2)}
+        if name in kernel_bytes:
+            entry["GBps"] = round(kernel_bytes[name] / (us * 1e-6) / 1e9, 1)
+        per_kernel[name] = entry
+    sess.check_status()
+    dom = "experts_gate_up"
+    ach = kernel_bytes[dom] / (per_kernel[dom]["us"] * 1e-6) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(dom)
+    roofline = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(ach / peak, 4), "traffic": traffic,
+                "algorithmic_bytes_per_launch": int(kernel_bytes[dom]), "peak_source": peak_kind}
+    step_bytes = cfg.weight_bytes_per_token() + cfg.kv_bytes_per_token(ctx0 + W + K // 2)
+    step_roofline = {"bytes_per_step": int(step_bytes),
+                     "achieved_GBps": round(step_bytes / (t_max / K) / 1e9, 1),
+                     "frac": round(step_bytes / (t_max / K) / 1e9 / peak, 4),
+                     "ideal_tokens_per_s": round(peak * 1e9 / step_bytes, 1)}
+
+    # ---- e2e through the public API: packets of 8 with a host round trip
+    engine = FullModel(weights)
+    storage = KVStorage.wrap(weights, kv, sess)
+    state = {"usable": True, "kv": storage, "metadata": None, "position": pos, "initial": ctx0,
+             "capacity": capacity, "limit": capacity, "growth_count": 0, "growth_seconds": 0.0}
+    sampler = ResidentSampler(engine)
+    token = int(sess.ids[0].item())
+    e2e_packets = max(1, min(K // 2, capacity - pos - 16) // 8)
+    sampler.block(state, token, 8, 0, temperature=0)  # warm
+    token_host = torch.tensor([token], dtype=torch.int32).pin_memory()
+    barrier()
+    t0 = time.perf_counter()
+    produced = 0
+    for _ in range(e2e_packets):
+        ids = sampler.block(state, int(token_host[0]), 8, 0, temperature=0)
+        token_host[0] = ids[-1]
+        produced += len(ids)
+    barrier()
+    e2e_t = time.perf_counter() - t0
+    e2e_local = produced / e2e_t
+    te = torch.tensor([e2e_local], device="cuda")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MIN)
+    e2e = {"value": round(float(te.item()) * world, 2), "unit": UNIT, "h2d_bytes_per_step": 8,
+           "d2h_bytes_per_step": 4 * 8 + 4, "packet_tokens": 8, "api": "rec_b200.engine.ResidentSampler.block"}
+
+    # ---- CPU baseline: the oracle on this host's cores, same weights and cache
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_same_weights(weights, kv, cfg, state["position"])
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(t_max / K * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "weights": "int4 g64 affine (fp16 scale/bias)",
+        "activations": "bf16",
+        "data": "synthetic (random-init weights of the config-3 architecture; prompt ids uniform, seed 1)",
+        "config": {"workload": cfg.name, "model": "Flint-shaped MoE, 48L, 128 experts top-8, I=768",
+                   "global_batch": world, "batch_per_gpu": 1, "seq_len": ctx0, "context_at_timing": ctx0 + W,
+                   "kv_bits": cfg.kv_bits, "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2_flush": "none needed: 1.78 GB streamed per step > 126 MB L2"},
+        "clocks": clk,
+        "e2e": e2e,
+        "gpu_launches": K * kernels_per_step + packets,
+        "roofline": roofline,
+        "step_roofline": step_roofline,
+        "kernels": per_kernel,
+        "phases_us": phases,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(out), flush=True)
+
+
+def cpu_baseline_same_weights(weights, kv, cfg, pos):
+    import torch
+
+    import oracle
+    from oracle.host import HostKV, HostModel
+
+    threads = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    oracle.lib()
+    host = HostModel(weights)
+    hkv = HostKV.from_device(cfg, kv)
+    token = 1
+    n, t0 = 0, time.perf_counter()
+    while n < 2 or (time.perf_counter() - t0 < 10 and n < 8):
+        logits, _ = host.step(hkv, token, pos + n, want_trace=False)
+        token = oracle.argmax_bf16(logits)
+        n += 1
+    dt = time.perf_counter() - t0
+    del host
+    return {"value": round(n / dt, 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{n} full decode tokens of the same model and cache on the host (oracle/rec_oracle.c, "
+                      f"OpenMP over rows), {dt:.1f} s"}
+
+
+# ---------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    """The reference's CPU path for this hot path (oracle/rec_oracle.c; MLX is
+    not installable here) on the host cores, same config and metric."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    import oracle
+    from oracle.host import HostModel
+    from oracle.synthetic import random_model
+    from rec_b200.model import CONFIG3
+
+    cfg = CONFIG3
+    oracle.lib()
+    model = random_model(cfg, seed=0)
+    host = HostModel(model)
+    ctx0 = args.context
+    W, K = max(3, args.warmup), args.steps
+    capacity = (ctx0 + 64 + 255) // 256 * 256
+    hkv = host.new_kv(capacity)
+    # cache: prefilled by quantizing synthetic K, V ~ N(0, 1)
+    import numpy as np
+
+    rng = np.random.default_rng(4)
+    for L in hkv.layers:
+        for name in ("k", "v"):
+            x = rng.standard_normal((cfg.n_kv_heads, ctx0, 128), dtype=np.float32)
+            x = oracle.bf16_to_f32(oracle.f32_to_bf16(x))
+            c, s, b = oracle.quantize(x, cfg.kv_bits, 1)
+            L[f"{name}_codes"][:, :ctx0] = c
+            L[f"{name}_scales"][:, :ctx0] = s
+            L[f"{name}_biases"][:, :ctx0] = b
+    token, pos = 1, ctx0
+    t_first = time.perf_counter()
+    logits, _ = host.step(hkv, token, pos, want_trace=False)
+    t1 = time.perf_counter() - t_first
+    token = oracle.argmax_bf16(logits)
+    pos += 1
+    budget = 150.0
+    n_exec = int(max(2, min(K, budget // max(t1, 1e-3))))
+    n_warm = min(W - 1, 1)
+    for _ in range(n_warm):
+        logits, _ = host.step(hkv, token, pos, want_trace=False)
+        token = oracle.argmax_bf16(logits)
+        pos += 1
+    t0 = time.perf_counter()
+    for _ in range(n_exec):
+        logits, _ = host.step(hkv, token, pos, want_trace=False)
+        token = oracle.argmax_bf16(logits)
+        pos += 1
+    dt = time.perf_counter() - t0
+    value = n_exec / dt
+    sample = (f"{n_exec} of the {K} requested decode tokens executed (bounded sample), config-3 shapes with "
+              f"random int4 codes, {ctx0}-token 8-bit cache; oracle/rec_oracle.c with {threads} OpenMP threads")
+    out = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": 0,
+           "steps": K, "warmup": W, "ms_per_step": round(dt / n_exec * 1e3, 2), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": cfg.name, "seq_len": ctx0, "kv_bits": cfg.kv_bits},
+           "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                            "sample": sample},
+           "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_rec(args)
+
+
+if __name__ == "__main__":
+    main()

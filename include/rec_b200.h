@@ -139,11 +139,28 @@ REC_API int rec_decode_step(RecCtx* ctx, int32_t token, int32_t position, void* 
                             void* trace_dev, void* stream);
 /* Up to `count` greedy steps with the argmax fed back on the device; stops
  * after an EOS id.  ids_dev int32[count] receives the produced ids, produced_dev
- * int32[1] their number.  Replaces ResidentSampler.block for temperature 0
- * (sampling.py:62-169, resident_block.py:12-88). */
+ * int32[1] their number.  token = -1 continues from the token and position
+ * the device holds after the previous call (no host round trip).  Replaces
+ * ResidentSampler.block for temperature 0 (sampling.py:62-169,
+ * resident_block.py:12-88). */
 REC_API int rec_decode_greedy(RecCtx* ctx, int32_t token, int32_t position, int32_t count,
                               const int32_t* eos, int32_t n_eos, int32_t* ids_dev,
                               int32_t* produced_dev, void* stream);
+/* Kernels of one step, in launch order; layer kernels repeat per layer. */
+enum {
+  REC_K_EMBED = 0, REC_K_QKV = 1, REC_K_ATTN = 2, REC_K_COMBINE = 3, REC_K_OPROJ = 4, REC_K_ROUTER = 5,
+  REC_K_GATEUP = 6, REC_K_DOWN = 7, REC_K_HEAD = 8, REC_K_STEP_END = 9
+};
+/* Launches one kernel of the step on `stream` against the session's current
+ * state (profiling and per-kernel timing; no reference counterpart: the
+ * reference's step is a single Metal dispatch). */
+REC_API int rec_launch_kernel(RecCtx* ctx, int32_t kind, int32_t layer, void* stream);
+/* Optional phase timeline of the persistent decode kernel: when set, every
+ * CTA stamps %globaltimer (ns) at each grid-barrier arrival and release into
+ * buf_dev as uint64 [barrier][cta][2]; a step has 6*n_layers + 1 barriers.
+ * Counterpart of the reference's PROFILE schedule flag
+ * (megakernel.py:151,1269-1299).  NULL disables. */
+REC_API int rec_set_profile(RecCtx* ctx, void* buf_dev, size_t entries);
 /* Reads the device status word (synchronises `stream`).  Non-zero marks the
  * session unusable. */
 REC_API int rec_check_status(RecCtx* ctx, void* stream);

@@ -12,15 +12,20 @@ from . import lib
 
 
 def _np(t) -> np.ndarray:
-    """torch tensor -> contiguous host numpy (uint16 for 16-bit, uint32 for int32)."""
+    """torch tensor (or numpy array) -> contiguous host numpy (uint16 for
+    16-bit, uint32 for int32).  The array shares memory with a fresh host copy
+    of the tensor; no second copy is made."""
+    if isinstance(t, np.ndarray):
+        return np.ascontiguousarray(t)
     import torch
 
-    t = t.detach().contiguous().cpu()
+    t = t.detach().contiguous()
+    t = t.cpu() if t.is_cuda else t.clone()
     if t.dtype in (torch.bfloat16, torch.float16):
-        return t.view(torch.int16).numpy().view(np.uint16).copy()
+        return t.view(torch.int16).numpy().view(np.uint16)
     if t.dtype == torch.int32:
-        return t.numpy().view(np.uint32).copy()
-    return t.numpy().copy()
+        return t.numpy().view(np.uint32)
+    return t.numpy()
 
 
 class HostModel:

@@ -216,8 +216,7 @@ typedef struct {
 
 static void prep_chunk(const uint16_t* x32, ChunkX* cx) {
   static const float lo_scale[4] = {1.0f, 0.0625f, 0.00390625f, 0.000244140625f};
-  static const float hi_scale[4] = {1.52587890625e-05f, 0.00390625f, 0.000244140625f,
-                                    1.52587890625e-05f};
+  static const float hi_scale[4] = {0.0625f, 0.00390625f, 0.000244140625f, 1.52587890625e-05f};
   float xl = 0.0f, xh = 0.0f;
   for (int k = 0; k < 4; ++k)
     for (int i = 0; i < 4; ++i) {
@@ -237,7 +236,7 @@ static float chunk_dot(const uint32_t* w4, const ChunkX* cx) {
     uint32_t a = w4[k], a12 = a >> 12;
     float fl[4] = {u2f((a & 0xFu) | M), u2f((a & 0xF0u) | M), u2f((a & 0xF00u) | M),
                    u2f((a & 0xF000u) | M)};
-    float fh[4] = {u2f((a & 0xF0000u) | M), u2f((a12 & 0xF00u) | M), u2f((a12 & 0xF000u) | M),
+    float fh[4] = {u2f((a12 & 0xF0u) | M), u2f((a12 & 0xF00u) | M), u2f((a12 & 0xF000u) | M),
                    u2f((a12 & 0xF0000u) | M)};
     for (int i = 0; i < 4; ++i) {
       fl[i] = fl[i] - 8388608.0f;

@@ -30,6 +30,8 @@ _SIGNATURES = {
     "rec_decode_greedy": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_int32), C.c_int32,
                                     C.c_void_p, C.c_void_p, C.c_void_p]),
     "rec_check_status": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "rec_launch_kernel": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
+    "rec_set_profile": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
 }
 
 

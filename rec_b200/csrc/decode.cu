@@ -13,8 +13,11 @@
 #include <set>
 #include <vector>
 
+#include <cstdlib>
+
 #include "attn.cuh"
 #include "capi_common.h"
+#include "mega.cuh"
 #include "moe.cuh"
 
 namespace rec {
@@ -36,10 +39,13 @@ enum Ctrl : int {
 constexpr int kMaxPacket = 64;
 constexpr int kMaxEos = 8;
 
+// token < 0: continue from the token and position held on the device.
 __global__ void k_set_step(int* ctl, int token, int position, int n_eos, const int4 eos_lo, const int4 eos_hi) {
   if (threadIdx.x == 0) {
-    ctl[kCtlToken] = token;
-    ctl[kCtlPosition] = position;
+    if (token >= 0) {
+      ctl[kCtlToken] = token;
+      ctl[kCtlPosition] = position;
+    }
     ctl[kCtlActive] = 1;
     ctl[kCtlProduced] = 0;
     ctl[kCtlStep] = 0;
@@ -149,6 +155,12 @@ struct RecCtx {
   int grid = 148;
   cudaStream_t cap_stream = nullptr;
   cudaGraphExec_t step_exec = nullptr;
+  // persistent schedule
+  bool use_mega = true;
+  MegaLayer* mega_layers = nullptr;  // device table, in the workspace
+  unsigned* mega_cnt = nullptr;      // [2] grid barrier + abort, [Hq] heads, [Hq*n_super] supers
+  unsigned long long* prof = nullptr;  // optional phase timeline
+  size_t prof_entries = 0;
 };
 
 namespace {
@@ -161,8 +173,8 @@ struct Layout {
 };
 
 enum Region {
-  rCtl, rCounters, rH, rQkv, rAttn, rXn, rAct, rLogits, rTrace, rRouter, rIds, rWts, rCandV, rCandI, rPartials,
-  rSupers, rRope, rCount
+  rCtl, rCounters, rMegaCnt, rH, rQkv, rAttn, rXn, rAct, rLogits, rTrace, rRouter, rIds, rWts, rCandV, rCandI,
+  rPartials, rSupers, rMegaLayers, rRope, rCount
 };
 
 Layout layout_of(const RecCtx* c) {
@@ -173,6 +185,8 @@ Layout layout_of(const RecCtx* c) {
   size_t sz[rCount];
   sz[rCtl] = kCtlInts * 4;
   sz[rCounters] = (64 + d.n_q_heads) * 4;
+  sz[rMegaCnt] = size_t(2 + d.n_q_heads + d.n_q_heads * nsup) * 4;
+  sz[rMegaLayers] = size_t(d.n_layers) * sizeof(MegaLayer);
   sz[rH] = size_t(d.hidden) * 2;
   sz[rQkv] = size_t(d.n_q_heads + 2 * d.n_kv_heads) * 128 * 2;
   sz[rAttn] = size_t(d.n_q_heads) * 128 * 2;
@@ -198,22 +212,27 @@ Layout layout_of(const RecCtx* c) {
   return L;
 }
 
+// Kernels of one decode step, in launch order (per layer: kKQkv..kKDown).
+enum KernelKind { kKEmbed = 0, kKQkv, kKAttn, kKCombine, kKOproj, kKRouter, kKGateUp, kKDown, kKHead, kKStepEnd,
+                  kKCount };
+
 template <int SD>
-cudaError_t enqueue_step_sd(RecCtx* c, cudaStream_t st) {
+cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool pdl) {
   const RecModelDesc& d = c->d;
   const int H = d.hidden;
   const int grid = c->grid;
-  cudaError_t e;
-  e = launch(k_embed<SD>, 1, 256, 0, st, false, c->ctl, QMatDev{(const uint32_t*)c->g.embed.w,
-             (const uint16_t*)c->g.embed.scales, (const uint16_t*)c->g.embed.biases}, H, d.vocab, c->capacity,
-             c->token_base, c->h, c->trace);
-  if (e != cudaSuccess) return e;
+  cudaError_t e = cudaSuccess;
   int* status = c->ctl + kCtlStatus;
-  for (int li = 0; li < d.n_layers; ++li) {
+  if (kind == kKEmbed)
+    return launch(k_embed<SD>, 1, 256, 0, st, false, c->ctl, QMatDev{(const uint32_t*)c->g.embed.w,
+                  (const uint16_t*)c->g.embed.scales, (const uint16_t*)c->g.embed.biases}, H, d.vocab, c->capacity,
+                  c->token_base, c->h, c->trace);
+  if (kind == kKStepEnd) return launch(k_step_end, 1, 32, 0, st, pdl, c->ctl);
+  if (kind != kKHead) {
     const RecLayerWeights& L = c->layers[li];
     const RecKVLayer& kv = c->kv[li];
-    // 1. RMSNorm + QKV projection
-    {
+    switch (kind) {
+    case kKQkv: {  // RMSNorm + QKV projection
       GemvArgs a = {};
       a.mat[0] = {(const uint32_t*)L.q.w, (const uint16_t*)L.q.scales, (const uint16_t*)L.q.biases};
       a.mat[1] = {(const uint32_t*)L.k.w, (const uint16_t*)L.k.scales, (const uint16_t*)L.k.biases};
@@ -227,13 +246,13 @@ cudaError_t enqueue_step_sd(RecCtx* c, cudaStream_t st) {
       a.eps = d.rms_eps;
       a.out = c->qkv;
       a.status = status;
-      a.pdl = 1;
+      a.pdl = pdl;
       using Kq = GemvSmem<2048, gemv_rs<2048>(), 3>;
-      e = launch(k_gemv<2048, SD, gemv_rs<2048>(), 3, kEpiStore>, grid, kThreads, sizeof(Kq), st, true, a);
-      if (e != cudaSuccess) return e;
+      e = launch(k_gemv<2048, SD, gemv_rs<2048>(), 3, kEpiStore>, grid, kThreads, sizeof(Kq), st, pdl, a);
+      return e;
     }
-    // 2. attention partials (+ RoPE, quantize-on-append) and combine
-    {
+    case kKAttn:
+    case kKCombine: {  // attention partials (+ RoPE, quantize-on-append) / combine
       AttnArgs a = {};
       a.qkv = c->qkv;
       a.k_codes = (uint32_t*)kv.k_codes;
@@ -261,27 +280,24 @@ cudaError_t enqueue_step_sd(RecCtx* c, cudaStream_t st) {
       a.n_super_max = c->n_super_max;
       a.final_merge = 1;
       a.status = status;
-      a.pdl = 1;
+      a.pdl = pdl;
+      a.pdl = pdl;
       const int agrid = 2 * sm_count();
-      if (d.kv_bits == 4)
-        e = launch(k_attn_partial<4>, agrid, 128, sizeof(AttnSmem<4>), st, true, a);
-      else
-        e = launch(k_attn_partial<8>, agrid, 128, sizeof(AttnSmem<8>), st, true, a);
-      if (e != cudaSuccess) return e;
+      if (kind == kKAttn)
+        return d.kv_bits == 4 ? launch(k_attn_partial<4>, agrid, 128, sizeof(AttnSmem<4>), st, pdl, a)
+                              : launch(k_attn_partial<8>, agrid, 128, sizeof(AttnSmem<8>), st, pdl, a);
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(d.n_q_heads, std::max(1, c->n_super_max));
       cfg.blockDim = dim3(32);
       cfg.stream = st;
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      e = cudaLaunchKernelEx(&cfg, k_attn_combine, a);
-      if (e != cudaSuccess) return e;
+      return cudaLaunchKernelEx(&cfg, k_attn_combine, a);
     }
-    // 3. O projection + residual
-    {
+    case kKOproj: {  // O projection + residual
       GemvArgs a = {};
       a.mat[0] = {(const uint32_t*)L.o.w, (const uint16_t*)L.o.scales, (const uint16_t*)L.o.biases};
       a.rows[0] = H;
@@ -289,18 +305,17 @@ cudaError_t enqueue_step_sd(RecCtx* c, cudaStream_t st) {
       a.x = c->attn;
       a.resid = c->h;
       a.status = status;
-      a.pdl = 1;
+      a.pdl = pdl;
       if (d.n_q_heads * 128 == 4096) {
         using Ko = GemvSmem<4096, gemv_rs<4096>(), 3>;
-        e = launch(k_gemv<4096, SD, gemv_rs<4096>(), 3, kEpiResidual>, grid, kThreads, sizeof(Ko), st, true, a);
+        e = launch(k_gemv<4096, SD, gemv_rs<4096>(), 3, kEpiResidual>, grid, kThreads, sizeof(Ko), st, pdl, a);
       } else {
         using Ko = GemvSmem<2048, gemv_rs<2048>(), 3>;
-        e = launch(k_gemv<2048, SD, gemv_rs<2048>(), 3, kEpiResidual>, grid, kThreads, sizeof(Ko), st, true, a);
+        e = launch(k_gemv<2048, SD, gemv_rs<2048>(), 3, kEpiResidual>, grid, kThreads, sizeof(Ko), st, pdl, a);
       }
-      if (e != cudaSuccess) return e;
+      return e;
     }
-    // 4. router
-    {
+    case kKRouter: {
       RouterArgs a = {};
       a.h = c->h;
       a.norm_w = (const uint16_t*)L.post_norm;
@@ -316,12 +331,11 @@ cudaError_t enqueue_step_sd(RecCtx* c, cudaStream_t st) {
       a.wts = c->wts;
       a.counter = c->counters + 1;
       a.status = status;
-      a.pdl = 1;
-      e = launch(k_router<2048>, (d.n_experts + kWarps - 1) / kWarps, kThreads, sizeof(RouterSmem<2048>), st, true, a);
-      if (e != cudaSuccess) return e;
+      a.pdl = pdl;
+      e = launch(k_router<2048>, (d.n_experts + kWarps - 1) / kWarps, kThreads, sizeof(RouterSmem<2048>), st, pdl, a);
+      return e;
     }
-    // 5. experts gate/up + SwiGLU
-    {
+    case kKGateUp: {  // experts gate/up + SwiGLU
       GateUpArgs a = {};
       a.gate = {(const uint32_t*)L.gate.w, (const uint16_t*)L.gate.scales, (const uint16_t*)L.gate.biases};
       a.up = {(const uint32_t*)L.up.w, (const uint16_t*)L.up.scales, (const uint16_t*)L.up.biases};
@@ -333,13 +347,12 @@ cudaError_t enqueue_step_sd(RecCtx* c, cudaStream_t st) {
       a.expert_hi = d.n_experts;
       a.act = c->act;
       a.status = status;
-      a.pdl = 1;
+      a.pdl = pdl;
       constexpr int RSP = 16;
-      e = launch(k_gateup<SD, RSP, 3>, grid, kThreads, sizeof(GateUpSmem<RSP, 3>), st, true, a);
-      if (e != cudaSuccess) return e;
+      e = launch(k_gateup<SD, RSP, 3>, grid, kThreads, sizeof(GateUpSmem<RSP, 3>), st, pdl, a);
+      return e;
     }
-    // 6. experts down + bf16 mix + residual
-    {
+    case kKDown: {  // experts down + bf16 mix + residual
       DownArgs a = {};
       a.down = {(const uint32_t*)L.down.w, (const uint16_t*)L.down.scales, (const uint16_t*)L.down.biases};
       a.act = c->act;
@@ -352,20 +365,22 @@ cudaError_t enqueue_step_sd(RecCtx* c, cudaStream_t st) {
       a.h = c->h;
       a.trace_row = c->trace + size_t(li + 1) * H;
       a.status = status;
-      a.pdl = 1;
+      a.pdl = pdl;
       const int dgrid = std::max(grid, H / (2 * DownSmem<768>::RMAX / 2));
       switch (d.moe_inter) {
-        case 256: e = launch(k_down<256, SD>, dgrid, kThreads, sizeof(DownSmem<256>), st, true, a); break;
-        case 512: e = launch(k_down<512, SD>, dgrid, kThreads, sizeof(DownSmem<512>), st, true, a); break;
-        case 768: e = launch(k_down<768, SD>, dgrid, kThreads, sizeof(DownSmem<768>), st, true, a); break;
-        case 1024: e = launch(k_down<1024, SD>, dgrid, kThreads, sizeof(DownSmem<1024>), st, true, a); break;
+        case 256: e = launch(k_down<256, SD>, dgrid, kThreads, sizeof(DownSmem<256>), st, pdl, a); break;
+        case 512: e = launch(k_down<512, SD>, dgrid, kThreads, sizeof(DownSmem<512>), st, pdl, a); break;
+        case 768: e = launch(k_down<768, SD>, dgrid, kThreads, sizeof(DownSmem<768>), st, pdl, a); break;
+        case 1024: e = launch(k_down<1024, SD>, dgrid, kThreads, sizeof(DownSmem<1024>), st, pdl, a); break;
         default: return cudaErrorInvalidValue;
       }
-      if (e != cudaSuccess) return e;
+      return e;
+    }
+    default:
+      return cudaErrorInvalidValue;
     }
   }
-  // final norm + lm_head + argmax
-  {
+  {  // final norm + lm_head + argmax
     GemvArgs a = {};
     a.mat[0] = {(const uint32_t*)c->g.lm_head.w, (const uint16_t*)c->g.lm_head.scales,
                 (const uint16_t*)c->g.lm_head.biases};
@@ -380,12 +395,20 @@ cudaError_t enqueue_step_sd(RecCtx* c, cudaStream_t st) {
     a.counter = c->counters + 0;
     a.token_out = c->ctl + kCtlArgmax;
     a.status = status;
-    a.pdl = 1;
+    a.pdl = pdl;
     using Kh = GemvSmem<2048, gemv_rs<2048>(), 3>;
-    e = launch(k_gemv<2048, SD, gemv_rs<2048>(), 3, kEpiArgmax>, grid, kThreads, sizeof(Kh), st, true, a);
-    if (e != cudaSuccess) return e;
+    return launch(k_gemv<2048, SD, gemv_rs<2048>(), 3, kEpiArgmax>, grid, kThreads, sizeof(Kh), st, pdl, a);
   }
-  return launch(k_step_end, 1, 32, 0, st, true, c->ctl);
+}
+
+template <int SD>
+cudaError_t enqueue_step_sd(RecCtx* c, cudaStream_t st) {
+  cudaError_t e = enqueue_kernel_sd<SD>(c, kKEmbed, 0, st, false);
+  for (int li = 0; li < c->d.n_layers && e == cudaSuccess; ++li)
+    for (int k = kKQkv; k <= kKDown && e == cudaSuccess; ++k) e = enqueue_kernel_sd<SD>(c, k, li, st, true);
+  if (e == cudaSuccess) e = enqueue_kernel_sd<SD>(c, kKHead, 0, st, true);
+  if (e == cudaSuccess) e = enqueue_kernel_sd<SD>(c, kKStepEnd, 0, st, true);
+  return e;
 }
 
 cudaError_t enqueue_step(RecCtx* c, cudaStream_t st) {
@@ -536,8 +559,30 @@ REC_API int rec_set_workspace(RecCtx* c, void* ws, size_t bytes) {
   c->partials = reinterpret_cast<float*>(b + L.off[rPartials]);
   c->supers = reinterpret_cast<float*>(b + L.off[rSupers]);
   c->rope = reinterpret_cast<float*>(b + L.off[rRope]);
+  c->mega_cnt = reinterpret_cast<unsigned*>(b + L.off[rMegaCnt]);
+  c->mega_layers = reinterpret_cast<MegaLayer*>(b + L.off[rMegaLayers]);
   // control block and counters start at zero
   REC_CHECK_CUDA(cudaMemset(b, 0, L.off[rH]));
+  // layer table of the persistent kernel
+  {
+    const bool qk = (c->d.flags & REC_FLAG_QK_NORM) != 0, sinks = (c->d.flags & REC_FLAG_SINKS) != 0;
+    auto q = [](const RecQMat& m) {
+      return QMatDev{(const uint32_t*)m.w, (const uint16_t*)m.scales, (const uint16_t*)m.biases};
+    };
+    std::vector<MegaLayer> t(c->d.n_layers);
+    for (int i = 0; i < c->d.n_layers; ++i) {
+      const RecLayerWeights& W = c->layers[i];
+      const RecKVLayer& K = c->kv[i];
+      t[i] = MegaLayer{q(W.q), q(W.k), q(W.v), q(W.o), q(W.gate), q(W.up), q(W.down),
+                       (const uint16_t*)W.input_norm, (const uint16_t*)W.post_norm, (const uint16_t*)W.router,
+                       (const float*)W.expert_bias, sinks ? (const uint16_t*)W.sinks : nullptr,
+                       qk ? (const uint16_t*)W.q_norm : nullptr, qk ? (const uint16_t*)W.k_norm : nullptr,
+                       (uint32_t*)K.k_codes, (uint16_t*)K.k_scales, (uint16_t*)K.k_biases, (uint32_t*)K.v_codes,
+                       (uint16_t*)K.v_scales, (uint16_t*)K.v_biases};
+    }
+    if (c->has_weights)
+      REC_CHECK_CUDA(cudaMemcpy(c->mega_layers, t.data(), t.size() * sizeof(MegaLayer), cudaMemcpyHostToDevice));
+  }
   // RoPE table: cos/sin of pos * theta^(-i/64) in double, rounded to float
   std::vector<float> cs(size_t(c->capacity) * 128);
   for (int p = 0; p < c->capacity; ++p)
@@ -563,7 +608,88 @@ static int check_ready(RecCtx* c) {
     set_error("session not configured (weights, KV and workspace are required)");
     return REC_ESTATE;
   }
-  return ensure_graph(c);
+  const char* sched = std::getenv("REC_SCHEDULE");
+  c->use_mega = !(sched && std::strcmp(sched, "graph") == 0);
+  return c->use_mega ? REC_OK : ensure_graph(c);
+}
+
+// One cooperative launch of the persistent kernel for `steps` tokens.
+template <int SD, int I>
+static cudaError_t launch_mega_t(RecCtx* c, int steps, cudaStream_t st) {
+  const RecModelDesc& d = c->d;
+  MegaArgs A = {};
+  A.layers = c->mega_layers;
+  A.n_layers = d.n_layers;
+  A.H = d.hidden;
+  A.hq = d.n_q_heads;
+  A.hkv = d.n_kv_heads;
+  A.E = d.n_experts;
+  A.k = d.top_k;
+  A.I = d.moe_inter;
+  A.V = d.vocab;
+  A.kv_bits = d.kv_bits;
+  A.router_mode = d.router_mode;
+  A.capacity = c->capacity;
+  A.n_super_max = c->n_super_max;
+  A.eps = d.rms_eps;
+  A.embed = {(const uint32_t*)c->g.embed.w, (const uint16_t*)c->g.embed.scales, (const uint16_t*)c->g.embed.biases};
+  A.lm_head = {(const uint32_t*)c->g.lm_head.w, (const uint16_t*)c->g.lm_head.scales,
+               (const uint16_t*)c->g.lm_head.biases};
+  A.final_norm = (const uint16_t*)c->g.final_norm;
+  A.rope = c->rope;
+  A.ctl = c->ctl;
+  A.gbar = c->mega_cnt;
+  A.cnt = c->mega_cnt + 2;
+  A.h = c->h;
+  A.qkv = c->qkv;
+  A.attn = c->attn;
+  A.act = c->act;
+  A.logits = c->logits;
+  A.trace = c->trace;
+  A.partials = c->partials;
+  A.supers = c->supers;
+  A.router_logits = c->router_logits;
+  A.cand_val = c->cand_val;
+  A.cand_idx = c->cand_idx;
+  A.steps = steps;
+  const size_t need = size_t(steps) * (6 * d.n_layers + 1) * c->grid * 2;
+  A.prof = (c->prof && c->prof_entries >= need) ? c->prof : nullptr;
+  auto kern = k_decode_mega<SD, I>;
+  const size_t smem = sizeof(MegaSmem);
+  static std::mutex mu;
+  static std::set<const void*> configured;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    if (!configured.count(reinterpret_cast<const void*>(kern))) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+      if (e != cudaSuccess) return e;
+      configured.insert(reinterpret_cast<const void*>(kern));
+    }
+  }
+  cudaError_t e = cudaMemsetAsync(c->mega_cnt, 0, 2 * sizeof(unsigned), st);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(c->grid);
+  cfg.blockDim = dim3(kMegaThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, A);
+}
+
+static cudaError_t launch_mega(RecCtx* c, int steps, cudaStream_t st) {
+  const bool fp16 = c->d.scale_dtype == REC_SCALE_FP16;
+  switch (c->d.moe_inter) {
+    case 256: return fp16 ? launch_mega_t<0, 256>(c, steps, st) : launch_mega_t<1, 256>(c, steps, st);
+    case 512: return fp16 ? launch_mega_t<0, 512>(c, steps, st) : launch_mega_t<1, 512>(c, steps, st);
+    case 768: return fp16 ? launch_mega_t<0, 768>(c, steps, st) : launch_mega_t<1, 768>(c, steps, st);
+    case 1024: return fp16 ? launch_mega_t<0, 1024>(c, steps, st) : launch_mega_t<1, 1024>(c, steps, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 REC_API int rec_decode_step(RecCtx* c, int32_t token, int32_t position, void* logits_dev, void* trace_dev,
@@ -578,7 +704,8 @@ REC_API int rec_decode_step(RecCtx* c, int32_t token, int32_t position, void* lo
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   k_set_step<<<1, 32, 0, st>>>(c->ctl, token, position, 0, make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0));
   REC_CHECK_CUDA(cudaGetLastError());
-  REC_CHECK_CUDA(cudaGraphLaunch(c->step_exec, st));
+  if (c->use_mega) REC_CHECK_CUDA(launch_mega(c, 1, st));
+  else REC_CHECK_CUDA(cudaGraphLaunch(c->step_exec, st));
   if (logits_dev)
     REC_CHECK_CUDA(cudaMemcpyAsync(logits_dev, c->logits, size_t(c->d.vocab) * 2, cudaMemcpyDeviceToDevice, st));
   if (trace_dev)
@@ -593,7 +720,7 @@ REC_API int rec_decode_greedy(RecCtx* c, int32_t token, int32_t position, int32_
   if (rc) return rc;
   REC_CHECK_ARG(count >= 1 && count <= kMaxPacket, "packet must contain between 1 and %d tokens", kMaxPacket);
   REC_CHECK_ARG(n_eos >= 0 && n_eos <= kMaxEos && (n_eos == 0 || eos), "between 0 and %d EOS ids", kMaxEos);
-  REC_CHECK_ARG(token >= 0 && token < c->d.vocab, "token %d outside the vocabulary", token);
+  REC_CHECK_ARG(token >= -1 && token < c->d.vocab, "token %d outside the vocabulary", token);
   if (position < c->token_base || position + count - c->token_base > c->capacity) {
     set_error("Decode context limit exhausted");
     return REC_ELIMIT;
@@ -604,11 +731,34 @@ REC_API int rec_decode_greedy(RecCtx* c, int32_t token, int32_t position, int32_
   k_set_step<<<1, 32, 0, st>>>(c->ctl, token, position, n_eos, make_int4(e8[0], e8[1], e8[2], e8[3]),
                                make_int4(e8[4], e8[5], e8[6], e8[7]));
   REC_CHECK_CUDA(cudaGetLastError());
-  for (int i = 0; i < count; ++i) REC_CHECK_CUDA(cudaGraphLaunch(c->step_exec, st));
+  if (c->use_mega) REC_CHECK_CUDA(launch_mega(c, count, st));
+  else
+    for (int i = 0; i < count; ++i) REC_CHECK_CUDA(cudaGraphLaunch(c->step_exec, st));
   if (ids_dev)
     REC_CHECK_CUDA(cudaMemcpyAsync(ids_dev, c->ctl + kCtlRecorded, size_t(count) * 4, cudaMemcpyDeviceToDevice, st));
   if (produced_dev)
     REC_CHECK_CUDA(cudaMemcpyAsync(produced_dev, c->ctl + kCtlProduced, 4, cudaMemcpyDeviceToDevice, st));
+  return REC_OK;
+}
+
+REC_API int rec_launch_kernel(RecCtx* c, int32_t kind, int32_t layer, void* stream) {
+  int rc = check_ready(c);
+  if (rc) return rc;
+  REC_CHECK_ARG(kind >= 0 && kind < kKCount, "unknown kernel kind %d", kind);
+  rc = ensure_graph(c);
+  if (rc) return rc;
+  REC_CHECK_ARG(layer >= 0 && layer < c->d.n_layers, "layer %d out of range", layer);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = c->d.scale_dtype == REC_SCALE_FP16 ? enqueue_kernel_sd<0>(c, kind, layer, st, false)
+                                                     : enqueue_kernel_sd<1>(c, kind, layer, st, false);
+  REC_CHECK_CUDA(e);
+  return REC_OK;
+}
+
+REC_API int rec_set_profile(RecCtx* c, void* buf_dev, size_t entries) {
+  REC_CHECK_ARG(c, "null context");
+  c->prof = static_cast<unsigned long long*>(buf_dev);
+  c->prof_entries = buf_dev ? entries : 0;
   return REC_OK;
 }
 

@@ -1,0 +1,1130 @@
+// Persistent decode kernel: the whole decode step (or a packet of steps) in
+// one cooperative launch with one CTA per SM.
+//
+// Warp 0 of every CTA is a producer: it walks the step's fixed schedule of
+// weight (and KV) chunks for this CTA and streams them with cp.async.bulk into
+// a ring of shared-memory slots (full/empty mbarriers).  Weights do not depend
+// on activations, so the producer runs ahead across phase and layer
+// boundaries; only the expert chunks wait for this layer's routing.  Warps
+// 1..8 are consumers: they take the chunks in the same order and run the same
+// math as the standalone kernels (gemv.cuh, attn.cuh, moe.cuh), in the same
+// canonical order, so results are bit-identical to them and to the oracle.
+//
+// Phases of a layer, separated by bounded software grid barriers:
+//   Q  RMSNorm + QKV rows                       -> qkv
+//   A  split-KV attention items (+RoPE, quantize-on-append); the last CTA to
+//      finish a super-chunk / head merges it (log-sum-exp)   -> attn
+//   O  O rows + residual (rows owned like D)   -> h
+//   R  RMSNorm + router logits                 -> router_logits
+//   G  expert gate/up pairs + SwiGLU (selection recomputed per CTA) -> act
+//   D  expert down rows for all k experts + bf16 mix + residual -> h, trace
+// then H (final RMSNorm + lm_head + CTA argmax) and E (global argmax, done
+// redundantly by every CTA, so the next token needs no extra barrier).
+//
+// Reference counterpart: the persistent Metal megakernel
+// (engine/src/rec_mlx/kernels/megakernel.py:823-975) with its spin-capped
+// grid barrier (megakernel.py:137-159) and 8-token resident loop
+// (resident_block.py:62-88).
+#pragma once
+#include "attn.cuh"
+#include "moe.cuh"
+
+namespace rec {
+
+constexpr int kMegaCons = 8;                        // consumer warps
+constexpr int kMegaThreads = 32 * (kMegaCons + 1);  // + producer warp
+constexpr int kSlotBytes = 36864;
+constexpr int kSlots = 4;
+constexpr int kBarCons = 1;   // named barrier: all consumer warps
+constexpr int kBarAttn = 6;   // named barrier: consumer warps 0..3
+constexpr int kBarTeam0 = 2;  // named barriers 2..5: warp pairs (K = 4096 rows)
+constexpr int kQRows = 32;    // rows per Q / H chunk (K = 2048)
+constexpr int kORows = 16;    // rows per O chunk (K = 4096)
+constexpr int kGPairs = 16;   // gate/up pairs per G chunk
+constexpr int kDExperts = 4;  // experts per D chunk
+constexpr int kDRowsMax = 16; // output rows per CTA in O / D
+
+struct MegaLayer {
+  QMatDev q, k, v, o, gate, up, down;
+  const uint16_t* input_norm;
+  const uint16_t* post_norm;
+  const uint16_t* router;
+  const float* expert_bias;
+  const uint16_t* sinks;
+  const uint16_t* q_norm;
+  const uint16_t* k_norm;
+  uint32_t* k_codes;
+  uint16_t* k_scales;
+  uint16_t* k_biases;
+  uint32_t* v_codes;
+  uint16_t* v_scales;
+  uint16_t* v_biases;
+};
+
+struct MegaArgs {
+  const MegaLayer* layers;
+  int n_layers, H, hq, hkv, E, k, I, V, kv_bits, router_mode, capacity, n_super_max;
+  float eps;
+  QMatDev embed, lm_head;
+  const uint16_t* final_norm;
+  const float* rope;
+  int* ctl;            // control block (token, position, EOS, recorded ids)
+  unsigned* gbar;      // [0] grid barrier arrivals (zeroed before launch), [1] abort flag
+  unsigned* cnt;       // [Hq] head counters, then [Hq * n_super_max] super counters
+  uint16_t *h, *qkv, *attn, *act, *logits, *trace;
+  float *partials, *supers, *router_logits, *cand_val;
+  int* cand_idx;
+  int steps;
+  unsigned long long* prof;  // optional: [barrier][cta] x (arrive, release) globaltimer stamps
+};
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+struct MegaSmem {
+  alignas(128) uint8_t ring[kSlots][kSlotBytes];
+  alignas(16) uint16_t h0[2048];
+  alignas(16) uint16_t xn[4096];
+  alignas(16) uint16_t act[kMaxTopK * 1024];
+  alignas(16) float qs[8][128];
+  float QS[8][2];
+  alignas(16) float p[4][8][32];
+  alignas(16) float wacc[4][8][128];
+  float wm[4][8], wl[4][8];
+  float red[40];
+  float seg_part[kMegaCons][4];
+  float best_val[kMegaCons];
+  int best_idx[kMegaCons];
+  float route_p[kMaxExperts];
+  float route_c[kMaxExperts];
+  int ids[kMaxTopK];
+  float wts[kMaxTopK];
+  float dsm[kMaxTopK][kDRowsMax];
+  uint64_t full[kSlots], empty[kSlots];
+  volatile int route_seq;
+  int token;
+  int token0, pos0;  // starting token / position, read once at kernel entry
+};
+
+__device__ __forceinline__ void cons_sync() { asm volatile("bar.sync %0, %1;" ::"r"(kBarCons), "r"(kMegaCons * 32)); }
+__device__ __forceinline__ void attn_sync() { asm volatile("bar.sync %0, %1;" ::"r"(kBarAttn), "r"(128)); }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Data written by other CTAs during this launch is read through L2 only
+// (L1 is not coherent across SMs inside one kernel).
+__device__ __forceinline__ uint4 ldcg128(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
+__device__ __forceinline__ float ldcg_bf(const uint16_t* p) {
+  return bf(__ldcg(reinterpret_cast<const unsigned short*>(p)));
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Static partition of the step's work over CTAs (shared by both roles)
+// ---------------------------------------------------------------------------
+struct Part {
+  int q0, q1;   // QKV rows
+  int o0, o1;   // output rows of O and D (same owner)
+  int g0, g1;   // gate/up pair units
+};
+__device__ __forceinline__ Part partition(const MegaArgs& a) {
+  Part p;
+  const int G = gridDim.x, c = blockIdx.x;
+  const int qrows = (a.hq + 2 * a.hkv) * 128;
+  split_range(qrows / 2, G, c, p.q0, p.q1);
+  p.q0 *= 2;
+  p.q1 *= 2;
+  split_range(a.H / 2, G, c, p.o0, p.o1);
+  p.o0 *= 2;
+  p.o1 *= 2;
+  split_range(a.k * a.I / 2, G, c, p.g0, p.g1);
+  p.g0 *= 2;
+  p.g1 *= 2;
+  return p;
+}
+
+struct AttnPlan {
+  int T, nblk, hq, nq, items;
+};
+__device__ __forceinline__ AttnPlan attn_plan(const MegaArgs& a, int pos) {
+  AttnPlan p;
+  p.T = pos + 1;
+  p.nblk = (p.T + kAttBlock - 1) / kAttBlock;
+  p.hq = att_hq(a.hkv, p.nblk, gridDim.x);
+  p.nq = (a.hq / a.hkv) / p.hq;
+  p.items = p.nblk * a.hkv * p.nq;
+  return p;
+}
+__device__ __forceinline__ void attn_item(const AttnPlan& P, int hkv, int it, int& b, int& g, int& qsub) {
+  qsub = it % P.nq;
+  g = (it / P.nq) % hkv;
+  b = it / (P.nq * hkv);
+}
+
+// Grid barrier index of a phase: each step has 6 per layer + 1 (after H).
+__device__ __forceinline__ unsigned bar_index(const MegaArgs& a, int step, int layer, int ph) {
+  return unsigned(step * (6 * a.n_layers + 1) + 6 * layer + ph);
+}
+
+__device__ __forceinline__ bool aborted(const MegaArgs& a) {
+  return *reinterpret_cast<volatile unsigned*>(a.gbar + 1) != 0;
+}
+__device__ __forceinline__ void set_abort(const MegaArgs& a, int code) {
+  report(a.ctl + 0, code);
+  atomicExch(a.gbar + 1, 1u);
+}
+
+// Bounded grid barrier among consumers of all CTAs.  Returns false on abort.
+__device__ __forceinline__ bool grid_barrier(const MegaArgs& a, unsigned idx) {
+  cons_sync();
+  __shared__ int ok_flag;
+  if (threadIdx.x == 32) {
+    if (a.prof) a.prof[(size_t(idx) * gridDim.x + blockIdx.x) * 2] = globaltimer();
+    __threadfence();
+    atomicAdd(a.gbar, 1u);
+    const unsigned target = gridDim.x * (idx + 1);
+    int ok = 1;
+    uint32_t spins = 0;
+    while (ld_acquire(a.gbar) < target) {
+      if (aborted(a)) { ok = 0; break; }
+      if (++spins > kSpinLimit * 4) {
+        set_abort(a, kStatusCounterTimeout);
+        ok = 0;
+        break;
+      }
+    }
+    __threadfence();
+    if (a.prof) a.prof[(size_t(idx) * gridDim.x + blockIdx.x) * 2 + 1] = globaltimer();
+    ok_flag = ok && !aborted(a);
+  }
+  cons_sync();
+  return ok_flag != 0;
+}
+
+// ---------------------------------------------------------------------------
+// Producer
+// ---------------------------------------------------------------------------
+struct Producer {
+  const MegaArgs& a;
+  MegaSmem& sm;
+  uint32_t chunk = 0;
+  bool ok = true;
+  uint32_t issued_mask = 0, last_par = 0;  // per slot: ever issued, parity of its last phase
+
+  __device__ Producer(const MegaArgs& a_, MegaSmem& sm_) : a(a_), sm(sm_) {}
+
+  __device__ void issued(int slot) {
+    issued_mask |= 1u << slot;
+    last_par = (last_par & ~(1u << slot)) | (((chunk / kSlots) & 1u) << slot);
+    ++chunk;
+  }
+  // lane 0 only
+  __device__ uint8_t* acquire(int& slot) {
+    slot = chunk % kSlots;
+    if (chunk >= kSlots) {
+      const uint32_t par = ((chunk / kSlots) - 1) & 1;
+      uint32_t spins = 0;
+      while (!mbar_try_wait(&sm.empty[slot], par)) {
+        if (aborted(a)) { ok = false; return nullptr; }
+        if (++spins > kSpinLimit) {
+          set_abort(a, kStatusBulkTimeout);
+          ok = false;
+          return nullptr;
+        }
+      }
+    }
+    return sm.ring[slot];
+  }
+  __device__ void gemv_chunk(const QMatDev& m, int K, int row0, int n) {
+    int slot;
+    uint8_t* dst = acquire(slot);
+    if (!dst) return;
+    const uint32_t wb = uint32_t(n) * (K / 2), sbytes = uint32_t(n) * (K / 32);
+    const uint32_t soff = wb, boff = wb + ((sbytes + 15) & ~15u);
+    mbar_expect_tx(&sm.full[slot], wb + 2 * sbytes);
+    bulk_g2s(dst, reinterpret_cast<const uint8_t*>(m.w) + size_t(row0) * (K / 2), wb, &sm.full[slot]);
+    bulk_g2s(dst + soff, m.s + size_t(row0) * (K / 64), sbytes, &sm.full[slot]);
+    bulk_g2s(dst + boff, m.b + size_t(row0) * (K / 64), sbytes, &sm.full[slot]);
+    issued(slot);
+  }
+  __device__ void pair_chunk(const MegaLayer& L, int expert, int i0, int n) {
+    int slot;
+    uint8_t* dst = acquire(slot);
+    if (!dst) return;
+    const size_t row = size_t(expert) * a.I + i0;
+    const uint32_t wb = uint32_t(n) * 1024, sbytes = uint32_t(n) * 64;
+    mbar_expect_tx(&sm.full[slot], 2 * wb + 4 * sbytes);
+    bulk_g2s(dst, reinterpret_cast<const uint8_t*>(L.gate.w) + row * 1024, wb, &sm.full[slot]);
+    bulk_g2s(dst + wb, reinterpret_cast<const uint8_t*>(L.up.w) + row * 1024, wb, &sm.full[slot]);
+    bulk_g2s(dst + 2 * wb, L.gate.s + row * 32, sbytes, &sm.full[slot]);
+    bulk_g2s(dst + 2 * wb + sbytes, L.up.s + row * 32, sbytes, &sm.full[slot]);
+    bulk_g2s(dst + 2 * wb + 2 * sbytes, L.gate.b + row * 32, sbytes, &sm.full[slot]);
+    bulk_g2s(dst + 2 * wb + 3 * sbytes, L.up.b + row * 32, sbytes, &sm.full[slot]);
+    issued(slot);
+  }
+  // D chunk: experts ids[r0..r1) rows [o0, o0+n) of the down matrices (K = I)
+  __device__ void down_chunk(const MegaLayer& L, const int* ids, int r0, int r1, int o0, int n) {
+    int slot;
+    uint8_t* dst = acquire(slot);
+    if (!dst) return;
+    const uint32_t wb = uint32_t(n) * (a.I / 2), sbytes = uint32_t(n) * (a.I / 32);
+    const uint32_t per = wb + 2 * ((sbytes + 15) & ~15u);
+    mbar_expect_tx(&sm.full[slot], uint32_t(r1 - r0) * (wb + 2 * sbytes));
+    for (int r = r0; r < r1; ++r) {
+      const size_t row = size_t(ids[r]) * a.H + o0;
+      uint8_t* d = dst + (r - r0) * per;
+      bulk_g2s(d, reinterpret_cast<const uint8_t*>(L.down.w) + row * (a.I / 2), wb, &sm.full[slot]);
+      bulk_g2s(d + wb, L.down.s + row * (a.I / 64), sbytes, &sm.full[slot]);
+      bulk_g2s(d + wb + ((sbytes + 15) & ~15u), L.down.b + row * (a.I / 64), sbytes, &sm.full[slot]);
+    }
+    issued(slot);
+  }
+  __device__ void kv_chunk(const uint32_t* codes, const uint16_t* sc, const uint16_t* bi, int g, int b, int n) {
+    int slot;
+    uint8_t* dst = acquire(slot);
+    if (!dst) return;
+    const int rw = 128 * a.kv_bits / 32;
+    const int n4 = (n + 3) & ~3;
+    const size_t s0 = size_t(g) * a.capacity + size_t(b) * kAttBlock;
+    const uint32_t cb = uint32_t(n4) * rw * 4, sbytes = uint32_t(n4) * 4;
+    mbar_expect_tx(&sm.full[slot], cb + 2 * sbytes);
+    bulk_g2s(dst, codes + s0 * rw, cb, &sm.full[slot]);
+    bulk_g2s(dst + cb, sc + s0 * 2, sbytes, &sm.full[slot]);
+    bulk_g2s(dst + cb + sbytes, bi + s0 * 2, sbytes, &sm.full[slot]);
+    issued(slot);
+  }
+
+  __device__ void run() {
+    const int lane = threadIdx.x & 31;
+    const Part P = partition(a);
+    const int pos0 = sm.pos0;
+    const int qrows[3] = {a.hq * 128, a.hkv * 128, a.hkv * 128};
+    for (int step = 0; step < a.steps && ok; ++step) {
+      const int pos = pos0 + step;
+      const AttnPlan AP = attn_plan(a, pos);
+      for (int l = 0; l < a.n_layers && ok; ++l) {
+        const MegaLayer& L = a.layers[l];
+        if (lane == 0) {
+          // Q rows (q | k | v), chunks never cross matrices
+          for (int r = P.q0; r < P.q1 && ok;) {
+            int m = 0, base = 0;
+            while (m < 2 && r >= base + qrows[m]) base += qrows[m++];
+            const int n = min(min(kQRows, P.q1 - r), base + qrows[m] - r);
+            gemv_chunk(m == 0 ? L.q : (m == 1 ? L.k : L.v), a.H, r - base, n);
+            r += n;
+          }
+          // A: K and V tiles of this CTA's items
+          for (int it = blockIdx.x; it < AP.items && ok; it += gridDim.x) {
+            int b, g, qsub;
+            attn_item(AP, a.hkv, it, b, g, qsub);
+            const int n = min(kAttBlock, AP.T - b * kAttBlock);
+            kv_chunk(L.k_codes, L.k_scales, L.k_biases, g, b, n);
+            kv_chunk(L.v_codes, L.v_scales, L.v_biases, g, b, n);
+          }
+          // O rows
+          for (int r = P.o0; r < P.o1 && ok; r += kORows) gemv_chunk(L.o, a.hq * 128, r, min(kORows, P.o1 - r));
+          // G / D need this layer's routing: wait for the consumers' selection
+          const int seq = step * a.n_layers + l + 1;
+          uint32_t spins = 0;
+          while (sm.route_seq < seq) {
+            if (aborted(a)) { ok = false; break; }
+            if (++spins > kSpinLimit * 64) {
+              set_abort(a, kStatusCounterTimeout);
+              ok = false;
+              break;
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0 && ok) {
+          int ids[kMaxTopK];
+          for (int r = 0; r < a.k; ++r) ids[r] = sm.ids[r];
+          for (int u = P.g0; u < P.g1 && ok;) {
+            const int r = u / a.I, i0 = u % a.I;
+            const int n = min(min(kGPairs, P.g1 - u), a.I - i0);
+            pair_chunk(L, ids[r], i0, n);
+            u += n;
+          }
+          if (P.o1 > P.o0)
+            for (int r0 = 0; r0 < a.k && ok; r0 += kDExperts)
+              down_chunk(L, ids, r0, min(a.k, r0 + kDExperts), P.o0, P.o1 - P.o0);
+        }
+        __syncwarp();
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+      }
+      if (lane == 0) {
+        int v0, v1;
+        split_range(a.V / 2, gridDim.x, blockIdx.x, v0, v1);
+        v0 *= 2;
+        v1 *= 2;
+        for (int r = v0; r < v1 && ok; r += kQRows) gemv_chunk(a.lm_head, a.H, r, min(kQRows, v1 - r));
+      }
+      __syncwarp();
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+    // on abort: let the copies already issued land before the CTA exits
+    if (lane == 0 && !ok) {
+      for (int s = 0; s < kSlots; ++s)
+        if (issued_mask & (1u << s)) mbar_wait(&sm.full[s], (last_par >> s) & 1u);
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Consumers
+// ---------------------------------------------------------------------------
+struct Consumers {
+  const MegaArgs& a;
+  MegaSmem& sm;
+  const int warp, lane;  // warp in 0..7
+  uint32_t chunk = 0;
+  int slot = 0;
+  bool ok = true;
+
+  __device__ Consumers(const MegaArgs& a_, MegaSmem& sm_)
+      : a(a_), sm(sm_), warp((threadIdx.x >> 5) - 1), lane(threadIdx.x & 31) {}
+
+  __device__ const uint8_t* take() {
+    slot = chunk % kSlots;
+    const uint32_t par = (chunk / kSlots) & 1;
+    uint32_t spins = 0;
+    while (!mbar_try_wait(&sm.full[slot], par)) {
+      if (aborted(a)) { ok = false; break; }
+      if (++spins > kSpinLimit) {
+        set_abort(a, kStatusBulkTimeout);  // every CTA leaves at its next grid barrier
+        ok = false;
+        break;
+      }
+    }
+    return sm.ring[slot];
+  }
+  __device__ void release(bool wrote_smem = false) {
+    if (wrote_smem) fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[slot]);
+    ++chunk;
+  }
+
+  // RMSNorm of src (bf16[H], global or shared) into sm.xn (canonical order).
+  __device__ void norm(const uint16_t* src, const uint16_t* w, bool from_smem = false) {
+    const int H = a.H, groups = H >> 8;
+    for (int g = warp; g < groups; g += kMegaCons) {
+      const uint4 u = from_smem ? *reinterpret_cast<const uint4*>(src + (g * 32 + lane) * 8)
+                                : ldcg128(src + (g * 32 + lane) * 8);
+      const uint32_t us[4] = {u.x, u.y, u.z, u.w};
+      float acc = 0.0f;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float x0 = __uint_as_float(us[t] << 16), x1 = __uint_as_float(us[t] & 0xFFFF0000u);
+        acc = __fmaf_rn(x0, x0, acc);
+        acc = __fmaf_rn(x1, x1, acc);
+      }
+      acc = bfly_sum(acc);
+      if (lane == 0) sm.red[g] = acc;
+    }
+    cons_sync();
+    if (warp == 0 && lane == 0) {
+      float total = 0.0f;
+      for (int g = 0; g < groups; ++g) total = __fadd_rn(total, sm.red[g]);
+      sm.red[32] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, float(H)), a.eps)));
+    }
+    cons_sync();
+    const float inv = sm.red[32];
+    for (int i = threadIdx.x - 32; i < H; i += kMegaCons * 32)
+      sm.xn[i] = to_bf(__fmul_rn(bf(w[i]), rbf(__fmul_rn(from_smem ? bf(src[i]) : ldcg_bf(src + i), inv))));
+    cons_sync();
+  }
+  __device__ void load_x(const uint16_t* src, int n) {
+    for (int i = (threadIdx.x - 32) * 8; i < n; i += kMegaCons * 32 * 8)
+      *reinterpret_cast<uint4*>(sm.xn + i) = ldcg128(src + i);
+    cons_sync();
+  }
+
+  // --- Q and H: K = 2048 rows, 8 warps x ILP 4 ---------------------------------
+  template <int SD, bool HEAD>
+  __device__ void rows2048(const uint8_t* st, int n, int grow0, const ChunkX (&cx)[2], uint16_t* out, float& best,
+                           int& best_i) {
+    const uint32_t wb = uint32_t(n) * 1024, sbytes = uint32_t(n) * 64;
+    const uint8_t* wbase = st;
+    const uint16_t* sbase = reinterpret_cast<const uint16_t*>(st + wb);
+    const uint16_t* bbase = reinterpret_cast<const uint16_t*>(st + wb + ((sbytes + 15) & ~15u));
+    int rows[4];
+    bool valid[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = warp + i * kMegaCons;
+      valid[i] = r < n;
+      rows[i] = valid[i] ? r : 0;
+    }
+    float v[4];
+    lane_rows_partial<2048, SD, 4>(wbase, sbase, bbase, rows, 0, lane, cx, v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[i] = bfly_sum(valid[i] ? v[i] : 0.0f);
+      if (valid[i] && lane == 0) {
+        const int g = grow0 + rows[i];
+        const uint16_t o = to_bf(v[i]);
+        out[g] = o;
+        if (HEAD) {
+          const float fv = bf(o);
+          if (fv > best || (fv == best && g < best_i)) { best = fv; best_i = g; }
+        }
+      }
+    }
+  }
+
+  // --- O: K = 4096 rows, warp pairs (one 2048 segment each) x ILP 4 ---------
+  template <int SD>
+  __device__ void rows4096(const uint8_t* st, int n, int grow0, const ChunkX (&cx)[2]) {
+    // always called by every consumer warp: the team barriers below must match
+    const int seg = warp & 1, team = warp >> 1;
+    const uint32_t wb = uint32_t(n) * 2048, sbytes = uint32_t(n) * 128;
+    const uint8_t* wbase = st;
+    const uint16_t* sbase = reinterpret_cast<const uint16_t*>(st + wb);
+    const uint16_t* bbase = reinterpret_cast<const uint16_t*>(st + wb + sbytes);
+    int rows[4];
+    bool valid[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = team + 4 * i;
+      valid[i] = r < n;
+      rows[i] = valid[i] ? r : 0;
+    }
+    float v[4];
+    lane_rows_partial<4096, SD, 4>(wbase, sbase, bbase, rows, seg, lane, cx, v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = bfly_sum(valid[i] ? v[i] : 0.0f);
+    if (lane == 0)
+      for (int i = 0; i < 4; ++i) sm.seg_part[warp][i] = v[i];
+    asm volatile("bar.sync %0, %1;" ::"r"(kBarTeam0 + team), "r"(64));
+    if (seg == 0 && lane == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (!valid[i]) continue;
+        const float t = __fadd_rn(v[i], sm.seg_part[warp + 1][i]);
+        const int g = grow0 + rows[i];
+        a.h[g] = to_bf(__fadd_rn(ldcg_bf(a.h + g), rbf(t)));
+      }
+    }
+    asm volatile("bar.sync %0, %1;" ::"r"(kBarTeam0 + team), "r"(64));
+  }
+
+  // --- attention ----------------------------------------------------------------
+  template <int BITS>
+  __device__ void attn_item_compute(const MegaLayer& L, const AttnPlan& P, int pos, int b, int g, int qsub,
+                                    uint8_t* kt, uint8_t* vt, bool& patched) {
+    // warps 0..3 only
+    constexpr int RW = 128 * BITS / 32;
+    const int n = min(kAttBlock, P.T - b * kAttBlock), n4 = (n + 3) & ~3;
+    uint32_t* kc = reinterpret_cast<uint32_t*>(kt);
+    uint16_t* ks = reinterpret_cast<uint16_t*>(kt + n4 * RW * 4);
+    uint16_t* kb = ks + n4 * 2;
+    uint32_t* vc = reinterpret_cast<uint32_t*>(vt);
+    uint16_t* vs = reinterpret_cast<uint16_t*>(vt + n4 * RW * 4);
+    uint16_t* vb = vs + n4 * 2;
+    const int hq = P.hq;
+    const int h0 = g * (a.hq / a.hkv) + qsub * hq;
+    const float* cs = a.rope + size_t(pos) * 128;
+    for (int hh = warp; hh < hq; hh += 4) {
+      const uint16_t* qr = a.qkv + (h0 + hh) * 128;
+      float x[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) x[j] = ldcg_bf(qr + 4 * lane + j);
+      if (L.q_norm) head_norm4(x, L.q_norm, a.eps);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sm.qs[hh][4 * lane + j] = x[j];
+      __syncwarp();
+      float y[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int d = 4 * lane + j, i = d & 63;
+        const float c = cs[i], s = cs[64 + i];
+        const float lo = sm.qs[hh][i], hi = sm.qs[hh][i + 64];
+        y[j] = d < 64 ? rbf(__fmaf_rn(lo, c, -__fmul_rn(hi, s))) : rbf(__fmaf_rn(lo, s, __fmul_rn(hi, c)));
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sm.qs[hh][4 * lane + j] = rbf(__fmul_rn(y[j], kQScale));
+      __syncwarp();
+      if (lane < 2) {
+        float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int d = 64 * lane; d < 64 * lane + 64; ++d) a4[d & 3] = __fadd_rn(a4[d & 3], sm.qs[hh][d]);
+        sm.QS[hh][lane] = __fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]));
+      }
+    }
+    // the new token: RoPE'd k / v quantized and patched into the tiles
+    if (pos >= b * kAttBlock && pos < b * kAttBlock + n) {
+      patched = true;
+      const int tloc = pos - b * kAttBlock;
+      const bool is_k = warp < 2;
+      const int grp = warp & 1;
+      const uint16_t* src = a.qkv + (a.hq + (is_k ? 0 : a.hkv) + g) * 128;
+      float kv4[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kv4[j] = ldcg_bf(src + 4 * lane + j);
+      float* tmp = sm.wacc[warp][0];
+      if (is_k) {
+        if (L.k_norm) head_norm4(kv4, L.k_norm, a.eps);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tmp[4 * lane + j] = kv4[j];
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int d = 4 * lane + j, i = d & 63;
+          const float c = cs[i], s = cs[64 + i];
+          const float lo = tmp[i], hi = tmp[i + 64];
+          kv4[j] = d < 64 ? rbf(__fmaf_rn(lo, c, -__fmul_rn(hi, s))) : rbf(__fmaf_rn(lo, s, __fmul_rn(hi, c)));
+        }
+        __syncwarp();
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) tmp[4 * lane + j] = kv4[j];
+      __syncwarp();
+      const float v0 = tmp[64 * grp + 2 * lane], v1 = tmp[64 * grp + 2 * lane + 1];
+      const QGroupParams qp = warp_group_params(v0, v1, BITS);
+      const uint32_t word = warp_pack(quant_code(v0, qp, BITS), quant_code(v1, qp, BITS), BITS);
+      constexpr int GW = 64 * BITS / 32;
+      uint32_t* crow = (is_k ? kc : vc) + tloc * RW + grp * GW;
+      if (lane < GW) crow[lane] = word;
+      const uint16_t sc = to_bf(qp.scale), bi = to_bf(qp.bias);
+      if (lane == 0) {
+        (is_k ? ks : vs)[tloc * 2 + grp] = sc;
+        (is_k ? kb : vb)[tloc * 2 + grp] = bi;
+      }
+      if (qsub == 0) {
+        const size_t slot = size_t(g) * a.capacity + size_t(pos);
+        uint32_t* gc = (is_k ? L.k_codes : L.v_codes) + slot * RW + grp * GW;
+        if (lane < GW) gc[lane] = word;
+        if (lane == 0) {
+          (is_k ? L.k_scales : L.v_scales)[slot * 2 + grp] = sc;
+          (is_k ? L.k_biases : L.v_biases)[slot * 2 + grp] = bi;
+        }
+      }
+    }
+    attn_sync();
+    // per-warp online softmax over tiles warp, warp+4
+    float m[8], l[8], acc[8][4];
+#pragma unroll
+    for (int hh = 0; hh < 8; ++hh) {
+      m[hh] = -INFINITY;
+      l[hh] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[hh][j] = 0.0f;
+    }
+    for (int tile = warp; tile < kAttBlock / kAttTile; tile += kAttWarps) {
+      const int base = tile * kAttTile;
+      if (base >= n) break;
+      const int tl = base + lane;
+      const bool valid = tl < n;
+      const int row = valid ? tl : 0;
+      uint32_t krow[RW];
+#pragma unroll
+      for (int w = 0; w < RW; w += 4) {
+        const uint4 q4 = *reinterpret_cast<const uint4*>(&kc[row * RW + w]);
+        krow[w] = q4.x;
+        krow[w + 1] = q4.y;
+        krow[w + 2] = q4.z;
+        krow[w + 3] = q4.w;
+      }
+      const float s0 = bf(ks[row * 2]), s1 = bf(ks[row * 2 + 1]);
+      const float bb0 = bf(kb[row * 2]), bb1 = bf(kb[row * 2 + 1]);
+      for (int hh = 0; hh < hq; ++hh) {
+        const float sc = valid ? att_score<BITS>(krow, sm.qs[hh], sm.QS[hh], s0, bb0, s1, bb1) : -INFINITY;
+        const float tmax = bfly_max(sc);
+        const float mnew = fmaxf(m[hh], tmax);
+        const float alpha = rexp(__fsub_rn(m[hh], mnew));
+        const float pt = valid ? rexp(__fsub_rn(sc, mnew)) : 0.0f;
+        const float ts = bfly_sum(pt);
+        l[hh] = __fmaf_rn(l[hh], alpha, ts);
+        m[hh] = mnew;
+        sm.p[warp][hh][lane] = pt;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[hh][j] = __fmul_rn(acc[hh][j], alpha);
+      }
+      __syncwarp();
+      const int nt = min(kAttTile, n - base);
+      const int grp = lane >> 4;
+      for (int t = 0; t < nt; ++t) {
+        const int tok = base + t;
+        uint32_t c4;
+        if constexpr (BITS == 4) c4 = reinterpret_cast<const uint16_t*>(vc + tok * RW)[lane];
+        else c4 = vc[tok * RW + lane];
+        const float vsc = bf(vs[tok * 2 + grp]), vbi = bf(vb[tok * 2 + grp]);
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t c = BITS == 4 ? (c4 >> (4 * j)) & 15u : (c4 >> (8 * j)) & 255u;
+          v[j] = __fmaf_rn(vsc, float(c), vbi);
+        }
+        for (int hh = 0; hh < hq; ++hh) {
+          const float pp = sm.p[warp][hh][t];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[hh][j] = __fmaf_rn(pp, v[j], acc[hh][j]);
+        }
+      }
+      __syncwarp();
+    }
+    for (int hh = 0; hh < hq; ++hh) {
+      if (lane == 0) {
+        sm.wm[warp][hh] = m[hh];
+        sm.wl[warp][hh] = l[hh];
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sm.wacc[warp][hh][4 * lane + j] = acc[hh][j];
+    }
+    attn_sync();
+    // block partial (warps merged in order) and the last-arriver merges
+    const int nblk_cap = a.capacity / kAttBlock;
+    const int s = b / kAttSuper;
+    const int n_super = (P.nblk + kAttSuper - 1) / kAttSuper;
+    const int in_super = min(kAttSuper, P.nblk - s * kAttSuper);
+    for (int hh = warp; hh < hq; hh += 4) {
+      const int h = h0 + hh;
+      Partial4 Pt;
+      Pt.m = -INFINITY;
+      Pt.l = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) Pt.a[j] = 0.0f;
+      for (int w = 0; w < kAttWarps; ++w) {
+        Partial4 Q;
+        Q.m = sm.wm[w][hh];
+        Q.l = sm.wl[w][hh];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) Q.a[j] = sm.wacc[w][hh][4 * lane + j];
+        merge_into(Pt, Q);
+      }
+      float* dst = a.partials + (size_t(h) * nblk_cap + b) * kPartialFloats;
+      if (lane == 0) {
+        dst[0] = Pt.m;
+        dst[1] = Pt.l;
+      }
+      *reinterpret_cast<float4*>(dst + 4 + 4 * lane) = make_float4(Pt.a[0], Pt.a[1], Pt.a[2], Pt.a[3]);
+      __threadfence();
+      unsigned prev = 0;
+      if (lane == 0) prev = atomicAdd(a.cnt + a.hq + h * a.n_super_max + s, 1u);
+      prev = __shfl_sync(0xffffffffu, prev, 0);
+      if (int(prev) != in_super - 1) continue;
+      // this warp merges super-chunk s of head h
+      __threadfence();
+      Partial4 S;
+      S.m = -INFINITY;
+      S.l = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) S.a[j] = 0.0f;
+      for (int bb = s * kAttSuper; bb < s * kAttSuper + in_super; ++bb) {
+        const float* src = a.partials + (size_t(h) * nblk_cap + bb) * kPartialFloats;
+        Partial4 Q;
+        Q.m = __ldcg(src);
+        Q.l = __ldcg(src + 1);
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(src + 4) + lane);
+        Q.a[0] = v.x; Q.a[1] = v.y; Q.a[2] = v.z; Q.a[3] = v.w;
+        merge_into(S, Q);
+      }
+      if (lane == 0) a.cnt[a.hq + h * a.n_super_max + s] = 0;
+      float* sd = a.supers + (size_t(h) * a.n_super_max + s) * kPartialFloats;
+      if (lane == 0) {
+        sd[0] = S.m;
+        sd[1] = S.l;
+      }
+      *reinterpret_cast<float4*>(sd + 4 + 4 * lane) = make_float4(S.a[0], S.a[1], S.a[2], S.a[3]);
+      __threadfence();
+      if (lane == 0) prev = atomicAdd(a.cnt + h, 1u);
+      prev = __shfl_sync(0xffffffffu, prev, 0);
+      if (int(prev) != n_super - 1) continue;
+      __threadfence();
+      Partial4 F;
+      F.m = -INFINITY;
+      F.l = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) F.a[j] = 0.0f;
+      if (L.sinks) {
+        F.m = bf(L.sinks[h]);
+        F.l = 1.0f;
+      }
+      for (int ss = 0; ss < n_super; ++ss) {
+        const float* src = a.supers + (size_t(h) * a.n_super_max + ss) * kPartialFloats;
+        Partial4 Q;
+        Q.m = __ldcg(src);
+        Q.l = __ldcg(src + 1);
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(src + 4) + lane);
+        Q.a[0] = v.x; Q.a[1] = v.y; Q.a[2] = v.z; Q.a[3] = v.w;
+        merge_into(F, Q);
+      }
+      uint2 o;
+      o.x = uint32_t(to_bf(__fdiv_rn(F.a[0], F.l))) | (uint32_t(to_bf(__fdiv_rn(F.a[1], F.l))) << 16);
+      o.y = uint32_t(to_bf(__fdiv_rn(F.a[2], F.l))) | (uint32_t(to_bf(__fdiv_rn(F.a[3], F.l))) << 16);
+      *reinterpret_cast<uint2*>(a.attn + h * 128 + 4 * lane) = o;
+      if (lane == 0) a.cnt[h] = 0;
+    }
+  }
+
+  // --- routing (every CTA, consumer warp 0) -----------------------------------
+  __device__ void route(const MegaLayer& L) {
+    if (warp != 0) return;
+    const int E = a.E;
+    if (a.router_mode == 0) {
+      float mx = -INFINITY;
+      for (int i = lane; i < E; i += 32) mx = fmaxf(mx, __ldcg(a.router_logits + i));
+      mx = bfly_max(mx);
+      float s = 0.0f;
+      for (int i = lane; i < E; i += 32) s = __fadd_rn(s, rexp(__fsub_rn(__ldcg(a.router_logits + i), mx)));
+      s = bfly_sum(s);
+      for (int i = lane; i < E; i += 32) {
+        const float pi = __fdiv_rn(rexp(__fsub_rn(__ldcg(a.router_logits + i), mx)), s);
+        sm.route_p[i] = pi;
+        sm.route_c[i] = pi;
+      }
+    } else {
+      for (int i = lane; i < E; i += 32) {
+        const float pi = rsigmoid(__ldcg(a.router_logits + i));
+        sm.route_p[i] = pi;
+        sm.route_c[i] = __fadd_rn(pi, L.expert_bias[i]);
+      }
+    }
+    __syncwarp();
+    select_top(E);
+  }
+  __device__ void select_top(int E) {
+    for (int r = 0; r < a.k; ++r) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int i = lane; i < E; i += 32) {
+        const float c = sm.route_c[i];
+        if (c > bv || (c == bv && i < bi)) { bv = c; bi = i; }
+      }
+      for (int off = 16; off >= 1; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      if (lane == 0) {
+        sm.ids[r] = bi;
+        sm.route_c[bi] = -INFINITY;
+      }
+      __syncwarp();
+    }
+    if (lane == 0) {
+      float sum = 0.0f;
+      for (int r = 0; r < a.k; ++r) sum = __fadd_rn(sum, sm.route_p[sm.ids[r]]);
+      sum = __fadd_rn(sum, 1e-20f);
+      for (int r = 0; r < a.k; ++r) sm.wts[r] = __fdiv_rn(sm.route_p[sm.ids[r]], sum);
+    }
+    __syncwarp();
+  }
+
+  template <int SD, int I>
+  __device__ void run() {
+    const Part P = partition(a);
+    int token = sm.token0;
+    const int pos0 = sm.pos0;
+    const int H = a.H;
+    float best = -INFINITY;
+    int best_i = 0x7fffffff;
+    for (int step = 0; step < a.steps; ++step) {
+      const int pos = pos0 + step;
+      const AttnPlan AP = attn_plan(a, pos);
+      // embedding (every CTA, for its own layer-0 norm); owners publish rows
+      {
+        const int tok = (token >= 0 && token < a.V) ? token : 0;
+        if (tok != token && blockIdx.x == 0 && warp == 0 && lane == 0) report(a.ctl + 0, kStatusBadToken);
+        const uint32_t* w = a.embed.w + size_t(tok) * (H / 8);
+        for (int i = threadIdx.x - 32; i < H; i += kMegaCons * 32) {
+          const float q = float((w[i >> 3] >> (4 * (i & 7))) & 15u);
+          const float s = sb<SD>(a.embed.s[size_t(tok) * (H / 64) + (i >> 6)]);
+          const float bb = sb<SD>(a.embed.b[size_t(tok) * (H / 64) + (i >> 6)]);
+          const uint16_t v = to_bf(__fmaf_rn(s, q, bb));
+          sm.h0[i] = v;
+          if (i >= P.o0 && i < P.o1) a.h[i] = v;
+          if (blockIdx.x == 0) a.trace[i] = v;
+        }
+        cons_sync();
+      }
+      for (int l = 0; l < a.n_layers; ++l) {
+        const MegaLayer& L = a.layers[l];
+        // ---- Q
+        norm(l == 0 ? sm.h0 : a.h, L.input_norm, l == 0);
+        {
+          ChunkX cx[2];
+          prep_lane_x<2048>(sm.xn, 0, lane, cx);
+          const int qrows[3] = {a.hq * 128, a.hkv * 128, a.hkv * 128};
+          for (int r = P.q0; r < P.q1;) {
+            int m = 0, base = 0;
+            while (m < 2 && r >= base + qrows[m]) base += qrows[m++];
+            const int n = min(min(kQRows, P.q1 - r), base + qrows[m] - r);
+            const uint8_t* st = take();
+            rows2048<SD, false>(st, n, r, cx, a.qkv, best, best_i);
+            release();
+            r += n;
+          }
+        }
+        if (!grid_barrier(a, bar_index(a, step, l, 0))) return;
+        // ---- A
+        for (int it = blockIdx.x; it < AP.items; it += gridDim.x) {
+          int b, g, qsub;
+          attn_item(AP, a.hkv, it, b, g, qsub);
+          uint8_t* kt = const_cast<uint8_t*>(take());
+          const int kslot = slot;
+          ++chunk;
+          uint8_t* vt = const_cast<uint8_t*>(take());
+          const int vslot = slot;
+          --chunk;
+          bool patched = false;
+          if (warp < 4) {
+            if (a.kv_bits == 4) attn_item_compute<4>(L, AP, pos, b, g, qsub, kt, vt, patched);
+            else attn_item_compute<8>(L, AP, pos, b, g, qsub, kt, vt, patched);
+          }
+          cons_sync();
+          slot = kslot;
+          release(true);
+          slot = vslot;
+          release(true);
+        }
+        if (!grid_barrier(a, bar_index(a, step, l, 1))) return;
+        // ---- O
+        {
+          load_x(a.attn, a.hq * 128);
+          ChunkX cx[2];
+          prep_lane_x<4096>(sm.xn, warp & 1, lane, cx);
+          for (int r = P.o0; r < P.o1; r += kORows) {
+            const int n = min(kORows, P.o1 - r);
+            const uint8_t* st = take();
+            rows4096<SD>(st, n, r, cx);
+            release();
+          }
+        }
+        if (!grid_barrier(a, bar_index(a, step, l, 2))) return;
+        // ---- R
+        norm(a.h, L.post_norm);
+        {
+          int j = 0;
+          for (int e = blockIdx.x; e < a.E; e += gridDim.x, ++j) {
+            if ((j % kMegaCons) != warp) continue;
+            float acc = 0.0f;
+            for (int mm = 0; mm < H / 256; ++mm) {
+              const int c = lane + 32 * mm;
+              const uint4 wv = ldg128_nc(L.router + size_t(e) * H + c * 8);
+              const uint4 xv = *reinterpret_cast<const uint4*>(sm.xn + c * 8);
+              const uint32_t ws_[4] = {wv.x, wv.y, wv.z, wv.w};
+              const uint32_t xs_[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                acc = __fmaf_rn(__uint_as_float(ws_[t] << 16), __uint_as_float(xs_[t] << 16), acc);
+                acc = __fmaf_rn(__uint_as_float(ws_[t] & 0xFFFF0000u), __uint_as_float(xs_[t] & 0xFFFF0000u), acc);
+              }
+            }
+            acc = bfly_sum(acc);
+            if (lane == 0) a.router_logits[e] = rbf(acc);
+          }
+        }
+        if (!grid_barrier(a, bar_index(a, step, l, 3))) return;
+        // ---- G: selection (same on every CTA), then gate/up pairs
+        route(L);
+        if (warp == 0 && lane == 0) {
+          __threadfence_block();
+          sm.route_seq = step * a.n_layers + l + 1;
+        }
+        cons_sync();
+        {
+          ChunkX cx[2];
+          prep_lane_x<2048>(sm.xn, 0, lane, cx);
+          for (int u = P.g0; u < P.g1;) {
+            const int r = u / a.I, i0 = u % a.I;
+            const int n = min(min(kGPairs, P.g1 - u), a.I - i0);
+            const uint8_t* st = take();
+            {
+              const uint32_t wb = uint32_t(n) * 1024, sbytes = uint32_t(n) * 64;
+              const uint16_t* sbase = reinterpret_cast<const uint16_t*>(st + 2 * wb);
+              const uint16_t* bbase = reinterpret_cast<const uint16_t*>(st + 2 * wb + 2 * sbytes);
+              // rows: gate i at row i, up i at row n + i (scales likewise)
+              const int pa = warp, pc = warp + kMegaCons;
+              const bool va = pa < n, vc = pc < n;
+              int rows[4] = {va ? pa : 0, va ? n + pa : 0, vc ? pc : 0, vc ? n + pc : 0};
+              float v[4];
+              lane_rows_partial<2048, SD, 4>(st, sbase, bbase, rows, 0, lane, cx, v);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) v[q] = bfly_sum(v[q]);
+              if (lane == 0) {
+                if (va) {
+                  const float gg = rbf(v[0]), uu = rbf(v[1]);
+                  a.act[r * a.I + i0 + pa] = to_bf(__fmul_rn(rbf(__fmul_rn(gg, rbf(rsigmoid(gg)))), uu));
+                }
+                if (vc) {
+                  const float gg = rbf(v[2]), uu = rbf(v[3]);
+                  a.act[r * a.I + i0 + pc] = to_bf(__fmul_rn(rbf(__fmul_rn(gg, rbf(rsigmoid(gg)))), uu));
+                }
+              }
+            }
+            release();
+            u += n;
+          }
+        }
+        if (!grid_barrier(a, bar_index(a, step, l, 4))) return;
+        // ---- D: down rows of all k experts, mix, residual
+        {
+          for (int i = (threadIdx.x - 32) * 8; i < a.k * I; i += kMegaCons * 32 * 8)
+            *reinterpret_cast<uint4*>(sm.act + i) = ldcg128(a.act + i);
+          cons_sync();
+          const int n = P.o1 - P.o0;
+          if (n > 0) {
+            for (int r0 = 0; r0 < a.k; r0 += kDExperts) {
+              const int r1 = min(a.k, r0 + kDExperts);
+              const uint8_t* st = take();
+              // warp w: expert r0 + (w % 4), rows of half (w / 4)
+              const int rr = r0 + (warp % kDExperts), half = warp / kDExperts;
+              if (rr < r1) {
+                using C = KCfg<I>;
+                const uint32_t wb = uint32_t(n) * (I / 2), sbytes = uint32_t(n) * (I / 32);
+                const uint32_t per = wb + 2 * ((sbytes + 15) & ~15u);
+                const uint8_t* e0 = st + (rr - r0) * per;
+                const uint16_t* sbase = reinterpret_cast<const uint16_t*>(e0 + wb);
+                const uint16_t* bbase = reinterpret_cast<const uint16_t*>(e0 + wb + ((sbytes + 15) & ~15u));
+                ChunkX cx[C::CH];
+                const int sub = lane >> 3, l8 = lane & 7;
+                prep_lane_x<I>(sm.act + rr * I, 0, l8, cx);
+                const int rbeg = half * ((n + 1) / 2), rend = half == 0 ? (n + 1) / 2 : n;
+                for (int rb = rbeg; rb < rend; rb += 8) {
+                  int rows[2];
+                  bool valid[2];
+#pragma unroll
+                  for (int q = 0; q < 2; ++q) {
+                    const int x = rb + 4 * q + sub;
+                    valid[q] = x < rend;
+                    rows[q] = valid[q] ? x : rbeg;
+                  }
+                  float v[2];
+                  lane_rows_partial<I, SD, 2>(e0, sbase, bbase, rows, 0, l8, cx, v);
+#pragma unroll
+                  for (int q = 0; q < 2; ++q) {
+                    v[q] = bfly_sum<8>(valid[q] ? v[q] : 0.0f);
+                    if (valid[q] && l8 == 0) sm.dsm[rr][rows[q]] = rbf(v[q]);
+                  }
+                }
+              }
+              release();
+            }
+            cons_sync();
+            for (int i = threadIdx.x - 32; i < n; i += kMegaCons * 32) {
+              float mix = 0.0f;
+              for (int r = 0; r < a.k; ++r) {
+                const float t = __fadd_rn(rbf(__fmul_rn(sm.dsm[r][i], rbf(sm.wts[r]))), 0.0f);
+                mix = r == 0 ? t : rbf(__fadd_rn(t, mix));
+              }
+              const uint16_t hn = to_bf(__fadd_rn(ldcg_bf(a.h + P.o0 + i), mix));
+              a.h[P.o0 + i] = hn;
+              a.trace[size_t(l + 1) * H + P.o0 + i] = hn;
+            }
+          }
+        }
+        if (!grid_barrier(a, bar_index(a, step, l, 5))) return;
+      }
+      // ---- H: final norm + lm_head + CTA argmax
+      norm(a.h, a.final_norm);
+      {
+        ChunkX cx[2];
+        prep_lane_x<2048>(sm.xn, 0, lane, cx);
+        best = -INFINITY;
+        best_i = 0x7fffffff;
+        int v0, v1;
+        split_range(a.V / 2, gridDim.x, blockIdx.x, v0, v1);
+        v0 *= 2;
+        v1 *= 2;
+        for (int r = v0; r < v1; r += kQRows) {
+          const int n = min(kQRows, v1 - r);
+          const uint8_t* st = take();
+          rows2048<SD, true>(st, n, r, cx, a.logits, best, best_i);
+          release();
+        }
+        for (int off = 16; off >= 1; off >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+          const int oi = __shfl_xor_sync(0xffffffffu, best_i, off);
+          if (ov > best || (ov == best && oi < best_i)) { best = ov; best_i = oi; }
+        }
+        if (lane == 0) {
+          sm.best_val[warp] = best;
+          sm.best_idx[warp] = best_i;
+        }
+        cons_sync();
+        if (warp == 0 && lane == 0) {
+          float bv = sm.best_val[0];
+          int bi = sm.best_idx[0];
+          for (int w = 1; w < kMegaCons; ++w)
+            if (sm.best_val[w] > bv || (sm.best_val[w] == bv && sm.best_idx[w] < bi)) {
+              bv = sm.best_val[w];
+              bi = sm.best_idx[w];
+            }
+          a.cand_val[blockIdx.x] = bv;
+          a.cand_idx[blockIdx.x] = bi;
+        }
+      }
+      if (!grid_barrier(a, bar_index(a, step, a.n_layers, 0))) return;
+      // ---- E: global argmax (every CTA), bookkeeping (CTA 0)
+      if (warp == 0) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int c = lane; c < gridDim.x; c += 32) {
+          const float v = __ldcg(a.cand_val + c);
+          const int i = __ldcg(a.cand_idx + c);
+          if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+        }
+        for (int off = 16; off >= 1; off >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+          if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) {
+          sm.token = bi;
+          if (blockIdx.x == 0) {
+            int* ctl = a.ctl;
+            if (ctl[3]) {  // active
+              if (ctl[5] < 64) ctl[16 + ctl[5]] = bi;
+              ctl[4] += 1;
+              for (int i = 0; i < ctl[6]; ++i)
+                if (ctl[8 + i] == bi) ctl[3] = 0;
+            }
+            ctl[7] = bi;
+            ctl[1] = bi;
+            ctl[2] = pos + 1;
+            ctl[5] += 1;
+          }
+        }
+      }
+      cons_sync();
+      token = sm.token;
+    }
+  }
+};
+
+template <int SD, int I>
+__global__ void __launch_bounds__(kMegaThreads, 1) k_decode_mega(const MegaArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  MegaSmem& sm = *reinterpret_cast<MegaSmem*>(smem_raw);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], kMegaCons);
+    }
+    sm.route_seq = 0;
+    sm.token0 = a.ctl[1];
+    sm.pos0 = a.ctl[2];
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    Producer p(a, sm);
+    p.run();
+  } else {
+    Consumers c(a, sm);
+    c.template run<SD, I>();
+  }
+}
+
+}  // namespace rec

@@ -40,9 +40,11 @@ struct ChunkX {
 };
 
 __device__ __forceinline__ void prep_chunk(const float* x32, ChunkX& cx) {
-  // x32: the 32 chunk values as floats (already rounded to bf16 values)
-  const float lo_scale[4] = {1.0f, 0.0625f, 0.00390625f, 0.000244140625f};   // 2^-4i
-  const float hi_scale[4] = {1.52587890625e-05f, 0.00390625f, 0.000244140625f, 1.52587890625e-05f};
+  // x32: the 32 chunk values as floats (already rounded to bf16 values).
+  // lo nibble i is masked in place from the word (value q*2^(4i)); hi nibble
+  // 4+i from the word shifted right by 12 (value q*2^(4i+4)).
+  const float lo_scale[4] = {1.0f, 0.0625f, 0.00390625f, 0.000244140625f};          // 2^-4i
+  const float hi_scale[4] = {0.0625f, 0.00390625f, 0.000244140625f, 1.52587890625e-05f};  // 2^-(4i+4)
   float xl = 0.0f, xh = 0.0f;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
@@ -58,26 +60,29 @@ __device__ __forceinline__ void prep_chunk(const float* x32, ChunkX& cx) {
 }
 
 // --- one 16-byte chunk against prepared x -------------------------------------
+__device__ __forceinline__ float2 u64_as_float2(unsigned long long v) {
+  float2 f;
+  f.x = __uint_as_float(uint32_t(v));
+  f.y = __uint_as_float(uint32_t(v >> 32));
+  return f;
+}
+
 __device__ __forceinline__ float chunk_dot(uint4 w, const ChunkX& cx) {
-  const uint32_t M = 0x4B000000u;
+  // (word, word >> 12) form one 64-bit register pair; each 64-bit AND/OR
+  // yields a (lo, hi) float pair ready for the packed f32x2 add and FMA.
+  const unsigned long long M = 0x4B0000004B000000ull;
   const float2 off = make_float2(-8388608.0f, -8388608.0f);
   float2 acc = make_float2(0.0f, 0.0f);
   const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    uint32_t a = ws[k], a12 = a >> 12;
-    float2 f0 = make_float2(__uint_as_float((a & 0xFu) | M), __uint_as_float((a & 0xF0000u) | M));
-    float2 f1 = make_float2(__uint_as_float((a & 0xF0u) | M), __uint_as_float((a12 & 0xF00u) | M));
-    float2 f2 = make_float2(__uint_as_float((a & 0xF00u) | M), __uint_as_float((a12 & 0xF000u) | M));
-    float2 f3 = make_float2(__uint_as_float((a & 0xF000u) | M), __uint_as_float((a12 & 0xF0000u) | M));
-    f0 = __fadd2_rn(f0, off);
-    f1 = __fadd2_rn(f1, off);
-    f2 = __fadd2_rn(f2, off);
-    f3 = __fadd2_rn(f3, off);
-    acc = __ffma2_rn(cx.p[k][0], f0, acc);
-    acc = __ffma2_rn(cx.p[k][1], f1, acc);
-    acc = __ffma2_rn(cx.p[k][2], f2, acc);
-    acc = __ffma2_rn(cx.p[k][3], f3, acc);
+    const unsigned long long p = (static_cast<unsigned long long>(ws[k] >> 12) << 32) | ws[k];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const unsigned long long mask = (static_cast<unsigned long long>(0xF0u << (4 * i)) << 32) | (0xFu << (4 * i));
+      const float2 f = __fadd2_rn(u64_as_float2((p & mask) | M), off);
+      acc = __ffma2_rn(cx.p[k][i], f, acc);
+    }
   }
   return __fadd_rn(acc.x, acc.y);
 }

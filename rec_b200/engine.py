@@ -1,0 +1,208 @@
+"""Drop-in replacement of the reference decoder API on B200.
+
+Mirrors recursive-oss/rec engine/src/rec_mlx:
+  kernels/__init__.py:1-65      build_decoder(model, *, optimized) -> (engine, resident_sampler)
+  kernels/megakernel.py:983-1337 FullModel: forward, make_session, prefill_state, ensure_capacity
+  kernels/sampling.py:17-169     ResidentSampler.block
+  quantized.py:98-151            QATSession.prefill / forward_token
+
+State dict keys and error conventions follow the reference
+(megakernel.py:1264-1268, 1308-1337; sampling.py:77-78): a device-wait
+timeout raises RuntimeError("GPU synchronization failed: ...") and marks the
+state unusable; reusing it raises "Session was invalidated ..."; running past
+the limit raises ValueError("Decode context limit exhausted"); packets must
+hold 1..8 tokens.
+"""
+from __future__ import annotations
+
+import time
+
+import torch
+
+from ._lib import RecError
+from .model import KVCache, ModelWeights
+from .session import DecodeSession
+
+WIDTH = 8  # resident packet size (sampling.py:8)
+
+
+class KVStorage:
+    """Growable quantized KV storage of a state (reference cache.py:52-119)."""
+
+    def __init__(self, weights: ModelWeights, capacity: int, device):
+        self.weights = weights
+        self.device = device
+        self.capacity = 0
+        self.cache: KVCache | None = None
+        self.session: DecodeSession | None = None
+        self.grow(capacity)
+
+    @classmethod
+    def wrap(cls, weights: ModelWeights, cache: KVCache, session: DecodeSession) -> "KVStorage":
+        """Storage around an existing cache and session (no copy)."""
+        obj = cls.__new__(cls)
+        obj.weights, obj.cache, obj.session = weights, cache, session
+        obj.device = cache.layers[0]["k_codes"].device
+        obj.capacity = cache.capacity
+        return obj
+
+    @staticmethod
+    def _round(n: int) -> int:
+        return max(256, (n + 4095) // 4096 * 4096)
+
+    def grow(self, count: int) -> None:
+        need = self._round(count)
+        if self.cache is not None and need <= self.capacity:
+            return
+        new = KVCache.allocate(self.weights.cfg, need, self.device)
+        if self.cache is not None:
+            for dst, src in zip(new.layers, self.cache.layers):
+                for name in dst:
+                    dst[name][:, : self.capacity].copy_(src[name])
+        self.cache = new
+        self.capacity = need
+        self.session = DecodeSession(self.weights, new)
+
+    @property
+    def nbytes(self) -> int:
+        return self.cache.nbytes() if self.cache is not None else 0
+
+
+class FullModel:
+    """B200 decode engine for one model (one GPU)."""
+
+    def __init__(self, weights: ModelWeights, *, prefill_chunk_size: int = 1024, device="cuda"):
+        self.model = weights
+        self.weights = weights
+        self.cfg = weights.cfg
+        self.device = torch.device(device)
+        self.prefill_chunk_size = prefill_chunk_size
+        self.device_profile = torch.cuda.get_device_name(self.device) if torch.cuda.is_available() else None
+        self.workers = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.schedule = {"workers": self.workers, "graph": "per-token CUDA graph, programmatic dependent launch"}
+
+    # -- state ---------------------------------------------------------------
+    def prefill_state(self, capacity, *, limit=None, storage=None):
+        if storage is None:
+            storage = KVStorage(self.weights, capacity, self.device)
+        else:
+            storage.grow(capacity)
+        return {"usable": True, "kv": storage, "metadata": None, "position": 0, "initial": 0,
+                "capacity": storage.capacity, "limit": capacity if limit is None else limit,
+                "growth_count": 0, "growth_seconds": 0.0}
+
+    def ensure_capacity(self, state, count):
+        if not state["usable"]:
+            raise RuntimeError("Session was invalidated by a GPU synchronization failure")
+        required = state["position"] + count
+        if required > state["limit"]:
+            raise ValueError("Decode context limit exhausted")
+        if required > state["capacity"]:
+            started = time.perf_counter()
+            state["kv"].grow(required)
+            state["capacity"] = state["kv"].capacity
+            state["growth_count"] += 1
+            state["growth_seconds"] += time.perf_counter() - started
+
+    def _session(self, state) -> DecodeSession:
+        return state["kv"].session
+
+    def _guard(self, state, fn):
+        try:
+            return fn()
+        except RecError as exc:
+            state["usable"] = False
+            raise RuntimeError(f"GPU synchronization failed: {exc}") from None
+
+    # -- one step -------------------------------------------------------------
+    def forward(self, state, token, layer_count=None):
+        """One token; returns (logits bf16[V], trace bf16[L+1, H])."""
+        if layer_count is not None and layer_count != self.cfg.n_layers:
+            raise ValueError("partial-depth forward is not supported; use the full layer count")
+        self.ensure_capacity(state, 1)
+        sess = self._session(state)
+
+        def run():
+            logits, trace = sess.step(int(token), state["position"], want_trace=True)
+            sess.check_status()
+            return logits.clone(), trace.clone()
+
+        out = self._guard(state, run)
+        state["position"] += 1
+        return out
+
+    def make_session(self, *, max_new_tokens=512) -> "QATSession":
+        return QATSession(self, max_new_tokens)
+
+
+class QATSession:
+    """Prefill + scalar decode (reference quantized.py:98-151).  Prefill runs
+    the prompt through the decode step token by token (exact: the cache holds
+    what decoding would have written)."""
+
+    context_limit = 262144
+
+    def __init__(self, engine: FullModel, max_new_tokens: int):
+        self.engine, self.maximum = engine, max_new_tokens
+        self._state = None
+        self.cached_tokens = 0
+        self.common_prefix_tokens = 0
+
+    def prefill(self, tokens, *, prefix=None, should_stop=lambda: False, interrupt_between_layers=False):
+        if prefix is not None:
+            raise NotImplementedError("prompt-prefix reuse is outside the decode hot path")
+        limit = len(tokens) + self.maximum
+        if limit > self.context_limit:
+            raise ValueError("prompt plus output allowance exceeds the context limit")
+        state = self.engine.prefill_state(len(tokens) + 1, limit=limit)
+        sess = self.engine._session(state)
+        logits = None
+        for i, t in enumerate(tokens):
+            if should_stop() and i % self.engine.prefill_chunk_size == 0:
+                from .errors import PrefillCancelled
+
+                raise PrefillCancelled()
+            logits, _ = sess.step(int(t), i)
+        self.engine._guard(state, sess.check_status)
+        state["position"] = state["initial"] = len(tokens)
+        self._state = state
+        return logits.clone()
+
+    def forward_token(self, token):
+        return self.engine.forward(self._state, token)[0]
+
+
+class ResidentSampler:
+    """Packets of up to 8 tokens decoded with the next token fed back on the
+    device (reference sampling.py:62-169, resident_block.py:12-88)."""
+
+    def __init__(self, engine: FullModel, eos_tokens=()):
+        self.engine = engine
+        self.eos_tokens = list(eos_tokens)
+
+    def block(self, state, token, count, seed, *, temperature=1.0, top_p=1.0, top_k=0, presence_penalty=0.0,
+              grammar=None, logprobs=None):
+        if not 1 <= count <= WIDTH:
+            raise ValueError("Resident packet must contain between one and eight tokens")
+        self.engine.ensure_capacity(state, count)
+        if grammar is not None or logprobs is not None:
+            raise NotImplementedError("grammar masks and logprobs are outside the decode hot path")
+        if temperature != 0:
+            from .sampling import sampled_block
+
+            ids = sampled_block(self.engine, state, token, count, seed, temperature=temperature, top_p=top_p,
+                                top_k=top_k, presence_penalty=presence_penalty, eos=self.eos_tokens)
+        else:
+            sess = self.engine._session(state)
+            ids = self.engine._guard(state, lambda: sess.greedy(int(token), state["position"], count,
+                                                                self.eos_tokens))
+        if not 1 <= len(ids) <= count:
+            raise RuntimeError("Invalid sampled chain")
+        state["position"] += len(ids)
+        return ids
+
+
+def build_decoder(model: ModelWeights, *, optimized: bool = True, eos_tokens=()):
+    """(engine, resident_sampler) for a model, as kernels.build_decoder."""
+    engine = FullModel(model)
+    return engine, (ResidentSampler(engine, eos_tokens) if optimized else None)

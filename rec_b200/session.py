@@ -50,12 +50,20 @@ class DecodeSession:
     def _stream():
         return C.c_void_p(torch.cuda.current_stream().cuda_stream)
 
-    def step(self, token: int, position: int, want_trace: bool = False):
-        """One decode step; returns (logits bf16[V], trace bf16[L+1, H] or None)."""
-        check(lib().rec_decode_step(self.ctx, int(token), int(position), C.c_void_p(self.logits.data_ptr()),
+    def step(self, token: int, position: int, want_trace: bool = False, want_logits: bool = True):
+        """One decode step; returns (logits bf16[V] or None, trace bf16[L+1, H] or None)."""
+        check(lib().rec_decode_step(self.ctx, int(token), int(position),
+                                    C.c_void_p(self.logits.data_ptr()) if want_logits else None,
                                     C.c_void_p(self.trace.data_ptr()) if want_trace else None, self._stream()),
               "rec_decode_step")
-        return self.logits, (self.trace if want_trace else None)
+        return (self.logits if want_logits else None), (self.trace if want_trace else None)
+
+    def prefill(self, tokens, start: int = 0) -> None:
+        """Runs tokens through the decode step at positions start.. (fills the
+        cache exactly as decoding would)."""
+        for i, t in enumerate(tokens):
+            self.step(int(t), start + i, want_logits=False)
+        self.check_status()
 
     def greedy(self, token: int, position: int, count: int, eos=()):
         """Up to `count` greedy tokens with device-side feedback; stops after

@@ -15,6 +15,13 @@ from rec_b200.session import DecodeSession
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(params=["mega", "graph"])
+def schedule(request, monkeypatch):
+    """The persistent kernel (default) and the per-kernel CUDA graph."""
+    monkeypatch.setenv("REC_SCHEDULE", request.param)
+    return request.param
+
 VARIANTS = {
     "tiny_kv8_fp16": TINY,
     "tiny_kv4_bf16_sigmoid": replace(TINY, kv_bits=4, scale_dtype=torch.bfloat16,
@@ -45,7 +52,7 @@ def _compare_kv(kv, hkv, upto):
 
 
 @pytest.mark.parametrize("variant", list(VARIANTS))
-def test_decode_steps_bitexact(cuda, variant):
+def test_decode_steps_bitexact(cuda, schedule, variant):
     cfg = VARIANTS[variant]
     _, kv, sess, host, hkv = _setup(cfg, 512, seed=3)
     rng = np.random.default_rng(5)
@@ -61,7 +68,7 @@ def test_decode_steps_bitexact(cuda, variant):
     _compare_kv(kv, hkv, 12)
 
 
-def test_greedy_packet_bitexact(cuda):
+def test_greedy_packet_bitexact(cuda, schedule):
     cfg = TINY
     _, kv, sess, host, hkv = _setup(cfg, 512, seed=9)
     tok, pos = 17, 0
@@ -81,7 +88,7 @@ def test_greedy_packet_bitexact(cuda):
     assert got == ref
 
 
-def test_greedy_packet_stops_at_eos(cuda):
+def test_greedy_packet_stops_at_eos(cuda, schedule):
     cfg = TINY
     _, kv, sess, host, hkv = _setup(cfg, 512, seed=9)
     first = sess.greedy(17, 0, 8)
@@ -93,7 +100,7 @@ def test_greedy_packet_stops_at_eos(cuda):
 
 @pytest.mark.parametrize("context", [1000, 16384 + 300])
 @pytest.mark.parametrize("bits", [4, 8])
-def test_long_context_step_bitexact(cuda, context, bits):
+def test_long_context_step_bitexact(cuda, schedule, context, bits):
     """A prefilled synthetic cache (K, V ~ N(0,1) quantized) spanning several
     blocks and, at 16,684 tokens, two super-chunks."""
     cfg = replace(TINY, n_layers=1, kv_bits=bits)
