@@ -209,92 +209,99 @@ ORC_API void orc_rmsnorm(const uint16_t* h, const uint16_t* w, int H, float eps,
 }
 
 /* ---------------------------------------------------------- int4 GEMV */
+/* x in 16-bit fixed point with one power-of-two scale per vector:
+ * E = exponent of max|x|, F = min(14 - E, 100), xi = rint(x * 2^F). */
 typedef struct {
-  float p[4][4][2];
-  float X;
-} ChunkX;
+  int F;
+  float up, down;
+} FixScale;
 
-static void prep_chunk(const uint16_t* x32, ChunkX* cx) {
-  static const float lo_scale[4] = {1.0f, 0.0625f, 0.00390625f, 0.000244140625f};
-  static const float hi_scale[4] = {0.0625f, 0.00390625f, 0.000244140625f, 1.52587890625e-05f};
-  float xl = 0.0f, xh = 0.0f;
-  for (int k = 0; k < 4; ++k)
-    for (int i = 0; i < 4; ++i) {
-      float a = bf(x32[8 * k + i]), b = bf(x32[8 * k + 4 + i]);
-      cx->p[k][i][0] = a * lo_scale[i];
-      cx->p[k][i][1] = b * hi_scale[i];
-      xl = xl + a;
-      xh = xh + b;
-    }
-  cx->X = xl + xh;
-}
-
-static float chunk_dot(const uint32_t* w4, const ChunkX* cx) {
-  const uint32_t M = 0x4B000000u;
-  float lo = 0.0f, hi = 0.0f;
-  for (int k = 0; k < 4; ++k) {
-    uint32_t a = w4[k], a12 = a >> 12;
-    float fl[4] = {u2f((a & 0xFu) | M), u2f((a & 0xF0u) | M), u2f((a & 0xF00u) | M),
-                   u2f((a & 0xF000u) | M)};
-    float fh[4] = {u2f((a12 & 0xF0u) | M), u2f((a12 & 0xF00u) | M), u2f((a12 & 0xF000u) | M),
-                   u2f((a12 & 0xF0000u) | M)};
-    for (int i = 0; i < 4; ++i) {
-      fl[i] = fl[i] - 8388608.0f;
-      fh[i] = fh[i] - 8388608.0f;
-    }
-    for (int i = 0; i < 4; ++i) {
-      lo = fmaf(cx->p[k][i][0], fl[i], lo);
-      hi = fmaf(cx->p[k][i][1], fh[i], hi);
-    }
+static FixScale fix_scale(const uint16_t* x, int K) {
+  float m = 0.0f;
+  for (int i = 0; i < K; ++i) {
+    float a = fabsf(bf(x[i]));
+    m = a > m ? a : m;
   }
-  return lo + hi;
+  int E = (int)((f2u(m) >> 23) & 0xFF) - 127;
+  int F = 14 - E;
+  if (F > 100) F = 100;
+  FixScale fs = {F, u2f((uint32_t)(F + 127) << 23), u2f((uint32_t)(127 - F) << 23)};
+  return fs;
 }
 
-/* One row of y = W x in the canonical lane order.  cx: prepared chunks of x. */
+/* Prepared vector: xi per element, X per group (float of an exact sum). */
+typedef struct {
+  int32_t* xi;
+  float* X;
+  FixScale fs;
+} PrepX;
+
+static PrepX prep_x(const uint16_t* x, int K) {
+  PrepX p;
+  p.fs = fix_scale(x, K);
+  p.xi = (int32_t*)malloc(sizeof(int32_t) * K);
+  p.X = (float*)malloc(sizeof(float) * (K / 64));
+  for (int i = 0; i < K; ++i) p.xi[i] = (int32_t)rintf(bf(x[i]) * p.fs.up);
+  for (int g = 0; g < K / 64; ++g) {
+    int32_t s = 0;
+    for (int j = 0; j < 64; ++j) s += p.xi[g * 64 + j];
+    p.X[g] = (float)s;
+  }
+  return p;
+}
+static void free_prep(PrepX* p) {
+  free(p->xi);
+  free(p->X);
+}
+
+/* Exact integer dot of group g of a row with xi. */
+static int32_t group_dot(const uint32_t* wrow, const int32_t* xi, int g) {
+  int64_t d = 0;
+  for (int j = 0; j < 64; ++j) {
+    int e = g * 64 + j;
+    d += (int64_t)((wrow[e >> 3] >> (4 * (e & 7))) & 15u) * xi[e];
+  }
+  return (int32_t)d;
+}
+
+/* One row in the canonical lane order (see rec_b200/csrc/qdot.cuh). */
 static float rowdot(const uint32_t* wrow, const uint16_t* srow, const uint16_t* brow, int sd, int K,
-                    const ChunkX* cx) {
+                    const PrepX* px) {
   int wide = (K % 2048) == 0;
-  int T = wide ? 32 : 8, SEG = wide ? K / 2048 : 1, CH = wide ? 2 : K / 256;
+  int T = wide ? 32 : 4, SEG = wide ? K / 2048 : 1, GPL = wide ? 1 : (K / 64) / 4;
   float total = 0.0f;
   for (int seg = 0; seg < SEG; ++seg) {
     float v[32];
     for (int l = 0; l < T; ++l) {
       float acc = 0.0f;
-      for (int m = 0; m < CH; ++m) {
-        int c = wide ? seg * 64 + l + 32 * m : l + 8 * m;
-        float d = chunk_dot(wrow + c * 4, &cx[c]);
-        float s = sbv(srow[c >> 1], sd), b = sbv(brow[c >> 1], sd);
-        acc = fmaf(s, d, acc);
-        acc = fmaf(b, cx[c].X, acc);
+      for (int m = 0; m < GPL; ++m) {
+        int g = wide ? 32 * seg + l : l + 4 * m;
+        int32_t D = group_dot(wrow, px->xi, g);
+        acc = fmaf(sbv(srow[g], sd), (float)D, acc);
+        acc = fmaf(sbv(brow[g], sd), px->X[g], acc);
       }
       v[l] = acc;
     }
     bfly(v, T);
     total = seg == 0 ? v[0] : total + v[0];
   }
-  return total;
-}
-
-static ChunkX* prep_x(const uint16_t* x, int K) {
-  ChunkX* cx = (ChunkX*)malloc(sizeof(ChunkX) * (K / 32));
-  for (int c = 0; c < K / 32; ++c) prep_chunk(x + c * 32, &cx[c]);
-  return cx;
+  return total * px->fs.down;
 }
 
 static void gemv(const RecQMat* m, int sd, int64_t row0, int64_t n, int K, const uint16_t* x,
                  float* yf, uint16_t* y) {
-  ChunkX* cx = prep_x(x, K);
+  PrepX px = prep_x(x, K);
   const uint32_t* W = (const uint32_t*)m->w;
   const uint16_t* S = (const uint16_t*)m->scales;
   const uint16_t* B = (const uint16_t*)m->biases;
 #pragma omp parallel for schedule(static)
   for (int64_t r = 0; r < n; ++r) {
     int64_t row = row0 + r;
-    float v = rowdot(W + row * (K / 8), S + row * (K / 64), B + row * (K / 64), sd, K, cx);
+    float v = rowdot(W + row * (K / 8), S + row * (K / 64), B + row * (K / 64), sd, K, &px);
     if (yf) yf[r] = v;
     if (y) y[r] = to_bf(v);
   }
-  free(cx);
+  free_prep(&px);
 }
 
 ORC_API void orc_gemv_int4(const uint32_t* w, const uint16_t* s, const uint16_t* b, int sd,
@@ -377,7 +384,6 @@ ORC_API void orc_kv_store(const RecKVLayer* kv, int Hkv, int C, int bits, int po
 /* ---------------------------------------------------------- attention */
 #define ATT_BLOCK 256
 #define ATT_TILE 32
-#define ATT_WARPS 4
 #define ATT_SUPER 64 /* blocks per super-chunk */
 #define NEG_INF (-INFINITY)
 
@@ -409,77 +415,91 @@ static inline uint32_t kv_code(const uint32_t* row, int bits, int d) {
   return bits == 4 ? (row[d >> 3] >> (4 * (d & 7))) & 15u : (row[d >> 2] >> (8 * (d & 3))) & 255u;
 }
 
-/* qs: scaled bf16 query of one head as floats[128]; QS[2]: group sums. */
-static float att_score(const float* qs, const float* QS, const uint32_t* krow, const uint16_t* ks,
-                       const uint16_t* kb, int bits) {
-  float t = 0.0f;
-  for (int g = 0; g < 2; ++g) {
-    float a[4] = {0, 0, 0, 0};
-    for (int d = 64 * g; d < 64 * g + 64; ++d) a[d & 3] = fmaf(qs[d], (float)kv_code(krow, bits, d), a[d & 3]);
-    float A = (a[0] + a[1]) + (a[2] + a[3]);
-    float s = bf(ks[g]), b = bf(kb[g]);
-    t = g == 0 ? fmaf(b, QS[0], s * A) : fmaf(b, QS[1], fmaf(s, A, t));
+/* Prepared query of one head: qs = bf16(q / sqrt(128)); 16-bit fixed point
+ * qi = rint(qs * 2^F), F = min(14 - exponent(max|qs|), 100); QS[g] = float of
+ * the exact sum of qi over group g; down = 2^-F. */
+typedef struct {
+  int32_t qi[128];
+  float QS[2];
+  float down;
+} QPrep;
+
+static void prep_query(const uint16_t* q, QPrep* Q) {
+  float qs[128], mx = 0.0f;
+  for (int d = 0; d < 128; ++d) {
+    qs[d] = rbf(bf(q[d]) * 0.0883883476483184405f);
+    float a = fabsf(qs[d]);
+    mx = a > mx ? a : mx;
   }
-  return rbf(t);
+  uint32_t u;
+  memcpy(&u, &mx, 4);
+  int E = (int)((u >> 23) & 0xFF) - 127;
+  int F = 14 - E;
+  if (F > 100) F = 100;
+  float up = ldexpf(1.0f, F);
+  int32_t S[2] = {0, 0};
+  for (int d = 0; d < 128; ++d) {
+    Q->qi[d] = (int32_t)rintf(qs[d] * up);
+    S[d >> 6] += Q->qi[d];
+  }
+  Q->QS[0] = (float)S[0];
+  Q->QS[1] = (float)S[1];
+  Q->down = ldexpf(1.0f, -F);
 }
 
-/* Partial of q head h over tokens [t0, t1) in the canonical tile/warp order
- * (block-local). */
-static void att_block(const float* qs, const float* QS, const RecKVLayer* kv, int g, int C, int bits,
-                      int b, int T, Partial* out) {
+/* score = bf16(fma(b1, QS1, fma(s1, D1, fma(b0, QS0, s0*D0))) * 2^-F) with
+ * D_g = sum over group g of qi * code, exact. */
+static float att_score(const QPrep* Q, const uint32_t* krow, const uint16_t* ks, const uint16_t* kb, int bits) {
+  int32_t D[2] = {0, 0};
+  for (int d = 0; d < 128; ++d) D[d >> 6] += Q->qi[d] * (int32_t)kv_code(krow, bits, d);
+  float t = fmaf(bf(kb[0]), Q->QS[0], bf(ks[0]) * (float)D[0]);
+  t = fmaf(bf(ks[1]), (float)D[1], t);
+  t = fmaf(bf(kb[1]), Q->QS[1], t);
+  return rbf(t * Q->down);
+}
+
+/* Partial of one q head over block b (tokens < T): tile w of 32 tokens is
+ * one warp's (m = tile max, p = exp(s - m), l = butterfly sum of p,
+ * acc = sum of p * v in token order); the tiles are merged in order. */
+static void att_block(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bits, int b, int T, Partial* out) {
   int words = 128 * bits / 32;
   const uint32_t* KC = (const uint32_t*)kv->k_codes;
   const uint32_t* VC = (const uint32_t*)kv->v_codes;
   const uint16_t *KS = (const uint16_t*)kv->k_scales, *KB = (const uint16_t*)kv->k_biases;
   const uint16_t *VS = (const uint16_t*)kv->v_scales, *VB = (const uint16_t*)kv->v_biases;
-  Partial warp[ATT_WARPS];
-  for (int w = 0; w < ATT_WARPS; ++w) {
-    Partial* P = &warp[w];
-    p_empty(P);
-    for (int j = w; j < ATT_BLOCK / ATT_TILE; j += ATT_WARPS) {
-      int base = b * ATT_BLOCK + j * ATT_TILE;
-      if (base >= T) break;
-      float s[ATT_TILE], p[ATT_TILE];
-      float tmax = NEG_INF;
-      for (int t = 0; t < ATT_TILE; ++t) {
-        int tok = base + t;
-        if (tok < T) {
-          int64_t slot = (int64_t)g * C + tok;
-          s[t] = att_score(qs, QS, KC + slot * words, KS + slot * 2, KB + slot * 2, bits);
-          tmax = s[t] > tmax ? s[t] : tmax;
-        }
-      }
-      float mnew = P->m > tmax ? P->m : tmax;
-      float alpha = rexp(P->m - mnew);
-      for (int t = 0; t < ATT_TILE; ++t) p[t] = (base + t < T) ? rexp(s[t] - mnew) : 0.0f;
-      float v[32];
-      memcpy(v, p, sizeof(v));
-      bfly(v, 32);
-      P->l = fmaf(P->l, alpha, v[0]);
-      for (int d = 0; d < 128; ++d) P->acc[d] = P->acc[d] * alpha;
-      for (int t = 0; t < ATT_TILE; ++t) {
-        int tok = base + t;
-        if (tok >= T) break;
-        int64_t slot = (int64_t)g * C + tok;
-        const uint32_t* vrow = VC + slot * words;
-        for (int d = 0; d < 128; ++d) {
-          float val = fmaf(bf(VS[slot * 2 + d / 64]), (float)kv_code(vrow, bits, d), bf(VB[slot * 2 + d / 64]));
-          P->acc[d] = fmaf(p[t], val, P->acc[d]);
-        }
-      }
-      P->m = mnew;
-    }
-  }
   p_empty(out);
-  for (int w = 0; w < ATT_WARPS; ++w) p_merge(out, &warp[w]);
-}
-
-static void prep_query(const uint16_t* q, float* qs, float* QS) {
-  for (int d = 0; d < 128; ++d) qs[d] = rbf(bf(q[d]) * 0.0883883476483184405f);
-  for (int g = 0; g < 2; ++g) {
-    float a[4] = {0, 0, 0, 0};
-    for (int d = 64 * g; d < 64 * g + 64; ++d) a[d & 3] = a[d & 3] + qs[d];
-    QS[g] = (a[0] + a[1]) + (a[2] + a[3]);
+  for (int w = 0; w < ATT_BLOCK / ATT_TILE; ++w) {
+    int base = b * ATT_BLOCK + w * ATT_TILE;
+    if (base >= T) break;
+    Partial P;
+    float s[ATT_TILE], p[ATT_TILE];
+    float tmax = NEG_INF;
+    for (int t = 0; t < ATT_TILE; ++t) {
+      int tok = base + t;
+      if (tok < T) {
+        int64_t slot = (int64_t)g * C + tok;
+        s[t] = att_score(Q, KC + slot * words, KS + slot * 2, KB + slot * 2, bits);
+        tmax = s[t] > tmax ? s[t] : tmax;
+      }
+    }
+    for (int t = 0; t < ATT_TILE; ++t) p[t] = (base + t < T) ? rexp(s[t] - tmax) : 0.0f;
+    float v[32];
+    memcpy(v, p, sizeof(v));
+    bfly(v, 32);
+    P.m = tmax;
+    P.l = v[0];
+    memset(P.acc, 0, sizeof(P.acc));
+    for (int t = 0; t < ATT_TILE; ++t) {
+      int tok = base + t;
+      if (tok >= T) break;
+      int64_t slot = (int64_t)g * C + tok;
+      const uint32_t* vrow = VC + slot * words;
+      for (int d = 0; d < 128; ++d) {
+        float val = fmaf(bf(VS[slot * 2 + d / 64]), (float)kv_code(vrow, bits, d), bf(VB[slot * 2 + d / 64]));
+        P.acc[d] = fmaf(p[t], val, P.acc[d]);
+      }
+    }
+    p_merge(out, &P);
   }
 }
 
@@ -490,15 +510,15 @@ ORC_API void orc_attention_supers(const uint16_t* q, const RecKVLayer* kv, int H
   int nblocks = (T + ATT_BLOCK - 1) / ATT_BLOCK;
 #pragma omp parallel for schedule(dynamic)
   for (int h = 0; h < Hq; ++h) {
-    float qs[128], QS[2];
-    prep_query(q + h * 128, qs, QS);
+    QPrep Q;
+    prep_query(q + h * 128, &Q);
     int g = h / (Hq / Hkv);
     for (int s = 0; s < n_super; ++s) {
       Partial* S = &supers[h * n_super + s];
       p_empty(S);
       for (int b = s * ATT_SUPER; b < (s + 1) * ATT_SUPER && b < nblocks; ++b) {
         Partial P;
-        att_block(qs, QS, kv, g, C, bits, b, T, &P);
+        att_block(&Q, kv, g, C, bits, b, T, &P);
         p_merge(S, &P);
       }
     }

@@ -1,39 +1,14 @@
-// GQA decode attention over the quantized KV cache: split-KV partials with
-// fused RoPE / quantize-on-append, and the log-sum-exp combine.
+// GQA decode attention over the quantized KV cache: split-KV block partials
+// with fused RoPE / quantize-on-append, and the log-sum-exp combine.  The
+// math and its canonical order are in attn_core.cuh.
 //
 // Reference: engine/src/rec_mlx/model.py:45-82 (quantize-on-append),
 // model.py:108-139 (scores, sink, softmax), megakernel.py:619-693 (split-KV
 // partials (max, sum, acc)), megakernel.py:276-318 (LSE merge).
-//
-// Canonical order (restated by oracle/rec_oracle.c):
-//   * q is RoPE'd (pairs (i, i+64), fp32 table of cos/sin), scaled and
-//     rounded: qs = bf16(q * 1/sqrt(128)); QS_g = sum of qs over group g
-//     (4 accumulators by d mod 4, then (a0+a1)+(a2+a3)).
-//   * score(t) = bf16(fma(b1, QS1, fma(s1, A1, fma(b0, QS0, s0*A0)))) with
-//     A_g = sum_d qs_d * code_d in the same 4-accumulator order.
-//   * tokens are cut into blocks of 256 and tiles of 32; warp w of 4 owns
-//     tiles w and w+4 of a block and runs an online softmax over them:
-//     m' = max(m, tile max); alpha = exp(m - m'); p_t = exp(s_t - m');
-//     l = fma(l, alpha, butterfly-sum(p)); acc = acc*alpha, then
-//     acc = fma(p_t, v_t, acc) in token order, v = fma(scale, code, bias).
-//   * warp partials merge in order into a block partial; blocks merge in
-//     order into super-chunks of 64 blocks; super-chunks merge in order
-//     (after the sink partial (sink, 1, 0) when sinks are on);
-//     merge: m = max; a_i = exp(m_i - m); l = fma(l1, a1, l2*a2);
-//     acc = fma(acc1, a1, acc2*a2); an empty side is the identity.
-//   * out = bf16(acc / l).
 #pragma once
-#include "common.cuh"
-#include "quant.cuh"
+#include "attn_core.cuh"
 
 namespace rec {
-
-constexpr int kAttBlock = 256;
-constexpr int kAttTile = 32;
-constexpr int kAttWarps = 4;
-constexpr int kAttSuper = 64;          // blocks per super-chunk
-constexpr int kPartialFloats = 132;    // m, l, pad, pad, acc[128]
-constexpr float kQScale = 0.0883883476483184405f;  // 1/sqrt(128)
 
 struct AttnArgs {
   const uint16_t* qkv;     // bf16 [Hq*128 | Hkv*128 | Hkv*128] pre-RoPE projections
@@ -63,119 +38,217 @@ struct AttnArgs {
   int pdl;
 };
 
-struct Partial4 {  // lane-distributed partial: dims 4*lane .. 4*lane+3
-  float m, l;
-  float a[4];
+// Shared-memory scratch of one attention item (hq <= kMaxHq heads).
+struct AttnScratch {
+  QHead qh[kMaxHq];
+  alignas(16) float p[kAttWarps][kMaxHq][kAttTile];
+  alignas(16) float wacc[kAttWarps][kMaxHq][128];
+  float wm[kAttWarps][kMaxHq], wl[kAttWarps][kMaxHq];
 };
 
-__device__ __forceinline__ void merge_into(Partial4& x, const Partial4& y) {
-  if (y.m == -INFINITY) return;
-  if (x.m == -INFINITY) { x = y; return; }
-  const float m = fmaxf(x.m, y.m);
-  const float a1 = rexp(__fsub_rn(x.m, m)), a2 = rexp(__fsub_rn(y.m, m));
-  x.l = __fmaf_rn(x.l, a1, __fmul_rn(y.l, a2));
+// Tile of one (block, kv head): codes then scales then biases for K and V,
+// rows padded to a multiple of 4 tokens.
+struct TileView {
+  uint32_t *kc, *vc;
+  uint16_t *ks, *kb, *vs, *vb;
+};
+
+// One work item: one block (n tokens) of kv head g for q heads [h0, h0+hq).
+// Called by all kAttWarps warps of a group (ids warp 0..7, synchronised by
+// `sync`); warp h < hq returns the block partial of head h0 + h.
+struct AttnBlock {
+  const uint16_t* qkv;
+  int hq_total, hkv;
+  int g, h0, hq, n;
+  const float* cs;              // cos/sin row of pos
+  const uint16_t *q_norm, *k_norm;
+  float eps;
+  bool has_new;                 // the block holds position pos
+  int tnew;                     // its row in the tile
+  uint32_t* g_kcodes;           // non-null: publish the new token here (row slot)
+  uint32_t* g_vcodes;
+  uint16_t *g_ks, *g_kb, *g_vs, *g_vb;
+};
+
+template <int BITS, typename Sync>
+__device__ __forceinline__ void attn_block(const AttnBlock& it, TileView tv, AttnScratch& sc, int warp, Sync sync,
+                                           Partial4& P) {
+  constexpr int RW = 128 * BITS / 32;
+  const int lane = threadIdx.x & 31;
+  // --- queries (warps 4..7) and the new token's K/V (warps 0..3) --------------
+  if (warp >= 4) {
+    const int hh = warp - 4;
+    if (hh < it.hq) {
+      const uint16_t* qr = it.qkv + (it.h0 + hh) * 128;
+      float x[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) x.a[j] = __fmaf_rn(x.a[j], a1, __fmul_rn(y.a[j], a2));
-  x.m = m;
+      for (int j = 0; j < 4; ++j) x[j] = bf(__ldcg(reinterpret_cast<const unsigned short*>(qr + 4 * lane + j)));
+      if (it.q_norm) head_norm4(x, it.q_norm, it.eps);
+      float* scratch = sc.wacc[warp][0];
+      rope4(x, it.cs, scratch);
+      prep_qhead<BITS>(x, sc.qh[hh], scratch);
+    }
+  } else if (it.has_new) {
+    const bool is_k = warp < 2;
+    const int grp = warp & 1;
+    const uint16_t* src = it.qkv + (it.hq_total + (is_k ? 0 : it.hkv) + it.g) * 128;
+    float kv4[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) kv4[j] = bf(__ldcg(reinterpret_cast<const unsigned short*>(src + 4 * lane + j)));
+    float* tmp = sc.wacc[warp][0];
+    if (is_k) {
+      if (it.k_norm) head_norm4(kv4, it.k_norm, it.eps);
+      rope4(kv4, it.cs, tmp);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tmp[4 * lane + j] = kv4[j];
+    __syncwarp();
+    const float v0 = tmp[64 * grp + 2 * lane], v1 = tmp[64 * grp + 2 * lane + 1];
+    const QGroupParams qp = warp_group_params(v0, v1, BITS);
+    const uint32_t word = warp_pack(quant_code(v0, qp, BITS), quant_code(v1, qp, BITS), BITS);
+    constexpr int GW = 64 * BITS / 32;
+    uint32_t* crow = (is_k ? tv.kc : tv.vc) + it.tnew * RW + grp * GW;
+    if (lane < GW) crow[lane] = word;
+    const uint16_t scb = to_bf(qp.scale), bib = to_bf(qp.bias);
+    if (lane == 0) {
+      (is_k ? tv.ks : tv.vs)[it.tnew * 2 + grp] = scb;
+      (is_k ? tv.kb : tv.vb)[it.tnew * 2 + grp] = bib;
+    }
+    if (it.g_kcodes) {
+      uint32_t* gc = (is_k ? it.g_kcodes : it.g_vcodes) + grp * GW;
+      if (lane < GW) gc[lane] = word;
+      if (lane == 0) {
+        (is_k ? it.g_ks : it.g_vs)[grp] = scb;
+        (is_k ? it.g_kb : it.g_vb)[grp] = bib;
+      }
+    }
+  }
+  sync();
+  // --- warp w: tile w ------------------------------------------------------------
+  const int hq = it.hq;
+  float m[kMaxHq], l[kMaxHq], acc[kMaxHq][4];
+#pragma unroll
+  for (int h = 0; h < kMaxHq; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[h][j] = 0.0f;
+  }
+  const int base = warp * kAttTile;
+  if (base < it.n) {
+    const int tl = base + lane;
+    const bool valid = tl < it.n;
+    const int row = valid ? tl : base;
+    const float s0 = bf(tv.ks[row * 2]), s1 = bf(tv.ks[row * 2 + 1]);
+    const float b0 = bf(tv.kb[row * 2]), b1 = bf(tv.kb[row * 2 + 1]);
+    tile_scores<BITS>(tv.kc + row * RW, valid, s0, b0, s1, b1, sc.qh, hq, m, l, sc.p[warp]);
+    __syncwarp();
+    const int nt = min(kAttTile, it.n - base);
+    const int grp = lane >> 4;
+    for (int t = 0; t < nt; ++t) {
+      const int tok = base + t;
+      uint32_t c4;
+      if constexpr (BITS == 4) c4 = reinterpret_cast<const uint16_t*>(tv.vc + tok * RW)[lane];
+      else c4 = tv.vc[tok * RW + lane];
+      const float vsc = bf(tv.vs[tok * 2 + grp]), vbi = bf(tv.vb[tok * 2 + grp]);
+      float v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t c = BITS == 4 ? (c4 >> (4 * j)) & 15u : (c4 >> (8 * j)) & 255u;
+        v[j] = __fmaf_rn(vsc, code_f(c), vbi);
+      }
+#pragma unroll
+      for (int h = 0; h < kMaxHq; ++h) {
+        if (h >= hq) break;
+        const float pp = sc.p[warp][h][t];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[h][j] = __fmaf_rn(pp, v[j], acc[h][j]);
+      }
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < kMaxHq; ++h) {
+    if (h >= hq) break;
+    if (lane == 0) {
+      sc.wm[warp][h] = m[h];
+      sc.wl[warp][h] = l[h];
+    }
+    *reinterpret_cast<float4*>(&sc.wacc[warp][h][4 * lane]) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+  }
+  sync();
+  // --- block partial: warps merged in order ----------------------------------
+  P = empty_partial();
+  if (warp < hq) {
+    const int h = warp;
+    for (int w = 0; w < kAttWarps; ++w) {
+      Partial4 Q;
+      Q.m = sc.wm[w][h];
+      Q.l = sc.wl[w][h];
+      const float4 a4 = *reinterpret_cast<const float4*>(&sc.wacc[w][h][4 * lane]);
+      Q.a[0] = a4.x; Q.a[1] = a4.y; Q.a[2] = a4.z; Q.a[3] = a4.w;
+      if (w * kAttTile >= it.n) Q = empty_partial();
+      merge_into(P, Q);
+    }
+  }
 }
 
-// Per-head RMSNorm over 128 dims (q_norm / k_norm): lane l holds 4l..4l+3.
-__device__ __forceinline__ void head_norm4(float (&x)[4], const uint16_t* w, float eps) {
+__device__ __forceinline__ void store_partial(float* dst, const Partial4& P) {
   const int lane = threadIdx.x & 31;
-  float a = 0.0f;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) a = __fmaf_rn(x[j], x[j], a);
-  a = bfly_sum(a);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(a, 128.0f), eps)));
-#pragma unroll
-  for (int j = 0; j < 4; ++j) x[j] = rbf(__fmul_rn(bf(w[4 * lane + j]), rbf(__fmul_rn(x[j], inv))));
+  if (lane == 0) {
+    dst[0] = P.m;
+    dst[1] = P.l;
+  }
+  *reinterpret_cast<float4*>(dst + 4 + 4 * lane) = make_float4(P.a[0], P.a[1], P.a[2], P.a[3]);
+}
+
+__device__ __forceinline__ int att_hq(int hkv, int nblk, int slots) {
+  // q heads per work item: as few as possible while the items fit `slots`
+  int hq = 1;
+  while (hq < kMaxHq && hkv * (8 / hq) * nblk > slots) hq *= 2;
+  return hq;
 }
 
 template <int BITS>
-struct AttnTile {
-  static constexpr int ROW_WORDS = 128 * BITS / 32;  // 16 or 32
-  static constexpr int ROW_BYTES = ROW_WORDS * 4;
+struct AttnSmem {
+  static constexpr int ROW_WORDS = 128 * BITS / 32;
   alignas(128) uint32_t kc[kAttBlock * ROW_WORDS];
   alignas(128) uint32_t vc[kAttBlock * ROW_WORDS];
   alignas(16) uint16_t ks[kAttBlock * 2];
   alignas(16) uint16_t kb[kAttBlock * 2];
   alignas(16) uint16_t vs[kAttBlock * 2];
   alignas(16) uint16_t vb[kAttBlock * 2];
-};
-
-template <int BITS>
-struct AttnSmem {
-  AttnTile<BITS> tile;
-  alignas(16) float qs[8][128];
-  float QS[8][2];
-  alignas(16) float p[kAttWarps][8][kAttTile];
-  Partial4 wp_dummy;
-  alignas(16) float wacc[kAttWarps][8][128];
-  float wm[kAttWarps][8], wl[kAttWarps][8];
+  AttnScratch sc;
   uint64_t bar;
 };
 
-__device__ __forceinline__ uint32_t code_of(const uint32_t* row, int bits, int d) {
-  return bits == 4 ? (row[d >> 3] >> (4 * (d & 7))) & 15u : (row[d >> 2] >> (8 * (d & 3))) & 255u;
-}
-
-// Issue the bulk copies of block b of kv head g (n tokens, rounded up to 4).
+// Issue the bulk copies of block b (local index) of kv head g, n tokens
+// (rounded up to 4).
 template <int BITS>
 __device__ __forceinline__ void issue_kv_tile(AttnSmem<BITS>& sm, const AttnArgs& a, int g, int b_local, int n) {
-  using Tl = AttnTile<BITS>;
+  constexpr int RW = AttnSmem<BITS>::ROW_WORDS;
   const int n4 = (n + 3) & ~3;
   const size_t slot = size_t(g) * a.capacity + size_t(b_local) * kAttBlock;
-  const uint32_t cb = uint32_t(n4) * Tl::ROW_BYTES, sbytes = uint32_t(n4) * 4;
+  const uint32_t cb = uint32_t(n4) * RW * 4, sbytes = uint32_t(n4) * 4;
   mbar_expect_tx(&sm.bar, 2 * cb + 4 * sbytes);
-  bulk_g2s(sm.tile.kc, a.k_codes + slot * Tl::ROW_WORDS, cb, &sm.bar);
-  bulk_g2s(sm.tile.vc, a.v_codes + slot * Tl::ROW_WORDS, cb, &sm.bar);
-  bulk_g2s(sm.tile.ks, a.k_scales + slot * 2, sbytes, &sm.bar);
-  bulk_g2s(sm.tile.kb, a.k_biases + slot * 2, sbytes, &sm.bar);
-  bulk_g2s(sm.tile.vs, a.v_scales + slot * 2, sbytes, &sm.bar);
-  bulk_g2s(sm.tile.vb, a.v_biases + slot * 2, sbytes, &sm.bar);
+  bulk_g2s(sm.kc, a.k_codes + slot * RW, cb, &sm.bar);
+  bulk_g2s(sm.vc, a.v_codes + slot * RW, cb, &sm.bar);
+  bulk_g2s(sm.ks, a.k_scales + slot * 2, sbytes, &sm.bar);
+  bulk_g2s(sm.kb, a.k_biases + slot * 2, sbytes, &sm.bar);
+  bulk_g2s(sm.vs, a.v_scales + slot * 2, sbytes, &sm.bar);
+  bulk_g2s(sm.vb, a.v_biases + slot * 2, sbytes, &sm.bar);
 }
 
-__device__ __forceinline__ int att_hq(int hkv, int nblk, int grid) {
-  // q heads per work item: as few as possible while keeping ~2 items per CTA
-  int hq = 1;
-  while (hq < 8 && hkv * (8 / hq) * nblk > 2 * grid) hq *= 2;
-  return hq;
-}
-
-// Score of the lane's token for one head; krow holds the token's code words.
-template <int BITS>
-__device__ __forceinline__ float att_score(const uint32_t (&krow)[AttnTile<BITS>::ROW_WORDS], const float* qs,
-                                           const float* QS, float s0, float b0, float s1, float b1) {
-  float A[2];
-#pragma unroll
-  for (int g = 0; g < 2; ++g) {
-    float acc4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-    for (int d0 = 64 * g; d0 < 64 * g + 64; d0 += 4) {
-      const float4 q4 = *reinterpret_cast<const float4*>(qs + d0);
-      const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int d = d0 + j;
-        const uint32_t c = BITS == 4 ? (krow[d >> 3] >> (4 * (d & 7))) & 15u : (krow[d >> 2] >> (8 * (d & 3))) & 255u;
-        acc4[j] = __fmaf_rn(qv[j], float(c), acc4[j]);
-      }
-    }
-    A[g] = __fadd_rn(__fadd_rn(acc4[0], acc4[1]), __fadd_rn(acc4[2], acc4[3]));
-  }
-  float t = __fmaf_rn(b0, QS[0], __fmul_rn(s0, A[0]));
-  t = __fmaf_rn(s1, A[1], t);
-  t = __fmaf_rn(b1, QS[1], t);
-  return rbf(t);
-}
+struct CtaSync {
+  __device__ void operator()() const { __syncthreads(); }
+};
 
 // Block partials.  Persistent grid; work item = (block, kv head, q-head slice).
 template <int BITS>
-__global__ void __launch_bounds__(128, 2) k_attn_partial(const AttnArgs a) {
-  using Tl = AttnTile<BITS>;
+__global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnArgs a) {
+  constexpr int RW = AttnSmem<BITS>::ROW_WORDS;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnSmem<BITS>& sm = *reinterpret_cast<AttnSmem<BITS>*>(smem_raw);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.bar, 1);
@@ -188,11 +261,12 @@ __global__ void __launch_bounds__(128, 2) k_attn_partial(const AttnArgs a) {
   const int b0 = a.block_begin, b1 = min(a.block_end, nblk_total);
   const int nblk = max(b1 - b0, 0);
   const int hq = att_hq(a.hkv, max(nblk, 1), gridDim.x);
-  const int nq = (a.hq / a.hkv) / hq;  // q-head slices per kv head
+  const int nq = (a.hq / a.hkv) / hq;
   const int items = nblk * a.hkv * nq;
-  const bool pos_ok = p >= 0 && p < a.capacity + a.token_base && p >= a.token_base - 0;
+  const bool pos_ok = p >= a.token_base && p < a.capacity + a.token_base;
+  const int blk0 = a.token_base / kAttBlock;
 
-  auto item_coords = [&](int it, int& b, int& g, int& qsub) {
+  auto coords = [&](int it, int& b, int& g, int& qsub) {
     qsub = it % nq;
     g = (it / nq) % a.hkv;
     b = b0 + it / (nq * a.hkv);
@@ -200,12 +274,12 @@ __global__ void __launch_bounds__(128, 2) k_attn_partial(const AttnArgs a) {
   auto block_tokens = [&](int b) { return min(kAttBlock, T - b * kAttBlock); };
 
   uint32_t phase = 0;
-  bool pending = false;
   int it = blockIdx.x;
+  bool pending = false;
   if (threadIdx.x == 0 && it < items && pos_ok) {
-    int b, g, qs_;
-    item_coords(it, b, g, qs_);
-    issue_kv_tile<BITS>(sm, a, g, b - a.token_base / kAttBlock, block_tokens(b));
+    int b, g, q_;
+    coords(it, b, g, q_);
+    issue_kv_tile<BITS>(sm, a, g, b - blk0, block_tokens(b));
   }
   pending = it < items && pos_ok;
   if (a.pdl) grid_wait();
@@ -214,210 +288,55 @@ __global__ void __launch_bounds__(128, 2) k_attn_partial(const AttnArgs a) {
     if (blockIdx.x == 0 && threadIdx.x == 0) report(a.status, kStatusBadPosition);
     return;
   }
-
+  const float* cs = a.rope + size_t(p - a.token_base) * 128;
   for (; it < items; it += gridDim.x) {
     int b, g, qsub;
-    item_coords(it, b, g, qsub);
+    coords(it, b, g, qsub);
     const int n = block_tokens(b);
-    const int h0 = g * (a.hq / a.hkv) + qsub * hq;
-    if (!pending && threadIdx.x == 0) issue_kv_tile<BITS>(sm, a, g, b - a.token_base / kAttBlock, n);
+    if (!pending && threadIdx.x == 0) issue_kv_tile<BITS>(sm, a, g, b - blk0, n);
     pending = false;
-
-    // --- queries: (norm,) RoPE, scale, group sums ---------------------------
-    const float* cs = a.rope + size_t(p - a.token_base) * 128;
-    for (int hh = warp; hh < hq; hh += kAttWarps) {
-      const uint16_t* qr = a.qkv + (h0 + hh) * 128;
-      float x[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) x[j] = bf(qr[4 * lane + j]);
-      if (a.q_norm) head_norm4(x, a.q_norm, a.eps);
-      // RoPE on pairs (i, i+64): exchange halves through shared memory
-#pragma unroll
-      for (int j = 0; j < 4; ++j) sm.qs[hh][4 * lane + j] = x[j];
-      __syncwarp();
-      float y[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int d = 4 * lane + j, i = d & 63;
-        const float c = cs[i], s = cs[64 + i];
-        const float lo = sm.qs[hh][i], hi = sm.qs[hh][i + 64];
-        y[j] = d < 64 ? rbf(__fmaf_rn(lo, c, -__fmul_rn(hi, s))) : rbf(__fmaf_rn(lo, s, __fmul_rn(hi, c)));
-      }
-      __syncwarp();
-#pragma unroll
-      for (int j = 0; j < 4; ++j) sm.qs[hh][4 * lane + j] = rbf(__fmul_rn(y[j], kQScale));
-      __syncwarp();
-      if (lane < 2) {
-        float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int d = 64 * lane; d < 64 * lane + 64; ++d) a4[d & 3] = __fadd_rn(a4[d & 3], sm.qs[hh][d]);
-        sm.QS[hh][lane] = __fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]));
-      }
-    }
-
-    // --- tile arrival -------------------------------------------------------
-    bool ok = mbar_wait(&sm.bar, phase);
+    const bool ok = mbar_wait(&sm.bar, phase);
     phase ^= 1;
     if (!__syncthreads_and(ok)) {
-      if (threadIdx.x == 0) report(a.status, kStatusBulkTimeout);
-      if (threadIdx.x == 0) mbar_wait(&sm.bar, phase ^ 1);
+      if (threadIdx.x == 0) {
+        report(a.status, kStatusBulkTimeout);
+        mbar_wait(&sm.bar, phase ^ 1);
+      }
       return;
     }
-
-    // --- the new token: RoPE'd k and v, quantized, patched into the tile ----
-    if (p >= b * kAttBlock && p < b * kAttBlock + n) {
-      const int tloc = p - b * kAttBlock;
-      // warps 0,1: k groups 0,1; warps 2,3: v groups 0,1
-      const bool is_k = warp < 2;
-      const int grp = warp & 1;
-      const uint16_t* src = a.qkv + (a.hq + (is_k ? 0 : a.hkv) + g) * 128;
-      float kv4[4];
-      // each warp needs the full head for norm/RoPE of k; compute all 128 dims
-#pragma unroll
-      for (int j = 0; j < 4; ++j) kv4[j] = bf(src[4 * lane + j]);
-      if (is_k) {
-        if (a.k_norm) head_norm4(kv4, a.k_norm, a.eps);
-        float* tmp = sm.wacc[warp][0];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) tmp[4 * lane + j] = kv4[j];
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int d = 4 * lane + j, i = d & 63;
-          const float c = cs[i], s = cs[64 + i];
-          const float lo = tmp[i], hi = tmp[i + 64];
-          kv4[j] = d < 64 ? rbf(__fmaf_rn(lo, c, -__fmul_rn(hi, s))) : rbf(__fmaf_rn(lo, s, __fmul_rn(hi, c)));
-        }
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 4; ++j) tmp[4 * lane + j] = kv4[j];
-      } else {
-        float* tmp = sm.wacc[warp][0];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) tmp[4 * lane + j] = kv4[j];
-      }
-      __syncwarp();
-      const float* tmp = sm.wacc[warp][0];
-      const float v0 = tmp[64 * grp + 2 * lane], v1 = tmp[64 * grp + 2 * lane + 1];
-      QGroupParams qp = warp_group_params(v0, v1, BITS);
-      const uint32_t word = warp_pack(quant_code(v0, qp, BITS), quant_code(v1, qp, BITS), BITS);
-      constexpr int GW = 64 * BITS / 32;  // words per group
-      uint32_t* crow = (is_k ? sm.tile.kc : sm.tile.vc) + tloc * Tl::ROW_WORDS + grp * GW;
-      if (lane < GW) crow[lane] = word;
-      const uint16_t sc = to_bf(qp.scale), bi = to_bf(qp.bias);
-      if (lane == 0) {
-        (is_k ? sm.tile.ks : sm.tile.vs)[tloc * 2 + grp] = sc;
-        (is_k ? sm.tile.kb : sm.tile.vb)[tloc * 2 + grp] = bi;
-      }
-      if (qsub == 0) {  // one writer per kv head publishes the new slot
-        const size_t slot = size_t(g) * a.capacity + size_t(p - a.token_base);
-        uint32_t* gc = (is_k ? a.k_codes : a.v_codes) + slot * Tl::ROW_WORDS + grp * GW;
-        if (lane < GW) gc[lane] = word;
-        if (lane == 0) {
-          (is_k ? a.k_scales : a.v_scales)[slot * 2 + grp] = sc;
-          (is_k ? a.k_biases : a.v_biases)[slot * 2 + grp] = bi;
-        }
-      }
+    AttnBlock ai = {};
+    ai.qkv = a.qkv;
+    ai.hq_total = a.hq;
+    ai.hkv = a.hkv;
+    ai.g = g;
+    ai.h0 = g * (a.hq / a.hkv) + qsub * hq;
+    ai.hq = hq;
+    ai.n = n;
+    ai.cs = cs;
+    ai.q_norm = a.q_norm;
+    ai.k_norm = a.k_norm;
+    ai.eps = a.eps;
+    ai.has_new = p >= b * kAttBlock && p < b * kAttBlock + n;
+    ai.tnew = p - b * kAttBlock;
+    if (ai.has_new && qsub == 0) {
+      const size_t slot = size_t(g) * a.capacity + size_t(p - a.token_base);
+      ai.g_kcodes = a.k_codes + slot * RW;
+      ai.g_vcodes = a.v_codes + slot * RW;
+      ai.g_ks = a.k_scales + slot * 2;
+      ai.g_kb = a.k_biases + slot * 2;
+      ai.g_vs = a.v_scales + slot * 2;
+      ai.g_vb = a.v_biases + slot * 2;
     }
-    __syncthreads();
-
-    // --- per-warp online softmax over tiles w, w+4 --------------------------
-    float m[8], l[8], acc[8][4];
-#pragma unroll
-    for (int hh = 0; hh < 8; ++hh) {
-      m[hh] = -INFINITY;
-      l[hh] = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[hh][j] = 0.0f;
+    TileView tv = {sm.kc, sm.vc, sm.ks, sm.kb, sm.vs, sm.vb};
+    Partial4 P;
+    attn_block<BITS>(ai, tv, sm.sc, warp, CtaSync{}, P);
+    if (warp < hq) {
+      const int nblk_cap = a.capacity / kAttBlock;
+      store_partial(a.partials + (size_t(ai.h0 + warp) * nblk_cap + (b - blk0)) * kPartialFloats, P);
     }
-    for (int tile = warp; tile < kAttBlock / kAttTile; tile += kAttWarps) {
-      const int base = tile * kAttTile;
-      if (base >= n) break;
-      const int tl = base + lane;
-      const bool valid = tl < n;
-      // scores (lane = token)
-      uint32_t krow[Tl::ROW_WORDS];
-#pragma unroll
-      for (int w = 0; w < Tl::ROW_WORDS; w += 4) {
-        const uint4 q4 = *reinterpret_cast<const uint4*>(&sm.tile.kc[(valid ? tl : 0) * Tl::ROW_WORDS + w]);
-        krow[w] = q4.x;
-        krow[w + 1] = q4.y;
-        krow[w + 2] = q4.z;
-        krow[w + 3] = q4.w;
-      }
-      const float s0 = bf(sm.tile.ks[(valid ? tl : 0) * 2]), s1 = bf(sm.tile.ks[(valid ? tl : 0) * 2 + 1]);
-      const float bb0 = bf(sm.tile.kb[(valid ? tl : 0) * 2]), bb1 = bf(sm.tile.kb[(valid ? tl : 0) * 2 + 1]);
-      for (int hh = 0; hh < hq; ++hh) {
-        const float sc = valid ? att_score<BITS>(krow, sm.qs[hh], sm.QS[hh], s0, bb0, s1, bb1) : -INFINITY;
-        const float tmax = bfly_max(sc);
-        const float mnew = fmaxf(m[hh], tmax);
-        const float alpha = rexp(__fsub_rn(m[hh], mnew));
-        const float pt = valid ? rexp(__fsub_rn(sc, mnew)) : 0.0f;
-        const float ts = bfly_sum(pt);
-        l[hh] = __fmaf_rn(l[hh], alpha, ts);
-        m[hh] = mnew;
-        sm.p[warp][hh][lane] = pt;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[hh][j] = __fmul_rn(acc[hh][j], alpha);
-      }
-      __syncwarp();
-      // P*V (lane = 4 dims)
-      const int nt = min(kAttTile, n - base);
-      const int grp = lane >> 4;
-      for (int t = 0; t < nt; ++t) {
-        const int tok = base + t;
-        uint32_t c4;
-        if constexpr (BITS == 4) {
-          const uint16_t* row16 = reinterpret_cast<const uint16_t*>(sm.tile.vc + tok * Tl::ROW_WORDS);
-          c4 = row16[lane];
-        } else {
-          c4 = sm.tile.vc[tok * Tl::ROW_WORDS + lane];
-        }
-        const float vs = bf(sm.tile.vs[tok * 2 + grp]), vb = bf(sm.tile.vb[tok * 2 + grp]);
-        float v[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t c = BITS == 4 ? (c4 >> (4 * j)) & 15u : (c4 >> (8 * j)) & 255u;
-          v[j] = __fmaf_rn(vs, float(c), vb);
-        }
-        for (int hh = 0; hh < hq; ++hh) {
-          const float pp = sm.p[warp][hh][t];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) acc[hh][j] = __fmaf_rn(pp, v[j], acc[hh][j]);
-        }
-      }
-      __syncwarp();
-    }
-    // --- warp partials -> block partial (warps merged in order) --------------
-    for (int hh = 0; hh < hq; ++hh) {
-      if (lane == 0) {
-        sm.wm[warp][hh] = m[hh];
-        sm.wl[warp][hh] = l[hh];
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) sm.wacc[warp][hh][4 * lane + j] = acc[hh][j];
-    }
-    __syncthreads();
-    for (int hh = warp; hh < hq; hh += kAttWarps) {
-      Partial4 P;
-      P.m = -INFINITY;
-      P.l = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) P.a[j] = 0.0f;
-      for (int w = 0; w < kAttWarps; ++w) {
-        Partial4 Q;
-        Q.m = sm.wm[w][hh];
-        Q.l = sm.wl[w][hh];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) Q.a[j] = sm.wacc[w][hh][4 * lane + j];
-        merge_into(P, Q);
-      }
-      float* dst = a.partials + (size_t(h0 + hh) * (a.capacity / kAttBlock) + (b - a.token_base / kAttBlock)) * kPartialFloats;
-      if (lane == 0) {
-        dst[0] = P.m;
-        dst[1] = P.l;
-      }
-      *reinterpret_cast<float4*>(dst + 4 + 4 * lane) = make_float4(P.a[0], P.a[1], P.a[2], P.a[3]);
-    }
+    // the tile was patched by the generic proxy; order that before the next
+    // bulk copy overwrites it
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
   }
 }
@@ -439,11 +358,7 @@ __global__ void __launch_bounds__(32) k_attn_combine(const AttnArgs a) {
   const int nblk_cap = a.capacity / kAttBlock;
   for (int si = blockIdx.y; si < max(n_local, 0); si += gridDim.y) {
     const int s = s_first + si;
-    Partial4 P;
-    P.m = -INFINITY;
-    P.l = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) P.a[j] = 0.0f;
+    Partial4 P = empty_partial();
     const int bb0 = max(s * kAttSuper, b0), bb1 = min((s + 1) * kAttSuper, b1);
     for (int b = bb0; b < bb1; ++b) {
       const float* src = a.partials + (size_t(h) * nblk_cap + (b - a.token_base / kAttBlock)) * kPartialFloats;
@@ -469,11 +384,7 @@ __global__ void __launch_bounds__(32) k_attn_combine(const AttnArgs a) {
   prev = __shfl_sync(0xffffffffu, prev, 0);
   if (prev != gridDim.y - 1) return;
   __threadfence();
-  Partial4 F;
-  F.m = -INFINITY;
-  F.l = 0.0f;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) F.a[j] = 0.0f;
+  Partial4 F = empty_partial();
   if (a.sinks) {
     F.m = bf(a.sinks[h]);
     F.l = 1.0f;

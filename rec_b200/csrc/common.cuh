@@ -46,6 +46,11 @@ template <int SD>
 __device__ __forceinline__ float sb(uint16_t v) {
   if constexpr (SD == 0) return hf(v); else return bf(v);
 }
+// SD == 2: the type is a runtime flag (1 = bf16).
+template <int SD>
+__device__ __forceinline__ float sb(uint16_t v, int sd_rt) {
+  if constexpr (SD == 2) return sd_rt ? bf(v) : hf(v); else return sb<SD>(v);
+}
 
 // ----------------------------------------------------------------------------
 // Deterministic exp.  Cody-Waite reduction x = n*ln2 + r with ln2 split in a

@@ -161,6 +161,8 @@ struct RecCtx {
   unsigned* mega_cnt = nullptr;      // [2] grid barrier + abort, [Hq] heads, [Hq*n_super] supers
   unsigned long long* prof = nullptr;  // optional phase timeline
   size_t prof_entries = 0;
+  unsigned long long* prof2 = nullptr;  // optional stamps inside one layer
+  int prof_layer = -1;
 };
 
 namespace {
@@ -281,11 +283,10 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
       a.final_merge = 1;
       a.status = status;
       a.pdl = pdl;
-      a.pdl = pdl;
       const int agrid = 2 * sm_count();
       if (kind == kKAttn)
-        return d.kv_bits == 4 ? launch(k_attn_partial<4>, agrid, 128, sizeof(AttnSmem<4>), st, pdl, a)
-                              : launch(k_attn_partial<8>, agrid, 128, sizeof(AttnSmem<8>), st, pdl, a);
+        return d.kv_bits == 4 ? launch(k_attn_partial<4>, agrid, kAttWarps * 32, sizeof(AttnSmem<4>), st, pdl, a)
+                              : launch(k_attn_partial<8>, agrid, kAttWarps * 32, sizeof(AttnSmem<8>), st, pdl, a);
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(d.n_q_heads, std::max(1, c->n_super_max));
       cfg.blockDim = dim3(32);
@@ -467,7 +468,7 @@ REC_API int rec_create(const RecModelDesc* desc, RecCtx** out) {
   REC_CHECK_ARG(d.scale_dtype == REC_SCALE_FP16 || d.scale_dtype == REC_SCALE_BF16, "bad scale dtype");
   REC_CHECK_ARG(d.kv_bits == 4 || d.kv_bits == 8, "kv_bits must be 4 or 8");
   REC_CHECK_ARG(d.router_mode == REC_ROUTER_SOFTMAX || d.router_mode == REC_ROUTER_SIGMOID, "bad router mode");
-  REC_CHECK_ARG(d.n_layers >= 1, "need at least one layer");
+  REC_CHECK_ARG(d.n_layers >= 1 && d.n_layers <= kMaxLayers, "n_layers must be in 1..%d", kMaxLayers);
   RecCtx* c = new RecCtx();
   c->d = d;
   c->grid = sm_count();
@@ -614,7 +615,7 @@ static int check_ready(RecCtx* c) {
 }
 
 // One cooperative launch of the persistent kernel for `steps` tokens.
-template <int SD, int I>
+template <int I, int BITS>
 static cudaError_t launch_mega_t(RecCtx* c, int steps, cudaStream_t st) {
   const RecModelDesc& d = c->d;
   MegaArgs A = {};
@@ -629,6 +630,7 @@ static cudaError_t launch_mega_t(RecCtx* c, int steps, cudaStream_t st) {
   A.V = d.vocab;
   A.kv_bits = d.kv_bits;
   A.router_mode = d.router_mode;
+  A.sd = d.scale_dtype == REC_SCALE_BF16 ? 1 : 0;
   A.capacity = c->capacity;
   A.n_super_max = c->n_super_max;
   A.eps = d.rms_eps;
@@ -654,7 +656,9 @@ static cudaError_t launch_mega_t(RecCtx* c, int steps, cudaStream_t st) {
   A.steps = steps;
   const size_t need = size_t(steps) * (6 * d.n_layers + 1) * c->grid * 2;
   A.prof = (c->prof && c->prof_entries >= need) ? c->prof : nullptr;
-  auto kern = k_decode_mega<SD, I>;
+  A.prof2 = c->prof2;
+  A.prof_layer = c->prof_layer;
+  auto kern = k_decode_mega<I, BITS>;
   const size_t smem = sizeof(MegaSmem);
   static std::mutex mu;
   static std::set<const void*> configured;
@@ -682,12 +686,12 @@ static cudaError_t launch_mega_t(RecCtx* c, int steps, cudaStream_t st) {
 }
 
 static cudaError_t launch_mega(RecCtx* c, int steps, cudaStream_t st) {
-  const bool fp16 = c->d.scale_dtype == REC_SCALE_FP16;
+  const bool kv4 = c->d.kv_bits == 4;
   switch (c->d.moe_inter) {
-    case 256: return fp16 ? launch_mega_t<0, 256>(c, steps, st) : launch_mega_t<1, 256>(c, steps, st);
-    case 512: return fp16 ? launch_mega_t<0, 512>(c, steps, st) : launch_mega_t<1, 512>(c, steps, st);
-    case 768: return fp16 ? launch_mega_t<0, 768>(c, steps, st) : launch_mega_t<1, 768>(c, steps, st);
-    case 1024: return fp16 ? launch_mega_t<0, 1024>(c, steps, st) : launch_mega_t<1, 1024>(c, steps, st);
+    case 256: return kv4 ? launch_mega_t<256, 4>(c, steps, st) : launch_mega_t<256, 8>(c, steps, st);
+    case 512: return kv4 ? launch_mega_t<512, 4>(c, steps, st) : launch_mega_t<512, 8>(c, steps, st);
+    case 768: return kv4 ? launch_mega_t<768, 4>(c, steps, st) : launch_mega_t<768, 8>(c, steps, st);
+    case 1024: return kv4 ? launch_mega_t<1024, 4>(c, steps, st) : launch_mega_t<1024, 8>(c, steps, st);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -759,6 +763,14 @@ REC_API int rec_set_profile(RecCtx* c, void* buf_dev, size_t entries) {
   REC_CHECK_ARG(c, "null context");
   c->prof = static_cast<unsigned long long*>(buf_dev);
   c->prof_entries = buf_dev ? entries : 0;
+  return REC_OK;
+}
+
+REC_API int rec_set_layer_profile(RecCtx* c, void* buf_dev, int32_t layer) {
+  REC_CHECK_ARG(c, "null context");
+  REC_CHECK_ARG(!buf_dev || (layer >= 0 && layer < c->d.n_layers), "layer out of range");
+  c->prof2 = static_cast<unsigned long long*>(buf_dev);
+  c->prof_layer = buf_dev ? layer : -1;
   return REC_OK;
 }
 

@@ -97,10 +97,12 @@ struct StageCursor {
 
 // Rows computed together by one warp (independent dependency chains).
 template <int K>
-constexpr int gemv_ilp() { return KCfg<K>::wide ? 4 : 2; }
+constexpr int gemv_ilp() { return KCfg<K>::wide ? 4 : 1; }
 // Stage rows: one full pass of the CTA over its row slots.
 template <int K>
-constexpr int gemv_rs() { return (kWarps / (KCfg<K>::wide ? KCfg<K>::SEG : 1)) * (KCfg<K>::wide ? 1 : 4) * gemv_ilp<K>(); }
+constexpr int gemv_rs() {
+  return (kWarps / (KCfg<K>::wide ? KCfg<K>::SEG : 1)) * (32 / KCfg<K>::T) * gemv_ilp<K>();
+}
 
 template <int K, int SD, int RS, int NS, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
@@ -144,19 +146,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
       *reinterpret_cast<uint4*>(sm.xn + i) = ldg128(a.x + i);
     __syncthreads();
   }
+  const FixScale fs = fix_scale_from_max(block_maxabs(sm.xn, K, threadIdx.x, kThreads, sm.red, 0));
   // Team layout: TEAM warps per row for SEG > 1 (one segment each); for
-  // narrow K, 4 rows per warp with 8 lanes each.
+  // narrow K, 8 rows per warp with 4 lanes each.
   constexpr int SEG = C::SEG;
   constexpr int TEAM = C::wide ? SEG : 1;
   static_assert(kWarps % TEAM == 0, "teams must tile the CTA");
   constexpr int TEAMS = kWarps / TEAM;
-  constexpr int ROWS_PER_WARP = C::wide ? 1 : 4;
+  constexpr int ROWS_PER_WARP = 32 / C::T;
   const int seg = C::wide ? warp % TEAM : 0;
   const int team = warp / TEAM;
-  const int sub = C::wide ? 0 : lane >> 3;   // row slot inside the warp (narrow)
-  const int l = C::wide ? lane : (lane & 7);  // lane inside the row
-  ChunkX cx[C::CH];
-  prep_lane_x<K>(sm.xn, seg, l, cx);
+  const int sub = lane / C::T;  // row slot inside the warp
+  const int l = lane % C::T;    // lane inside the row
+  GroupX gx[C::GPL];
+  prep_lane_x<K>(sm.xn, fs, seg, l, gx);
 
   float best = -INFINITY;
   int best_i = 0x7fffffff;
@@ -185,11 +188,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
           rows[i] = valid[i] ? r : 0;
         }
         float v[ILP];
-        lane_rows_partial<K, SD, ILP>(wbase, sbase, bbase, rows, seg, l, cx, v);
+        lane_rows_partial<K, SD, ILP>(wbase, sbase, bbase, rows, seg, l, gx, v);
 #pragma unroll
         for (int i = 0; i < ILP; ++i) {
           if (!valid[i]) v[i] = 0.0f;
-          if constexpr (C::wide) v[i] = bfly_sum<32>(v[i]); else v[i] = bfly_sum<8>(v[i]);
+          v[i] = row_reduce<K>(v[i]);
         }
         if constexpr (SEG > 1) {
           // segment partials added in order by the team's first warp
@@ -211,6 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
 #pragma unroll
         for (int i = 0; i < ILP; ++i) {
           const bool writer = valid[i] && (C::wide ? (lane == 0 && seg == 0) : (l == 0));
+          v[i] = __fmul_rn(v[i], fs.down);
           if (writer) {
             const int grow = g0 + rows[i];
             if constexpr (EPI == kEpiStore) {

@@ -36,13 +36,13 @@ constexpr int kMegaThreads = 32 * (kMegaCons + 1);  // + producer warp
 constexpr int kSlotBytes = 36864;
 constexpr int kSlots = 4;
 constexpr int kBarCons = 1;   // named barrier: all consumer warps
-constexpr int kBarAttn = 6;   // named barrier: consumer warps 0..3
 constexpr int kBarTeam0 = 2;  // named barriers 2..5: warp pairs (K = 4096 rows)
 constexpr int kQRows = 32;    // rows per Q / H chunk (K = 2048)
 constexpr int kORows = 16;    // rows per O chunk (K = 4096)
 constexpr int kGPairs = 16;   // gate/up pairs per G chunk
 constexpr int kDExperts = 4;  // experts per D chunk
 constexpr int kDRowsMax = 16; // output rows per CTA in O / D
+constexpr int kMaxLayers = 64;  // layer descriptors kept in shared memory
 
 struct MegaLayer {
   QMatDev q, k, v, o, gate, up, down;
@@ -64,6 +64,7 @@ struct MegaLayer {
 struct MegaArgs {
   const MegaLayer* layers;
   int n_layers, H, hq, hkv, E, k, I, V, kv_bits, router_mode, capacity, n_super_max;
+  int sd;  // scale/bias type of the int4 weights: 0 fp16, 1 bf16
   float eps;
   QMatDev embed, lm_head;
   const uint16_t* final_norm;
@@ -76,6 +77,8 @@ struct MegaArgs {
   int* cand_idx;
   int steps;
   unsigned long long* prof;  // optional: [barrier][cta] x (arrive, release) globaltimer stamps
+  unsigned long long* prof2; // optional: [cta][32] stamps inside layer prof_layer of step 0
+  int prof_layer;
 };
 
 __device__ __forceinline__ unsigned long long globaltimer() {
@@ -86,14 +89,11 @@ __device__ __forceinline__ unsigned long long globaltimer() {
 
 struct MegaSmem {
   alignas(128) uint8_t ring[kSlots][kSlotBytes];
+  MegaLayer layers[kMaxLayers];  // descriptors, copied once per launch
   alignas(16) uint16_t h0[2048];
   alignas(16) uint16_t xn[4096];
   alignas(16) uint16_t act[kMaxTopK * 1024];
-  alignas(16) float qs[8][128];
-  float QS[8][2];
-  alignas(16) float p[4][8][32];
-  alignas(16) float wacc[4][8][128];
-  float wm[4][8], wl[4][8];
+  AttnScratch att;
   float red[40];
   float seg_part[kMegaCons][4];
   float best_val[kMegaCons];
@@ -104,13 +104,16 @@ struct MegaSmem {
   float wts[kMaxTopK];
   float dsm[kMaxTopK][kDRowsMax];
   uint64_t full[kSlots], empty[kSlots];
+  uint16_t hown[kDRowsMax];  // this CTA's rows of h (it owns them in embed, O and D)
   volatile int route_seq;
   int token;
   int token0, pos0;  // starting token / position, read once at kernel entry
 };
 
 __device__ __forceinline__ void cons_sync() { asm volatile("bar.sync %0, %1;" ::"r"(kBarCons), "r"(kMegaCons * 32)); }
-__device__ __forceinline__ void attn_sync() { asm volatile("bar.sync %0, %1;" ::"r"(kBarAttn), "r"(128)); }
+struct ConsSync {
+  __device__ void operator()() const { cons_sync(); }
+};
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
@@ -159,15 +162,19 @@ __device__ __forceinline__ AttnPlan attn_plan(const MegaArgs& a, int pos) {
   AttnPlan p;
   p.T = pos + 1;
   p.nblk = (p.T + kAttBlock - 1) / kAttBlock;
-  p.hq = att_hq(a.hkv, p.nblk, gridDim.x);
+  p.hq = att_hq(a.hkv, p.nblk, gridDim.x / 2);  // at most one item per CTA while that is possible
   p.nq = (a.hq / a.hkv) / p.hq;
   p.items = p.nblk * a.hkv * p.nq;
   return p;
 }
-__device__ __forceinline__ void attn_item(const AttnPlan& P, int hkv, int it, int& b, int& g, int& qsub) {
+__device__ __forceinline__ void attn_coords(const AttnPlan& P, int hkv, int it, int& b, int& g, int& qsub) {
   qsub = it % P.nq;
   g = (it / P.nq) % hkv;
   b = it / (P.nq * hkv);
+}
+
+__device__ __forceinline__ void stamp(const MegaArgs& a, int step, int layer, int slot) {
+  if (a.prof2 && step == 0 && layer == a.prof_layer) a.prof2[blockIdx.x * 32 + slot] = globaltimer();
 }
 
 // Grid barrier index of a phase: each step has 6 per layer + 1 (after H).
@@ -312,7 +319,7 @@ struct Producer {
       const int pos = pos0 + step;
       const AttnPlan AP = attn_plan(a, pos);
       for (int l = 0; l < a.n_layers && ok; ++l) {
-        const MegaLayer& L = a.layers[l];
+        const MegaLayer& L = sm.layers[l];
         if (lane == 0) {
           // Q rows (q | k | v), chunks never cross matrices
           for (int r = P.q0; r < P.q1 && ok;) {
@@ -325,7 +332,7 @@ struct Producer {
           // A: K and V tiles of this CTA's items
           for (int it = blockIdx.x; it < AP.items && ok; it += gridDim.x) {
             int b, g, qsub;
-            attn_item(AP, a.hkv, it, b, g, qsub);
+            attn_coords(AP, a.hkv, it, b, g, qsub);
             const int n = min(kAttBlock, AP.T - b * kAttBlock);
             kv_chunk(L.k_codes, L.k_scales, L.k_biases, g, b, n);
             kv_chunk(L.v_codes, L.v_scales, L.v_biases, g, b, n);
@@ -336,6 +343,7 @@ struct Producer {
           const int seq = step * a.n_layers + l + 1;
           uint32_t spins = 0;
           while (sm.route_seq < seq) {
+            __nanosleep(64);  // a hot spin would take issue slots from the consumer warps
             if (aborted(a)) { ok = false; break; }
             if (++spins > kSpinLimit * 64) {
               set_abort(a, kStatusCounterTimeout);
@@ -345,6 +353,7 @@ struct Producer {
           }
         }
         __syncwarp();
+        if (lane == 0) stamp(a, step, l, 20);
         if (lane == 0 && ok) {
           int ids[kMaxTopK];
           for (int r = 0; r < a.k; ++r) ids[r] = sm.ids[r];
@@ -352,6 +361,7 @@ struct Producer {
             const int r = u / a.I, i0 = u % a.I;
             const int n = min(min(kGPairs, P.g1 - u), a.I - i0);
             pair_chunk(L, ids[r], i0, n);
+            stamp(a, step, l, 21 + min((u - P.g0) / kGPairs, 3));
             u += n;
           }
           if (P.o1 > P.o0)
@@ -414,45 +424,74 @@ struct Consumers {
     ++chunk;
   }
 
-  // RMSNorm of src (bf16[H], global or shared) into sm.xn (canonical order).
-  __device__ void norm(const uint16_t* src, const uint16_t* w, bool from_smem = false) {
-    const int H = a.H, groups = H >> 8;
-    for (int g = warp; g < groups; g += kMegaCons) {
-      const uint4 u = from_smem ? *reinterpret_cast<const uint4*>(src + (g * 32 + lane) * 8)
-                                : ldcg128(src + (g * 32 + lane) * 8);
-      const uint32_t us[4] = {u.x, u.y, u.z, u.w};
-      float acc = 0.0f;
+  // RMSNorm of src (bf16[2048], global or shared) into sm.xn, canonical
+  // order: consumer thread t owns chunk t (8 elements) = group t/32 = its warp.
+  __device__ FixScale norm(const uint16_t* src, const uint16_t* w, bool from_smem = false) {
+    const int t = threadIdx.x - 32;
+    const uint4 u = from_smem ? *reinterpret_cast<const uint4*>(src + t * 8) : ldcg128(src + t * 8);
+    const uint4 wv = ldg128_nc(w + t * 8);
+    const uint32_t us[4] = {u.x, u.y, u.z, u.w};
+    float x[8];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float x0 = __uint_as_float(us[t] << 16), x1 = __uint_as_float(us[t] & 0xFFFF0000u);
-        acc = __fmaf_rn(x0, x0, acc);
-        acc = __fmaf_rn(x1, x1, acc);
-      }
-      acc = bfly_sum(acc);
-      if (lane == 0) sm.red[g] = acc;
+    for (int q = 0; q < 4; ++q) {
+      x[2 * q] = __uint_as_float(us[q] << 16);
+      x[2 * q + 1] = __uint_as_float(us[q] & 0xFFFF0000u);
     }
+    float acc = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc = __fmaf_rn(x[q], x[q], acc);
+    acc = bfly_sum(acc);
+    if (lane == 0) sm.red[warp] = acc;
     cons_sync();
     if (warp == 0 && lane == 0) {
       float total = 0.0f;
-      for (int g = 0; g < groups; ++g) total = __fadd_rn(total, sm.red[g]);
-      sm.red[32] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, float(H)), a.eps)));
+      for (int g = 0; g < kMegaCons; ++g) total = __fadd_rn(total, sm.red[g]);
+      sm.red[32] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, 2048.0f), a.eps)));
     }
     cons_sync();
     const float inv = sm.red[32];
-    for (int i = threadIdx.x - 32; i < H; i += kMegaCons * 32)
-      sm.xn[i] = to_bf(__fmul_rn(bf(w[i]), rbf(__fmul_rn(from_smem ? bf(src[i]) : ldcg_bf(src + i), inv))));
+    const uint32_t ws_[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+    float mx = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t lo = to_bf(__fmul_rn(__uint_as_float(ws_[q] << 16), rbf(__fmul_rn(x[2 * q], inv))));
+      const uint32_t hi = to_bf(__fmul_rn(__uint_as_float(ws_[q] & 0xFFFF0000u), rbf(__fmul_rn(x[2 * q + 1], inv))));
+      o[q] = lo | (hi << 16);
+      mx = fmaxf(mx, fmaxf(fabsf(bf(uint16_t(lo))), fabsf(bf(uint16_t(hi)))));
+    }
+    *reinterpret_cast<uint4*>(sm.xn + t * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    mx = bfly_max(mx);
+    if (lane == 0) sm.red[8 + warp] = mx;
+    cons_sync();
+    float r = 0.0f;
+    for (int g = 0; g < kMegaCons; ++g) r = fmaxf(r, sm.red[8 + g]);
+    return fix_scale_from_max(r);
+  }
+  // Copies n bf16 (n <= 4096 * ... multiple of 2048) into dst with every load issued
+  // before the first store.
+  __device__ void load_vec(uint16_t* dst, const uint16_t* src, int n) {
+    constexpr int kMax = 4;
+    const int t = threadIdx.x - 32, stride = kMegaCons * 32 * 8;
+    uint4 v[kMax];
+#pragma unroll
+    for (int q = 0; q < kMax; ++q)
+      if (t * 8 + q * stride < n) v[q] = ldcg128(src + t * 8 + q * stride);
+#pragma unroll
+    for (int q = 0; q < kMax; ++q)
+      if (t * 8 + q * stride < n) *reinterpret_cast<uint4*>(dst + t * 8 + q * stride) = v[q];
     cons_sync();
   }
-  __device__ void load_x(const uint16_t* src, int n) {
-    for (int i = (threadIdx.x - 32) * 8; i < n; i += kMegaCons * 32 * 8)
-      *reinterpret_cast<uint4*>(sm.xn + i) = ldcg128(src + i);
-    cons_sync();
+  // Loads x into sm.xn and returns its fixed-point scale.
+  __device__ FixScale load_x(const uint16_t* src, int n) {
+    load_vec(sm.xn, src, n);
+    return fix_scale_from_max(block_maxabs(sm.xn, n, threadIdx.x - 32, kMegaCons * 32, sm.red, kBarCons));
   }
 
   // --- Q and H: K = 2048 rows, 8 warps x ILP 4 ---------------------------------
-  template <int SD, bool HEAD>
-  __device__ void rows2048(const uint8_t* st, int n, int grow0, const ChunkX (&cx)[2], uint16_t* out, float& best,
-                           int& best_i) {
+  template <bool HEAD>
+  __device__ void rows2048(const uint8_t* st, int n, int grow0, const GroupX (&gx)[1], FixScale fs, uint16_t* out,
+                           float& best, int& best_i) {
     const uint32_t wb = uint32_t(n) * 1024, sbytes = uint32_t(n) * 64;
     const uint8_t* wbase = st;
     const uint16_t* sbase = reinterpret_cast<const uint16_t*>(st + wb);
@@ -466,10 +505,10 @@ struct Consumers {
       rows[i] = valid[i] ? r : 0;
     }
     float v[4];
-    lane_rows_partial<2048, SD, 4>(wbase, sbase, bbase, rows, 0, lane, cx, v);
+    lane_rows_partial<2048, 2, 4>(wbase, sbase, bbase, rows, 0, lane, gx, v, a.sd);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      v[i] = bfly_sum(valid[i] ? v[i] : 0.0f);
+      v[i] = __fmul_rn(bfly_sum(valid[i] ? v[i] : 0.0f), fs.down);
       if (valid[i] && lane == 0) {
         const int g = grow0 + rows[i];
         const uint16_t o = to_bf(v[i]);
@@ -483,8 +522,7 @@ struct Consumers {
   }
 
   // --- O: K = 4096 rows, warp pairs (one 2048 segment each) x ILP 4 ---------
-  template <int SD>
-  __device__ void rows4096(const uint8_t* st, int n, int grow0, const ChunkX (&cx)[2]) {
+  __device__ void rows4096(const uint8_t* st, int n, int grow0, int own0, const GroupX (&gx)[1], FixScale fs) {
     // always called by every consumer warp: the team barriers below must match
     const int seg = warp & 1, team = warp >> 1;
     const uint32_t wb = uint32_t(n) * 2048, sbytes = uint32_t(n) * 128;
@@ -500,7 +538,7 @@ struct Consumers {
       rows[i] = valid[i] ? r : 0;
     }
     float v[4];
-    lane_rows_partial<4096, SD, 4>(wbase, sbase, bbase, rows, seg, lane, cx, v);
+    lane_rows_partial<4096, 2, 4>(wbase, sbase, bbase, rows, seg, lane, gx, v, a.sd);
 #pragma unroll
     for (int i = 0; i < 4; ++i) v[i] = bfly_sum(valid[i] ? v[i] : 0.0f);
     if (lane == 0)
@@ -510,209 +548,72 @@ struct Consumers {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         if (!valid[i]) continue;
-        const float t = __fadd_rn(v[i], sm.seg_part[warp + 1][i]);
+        const float t = __fmul_rn(__fadd_rn(v[i], sm.seg_part[warp + 1][i]), fs.down);
         const int g = grow0 + rows[i];
-        a.h[g] = to_bf(__fadd_rn(ldcg_bf(a.h + g), rbf(t)));
+        const int own = g - own0;
+        const uint16_t hn = to_bf(__fadd_rn(bf(sm.hown[own]), rbf(t)));
+        sm.hown[own] = hn;
+        a.h[g] = hn;
       }
     }
     asm volatile("bar.sync %0, %1;" ::"r"(kBarTeam0 + team), "r"(64));
   }
 
   // --- attention ----------------------------------------------------------------
+  // All consumer warps: block b of kv head g (tiles in ring slots kt / vt),
+  // then the last-arriver merges of super-chunk and head.
   template <int BITS>
   __device__ void attn_item_compute(const MegaLayer& L, const AttnPlan& P, int pos, int b, int g, int qsub,
-                                    uint8_t* kt, uint8_t* vt, bool& patched) {
-    // warps 0..3 only
+                                    uint8_t* kt, uint8_t* vt) {
     constexpr int RW = 128 * BITS / 32;
     const int n = min(kAttBlock, P.T - b * kAttBlock), n4 = (n + 3) & ~3;
-    uint32_t* kc = reinterpret_cast<uint32_t*>(kt);
-    uint16_t* ks = reinterpret_cast<uint16_t*>(kt + n4 * RW * 4);
-    uint16_t* kb = ks + n4 * 2;
-    uint32_t* vc = reinterpret_cast<uint32_t*>(vt);
-    uint16_t* vs = reinterpret_cast<uint16_t*>(vt + n4 * RW * 4);
-    uint16_t* vb = vs + n4 * 2;
+    TileView tv;
+    tv.kc = reinterpret_cast<uint32_t*>(kt);
+    tv.ks = reinterpret_cast<uint16_t*>(kt + n4 * RW * 4);
+    tv.kb = tv.ks + n4 * 2;
+    tv.vc = reinterpret_cast<uint32_t*>(vt);
+    tv.vs = reinterpret_cast<uint16_t*>(vt + n4 * RW * 4);
+    tv.vb = tv.vs + n4 * 2;
     const int hq = P.hq;
-    const int h0 = g * (a.hq / a.hkv) + qsub * hq;
-    const float* cs = a.rope + size_t(pos) * 128;
-    for (int hh = warp; hh < hq; hh += 4) {
-      const uint16_t* qr = a.qkv + (h0 + hh) * 128;
-      float x[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) x[j] = ldcg_bf(qr + 4 * lane + j);
-      if (L.q_norm) head_norm4(x, L.q_norm, a.eps);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) sm.qs[hh][4 * lane + j] = x[j];
-      __syncwarp();
-      float y[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int d = 4 * lane + j, i = d & 63;
-        const float c = cs[i], s = cs[64 + i];
-        const float lo = sm.qs[hh][i], hi = sm.qs[hh][i + 64];
-        y[j] = d < 64 ? rbf(__fmaf_rn(lo, c, -__fmul_rn(hi, s))) : rbf(__fmaf_rn(lo, s, __fmul_rn(hi, c)));
-      }
-      __syncwarp();
-#pragma unroll
-      for (int j = 0; j < 4; ++j) sm.qs[hh][4 * lane + j] = rbf(__fmul_rn(y[j], kQScale));
-      __syncwarp();
-      if (lane < 2) {
-        float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int d = 64 * lane; d < 64 * lane + 64; ++d) a4[d & 3] = __fadd_rn(a4[d & 3], sm.qs[hh][d]);
-        sm.QS[hh][lane] = __fadd_rn(__fadd_rn(a4[0], a4[1]), __fadd_rn(a4[2], a4[3]));
-      }
+    AttnBlock ab = {};
+    ab.qkv = a.qkv;
+    ab.hq_total = a.hq;
+    ab.hkv = a.hkv;
+    ab.g = g;
+    ab.h0 = g * (a.hq / a.hkv) + qsub * hq;
+    ab.hq = hq;
+    ab.n = n;
+    ab.cs = a.rope + size_t(pos) * 128;
+    ab.q_norm = L.q_norm;
+    ab.k_norm = L.k_norm;
+    ab.eps = a.eps;
+    ab.has_new = pos >= b * kAttBlock && pos < b * kAttBlock + n;
+    ab.tnew = pos - b * kAttBlock;
+    if (ab.has_new && qsub == 0) {
+      const size_t slot = size_t(g) * a.capacity + size_t(pos);
+      ab.g_kcodes = L.k_codes + slot * RW;
+      ab.g_vcodes = L.v_codes + slot * RW;
+      ab.g_ks = L.k_scales + slot * 2;
+      ab.g_kb = L.k_biases + slot * 2;
+      ab.g_vs = L.v_scales + slot * 2;
+      ab.g_vb = L.v_biases + slot * 2;
     }
-    // the new token: RoPE'd k / v quantized and patched into the tiles
-    if (pos >= b * kAttBlock && pos < b * kAttBlock + n) {
-      patched = true;
-      const int tloc = pos - b * kAttBlock;
-      const bool is_k = warp < 2;
-      const int grp = warp & 1;
-      const uint16_t* src = a.qkv + (a.hq + (is_k ? 0 : a.hkv) + g) * 128;
-      float kv4[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) kv4[j] = ldcg_bf(src + 4 * lane + j);
-      float* tmp = sm.wacc[warp][0];
-      if (is_k) {
-        if (L.k_norm) head_norm4(kv4, L.k_norm, a.eps);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) tmp[4 * lane + j] = kv4[j];
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int d = 4 * lane + j, i = d & 63;
-          const float c = cs[i], s = cs[64 + i];
-          const float lo = tmp[i], hi = tmp[i + 64];
-          kv4[j] = d < 64 ? rbf(__fmaf_rn(lo, c, -__fmul_rn(hi, s))) : rbf(__fmaf_rn(lo, s, __fmul_rn(hi, c)));
-        }
-        __syncwarp();
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) tmp[4 * lane + j] = kv4[j];
-      __syncwarp();
-      const float v0 = tmp[64 * grp + 2 * lane], v1 = tmp[64 * grp + 2 * lane + 1];
-      const QGroupParams qp = warp_group_params(v0, v1, BITS);
-      const uint32_t word = warp_pack(quant_code(v0, qp, BITS), quant_code(v1, qp, BITS), BITS);
-      constexpr int GW = 64 * BITS / 32;
-      uint32_t* crow = (is_k ? kc : vc) + tloc * RW + grp * GW;
-      if (lane < GW) crow[lane] = word;
-      const uint16_t sc = to_bf(qp.scale), bi = to_bf(qp.bias);
-      if (lane == 0) {
-        (is_k ? ks : vs)[tloc * 2 + grp] = sc;
-        (is_k ? kb : vb)[tloc * 2 + grp] = bi;
-      }
-      if (qsub == 0) {
-        const size_t slot = size_t(g) * a.capacity + size_t(pos);
-        uint32_t* gc = (is_k ? L.k_codes : L.v_codes) + slot * RW + grp * GW;
-        if (lane < GW) gc[lane] = word;
-        if (lane == 0) {
-          (is_k ? L.k_scales : L.v_scales)[slot * 2 + grp] = sc;
-          (is_k ? L.k_biases : L.v_biases)[slot * 2 + grp] = bi;
-        }
-      }
-    }
-    attn_sync();
-    // per-warp online softmax over tiles warp, warp+4
-    float m[8], l[8], acc[8][4];
-#pragma unroll
-    for (int hh = 0; hh < 8; ++hh) {
-      m[hh] = -INFINITY;
-      l[hh] = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[hh][j] = 0.0f;
-    }
-    for (int tile = warp; tile < kAttBlock / kAttTile; tile += kAttWarps) {
-      const int base = tile * kAttTile;
-      if (base >= n) break;
-      const int tl = base + lane;
-      const bool valid = tl < n;
-      const int row = valid ? tl : 0;
-      uint32_t krow[RW];
-#pragma unroll
-      for (int w = 0; w < RW; w += 4) {
-        const uint4 q4 = *reinterpret_cast<const uint4*>(&kc[row * RW + w]);
-        krow[w] = q4.x;
-        krow[w + 1] = q4.y;
-        krow[w + 2] = q4.z;
-        krow[w + 3] = q4.w;
-      }
-      const float s0 = bf(ks[row * 2]), s1 = bf(ks[row * 2 + 1]);
-      const float bb0 = bf(kb[row * 2]), bb1 = bf(kb[row * 2 + 1]);
-      for (int hh = 0; hh < hq; ++hh) {
-        const float sc = valid ? att_score<BITS>(krow, sm.qs[hh], sm.QS[hh], s0, bb0, s1, bb1) : -INFINITY;
-        const float tmax = bfly_max(sc);
-        const float mnew = fmaxf(m[hh], tmax);
-        const float alpha = rexp(__fsub_rn(m[hh], mnew));
-        const float pt = valid ? rexp(__fsub_rn(sc, mnew)) : 0.0f;
-        const float ts = bfly_sum(pt);
-        l[hh] = __fmaf_rn(l[hh], alpha, ts);
-        m[hh] = mnew;
-        sm.p[warp][hh][lane] = pt;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[hh][j] = __fmul_rn(acc[hh][j], alpha);
-      }
-      __syncwarp();
-      const int nt = min(kAttTile, n - base);
-      const int grp = lane >> 4;
-      for (int t = 0; t < nt; ++t) {
-        const int tok = base + t;
-        uint32_t c4;
-        if constexpr (BITS == 4) c4 = reinterpret_cast<const uint16_t*>(vc + tok * RW)[lane];
-        else c4 = vc[tok * RW + lane];
-        const float vsc = bf(vs[tok * 2 + grp]), vbi = bf(vb[tok * 2 + grp]);
-        float v[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t c = BITS == 4 ? (c4 >> (4 * j)) & 15u : (c4 >> (8 * j)) & 255u;
-          v[j] = __fmaf_rn(vsc, float(c), vbi);
-        }
-        for (int hh = 0; hh < hq; ++hh) {
-          const float pp = sm.p[warp][hh][t];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) acc[hh][j] = __fmaf_rn(pp, v[j], acc[hh][j]);
-        }
-      }
-      __syncwarp();
-    }
-    for (int hh = 0; hh < hq; ++hh) {
-      if (lane == 0) {
-        sm.wm[warp][hh] = m[hh];
-        sm.wl[warp][hh] = l[hh];
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) sm.wacc[warp][hh][4 * lane + j] = acc[hh][j];
-    }
-    attn_sync();
-    // block partial (warps merged in order) and the last-arriver merges
+    Partial4 Pt;
+    attn_block<BITS>(ab, tv, sm.att, warp, ConsSync{}, Pt);
+    // the block partial and the last-arriver merges
     const int nblk_cap = a.capacity / kAttBlock;
     const int s = b / kAttSuper;
     const int n_super = (P.nblk + kAttSuper - 1) / kAttSuper;
     const int in_super = min(kAttSuper, P.nblk - s * kAttSuper);
-    for (int hh = warp; hh < hq; hh += 4) {
-      const int h = h0 + hh;
-      Partial4 Pt;
-      Pt.m = -INFINITY;
-      Pt.l = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) Pt.a[j] = 0.0f;
-      for (int w = 0; w < kAttWarps; ++w) {
-        Partial4 Q;
-        Q.m = sm.wm[w][hh];
-        Q.l = sm.wl[w][hh];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) Q.a[j] = sm.wacc[w][hh][4 * lane + j];
-        merge_into(Pt, Q);
-      }
-      float* dst = a.partials + (size_t(h) * nblk_cap + b) * kPartialFloats;
-      if (lane == 0) {
-        dst[0] = Pt.m;
-        dst[1] = Pt.l;
-      }
-      *reinterpret_cast<float4*>(dst + 4 + 4 * lane) = make_float4(Pt.a[0], Pt.a[1], Pt.a[2], Pt.a[3]);
+    if (warp >= hq) return;
+    {
+      const int h = ab.h0 + warp;
+      store_partial(a.partials + (size_t(h) * nblk_cap + b) * kPartialFloats, Pt);
       __threadfence();
       unsigned prev = 0;
       if (lane == 0) prev = atomicAdd(a.cnt + a.hq + h * a.n_super_max + s, 1u);
       prev = __shfl_sync(0xffffffffu, prev, 0);
-      if (int(prev) != in_super - 1) continue;
+      if (int(prev) != in_super - 1) return;
       // this warp merges super-chunk s of head h
       __threadfence();
       Partial4 S;
@@ -739,7 +640,7 @@ struct Consumers {
       __threadfence();
       if (lane == 0) prev = atomicAdd(a.cnt + h, 1u);
       prev = __shfl_sync(0xffffffffu, prev, 0);
-      if (int(prev) != n_super - 1) continue;
+      if (int(prev) != n_super - 1) return;
       __threadfence();
       Partial4 F;
       F.m = -INFINITY;
@@ -768,60 +669,82 @@ struct Consumers {
   }
 
   // --- routing (every CTA, consumer warp 0) -----------------------------------
-  __device__ void route(const MegaLayer& L) {
-    if (warp != 0) return;
-    const int E = a.E;
+  // Routing, computed by all consumer warps of every CTA (one thread per
+  // expert; the sums keep the canonical lane order).  The code is compact
+  // (runtime loops): it runs once per layer and is fetched cold.
+  __device__ void route(const MegaLayer& L, int step_, int layer_) {
+    const int E = a.E, t = threadIdx.x - 32, nt = kMegaCons * 32;
+#pragma unroll 1
+    for (int i = t; i < E; i += nt) sm.route_p[i] = __ldcg(a.router_logits + i);
+    cons_sync();
+    if (warp == 0 && lane == 0) stamp(a, step_, layer_, 14);
     if (a.router_mode == 0) {
-      float mx = -INFINITY;
-      for (int i = lane; i < E; i += 32) mx = fmaxf(mx, __ldcg(a.router_logits + i));
-      mx = bfly_max(mx);
-      float s = 0.0f;
-      for (int i = lane; i < E; i += 32) s = __fadd_rn(s, rexp(__fsub_rn(__ldcg(a.router_logits + i), mx)));
-      s = bfly_sum(s);
-      for (int i = lane; i < E; i += 32) {
-        const float pi = __fdiv_rn(rexp(__fsub_rn(__ldcg(a.router_logits + i), mx)), s);
+      // max and the canonical sum of exp(l - max): lane l of warp 0 adds
+      // experts l, l+32, ... in order, then a butterfly
+      if (warp == 0) {
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int i = lane; i < E; i += 32) mx = fmaxf(mx, sm.route_p[i]);
+        mx = bfly_max(mx);
+        if (lane == 0) sm.red[34] = mx;
+      }
+      cons_sync();
+      const float mx = sm.red[34];
+#pragma unroll 1
+      for (int i = t; i < E; i += nt) sm.route_c[i] = rexp(__fsub_rn(sm.route_p[i], mx));
+      cons_sync();
+      if (warp == 0) {
+        float sum = 0.0f;
+#pragma unroll 1
+        for (int i = lane; i < E; i += 32) sum = __fadd_rn(sum, sm.route_c[i]);
+        sum = bfly_sum(sum);
+        if (lane == 0) sm.red[35] = sum;
+      }
+      cons_sync();
+      const float sum = sm.red[35];
+#pragma unroll 1
+      for (int i = t; i < E; i += nt) {
+        const float pi = __fdiv_rn(sm.route_c[i], sum);
         sm.route_p[i] = pi;
         sm.route_c[i] = pi;
       }
     } else {
-      for (int i = lane; i < E; i += 32) {
-        const float pi = rsigmoid(__ldcg(a.router_logits + i));
+#pragma unroll 1
+      for (int i = t; i < E; i += nt) {
+        const float pi = rsigmoid(sm.route_p[i]);
         sm.route_p[i] = pi;
         sm.route_c[i] = __fadd_rn(pi, L.expert_bias[i]);
       }
     }
-    __syncwarp();
-    select_top(E);
-  }
-  __device__ void select_top(int E) {
-    for (int r = 0; r < a.k; ++r) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-      for (int i = lane; i < E; i += 32) {
-        const float c = sm.route_c[i];
-        if (c > bv || (c == bv && i < bi)) { bv = c; bi = i; }
+    cons_sync();
+    if (warp == 0 && lane == 0) stamp(a, step_, layer_, 15);
+    // rank of i = #{j : c_j > c_i or (c_j == c_i and j < i)}; ranks < k are
+    // the selection, in rank order (largest first, lowest index on ties)
+#pragma unroll 1
+    for (int i = t; i < E; i += nt) {
+      const float ci = sm.route_c[i];
+      int rank = 0;
+#pragma unroll 4
+      for (int j = 0; j < E; ++j) {
+        const float cj = sm.route_c[j];
+        rank += (cj > ci || (cj == ci && j < i)) ? 1 : 0;
       }
-      for (int off = 16; off >= 1; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-      }
-      if (lane == 0) {
-        sm.ids[r] = bi;
-        sm.route_c[bi] = -INFINITY;
-      }
-      __syncwarp();
+      if (rank < a.k) sm.ids[rank] = i;
     }
-    if (lane == 0) {
-      float sum = 0.0f;
-      for (int r = 0; r < a.k; ++r) sum = __fadd_rn(sum, sm.route_p[sm.ids[r]]);
-      sum = __fadd_rn(sum, 1e-20f);
-      for (int r = 0; r < a.k; ++r) sm.wts[r] = __fdiv_rn(sm.route_p[sm.ids[r]], sum);
+    cons_sync();
+    if (warp == 0) {
+      // renormalise: lane r holds p of rank r; the sum runs in rank order
+      const float pr = lane < a.k ? sm.route_p[sm.ids[lane]] : 0.0f;
+      float s2 = 0.0f;
+#pragma unroll 1
+      for (int r = 0; r < a.k; ++r) s2 = __fadd_rn(s2, __shfl_sync(0xffffffffu, pr, r));
+      s2 = __fadd_rn(s2, 1e-20f);
+      if (lane < a.k) sm.wts[lane] = __fdiv_rn(pr, s2);
     }
-    __syncwarp();
+    cons_sync();
   }
 
-  template <int SD, int I>
+  template <int I, int BITS>
   __device__ void run() {
     const Part P = partition(a);
     int token = sm.token0;
@@ -839,50 +762,52 @@ struct Consumers {
         const uint32_t* w = a.embed.w + size_t(tok) * (H / 8);
         for (int i = threadIdx.x - 32; i < H; i += kMegaCons * 32) {
           const float q = float((w[i >> 3] >> (4 * (i & 7))) & 15u);
-          const float s = sb<SD>(a.embed.s[size_t(tok) * (H / 64) + (i >> 6)]);
-          const float bb = sb<SD>(a.embed.b[size_t(tok) * (H / 64) + (i >> 6)]);
+          const float s = sb<2>(a.embed.s[size_t(tok) * (H / 64) + (i >> 6)], a.sd);
+          const float bb = sb<2>(a.embed.b[size_t(tok) * (H / 64) + (i >> 6)], a.sd);
           const uint16_t v = to_bf(__fmaf_rn(s, q, bb));
           sm.h0[i] = v;
-          if (i >= P.o0 && i < P.o1) a.h[i] = v;
+          if (i >= P.o0 && i < P.o1) {
+            a.h[i] = v;
+            sm.hown[i - P.o0] = v;
+          }
           if (blockIdx.x == 0) a.trace[i] = v;
         }
         cons_sync();
       }
       for (int l = 0; l < a.n_layers; ++l) {
-        const MegaLayer& L = a.layers[l];
+        const MegaLayer& L = sm.layers[l];
         // ---- Q
-        norm(l == 0 ? sm.h0 : a.h, L.input_norm, l == 0);
+        const FixScale fq = norm(l == 0 ? sm.h0 : a.h, L.input_norm, l == 0);
         {
-          ChunkX cx[2];
-          prep_lane_x<2048>(sm.xn, 0, lane, cx);
+          GroupX gx[1];
+          prep_lane_x<2048>(sm.xn, fq, 0, lane, gx);
           const int qrows[3] = {a.hq * 128, a.hkv * 128, a.hkv * 128};
           for (int r = P.q0; r < P.q1;) {
             int m = 0, base = 0;
             while (m < 2 && r >= base + qrows[m]) base += qrows[m++];
             const int n = min(min(kQRows, P.q1 - r), base + qrows[m] - r);
             const uint8_t* st = take();
-            rows2048<SD, false>(st, n, r, cx, a.qkv, best, best_i);
+            rows2048<false>(st, n, r, gx, fq, a.qkv, best, best_i);
             release();
             r += n;
           }
         }
         if (!grid_barrier(a, bar_index(a, step, l, 0))) return;
         // ---- A
+        if (warp == 0 && lane == 0) stamp(a, step, l, 11);
         for (int it = blockIdx.x; it < AP.items; it += gridDim.x) {
           int b, g, qsub;
-          attn_item(AP, a.hkv, it, b, g, qsub);
+          attn_coords(AP, a.hkv, it, b, g, qsub);
           uint8_t* kt = const_cast<uint8_t*>(take());
           const int kslot = slot;
           ++chunk;
           uint8_t* vt = const_cast<uint8_t*>(take());
           const int vslot = slot;
           --chunk;
-          bool patched = false;
-          if (warp < 4) {
-            if (a.kv_bits == 4) attn_item_compute<4>(L, AP, pos, b, g, qsub, kt, vt, patched);
-            else attn_item_compute<8>(L, AP, pos, b, g, qsub, kt, vt, patched);
-          }
+          if (warp == 0 && lane == 0) stamp(a, step, l, 12);
+          attn_item_compute<BITS>(L, AP, pos, b, g, qsub, kt, vt);
           cons_sync();
+          if (warp == 0 && lane == 0) stamp(a, step, l, 13);
           slot = kslot;
           release(true);
           slot = vslot;
@@ -891,19 +816,19 @@ struct Consumers {
         if (!grid_barrier(a, bar_index(a, step, l, 1))) return;
         // ---- O
         {
-          load_x(a.attn, a.hq * 128);
-          ChunkX cx[2];
-          prep_lane_x<4096>(sm.xn, warp & 1, lane, cx);
+          const FixScale fo = load_x(a.attn, a.hq * 128);
+          GroupX gx[1];
+          prep_lane_x<4096>(sm.xn, fo, warp & 1, lane, gx);
           for (int r = P.o0; r < P.o1; r += kORows) {
             const int n = min(kORows, P.o1 - r);
             const uint8_t* st = take();
-            rows4096<SD>(st, n, r, cx);
+            rows4096(st, n, r, P.o0, gx, fo);
             release();
           }
         }
         if (!grid_barrier(a, bar_index(a, step, l, 2))) return;
         // ---- R
-        norm(a.h, L.post_norm);
+        const FixScale fr = norm(a.h, L.post_norm);
         {
           int j = 0;
           for (int e = blockIdx.x; e < a.E; e += gridDim.x, ++j) {
@@ -927,19 +852,22 @@ struct Consumers {
         }
         if (!grid_barrier(a, bar_index(a, step, l, 3))) return;
         // ---- G: selection (same on every CTA), then gate/up pairs
-        route(L);
+        if (warp == 0 && lane == 0) stamp(a, step, l, 0);
+        route(L, step, l);
+        if (warp == 0 && lane == 0) stamp(a, step, l, 1);
         if (warp == 0 && lane == 0) {
           __threadfence_block();
           sm.route_seq = step * a.n_layers + l + 1;
         }
         cons_sync();
         {
-          ChunkX cx[2];
-          prep_lane_x<2048>(sm.xn, 0, lane, cx);
+          GroupX gx[1];
+          prep_lane_x<2048>(sm.xn, fr, 0, lane, gx);
           for (int u = P.g0; u < P.g1;) {
             const int r = u / a.I, i0 = u % a.I;
             const int n = min(min(kGPairs, P.g1 - u), a.I - i0);
             const uint8_t* st = take();
+            if (warp == 0 && lane == 0) stamp(a, step, l, 2 + 2 * min((u - P.g0) / kGPairs, 3));
             {
               const uint32_t wb = uint32_t(n) * 1024, sbytes = uint32_t(n) * 64;
               const uint16_t* sbase = reinterpret_cast<const uint16_t*>(st + 2 * wb);
@@ -949,9 +877,9 @@ struct Consumers {
               const bool va = pa < n, vc = pc < n;
               int rows[4] = {va ? pa : 0, va ? n + pa : 0, vc ? pc : 0, vc ? n + pc : 0};
               float v[4];
-              lane_rows_partial<2048, SD, 4>(st, sbase, bbase, rows, 0, lane, cx, v);
+              lane_rows_partial<2048, 2, 4>(st, sbase, bbase, rows, 0, lane, gx, v, a.sd);
 #pragma unroll
-              for (int q = 0; q < 4; ++q) v[q] = bfly_sum(v[q]);
+              for (int q = 0; q < 4; ++q) v[q] = __fmul_rn(bfly_sum(v[q]), fr.down);
               if (lane == 0) {
                 if (va) {
                   const float gg = rbf(v[0]), uu = rbf(v[1]);
@@ -964,15 +892,15 @@ struct Consumers {
               }
             }
             release();
+            if (warp == 0 && lane == 0) stamp(a, step, l, 3 + 2 * min((u - P.g0) / kGPairs, 3));
             u += n;
           }
         }
+        if (warp == 0 && lane == 0) stamp(a, step, l, 10);
         if (!grid_barrier(a, bar_index(a, step, l, 4))) return;
         // ---- D: down rows of all k experts, mix, residual
         {
-          for (int i = (threadIdx.x - 32) * 8; i < a.k * I; i += kMegaCons * 32 * 8)
-            *reinterpret_cast<uint4*>(sm.act + i) = ldcg128(a.act + i);
-          cons_sync();
+          load_vec(sm.act, a.act, a.k * I);
           const int n = P.o1 - P.o0;
           if (n > 0) {
             for (int r0 = 0; r0 < a.k; r0 += kDExperts) {
@@ -987,26 +915,20 @@ struct Consumers {
                 const uint8_t* e0 = st + (rr - r0) * per;
                 const uint16_t* sbase = reinterpret_cast<const uint16_t*>(e0 + wb);
                 const uint16_t* bbase = reinterpret_cast<const uint16_t*>(e0 + wb + ((sbytes + 15) & ~15u));
-                ChunkX cx[C::CH];
-                const int sub = lane >> 3, l8 = lane & 7;
-                prep_lane_x<I>(sm.act + rr * I, 0, l8, cx);
+                const FixScale fd = fix_scale_from_max(warp_maxabs(sm.act + rr * I, I));
+                GroupX gx[C::GPL];
+                const int sub = lane >> 2, l4 = lane & 3;  // 8 rows per pass, 4 lanes per row
+                prep_lane_x<I>(sm.act + rr * I, fd, 0, l4, gx);
                 const int rbeg = half * ((n + 1) / 2), rend = half == 0 ? (n + 1) / 2 : n;
                 for (int rb = rbeg; rb < rend; rb += 8) {
-                  int rows[2];
-                  bool valid[2];
-#pragma unroll
-                  for (int q = 0; q < 2; ++q) {
-                    const int x = rb + 4 * q + sub;
-                    valid[q] = x < rend;
-                    rows[q] = valid[q] ? x : rbeg;
-                  }
-                  float v[2];
-                  lane_rows_partial<I, SD, 2>(e0, sbase, bbase, rows, 0, l8, cx, v);
-#pragma unroll
-                  for (int q = 0; q < 2; ++q) {
-                    v[q] = bfly_sum<8>(valid[q] ? v[q] : 0.0f);
-                    if (valid[q] && l8 == 0) sm.dsm[rr][rows[q]] = rbf(v[q]);
-                  }
+                  int rows[1];
+                  const int x = rb + sub;
+                  const bool valid = x < rend;
+                  rows[0] = valid ? x : rbeg;
+                  float v[1];
+                  lane_rows_partial<I, 2, 1>(e0, sbase, bbase, rows, 0, l4, gx, v, a.sd);
+                  v[0] = bfly_sum<4>(valid ? v[0] : 0.0f);
+                  if (valid && l4 == 0) sm.dsm[rr][rows[0]] = rbf(__fmul_rn(v[0], fd.down));
                 }
               }
               release();
@@ -1018,7 +940,8 @@ struct Consumers {
                 const float t = __fadd_rn(rbf(__fmul_rn(sm.dsm[r][i], rbf(sm.wts[r]))), 0.0f);
                 mix = r == 0 ? t : rbf(__fadd_rn(t, mix));
               }
-              const uint16_t hn = to_bf(__fadd_rn(ldcg_bf(a.h + P.o0 + i), mix));
+              const uint16_t hn = to_bf(__fadd_rn(bf(sm.hown[i]), mix));
+              sm.hown[i] = hn;
               a.h[P.o0 + i] = hn;
               a.trace[size_t(l + 1) * H + P.o0 + i] = hn;
             }
@@ -1027,10 +950,10 @@ struct Consumers {
         if (!grid_barrier(a, bar_index(a, step, l, 5))) return;
       }
       // ---- H: final norm + lm_head + CTA argmax
-      norm(a.h, a.final_norm);
+      const FixScale fh = norm(a.h, a.final_norm);
       {
-        ChunkX cx[2];
-        prep_lane_x<2048>(sm.xn, 0, lane, cx);
+        GroupX gx[1];
+        prep_lane_x<2048>(sm.xn, fh, 0, lane, gx);
         best = -INFINITY;
         best_i = 0x7fffffff;
         int v0, v1;
@@ -1040,7 +963,7 @@ struct Consumers {
         for (int r = v0; r < v1; r += kQRows) {
           const int n = min(kQRows, v1 - r);
           const uint8_t* st = take();
-          rows2048<SD, true>(st, n, r, cx, a.logits, best, best_i);
+          rows2048<true>(st, n, r, gx, fh, a.logits, best, best_i);
           release();
         }
         for (int off = 16; off >= 1; off >>= 1) {
@@ -1103,7 +1026,7 @@ struct Consumers {
   }
 };
 
-template <int SD, int I>
+template <int I, int BITS>
 __global__ void __launch_bounds__(kMegaThreads, 1) k_decode_mega(const MegaArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   MegaSmem& sm = *reinterpret_cast<MegaSmem*>(smem_raw);
@@ -1117,13 +1040,19 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_decode_mega(const MegaArgs 
     sm.pos0 = a.ctl[2];
     fence_barrier_init();
   }
+  {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(a.layers);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(sm.layers);
+    const int words = a.n_layers * int(sizeof(MegaLayer) / 4);
+    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+  }
   __syncthreads();
   if (threadIdx.x < 32) {
     Producer p(a, sm);
     p.run();
   } else {
     Consumers c(a, sm);
-    c.template run<SD, I>();
+    c.template run<I, BITS>();
   }
 }
 

@@ -152,6 +152,7 @@ struct GateUpSmem {
   using L = StageLayout<2048, 2 * RSP>;
   alignas(128) uint8_t stage[NS][L::BYTES];
   alignas(16) uint16_t xn[2048];
+  float red[kWarps];
   uint64_t full[NS];
 };
 
@@ -227,8 +228,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gateup(const GateUpArgs a) {
   for (int i = threadIdx.x * 8; i < K; i += kThreads * 8)
     *reinterpret_cast<uint4*>(sm.xn + i) = ldg128(a.xn + i);
   __syncthreads();
-  ChunkX cx[KCfg<K>::CH];
-  prep_lane_x<K>(sm.xn, 0, lane, cx);
+  const FixScale fs = fix_scale_from_max(block_maxabs(sm.xn, K, threadIdx.x, kThreads, sm.red, 0));
+  GroupX gx[1];
+  prep_lane_x<K>(sm.xn, fs, 0, lane, gx);
 
   bool failed = false;
   int j = 0, r, i0, n;
@@ -254,9 +256,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gateup(const GateUpArgs a) {
         const bool va = pa < n, vc = pc < n;
         int rows[4] = {va ? pa : 0, va ? RSP + pa : 0, vc ? pc : 0, vc ? RSP + pc : 0};
         float v[4];
-        lane_rows_partial<K, SD, 4>(wbase, sbase, bbase, rows, 0, lane, cx, v);
+        lane_rows_partial<K, SD, 4>(wbase, sbase, bbase, rows, 0, lane, gx, v);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) v[q] = bfly_sum(v[q]);
+        for (int q = 0; q < 4; ++q) v[q] = __fmul_rn(bfly_sum(v[q]), fs.down);
         if (lane == 0) {
           if (va) {
             const float g = rbf(v[0]), u = rbf(v[1]);
@@ -371,26 +373,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_down(const DownArgs a) {
   }
   const int r = warp;
   if (r < a.k && local(r)) {
-    ChunkX cx[C::CH];
-    const int sub = lane >> 3, l = lane & 7;
-    prep_lane_x<I>(sm.act[r], 0, l, cx);
+    const FixScale fs = fix_scale_from_max(warp_maxabs(sm.act[r], I));
+    GroupX gx[C::GPL];
+    const int sub = lane >> 2, l = lane & 3;  // 8 rows per pass, 4 lanes per row
+    prep_lane_x<I>(sm.act[r], fs, 0, l, gx);
     const uint8_t* st = sm.stage[r];
-    for (int rb = 0; rb < n; rb += 8) {
+    for (int rb = 0; rb < n; rb += 16) {
       int rows[2];
       bool valid[2];
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
-        const int rr = rb + 4 * q + sub;
+        const int rr = rb + 8 * q + sub;
         valid[q] = rr < n;
         rows[q] = valid[q] ? rr : 0;
       }
       float v[2];
       lane_rows_partial<I, SD, 2>(stage_wrow<I, S::RMAX>(st, 0), stage_srow<I, S::RMAX>(st, 0),
-                                  stage_brow<I, S::RMAX>(st, 0), rows, 0, l, cx, v);
+                                  stage_brow<I, S::RMAX>(st, 0), rows, 0, l, gx, v);
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
-        v[q] = bfly_sum<8>(valid[q] ? v[q] : 0.0f);
-        if (valid[q] && l == 0) sm.d[r][rows[q]] = rbf(v[q]);
+        v[q] = bfly_sum<4>(valid[q] ? v[q] : 0.0f);
+        if (valid[q] && l == 0) sm.d[r][rows[q]] = rbf(__fmul_rn(v[q], fs.down));
       }
     }
   }

@@ -6,180 +6,196 @@
 //   weights  uint32[N, K/8]: element j of a row is (word[j/8] >> 4*(j%8)) & 15
 //   scales   [N, K/64] fp16 or bf16, biases [N, K/64]
 //   w[n, j] = scale[n, j/64] * q[n, j] + bias[n, j/64]
+//   y[n] = sum_g scale_g * sum_{j in g} x_j q_j + bias_g * sum_{j in g} x_j
 //
-// Canonical order of one row (what the CPU oracle restates):
-//   * the row is cut into 32-element chunks c (16 bytes of codes, half a group);
-//   * every sum starts from +0.0 and adds its terms one at a time;
-//   * in a chunk, two accumulators run over the words k = 0..3 and nibbles
-//     i = 0..3: lo += x[8k+i] q[8k+i], hi += x[8k+4+i] q[8k+4+i] (fused
-//     multiply-adds of exact products); D_c = lo + hi.  X_c (sum of x over the
-//     chunk) is formed the same way;
-//   * a lane owns a fixed set of chunks and folds them in order:
-//     acc = fma(scale_g, D_c, acc); acc = fma(bias_g, X_c, acc)  (g = c/2);
-//   * lanes are combined with an xor butterfly over T lanes;
-//   * K % 2048 == 0: T = 32, the row is split in 2048-element segments, lane l
-//     of segment s owns chunks 64s+l and 64s+l+32, and segment sums are added
-//     in order.  Otherwise (K = 256*n, n <= 4): T = 8, lane l owns chunks
-//     l, l+8, ... and there is one segment.
-//   * the result is rounded once to bf16.
-//
-// The multiply uses x prescaled by a power of two so that each nibble can be
-// turned into a float with a single AND/OR (exponent-magic) and a subtraction
-// of 2^23, without shifting it down first.  Prescaling by 2^-p is exact for
-// every bf16 input, so products are unchanged.
+// Canonical arithmetic (restated by oracle/rec_oracle.c):
+//   * the input vector x (bf16[K]) is put in 16-bit fixed point with one
+//     power-of-two scale for the whole vector: E = exponent of max|x|,
+//     F = min(14 - E, 100), xi_j = rint(x_j * 2^F) (|xi| <= 32640);
+//   * per group g of 64: D_g = sum_j q_j * xi_j and X_g = sum_j xi_j are
+//     exact integers (int32), computed with byte dot products on the
+//     limbs xi = 256*hi + lo (hi signed, lo unsigned), so their order is
+//     irrelevant;
+//   * a lane owns groups and folds them in order, starting from +0:
+//     acc = fma(scale_g, float(D_g), acc); acc = fma(bias_g, float(X_g), acc);
+//   * K % 2048 == 0: 32 lanes per row, lane l of 2048-element segment s owns
+//     group 32s + l; segments are reduced by an xor butterfly and added in
+//     order.  K = 256*n (n <= 4): 4 lanes per row, lane l owns groups
+//     l, l+4, l+8, ...; butterfly over the 4 lanes;
+//   * y = bf16(row_sum * 2^-F).
+// Every fixed-point element within 2^7 of max|x| is exact; smaller ones are
+// rounded to a multiple of 2^-F, which moves y by ~1e-4 of its size — an
+// order of magnitude below the bf16 rounding of y.
 #pragma once
 #include "common.cuh"
 
 namespace rec {
 
-// --- x preparation -----------------------------------------------------------
-// xp[k][i] = (x'lo, x'hi) pair for word k, nibble pair i of one chunk.
-struct ChunkX {
-  float2 p[4][4];
-  float X;  // sum of x over the chunk, canonical order
-};
-
-__device__ __forceinline__ void prep_chunk(const float* x32, ChunkX& cx) {
-  // x32: the 32 chunk values as floats (already rounded to bf16 values).
-  // lo nibble i is masked in place from the word (value q*2^(4i)); hi nibble
-  // 4+i from the word shifted right by 12 (value q*2^(4i+4)).
-  const float lo_scale[4] = {1.0f, 0.0625f, 0.00390625f, 0.000244140625f};          // 2^-4i
-  const float hi_scale[4] = {0.0625f, 0.00390625f, 0.000244140625f, 1.52587890625e-05f};  // 2^-(4i+4)
-  float xl = 0.0f, xh = 0.0f;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float a = x32[8 * k + i], b = x32[8 * k + 4 + i];
-      cx.p[k][i] = make_float2(__fmul_rn(a, lo_scale[i]), __fmul_rn(b, hi_scale[i]));
-      xl = __fadd_rn(xl, a);
-      xh = __fadd_rn(xh, b);
-    }
-  }
-  cx.X = __fadd_rn(xl, xh);
-}
-
-// --- one 16-byte chunk against prepared x -------------------------------------
-__device__ __forceinline__ float2 u64_as_float2(unsigned long long v) {
-  float2 f;
-  f.x = __uint_as_float(uint32_t(v));
-  f.y = __uint_as_float(uint32_t(v >> 32));
-  return f;
-}
-
-__device__ __forceinline__ float chunk_dot(uint4 w, const ChunkX& cx) {
-  // (word, word >> 12) form one 64-bit register pair; each 64-bit AND/OR
-  // yields a (lo, hi) float pair ready for the packed f32x2 add and FMA.
-  const unsigned long long M = 0x4B0000004B000000ull;
-  const float2 off = make_float2(-8388608.0f, -8388608.0f);
-  float2 acc = make_float2(0.0f, 0.0f);
-  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const unsigned long long p = (static_cast<unsigned long long>(ws[k] >> 12) << 32) | ws[k];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const unsigned long long mask = (static_cast<unsigned long long>(0xF0u << (4 * i)) << 32) | (0xFu << (4 * i));
-      const float2 f = __fadd2_rn(u64_as_float2((p & mask) | M), off);
-      acc = __ffma2_rn(cx.p[k][i], f, acc);
-    }
-  }
-  return __fadd_rn(acc.x, acc.y);
-}
-
-// Fold one chunk into a lane accumulator.
-__device__ __forceinline__ float fold_chunk(float acc, float d, float X, float s, float b) {
-  acc = __fmaf_rn(s, d, acc);
-  return __fmaf_rn(b, X, acc);
-}
-
-// --- K configurations ----------------------------------------------------------
-// T lanes per row, CH chunks per lane (per segment), SEG segments.
 template <int K>
 struct KCfg {
   static_assert(K % 256 == 0, "K must be a multiple of 256");
   static constexpr bool wide = (K % 2048 == 0);
-  static constexpr int T = wide ? 32 : 8;
-  static constexpr int SEG = wide ? K / 2048 : 1;
-  static constexpr int CH = wide ? 2 : K / 256;
-  static_assert(wide || K / 256 <= 4, "K = 256*n needs n <= 4");
-  static constexpr int CHUNKS = K / 32;
-  static constexpr int ROW_BYTES = K / 2;
+  static constexpr int T = wide ? 32 : 4;           // lanes per row
+  static constexpr int SEG = wide ? K / 2048 : 1;   // segments per row
   static constexpr int GROUPS = K / 64;
-  // chunk index owned by (segment, lane-in-row, m)
-  __device__ static __forceinline__ int chunk(int seg, int l, int m) {
-    return wide ? seg * 64 + l + 32 * m : l + 8 * m;
-  }
+  static constexpr int GPL = wide ? 1 : GROUPS / 4;  // groups per lane (per segment)
+  static_assert(wide || K / 256 <= 4, "K = 256*n needs n <= 4");
+  static constexpr int ROW_BYTES = K / 2;
+  __device__ static __forceinline__ int group(int seg, int l, int m) { return wide ? 32 * seg + l : l + 4 * m; }
 };
 
-// Prepare a lane's chunks of x (bf16 in global or shared memory, given as a
-// generic pointer to uint16) for segment `seg`.
-template <int K>
-__device__ __forceinline__ void prep_lane_x(const uint16_t* x, int seg, int l, ChunkX (&cx)[KCfg<K>::CH]) {
+// Fixed-point scale of a vector: returns F; 2^F and 2^-F as floats.
+struct FixScale {
+  int F;
+  float up, down;
+};
+__device__ __forceinline__ FixScale fix_scale_from_max(float maxabs) {
+  const int E = int((__float_as_uint(maxabs) >> 23) & 0xFF) - 127;
+  int F = 14 - E;
+  F = F > 100 ? 100 : F;
+  return {F, __uint_as_float(uint32_t(F + 127) << 23), __uint_as_float(uint32_t(127 - F) << 23)};
+}
+
+// Max |x| over a bf16 vector in shared/global memory, reduced over the
+// threads [t0, t0 + nthreads) that call it; red: shared scratch of
+// nthreads/32 floats.  Returns the same value to all callers.
+__device__ __forceinline__ float block_maxabs(const uint16_t* x, int n, int tid, int nthreads, float* red,
+                                              int bar_id) {
+  float m = 0.0f;
+  for (int i = tid * 8; i < n; i += nthreads * 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(x + i);
+    const uint32_t us[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-  for (int m = 0; m < KCfg<K>::CH; ++m) {
-    int c = KCfg<K>::chunk(seg, l, m);
-    float v[32];
-    const uint4* src = reinterpret_cast<const uint4*>(x + c * 32);
+    for (int q = 0; q < 4; ++q) m = fmaxf(m, fmaxf(fabsf(__uint_as_float(us[q] << 16)),
+                                                   fabsf(__uint_as_float(us[q] & 0xFFFF0000u))));
+  }
+  m = bfly_max(m);
+  if ((tid & 31) == 0) red[tid >> 5] = m;
+  asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads));
+  float r = 0.0f;
+  for (int w = 0; w < nthreads / 32; ++w) r = fmaxf(r, red[w]);
+  asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(nthreads));
+  return r;
+}
+
+// Max |x| over a bf16 vector, reduced within one warp (all lanes call it).
+__device__ __forceinline__ float warp_maxabs(const uint16_t* x, int n) {
+  const int lane = threadIdx.x & 31;
+  float m = 0.0f;
+  for (int i = lane * 8; i < n; i += 256) {
+    const uint4 u = *reinterpret_cast<const uint4*>(x + i);
+    const uint32_t us[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) m = fmaxf(m, fmaxf(fabsf(__uint_as_float(us[q] << 16)),
+                                                   fabsf(__uint_as_float(us[q] & 0xFFFF0000u))));
+  }
+  return bfly_max(m);
+}
+
+// A lane's prepared group of x: per word w of the group, byte-packed limbs
+// matching the even nibbles (0,2,4,6) and odd nibbles (1,3,5,7) of the
+// weight word.
+struct GroupX {
+  uint32_t hi_e[8], hi_o[8], lo_e[8], lo_o[8];
+  float X;  // float(sum of xi over the group), exact
+};
+
+__device__ __forceinline__ void prep_group(const uint16_t* xg, FixScale fs, GroupX& gx) {
+  int sum = 0;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const uint4 u = *reinterpret_cast<const uint4*>(xg + 8 * w);
+    const uint32_t us[4] = {u.x, u.y, u.z, u.w};
+    int xi[8];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      uint4 u = src[q];
-      const uint32_t us[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        v[8 * q + 2 * t] = __uint_as_float(us[t] << 16);
-        v[8 * q + 2 * t + 1] = __uint_as_float(us[t] & 0xFFFF0000u);
-      }
+      xi[2 * q] = __float2int_rn(__fmul_rn(__uint_as_float(us[q] << 16), fs.up));
+      xi[2 * q + 1] = __float2int_rn(__fmul_rn(__uint_as_float(us[q] & 0xFFFF0000u), fs.up));
     }
-    prep_chunk(v, cx[m]);
-  }
-}
-
-// Lane partial of one row whose codes/scales/biases sit in shared memory.
-template <int K, int SD>
-__device__ __forceinline__ float lane_row_partial(const uint8_t* wrow, const uint16_t* srow,
-                                                  const uint16_t* brow, int seg, int l,
-                                                  const ChunkX (&cx)[KCfg<K>::CH]) {
-  float acc = 0.0f;
+    uint32_t he = 0, ho = 0, le = 0, lo = 0;
 #pragma unroll
-  for (int m = 0; m < KCfg<K>::CH; ++m) {
-    int c = KCfg<K>::chunk(seg, l, m);
-    uint4 w = lds128(wrow + c * 16);
-    float d = chunk_dot(w, cx[m]);
-    float s = sb<SD>(srow[c >> 1]), b = sb<SD>(brow[c >> 1]);
-    acc = fold_chunk(acc, d, cx[m].X, s, b);
+    for (int q = 0; q < 4; ++q) {
+      const int a = xi[2 * q], b = xi[2 * q + 1];
+      he |= (uint32_t(a >> 8) & 0xFFu) << (8 * q);
+      ho |= (uint32_t(b >> 8) & 0xFFu) << (8 * q);
+      le |= (uint32_t(a) & 0xFFu) << (8 * q);
+      lo |= (uint32_t(b) & 0xFFu) << (8 * q);
+      sum += a + b;
+    }
+    gx.hi_e[w] = he;
+    gx.hi_o[w] = ho;
+    gx.lo_e[w] = le;
+    gx.lo_o[w] = lo;
   }
-  return acc;
+  gx.X = float(sum);
 }
 
-// Lane partials of ILP rows at once (independent chains for the scheduler);
-// row i lives at wrow0 + i*row_stride etc.  valid[i] false rows give 0.
+// Exact integer dot of one group (32 bytes of codes) with prepared x.
+__device__ __forceinline__ int group_dot(const uint4 (&w)[2], const GroupX& gx) {
+  int hi = 0;
+  unsigned lo = 0;
+  const uint32_t ws[8] = {w[0].x, w[0].y, w[0].z, w[0].w, w[1].x, w[1].y, w[1].z, w[1].w};
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t e = ws[k] & 0x0F0F0F0Fu, o = (ws[k] >> 4) & 0x0F0F0F0Fu;
+    hi = __dp4a(int(e), int(gx.hi_e[k]), hi);
+    hi = __dp4a(int(o), int(gx.hi_o[k]), hi);
+    lo = __dp4a(e, gx.lo_e[k], lo);
+    lo = __dp4a(o, gx.lo_o[k], lo);
+  }
+  return hi * 256 + int(lo);
+}
+
+__device__ __forceinline__ float fold_group(float acc, int D, float X, float s, float b) {
+  acc = __fmaf_rn(s, float(D), acc);
+  return __fmaf_rn(b, X, acc);
+}
+
+// Prepare a lane's groups of x (bf16 vector in shared memory) for segment seg.
+template <int K>
+__device__ __forceinline__ void prep_lane_x(const uint16_t* x, FixScale fs, int seg, int l,
+                                            GroupX (&gx)[KCfg<K>::GPL]) {
+#pragma unroll
+  for (int m = 0; m < KCfg<K>::GPL; ++m) prep_group(x + KCfg<K>::group(seg, l, m) * 64, fs, gx[m]);
+}
+
+// Lane partials of ILP rows at once (independent chains for the scheduler).
 template <int K, int SD, int ILP>
 __device__ __forceinline__ void lane_rows_partial(const uint8_t* wbase, const uint16_t* sbase,
-                                                  const uint16_t* bbase, const int (&rows)[ILP],
-                                                  int seg, int l, const ChunkX (&cx)[KCfg<K>::CH],
-                                                  float (&out)[ILP]) {
+                                                  const uint16_t* bbase, const int (&rows)[ILP], int seg, int l,
+                                                  const GroupX (&gx)[KCfg<K>::GPL], float (&out)[ILP],
+                                                  int sd_rt = 0) {
   float acc[ILP];
 #pragma unroll
   for (int i = 0; i < ILP; ++i) acc[i] = 0.0f;
 #pragma unroll
-  for (int m = 0; m < KCfg<K>::CH; ++m) {
-    const int c = KCfg<K>::chunk(seg, l, m);
-    uint4 w[ILP];
-#pragma unroll
-    for (int i = 0; i < ILP; ++i) w[i] = lds128(wbase + rows[i] * KCfg<K>::ROW_BYTES + c * 16);
-    float d[ILP];
-#pragma unroll
-    for (int i = 0; i < ILP; ++i) d[i] = chunk_dot(w[i], cx[m]);
+  for (int m = 0; m < KCfg<K>::GPL; ++m) {
+    const int g = KCfg<K>::group(seg, l, m);
+    uint4 w[ILP][2];
 #pragma unroll
     for (int i = 0; i < ILP; ++i) {
-      const float s = sb<SD>(sbase[rows[i] * KCfg<K>::GROUPS + (c >> 1)]);
-      const float b = sb<SD>(bbase[rows[i] * KCfg<K>::GROUPS + (c >> 1)]);
-      acc[i] = fold_chunk(acc[i], d[i], cx[m].X, s, b);
+      const uint8_t* p = wbase + rows[i] * KCfg<K>::ROW_BYTES + g * 32;
+      w[i][0] = lds128(p);
+      w[i][1] = lds128(p + 16);
+    }
+    int D[ILP];
+#pragma unroll
+    for (int i = 0; i < ILP; ++i) D[i] = group_dot(w[i], gx[m]);
+#pragma unroll
+    for (int i = 0; i < ILP; ++i) {
+      const float s = sb<SD>(sbase[rows[i] * KCfg<K>::GROUPS + g], sd_rt);
+      const float b = sb<SD>(bbase[rows[i] * KCfg<K>::GROUPS + g], sd_rt);
+      acc[i] = fold_group(acc[i], D[i], gx[m].X, s, b);
     }
   }
 #pragma unroll
   for (int i = 0; i < ILP; ++i) out[i] = acc[i];
+}
+
+// Butterfly over the lanes of one row.
+template <int K>
+__device__ __forceinline__ float row_reduce(float v) {
+  return bfly_sum<KCfg<K>::T>(v);
 }
 
 // --- shared-memory stage pipeline ---------------------------------------------
