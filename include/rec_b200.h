@@ -175,6 +175,33 @@ REC_API int rec_last_error(char* buf, size_t len);
 REC_API int rec_gemv_int4(const RecQMat* w, int32_t scale_dtype, int64_t n, int32_t k,
                           const void* x_dev, const void* norm_weight_dev, float eps, void* y_dev,
                           void* stream);
+/* y = W x (int4 g64, optional fused RMSNorm on x) and the greedy token
+ * argmax(y) (lowest index among equal maxima, as the decode step's lm_head)
+ * without any caller-provided scratch.  No counterpart in the reference: its
+ * argmax kernel always runs inside a session that owns its buffers.
+ *
+ * For callers that cannot allocate device memory: a plain C or ctypes host
+ * that has no device allocator of its own (the library allocates nothing, and
+ * every other entry point that needs scratch takes it from a session
+ * workspace), or a sampler that runs in a process whose HBM is already handed
+ * out in full to weight banks and the KV pool, where an extra cudaMalloc
+ * fails or fragments the pool.
+ *
+ * The cross-CTA scratch (arrival counter, per-CTA candidates and, when y_dev
+ * is NULL, the bf16 logits) is one static device array of 532,736 bytes per
+ * device.  Limits: N <= 262,144 rows when y_dev is NULL (larger N is rejected
+ * with REC_EINVAL; pass y_dev for a larger vocabulary); N even, K as in
+ * rec_gemv_int4.  token_dev receives -1 if a bounded device wait ran out.
+ * The first call on each device looks up the array's device address (with
+ * that device current) and sets the kernels' shared-memory limit; make that
+ * first call before any stream capture.  Every call shares the array and it
+ * keeps the last call's contents (each call clears what must start at zero):
+ * calls that overlap on the GPU (different streams or threads) race on it.
+ * The call allocates nothing: no cudaMalloc, no cudaFree, no library
+ * allocator. */
+REC_API int rec_gemv_int4_argmax_noalloc(const RecQMat* w, int32_t scale_dtype, int64_t n, int32_t k,
+                                         const void* x_dev, const void* norm_weight_dev, float eps,
+                                         void* y_dev, int32_t* token_dev, void* stream);
 /* MLX affine quantization of fp32 groups into codes + (bf16|fp16) scale/bias. */
 REC_API int rec_quantize_affine(const float* w_dev, int64_t n_groups, int32_t bits,
                                 int32_t scale_dtype, void* codes_dev, void* scales_dev,
