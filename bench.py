@@ -29,6 +29,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "decode tokens/s at batch 1 vs context 1K-252K; achieved HBM GB/s per kernel"
 UNIT = "tokens/s"
+PACKET = 64  # tokens per persistent-kernel launch
 KERNEL_NAMES = ["embed", "qkv", "attn_partial", "attn_combine", "o_proj", "router", "experts_gate_up",
                 "experts_down_mix", "lm_head_argmax", "step_end"]
 
@@ -139,15 +140,25 @@ def run_rec(args):
     stream = torch.cuda.current_stream()
     ids_dev, prod_dev = sess.ids, sess.produced
 
-    def decode(n, token, position):
-        """n greedy steps; token < 0 continues from the device state."""
-        done = 0
+    def decode(n, token, position, events=None):
+        """n greedy steps in device-side packets of up to 64 tokens; token < 0
+        continues from the device state.  Returns the packet sizes; with
+        `events`, brackets every packet with a pair of CUDA events."""
+        done, sizes = 0, []
         while done < n:
-            c = min(64, n - done)
+            c = min(PACKET, n - done)
+            if events is not None:
+                a = torch.cuda.Event(enable_timing=True)
+                a.record(stream)
             check(lib().rec_decode_greedy(sess.ctx, token if done == 0 else -1, position + done, c, None, 0,
                                           ids_dev.data_ptr(), prod_dev.data_ptr(), stream.cuda_stream))
+            if events is not None:
+                b = torch.cuda.Event(enable_timing=True)
+                b.record(stream)
+                events.append((a, b))
             done += c
-        return (n + 63) // 64
+            sizes.append(c)
+        return sizes
 
     decode(W, first, pos)
     pos += W
@@ -156,10 +167,13 @@ def run_rec(args):
     clocks.start()
     time.sleep(0.3)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launch_events = []
     barrier()
+    torch.cuda.nvtx.range_push("timed")
     e0.record(stream)
-    packets = decode(K, -1, pos)
+    packets = decode(K, -1, pos, launch_events)
     e1.record(stream)
+    torch.cuda.nvtx.range_pop()
     barrier()
     clk = clocks.stop()
     sess.check_status()
@@ -169,8 +183,10 @@ def run_rec(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     t_max = float(t.item())
-    kernels_per_step = 1 + cfg.n_layers * 7 + 2
     value = K * world / t_max
+    # per packet: k_set_step (token, position, EOS ids) + k_decode_mega
+    launches = 2 * len(packets)
+    launch_s = [a.elapsed_time(b) / 1e3 for a, b in launch_events]
 
     phases = None
     if args.profile_phases:
@@ -224,16 +240,28 @@ def run_rec(args):
             entry["GBps"] = round(kernel_bytes[name] / (us * 1e-6) / 1e9, 1)
         per_kernel[name] = entry
     sess.check_status()
-    dom = "experts_gate_up"
-    ach = kernel_bytes[dom] / (per_kernel[dom]["us"] * 1e-6) / 1e9
+    # Dominant kernel of the timed region: the persistent decode kernel (one
+    # launch per packet).  Algorithmic bytes of a launch = its tokens x
+    # (weights + scales/biases of every used row and the selected experts +
+    # KV of the attended tokens).
+    ctx_mid = ctx0 + W + K // 2
+    tok_bytes = cfg.weight_bytes_per_token() + cfg.kv_bytes_per_token(ctx_mid)
+    launch_bytes = tok_bytes * sum(packets) / len(packets)
+    mean_launch = sum(launch_s) / len(launch_s)
+    ach = launch_bytes / mean_launch / 1e9
     traffic = None
     tf = ROOT / "profiles" / "traffic.json"
     if tf.exists():
-        traffic = json.loads(tf.read_text()).get(dom)
-    roofline = {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(ach / peak, 4), "traffic": traffic,
-                "algorithmic_bytes_per_launch": int(kernel_bytes[dom]), "peak_source": peak_kind}
-    step_bytes = cfg.weight_bytes_per_token() + cfg.kv_bytes_per_token(ctx0 + W + K // 2)
+        rec = json.loads(tf.read_text()).get("k_decode_mega")
+        if rec:
+            # measured DRAM bytes / algorithmic bytes of a captured one-token
+            # launch, applied to this launch's algorithmic bytes
+            traffic = int(rec["dram_bytes"] / rec["algorithmic_bytes"] * launch_bytes)
+    roofline = {"kernel": "k_decode_mega", "bound": "hbm", "achieved": round(ach, 1), "peak": peak,
+                "unit": "GB/s", "frac": round(ach / peak, 4), "traffic": traffic,
+                "algorithmic_bytes_per_launch": int(launch_bytes), "tokens_per_launch": sum(packets) / len(packets),
+                "mean_launch_ms": round(mean_launch * 1e3, 3), "peak_source": peak_kind}
+    step_bytes = tok_bytes
     step_roofline = {"bytes_per_step": int(step_bytes),
                      "achieved_GBps": round(step_bytes / (t_max / K) / 1e9, 1),
                      "frac": round(step_bytes / (t_max / K) / 1e9 / peak, 4),
@@ -262,8 +290,10 @@ def run_rec(args):
     te = torch.tensor([e2e_local], device="cuda")
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MIN)
-    e2e = {"value": round(float(te.item()) * world, 2), "unit": UNIT, "h2d_bytes_per_step": 8,
-           "d2h_bytes_per_step": 4 * 8 + 4, "packet_tokens": 8, "api": "rec_b200.engine.ResidentSampler.block"}
+    # per packet of 8: the start token goes in (4 B, kernel argument); status,
+    # count and the 8 ids come back (4 + 4 + 32 B)
+    e2e = {"value": round(float(te.item()) * world, 2), "unit": UNIT, "h2d_bytes_per_step": 4 / 8,
+           "d2h_bytes_per_step": 40 / 8, "packet_tokens": 8, "api": "rec_b200.engine.ResidentSampler.block"}
 
     # ---- CPU baseline: the oracle on this host's cores, same weights and cache
     cpu = None
@@ -287,10 +317,10 @@ def run_rec(args):
                    "l2_flush": "none needed: 1.78 GB streamed per step > 126 MB L2"},
         "clocks": clk,
         "e2e": e2e,
-        "gpu_launches": K * kernels_per_step + packets,
+        "gpu_launches": launches,
         "roofline": roofline,
         "step_roofline": step_roofline,
-        "kernels": per_kernel,
+        "graph_schedule_kernels_us": per_kernel,
         "phases_us": phases,
         "cpu_baseline": cpu,
     }

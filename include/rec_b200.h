@@ -57,14 +57,14 @@ enum { REC_FLAG_SINKS = 1, REC_FLAG_QK_NORM = 2 };
 
 /* Model shape (reference ModelArgs, engine/src/rec_mlx/model.py:14-37). */
 typedef struct RecModelDesc {
-  int32_t hidden;      /* H, multiple of 2048 */
-  int32_t n_layers;
-  int32_t n_q_heads;   /* 32 */
-  int32_t n_kv_heads;  /* 4 */
+  int32_t hidden;      /* H = 2048 */
+  int32_t n_layers;    /* 1..64 */
+  int32_t n_q_heads;   /* 8 * n_kv_heads, with n_q_heads * 128 = 2048 or 4096 */
+  int32_t n_kv_heads;
   int32_t head_dim;    /* 128 */
-  int32_t n_experts;   /* E */
+  int32_t n_experts;   /* E <= 1024 */
   int32_t top_k;       /* k <= 8 */
-  int32_t moe_inter;   /* I: 256*n (n<=4) or a multiple of 2048 */
+  int32_t moe_inter;   /* I: 256, 512, 768 or 1024 */
   int32_t vocab;       /* V */
   int32_t group_size;  /* 64 */
   int32_t scale_dtype; /* REC_SCALE_* of the int4 weights */

@@ -1,0 +1,160 @@
+"""Seeded golden cases: inputs regenerated from numpy seeds, outputs frozen in
+the .npz fixtures beside this file (written by make_golden.py from the C
+oracle).
+
+The CPU tests check that the oracle still produces the frozen outputs; the
+GPU tests check that the CUDA path produces them through the C ABI.  Inputs
+are not stored: numpy's PCG64 streams are stable, and every fixture records
+a SHA-256 of its regenerated inputs so that a generator change is reported
+as such rather than as a numerical mismatch.
+"""
+from __future__ import annotations
+
+import hashlib
+from dataclasses import replace
+from pathlib import Path
+from types import SimpleNamespace
+
+import numpy as np
+import torch
+
+import oracle
+from rec_b200 import abi
+from rec_b200.model import ModelConfig
+
+HERE = Path(__file__).resolve().parent
+
+# Small models with the kernels' real shapes (hidden 2048, head_dim 128,
+# GQA 8:1) and few layers / experts / vocabulary rows.
+GOLDEN_A = ModelConfig(name="golden_a", n_layers=2, n_q_heads=16, n_kv_heads=2, n_experts=8, top_k=2,
+                       moe_inter=256, vocab=2048, kv_bits=8)
+GOLDEN_B = replace(GOLDEN_A, name="golden_b", n_q_heads=32, n_kv_heads=4, n_experts=16, top_k=6, moe_inter=512,
+                   kv_bits=4, scale_dtype=torch.bfloat16, router_mode=abi.REC_ROUTER_SIGMOID,
+                   flags=abi.REC_FLAG_SINKS | abi.REC_FLAG_QK_NORM)
+DECODE_CASES = {"decode_a": (GOLDEN_A, 101), "decode_b": (GOLDEN_B, 202)}
+
+CAPACITY = 512
+CONTEXT = 300      # cached positions before decoding (a ragged second block)
+STEPS = 6
+START_TOKEN = 5
+
+
+def sha(*arrays) -> str:
+    h = hashlib.sha256()
+    for a in arrays:
+        h.update(np.ascontiguousarray(a).tobytes())
+    return h.hexdigest()
+
+
+def _sd(cfg) -> int:
+    return 0 if cfg.scale_dtype == torch.float16 else 1
+
+
+def _q(rng, n, k, sd, std=0.02):
+    w = oracle.bf16_to_f32(oracle.f32_to_bf16((std * rng.standard_normal((n, k), dtype=np.float32))))
+    c, s, b = oracle.quantize(w, 4, sd)
+    return SimpleNamespace(w=c, s=s, b=b)
+
+
+def _bf(rng, shape, std, mean=0.0):
+    return oracle.f32_to_bf16((mean + std * rng.standard_normal(shape, dtype=np.float32)).astype(np.float32))
+
+
+def host_model(cfg: ModelConfig, seed: int) -> SimpleNamespace:
+    """Weights of `cfg` in host memory: linear weights N(0, 0.02) rounded to
+    bf16 then int4 g64; router bf16 N(0, 0.02); embedding rows N(0, 1)."""
+    rng = np.random.default_rng(seed)
+    h, d, sd = cfg.hidden, cfg.head_dim, _sd(cfg)
+    layers = []
+    for _ in range(cfg.n_layers):
+        L = SimpleNamespace(
+            input_norm=_bf(rng, h, 0.1, 1.0), post_norm=_bf(rng, h, 0.1, 1.0),
+            q=_q(rng, cfg.n_q_heads * d, h, sd), k=_q(rng, cfg.n_kv_heads * d, h, sd),
+            v=_q(rng, cfg.n_kv_heads * d, h, sd), o=_q(rng, h, cfg.n_q_heads * d, sd),
+            router=_bf(rng, (cfg.n_experts, h), 0.02),
+            gate=_q(rng, cfg.n_experts * cfg.moe_inter, h, sd), up=_q(rng, cfg.n_experts * cfg.moe_inter, h, sd),
+            down=_q(rng, cfg.n_experts * h, cfg.moe_inter, sd),
+            expert_bias=None, sinks=None, q_norm=None, k_norm=None)
+        if cfg.router_mode == abi.REC_ROUTER_SIGMOID:
+            L.expert_bias = (0.05 * rng.standard_normal(cfg.n_experts, dtype=np.float32)).astype(np.float32)
+        if cfg.flags & abi.REC_FLAG_SINKS:
+            L.sinks = _bf(rng, cfg.n_q_heads, 1.0)
+        if cfg.flags & abi.REC_FLAG_QK_NORM:
+            L.q_norm = _bf(rng, d, 0.1, 1.0)
+            L.k_norm = _bf(rng, d, 0.1, 1.0)
+        layers.append(L)
+    return SimpleNamespace(cfg=cfg, layers=layers, embed=_q(rng, cfg.vocab, h, sd, std=1.0),
+                           final_norm=_bf(rng, h, 0.1, 1.0), lm_head=_q(rng, cfg.vocab, h, sd))
+
+
+def model_sha(m) -> str:
+    parts = [m.embed.w, m.lm_head.w, m.final_norm]
+    for L in m.layers:
+        parts += [L.q.w, L.q.s, L.o.w, L.gate.w, L.down.b, L.router, L.input_norm]
+    return sha(*parts)
+
+
+def fill_kv(hkv, cfg: ModelConfig, seed: int) -> None:
+    """Positions [0, CONTEXT) of every layer: K, V ~ N(0, 1) rounded to bf16,
+    quantized (group 64 along head_dim, bf16 scales)."""
+    rng = np.random.default_rng(seed)
+    for L in hkv.layers:
+        for name in ("k", "v"):
+            x = oracle.bf16_to_f32(oracle.f32_to_bf16(
+                rng.standard_normal((cfg.n_kv_heads, CONTEXT, 128), dtype=np.float32)))
+            c, s, b = oracle.quantize(x, cfg.kv_bits, 1)
+            L[f"{name}_codes"][:, :CONTEXT] = c
+            L[f"{name}_scales"][:, :CONTEXT] = s
+            L[f"{name}_biases"][:, :CONTEXT] = b
+
+
+def kv_sha(layers, lo: int, hi: int) -> str:
+    return sha(*(L[n][:, lo:hi] for L in layers for n in sorted(L)))
+
+
+def run_oracle_decode(cfg: ModelConfig, seed: int) -> dict:
+    """Greedy decode of STEPS tokens from START_TOKEN at position CONTEXT."""
+    from oracle.host import HostModel
+
+    m = host_model(cfg, seed)
+    host = HostModel(m)
+    hkv = host.new_kv(CAPACITY)
+    fill_kv(hkv, cfg, seed + 1)
+    token, ids, shas = START_TOKEN, [], []
+    trace0 = logits = None
+    for i in range(STEPS):
+        logits, trace = host.step(hkv, token, CONTEXT + i, want_trace=True)
+        if i == 0:
+            trace0 = trace.copy()
+        shas.append(sha(logits))
+        token = oracle.argmax_bf16(logits)
+        ids.append(token)
+    return {"input_sha": model_sha(m), "ids": np.array(ids, np.int32), "logits_sha": np.array(shas),
+            "last_logits": logits.copy(), "trace0_sha": sha(trace0),
+            "kv_new_sha": kv_sha(hkv.layers, CONTEXT, CONTEXT + STEPS)}
+
+
+# ---- GEMV: one seeded matrix per K, with and without the fused RMSNorm
+GEMV_CASES = {"gemv_k2048_fp16": (2048, 0, 31), "gemv_k4096_bf16": (4096, 1, 32), "gemv_k768_fp16": (768, 0, 33)}
+GEMV_ROWS = 256 + 2 * 37
+
+
+def gemv_inputs(k: int, sd: int, seed: int):
+    rng = np.random.default_rng(seed)
+    w = _q(rng, GEMV_ROWS, k, sd)
+    x = _bf(rng, k, 1.0)
+    nw = _bf(rng, k, 0.1, 1.0)
+    return w, x, nw
+
+
+def run_oracle_gemv(k: int, sd: int, seed: int) -> dict:
+    w, x, nw = gemv_inputs(k, sd, seed)
+    out = {"input_sha": sha(w.w, w.s, w.b, x, nw), "y": oracle.gemv(w.w, w.s, w.b, x, sd)}
+    if k % 256 == 0:
+        out["y_norm"] = oracle.gemv(w.w, w.s, w.b, oracle.rmsnorm(x, nw, 1e-6), sd)
+    return out
+
+
+def load(name: str) -> dict:
+    with np.load(HERE / f"{name}.npz", allow_pickle=False) as f:
+        return {k: f[k] for k in f.files}

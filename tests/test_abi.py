@@ -1,0 +1,69 @@
+"""The C-ABI library loads without a GPU and exports every function that
+include/rec_b200.h declares; the ctypes mirror matches the header's
+constants and structure sizes.  No compute calls."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+from rec_b200 import _lib, abi
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "rec_b200.h"
+
+
+def _declared():
+    text = HEADER.read_text()
+    return re.findall(r"REC_API\s+[\w\s\*]+?\b(rec_\w+)\s*\(", text)
+
+
+def _lib_or_skip():
+    if not _lib.LIB_PATH.exists():
+        pytest.skip("librec_b200.so not built")
+    return _lib.lib()
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert len(names) == len(set(names))
+    for n in ("rec_create", "rec_decode_step", "rec_decode_greedy", "rec_gemv_int4", "rec_quantize_affine",
+              "rec_gemv_int4_argmax_noalloc"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib_or_skip()
+    missing = [n for n in _declared() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_ctypes_signatures_cover_the_header():
+    assert set(_declared()) <= set(_lib._SIGNATURES)
+
+
+def test_constants_match_header():
+    text = HEADER.read_text()
+    for name in ("REC_OK", "REC_EINVAL", "REC_ECUDA", "REC_ESTATE", "REC_ELIMIT", "REC_DEV_BULK_TIMEOUT",
+                 "REC_DEV_COUNTER_TIMEOUT", "REC_DEV_BAD_TOKEN", "REC_DEV_BAD_POSITION", "REC_SCALE_FP16",
+                 "REC_SCALE_BF16", "REC_ROUTER_SOFTMAX", "REC_ROUTER_SIGMOID", "REC_FLAG_SINKS", "REC_FLAG_QK_NORM"):
+        m = re.search(rf"\b{name}\s*=\s*(-?\d+)", text)
+        assert m, name
+        assert int(m.group(1)) == getattr(abi, name), name
+
+
+def test_struct_sizes():
+    p = C.sizeof(C.c_void_p)
+    assert C.sizeof(abi.RecModelDesc) == 16 * 4
+    assert C.sizeof(abi.RecQMat) == 3 * p
+    assert C.sizeof(abi.RecLayerWeights) == (2 + 4 * 3 + 2 + 3 * 3 + 3) * p
+    assert C.sizeof(abi.RecGlobalWeights) == (3 + 1 + 3) * p
+    assert C.sizeof(abi.RecKVLayer) == 6 * p
+
+
+def test_argument_errors_need_no_device():
+    lib = _lib_or_skip()
+    out = C.c_void_p()
+    desc = abi.RecModelDesc(hidden=1000, n_layers=1, n_q_heads=32, n_kv_heads=4, head_dim=128, n_experts=8,
+                            top_k=2, moe_inter=256, vocab=64, group_size=64)
+    assert lib.rec_create(C.byref(desc), C.byref(out)) == abi.REC_EINVAL
+    assert "hidden" in _lib.last_error().lower()
