@@ -113,12 +113,14 @@ typedef struct RecKVLayer {
   void* v_biases;
 } RecKVLayer;
 
-/* Sampling parameters of the sampling head. */
+/* Sampling parameters of the sampling head (reference engine.py:206-212,
+ * masked_sampling.py:98-125, filtered_sampling.py:7-22). */
 typedef struct RecSampling {
   float temperature;        /* 0 = greedy */
-  int32_t top_k;            /* 0 = off */
-  float top_p;              /* 1 = off */
-  float repetition_penalty; /* 1 = off */
+  int32_t top_k;            /* 0 = off; <= 256 */
+  float top_p;              /* >= 1 = off; < 1 needs top_k > 0 */
+  float repetition_penalty; /* 1 = off: x<0 ? x*p : x/p for ids in the history */
+  float presence_penalty;   /* 0 = off: x - p for ids in the history */
 } RecSampling;
 
 typedef struct RecCtx RecCtx;
@@ -202,6 +204,16 @@ REC_API int rec_gemv_int4(const RecQMat* w, int32_t scale_dtype, int64_t n, int3
 REC_API int rec_gemv_int4_argmax_noalloc(const RecQMat* w, int32_t scale_dtype, int64_t n, int32_t k,
                                          const void* x_dev, const void* norm_weight_dev, float eps,
                                          void* y_dev, int32_t* token_dev, void* stream);
+/* Samples one id per row of bf16 logits [batch, stride] (vocab <= 262,144):
+ * penalties over the row's history (int32 [batch, history_len]), then greedy
+ * argmax (temperature 0), or temperature / top-k / top-p with the injected
+ * uniforms (fp32 [batch, vocab], u in [0, 1)) as Gumbel noise -log(-log u).
+ * Replaces the reference's sampler step (engine.py:279-301,
+ * masked_sampling.py:98-125, filtered_sampling.py:7-22, sampling.py:48-52).
+ * ids_dev[b] = -1 when more than 1,024 logits tie at the top-k threshold. */
+REC_API int rec_sample_logits(const void* logits_dev, int32_t batch, int32_t vocab, int64_t stride,
+                              const int32_t* history_dev, int32_t history_len, const RecSampling* params,
+                              const float* uniforms_dev, int32_t* ids_dev, void* stream);
 /* MLX affine quantization of fp32 groups into codes + (bf16|fp16) scale/bias. */
 REC_API int rec_quantize_affine(const float* w_dev, int64_t n_groups, int32_t bits,
                                 int32_t scale_dtype, void* codes_dev, void* scales_dev,

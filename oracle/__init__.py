@@ -55,6 +55,10 @@ def lib() -> C.CDLL:
         L.orc_argmax_bf16.argtypes = [_u16p, C.c_int64]
         L.orc_partial_bytes.restype = C.c_int
         L.orc_sample.restype = C.c_int32
+        L.orc_sample.argtypes = [_u16p, C.c_int64, C.c_void_p, C.c_int, C.c_void_p, _f32p]
+        L.orc_log.restype = C.c_float
+        L.orc_log.argtypes = [C.c_float]
+        L.orc_log_n.argtypes = [_f32p, _f32p, C.c_int64]
         L.orc_to_bf.restype = C.c_uint16
         L.orc_to_bf.argtypes = [C.c_float]
         L.orc_to_hf.restype = C.c_uint16
@@ -185,3 +189,24 @@ def swiglu(g_bf16: int, u_bf16: int) -> int:
 def argmax_bf16(x) -> int:
     x = np.ascontiguousarray(x, np.uint16)
     return int(lib().orc_argmax_bf16(x, x.size))
+
+
+def log(x: np.ndarray) -> np.ndarray:
+    """The kernels' canonical natural logarithm (sampler)."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    lib().orc_log_n(x, y, x.size)
+    return y
+
+
+def sample(logits_bf16, history, params, uniforms) -> int:
+    """orc_sample on one row: logits uint16[V] (bf16 bits), history int32 ids,
+    params a rec_b200.abi.RecSampling, uniforms float32[V] (or None when the
+    temperature is 0)."""
+    from rec_b200 import abi
+
+    lg = np.ascontiguousarray(logits_bf16, np.uint16)
+    h = np.ascontiguousarray(history if history is not None else np.zeros(0), np.int32)
+    u = np.ascontiguousarray(uniforms if uniforms is not None else np.zeros(lg.size), np.float32)
+    assert isinstance(params, abi.RecSampling)
+    return int(lib().orc_sample(lg, lg.size, h.ctypes.data if h.size else None, h.size, C.byref(params), u))

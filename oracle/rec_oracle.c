@@ -689,70 +689,180 @@ static int32_t argmax_bf16(const uint16_t* x, int64_t n) {
 }
 ORC_API int32_t orc_argmax_bf16(const uint16_t* x, int64_t n) { return argmax_bf16(x, n); }
 
-/* Sampler: z = penalised(logit)/T; keep the top_k by z (ties -> lower
- * index) in descending order; e_i = exp(z_i - z_0); S = sum e_i; p_i = e_i/S;
- * keep the shortest prefix whose cumulative p reaches top_p; draw with the
- * uniform u as the first i with cumsum(e)_i > u * sum(e over kept).
- * Penalty (repetition): for ids present in history, l > 0 ? l/pen : l*pen. */
+/* Natural logarithm in the kernels' canonical form (rec_b200/csrc/common.cuh
+ * rlog): x = m*2^e, m in [sqrt(1/2), sqrt(2)); atanh series in
+ * f = (m-1)/(m+1) through f^13 by Horner in f^2. */
+ORC_API float orc_log(float x) {
+  if (x != x) return x;
+  if (x == 0.0f) return -INFINITY;
+  if (x < 0.0f) return NAN;
+  if (isinf(x)) return x;
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  int e = 0;
+  if (u < 0x00800000u) {
+    float y = x * 16777216.0f;
+    memcpy(&u, &y, 4);
+    e = -24;
+  }
+  e += (int)(u >> 23) - 127;
+  uint32_t mu = (u & 0x007fffffu) | 0x3f800000u;
+  float m;
+  memcpy(&m, &mu, 4);
+  if (m > 1.41421353816986084f) {
+    m = m * 0.5f;
+    e += 1;
+  }
+  float f = (m - 1.0f) / (m + 1.0f);
+  float f2 = f * f;
+  float p = 7.69230769230769231e-2f;
+  p = fmaf(p, f2, 9.09090909090909091e-2f);
+  p = fmaf(p, f2, 1.11111111111111111e-1f);
+  p = fmaf(p, f2, 1.42857142857142857e-1f);
+  p = fmaf(p, f2, 2.00000000000000000e-1f);
+  p = fmaf(p, f2, 3.33333333333333333e-1f);
+  p = p * f2;
+  float f2x = 2.0f * f;
+  float lnm = fmaf(f2x, p, f2x);
+  float ef = (float)e;
+  return fmaf(ef, 0.693145751953125f, fmaf(ef, 1.42860682030941723e-6f, lnm));
+}
+static inline float rlog(float x) { return orc_log(x); }
+ORC_API void orc_log_n(const float* x, float* y, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) y[i] = orc_log(x[i]);
+}
+static inline float gumbel(float u) { return -rlog(-rlog(u)); }
+
+typedef struct {
+  float x;
+  int32_t i;
+} Cand;
+/* descending (x, index) */
+static int cand_desc(const void* pa, const void* pb) {
+  const Cand *a = (const Cand*)pa, *b = (const Cand*)pb;
+  if (a->x != b->x) return a->x > b->x ? -1 : 1;
+  return a->i > b->i ? -1 : (a->i < b->i ? 1 : 0);
+}
+
+#define SAMPLE_THREADS 1024
+#define SAMPLE_MAX_CAND 1024
+
+/* Sampling head of one row (rec_b200/csrc/sample.cuh states the rule):
+ * penalties over the history, then greedy argmax, or Gumbel-max with the
+ * injected uniforms u[V] over all logits (top_k = 0) or over the reference's
+ * joint top-k / top-p filter (engine.py:279-301, masked_sampling.py:98-125,
+ * filtered_sampling.py:7-22, sampling.py:48-52).  Returns -1 when more than
+ * 1,024 logits tie at the top-k threshold. */
 ORC_API int32_t orc_sample(const uint16_t* logits, int64_t V, const int32_t* hist, int n_hist,
-                           const RecSampling* sp, float u) {
-  if (sp->temperature == 0.0f) return argmax_bf16(logits, V);
+                           const RecSampling* sp, const float* u) {
+  const int pen = sp->repetition_penalty != 1.0f || sp->presence_penalty != 0.0f;
   uint8_t* seen = (uint8_t*)calloc((size_t)V, 1);
-  for (int i = 0; i < n_hist; ++i)
-    if (hist[i] >= 0 && hist[i] < V) seen[hist[i]] = 1;
-  int K = sp->top_k > 0 ? sp->top_k : (int)V;
-  if (K > V) K = (int)V;
-  float* z = (float*)malloc(sizeof(float) * V);
-  for (int64_t v = 0; v < V; ++v) {
-    float l = bf(logits[v]);
-    if (seen[v] && sp->repetition_penalty != 1.0f)
-      l = l > 0.0f ? l / sp->repetition_penalty : l * sp->repetition_penalty;
-    z[v] = l / sp->temperature;
-  }
-  /* top-K selection by repeated max (ties -> lower index) */
-  int32_t* sel = (int32_t*)malloc(sizeof(int32_t) * K);
-  uint8_t* used = (uint8_t*)calloc((size_t)V, 1);
-  for (int r = 0; r < K; ++r) {
-    int64_t best = -1;
-    for (int64_t v = 0; v < V; ++v)
-      if (!used[v] && (best < 0 || z[v] > z[best])) best = v;
-    used[best] = 1;
-    sel[r] = (int32_t)best;
-  }
-  float* e = (float*)malloc(sizeof(float) * K);
-  float S = 0.0f;
-  for (int r = 0; r < K; ++r) {
-    e[r] = rexp(z[sel[r]] - z[sel[0]]);
-    S = S + e[r];
-  }
-  int n = K;
-  if (sp->top_p < 1.0f) {
-    float c = 0.0f;
-    for (int r = 0; r < K; ++r) {
-      c = c + e[r] / S;
-      if (c >= sp->top_p) {
-        n = r + 1;
-        break;
-      }
+  if (pen)
+    for (int i = 0; i < n_hist; ++i)
+      if (hist[i] >= 0 && hist[i] < V) seen[hist[i]] = 1;
+  float* x = (float*)malloc(sizeof(float) * V);
+  for (int64_t i = 0; i < V; ++i) {
+    float v = bf(logits[i]);
+    if (seen[i]) {
+      if (sp->repetition_penalty != 1.0f)
+        v = v < 0.0f ? v * sp->repetition_penalty : v / sp->repetition_penalty;
+      if (sp->presence_penalty != 0.0f) v = v - sp->presence_penalty;
     }
-  }
-  float Sn = 0.0f;
-  for (int r = 0; r < n; ++r) Sn = Sn + e[r];
-  float target = u * Sn;
-  float c = 0.0f;
-  int32_t out = sel[n - 1];
-  for (int r = 0; r < n; ++r) {
-    c = c + e[r];
-    if (c > target) {
-      out = sel[r];
-      break;
-    }
+    x[i] = v + 0.0f;
   }
   free(seen);
-  free(z);
-  free(sel);
-  free(used);
-  free(e);
+  float M = -INFINITY;
+  int32_t Mi = 0;
+  for (int64_t i = 0; i < V; ++i)
+    if (x[i] > M) {
+      M = x[i];
+      Mi = (int32_t)i;
+    }
+  if (sp->temperature == 0.0f) {
+    free(x);
+    return Mi;
+  }
+  /* S: thread t sums i = t, t+1024, ...; warp butterflies; warps in order */
+  float tot = 0.0f;
+  for (int w = 0; w < SAMPLE_THREADS / 32; ++w) {
+    float lanes[32];
+    for (int l = 0; l < 32; ++l) {
+      float acc = 0.0f;
+      for (int64_t i = w * 32 + l; i < V; i += SAMPLE_THREADS) acc = acc + rexp(x[i] - M);
+      lanes[l] = acc;
+    }
+    bfly(lanes, 32);
+    tot = tot + lanes[0];
+  }
+  const float lse = M + rlog(tot);
+  const float inv_t = 1.0f / sp->temperature;
+  int32_t out = -1;
+  if (sp->top_k == 0) {
+    const int t1 = sp->temperature == 1.0f && sp->top_p >= 1.0f;
+    float bv = -INFINITY;
+    int32_t bi = 0x7fffffff;
+    for (int64_t i = 0; i < V; ++i) {
+      float z = t1 ? x[i] + gumbel(u[i]) : (x[i] - lse) * inv_t + gumbel(u[i]);
+      if (z > bv) {
+        bv = z;
+        bi = (int32_t)i;
+      }
+    }
+    free(x);
+    return bi;
+  }
+  /* top-k threshold: the k-th largest x */
+  Cand* all = (Cand*)malloc(sizeof(Cand) * V);
+  for (int64_t i = 0; i < V; ++i) {
+    all[i].x = x[i];
+    all[i].i = (int32_t)i;
+  }
+  qsort(all, (size_t)V, sizeof(Cand), cand_desc);
+  const float theta = all[sp->top_k - 1].x;
+  int greater = 0, n = 0;
+  while (n < V && all[n].x >= theta) {
+    if (all[n].x > theta) ++greater;
+    ++n;
+  }
+  if (n > SAMPLE_MAX_CAND) {
+    free(all);
+    free(x);
+    return -1;
+  }
+  /* keep_p along the descending (x, index) order */
+  int* keep_p = (int*)malloc(sizeof(int) * n);
+  float* lp = (float*)malloc(sizeof(float) * n);
+  const int use_p = sp->top_p < 1.0f;
+  float U = 0.0f;
+  for (int q = 0; q < n; ++q) {
+    lp[q] = all[q].x - lse;
+    keep_p[q] = !use_p || U < sp->top_p;
+    U = U + rexp(lp[q]);
+  }
+  int first = -1;
+  for (int q = n - 1; q >= greater; --q)
+    if (keep_p[q]) {
+      first = q;
+      break;
+    }
+  const int allowed = sp->top_k - greater;
+  const int lo = first < 0 ? n : (first - allowed + 1 > greater ? first - allowed + 1 : greater);
+  float bv = -INFINITY;
+  int32_t bi = 0x7fffffff;
+  for (int q = 0; q < n; ++q) {
+    int keep = q < greater ? keep_p[q] : (q >= lo && q <= first);
+    if (!keep) continue;
+    float z = lp[q] * inv_t + gumbel(u[all[q].i]);
+    if (z > bv || (z == bv && all[q].i < bi)) {
+      bv = z;
+      bi = all[q].i;
+    }
+  }
+  out = bi;
+  free(keep_p);
+  free(lp);
+  free(all);
+  free(x);
   return out;
 }
 

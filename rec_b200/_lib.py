@@ -20,6 +20,8 @@ _SIGNATURES = {
     "rec_gemv_int4_argmax_noalloc": (C.c_int, [C.POINTER(abi.RecQMat), C.c_int32, C.c_int64, C.c_int32,
                                                C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_void_p,
                                                C.c_void_p]),
+    "rec_sample_logits": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int64, C.c_void_p, C.c_int32,
+                                    C.POINTER(abi.RecSampling), C.c_void_p, C.c_void_p, C.c_void_p]),
     "rec_quantize_affine": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_void_p]),
     "rec_create": (C.c_int, [C.POINTER(abi.RecModelDesc), C.POINTER(C.c_void_p)]),

@@ -86,4 +86,5 @@ class RecSampling(C.Structure):
         ("top_k", C.c_int32),
         ("top_p", C.c_float),
         ("repetition_penalty", C.c_float),
+        ("presence_penalty", C.c_float),
     ]

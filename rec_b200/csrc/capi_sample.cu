@@ -1,0 +1,44 @@
+// C-ABI entry point of the sampling head over bf16 logits.
+#include "capi_common.h"
+#include "sample.cuh"
+
+using namespace rec;
+
+REC_API int rec_sample_logits(const void* logits_dev, int32_t batch, int32_t vocab, int64_t stride,
+                              const int32_t* history_dev, int32_t history_len, const RecSampling* params,
+                              const float* uniforms_dev, int32_t* ids_dev, void* stream) {
+  REC_CHECK_ARG(logits_dev && ids_dev && params, "rec_sample_logits: null pointer");
+  REC_CHECK_ARG(batch >= 1 && batch <= 64, "rec_sample_logits: batch %d outside 1..64", batch);
+  REC_CHECK_ARG(vocab >= 2 && vocab <= kSampleMaxVocab, "rec_sample_logits: vocab %d outside 2..%d", vocab,
+                kSampleMaxVocab);
+  REC_CHECK_ARG(stride >= vocab, "rec_sample_logits: row stride %lld < vocab", (long long)stride);
+  REC_CHECK_ARG(history_len >= 0 && (history_len == 0 || history_dev), "rec_sample_logits: bad history");
+  const RecSampling& p = *params;
+  REC_CHECK_ARG(p.temperature >= 0.0f && p.temperature < 1e30f, "rec_sample_logits: bad temperature");
+  REC_CHECK_ARG(p.repetition_penalty > 0.0f, "rec_sample_logits: repetition penalty must be positive");
+  if (p.temperature > 0.0f) {
+    REC_CHECK_ARG(uniforms_dev, "rec_sample_logits: temperature > 0 needs uniforms");
+    REC_CHECK_ARG(p.top_k >= 0 && p.top_k < vocab && p.top_k <= kSampleMaxTopK,
+                  "top_k must be between 0 and %d", vocab - 1 < kSampleMaxTopK ? vocab - 1 : kSampleMaxTopK);
+    REC_CHECK_ARG(p.top_p > 0.0f, "top_p must be positive");
+    REC_CHECK_ARG(p.top_k > 0 || p.top_p >= 1.0f, "top_p < 1 needs top_k > 0");
+  }
+  SampleArgs a = {};
+  a.logits = static_cast<const uint16_t*>(logits_dev);
+  a.stride = stride;
+  a.V = vocab;
+  a.history = history_dev;
+  a.n_hist = history_len;
+  a.temperature = p.temperature;
+  a.top_k = p.top_k;
+  a.top_p = p.top_p;
+  a.rep = p.repetition_penalty;
+  a.presence = p.presence_penalty;
+  a.uniforms = uniforms_dev;
+  a.ids = ids_dev;
+  const size_t dyn = size_t((vocab + 31) / 32) * 4;
+  REC_CHECK_CUDA(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, int(dyn)));
+  k_sample<<<batch, kSampleThreads, dyn, static_cast<cudaStream_t>(stream)>>>(a);
+  REC_CHECK_CUDA(cudaGetLastError());
+  return REC_OK;
+}

@@ -85,6 +85,44 @@ __device__ __forceinline__ float rexp(float x) {
   return __fmul_rn(p, __int_as_float((e2 + 127) << 23));
 }
 
+// Natural logarithm shared by the kernels and the oracle (the sampler's
+// log-sum-exp and Gumbel noise).  Argument reduction x = m * 2^e with m in
+// [sqrt(1/2), sqrt(2)), then the atanh series ln m = 2f + 2f(f^2/3 + f^4/5 +
+// ... + f^12/13), f = (m-1)/(m+1), by Horner in f^2 with fused
+// multiply-adds; ln x = e*ln2_hi + (e*ln2_lo + ln m).  ln(+-0) = -inf,
+// ln(x<0) = NaN, ln(inf) = inf.
+__device__ __forceinline__ float rlog(float x) {
+  if (x != x) return x;
+  if (x == 0.0f) return __int_as_float(0xff800000);
+  if (x < 0.0f) return __int_as_float(0x7fc00000);
+  if (x == __int_as_float(0x7f800000)) return x;
+  uint32_t u = __float_as_uint(x);
+  int e = 0;
+  if (u < 0x00800000u) {  // subnormal: scale by 2^24 (exact)
+    u = __float_as_uint(__fmul_rn(x, 16777216.0f));
+    e = -24;
+  }
+  e += int(u >> 23) - 127;
+  float m = __uint_as_float((u & 0x007fffffu) | 0x3f800000u);
+  if (m > 1.41421353816986084f) {
+    m = __fmul_rn(m, 0.5f);
+    e += 1;
+  }
+  const float f = __fdiv_rn(__fsub_rn(m, 1.0f), __fadd_rn(m, 1.0f));
+  const float f2 = __fmul_rn(f, f);
+  float p = 7.69230769230769231e-2f;            // 1/13
+  p = __fmaf_rn(p, f2, 9.09090909090909091e-2f);  // 1/11
+  p = __fmaf_rn(p, f2, 1.11111111111111111e-1f);  // 1/9
+  p = __fmaf_rn(p, f2, 1.42857142857142857e-1f);  // 1/7
+  p = __fmaf_rn(p, f2, 2.00000000000000000e-1f);  // 1/5
+  p = __fmaf_rn(p, f2, 3.33333333333333333e-1f);  // 1/3
+  p = __fmul_rn(p, f2);
+  const float f2x = __fmul_rn(2.0f, f);
+  const float lnm = __fmaf_rn(f2x, p, f2x);
+  const float ef = float(e);
+  return __fmaf_rn(ef, 0.693145751953125f, __fmaf_rn(ef, 1.42860682030941723e-6f, lnm));
+}
+
 // SiLU factor used by the reference's routed experts:
 // tail = 1/(1+exp(|g|)), sigmoid = g<0 ? tail : 1-tail.
 __device__ __forceinline__ float rsigmoid(float g) {

@@ -521,6 +521,35 @@ struct Consumers {
     }
   }
 
+  // --- O with K = 2048 (n_q_heads = 16): 8 warps x ILP 4, residual into own rows
+  __device__ void rows2048_resid(const uint8_t* st, int n, int grow0, int own0, const GroupX (&gx)[1], FixScale fs) {
+    const uint32_t wb = uint32_t(n) * 1024, sbytes = uint32_t(n) * 64;
+    const uint8_t* wbase = st;
+    const uint16_t* sbase = reinterpret_cast<const uint16_t*>(st + wb);
+    const uint16_t* bbase = reinterpret_cast<const uint16_t*>(st + wb + ((sbytes + 15) & ~15u));
+    int rows[4];
+    bool valid[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = warp + i * kMegaCons;
+      valid[i] = r < n;
+      rows[i] = valid[i] ? r : 0;
+    }
+    float v[4];
+    lane_rows_partial<2048, 2, 4>(wbase, sbase, bbase, rows, 0, lane, gx, v, a.sd);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[i] = __fmul_rn(bfly_sum(valid[i] ? v[i] : 0.0f), fs.down);
+      if (valid[i] && lane == 0) {
+        const int g = grow0 + rows[i];
+        const int own = g - own0;
+        const uint16_t hn = to_bf(__fadd_rn(bf(sm.hown[own]), rbf(v[i])));
+        sm.hown[own] = hn;
+        a.h[g] = hn;
+      }
+    }
+  }
+
   // --- O: K = 4096 rows, warp pairs (one 2048 segment each) x ILP 4 ---------
   __device__ void rows4096(const uint8_t* st, int n, int grow0, int own0, const GroupX (&gx)[1], FixScale fs) {
     // always called by every consumer warp: the team barriers below must match
@@ -818,12 +847,22 @@ struct Consumers {
         {
           const FixScale fo = load_x(a.attn, a.hq * 128);
           GroupX gx[1];
-          prep_lane_x<4096>(sm.xn, fo, warp & 1, lane, gx);
-          for (int r = P.o0; r < P.o1; r += kORows) {
-            const int n = min(kORows, P.o1 - r);
-            const uint8_t* st = take();
-            rows4096(st, n, r, P.o0, gx, fo);
-            release();
+          if (a.hq * 128 == 4096) {
+            prep_lane_x<4096>(sm.xn, fo, warp & 1, lane, gx);
+            for (int r = P.o0; r < P.o1; r += kORows) {
+              const int n = min(kORows, P.o1 - r);
+              const uint8_t* st = take();
+              rows4096(st, n, r, P.o0, gx, fo);
+              release();
+            }
+          } else {
+            prep_lane_x<2048>(sm.xn, fo, 0, lane, gx);
+            for (int r = P.o0; r < P.o1; r += kORows) {
+              const int n = min(kORows, P.o1 - r);
+              const uint8_t* st = take();
+              rows2048_resid(st, n, r, P.o0, gx, fo);
+              release();
+            }
           }
         }
         if (!grid_barrier(a, bar_index(a, step, l, 2))) return;

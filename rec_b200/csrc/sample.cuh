@@ -1,0 +1,293 @@
+// Sampling head over bf16 logits: repetition / presence penalty, temperature,
+// top-k and top-p with injected uniforms, or greedy argmax.  One CTA of 1024
+// threads per batch row; the row's logits are re-read from L2 by each pass.
+//
+// Canonical rule (restated by oracle/rec_oracle.c:orc_sample):
+//   x_i   = float(logit_i); for ids in the row's history: x = x<0 ? x*rho : x/rho
+//           (rho != 1; mlx-lm repetition-penalty processor), then x -= alpha
+//           (alpha != 0; the reference's presence mask, masked_sampling.py:99-100);
+//           -0 is canonicalised to +0.
+//   T = 0 : argmax x, lowest index among equal maxima (engine.py:284-285).
+//   lse   = M + log(S), M = max x, S = sum exp(x - M): thread t sums i = t,
+//           t+1024, ... in order, then a warp butterfly, then the 32 warp sums in
+//           order.  lp_i = x_i - lse.
+//   (T, top_p, top_k) = (1, 1, 0): id = argmax(x_i + g_i)      (sampling.py:48-52)
+//   top_k = 0 (top_p = 1): id = argmax(lp_i * (1/T) + g_i)     (mlx-lm categorical)
+//   top_k > 0: the reference's joint filter (filtered_sampling.py:7-22) over the
+//           stable ascending order of (x, index): theta = k-th largest x,
+//           greater = #(x > theta); U_j = sum of exp(lp) of every element after j
+//           in that order, accumulated in fp32 from the top; keep_p(j) <=> U_j <
+//           top_p (the exact-arithmetic form of cumsum_j > 1 - top_p; always true
+//           when top_p >= 1); keep = keep_p and (x > theta, or x == theta and
+//           among the first (top_k - greater) tied elements, by index, from the
+//           lowest-index tied element with keep_p).  id = argmax over kept of
+//           lp * (1/T) + g, lowest index on ties.
+//   g_i   = -log(-log(u_i)) with the injected uniform u_i (the reference draws it
+//           with mx.random.gumbel; fixing u makes the ids comparable).
+#pragma once
+#include "common.cuh"
+
+namespace rec {
+
+constexpr int kSampleThreads = 1024;
+constexpr int kSampleMaxCand = 1024;  // elements >= the top-k threshold (ties included)
+constexpr int kSampleMaxTopK = 256;
+constexpr int kSampleMaxVocab = 262144;
+
+struct SampleArgs {
+  const uint16_t* logits;  // bf16 [B, stride]
+  int64_t stride;
+  int V;
+  const int* history;      // int32 [B, n_hist] or null
+  int n_hist;
+  float temperature, top_p, rep, presence;
+  int top_k;
+  const float* uniforms;   // fp32 [B, V] (temperature > 0)
+  int* ids;                // int32 [B]; -1: more than kSampleMaxCand ties at the threshold
+};
+
+// Order-preserving unsigned key of a non-NaN float (-0 must be canonicalised).
+__device__ __forceinline__ uint32_t float_key(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float gumbel(float u) { return -rlog(-rlog(u)); }
+
+struct SampleSmem {
+  float red_v[32];
+  int red_i[32];
+  unsigned hist[256];
+  float cx[kSampleMaxCand];
+  int ci[kSampleMaxCand];
+  float sx[kSampleMaxCand];
+  int si[kSampleMaxCand];
+  float sp[kSampleMaxCand];
+  float slp[kSampleMaxCand];
+  int n_cand;
+  uint32_t prefix, mask;
+  int rank, tied, keep_lo, keep_hi;
+  float lse;
+  float M;
+  int Mi;
+};
+
+// Block-wide argmax (value desc, index asc) of one value per thread; all
+// threads return the result.
+__device__ __forceinline__ void block_argmax(float& v, int& i, SampleSmem& s) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, off);
+    if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+  }
+  if (lane == 0) { s.red_v[warp] = v; s.red_i[warp] = i; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float bv = s.red_v[0];
+    int bi = s.red_i[0];
+    for (int w = 1; w < 32; ++w)
+      if (s.red_v[w] > bv || (s.red_v[w] == bv && s.red_i[w] < bi)) { bv = s.red_v[w]; bi = s.red_i[w]; }
+    s.M = bv;
+    s.Mi = bi;
+  }
+  __syncthreads();
+  v = s.M;
+  i = s.Mi;
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const SampleArgs a) {
+  extern __shared__ uint32_t seen[];  // history bitmap [ceil(V/32)]
+  __shared__ SampleSmem s;
+  const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int V = a.V;
+  const uint16_t* lg = a.logits + size_t(b) * a.stride;
+  const bool pen = a.rep != 1.0f || a.presence != 0.0f;
+  const int nw = (V + 31) >> 5;
+  if (pen) {
+    for (int i = t; i < nw; i += kSampleThreads) seen[i] = 0u;
+    __syncthreads();
+    for (int i = t; i < a.n_hist; i += kSampleThreads) {
+      const int id = a.history[size_t(b) * a.n_hist + i];
+      if (id >= 0 && id < V) atomicOr(&seen[id >> 5], 1u << (id & 31));
+    }
+    __syncthreads();
+  }
+  auto X = [&](int i) -> float {
+    float x = bf(lg[i]);
+    if (pen && ((seen[i >> 5] >> (i & 31)) & 1u)) {
+      if (a.rep != 1.0f) x = x < 0.0f ? __fmul_rn(x, a.rep) : __fdiv_rn(x, a.rep);
+      if (a.presence != 0.0f) x = __fsub_rn(x, a.presence);
+    }
+    return __fadd_rn(x, 0.0f);
+  };
+  const bool filtered = a.temperature != 0.0f && a.top_k > 0;
+
+  // ---- pass 1: max (argmax for greedy) and the top digit's histogram
+  if (filtered) {
+    for (int i = t; i < 256; i += kSampleThreads) s.hist[i] = 0u;
+    __syncthreads();
+  }
+  float mx = -INFINITY;
+  int mi = 0x7fffffff;
+  for (int i = t; i < V; i += kSampleThreads) {
+    const float x = X(i);
+    if (x > mx) { mx = x; mi = i; }
+    if (filtered) atomicAdd(&s.hist[float_key(x) >> 24], 1u);
+  }
+  block_argmax(mx, mi, s);
+  if (a.temperature == 0.0f) {
+    if (t == 0) a.ids[b] = mi;
+    return;
+  }
+  const float M = mx;
+
+  // radix select of the k-th largest key: resolve one digit from s.hist
+  auto resolve = [&](int level) {
+    if (t == 0) {
+      const int shift = 24 - 8 * level;
+      int rank = level == 0 ? a.top_k - 1 : s.rank;
+      unsigned c = 0;
+      int d = 255;
+      for (; d > 0; --d) {
+        if (c + s.hist[d] > unsigned(rank)) break;
+        c += s.hist[d];
+      }
+      s.rank = rank - int(c);
+      s.prefix = (level == 0 ? 0u : s.prefix) | (uint32_t(d) << shift);
+      s.mask = (level == 0 ? 0u : s.mask) | (0xFFu << shift);
+      if (level == 3) s.tied = int(s.hist[d]);
+    }
+    __syncthreads();
+  };
+  auto histogram = [&](int level) {  // elements matching the prefix of levels < level
+    for (int i = t; i < 256; i += kSampleThreads) s.hist[i] = 0u;
+    __syncthreads();
+    const uint32_t pre = s.prefix, msk = s.mask;
+    const int shift = 24 - 8 * level;
+    for (int i = t; i < V; i += kSampleThreads) {
+      const uint32_t k = float_key(X(i));
+      if ((k & msk) == pre) atomicAdd(&s.hist[(k >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+  };
+  if (filtered) resolve(0);
+
+  // ---- pass 2: log-sum-exp (canonical order) [+ next digit]
+  {
+    float sum = 0.0f;
+    for (int i = t; i < V; i += kSampleThreads) sum = __fadd_rn(sum, rexp(__fsub_rn(X(i), M)));
+    sum = bfly_sum(sum);
+    if (lane == 0) s.red_v[warp] = sum;
+    __syncthreads();
+    if (t == 0) {
+      float tot = 0.0f;
+      for (int w = 0; w < 32; ++w) tot = __fadd_rn(tot, s.red_v[w]);
+      s.lse = __fadd_rn(M, rlog(tot));
+    }
+    __syncthreads();
+  }
+  const float lse = s.lse;
+  const float inv_t = __fdiv_rn(1.0f, a.temperature);
+  const float* u = a.uniforms + size_t(b) * V;
+
+  if (!filtered) {
+    const bool t1 = a.temperature == 1.0f && a.top_p >= 1.0f;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = t; i < V; i += kSampleThreads) {
+      const float x = X(i);
+      const float z = t1 ? __fadd_rn(x, gumbel(u[i])) : __fadd_rn(__fmul_rn(__fsub_rn(x, lse), inv_t), gumbel(u[i]));
+      if (z > bv) { bv = z; bi = i; }
+    }
+    block_argmax(bv, bi, s);
+    if (t == 0) a.ids[b] = bi;
+    return;
+  }
+
+  for (int level = 1; level < 4; ++level) {
+    histogram(level);
+    resolve(level);
+  }
+  const uint32_t theta = s.prefix;
+  const int greater = a.top_k - 1 - s.rank;
+  const int n = greater + s.tied;
+  if (n > kSampleMaxCand) {
+    if (t == 0) a.ids[b] = -1;
+    return;
+  }
+  // ---- collect the elements >= theta
+  if (t == 0) s.n_cand = 0;
+  __syncthreads();
+  for (int i = t; i < V; i += kSampleThreads) {
+    const float x = X(i);
+    if (float_key(x) >= theta) {
+      const int slot = atomicAdd(&s.n_cand, 1);
+      if (slot < kSampleMaxCand) {
+        s.cx[slot] = x;
+        s.ci[slot] = i;
+      }
+    }
+  }
+  __syncthreads();
+  // descending (x desc, index desc) by rank counting
+  if (t < n) {
+    const float xi = s.cx[t];
+    const int ii = s.ci[t];
+    int r = 0;
+    for (int j = 0; j < n; ++j) {
+      const float xj = s.cx[j];
+      const int ij = s.ci[j];
+      r += (xj > xi || (xj == xi && ij > ii)) ? 1 : 0;
+    }
+    s.sx[r] = xi;
+    s.si[r] = ii;
+  }
+  __syncthreads();
+  if (t < n) {
+    const float lp = __fsub_rn(s.sx[t], lse);
+    s.slp[t] = lp;
+    s.sp[t] = rexp(lp);
+  }
+  __syncthreads();
+  if (t == 0) {
+    // keep_p along the descending order; cx reused as flags
+    const bool use_p = a.top_p < 1.0f;
+    float U = 0.0f;
+    for (int q = 0; q < n; ++q) {
+      s.cx[q] = (!use_p || U < a.top_p) ? 1.0f : 0.0f;
+      U = __fadd_rn(U, s.sp[q]);
+    }
+    // tied elements occupy q in [greater, n), index descending; the lowest
+    // index with keep_p is the largest such q
+    int first = -1;
+    for (int q = n - 1; q >= greater; --q)
+      if (s.cx[q] != 0.0f) { first = q; break; }
+    const int allowed = a.top_k - greater;
+    s.keep_lo = first < 0 ? n : max(greater, first - allowed + 1);
+    s.keep_hi = first;  // tied kept: q in [keep_lo, keep_hi]
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int q = lane; q < n; q += 32) {
+      const bool keep = q < greater ? (s.cx[q] != 0.0f) : (q >= s.keep_lo && q <= s.keep_hi);
+      if (!keep) continue;
+      const int i = s.si[q];
+      const float z = __fadd_rn(__fmul_rn(s.slp[q], inv_t), gumbel(u[i]));
+      if (z > bv || (z == bv && i < bi)) { bv = z; bi = i; }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) a.ids[b] = bi;
+  }
+}
+
+}  // namespace rec

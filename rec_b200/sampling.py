@@ -1,0 +1,114 @@
+"""Sampling head on the GPU: penalties, temperature, top-k / top-p with
+injected uniforms (reference engine.py:279-301, masked_sampling.py:98-125,
+filtered_sampling.py:7-22, sampling.py:48-52).
+
+The uniforms are drawn on the device from torch's Philox generator, one per
+vocabulary entry per token (the Gumbel noise of the reference's categorical
+draw is -log(-log u)); passing the same uniforms to the oracle reproduces the
+ids bit for bit.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import abi
+from ._lib import check, lib
+
+
+def params(temperature=0.0, top_k=0, top_p=1.0, repetition_penalty=1.0, presence_penalty=0.0) -> abi.RecSampling:
+    return abi.RecSampling(float(temperature), int(top_k), float(top_p), float(repetition_penalty),
+                           float(presence_penalty))
+
+
+def uniforms(batch: int, vocab: int, seed: int, device) -> torch.Tensor:
+    """fp32 [batch, vocab] in [0, 1) from a seeded Philox stream on `device`."""
+    g = torch.Generator(device=device)
+    g.manual_seed(int(seed))
+    return torch.rand(batch, vocab, generator=g, device=device, dtype=torch.float32)
+
+
+def sample_logits(logits: torch.Tensor, p: abi.RecSampling, u: torch.Tensor | None = None,
+                  history: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """ids int32 [B] for bf16 logits [B, V] (or [V]); history int32 [B, n]
+    (or [n]); u fp32 [B, V] (required when temperature > 0)."""
+    if logits.dtype != torch.bfloat16 or not logits.is_cuda:
+        raise ValueError("logits must be a bf16 CUDA tensor")
+    lg = logits.reshape(1, -1) if logits.dim() == 1 else logits
+    B, V = lg.shape
+    if lg.stride(1) != 1:
+        raise ValueError("logits rows must be contiguous")
+    if history is not None:
+        history = history.reshape(B, -1) if history.dim() == 1 else history
+        history = history.to(torch.int32).contiguous()
+    if u is not None:
+        u = u.reshape(B, V).contiguous()
+        if u.dtype != torch.float32:
+            raise ValueError("uniforms must be float32")
+    ids = out if out is not None else torch.empty(B, dtype=torch.int32, device=lg.device)
+    stream = torch.cuda.current_stream().cuda_stream
+    check(lib().rec_sample_logits(C.c_void_p(lg.data_ptr()), B, V, lg.stride(0),
+                                  C.c_void_p(history.data_ptr()) if history is not None else None,
+                                  history.shape[1] if history is not None else 0, C.byref(p),
+                                  C.c_void_p(u.data_ptr()) if u is not None else None, C.c_void_p(ids.data_ptr()),
+                                  C.c_void_p(stream)), "rec_sample_logits")
+    return ids
+
+
+def sample_head(h: torch.Tensor, final_norm: torch.Tensor, lm_head, scale_dtype: torch.dtype, p: abi.RecSampling,
+                u: torch.Tensor | None = None, history: torch.Tensor | None = None, eps: float = 1e-6):
+    """Final RMSNorm + int4 lm_head GEMV + sampler for B hidden rows
+    Returns (ids int32 [B], logits bf16 [B, V])."""
+    from .ops import scale_dtype_code
+
+    hb = h.reshape(-1, h.shape[-1])
+    B, H = hb.shape
+    V = lm_head.w.shape[0]
+    logits = torch.empty(B, V, dtype=torch.bfloat16, device=h.device)
+    m = abi.RecQMat(lm_head.w.data_ptr(), lm_head.s.data_ptr(), lm_head.b.data_ptr())
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for b in range(B):
+        row = hb[b].contiguous()
+        check(lib().rec_gemv_int4(C.byref(m), scale_dtype_code(scale_dtype), V, H, C.c_void_p(row.data_ptr()),
+                                  C.c_void_p(final_norm.data_ptr()), float(eps), C.c_void_p(logits[b].data_ptr()),
+                                  stream), "rec_gemv_int4")
+    return sample_logits(logits, p, u, history), logits
+
+
+def sampled_block(engine, state, token, count, seed, *, temperature, top_p, top_k, presence_penalty, eos=()):
+    """ResidentSampler.block for temperature > 0: each step decodes on the
+    device, samples with the step's uniforms and feeds the id back.
+    state["presence_mask"] (float [V], the reference's key) marks the ids the
+    presence penalty applies to."""
+    sess = engine._session(state)
+    V = engine.weights.cfg.vocab
+    dev = sess.logits.device
+    p = params(temperature, top_k, top_p, 1.0, presence_penalty)
+    u = uniforms(count, V, seed, dev)
+    mask = state.get("presence_mask")
+    if presence_penalty and mask is None:
+        mask = torch.zeros(V, dtype=torch.float32, device=dev)
+        state["presence_mask"] = mask
+    ids = []
+    ids_dev = torch.empty(1, dtype=torch.int32, device=dev)
+    pos = state["position"]
+
+    def run():
+        tok = int(token)
+        for i in range(count):
+            logits, _ = sess.step(tok, pos + i)
+            hist = torch.nonzero(mask).to(torch.int32).reshape(-1) if presence_penalty else None
+            sample_logits(logits, p, u[i], hist, out=ids_dev)
+            tok = int(ids_dev.item())
+            if tok < 0:
+                raise RuntimeError("Invalid sampled chain")
+            ids.append(tok)
+            if presence_penalty:
+                mask[tok] = 1.0
+            if tok in eos:
+                break
+        sess.check_status()
+        return ids
+
+    return engine._guard(state, run)
