@@ -70,9 +70,15 @@ struct AttnBlock {
   uint16_t *g_ks, *g_kb, *g_vs, *g_vb;
 };
 
-template <int BITS, typename Sync>
+struct NoMark {
+  __device__ void operator()(int) const {}
+};
+
+// mark(i) is called by every warp after the query/append step (i = 0) and
+// after the tiles (i = 1): a hook for timeline stamps.
+template <int BITS, typename Sync, typename Mark = NoMark>
 __device__ __forceinline__ void attn_block(const AttnBlock& it, TileView tv, AttnScratch& sc, int warp, Sync sync,
-                                           Partial4& P) {
+                                           Partial4& P, Mark mark = Mark()) {
   constexpr int RW = 128 * BITS / 32;
   const int lane = threadIdx.x & 31;
   // --- queries (warps 4..7) and the new token's K/V (warps 0..3) --------------
@@ -124,6 +130,7 @@ __device__ __forceinline__ void attn_block(const AttnBlock& it, TileView tv, Att
     }
   }
   sync();
+  mark(0);
   // --- warp w: tile w ------------------------------------------------------------
   const int hq = it.hq;
   float m[kMaxHq], l[kMaxHq], acc[kMaxHq][4];
@@ -145,18 +152,38 @@ __device__ __forceinline__ void attn_block(const AttnBlock& it, TileView tv, Att
     __syncwarp();
     const int nt = min(kAttTile, it.n - base);
     const int grp = lane >> 4;
-    for (int t = 0; t < nt; ++t) {
-      const int tok = base + t;
+    // two tokens per iteration: every shared-memory load of the pair is
+    // issued before its multiply-adds; acc still adds tokens in order
+    auto vvals = [&](int tok, float (&v)[4]) {
       uint32_t c4;
       if constexpr (BITS == 4) c4 = reinterpret_cast<const uint16_t*>(tv.vc + tok * RW)[lane];
       else c4 = tv.vc[tok * RW + lane];
       const float vsc = bf(tv.vs[tok * 2 + grp]), vbi = bf(tv.vb[tok * 2 + grp]);
-      float v[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t c = BITS == 4 ? (c4 >> (4 * j)) & 15u : (c4 >> (8 * j)) & 255u;
         v[j] = __fmaf_rn(vsc, code_f(c), vbi);
       }
+    };
+    int t = 0;
+    for (; t + 2 <= nt; t += 2) {
+      float v[2][4];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) vvals(base + t + q, v[q]);
+#pragma unroll
+      for (int h = 0; h < kMaxHq; ++h) {
+        if (h >= hq) break;
+        const float2 p2 = *reinterpret_cast<const float2*>(&sc.p[warp][h][t]);
+        const float pq[2] = {p2.x, p2.y};
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[h][j] = __fmaf_rn(pq[q], v[q][j], acc[h][j]);
+      }
+    }
+    for (; t < nt; ++t) {
+      float v[4];
+      vvals(base + t, v);
 #pragma unroll
       for (int h = 0; h < kMaxHq; ++h) {
         if (h >= hq) break;
@@ -176,6 +203,7 @@ __device__ __forceinline__ void attn_block(const AttnBlock& it, TileView tv, Att
     *reinterpret_cast<float4*>(&sc.wacc[warp][h][4 * lane]) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
   }
   sync();
+  mark(1);
   // --- block partial: warps merged in order ----------------------------------
   P = empty_partial();
   if (warp < hq) {

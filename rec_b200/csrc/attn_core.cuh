@@ -193,7 +193,8 @@ __device__ __forceinline__ void tile_scores(const uint32_t* krow, bool valid, fl
   // different banks.
   constexpr int CHUNKS = BITS == 8 ? 8 : 4;
   const int rot = BITS == 8 ? lane : (lane >> 1);
-#pragma unroll
+  // not unrolled: this runs once per layer from a cold instruction cache
+#pragma unroll 1
   for (int j = 0; j < CHUNKS; ++j) {
     const int c = (j + rot) & (CHUNKS - 1);
     const uint4 kw = *reinterpret_cast<const uint4*>(krow + 4 * c);

@@ -162,7 +162,7 @@ __device__ __forceinline__ AttnPlan attn_plan(const MegaArgs& a, int pos) {
   AttnPlan p;
   p.T = pos + 1;
   p.nblk = (p.T + kAttBlock - 1) / kAttBlock;
-  p.hq = att_hq(a.hkv, p.nblk, gridDim.x / 2);  // at most one item per CTA while that is possible
+  p.hq = att_hq(a.hkv, p.nblk, gridDim.x);  // at most one item per CTA while that is possible
   p.nq = (a.hq / a.hkv) / p.hq;
   p.items = p.nblk * a.hkv * p.nq;
   return p;
@@ -336,6 +336,7 @@ struct Producer {
             const int n = min(kAttBlock, AP.T - b * kAttBlock);
             kv_chunk(L.k_codes, L.k_scales, L.k_biases, g, b, n);
             kv_chunk(L.v_codes, L.v_scales, L.v_biases, g, b, n);
+            stamp(a, step, l, 24);
           }
           // O rows
           for (int r = P.o0; r < P.o1 && ok; r += kORows) gemv_chunk(L.o, a.hq * 128, r, min(kORows, P.o1 - r));
@@ -593,7 +594,7 @@ struct Consumers {
   // then the last-arriver merges of super-chunk and head.
   template <int BITS>
   __device__ void attn_item_compute(const MegaLayer& L, const AttnPlan& P, int pos, int b, int g, int qsub,
-                                    uint8_t* kt, uint8_t* vt) {
+                                    uint8_t* kt, uint8_t* vt, int step_, int layer_) {
     constexpr int RW = 128 * BITS / 32;
     const int n = min(kAttBlock, P.T - b * kAttBlock), n4 = (n + 3) & ~3;
     TileView tv;
@@ -628,72 +629,77 @@ struct Consumers {
       ab.g_vb = L.v_biases + slot * 2;
     }
     Partial4 Pt;
-    attn_block<BITS>(ab, tv, sm.att, warp, ConsSync{}, Pt);
+    const MegaArgs& A = a;
+    const int w0 = warp;
+    attn_block<BITS>(ab, tv, sm.att, warp, ConsSync{}, Pt, [&](int i) {
+      if (w0 == 0 && lane == 0) stamp(A, step_, layer_, 16 + i);
+    });
+    if (warp == 0 && lane == 0) stamp(a, step_, layer_, 18);
     // the block partial and the last-arriver merges
     const int nblk_cap = a.capacity / kAttBlock;
     const int s = b / kAttSuper;
     const int n_super = (P.nblk + kAttSuper - 1) / kAttSuper;
     const int in_super = min(kAttSuper, P.nblk - s * kAttSuper);
     if (warp >= hq) return;
-    {
-      const int h = ab.h0 + warp;
-      store_partial(a.partials + (size_t(h) * nblk_cap + b) * kPartialFloats, Pt);
-      __threadfence();
-      unsigned prev = 0;
-      if (lane == 0) prev = atomicAdd(a.cnt + a.hq + h * a.n_super_max + s, 1u);
-      prev = __shfl_sync(0xffffffffu, prev, 0);
-      if (int(prev) != in_super - 1) return;
-      // this warp merges super-chunk s of head h
-      __threadfence();
-      Partial4 S;
-      S.m = -INFINITY;
-      S.l = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) S.a[j] = 0.0f;
-      for (int bb = s * kAttSuper; bb < s * kAttSuper + in_super; ++bb) {
-        const float* src = a.partials + (size_t(h) * nblk_cap + bb) * kPartialFloats;
-        Partial4 Q;
-        Q.m = __ldcg(src);
-        Q.l = __ldcg(src + 1);
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(src + 4) + lane);
-        Q.a[0] = v.x; Q.a[1] = v.y; Q.a[2] = v.z; Q.a[3] = v.w;
-        merge_into(S, Q);
-      }
-      if (lane == 0) a.cnt[a.hq + h * a.n_super_max + s] = 0;
-      float* sd = a.supers + (size_t(h) * a.n_super_max + s) * kPartialFloats;
-      if (lane == 0) {
-        sd[0] = S.m;
-        sd[1] = S.l;
-      }
-      *reinterpret_cast<float4*>(sd + 4 + 4 * lane) = make_float4(S.a[0], S.a[1], S.a[2], S.a[3]);
+    const int h = ab.h0 + warp;
+    store_partial(a.partials + (size_t(h) * nblk_cap + b) * kPartialFloats, Pt);
+    __threadfence();
+    unsigned prev = 0;
+    if (lane == 0) prev = atomicAdd(a.cnt + a.hq + h * a.n_super_max + s, 1u);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (int(prev) != in_super - 1) return;
+    // this warp merges super-chunk s of head h: its own block from registers,
+    // the others loaded in batches so that their L2 round trips overlap
+    __threadfence();
+    Partial4 S = empty_partial();
+    merge_range(S, a.partials + size_t(h) * nblk_cap * kPartialFloats, s * kAttSuper, s * kAttSuper + in_super, b,
+                Pt);
+    if (lane == 0) a.cnt[a.hq + h * a.n_super_max + s] = 0;
+    Partial4 F = empty_partial();
+    if (L.sinks) {
+      F.m = bf(L.sinks[h]);
+      F.l = 1.0f;
+    }
+    if (n_super == 1) {
+      merge_into(F, S);
+    } else {
+      store_partial(a.supers + (size_t(h) * a.n_super_max + s) * kPartialFloats, S);
       __threadfence();
       if (lane == 0) prev = atomicAdd(a.cnt + h, 1u);
       prev = __shfl_sync(0xffffffffu, prev, 0);
       if (int(prev) != n_super - 1) return;
       __threadfence();
-      Partial4 F;
-      F.m = -INFINITY;
-      F.l = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) F.a[j] = 0.0f;
-      if (L.sinks) {
-        F.m = bf(L.sinks[h]);
-        F.l = 1.0f;
-      }
-      for (int ss = 0; ss < n_super; ++ss) {
-        const float* src = a.supers + (size_t(h) * a.n_super_max + ss) * kPartialFloats;
-        Partial4 Q;
-        Q.m = __ldcg(src);
-        Q.l = __ldcg(src + 1);
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(src + 4) + lane);
-        Q.a[0] = v.x; Q.a[1] = v.y; Q.a[2] = v.z; Q.a[3] = v.w;
-        merge_into(F, Q);
-      }
-      uint2 o;
-      o.x = uint32_t(to_bf(__fdiv_rn(F.a[0], F.l))) | (uint32_t(to_bf(__fdiv_rn(F.a[1], F.l))) << 16);
-      o.y = uint32_t(to_bf(__fdiv_rn(F.a[2], F.l))) | (uint32_t(to_bf(__fdiv_rn(F.a[3], F.l))) << 16);
-      *reinterpret_cast<uint2*>(a.attn + h * 128 + 4 * lane) = o;
+      merge_range(F, a.supers + size_t(h) * a.n_super_max * kPartialFloats, 0, n_super, s, S);
       if (lane == 0) a.cnt[h] = 0;
+    }
+    uint2 o;
+    o.x = uint32_t(to_bf(__fdiv_rn(F.a[0], F.l))) | (uint32_t(to_bf(__fdiv_rn(F.a[1], F.l))) << 16);
+    o.y = uint32_t(to_bf(__fdiv_rn(F.a[2], F.l))) | (uint32_t(to_bf(__fdiv_rn(F.a[3], F.l))) << 16);
+    *reinterpret_cast<uint2*>(a.attn + h * 128 + 4 * lane) = o;
+  }
+
+  // Merges partials [i0, i1) of a [*, kPartialFloats] array into P in order;
+  // entry `own` is taken from registers.  Loads go out kBatch at a time.
+  __device__ void merge_range(Partial4& P, const float* base, int i0, int i1, int own, const Partial4& own_p) {
+    constexpr int kBatch = 2;
+    for (int i = i0; i < i1; i += kBatch) {
+      Partial4 Q[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int ii = i + j;
+        if (ii < i1 && ii != own) {
+          const float* src = base + size_t(ii) * kPartialFloats;
+          Q[j].m = __ldcg(src);
+          Q[j].l = __ldcg(src + 1);
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(src + 4) + lane);
+          Q[j].a[0] = v.x; Q[j].a[1] = v.y; Q[j].a[2] = v.z; Q[j].a[3] = v.w;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int ii = i + j;
+        if (ii < i1) merge_into(P, ii == own ? own_p : Q[j]);
+      }
     }
   }
 
@@ -834,7 +840,7 @@ struct Consumers {
           const int vslot = slot;
           --chunk;
           if (warp == 0 && lane == 0) stamp(a, step, l, 12);
-          attn_item_compute<BITS>(L, AP, pos, b, g, qsub, kt, vt);
+          attn_item_compute<BITS>(L, AP, pos, b, g, qsub, kt, vt, step, l);
           cons_sync();
           if (warp == 0 && lane == 0) stamp(a, step, l, 13);
           slot = kslot;
