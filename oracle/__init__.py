@@ -54,6 +54,9 @@ def lib() -> C.CDLL:
         L.orc_argmax_bf16.restype = C.c_int32
         L.orc_argmax_bf16.argtypes = [_u16p, C.c_int64]
         L.orc_partial_bytes.restype = C.c_int
+        L.orc_attention_supers.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                           C.c_void_p, C.c_int]
+        L.orc_attention_final.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
         L.orc_sample.restype = C.c_int32
         L.orc_sample.argtypes = [_u16p, C.c_int64, C.c_void_p, C.c_int, C.c_void_p, _f32p]
         L.orc_log.restype = C.c_float
@@ -210,3 +213,36 @@ def sample(logits_bf16, history, params, uniforms) -> int:
     u = np.ascontiguousarray(uniforms if uniforms is not None else np.zeros(lg.size), np.float32)
     assert isinstance(params, abi.RecSampling)
     return int(lib().orc_sample(lg, lg.size, h.ctypes.data if h.size else None, h.size, C.byref(params), u))
+
+
+PARTIAL_FLOATS = 130  # (m, l, acc[128]) of one head's attention partial
+
+
+def attention_supers(q_bf16, kv: dict, n_kv_heads: int, capacity: int, bits: int, T: int, n_super: int):
+    """Super-chunk partials float32 [Hq, n_super, 130] of tokens [0, T) of one
+    layer's cache (kv: codes / scales / biases arrays [Hkv, capacity, ...])."""
+    from rec_b200 import abi
+
+    q = np.ascontiguousarray(q_bf16, np.uint16)
+    hq = q.size // 128
+    arrs = [np.ascontiguousarray(kv[n]) for n in ("k_codes", "k_scales", "k_biases", "v_codes", "v_scales",
+                                                  "v_biases")]
+    rec = abi.RecKVLayer(*(a.ctypes.data for a in arrs))
+    out = np.zeros((hq, n_super, PARTIAL_FLOATS), np.float32)
+    L = lib()
+    assert L.orc_partial_bytes() == PARTIAL_FLOATS * 4
+    L.orc_attention_supers(q.ctypes.data, C.addressof(rec), hq, n_kv_heads, capacity, bits, T, out.ctypes.data,
+                           n_super)
+    return out
+
+
+def attention_final(supers, sinks_bf16=None):
+    """LSE merge of [Hq, n_super, 130] partials (after the optional sink) into
+    bf16 [Hq * 128]."""
+    sp = np.ascontiguousarray(supers, np.float32)
+    hq, n_super, _ = sp.shape
+    out = np.zeros(hq * 128, np.uint16)
+    sk = None if sinks_bf16 is None else np.ascontiguousarray(sinks_bf16, np.uint16)
+    lib().orc_attention_final(sp.ctypes.data, hq, n_super, None if sk is None else sk.ctypes.data,
+                              out.ctypes.data)
+    return out
