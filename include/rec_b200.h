@@ -148,6 +148,32 @@ REC_API int rec_decode_step(RecCtx* ctx, int32_t token, int32_t position, void* 
 REC_API int rec_decode_greedy(RecCtx* ctx, int32_t token, int32_t position, int32_t count,
                               const int32_t* eos, int32_t n_eos, int32_t* ids_dev,
                               int32_t* produced_dev, void* stream);
+/* ---- one session over several GPUs (one process per GPU) ----------------
+ * Expert parallelism + split-KV along the sequence: rank r holds experts
+ * [expert_lo, expert_hi) (its layer weights' gate/up/down hold only those,
+ * stacked in order) and the KV of super-chunks [super_lo, super_hi) (64
+ * blocks of 256 tokens each; its cache starts at token_base = super_lo *
+ * 16384 and rec_set_kv gets its local capacity).  Dense weights, embedding
+ * and lm_head are replicated.  The persistent kernel exchanges super-chunk
+ * attention partials and per-expert outputs between the ranks through peer
+ * stores into each rank's exchange buffer (NVLink), with bounded waits; the
+ * merges keep the single-GPU order, so every rank's logits equal the
+ * single-GPU ones bit for bit.  Replaces the reference's planned split-KV /
+ * expert-parallel partitioning (BASELINE configs 2 and 4); no reference
+ * counterpart in code.  Call order: rec_create, rec_set_shard,
+ * rec_set_weights, rec_set_kv, rec_exchange_bytes (allocate the exchange
+ * buffer as peer-mapped memory, zeroed, on every rank), rec_set_shard again
+ * with the peer pointers, rec_set_workspace. */
+typedef struct RecShard {
+  int32_t world, rank;
+  int32_t expert_lo, expert_hi;
+  int32_t super_lo, super_hi;
+  int32_t capacity_total;  /* global context capacity (positions), multiple of 256 */
+  void* exchange[8];       /* rank q's exchange buffer as mapped in this process */
+} RecShard;
+REC_API int rec_set_shard(RecCtx* ctx, const RecShard* shard);
+REC_API size_t rec_exchange_bytes(const RecCtx* ctx);
+
 /* Kernels of one step, in launch order; layer kernels repeat per layer. */
 enum {
   REC_K_EMBED = 0, REC_K_QKV = 1, REC_K_ATTN = 2, REC_K_COMBINE = 3, REC_K_OPROJ = 4, REC_K_ROUTER = 5,

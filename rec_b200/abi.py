@@ -88,3 +88,16 @@ class RecSampling(C.Structure):
         ("repetition_penalty", C.c_float),
         ("presence_penalty", C.c_float),
     ]
+
+
+class RecShard(C.Structure):
+    _fields_ = [
+        ("world", C.c_int32),
+        ("rank", C.c_int32),
+        ("expert_lo", C.c_int32),
+        ("expert_hi", C.c_int32),
+        ("super_lo", C.c_int32),
+        ("super_hi", C.c_int32),
+        ("capacity_total", C.c_int32),
+        ("exchange", C.c_void_p * 8),
+    ]

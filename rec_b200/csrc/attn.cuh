@@ -316,7 +316,7 @@ __global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnAr
     if (blockIdx.x == 0 && threadIdx.x == 0) report(a.status, kStatusBadPosition);
     return;
   }
-  const float* cs = a.rope + size_t(p - a.token_base) * 128;
+  const float* cs = a.rope + size_t(p) * 128;  // rows are absolute positions
   for (; it < items; it += gridDim.x) {
     int b, g, qsub;
     coords(it, b, g, qsub);

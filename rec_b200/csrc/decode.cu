@@ -140,6 +140,10 @@ struct RecCtx {
   int capacity = 0;
   int token_base = 0;       // split-KV: first position held by this rank
   int block_begin = 0, block_end = 1 << 30;
+  // one session over several GPUs (rec_set_shard)
+  int world = 1, rank = 0, e_lo = 0, e_hi = 0, super_lo = 0, super_hi = 0, cap_total = 0;
+  uint8_t* xch[kMaxWorld] = {};
+  unsigned layer_seq = 0;  // layer steps run so far (exchange parity)
   uint8_t* ws = nullptr;
   size_t ws_bytes = 0;
   bool usable = true;
@@ -167,6 +171,8 @@ struct RecCtx {
 
 namespace {
 
+constexpr int kSuperTokens = kAttBlock * kAttSuper;  // tokens per super-chunk
+
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct Layout {
@@ -178,6 +184,10 @@ enum Region {
   rCtl, rCounters, rMegaCnt, rH, rQkv, rAttn, rXn, rAct, rLogits, rTrace, rRouter, rIds, rWts, rCandV, rCandI,
   rPartials, rSupers, rMegaLayers, rRope, rCount
 };
+
+// Positions the RoPE table covers: the local cache, or the whole context when
+// the session is split over ranks (every rank rotates every query).
+int rope_rows(const RecCtx* c) { return c->world > 1 ? c->cap_total : c->capacity; }
 
 Layout layout_of(const RecCtx* c) {
   const RecModelDesc& d = c->d;
@@ -203,7 +213,7 @@ Layout layout_of(const RecCtx* c) {
   sz[rCandI] = size_t(grid) * 4;
   sz[rPartials] = size_t(d.n_q_heads) * nblk * kPartialFloats * 4;
   sz[rSupers] = size_t(d.n_q_heads) * nsup * kPartialFloats * 4;
-  sz[rRope] = size_t(c->capacity) * 128 * 4;
+  sz[rRope] = size_t(rope_rows(c)) * 128 * 4;
   Layout L;
   size_t o = 0;
   for (int i = 0; i < rCount; ++i) {
@@ -476,6 +486,44 @@ REC_API int rec_create(const RecModelDesc* desc, RecCtx** out) {
   return REC_OK;
 }
 
+REC_API int rec_set_shard(RecCtx* c, const RecShard* sh) {
+  REC_CHECK_ARG(c && sh, "rec_set_shard: null argument");
+  const RecShard& s = *sh;
+  REC_CHECK_ARG(s.world >= 1 && s.world <= kMaxWorld, "world size must be 1..%d", kMaxWorld);
+  REC_CHECK_ARG(s.rank >= 0 && s.rank < s.world, "rank outside the world");
+  REC_CHECK_ARG(c->grid <= kMaxGrid, "too many SMs for the exchange layout");
+  REC_CHECK_ARG(s.capacity_total > 0 && s.capacity_total % kAttBlock == 0,
+                "capacity_total must be a positive multiple of %d", kAttBlock);
+  const int n_super = (s.capacity_total + kSuperTokens - 1) / kSuperTokens;
+  REC_CHECK_ARG(s.super_lo >= 0 && s.super_lo <= s.super_hi && s.super_hi <= n_super, "bad super-chunk range");
+  REC_CHECK_ARG(s.expert_lo >= 0 && s.expert_lo < s.expert_hi && s.expert_hi <= c->d.n_experts, "bad expert range");
+  c->world = s.world;
+  c->rank = s.rank;
+  c->e_lo = s.expert_lo;
+  c->e_hi = s.expert_hi;
+  c->super_lo = s.super_lo;
+  c->super_hi = s.super_hi;
+  c->cap_total = s.capacity_total;
+  c->token_base = s.super_lo * kSuperTokens;
+  bool all = true;
+  for (int q = 0; q < kMaxWorld; ++q) {
+    c->xch[q] = q < s.world ? static_cast<uint8_t*>(s.exchange[q]) : nullptr;
+    if (q < s.world) all = all && c->xch[q] != nullptr;
+  }
+  for (int q = 0; q < s.world && all; ++q)
+    REC_CHECK_ARG((reinterpret_cast<uintptr_t>(c->xch[q]) & 255u) == 0, "exchange buffers must be 256-byte aligned");
+  c->layer_seq = 0;
+  c->ws = nullptr;  // the workspace layout depends on the split
+  c->ws_bytes = 0;
+  drop_graph(c);
+  return REC_OK;
+}
+
+REC_API size_t rec_exchange_bytes(const RecCtx* c) {
+  if (!c || c->world < 1 || c->cap_total <= 0) return 0;
+  return xch_layout(c->d.n_q_heads, (c->cap_total + kSuperTokens - 1) / kSuperTokens, c->d.hidden).total;
+}
+
 REC_API void rec_destroy(RecCtx* ctx) {
   if (!ctx) return;
   drop_graph(ctx);
@@ -585,11 +633,13 @@ REC_API int rec_set_workspace(RecCtx* c, void* ws, size_t bytes) {
       REC_CHECK_CUDA(cudaMemcpy(c->mega_layers, t.data(), t.size() * sizeof(MegaLayer), cudaMemcpyHostToDevice));
   }
   // RoPE table: cos/sin of pos * theta^(-i/64) in double, rounded to float
-  std::vector<float> cs(size_t(c->capacity) * 128);
-  for (int p = 0; p < c->capacity; ++p)
+  // (row p = absolute position p)
+  const int rows = rope_rows(c);
+  std::vector<float> cs(size_t(rows) * 128);
+  for (int p = 0; p < rows; ++p)
     for (int i = 0; i < 64; ++i) {
       const double inv = std::pow(double(c->d.rope_theta), -double(i) / 64.0);
-      const double ang = double(c->token_base + p) * inv;
+      const double ang = double(p) * inv;
       cs[size_t(p) * 128 + i] = float(std::cos(ang));
       cs[size_t(p) * 128 + 64 + i] = float(std::sin(ang));
     }
@@ -611,8 +661,19 @@ static int check_ready(RecCtx* c) {
   }
   const char* sched = std::getenv("REC_SCHEDULE");
   c->use_mega = !(sched && std::strcmp(sched, "graph") == 0);
+  if (c->world > 1) {
+    REC_CHECK_ARG(c->use_mega, "a session split over ranks runs on the persistent kernel only");
+    for (int q = 0; q < c->world; ++q)
+      if (!c->xch[q]) {
+        set_error("rec_set_shard: exchange buffer of rank %d not set", q);
+        return REC_ESTATE;
+      }
+  }
   return c->use_mega ? REC_OK : ensure_graph(c);
 }
+
+// Position limit of the session (global when split over ranks).
+static int position_limit(const RecCtx* c) { return c->world > 1 ? c->cap_total : c->token_base + c->capacity; }
 
 // One cooperative launch of the persistent kernel for `steps` tokens.
 template <int I, int BITS>
@@ -654,6 +715,16 @@ static cudaError_t launch_mega_t(RecCtx* c, int steps, cudaStream_t st) {
   A.cand_val = c->cand_val;
   A.cand_idx = c->cand_idx;
   A.steps = steps;
+  A.world = c->world;
+  A.rank = c->rank;
+  A.e_lo = c->world > 1 ? c->e_lo : 0;
+  A.e_hi = c->world > 1 ? c->e_hi : d.n_experts;
+  A.super_lo = c->world > 1 ? c->super_lo : 0;
+  A.super_hi = c->world > 1 ? c->super_hi : c->n_super_max;
+  A.token_base = c->token_base;
+  A.layer_seq0 = c->layer_seq;
+  A.xl = xch_layout(d.n_q_heads, c->world > 1 ? (c->cap_total + kSuperTokens - 1) / kSuperTokens : 1, d.hidden);
+  for (int q = 0; q < kMaxWorld; ++q) A.xch[q] = c->xch[q];
   const size_t need = size_t(steps) * (6 * d.n_layers + 1) * c->grid * 2;
   A.prof = (c->prof && c->prof_entries >= need) ? c->prof : nullptr;
   A.prof2 = c->prof2;
@@ -682,7 +753,9 @@ static cudaError_t launch_mega_t(RecCtx* c, int steps, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, A);
+  e = cudaLaunchKernelEx(&cfg, kern, A);
+  if (e == cudaSuccess) c->layer_seq += unsigned(steps) * unsigned(d.n_layers);
+  return e;
 }
 
 static cudaError_t launch_mega(RecCtx* c, int steps, cudaStream_t st) {
@@ -700,7 +773,7 @@ REC_API int rec_decode_step(RecCtx* c, int32_t token, int32_t position, void* lo
                             void* stream) {
   int rc = check_ready(c);
   if (rc) return rc;
-  if (position < c->token_base || position - c->token_base >= c->capacity) {
+  if (position < 0 || position >= position_limit(c)) {
     set_error("position %d outside the KV capacity", position);
     return REC_ELIMIT;
   }
@@ -725,7 +798,7 @@ REC_API int rec_decode_greedy(RecCtx* c, int32_t token, int32_t position, int32_
   REC_CHECK_ARG(count >= 1 && count <= kMaxPacket, "packet must contain between 1 and %d tokens", kMaxPacket);
   REC_CHECK_ARG(n_eos >= 0 && n_eos <= kMaxEos && (n_eos == 0 || eos), "between 0 and %d EOS ids", kMaxEos);
   REC_CHECK_ARG(token >= -1 && token < c->d.vocab, "token %d outside the vocabulary", token);
-  if (position < c->token_base || position + count - c->token_base > c->capacity) {
+  if (position < 0 || position + count > position_limit(c)) {
     set_error("Decode context limit exhausted");
     return REC_ELIMIT;
   }

@@ -61,6 +61,47 @@ struct MegaLayer {
   uint16_t* v_biases;
 };
 
+// Exchange buffer of one rank (identical layout on every rank); two copies
+// of everything, selected by the parity of the global layer-step counter.
+constexpr int kMaxWorld = 8;
+// Waits on other GPUs: ranks launch independently, so allow more host jitter
+// than for waits inside one GPU (still bounded: a few seconds).
+constexpr uint32_t kPeerSpinLimit = kSpinLimit * 8;
+constexpr int kMaxGrid = 1024;
+struct XchLayout {
+  size_t head_cnt;  // unsigned [2][Hq]: super-chunk partials received per head
+  size_t xcnt;      // unsigned [2][kMaxGrid]: expert-output contributions received per CTA
+  size_t supers;    // float [2][Hq][n_super][132]
+  size_t xd;        // bf16 [2][kMaxTopK][H]: per-slot expert outputs
+  size_t total;
+  int hq, n_super, H;
+};
+inline __host__ __device__ size_t xch_align(size_t x) { return (x + 255) / 256 * 256; }
+inline __host__ __device__ XchLayout xch_layout(int hq, int n_super, int H) {
+  XchLayout x;
+  x.hq = hq;
+  x.n_super = n_super;
+  x.H = H;
+  x.head_cnt = 0;
+  x.xcnt = xch_align(x.head_cnt + size_t(2) * hq * 4);
+  x.supers = xch_align(x.xcnt + size_t(2) * kMaxGrid * 4);
+  x.xd = xch_align(x.supers + size_t(2) * hq * n_super * kPartialFloats * 4);
+  x.total = xch_align(x.xd + size_t(2) * kMaxTopK * H * 2);
+  return x;
+}
+__device__ __forceinline__ unsigned* xch_head_cnt(uint8_t* b, const XchLayout& x, int par, int h) {
+  return reinterpret_cast<unsigned*>(b + x.head_cnt) + par * x.hq + h;
+}
+__device__ __forceinline__ unsigned* xch_xcnt(uint8_t* b, const XchLayout& x, int par, int cta) {
+  return reinterpret_cast<unsigned*>(b + x.xcnt) + par * kMaxGrid + cta;
+}
+__device__ __forceinline__ float* xch_super(uint8_t* b, const XchLayout& x, int par, int h, int s) {
+  return reinterpret_cast<float*>(b + x.supers) + ((size_t(par) * x.hq + h) * x.n_super + s) * kPartialFloats;
+}
+__device__ __forceinline__ uint16_t* xch_xd(uint8_t* b, const XchLayout& x, int par, int slot) {
+  return reinterpret_cast<uint16_t*>(b + x.xd) + (size_t(par) * kMaxTopK + slot) * x.H;
+}
+
 struct MegaArgs {
   const MegaLayer* layers;
   int n_layers, H, hq, hkv, E, k, I, V, kv_bits, router_mode, capacity, n_super_max;
@@ -76,6 +117,13 @@ struct MegaArgs {
   float *partials, *supers, *router_logits, *cand_val;
   int* cand_idx;
   int steps;
+  // one session over several GPUs (world > 1): experts [e_lo, e_hi) and
+  // super-chunks [super_lo, super_hi) are local; xch[q] is rank q's exchange
+  // buffer (peer-mapped), laid out by XchLayout
+  int world, rank, e_lo, e_hi, super_lo, super_hi, token_base;
+  unsigned layer_seq0;  // layer steps run before this launch (exchange parity)
+  XchLayout xl;
+  uint8_t* xch[kMaxWorld];
   unsigned long long* prof;  // optional: [barrier][cta] x (arrive, release) globaltimer stamps
   unsigned long long* prof2; // optional: [cta][32] stamps inside layer prof_layer of step 0
   int prof_layer;
@@ -102,6 +150,10 @@ struct MegaSmem {
   float route_c[kMaxExperts];
   int ids[kMaxTopK];
   float wts[kMaxTopK];
+  int loc[kMaxTopK];   // selection slots whose expert is local, in slot order
+  int lids[kMaxTopK];  // their local expert indices
+  int n_loc;
+  int xok;             // world > 1: the expert-output exchange completed
   float dsm[kMaxTopK][kDRowsMax];
   uint64_t full[kSlots], empty[kSlots];
   uint16_t hown[kDRowsMax];  // this CTA's rows of h (it owns them in embed, O and D)
@@ -156,21 +208,36 @@ __device__ __forceinline__ Part partition(const MegaArgs& a) {
 }
 
 struct AttnPlan {
-  int T, nblk, hq, nq, items;
+  int T, nblk, n_super;  // global: tokens, blocks, super-chunks
+  int b_lo, b_hi;        // this rank's blocks (global indices)
+  int hq, nq, items;
 };
 __device__ __forceinline__ AttnPlan attn_plan(const MegaArgs& a, int pos) {
   AttnPlan p;
   p.T = pos + 1;
   p.nblk = (p.T + kAttBlock - 1) / kAttBlock;
-  p.hq = att_hq(a.hkv, p.nblk, gridDim.x);  // at most one item per CTA while that is possible
+  p.n_super = (p.nblk + kAttSuper - 1) / kAttSuper;
+  p.b_lo = min(a.super_lo * kAttSuper, p.nblk);
+  p.b_hi = min(a.super_hi * kAttSuper, p.nblk);
+  const int nloc = p.b_hi - p.b_lo;
+  p.hq = att_hq(a.hkv, max(nloc, 1), gridDim.x);  // at most one item per CTA while that is possible
   p.nq = (a.hq / a.hkv) / p.hq;
-  p.items = p.nblk * a.hkv * p.nq;
+  p.items = nloc * a.hkv * p.nq;
   return p;
 }
 __device__ __forceinline__ void attn_coords(const AttnPlan& P, int hkv, int it, int& b, int& g, int& qsub) {
   qsub = it % P.nq;
   g = (it / P.nq) % hkv;
-  b = it / (P.nq * hkv);
+  b = P.b_lo + it / (P.nq * hkv);
+}
+// Parity of the global layer step: selects one of the two exchange copies.
+__device__ __forceinline__ int xch_parity(const MegaArgs& a, int step, int layer) {
+  return int((a.layer_seq0 + unsigned(step) * unsigned(a.n_layers) + unsigned(layer)) & 1u);
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void stamp(const MegaArgs& a, int step, int layer, int slot) {
@@ -301,7 +368,7 @@ struct Producer {
     if (!dst) return;
     const int rw = 128 * a.kv_bits / 32;
     const int n4 = (n + 3) & ~3;
-    const size_t s0 = size_t(g) * a.capacity + size_t(b) * kAttBlock;
+    const size_t s0 = size_t(g) * a.capacity + size_t(b - a.token_base / kAttBlock) * kAttBlock;
     const uint32_t cb = uint32_t(n4) * rw * 4, sbytes = uint32_t(n4) * 4;
     mbar_expect_tx(&sm.full[slot], cb + 2 * sbytes);
     bulk_g2s(dst, codes + s0 * rw, cb, &sm.full[slot]);
@@ -356,18 +423,24 @@ struct Producer {
         __syncwarp();
         if (lane == 0) stamp(a, step, l, 20);
         if (lane == 0 && ok) {
-          int ids[kMaxTopK];
-          for (int r = 0; r < a.k; ++r) ids[r] = sm.ids[r];
-          for (int u = P.g0; u < P.g1 && ok;) {
-            const int r = u / a.I, i0 = u % a.I;
-            const int n = min(min(kGPairs, P.g1 - u), a.I - i0);
-            pair_chunk(L, ids[r], i0, n);
-            stamp(a, step, l, 21 + min((u - P.g0) / kGPairs, 3));
+          // this rank's selected experts only (all of them when world == 1)
+          int lids[kMaxTopK];
+          const int nl = sm.n_loc;
+          for (int j = 0; j < nl; ++j) lids[j] = sm.lids[j];
+          int g0, g1;
+          split_range(nl * a.I / 2, gridDim.x, blockIdx.x, g0, g1);
+          g0 *= 2;
+          g1 *= 2;
+          for (int u = g0; u < g1 && ok;) {
+            const int j = u / a.I, i0 = u % a.I;
+            const int n = min(min(kGPairs, g1 - u), a.I - i0);
+            pair_chunk(L, lids[j], i0, n);
+            stamp(a, step, l, 21 + min((u - g0) / kGPairs, 3));
             u += n;
           }
           if (P.o1 > P.o0)
-            for (int r0 = 0; r0 < a.k && ok; r0 += kDExperts)
-              down_chunk(L, ids, r0, min(a.k, r0 + kDExperts), P.o0, P.o1 - P.o0);
+            for (int j0 = 0; j0 < nl && ok; j0 += kDExperts)
+              down_chunk(L, lids, j0, min(nl, j0 + kDExperts), P.o0, P.o1 - P.o0);
         }
         __syncwarp();
         ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -620,7 +693,7 @@ struct Consumers {
     ab.has_new = pos >= b * kAttBlock && pos < b * kAttBlock + n;
     ab.tnew = pos - b * kAttBlock;
     if (ab.has_new && qsub == 0) {
-      const size_t slot = size_t(g) * a.capacity + size_t(pos);
+      const size_t slot = size_t(g) * a.capacity + size_t(pos - a.token_base);
       ab.g_kcodes = L.k_codes + slot * RW;
       ab.g_vcodes = L.v_codes + slot * RW;
       ab.g_ks = L.k_scales + slot * 2;
@@ -637,24 +710,36 @@ struct Consumers {
     if (warp == 0 && lane == 0) stamp(a, step_, layer_, 18);
     // the block partial and the last-arriver merges
     const int nblk_cap = a.capacity / kAttBlock;
+    const int blk0 = a.token_base / kAttBlock;  // first block of this rank's cache
     const int s = b / kAttSuper;
-    const int n_super = (P.nblk + kAttSuper - 1) / kAttSuper;
+    const int n_super = P.n_super;
     const int in_super = min(kAttSuper, P.nblk - s * kAttSuper);
     if (warp >= hq) return;
     const int h = ab.h0 + warp;
-    store_partial(a.partials + (size_t(h) * nblk_cap + b) * kPartialFloats, Pt);
+    const float* hpart = a.partials + size_t(h) * nblk_cap * kPartialFloats;
+    store_partial(const_cast<float*>(hpart) + size_t(b - blk0) * kPartialFloats, Pt);
     __threadfence();
     unsigned prev = 0;
-    if (lane == 0) prev = atomicAdd(a.cnt + a.hq + h * a.n_super_max + s, 1u);
+    const int s_loc = s - a.super_lo;
+    if (lane == 0) prev = atomicAdd(a.cnt + a.hq + h * a.n_super_max + s_loc, 1u);
     prev = __shfl_sync(0xffffffffu, prev, 0);
     if (int(prev) != in_super - 1) return;
     // this warp merges super-chunk s of head h: its own block from registers,
     // the others loaded in batches so that their L2 round trips overlap
     __threadfence();
     Partial4 S = empty_partial();
-    merge_range(S, a.partials + size_t(h) * nblk_cap * kPartialFloats, s * kAttSuper, s * kAttSuper + in_super, b,
-                Pt);
-    if (lane == 0) a.cnt[a.hq + h * a.n_super_max + s] = 0;
+    merge_range(S, hpart, s * kAttSuper - blk0, s * kAttSuper + in_super - blk0, b - blk0, Pt);
+    if (lane == 0) a.cnt[a.hq + h * a.n_super_max + s_loc] = 0;
+    if (a.world > 1) {
+      // publish the super-chunk to every rank; each merges them itself
+      const int par = xch_parity(a, step_, layer_);
+      for (int q = 0; q < a.world; ++q) store_partial(xch_super(a.xch[q], a.xl, par, h, s), S);
+      __threadfence_system();
+      __syncwarp();
+      if (lane == 0)
+        for (int q = 0; q < a.world; ++q) atomicAdd_system(xch_head_cnt(a.xch[q], a.xl, par, h), 1u);
+      return;
+    }
     Partial4 F = empty_partial();
     if (L.sinks) {
       F.m = bf(L.sinks[h]);
@@ -672,10 +757,95 @@ struct Consumers {
       merge_range(F, a.supers + size_t(h) * a.n_super_max * kPartialFloats, 0, n_super, s, S);
       if (lane == 0) a.cnt[h] = 0;
     }
+    write_attn(h, F);
+  }
+
+  // world > 1: send this rank's expert slots of rows [o0, o1) to every other
+  // rank, then take the other ranks' slots from this rank's exchange buffer.
+  // All consumer warps call it; false when a bounded wait ran out.
+  __device__ bool exchange_down(const Part& P, int n, int par) {
+    const int t = threadIdx.x - 32, nt = kMegaCons * 32;
+    const int nl = sm.n_loc;
+    uint8_t* own = a.xch[a.rank];
+    for (int q = 0; q < a.world; ++q) {
+      if (q == a.rank) continue;
+      for (int idx = t; idx < nl * n; idx += nt) {
+        const int j = idx / n, i = idx - j * n;
+        const int rr = sm.loc[j];
+        xch_xd(a.xch[q], a.xl, par, rr)[P.o0 + i] = to_bf(sm.dsm[rr][i]);
+      }
+    }
+    __threadfence_system();
+    cons_sync();
+    if (t == 0) {
+      for (int q = 0; q < a.world; ++q)
+        if (q != a.rank) atomicAdd_system(xch_xcnt(a.xch[q], a.xl, par, blockIdx.x), 1u);
+      unsigned* c = xch_xcnt(own, a.xl, par, blockIdx.x);
+      bool ok = true;
+      uint32_t spins = 0;
+      while (ld_acquire_sys(c) < unsigned(a.world - 1)) {
+        if (aborted(a)) { ok = false; break; }
+        if (++spins > kPeerSpinLimit) {
+          set_abort(a, kStatusCounterTimeout);
+          ok = false;
+          break;
+        }
+      }
+      if (ok) *reinterpret_cast<volatile unsigned*>(c) = 0u;
+      sm.xok = ok ? 1 : 0;
+    }
+    cons_sync();
+    if (!sm.xok) return false;
+    for (int idx = t; idx < a.k * n; idx += nt) {
+      const int rr = idx / n, i = idx - rr * n;
+      bool mine = false;
+      for (int j = 0; j < nl; ++j) mine = mine || sm.loc[j] == rr;
+      if (!mine)
+        sm.dsm[rr][i] = bf(__ldcg(reinterpret_cast<const unsigned short*>(xch_xd(own, a.xl, par, rr) + P.o0 + i)));
+    }
+    cons_sync();
+    return true;
+  }
+
+  __device__ void write_attn(int h, const Partial4& F) {
     uint2 o;
     o.x = uint32_t(to_bf(__fdiv_rn(F.a[0], F.l))) | (uint32_t(to_bf(__fdiv_rn(F.a[1], F.l))) << 16);
     o.y = uint32_t(to_bf(__fdiv_rn(F.a[2], F.l))) | (uint32_t(to_bf(__fdiv_rn(F.a[3], F.l))) << 16);
     *reinterpret_cast<uint2*>(a.attn + h * 128 + 4 * lane) = o;
+  }
+
+  // world > 1: heads h = blockIdx.x (mod grid) wait for every rank's
+  // super-chunk partials of this layer, then merge them in order.  Warp 0.
+  __device__ bool attn_final_sharded(const MegaLayer& L, const AttnPlan& P, int par) {
+    for (int h = blockIdx.x; h < a.hq; h += gridDim.x) {
+      unsigned* cnt = xch_head_cnt(a.xch[a.rank], a.xl, par, h);
+      uint32_t spins = 0;
+      bool ok = true;
+      if (lane == 0) {
+        while (ld_acquire_sys(cnt) < unsigned(P.n_super)) {
+          if (aborted(a)) { ok = false; break; }
+          if (++spins > kPeerSpinLimit) {
+            set_abort(a, kStatusCounterTimeout);
+            ok = false;
+            break;
+          }
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) return false;
+      __syncwarp();
+      Partial4 F = empty_partial();
+      if (L.sinks) {
+        F.m = bf(L.sinks[h]);
+        F.l = 1.0f;
+      }
+      const Partial4 none = empty_partial();
+      merge_range(F, xch_super(a.xch[a.rank], a.xl, par, h, 0), 0, P.n_super, -1, none);
+      write_attn(h, F);
+      __syncwarp();
+      if (lane == 0) *reinterpret_cast<volatile unsigned*>(cnt) = 0u;
+    }
+    return true;
   }
 
   // Merges partials [i0, i1) of a [*, kPartialFloats] array into P in order;
@@ -775,6 +945,18 @@ struct Consumers {
       for (int r = 0; r < a.k; ++r) s2 = __fadd_rn(s2, __shfl_sync(0xffffffffu, pr, r));
       s2 = __fadd_rn(s2, 1e-20f);
       if (lane < a.k) sm.wts[lane] = __fdiv_rn(pr, s2);
+      if (lane == 0) {
+        int n = 0;
+        for (int r = 0; r < a.k; ++r) {
+          const int e = sm.ids[r];
+          if (e >= a.e_lo && e < a.e_hi) {
+            sm.loc[n] = r;
+            sm.lids[n] = e - a.e_lo;
+            ++n;
+          }
+        }
+        sm.n_loc = n;
+      }
     }
     cons_sync();
   }
@@ -848,6 +1030,7 @@ struct Consumers {
           slot = vslot;
           release(true);
         }
+        if (a.world > 1 && warp == 0) attn_final_sharded(L, AP, xch_parity(a, step, l));
         if (!grid_barrier(a, bar_index(a, step, l, 1))) return;
         // ---- O
         {
@@ -908,11 +1091,15 @@ struct Consumers {
         {
           GroupX gx[1];
           prep_lane_x<2048>(sm.xn, fr, 0, lane, gx);
-          for (int u = P.g0; u < P.g1;) {
-            const int r = u / a.I, i0 = u % a.I;
-            const int n = min(min(kGPairs, P.g1 - u), a.I - i0);
+          int g0, g1;
+          split_range(sm.n_loc * a.I / 2, gridDim.x, blockIdx.x, g0, g1);
+          g0 *= 2;
+          g1 *= 2;
+          for (int u = g0; u < g1;) {
+            const int r = sm.loc[u / a.I], i0 = u % a.I;
+            const int n = min(min(kGPairs, g1 - u), a.I - i0);
             const uint8_t* st = take();
-            if (warp == 0 && lane == 0) stamp(a, step, l, 2 + 2 * min((u - P.g0) / kGPairs, 3));
+            if (warp == 0 && lane == 0) stamp(a, step, l, 2 + 2 * min((u - g0) / kGPairs, 3));
             {
               const uint32_t wb = uint32_t(n) * 1024, sbytes = uint32_t(n) * 64;
               const uint16_t* sbase = reinterpret_cast<const uint16_t*>(st + 2 * wb);
@@ -937,7 +1124,7 @@ struct Consumers {
               }
             }
             release();
-            if (warp == 0 && lane == 0) stamp(a, step, l, 3 + 2 * min((u - P.g0) / kGPairs, 3));
+            if (warp == 0 && lane == 0) stamp(a, step, l, 3 + 2 * min((u - g0) / kGPairs, 3));
             u += n;
           }
         }
@@ -947,17 +1134,19 @@ struct Consumers {
         {
           load_vec(sm.act, a.act, a.k * I);
           const int n = P.o1 - P.o0;
+          const int nl = sm.n_loc;
           if (n > 0) {
-            for (int r0 = 0; r0 < a.k; r0 += kDExperts) {
-              const int r1 = min(a.k, r0 + kDExperts);
+            for (int j0 = 0; j0 < nl; j0 += kDExperts) {
+              const int j1 = min(nl, j0 + kDExperts);
               const uint8_t* st = take();
-              // warp w: expert r0 + (w % 4), rows of half (w / 4)
-              const int rr = r0 + (warp % kDExperts), half = warp / kDExperts;
-              if (rr < r1) {
+              // warp w: local expert j0 + (w % 4), rows of half (w / 4)
+              const int jj = j0 + (warp % kDExperts), half = warp / kDExperts;
+              if (jj < j1) {
                 using C = KCfg<I>;
+                const int rr = sm.loc[jj];
                 const uint32_t wb = uint32_t(n) * (I / 2), sbytes = uint32_t(n) * (I / 32);
                 const uint32_t per = wb + 2 * ((sbytes + 15) & ~15u);
-                const uint8_t* e0 = st + (rr - r0) * per;
+                const uint8_t* e0 = st + (jj - j0) * per;
                 const uint16_t* sbase = reinterpret_cast<const uint16_t*>(e0 + wb);
                 const uint16_t* bbase = reinterpret_cast<const uint16_t*>(e0 + wb + ((sbytes + 15) & ~15u));
                 const FixScale fd = fix_scale_from_max(warp_maxabs(sm.act + rr * I, I));
@@ -979,6 +1168,9 @@ struct Consumers {
               release();
             }
             cons_sync();
+          }
+          if (a.world > 1 && !exchange_down(P, n, xch_parity(a, step, l))) return;
+          if (n > 0) {
             for (int i = threadIdx.x - 32; i < n; i += kMegaCons * 32) {
               float mix = 0.0f;
               for (int r = 0; r < a.k; ++r) {

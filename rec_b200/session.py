@@ -6,25 +6,38 @@ import ctypes as C
 
 import torch
 
+from . import abi
 from ._lib import RecError, check, lib
 from .model import KVCache, ModelWeights
 
 
 class DecodeSession:
-    def __init__(self, weights: ModelWeights, kv: KVCache):
+    """One decode session; with `plan` (rec_b200.shard.ShardPlan) and a
+    process group it is this rank's part of a session split over the group's
+    GPUs: `weights` hold the plan's experts, `kv` its local capacity, and every
+    rank must make the same calls in the same order."""
+
+    def __init__(self, weights: ModelWeights, kv: KVCache, plan=None, group=None):
         self.weights = weights
         self.kv = kv
         self.cfg = weights.cfg
+        self.plan = plan
         self._desc = self.cfg.desc()
         handle = C.c_void_p()
         check(lib().rec_create(C.byref(self._desc), C.byref(handle)), "rec_create")
         self.ctx = handle
+        if plan is not None:
+            self._shard = abi.RecShard(plan.world, plan.rank, plan.expert_lo, plan.expert_hi, plan.super_lo,
+                                       plan.super_hi, plan.capacity)
+            check(lib().rec_set_shard(self.ctx, C.byref(self._shard)), "rec_set_shard")
         self._layers = weights.rec_layers()
         self._global = weights.rec_global()
         check(lib().rec_set_weights(self.ctx, self._layers, len(weights.layers), C.byref(self._global)),
               "rec_set_weights")
         self._kv = kv.rec()
         check(lib().rec_set_kv(self.ctx, self._kv, len(kv.layers), kv.capacity), "rec_set_kv")
+        if plan is not None:
+            self._setup_exchange(group)
         nbytes = lib().rec_workspace_bytes(self.ctx)
         self.workspace = torch.empty(nbytes + 256, dtype=torch.uint8, device=kv.layers[0]["k_codes"].device)
         base = self.workspace.data_ptr()
@@ -36,6 +49,31 @@ class DecodeSession:
         self.ids = torch.zeros(64, dtype=torch.int32, device=dev)
         self.produced = torch.zeros(1, dtype=torch.int32, device=dev)
         self.usable = True
+
+    def _setup_exchange(self, group):
+        """Peer-mapped exchange buffers (torch symmetric memory over the
+        group), zeroed on every rank before any launch."""
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        nbytes = int(lib().rec_exchange_bytes(self.ctx))
+        dev = self.kv.layers[0]["k_codes"].device
+        try:
+            symm.set_backend("CUDA")
+        except Exception:  # already chosen by an earlier allocation
+            pass
+        group = group if group is not None else dist.group.WORLD
+        self.exchange = symm.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.exchange.zero_()
+        torch.cuda.synchronize(dev)
+        self._symm = symm.rendezvous(self.exchange, group)
+        ptrs = list(self._symm.buffer_ptrs)
+        if len(ptrs) != self.plan.world:
+            raise RuntimeError("symmetric memory group size does not match the shard plan")
+        for q, p in enumerate(ptrs):
+            self._shard.exchange[q] = p
+        check(lib().rec_set_shard(self.ctx, C.byref(self._shard)), "rec_set_shard")
+        dist.barrier(group=group)
 
     def __del__(self):
         ctx = getattr(self, "ctx", None)
