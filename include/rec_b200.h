@@ -240,6 +240,18 @@ REC_API int rec_gemv_int4_argmax_noalloc(const RecQMat* w, int32_t scale_dtype, 
 REC_API int rec_sample_logits(const void* logits_dev, int32_t batch, int32_t vocab, int64_t stride,
                               const int32_t* history_dev, int32_t history_len, const RecSampling* params,
                               const float* uniforms_dev, int32_t* ids_dev, void* stream);
+/* Decode attention of one layer alone (unit tests, the attention sweep):
+ * quantizes the new K / V of `*position_dev` from qkv_dev (bf16 [Hq*128 |
+ * Hkv*128 | Hkv*128], RoPE from rope_dev [positions][cos 64 | sin 64]) into
+ * the cache, then attends q over positions [0, position] with optional sinks;
+ * out bf16 [Hq*128].  scratch_dev: rec_attn_scratch_bytes(Hq, capacity) bytes,
+ * 256-byte aligned.  Replaces quantized_attention_with_sinks + the KV write
+ * (model.py:45-82,108-139; megakernel.py:276-318,619-693). */
+REC_API size_t rec_attn_scratch_bytes(int32_t n_q_heads, int32_t capacity);
+REC_API int rec_attn_decode(const void* qkv_dev, int32_t n_q_heads, int32_t n_kv_heads, const RecKVLayer* kv,
+                            int32_t capacity, int32_t kv_bits, const float* rope_dev, const void* sinks_dev,
+                            const int32_t* position_dev, void* scratch_dev, size_t scratch_bytes, void* out_dev,
+                            int32_t* status_dev, void* stream);
 /* MLX affine quantization of fp32 groups into codes + (bf16|fp16) scale/bias. */
 REC_API int rec_quantize_affine(const float* w_dev, int64_t n_groups, int32_t bits,
                                 int32_t scale_dtype, void* codes_dev, void* scales_dev,

@@ -385,6 +385,9 @@ ORC_API void orc_kv_store(const RecKVLayer* kv, int Hkv, int C, int bits, int po
 #define ATT_BLOCK 256
 #define ATT_TILE 32
 #define ATT_SUPER 64 /* blocks per super-chunk */
+/* blocks per work item: 1 while the context fits one super-chunk, 4 beyond */
+static int att_item_blocks(int nblocks) { return nblocks <= ATT_SUPER ? 1 : 4; }
+#define ATT_WARPS 8  /* tiles of a block = warps of an item */
 #define NEG_INF (-INFINITY)
 
 typedef struct {
@@ -458,56 +461,100 @@ static float att_score(const QPrep* Q, const uint32_t* krow, const uint16_t* ks,
   return rbf(t * Q->down);
 }
 
-/* Partial of one q head over block b (tokens < T): tile w of 32 tokens is
- * one warp's (m = tile max, p = exp(s - m), l = butterfly sum of p,
- * acc = sum of p * v in token order); the tiles are merged in order. */
-static void att_block(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bits, int b, int T, Partial* out) {
+/* Tile partial of one q head over tokens [t0, t0+32) ∩ [0, T), in the
+ * kernels' fragment order (rec_b200/csrc/attn_core.cuh):
+ *   m = max score; p_j = exp(s_j - m) (0 beyond T);
+ *   l: v[gq] = (p[gq] + p[gq+8]) + (p[16+gq] + p[24+gq]), then a butterfly
+ *      over gq = 0..7 (offsets 4, 2, 1);
+ *   per V group (64 dims): w_j = p_j * scale_j; F = min(13 - exponent(max|w|),
+ *      100); wq_j = rint(w_j * 2^F); acc_int_d = sum_j wq_j * code_jd (exact);
+ *      B = sum of p_j * bias_j in the order of l; acc_d = fma(acc_int_d, 2^-F, B). */
+static void att_tile(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bits, int t0, int T, Partial* out) {
   int words = 128 * bits / 32;
   const uint32_t* KC = (const uint32_t*)kv->k_codes;
   const uint32_t* VC = (const uint32_t*)kv->v_codes;
   const uint16_t *KS = (const uint16_t*)kv->k_scales, *KB = (const uint16_t*)kv->k_biases;
   const uint16_t *VS = (const uint16_t*)kv->v_scales, *VB = (const uint16_t*)kv->v_biases;
-  p_empty(out);
-  for (int w = 0; w < ATT_BLOCK / ATT_TILE; ++w) {
-    int base = b * ATT_BLOCK + w * ATT_TILE;
-    if (base >= T) break;
-    Partial P;
-    float s[ATT_TILE], p[ATT_TILE];
-    float tmax = NEG_INF;
-    for (int t = 0; t < ATT_TILE; ++t) {
-      int tok = base + t;
-      if (tok < T) {
-        int64_t slot = (int64_t)g * C + tok;
-        s[t] = att_score(Q, KC + slot * words, KS + slot * 2, KB + slot * 2, bits);
-        tmax = s[t] > tmax ? s[t] : tmax;
-      }
+  int nvalid = T - t0;
+  if (nvalid > ATT_TILE) nvalid = ATT_TILE;
+  if (nvalid <= 0) {
+    p_empty(out);
+    return;
+  }
+  float s[ATT_TILE], p[ATT_TILE];
+  float m = NEG_INF;
+  for (int j = 0; j < nvalid; ++j) {
+    int64_t slot = (int64_t)g * C + t0 + j;
+    s[j] = att_score(Q, KC + slot * words, KS + slot * 2, KB + slot * 2, bits);
+    m = s[j] > m ? s[j] : m;
+  }
+  for (int j = 0; j < ATT_TILE; ++j) p[j] = j < nvalid ? rexp(s[j] - m) : 0.0f;
+  float v[8];
+  for (int q = 0; q < 8; ++q) v[q] = (p[q] + p[q + 8]) + (p[16 + q] + p[24 + q]);
+  bfly(v, 8);
+  out->m = m;
+  out->l = v[0];
+  for (int gr = 0; gr < 2; ++gr) {
+    float w[ATT_TILE], x[ATT_TILE];
+    float mx = 0.0f;
+    for (int j = 0; j < ATT_TILE; ++j) {
+      int64_t slot = (int64_t)g * C + t0 + j;
+      w[j] = j < nvalid ? p[j] * bf(VS[slot * 2 + gr]) : 0.0f;
+      x[j] = j < nvalid ? p[j] * bf(VB[slot * 2 + gr]) : 0.0f;
+      float a = fabsf(w[j]);
+      mx = a > mx ? a : mx;
     }
-    for (int t = 0; t < ATT_TILE; ++t) p[t] = (base + t < T) ? rexp(s[t] - tmax) : 0.0f;
-    float v[32];
-    memcpy(v, p, sizeof(v));
-    bfly(v, 32);
-    P.m = tmax;
-    P.l = v[0];
-    memset(P.acc, 0, sizeof(P.acc));
-    for (int t = 0; t < ATT_TILE; ++t) {
-      int tok = base + t;
-      if (tok >= T) break;
-      int64_t slot = (int64_t)g * C + tok;
-      const uint32_t* vrow = VC + slot * words;
-      for (int d = 0; d < 128; ++d) {
-        float val = fmaf(bf(VS[slot * 2 + d / 64]), (float)kv_code(vrow, bits, d), bf(VB[slot * 2 + d / 64]));
-        P.acc[d] = fmaf(p[t], val, P.acc[d]);
+    uint32_t u;
+    memcpy(&u, &mx, 4);
+    int E = (int)((u >> 23) & 0xFF) - 127;
+    int F = 13 - E;
+    if (F > 100) F = 100;
+    float up = ldexpf(1.0f, F), down = ldexpf(1.0f, -F);
+    int32_t wq[ATT_TILE];
+    for (int j = 0; j < ATT_TILE; ++j) wq[j] = (int32_t)rintf(w[j] * up);
+    for (int q = 0; q < 8; ++q) v[q] = (x[q] + x[q + 8]) + (x[16 + q] + x[24 + q]);
+    bfly(v, 8);
+    const float B = v[0];
+    for (int d = 64 * gr; d < 64 * gr + 64; ++d) {
+      int32_t acc = 0;
+      for (int j = 0; j < nvalid; ++j) {
+        int64_t slot = (int64_t)g * C + t0 + j;
+        acc += wq[j] * (int32_t)kv_code(VC + slot * words, bits, d);
       }
+      out->acc[d] = fmaf((float)acc, down, B);
     }
-    p_merge(out, &P);
   }
 }
 
-/* Super-chunk partials of every q head: supers[h * n_super + s].  Tokens
- * [0, T) of one layer's cache. */
+/* Partial of one q head over item it (blocks [nbi*it, nbi*it+nbi) ∩ blocks < T):
+ * warp w folds tiles 8b + w of the item's blocks in order; the eight warp
+ * states are folded as a tree ((w0 w1)(w2 w3))((w4 w5)(w6 w7)). */
+static void att_item(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bits, int it, int T, Partial* out) {
+  const int nbi = att_item_blocks((T + ATT_BLOCK - 1) / ATT_BLOCK);
+  Partial st[ATT_WARPS];
+  for (int w = 0; w < ATT_WARPS; ++w) {
+    p_empty(&st[w]);
+    for (int b = it * nbi; b < (it + 1) * nbi; ++b) {
+      int t0 = b * ATT_BLOCK + w * ATT_TILE;
+      if (t0 >= T) break;
+      Partial P;
+      att_tile(Q, kv, g, C, bits, t0, T, &P);
+      p_merge(&st[w], &P);
+    }
+  }
+  for (int step = 1; step < ATT_WARPS; step *= 2)
+    for (int w = 0; w < ATT_WARPS; w += 2 * step) p_merge(&st[w], &st[w + step]);
+  *out = st[0];
+}
+
+/* Super-chunk partials of every q head: supers[h * n_super + s] = items of
+ * super s (64 blocks) merged in order.  Tokens [0, T) of one
+ * layer's cache. */
 ORC_API void orc_attention_supers(const uint16_t* q, const RecKVLayer* kv, int Hq, int Hkv, int C,
                                   int bits, int T, Partial* supers, int n_super) {
   int nblocks = (T + ATT_BLOCK - 1) / ATT_BLOCK;
+  int nbi = att_item_blocks(nblocks), per_super = ATT_SUPER / nbi;
+  int nitems = (nblocks + nbi - 1) / nbi;
 #pragma omp parallel for schedule(dynamic)
   for (int h = 0; h < Hq; ++h) {
     QPrep Q;
@@ -516,9 +563,9 @@ ORC_API void orc_attention_supers(const uint16_t* q, const RecKVLayer* kv, int H
     for (int s = 0; s < n_super; ++s) {
       Partial* S = &supers[h * n_super + s];
       p_empty(S);
-      for (int b = s * ATT_SUPER; b < (s + 1) * ATT_SUPER && b < nblocks; ++b) {
+      for (int it = s * per_super; it < (s + 1) * per_super && it < nitems; ++it) {
         Partial P;
-        att_block(&Q, kv, g, C, bits, b, T, &P);
+        att_item(&Q, kv, g, C, bits, it, T, &P);
         p_merge(S, &P);
       }
     }

@@ -1,6 +1,12 @@
-// GQA decode attention over the quantized KV cache: split-KV block partials
+// GQA decode attention over the quantized KV cache: split-KV item partials
 // with fused RoPE / quantize-on-append, and the log-sum-exp combine.  The
-// math and its canonical order are in attn_core.cuh.
+// tile math and its canonical order are in attn_core.cuh.
+//
+// Work item = (kv head g, item_blocks(nblk) consecutive blocks of 256
+// tokens: 1 up to one super-chunk of context, 4 beyond) for all 8 q heads of g.  Warp w folds tile w (32 tokens) of each of the item's blocks
+// into a running state; the 8 warp states are folded as a tree
+// ((w0 w1)(w2 w3))((w4 w5)(w6 w7)); super-chunks (64 blocks) fold
+// their items in order; the output folds [sink] and the super-chunks in order.
 //
 // Reference: engine/src/rec_mlx/model.py:45-82 (quantize-on-append),
 // model.py:108-139 (scores, sink, softmax), megakernel.py:619-693 (split-KV
@@ -9,6 +15,13 @@
 #include "attn_core.cuh"
 
 namespace rec {
+
+constexpr int kHeadsPerKv = 8;                          // q heads per kv head
+
+// Blocks per work item: 1 while the context fits one super-chunk (short
+// contexts want many small items), 4 beyond (fewer per-item overheads).
+__host__ __device__ inline int item_blocks(int nblk) { return nblk <= kAttSuper ? 1 : 4; }
+__host__ __device__ inline int super_items(int nblk) { return kAttSuper / item_blocks(nblk); }
 
 struct AttnArgs {
   const uint16_t* qkv;     // bf16 [Hq*128 | Hkv*128 | Hkv*128] pre-RoPE projections
@@ -20,224 +33,188 @@ struct AttnArgs {
   uint16_t* v_biases;
   int capacity;            // C, multiple of 256
   int hq, hkv;
-  const float* rope;       // [C, 128] cos | sin
+  const float* rope;       // [positions, 128] cos | sin, row = absolute position
   const uint16_t* q_norm;  // bf16 [128] or null
   const uint16_t* k_norm;
   float eps;
   const int* position;     // device position p; T = p + 1
-  int token_base;          // first global position stored in this cache (split-KV ranks)
-  int block_begin, block_end;  // global block range this rank computes (split-KV)
-  float* partials;         // [Hq, capacity/256, 132]
+  float* partials;         // [Hq, n_items_cap, 132]
   float* supers;           // [Hq, n_super_max, 132]
   unsigned* head_counters; // [Hq]
   uint16_t* out;           // bf16 [Hq*128]
   const uint16_t* sinks;   // bf16 [Hq] or null
   int n_super_max;
-  int final_merge;         // 1: combine also merges super-chunks into out
   int* status;
   int pdl;
 };
 
-// Shared-memory scratch of one attention item (hq <= kMaxHq heads).
+// Item partial slots per head: one per block covers every item size.
+__host__ __device__ inline int items_cap(int capacity) { return capacity / kAttBlock; }
+
+// Shared-memory scratch of the attention items of one CTA.
 struct AttnScratch {
-  QHead qh[kMaxHq];
-  alignas(16) float p[kAttWarps][kMaxHq][kAttTile];
-  alignas(16) float wacc[kAttWarps][kMaxHq][128];
-  float wm[kAttWarps][kMaxHq], wl[kAttWarps][kMaxHq];
+  QHead qh[kHeadsPerKv];
+  union {
+    uint8_t wbuf[kAttWarps][1024];         // per-warp fixed-point PV weights
+    float tree[kAttWarps / 2][36][32];     // warp states during the tree fold
+  } u;
+  uint32_t kpatch[32], vpatch[32];         // quantized K / V row of the new token
+  uint16_t kps[2], kpb[2], vps[2], vpb[2];
+  int qg;                                  // kv head whose queries are in qh (-1: none)
 };
 
-// Tile of one (block, kv head): codes then scales then biases for K and V,
-// rows padded to a multiple of 4 tokens.
-struct TileView {
-  uint32_t *kc, *vc;
-  uint16_t *ks, *kb, *vs, *vb;
-};
+// Queries of the 8 heads of kv head g: warp w prepares head 8g + w.
+template <int BITS>
+__device__ __forceinline__ void prep_q_heads(const uint16_t* qkv, int g, const float* cs, const uint16_t* q_norm,
+                                             float eps, AttnScratch& sc, int warp) {
+  const int lane = threadIdx.x & 31;
+  const uint16_t* qr = qkv + (g * kHeadsPerKv + warp) * 128;
+  float x[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) x[j] = bf(__ldcg(reinterpret_cast<const unsigned short*>(qr + 4 * lane + j)));
+  if (q_norm) head_norm4(x, q_norm, eps);
+  float* scratch = reinterpret_cast<float*>(sc.u.wbuf[warp]);
+  rope4(x, cs, scratch);
+  prep_qhead<BITS>(x, sc.qh[warp], scratch);
+  __syncwarp();
+}
 
-// One work item: one block (n tokens) of kv head g for q heads [h0, h0+hq).
-// Called by all kAttWarps warps of a group (ids warp 0..7, synchronised by
-// `sync`); warp h < hq returns the block partial of head h0 + h.
-struct AttnBlock {
-  const uint16_t* qkv;
-  int hq_total, hkv;
-  int g, h0, hq, n;
-  const float* cs;              // cos/sin row of pos
-  const uint16_t *q_norm, *k_norm;
-  float eps;
-  bool has_new;                 // the block holds position pos
-  int tnew;                     // its row in the tile
-  uint32_t* g_kcodes;           // non-null: publish the new token here (row slot)
-  uint32_t* g_vcodes;
-  uint16_t *g_ks, *g_kb, *g_vs, *g_vb;
-};
+// The new token's K and V of kv head g, RoPE'd (K) and quantized into the
+// patch rows; warps 0,1 = K groups, 2,3 = V groups.  With g_* non-null the
+// rows are also stored into the cache.
+template <int BITS>
+__device__ __forceinline__ void prep_new_kv(const uint16_t* qkv, int hq_total, int hkv, int g, const float* cs,
+                                            const uint16_t* k_norm, float eps, AttnScratch& sc, int warp,
+                                            uint32_t* g_kc, uint32_t* g_vc, uint16_t* g_ks, uint16_t* g_kb,
+                                            uint16_t* g_vs, uint16_t* g_vb) {
+  if (warp >= 4) return;
+  const int lane = threadIdx.x & 31;
+  const bool is_k = warp < 2;
+  const int grp = warp & 1;
+  const uint16_t* src = qkv + (hq_total + (is_k ? 0 : hkv) + g) * 128;
+  float kv4[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) kv4[j] = bf(__ldcg(reinterpret_cast<const unsigned short*>(src + 4 * lane + j)));
+  float* tmp = reinterpret_cast<float*>(sc.u.wbuf[warp]);
+  if (is_k) {
+    if (k_norm) head_norm4(kv4, k_norm, eps);
+    rope4(kv4, cs, tmp);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) tmp[4 * lane + j] = kv4[j];
+  __syncwarp();
+  const float v0 = tmp[64 * grp + 2 * lane], v1 = tmp[64 * grp + 2 * lane + 1];
+  const QGroupParams qp = warp_group_params(v0, v1, BITS);
+  const uint32_t word = warp_pack(quant_code(v0, qp, BITS), quant_code(v1, qp, BITS), BITS);
+  constexpr int GW = 64 * BITS / 32;
+  uint32_t* prow = (is_k ? sc.kpatch : sc.vpatch) + grp * GW;
+  if (lane < GW) prow[lane] = word;
+  const uint16_t scb = to_bf(qp.scale), bib = to_bf(qp.bias);
+  if (lane == 0) {
+    (is_k ? sc.kps : sc.vps)[grp] = scb;
+    (is_k ? sc.kpb : sc.vpb)[grp] = bib;
+  }
+  if (g_kc) {
+    uint32_t* gc = (is_k ? g_kc : g_vc) + grp * GW;
+    if (lane < GW) gc[lane] = word;
+    if (lane == 0) {
+      (is_k ? g_ks : g_vs)[grp] = scb;
+      (is_k ? g_kb : g_vb)[grp] = bib;
+    }
+  }
+  __syncwarp();
+}
 
-struct NoMark {
-  __device__ void operator()(int) const {}
-};
-
-// mark(i) is called by every warp after the query/append step (i = 0) and
-// after the tiles (i = 1): a hook for timeline stamps.
-template <int BITS, typename Sync, typename Mark = NoMark>
-__device__ __forceinline__ void attn_block(const AttnBlock& it, TileView tv, AttnScratch& sc, int warp, Sync sync,
-                                           Partial4& P, Mark mark = Mark()) {
+// One warp copies the patch rows into row `row` of a K / V tile pair.
+template <int BITS>
+__device__ __forceinline__ void patch_row(uint32_t* kc, uint16_t* ks, uint16_t* kb, uint32_t* vc, uint16_t* vs,
+                                          uint16_t* vb, int row, const AttnScratch& sc) {
   constexpr int RW = 128 * BITS / 32;
   const int lane = threadIdx.x & 31;
-  // --- queries (warps 4..7) and the new token's K/V (warps 0..3) --------------
-  if (warp >= 4) {
-    const int hh = warp - 4;
-    if (hh < it.hq) {
-      const uint16_t* qr = it.qkv + (it.h0 + hh) * 128;
-      float x[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) x[j] = bf(__ldcg(reinterpret_cast<const unsigned short*>(qr + 4 * lane + j)));
-      if (it.q_norm) head_norm4(x, it.q_norm, it.eps);
-      float* scratch = sc.wacc[warp][0];
-      rope4(x, it.cs, scratch);
-      prep_qhead<BITS>(x, sc.qh[hh], scratch);
-    }
-  } else if (it.has_new) {
-    const bool is_k = warp < 2;
-    const int grp = warp & 1;
-    const uint16_t* src = it.qkv + (it.hq_total + (is_k ? 0 : it.hkv) + it.g) * 128;
-    float kv4[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) kv4[j] = bf(__ldcg(reinterpret_cast<const unsigned short*>(src + 4 * lane + j)));
-    float* tmp = sc.wacc[warp][0];
-    if (is_k) {
-      if (it.k_norm) head_norm4(kv4, it.k_norm, it.eps);
-      rope4(kv4, it.cs, tmp);
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) tmp[4 * lane + j] = kv4[j];
-    __syncwarp();
-    const float v0 = tmp[64 * grp + 2 * lane], v1 = tmp[64 * grp + 2 * lane + 1];
-    const QGroupParams qp = warp_group_params(v0, v1, BITS);
-    const uint32_t word = warp_pack(quant_code(v0, qp, BITS), quant_code(v1, qp, BITS), BITS);
-    constexpr int GW = 64 * BITS / 32;
-    uint32_t* crow = (is_k ? tv.kc : tv.vc) + it.tnew * RW + grp * GW;
-    if (lane < GW) crow[lane] = word;
-    const uint16_t scb = to_bf(qp.scale), bib = to_bf(qp.bias);
-    if (lane == 0) {
-      (is_k ? tv.ks : tv.vs)[it.tnew * 2 + grp] = scb;
-      (is_k ? tv.kb : tv.vb)[it.tnew * 2 + grp] = bib;
-    }
-    if (it.g_kcodes) {
-      uint32_t* gc = (is_k ? it.g_kcodes : it.g_vcodes) + grp * GW;
-      if (lane < GW) gc[lane] = word;
-      if (lane == 0) {
-        (is_k ? it.g_ks : it.g_vs)[grp] = scb;
-        (is_k ? it.g_kb : it.g_vb)[grp] = bib;
-      }
-    }
+  if (lane < RW) {
+    kc[row * RW + lane] = sc.kpatch[lane];
+    vc[row * RW + lane] = sc.vpatch[lane];
   }
-  sync();
-  mark(0);
-  // --- warp w: tile w ------------------------------------------------------------
-  const int hq = it.hq;
-  float m[kMaxHq], l[kMaxHq], acc[kMaxHq][4];
-#pragma unroll
-  for (int h = 0; h < kMaxHq; ++h) {
-    m[h] = -INFINITY;
-    l[h] = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[h][j] = 0.0f;
+  if (lane < 2) {
+    ks[row * 2 + lane] = sc.kps[lane];
+    kb[row * 2 + lane] = sc.kpb[lane];
+    vs[row * 2 + lane] = sc.vps[lane];
+    vb[row * 2 + lane] = sc.vpb[lane];
   }
-  const int base = warp * kAttTile;
-  if (base < it.n) {
-    const int tl = base + lane;
-    const bool valid = tl < it.n;
-    const int row = valid ? tl : base;
-    const float s0 = bf(tv.ks[row * 2]), s1 = bf(tv.ks[row * 2 + 1]);
-    const float b0 = bf(tv.kb[row * 2]), b1 = bf(tv.kb[row * 2 + 1]);
-    tile_scores<BITS>(tv.kc + row * RW, valid, s0, b0, s1, b1, sc.qh, hq, m, l, sc.p[warp]);
-    __syncwarp();
-    const int nt = min(kAttTile, it.n - base);
-    const int grp = lane >> 4;
-    // two tokens per iteration: every shared-memory load of the pair is
-    // issued before its multiply-adds; acc still adds tokens in order
-    auto vvals = [&](int tok, float (&v)[4]) {
-      uint32_t c4;
-      if constexpr (BITS == 4) c4 = reinterpret_cast<const uint16_t*>(tv.vc + tok * RW)[lane];
-      else c4 = tv.vc[tok * RW + lane];
-      const float vsc = bf(tv.vs[tok * 2 + grp]), vbi = bf(tv.vb[tok * 2 + grp]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t c = BITS == 4 ? (c4 >> (4 * j)) & 15u : (c4 >> (8 * j)) & 255u;
-        v[j] = __fmaf_rn(vsc, code_f(c), vbi);
-      }
-    };
-    int t = 0;
-    for (; t + 2 <= nt; t += 2) {
-      float v[2][4];
-#pragma unroll
-      for (int q = 0; q < 2; ++q) vvals(base + t + q, v[q]);
-#pragma unroll
-      for (int h = 0; h < kMaxHq; ++h) {
-        if (h >= hq) break;
-        const float2 p2 = *reinterpret_cast<const float2*>(&sc.p[warp][h][t]);
-        const float pq[2] = {p2.x, p2.y};
-#pragma unroll
-        for (int q = 0; q < 2; ++q)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) acc[h][j] = __fmaf_rn(pq[q], v[q][j], acc[h][j]);
-      }
-    }
-    for (; t < nt; ++t) {
-      float v[4];
-      vvals(base + t, v);
-#pragma unroll
-      for (int h = 0; h < kMaxHq; ++h) {
-        if (h >= hq) break;
-        const float pp = sc.p[warp][h][t];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[h][j] = __fmaf_rn(pp, v[j], acc[h][j]);
-      }
-    }
-  }
-#pragma unroll
-  for (int h = 0; h < kMaxHq; ++h) {
-    if (h >= hq) break;
-    if (lane == 0) {
-      sc.wm[warp][h] = m[h];
-      sc.wl[warp][h] = l[h];
-    }
-    *reinterpret_cast<float4*>(&sc.wacc[warp][h][4 * lane]) = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
-  }
-  sync();
-  mark(1);
-  // --- block partial: warps merged in order ----------------------------------
-  P = empty_partial();
-  if (warp < hq) {
-    const int h = warp;
-    for (int w = 0; w < kAttWarps; ++w) {
-      Partial4 Q;
-      Q.m = sc.wm[w][h];
-      Q.l = sc.wl[w][h];
-      const float4 a4 = *reinterpret_cast<const float4*>(&sc.wacc[w][h][4 * lane]);
-      Q.a[0] = a4.x; Q.a[1] = a4.y; Q.a[2] = a4.z; Q.a[3] = a4.w;
-      if (w * kAttTile >= it.n) Q = empty_partial();
-      merge_into(P, Q);
-    }
-  }
+  __syncwarp();
 }
 
-__device__ __forceinline__ void store_partial(float* dst, const Partial4& P) {
+// Tree fold of the 8 warp states; warp 0 ends with the item state.  All
+// warps call it (sync: a barrier over the 8 warps) after a barrier that ends
+// every warp's tiles: the tree scratch overlays the per-warp PV buffers.
+template <typename Sync>
+__device__ __forceinline__ void warps_fold(WarpState& st, int warp, AttnScratch& sc, Sync sync) {
   const int lane = threadIdx.x & 31;
-  if (lane == 0) {
-    dst[0] = P.m;
-    dst[1] = P.l;
+  for (int step = 1; step < kAttWarps; step *= 2) {
+    if ((warp & (2 * step - 1)) == step) {
+      float(*d)[32] = sc.u.tree[warp / (2 * step)];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        d[hh][lane] = st.m[hh];
+        d[2 + hh][lane] = st.l[hh];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) d[4 + 16 * hh + i][lane] = st.acc[hh][i];
+      }
+    }
+    sync();
+    if ((warp & (2 * step - 1)) == 0) {
+      const float(*d)[32] = sc.u.tree[warp / (2 * step)];
+      WarpState y;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        y.m[hh] = d[hh][lane];
+        y.l[hh] = d[2 + hh][lane];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) y.acc[hh][i] = d[4 + 16 * hh + i][lane];
+      }
+      state_merge(st, y);
+    }
+    sync();
   }
-  *reinterpret_cast<float4*>(dst + 4 + 4 * lane) = make_float4(P.a[0], P.a[1], P.a[2], P.a[3]);
 }
 
-__device__ __forceinline__ int att_hq(int hkv, int nblk, int slots) {
-  // q heads per work item: as few as possible while the items fit `slots`
-  int hq = 1;
-  while (hq < kMaxHq && hkv * (8 / hq) * nblk > slots) hq *= 2;
-  return hq;
-}
-
+// Warp 0: the item state of heads h0 .. h0+7 into dst + head * head_stride
+// (m, l, pad, pad, acc[128]).
 template <int BITS>
-struct AttnSmem {
+__device__ __forceinline__ void store_item(const WarpState& st, float* dst, size_t head_stride) {
+  const int lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    float* d = dst + size_t(2 * tq + hh) * head_stride;
+    if (gq == 0) {
+      d[0] = st.m[hh];
+      d[1] = st.l[hh];
+    }
+#pragma unroll
+    for (int li = 0; li < 16; ++li) d[4 + dim_of<BITS>(li, gq)] = st.acc[hh][li];
+  }
+}
+
+// This warp's tile (tile `warp`) of one block held in the given K / V tiles
+// (n tokens of the block valid; new_row >= 0: that row is the new token).
+template <int BITS>
+__device__ __forceinline__ void block_tiles(uint32_t* kc, uint16_t* ks, uint16_t* kb, uint32_t* vc, uint16_t* vs,
+                                            uint16_t* vb, int n, int new_row, const AttnScratch& sc, uint8_t* wbuf,
+                                            int warp, WarpState& st) {
+  constexpr int RW = 128 * BITS / 32;
+  const int t0 = warp * kAttTile;
+  const int nvalid = min(kAttTile, n - t0);
+  if (nvalid <= 0) return;
+  if (new_row >= t0 && new_row < t0 + kAttTile) patch_row<BITS>(kc, ks, kb, vc, vs, vb, new_row, sc);
+  tile_fold<BITS>(kc + t0 * RW, ks + 2 * t0, kb + 2 * t0, vc + t0 * RW, vs + 2 * t0, vb + 2 * t0, nvalid, sc.qh,
+                  wbuf, st);
+}
+
+// ---------------------------------------------------------------------------
+// Standalone kernels (the graph schedule)
+// ---------------------------------------------------------------------------
+template <int BITS>
+struct AttnStage {
   static constexpr int ROW_WORDS = 128 * BITS / 32;
   alignas(128) uint32_t kc[kAttBlock * ROW_WORDS];
   alignas(128) uint32_t vc[kAttBlock * ROW_WORDS];
@@ -245,151 +222,129 @@ struct AttnSmem {
   alignas(16) uint16_t kb[kAttBlock * 2];
   alignas(16) uint16_t vs[kAttBlock * 2];
   alignas(16) uint16_t vb[kAttBlock * 2];
+};
+template <int BITS>
+struct AttnSmem {
+  AttnStage<BITS> st[2];
   AttnScratch sc;
-  uint64_t bar;
+  uint64_t bar[2];
 };
 
-// Issue the bulk copies of block b (local index) of kv head g, n tokens
-// (rounded up to 4).
+// Bulk copies of block b (global index) of kv head g into stage s.
 template <int BITS>
-__device__ __forceinline__ void issue_kv_tile(AttnSmem<BITS>& sm, const AttnArgs& a, int g, int b_local, int n) {
-  constexpr int RW = AttnSmem<BITS>::ROW_WORDS;
+__device__ __forceinline__ void issue_block(AttnSmem<BITS>& sm, int s, const AttnArgs& a, int g, int b, int T) {
+  constexpr int RW = AttnStage<BITS>::ROW_WORDS;
+  const int n = min(kAttBlock, T - b * kAttBlock);
   const int n4 = (n + 3) & ~3;
-  const size_t slot = size_t(g) * a.capacity + size_t(b_local) * kAttBlock;
+  const size_t slot = size_t(g) * a.capacity + size_t(b) * kAttBlock;
   const uint32_t cb = uint32_t(n4) * RW * 4, sbytes = uint32_t(n4) * 4;
-  mbar_expect_tx(&sm.bar, 2 * cb + 4 * sbytes);
-  bulk_g2s(sm.kc, a.k_codes + slot * RW, cb, &sm.bar);
-  bulk_g2s(sm.vc, a.v_codes + slot * RW, cb, &sm.bar);
-  bulk_g2s(sm.ks, a.k_scales + slot * 2, sbytes, &sm.bar);
-  bulk_g2s(sm.kb, a.k_biases + slot * 2, sbytes, &sm.bar);
-  bulk_g2s(sm.vs, a.v_scales + slot * 2, sbytes, &sm.bar);
-  bulk_g2s(sm.vb, a.v_biases + slot * 2, sbytes, &sm.bar);
+  mbar_expect_tx(&sm.bar[s], 2 * cb + 4 * sbytes);
+  bulk_g2s(sm.st[s].kc, a.k_codes + slot * RW, cb, &sm.bar[s]);
+  bulk_g2s(sm.st[s].vc, a.v_codes + slot * RW, cb, &sm.bar[s]);
+  bulk_g2s(sm.st[s].ks, a.k_scales + slot * 2, sbytes, &sm.bar[s]);
+  bulk_g2s(sm.st[s].kb, a.k_biases + slot * 2, sbytes, &sm.bar[s]);
+  bulk_g2s(sm.st[s].vs, a.v_scales + slot * 2, sbytes, &sm.bar[s]);
+  bulk_g2s(sm.st[s].vb, a.v_biases + slot * 2, sbytes, &sm.bar[s]);
 }
 
 struct CtaSync {
   __device__ void operator()() const { __syncthreads(); }
 };
 
-// Block partials.  Persistent grid; work item = (block, kv head, q-head slice).
+// Item partials.  Persistent grid; item it = (kv head it % Hkv, item it / Hkv).
 template <int BITS>
-__global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnArgs a) {
-  constexpr int RW = AttnSmem<BITS>::ROW_WORDS;
+__global__ void __launch_bounds__(kAttWarps * 32, 1) k_attn_partial(const AttnArgs a) {
+  constexpr int RW = AttnStage<BITS>::ROW_WORDS;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnSmem<BITS>& sm = *reinterpret_cast<AttnSmem<BITS>*>(smem_raw);
   const int warp = threadIdx.x >> 5;
-
   if (threadIdx.x == 0) {
-    mbar_init(&sm.bar, 1);
+    mbar_init(&sm.bar[0], 1);
+    mbar_init(&sm.bar[1], 1);
     fence_barrier_init();
+    sm.sc.qg = -1;
   }
   __syncthreads();
-  const int p = *a.position;
-  const int T = p + 1;
-  const int nblk_total = (T + kAttBlock - 1) / kAttBlock;
-  const int b0 = a.block_begin, b1 = min(a.block_end, nblk_total);
-  const int nblk = max(b1 - b0, 0);
-  const int hq = att_hq(a.hkv, max(nblk, 1), gridDim.x);
-  const int nq = (a.hq / a.hkv) / hq;
-  const int items = nblk * a.hkv * nq;
-  const bool pos_ok = p >= a.token_base && p < a.capacity + a.token_base;
-  const int blk0 = a.token_base / kAttBlock;
-
-  auto coords = [&](int it, int& b, int& g, int& qsub) {
-    qsub = it % nq;
-    g = (it / nq) % a.hkv;
-    b = b0 + it / (nq * a.hkv);
-  };
-  auto block_tokens = [&](int b) { return min(kAttBlock, T - b * kAttBlock); };
-
-  uint32_t phase = 0;
-  int it = blockIdx.x;
-  bool pending = false;
-  if (threadIdx.x == 0 && it < items && pos_ok) {
-    int b, g, q_;
-    coords(it, b, g, q_);
-    issue_kv_tile<BITS>(sm, a, g, b - blk0, block_tokens(b));
-  }
-  pending = it < items && pos_ok;
   if (a.pdl) grid_wait();
   grid_launch_dependents();
-  if (!pos_ok) {
+  const int p = *a.position;
+  const int T = p + 1;
+  if (p < 0 || p >= a.capacity) {
     if (blockIdx.x == 0 && threadIdx.x == 0) report(a.status, kStatusBadPosition);
     return;
   }
-  const float* cs = a.rope + size_t(p) * 128;  // rows are absolute positions
-  for (; it < items; it += gridDim.x) {
-    int b, g, qsub;
-    coords(it, b, g, qsub);
-    const int n = block_tokens(b);
-    if (!pending && threadIdx.x == 0) issue_kv_tile<BITS>(sm, a, g, b - blk0, n);
-    pending = false;
-    const bool ok = mbar_wait(&sm.bar, phase);
-    phase ^= 1;
-    if (!__syncthreads_and(ok)) {
+  const int nblk = (T + kAttBlock - 1) / kAttBlock;
+  const int nbi = item_blocks(nblk);
+  const int n_items = (nblk + nbi - 1) / nbi;
+  const int items = n_items * a.hkv;
+  const float* cs = a.rope + size_t(p) * 128;
+  const int icap = items_cap(a.capacity);
+  uint32_t phase[2] = {0, 0};
+  for (int it = blockIdx.x; it < items; it += gridDim.x) {
+    const int g = it % a.hkv, item = it / a.hkv;
+    const int b0 = item * nbi, b1 = min(b0 + nbi, nblk);
+    if (threadIdx.x == 0) issue_block<BITS>(sm, 0, a, g, b0, T);
+    if (sm.sc.qg != g) prep_q_heads<BITS>(a.qkv, g, cs, a.q_norm, a.eps, sm.sc, warp);
+    const bool has_new = p >= b0 * kAttBlock && p < b1 * kAttBlock;
+    if (has_new) {
+      const size_t slot = size_t(g) * a.capacity + size_t(p);
+      prep_new_kv<BITS>(a.qkv, a.hq, a.hkv, g, cs, a.k_norm, a.eps, sm.sc, warp, a.k_codes + slot * RW,
+                        a.v_codes + slot * RW, a.k_scales + slot * 2, a.k_biases + slot * 2, a.v_scales + slot * 2,
+                        a.v_biases + slot * 2);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) sm.sc.qg = g;
+    WarpState st;
+    state_empty(st);
+    bool ok = true;
+    for (int b = b0; b < b1; ++b) {
+      const int s = (b - b0) & 1;
+      if (threadIdx.x == 0 && b + 1 < b1) issue_block<BITS>(sm, s ^ 1, a, g, b + 1, T);
+      ok = mbar_wait(&sm.bar[s], phase[s]) && ok;
+      phase[s] ^= 1;
+      if (!__syncthreads_and(ok)) break;
+      const int n = min(kAttBlock, T - b * kAttBlock);
+      const int new_row = (has_new && p / kAttBlock == b) ? p - b * kAttBlock : -1;
+      AttnStage<BITS>& S = sm.st[s];
+      block_tiles<BITS>(S.kc, S.ks, S.kb, S.vc, S.vs, S.vb, n, new_row, sm.sc, sm.sc.u.wbuf[warp], warp, st);
+      // the tile may have been patched through the generic proxy, and the
+      // next bulk copy into this stage must not overtake this block's reads
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncthreads();
+    }
+    if (!ok) {
       if (threadIdx.x == 0) {
         report(a.status, kStatusBulkTimeout);
-        mbar_wait(&sm.bar, phase ^ 1);
+        for (int s = 0; s < 2; ++s) mbar_wait(&sm.bar[s], phase[s]);
       }
       return;
     }
-    AttnBlock ai = {};
-    ai.qkv = a.qkv;
-    ai.hq_total = a.hq;
-    ai.hkv = a.hkv;
-    ai.g = g;
-    ai.h0 = g * (a.hq / a.hkv) + qsub * hq;
-    ai.hq = hq;
-    ai.n = n;
-    ai.cs = cs;
-    ai.q_norm = a.q_norm;
-    ai.k_norm = a.k_norm;
-    ai.eps = a.eps;
-    ai.has_new = p >= b * kAttBlock && p < b * kAttBlock + n;
-    ai.tnew = p - b * kAttBlock;
-    if (ai.has_new && qsub == 0) {
-      const size_t slot = size_t(g) * a.capacity + size_t(p - a.token_base);
-      ai.g_kcodes = a.k_codes + slot * RW;
-      ai.g_vcodes = a.v_codes + slot * RW;
-      ai.g_ks = a.k_scales + slot * 2;
-      ai.g_kb = a.k_biases + slot * 2;
-      ai.g_vs = a.v_scales + slot * 2;
-      ai.g_vb = a.v_biases + slot * 2;
-    }
-    TileView tv = {sm.kc, sm.vc, sm.ks, sm.kb, sm.vs, sm.vb};
-    Partial4 P;
-    attn_block<BITS>(ai, tv, sm.sc, warp, CtaSync{}, P);
-    if (warp < hq) {
-      const int nblk_cap = a.capacity / kAttBlock;
-      store_partial(a.partials + (size_t(ai.h0 + warp) * nblk_cap + (b - blk0)) * kPartialFloats, P);
-    }
-    // the tile was patched by the generic proxy; order that before the next
-    // bulk copy overwrites it
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    warps_fold(st, warp, sm.sc, CtaSync{});
+    if (warp == 0)
+      store_item<BITS>(st, a.partials + (size_t(g * kHeadsPerKv) * icap + item) * kPartialFloats,
+                       size_t(icap) * kPartialFloats);
     __syncthreads();
   }
 }
 
-// Combine: one warp per (q head, super-chunk) merges its blocks in order; the
-// last warp of a head merges the super-chunks (and the sink) into out.
-__global__ void __launch_bounds__(32) k_attn_combine(const AttnArgs a) {
+// Combine: one warp per (q head, super-chunk) folds its items in order; the
+// last warp of a head folds [sink] and the super-chunks into out.
+static __global__ void __launch_bounds__(32) k_attn_combine(const AttnArgs a) {
   if (a.pdl) grid_wait();
   grid_launch_dependents();
   const int lane = threadIdx.x;
   const int p = *a.position;
   const int T = p + 1;
-  const int nblk_total = (T + kAttBlock - 1) / kAttBlock;
-  const int b0 = a.block_begin, b1 = min(a.block_end, nblk_total);
-  const int s_first = b0 / kAttSuper;
-  const int s_last = b1 > b0 ? (b1 - 1) / kAttSuper : s_first - 1;
-  const int n_local = s_last - s_first + 1;
+  const int nblk = (T + kAttBlock - 1) / kAttBlock;
+  const int nbi = item_blocks(nblk), per_super = super_items(nblk);
+  const int n_items = (nblk + nbi - 1) / nbi;
+  const int n_super = (n_items + per_super - 1) / per_super;
   const int h = blockIdx.x;
-  const int nblk_cap = a.capacity / kAttBlock;
-  for (int si = blockIdx.y; si < max(n_local, 0); si += gridDim.y) {
-    const int s = s_first + si;
+  const int icap = items_cap(a.capacity);
+  for (int s = blockIdx.y; s < n_super; s += gridDim.y) {
     Partial4 P = empty_partial();
-    const int bb0 = max(s * kAttSuper, b0), bb1 = min((s + 1) * kAttSuper, b1);
-    for (int b = bb0; b < bb1; ++b) {
-      const float* src = a.partials + (size_t(h) * nblk_cap + (b - a.token_base / kAttBlock)) * kPartialFloats;
+    for (int i = s * per_super; i < min((s + 1) * per_super, n_items); ++i) {
+      const float* src = a.partials + (size_t(h) * icap + i) * kPartialFloats;
       Partial4 Q;
       Q.m = __ldcg(src);
       Q.l = __ldcg(src + 1);
@@ -404,8 +359,7 @@ __global__ void __launch_bounds__(32) k_attn_combine(const AttnArgs a) {
     }
     *reinterpret_cast<float4*>(dst + 4 + 4 * lane) = make_float4(P.a[0], P.a[1], P.a[2], P.a[3]);
   }
-  if (!a.final_merge) return;
-  // last arriving warp of head h merges the super-chunks in order
+  // the last arriving warp of head h merges the super-chunks in order
   __threadfence();
   unsigned prev = 0;
   if (lane == 0) prev = atomicAdd(a.head_counters + h, 1u);
@@ -417,8 +371,7 @@ __global__ void __launch_bounds__(32) k_attn_combine(const AttnArgs a) {
     F.m = bf(a.sinks[h]);
     F.l = 1.0f;
   }
-  const int n_super_total = (nblk_total + kAttSuper - 1) / kAttSuper;
-  for (int s = 0; s < n_super_total; ++s) {
+  for (int s = 0; s < n_super; ++s) {
     const float* src = a.supers + (size_t(h) * a.n_super_max + s) * kPartialFloats;
     Partial4 Q;
     Q.m = __ldcg(src);

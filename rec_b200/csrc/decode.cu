@@ -281,19 +281,15 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
       a.k_norm = (d.flags & REC_FLAG_QK_NORM) ? (const uint16_t*)L.k_norm : nullptr;
       a.eps = d.rms_eps;
       a.position = c->ctl + kCtlPosition;
-      a.token_base = c->token_base;
-      a.block_begin = c->block_begin;
-      a.block_end = c->block_end;
       a.partials = c->partials;
       a.supers = c->supers;
       a.head_counters = c->counters + 2;
       a.out = c->attn;
       a.sinks = (d.flags & REC_FLAG_SINKS) ? (const uint16_t*)L.sinks : nullptr;
       a.n_super_max = c->n_super_max;
-      a.final_merge = 1;
       a.status = status;
       a.pdl = pdl;
-      const int agrid = 2 * sm_count();
+      const int agrid = sm_count();
       if (kind == kKAttn)
         return d.kv_bits == 4 ? launch(k_attn_partial<4>, agrid, kAttWarps * 32, sizeof(AttnSmem<4>), st, pdl, a)
                               : launch(k_attn_partial<8>, agrid, kAttWarps * 32, sizeof(AttnSmem<8>), st, pdl, a);

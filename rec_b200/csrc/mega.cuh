@@ -208,27 +208,28 @@ __device__ __forceinline__ Part partition(const MegaArgs& a) {
 }
 
 struct AttnPlan {
-  int T, nblk, n_super;  // global: tokens, blocks, super-chunks
-  int b_lo, b_hi;        // this rank's blocks (global indices)
-  int hq, nq, items;
+  int T, nblk, n_items, n_super;  // global: tokens, blocks, items, super-chunks
+  int nbi, per_super;             // blocks per item, items per super-chunk
+  int i_lo, i_hi;                 // this rank's items (global indices)
+  int items;                      // work items of this rank: local items x kv heads
 };
 __device__ __forceinline__ AttnPlan attn_plan(const MegaArgs& a, int pos) {
   AttnPlan p;
   p.T = pos + 1;
   p.nblk = (p.T + kAttBlock - 1) / kAttBlock;
-  p.n_super = (p.nblk + kAttSuper - 1) / kAttSuper;
-  p.b_lo = min(a.super_lo * kAttSuper, p.nblk);
-  p.b_hi = min(a.super_hi * kAttSuper, p.nblk);
-  const int nloc = p.b_hi - p.b_lo;
-  p.hq = att_hq(a.hkv, max(nloc, 1), gridDim.x);  // at most one item per CTA while that is possible
-  p.nq = (a.hq / a.hkv) / p.hq;
-  p.items = nloc * a.hkv * p.nq;
+  p.nbi = item_blocks(p.nblk);
+  p.per_super = super_items(p.nblk);
+  p.n_items = (p.nblk + p.nbi - 1) / p.nbi;
+  p.n_super = (p.n_items + p.per_super - 1) / p.per_super;
+  p.i_lo = min(a.super_lo * p.per_super, p.n_items);
+  p.i_hi = min(a.super_hi * p.per_super, p.n_items);
+  p.items = (p.i_hi - p.i_lo) * a.hkv;
   return p;
 }
-__device__ __forceinline__ void attn_coords(const AttnPlan& P, int hkv, int it, int& b, int& g, int& qsub) {
-  qsub = it % P.nq;
-  g = (it / P.nq) % hkv;
-  b = P.b_lo + it / (P.nq * hkv);
+// Work item it of this rank: kv head g and global item index.
+__device__ __forceinline__ void attn_coords(const AttnPlan& P, int hkv, int it, int& g, int& item) {
+  g = it % hkv;
+  item = P.i_lo + it / hkv;
 }
 // Parity of the global layer step: selects one of the two exchange copies.
 __device__ __forceinline__ int xch_parity(const MegaArgs& a, int step, int layer) {
@@ -398,11 +399,14 @@ struct Producer {
           }
           // A: K and V tiles of this CTA's items
           for (int it = blockIdx.x; it < AP.items && ok; it += gridDim.x) {
-            int b, g, qsub;
-            attn_coords(AP, a.hkv, it, b, g, qsub);
-            const int n = min(kAttBlock, AP.T - b * kAttBlock);
-            kv_chunk(L.k_codes, L.k_scales, L.k_biases, g, b, n);
-            kv_chunk(L.v_codes, L.v_scales, L.v_biases, g, b, n);
+            int g, item;
+            attn_coords(AP, a.hkv, it, g, item);
+            const int b1 = min(item * AP.nbi + AP.nbi, AP.nblk);
+            for (int b = item * AP.nbi; b < b1 && ok; ++b) {
+              const int n = min(kAttBlock, AP.T - b * kAttBlock);
+              kv_chunk(L.k_codes, L.k_scales, L.k_biases, g, b, n);
+              kv_chunk(L.v_codes, L.v_scales, L.v_biases, g, b, n);
+            }
             stamp(a, step, l, 24);
           }
           // O rows
@@ -663,73 +667,77 @@ struct Consumers {
   }
 
   // --- attention ----------------------------------------------------------------
-  // All consumer warps: block b of kv head g (tiles in ring slots kt / vt),
-  // then the last-arriver merges of super-chunk and head.
+  // All consumer warps: item `item` (4 blocks) of kv head g for its 8 q heads,
+  // blocks streamed through the ring (K slot, V slot per block); then the
+  // last-arriver merges of super-chunk and head.
   template <int BITS>
-  __device__ void attn_item_compute(const MegaLayer& L, const AttnPlan& P, int pos, int b, int g, int qsub,
-                                    uint8_t* kt, uint8_t* vt, int step_, int layer_) {
+  __device__ void attn_item(const MegaLayer& L, const AttnPlan& P, int pos, int g, int item, int step_,
+                            int layer_) {
     constexpr int RW = 128 * BITS / 32;
-    const int n = min(kAttBlock, P.T - b * kAttBlock), n4 = (n + 3) & ~3;
-    TileView tv;
-    tv.kc = reinterpret_cast<uint32_t*>(kt);
-    tv.ks = reinterpret_cast<uint16_t*>(kt + n4 * RW * 4);
-    tv.kb = tv.ks + n4 * 2;
-    tv.vc = reinterpret_cast<uint32_t*>(vt);
-    tv.vs = reinterpret_cast<uint16_t*>(vt + n4 * RW * 4);
-    tv.vb = tv.vs + n4 * 2;
-    const int hq = P.hq;
-    AttnBlock ab = {};
-    ab.qkv = a.qkv;
-    ab.hq_total = a.hq;
-    ab.hkv = a.hkv;
-    ab.g = g;
-    ab.h0 = g * (a.hq / a.hkv) + qsub * hq;
-    ab.hq = hq;
-    ab.n = n;
-    ab.cs = a.rope + size_t(pos) * 128;
-    ab.q_norm = L.q_norm;
-    ab.k_norm = L.k_norm;
-    ab.eps = a.eps;
-    ab.has_new = pos >= b * kAttBlock && pos < b * kAttBlock + n;
-    ab.tnew = pos - b * kAttBlock;
-    if (ab.has_new && qsub == 0) {
-      const size_t slot = size_t(g) * a.capacity + size_t(pos - a.token_base);
-      ab.g_kcodes = L.k_codes + slot * RW;
-      ab.g_vcodes = L.v_codes + slot * RW;
-      ab.g_ks = L.k_scales + slot * 2;
-      ab.g_kb = L.k_biases + slot * 2;
-      ab.g_vs = L.v_scales + slot * 2;
-      ab.g_vb = L.v_biases + slot * 2;
+    const int b0 = item * P.nbi, b1 = min(b0 + P.nbi, P.nblk);
+    const float* cs = a.rope + size_t(pos) * 128;
+    if (sm.att.qg != g) prep_q_heads<BITS>(a.qkv, g, cs, L.q_norm, a.eps, sm.att, warp);
+    const bool has_new = pos >= b0 * kAttBlock && pos < b1 * kAttBlock;
+    if (has_new) {
+      const size_t sl = size_t(g) * a.capacity + size_t(pos - a.token_base);
+      prep_new_kv<BITS>(a.qkv, a.hq, a.hkv, g, cs, L.k_norm, a.eps, sm.att, warp, L.k_codes + sl * RW,
+                        L.v_codes + sl * RW, L.k_scales + sl * 2, L.k_biases + sl * 2, L.v_scales + sl * 2,
+                        L.v_biases + sl * 2);
     }
-    Partial4 Pt;
-    const MegaArgs& A = a;
-    const int w0 = warp;
-    attn_block<BITS>(ab, tv, sm.att, warp, ConsSync{}, Pt, [&](int i) {
-      if (w0 == 0 && lane == 0) stamp(A, step_, layer_, 16 + i);
-    });
+    cons_sync();
+    if (warp == 0 && lane == 0) sm.att.qg = g;
+    WarpState st;
+    state_empty(st);
+    for (int b = b0; b < b1; ++b) {
+      uint8_t* kt = const_cast<uint8_t*>(take());
+      const int kslot = slot;
+      ++chunk;
+      uint8_t* vt = const_cast<uint8_t*>(take());
+      const int vslot = slot;
+      --chunk;
+      const int n = min(kAttBlock, P.T - b * kAttBlock), n4 = (n + 3) & ~3;
+      uint32_t* kc = reinterpret_cast<uint32_t*>(kt);
+      uint16_t* ks = reinterpret_cast<uint16_t*>(kt + n4 * RW * 4);
+      uint32_t* vc = reinterpret_cast<uint32_t*>(vt);
+      uint16_t* vs = reinterpret_cast<uint16_t*>(vt + n4 * RW * 4);
+      const int new_row = (has_new && pos / kAttBlock == b) ? pos - b * kAttBlock : -1;
+      block_tiles<BITS>(kc, ks, ks + n4 * 2, vc, vs, vs + n4 * 2, n, new_row, sm.att, sm.att.u.wbuf[warp], warp,
+                        st);
+      if (warp == 0 && lane == 0 && b == b0) stamp(a, step_, layer_, 16);
+      slot = kslot;
+      release(true);
+      slot = vslot;
+      release(true);
+    }
+    if (warp == 0 && lane == 0) stamp(a, step_, layer_, 17);
+    cons_sync();  // the tree scratch overlays the per-warp PV buffers
+    warps_fold(st, warp, sm.att, ConsSync{});
+    // item partial of the 8 heads (local item index), then the merges
+    const int icap = items_cap(a.capacity);
+    const int item0 = a.token_base / (kAttBlock * P.nbi);
+    if (warp == 0)
+      store_item<BITS>(st, a.partials + (size_t(g * kHeadsPerKv) * icap + (item - item0)) * kPartialFloats,
+                       size_t(icap) * kPartialFloats);
+    __threadfence();
     if (warp == 0 && lane == 0) stamp(a, step_, layer_, 18);
-    // the block partial and the last-arriver merges
-    const int nblk_cap = a.capacity / kAttBlock;
-    const int blk0 = a.token_base / kAttBlock;  // first block of this rank's cache
-    const int s = b / kAttSuper;
-    const int n_super = P.n_super;
-    const int in_super = min(kAttSuper, P.nblk - s * kAttSuper);
-    if (warp >= hq) return;
-    const int h = ab.h0 + warp;
-    const float* hpart = a.partials + size_t(h) * nblk_cap * kPartialFloats;
-    store_partial(const_cast<float*>(hpart) + size_t(b - blk0) * kPartialFloats, Pt);
-    __threadfence();
-    unsigned prev = 0;
+    const int s = item / P.per_super;
     const int s_loc = s - a.super_lo;
-    if (lane == 0) prev = atomicAdd(a.cnt + a.hq + h * a.n_super_max + s_loc, 1u);
-    prev = __shfl_sync(0xffffffffu, prev, 0);
-    if (int(prev) != in_super - 1) return;
-    // this warp merges super-chunk s of head h: its own block from registers,
-    // the others loaded in batches so that their L2 round trips overlap
+    const int in_super = min(P.per_super, P.n_items - s * P.per_super);
+    cons_sync();
+    if (warp == 0 && lane == 0) {
+      const unsigned prev = atomicAdd(a.cnt + a.hq + g * a.n_super_max + s_loc, 1u);
+      sm.xok = int(prev) == in_super - 1;
+      if (sm.xok) a.cnt[a.hq + g * a.n_super_max + s_loc] = 0;
+    }
+    cons_sync();
+    if (!sm.xok) return;
+    // the last item of super-chunk s: warp w merges head 8g + w
     __threadfence();
+    const int h = g * kHeadsPerKv + warp;
+    const float* hpart = a.partials + size_t(h) * icap * kPartialFloats;
     Partial4 S = empty_partial();
-    merge_range(S, hpart, s * kAttSuper - blk0, s * kAttSuper + in_super - blk0, b - blk0, Pt);
-    if (lane == 0) a.cnt[a.hq + h * a.n_super_max + s_loc] = 0;
+    const Partial4 none = empty_partial();
+    merge_range(S, hpart, s * P.per_super - item0, s * P.per_super + in_super - item0, -1, none);
     if (a.world > 1) {
       // publish the super-chunk to every rank; each merges them itself
       const int par = xch_parity(a, step_, layer_);
@@ -745,16 +753,17 @@ struct Consumers {
       F.m = bf(L.sinks[h]);
       F.l = 1.0f;
     }
-    if (n_super == 1) {
+    if (P.n_super == 1) {
       merge_into(F, S);
     } else {
       store_partial(a.supers + (size_t(h) * a.n_super_max + s) * kPartialFloats, S);
       __threadfence();
+      unsigned prev = 0;
       if (lane == 0) prev = atomicAdd(a.cnt + h, 1u);
       prev = __shfl_sync(0xffffffffu, prev, 0);
-      if (int(prev) != n_super - 1) return;
+      if (int(prev) != P.n_super - 1) return;
       __threadfence();
-      merge_range(F, a.supers + size_t(h) * a.n_super_max * kPartialFloats, 0, n_super, s, S);
+      merge_range(F, a.supers + size_t(h) * a.n_super_max * kPartialFloats, 0, P.n_super, s, S);
       if (lane == 0) a.cnt[h] = 0;
     }
     write_attn(h, F);
@@ -1012,23 +1021,14 @@ struct Consumers {
         if (!grid_barrier(a, bar_index(a, step, l, 0))) return;
         // ---- A
         if (warp == 0 && lane == 0) stamp(a, step, l, 11);
+        if (warp == 0 && lane == 0) sm.att.qg = -1;  // queries change every layer
+        cons_sync();
         for (int it = blockIdx.x; it < AP.items; it += gridDim.x) {
-          int b, g, qsub;
-          attn_coords(AP, a.hkv, it, b, g, qsub);
-          uint8_t* kt = const_cast<uint8_t*>(take());
-          const int kslot = slot;
-          ++chunk;
-          uint8_t* vt = const_cast<uint8_t*>(take());
-          const int vslot = slot;
-          --chunk;
+          int g, item;
+          attn_coords(AP, a.hkv, it, g, item);
           if (warp == 0 && lane == 0) stamp(a, step, l, 12);
-          attn_item_compute<BITS>(L, AP, pos, b, g, qsub, kt, vt, step, l);
-          cons_sync();
+          attn_item<BITS>(L, AP, pos, g, item, step, l);
           if (warp == 0 && lane == 0) stamp(a, step, l, 13);
-          slot = kslot;
-          release(true);
-          slot = vslot;
-          release(true);
         }
         if (a.world > 1 && warp == 0) attn_final_sharded(L, AP, xch_parity(a, step, l));
         if (!grid_barrier(a, bar_index(a, step, l, 1))) return;
