@@ -147,12 +147,17 @@ __device__ __forceinline__ void patch_row(uint32_t* kc, uint16_t* ks, uint16_t* 
 // Tree fold of the 8 warp states; warp 0 ends with the item state.  All
 // warps call it (sync: a barrier over the 8 warps) after a barrier that ends
 // every warp's tiles: the tree scratch overlays the per-warp PV buffers.
+// Slots: level 1 senders w = 1,3,5,7 write slot w/2; level 2 senders 2, 6
+// write slots 1, 3 and level 3 sender 4 writes slot 3 -- each a slot that only
+// the sender itself read in the level before, so one barrier per level.
 template <typename Sync>
 __device__ __forceinline__ void warps_fold(WarpState& st, int warp, AttnScratch& sc, Sync sync) {
   const int lane = threadIdx.x & 31;
   for (int step = 1; step < kAttWarps; step *= 2) {
+    // slot of the pair (receiver w, sender w + step) at this level
+    auto slot = [&](int recv) { return step == 1 ? recv / 2 : (step == 2 ? recv / 2 + 1 : 3); };
     if ((warp & (2 * step - 1)) == step) {
-      float(*d)[32] = sc.u.tree[warp / (2 * step)];
+      float(*d)[32] = sc.u.tree[slot(warp - step)];
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         d[hh][lane] = st.m[hh];
@@ -163,7 +168,7 @@ __device__ __forceinline__ void warps_fold(WarpState& st, int warp, AttnScratch&
     }
     sync();
     if ((warp & (2 * step - 1)) == 0) {
-      const float(*d)[32] = sc.u.tree[warp / (2 * step)];
+      const float(*d)[32] = sc.u.tree[slot(warp)];
       WarpState y;
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
@@ -174,7 +179,6 @@ __device__ __forceinline__ void warps_fold(WarpState& st, int warp, AttnScratch&
       }
       state_merge(st, y);
     }
-    sync();
   }
 }
 

@@ -393,6 +393,15 @@ __device__ __forceinline__ void tile_fold(const uint32_t* kc, const uint16_t* ks
 #pragma unroll
   for (int g = 0; g < 2; ++g) {
     float dnw[2], B[2];
+    float vsc[2][2], vbi[2][2];  // V scale / bias of the thread's tokens, group g
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int j = 16 * hf + 8 * r + gq;
+        vsc[hf][r] = bf(vs[2 * j + g]);
+        vbi[hf][r] = bf(vb[2 * j + g]);
+      }
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
       float w[2][2], x[2][2];
@@ -403,8 +412,8 @@ __device__ __forceinline__ void tile_fold(const uint32_t* kc, const uint16_t* ks
         for (int r = 0; r < 2; ++r) {
           const int j = 16 * hf + 8 * r + gq;
           const bool v = j < nvalid;
-          w[hf][r] = v ? __fmul_rn(p[hf][r][hh], bf(vs[2 * j + g])) : 0.0f;
-          x[hf][r] = v ? __fmul_rn(p[hf][r][hh], bf(vb[2 * j + g])) : 0.0f;
+          w[hf][r] = v ? __fmul_rn(p[hf][r][hh], vsc[hf][r]) : 0.0f;
+          x[hf][r] = v ? __fmul_rn(p[hf][r][hh], vbi[hf][r]) : 0.0f;
           mx = fmaxf(mx, fabsf(w[hf][r]));
         }
       mx = max_tokens(mx);
