@@ -47,6 +47,9 @@ def parse():
     p.add_argument("--context", type=int, default=1024)
     p.add_argument("--kv-bits", type=int, default=8, choices=[4, 8],
                    help="8: config 3 (the default workload); 4: the config-4 cache format")
+    p.add_argument("--attn-sweep", action="store_true",
+                   help="config 2: time the attention kernels alone over --contexts (4-bit cache unless --kv-bits 8)")
+    p.add_argument("--contexts", default="1024,8192,32768,131072,258048")
     p.add_argument("--shard", action="store_true",
                    help="with N GPUs: one session split over the GPUs (expert parallelism + split-KV, the "
                         "config-4 partitioning) instead of N independent sessions (config 3 replicas)")
@@ -443,9 +446,79 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+# ---------------------------------------------------------------------------- attention sweep
+def run_attn_sweep(args):
+    """Config 2: the decode attention kernels alone (rec_attn_decode: append +
+    item partials + combine) over 4-bit caches of the given contexts; one JSON
+    line with time, KV bytes and HBM fraction per context."""
+    import ctypes as C
+
+    import torch
+
+    from rec_b200 import abi
+    from rec_b200._lib import check, lib
+
+    torch.cuda.set_device(0)
+    peak, peak_kind = measured_peaks()
+    hq, hkv, bits = 32, 4, args.kv_bits
+    words = 128 * bits // 32
+    per_token = 2 * hkv * (128 * bits // 8 + 8)
+    rows = []
+    for T in [int(t) for t in args.contexts.split(",")]:
+        cap = (T + 255) // 256 * 256
+        g = torch.Generator(device="cuda").manual_seed(T)
+        kv = {}
+        for n in ("k", "v"):
+            kv[n + "_codes"] = torch.randint(0, 2**31 - 1, (hkv, cap, words), generator=g, device="cuda",
+                                             dtype=torch.int32)
+            kv[n + "_scales"] = (torch.rand(hkv, cap, 2, generator=g, device="cuda") * 0.1 + 0.01).to(torch.bfloat16)
+            kv[n + "_biases"] = (torch.rand(hkv, cap, 2, generator=g, device="cuda") - 0.5).to(torch.bfloat16)
+        rec = abi.RecKVLayer(*(kv[n].data_ptr() for n in ("k_codes", "k_scales", "k_biases", "v_codes", "v_scales",
+                                                         "v_biases")))
+        qkv = torch.randn((hq + 2 * hkv) * 128, generator=g, device="cuda").to(torch.bfloat16)
+        rope = torch.zeros(cap, 128, device="cuda")
+        rope[:, :64] = 1.0
+        pos = torch.tensor([T - 1], dtype=torch.int32, device="cuda")
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        nb = lib().rec_attn_scratch_bytes(hq, cap)
+        scratch = torch.empty(nb + 256, dtype=torch.uint8, device="cuda")
+        base = (scratch.data_ptr() + 255) // 256 * 256
+        out = torch.empty(hq * 128, dtype=torch.bfloat16, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+
+        def call():
+            check(lib().rec_attn_decode(C.c_void_p(qkv.data_ptr()), hq, hkv, C.byref(rec), cap, bits,
+                                        C.c_void_p(rope.data_ptr()), None, C.c_void_p(pos.data_ptr()),
+                                        C.c_void_p(base), nb, C.c_void_p(out.data_ptr()),
+                                        C.c_void_p(status.data_ptr()), C.c_void_p(stream)), "rec_attn_decode")
+
+        for _ in range(max(3, args.warmup)):
+            call()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            call()
+        b.record()
+        torch.cuda.synchronize()
+        if int(status.item()) != 0:
+            raise RuntimeError(f"attention kernels reported device status {int(status.item())}")
+        us = a.elapsed_time(b) / args.steps * 1e3
+        bytes_ = per_token * T
+        rows.append({"context": T, "us": round(us, 2), "kv_bytes": bytes_, "GBps": round(bytes_ / us / 1e3, 1),
+                     "frac": round(bytes_ / us / 1e3 / peak, 4)})
+        del kv, scratch
+        torch.cuda.empty_cache()
+    print(json.dumps({"workload": "config2_attention_sweep", "kv_bits": bits, "heads": "32q/4kv x 128",
+                      "peak_GBps": peak, "peak_source": peak_kind, "steps": args.steps, "contexts": rows}),
+          flush=True)
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.attn_sweep:
+        run_attn_sweep(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_rec(args)

@@ -347,15 +347,8 @@ static __global__ void __launch_bounds__(32) k_attn_combine(const AttnArgs a) {
   const int icap = items_cap(a.capacity);
   for (int s = blockIdx.y; s < n_super; s += gridDim.y) {
     Partial4 P = empty_partial();
-    for (int i = s * per_super; i < min((s + 1) * per_super, n_items); ++i) {
-      const float* src = a.partials + (size_t(h) * icap + i) * kPartialFloats;
-      Partial4 Q;
-      Q.m = __ldcg(src);
-      Q.l = __ldcg(src + 1);
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(src + 4) + lane);
-      Q.a[0] = v.x; Q.a[1] = v.y; Q.a[2] = v.z; Q.a[3] = v.w;
-      merge_into(P, Q);
-    }
+    fold_partials(P, a.partials + size_t(h) * icap * kPartialFloats, s * per_super,
+                  min((s + 1) * per_super, n_items));
     float* dst = a.supers + (size_t(h) * a.n_super_max + s) * kPartialFloats;
     if (lane == 0) {
       dst[0] = P.m;
@@ -375,15 +368,7 @@ static __global__ void __launch_bounds__(32) k_attn_combine(const AttnArgs a) {
     F.m = bf(a.sinks[h]);
     F.l = 1.0f;
   }
-  for (int s = 0; s < n_super; ++s) {
-    const float* src = a.supers + (size_t(h) * a.n_super_max + s) * kPartialFloats;
-    Partial4 Q;
-    Q.m = __ldcg(src);
-    Q.l = __ldcg(src + 1);
-    const float4 v = __ldcg(reinterpret_cast<const float4*>(src + 4) + lane);
-    Q.a[0] = v.x; Q.a[1] = v.y; Q.a[2] = v.z; Q.a[3] = v.w;
-    merge_into(F, Q);
-  }
+  fold_partials(F, a.supers + size_t(h) * a.n_super_max * kPartialFloats, 0, n_super);
   uint2 o;
   o.x = uint32_t(to_bf(__fdiv_rn(F.a[0], F.l))) | (uint32_t(to_bf(__fdiv_rn(F.a[1], F.l))) << 16);
   o.y = uint32_t(to_bf(__fdiv_rn(F.a[2], F.l))) | (uint32_t(to_bf(__fdiv_rn(F.a[3], F.l))) << 16);

@@ -75,6 +75,29 @@ __device__ __forceinline__ void store_partial(float* dst, const Partial4& P) {
   *reinterpret_cast<float4*>(dst + 4 + 4 * lane) = make_float4(P.a[0], P.a[1], P.a[2], P.a[3]);
 }
 
+// Folds partials [i0, i1) of a [*, kPartialFloats] array (L2 reads) into P in
+// order, with kBatch loads in flight.
+__device__ __forceinline__ void fold_partials(Partial4& P, const float* base, int i0, int i1) {
+  constexpr int kBatch = 4;
+  const int lane = threadIdx.x & 31;
+  for (int i = i0; i < i1; i += kBatch) {
+    Partial4 Q[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      if (i + j < i1) {
+        const float* src = base + size_t(i + j) * kPartialFloats;
+        Q[j].m = __ldcg(src);
+        Q[j].l = __ldcg(src + 1);
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(src + 4) + lane);
+        Q[j].a[0] = v.x; Q[j].a[1] = v.y; Q[j].a[2] = v.z; Q[j].a[3] = v.w;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j)
+      if (i + j < i1) merge_into(P, Q[j]);
+  }
+}
+
 // Exact small-integer to float: 2^23 + c has c in the low mantissa bits.
 __device__ __forceinline__ float code_f(uint32_t c) {
   return __fsub_rn(__uint_as_float(0x4B000000u | c), 8388608.0f);
