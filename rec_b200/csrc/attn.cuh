@@ -54,9 +54,10 @@ __host__ __device__ inline int items_cap(int capacity) { return capacity / kAttB
 // Shared-memory scratch of the attention items of one CTA.
 struct AttnScratch {
   QHead qh[kHeadsPerKv];
-  union {
+  union alignas(16) {
     uint8_t wbuf[kAttWarps][1024];         // per-warp fixed-point PV weights
     float tree[kAttWarps / 2][36][32];     // warp states during the tree fold
+    float stage[kAttWarps][4][kPartialFloats];  // per-warp partials being merged
   } u;
   uint32_t kpatch[32], vpatch[32];         // quantized K / V row of the new token
   uint16_t kps[2], kpb[2], vps[2], vpb[2];
@@ -257,7 +258,7 @@ struct CtaSync {
 
 // Item partials.  Persistent grid; item it = (kv head it % Hkv, item it / Hkv).
 template <int BITS>
-__global__ void __launch_bounds__(kAttWarps * 32, 1) k_attn_partial(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnArgs a) {
   constexpr int RW = AttnStage<BITS>::ROW_WORDS;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnSmem<BITS>& sm = *reinterpret_cast<AttnSmem<BITS>*>(smem_raw);

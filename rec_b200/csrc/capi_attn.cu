@@ -23,11 +23,15 @@ AttnScratchLayout attn_scratch_layout(int hq, int capacity) {
   return L;
 }
 
+// Persistent grid: as many CTAs as fit on every SM.
 template <class K>
-cudaError_t launch_smem(K kern, int grid, int threads, size_t smem, cudaStream_t st, const AttnArgs& a) {
+cudaError_t launch_smem(K kern, int threads, size_t smem, cudaStream_t st, const AttnArgs& a) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  kern<<<grid, threads, smem, st>>>(a);
+  int per_sm = 1;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
+  if (e != cudaSuccess) return e;
+  kern<<<sm_count() * (per_sm > 0 ? per_sm : 1), threads, smem, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -79,9 +83,8 @@ REC_API int rec_attn_decode(const void* qkv_dev, int32_t n_q_heads, int32_t n_kv
   a.n_super_max = L.n_super;
   a.status = status_dev;
   a.pdl = 0;
-  const int grid = sm_count();
-  cudaError_t e = kv_bits == 4 ? launch_smem(k_attn_partial<4>, grid, kAttWarps * 32, sizeof(AttnSmem<4>), st, a)
-                               : launch_smem(k_attn_partial<8>, grid, kAttWarps * 32, sizeof(AttnSmem<8>), st, a);
+  cudaError_t e = kv_bits == 4 ? launch_smem(k_attn_partial<4>, kAttWarps * 32, sizeof(AttnSmem<4>), st, a)
+                               : launch_smem(k_attn_partial<8>, kAttWarps * 32, sizeof(AttnSmem<8>), st, a);
   REC_CHECK_CUDA(e);
   k_attn_combine<<<dim3(n_q_heads, L.n_super), 32, 0, st>>>(a);
   REC_CHECK_CUDA(cudaGetLastError());

@@ -289,7 +289,7 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
       a.n_super_max = c->n_super_max;
       a.status = status;
       a.pdl = pdl;
-      const int agrid = sm_count();
+      const int agrid = sm_count() * (d.kv_bits == 4 ? 2 : 1);  // 4-bit stages fit two CTAs per SM
       if (kind == kKAttn)
         return d.kv_bits == 4 ? launch(k_attn_partial<4>, agrid, kAttWarps * 32, sizeof(AttnSmem<4>), st, pdl, a)
                               : launch(k_attn_partial<8>, agrid, kAttWarps * 32, sizeof(AttnSmem<8>), st, pdl, a);

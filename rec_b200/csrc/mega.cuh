@@ -244,6 +244,10 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 __device__ __forceinline__ void stamp(const MegaArgs& a, int step, int layer, int slot) {
   if (a.prof2 && step == 0 && layer == a.prof_layer) a.prof2[blockIdx.x * 32 + slot] = globaltimer();
 }
+// Adds v to a per-CTA diagnostic slot of the same layer profile.
+__device__ __forceinline__ void prof_add(const MegaArgs& a, int step, int layer, int slot, unsigned long long v) {
+  if (a.prof2 && step == 0 && layer == a.prof_layer) a.prof2[blockIdx.x * 32 + slot] += v;
+}
 
 // Grid barrier index of a phase: each step has 6 per layer + 1 (after H).
 __device__ __forceinline__ unsigned bar_index(const MegaArgs& a, int step, int layer, int ph) {
@@ -259,14 +263,18 @@ __device__ __forceinline__ void set_abort(const MegaArgs& a, int code) {
 }
 
 // Bounded grid barrier among consumers of all CTAs.  Returns false on abort.
-__device__ __forceinline__ bool grid_barrier(const MegaArgs& a, unsigned idx) {
+// seq: the launch's running barrier count (every CTA passes the same
+// sequence); idx: the timeline slot, or kNoStamp for barriers the timeline
+// does not record (the long-context merge phase).
+constexpr unsigned kNoStamp = 0xffffffffu;
+__device__ __forceinline__ bool grid_barrier(const MegaArgs& a, unsigned seq, unsigned idx) {
   cons_sync();
   __shared__ int ok_flag;
   if (threadIdx.x == 32) {
-    if (a.prof) a.prof[(size_t(idx) * gridDim.x + blockIdx.x) * 2] = globaltimer();
+    if (a.prof && idx != kNoStamp) a.prof[(size_t(idx) * gridDim.x + blockIdx.x) * 2] = globaltimer();
     __threadfence();
     atomicAdd(a.gbar, 1u);
-    const unsigned target = gridDim.x * (idx + 1);
+    const unsigned target = gridDim.x * (seq + 1);
     int ok = 1;
     uint32_t spins = 0;
     while (ld_acquire(a.gbar) < target) {
@@ -278,7 +286,7 @@ __device__ __forceinline__ bool grid_barrier(const MegaArgs& a, unsigned idx) {
       }
     }
     __threadfence();
-    if (a.prof) a.prof[(size_t(idx) * gridDim.x + blockIdx.x) * 2 + 1] = globaltimer();
+    if (a.prof && idx != kNoStamp) a.prof[(size_t(idx) * gridDim.x + blockIdx.x) * 2 + 1] = globaltimer();
     ok_flag = ok && !aborted(a);
   }
   cons_sync();
@@ -378,6 +386,25 @@ struct Producer {
     issued(slot);
   }
 
+  // 4-bit caches: K and V of one block fill exactly one slot (2 x 18,432 B).
+  __device__ void kv_pair_chunk(const MegaLayer& L, int g, int b, int n) {
+    int slot;
+    uint8_t* dst = acquire(slot);
+    if (!dst) return;
+    constexpr int rw = 16;
+    const int n4 = (n + 3) & ~3;
+    const size_t s0 = size_t(g) * a.capacity + size_t(b - a.token_base / kAttBlock) * kAttBlock;
+    const uint32_t cb = uint32_t(n4) * rw * 4, sbytes = uint32_t(n4) * 4, half = cb + 2 * sbytes;
+    mbar_expect_tx(&sm.full[slot], 2 * half);
+    bulk_g2s(dst, L.k_codes + s0 * rw, cb, &sm.full[slot]);
+    bulk_g2s(dst + cb, L.k_scales + s0 * 2, sbytes, &sm.full[slot]);
+    bulk_g2s(dst + cb + sbytes, L.k_biases + s0 * 2, sbytes, &sm.full[slot]);
+    bulk_g2s(dst + half, L.v_codes + s0 * rw, cb, &sm.full[slot]);
+    bulk_g2s(dst + half + cb, L.v_scales + s0 * 2, sbytes, &sm.full[slot]);
+    bulk_g2s(dst + half + cb + sbytes, L.v_biases + s0 * 2, sbytes, &sm.full[slot]);
+    issued(slot);
+  }
+
   __device__ void run() {
     const int lane = threadIdx.x & 31;
     const Part P = partition(a);
@@ -404,8 +431,12 @@ struct Producer {
             const int b1 = min(item * AP.nbi + AP.nbi, AP.nblk);
             for (int b = item * AP.nbi; b < b1 && ok; ++b) {
               const int n = min(kAttBlock, AP.T - b * kAttBlock);
-              kv_chunk(L.k_codes, L.k_scales, L.k_biases, g, b, n);
-              kv_chunk(L.v_codes, L.v_scales, L.v_biases, g, b, n);
+              if (a.kv_bits == 4) {
+                kv_pair_chunk(L, g, b, n);
+              } else {
+                kv_chunk(L.k_codes, L.k_scales, L.k_biases, g, b, n);
+                kv_chunk(L.v_codes, L.v_scales, L.v_biases, g, b, n);
+              }
             }
             stamp(a, step, l, 24);
           }
@@ -475,6 +506,9 @@ struct Consumers {
   MegaSmem& sm;
   const int warp, lane;  // warp in 0..7
   uint32_t chunk = 0;
+  unsigned nbar = 0;  // grid barriers passed in this launch
+
+  __device__ bool gbar(unsigned idx) { return grid_barrier(a, nbar++, idx); }
   int slot = 0;
   bool ok = true;
 
@@ -676,6 +710,7 @@ struct Consumers {
     constexpr int RW = 128 * BITS / 32;
     const int b0 = item * P.nbi, b1 = min(b0 + P.nbi, P.nblk);
     const float* cs = a.rope + size_t(pos) * 128;
+    cons_sync();  // a previous item's merges may still use the scratch
     if (sm.att.qg != g) prep_q_heads<BITS>(a.qkv, g, cs, L.q_norm, a.eps, sm.att, warp);
     const bool has_new = pos >= b0 * kAttBlock && pos < b1 * kAttBlock;
     if (has_new) {
@@ -689,13 +724,19 @@ struct Consumers {
     WarpState st;
     state_empty(st);
     for (int b = b0; b < b1; ++b) {
+      const int n = min(kAttBlock, P.T - b * kAttBlock), n4 = (n + 3) & ~3;
       uint8_t* kt = const_cast<uint8_t*>(take());
       const int kslot = slot;
-      ++chunk;
-      uint8_t* vt = const_cast<uint8_t*>(take());
-      const int vslot = slot;
-      --chunk;
-      const int n = min(kAttBlock, P.T - b * kAttBlock), n4 = (n + 3) & ~3;
+      uint8_t* vt;
+      int vslot = -1;
+      if constexpr (BITS == 4) {
+        vt = kt + n4 * RW * 4 + n4 * 8;  // V half of the same slot
+      } else {
+        ++chunk;
+        vt = const_cast<uint8_t*>(take());
+        vslot = slot;
+        --chunk;
+      }
       uint32_t* kc = reinterpret_cast<uint32_t*>(kt);
       uint16_t* ks = reinterpret_cast<uint16_t*>(kt + n4 * RW * 4);
       uint32_t* vc = reinterpret_cast<uint32_t*>(vt);
@@ -706,8 +747,10 @@ struct Consumers {
       if (warp == 0 && lane == 0 && b == b0) stamp(a, step_, layer_, 16);
       slot = kslot;
       release(true);
-      slot = vslot;
-      release(true);
+      if (vslot >= 0) {
+        slot = vslot;
+        release(true);
+      }
     }
     if (warp == 0 && lane == 0) stamp(a, step_, layer_, 17);
     cons_sync();  // the tree scratch overlays the per-warp PV buffers
@@ -718,26 +761,40 @@ struct Consumers {
     if (warp == 0)
       store_item<BITS>(st, a.partials + (size_t(g * kHeadsPerKv) * icap + (item - item0)) * kPartialFloats,
                        size_t(icap) * kPartialFloats);
+    if (warp == 0 && lane == 0) {
+      stamp(a, step_, layer_, 18);
+      prof_add(a, step_, layer_, 25, 1);
+    }
+    // several super-chunks: merged in a phase of their own (merge_phase)
+    if (P.n_super > 1) return;
     __threadfence();
-    if (warp == 0 && lane == 0) stamp(a, step_, layer_, 18);
-    const int s = item / P.per_super;
-    const int s_loc = s - a.super_lo;
-    const int in_super = min(P.per_super, P.n_items - s * P.per_super);
+    const int in_super = P.n_items;
     cons_sync();
     if (warp == 0 && lane == 0) {
-      const unsigned prev = atomicAdd(a.cnt + a.hq + g * a.n_super_max + s_loc, 1u);
+      const unsigned prev = atomicAdd(a.cnt + a.hq + g * a.n_super_max, 1u);
       sm.xok = int(prev) == in_super - 1;
-      if (sm.xok) a.cnt[a.hq + g * a.n_super_max + s_loc] = 0;
+      if (sm.xok) a.cnt[a.hq + g * a.n_super_max] = 0;
     }
     cons_sync();
     if (!sm.xok) return;
-    // the last item of super-chunk s: warp w merges head 8g + w
+    // the last item of the only super-chunk: warp w merges head 8g + w
     __threadfence();
+    super_done<BITS>(L, P, g, 0, item0, step_, layer_);
+  }
+
+  // Warp w folds super-chunk s of head 8g + w (its items in order), then
+  // publishes it (several ranks) or merges the output (one rank: directly
+  // with one super-chunk, else through the per-head last arriver).
+  template <int BITS>
+  __device__ void super_done(const MegaLayer& L, const AttnPlan& P, int g, int s, int item0, int step_, int layer_) {
+    const int icap = items_cap(a.capacity);
+    const int in_super = min(P.per_super, P.n_items - s * P.per_super);
     const int h = g * kHeadsPerKv + warp;
     const float* hpart = a.partials + size_t(h) * icap * kPartialFloats;
     Partial4 S = empty_partial();
     const Partial4 none = empty_partial();
     merge_range(S, hpart, s * P.per_super - item0, s * P.per_super + in_super - item0, -1, none);
+    if (warp == 0 && lane == 0) prof_add(a, step_, layer_, 26, 1);
     if (a.world > 1) {
       // publish the super-chunk to every rank; each merges them itself
       const int par = xch_parity(a, step_, layer_);
@@ -765,8 +822,25 @@ struct Consumers {
       __threadfence();
       merge_range(F, a.supers + size_t(h) * a.n_super_max * kPartialFloats, 0, P.n_super, s, S);
       if (lane == 0) a.cnt[h] = 0;
+      if (lane == 0) prof_add(a, step_, layer_, 28, 1);
     }
     write_attn(h, F);
+  }
+
+  // Several super-chunks (long contexts): after a grid barrier, task
+  // (kv head g, local super-chunk s) goes to CTA task % grid, so the folds
+  // spread over the grid instead of landing on the items' last arrivers.
+  template <int BITS>
+  __device__ void merge_phase(const MegaLayer& L, const AttnPlan& P, int step_, int layer_) {
+    const int s_hi = min(a.super_hi, P.n_super);
+    const int n_local = max(0, s_hi - a.super_lo);
+    const int tasks = n_local * a.hkv;
+    const int item0 = a.token_base / (kAttBlock * P.nbi);
+    for (int t = blockIdx.x; t < tasks; t += gridDim.x) {
+      const int g = t % a.hkv, s = a.super_lo + t / a.hkv;
+      cons_sync();  // merge_range stages through the attention scratch
+      super_done<BITS>(L, P, g, s, item0, step_, layer_);
+    }
   }
 
   // world > 1: send this rank's expert slots of rows [o0, o1) to every other
@@ -858,27 +932,36 @@ struct Consumers {
   }
 
   // Merges partials [i0, i1) of a [*, kPartialFloats] array into P in order;
-  // entry `own` is taken from registers.  Loads go out kBatch at a time.
+  // entry `own` is taken from registers.  Chunks of 4 partials are copied
+  // into this warp's shared staging with cp.async (all in flight together),
+  // then merged from shared memory.  Callers keep the other warps away from
+  // the staging (it overlays the attention scratch).
   __device__ void merge_range(Partial4& P, const float* base, int i0, int i1, int own, const Partial4& own_p) {
-    constexpr int kBatch = 2;
-    for (int i = i0; i < i1; i += kBatch) {
-      Partial4 Q[kBatch];
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        const int ii = i + j;
-        if (ii < i1 && ii != own) {
-          const float* src = base + size_t(ii) * kPartialFloats;
-          Q[j].m = __ldcg(src);
-          Q[j].l = __ldcg(src + 1);
-          const float4 v = __ldcg(reinterpret_cast<const float4*>(src + 4) + lane);
-          Q[j].a[0] = v.x; Q[j].a[1] = v.y; Q[j].a[2] = v.z; Q[j].a[3] = v.w;
+    constexpr int kChunk = 4;
+    float(*stage)[kPartialFloats] = sm.att.u.stage[warp];
+    for (int i = i0; i < i1; i += kChunk) {
+      const int n = min(kChunk, i1 - i);
+      for (int j = 0; j < n; ++j) {
+        if (i + j == own) continue;
+        const float* src = base + size_t(i + j) * kPartialFloats;
+        cp_async_cg16(&stage[j][4 + 4 * lane], src + 4 + 4 * lane);
+        if (lane == 0) cp_async_cg16(&stage[j][0], src);  // m, l, pad, pad
+      }
+      cp_async_wait_all();
+      __syncwarp();
+      for (int j = 0; j < n; ++j) {
+        if (i + j == own) {
+          merge_into(P, own_p);
+          continue;
         }
+        Partial4 Q;
+        Q.m = stage[j][0];
+        Q.l = stage[j][1];
+        const float4 v = *reinterpret_cast<const float4*>(&stage[j][4 + 4 * lane]);
+        Q.a[0] = v.x; Q.a[1] = v.y; Q.a[2] = v.z; Q.a[3] = v.w;
+        merge_into(P, Q);
       }
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        const int ii = i + j;
-        if (ii < i1) merge_into(P, ii == own ? own_p : Q[j]);
-      }
+      __syncwarp();
     }
   }
 
@@ -1018,7 +1101,7 @@ struct Consumers {
             r += n;
           }
         }
-        if (!grid_barrier(a, bar_index(a, step, l, 0))) return;
+        if (!gbar(bar_index(a, step, l, 0))) return;
         // ---- A
         if (warp == 0 && lane == 0) stamp(a, step, l, 11);
         if (warp == 0 && lane == 0) sm.att.qg = -1;  // queries change every layer
@@ -1030,8 +1113,12 @@ struct Consumers {
           attn_item<BITS>(L, AP, pos, g, item, step, l);
           if (warp == 0 && lane == 0) stamp(a, step, l, 13);
         }
+        if (AP.n_super > 1) {
+          if (!gbar(kNoStamp)) return;
+          merge_phase<BITS>(L, AP, step, l);
+        }
         if (a.world > 1 && warp == 0) attn_final_sharded(L, AP, xch_parity(a, step, l));
-        if (!grid_barrier(a, bar_index(a, step, l, 1))) return;
+        if (!gbar(bar_index(a, step, l, 1))) return;
         // ---- O
         {
           const FixScale fo = load_x(a.attn, a.hq * 128);
@@ -1054,7 +1141,7 @@ struct Consumers {
             }
           }
         }
-        if (!grid_barrier(a, bar_index(a, step, l, 2))) return;
+        if (!gbar(bar_index(a, step, l, 2))) return;
         // ---- R
         const FixScale fr = norm(a.h, L.post_norm);
         {
@@ -1078,7 +1165,7 @@ struct Consumers {
             if (lane == 0) a.router_logits[e] = rbf(acc);
           }
         }
-        if (!grid_barrier(a, bar_index(a, step, l, 3))) return;
+        if (!gbar(bar_index(a, step, l, 3))) return;
         // ---- G: selection (same on every CTA), then gate/up pairs
         if (warp == 0 && lane == 0) stamp(a, step, l, 0);
         route(L, step, l);
@@ -1129,7 +1216,7 @@ struct Consumers {
           }
         }
         if (warp == 0 && lane == 0) stamp(a, step, l, 10);
-        if (!grid_barrier(a, bar_index(a, step, l, 4))) return;
+        if (!gbar(bar_index(a, step, l, 4))) return;
         // ---- D: down rows of all k experts, mix, residual
         {
           load_vec(sm.act, a.act, a.k * I);
@@ -1184,7 +1271,7 @@ struct Consumers {
             }
           }
         }
-        if (!grid_barrier(a, bar_index(a, step, l, 5))) return;
+        if (!gbar(bar_index(a, step, l, 5))) return;
       }
       // ---- H: final norm + lm_head + CTA argmax
       const FixScale fh = norm(a.h, a.final_norm);
@@ -1225,7 +1312,7 @@ struct Consumers {
           a.cand_idx[blockIdx.x] = bi;
         }
       }
-      if (!grid_barrier(a, bar_index(a, step, a.n_layers, 0))) return;
+      if (!gbar(bar_index(a, step, a.n_layers, 0))) return;
       // ---- E: global argmax (every CTA), bookkeeping (CTA 0)
       if (warp == 0) {
         float bv = -INFINITY;
