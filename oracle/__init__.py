@@ -43,6 +43,7 @@ def lib() -> C.CDLL:
         L.orc_exp.restype = C.c_float
         L.orc_exp.argtypes = [C.c_float]
         L.orc_exp_n.argtypes = [_f32p, _f32p, C.c_int64]
+        L.orc_aexp_n.argtypes = [_f32p, _f32p, C.c_int64]
         L.orc_quantize_affine.argtypes = [_f32p, C.c_int64, C.c_int, C.c_int, _u32p, _u16p, _u16p]
         L.orc_gemv_int4.argtypes = [_u32p, _u16p, _u16p, C.c_int, C.c_int64, C.c_int, _u16p, _u16p]
         L.orc_rmsnorm.argtypes = [_u16p, _u16p, C.c_int, C.c_float, _u16p]
@@ -56,6 +57,8 @@ def lib() -> C.CDLL:
         L.orc_partial_bytes.restype = C.c_int
         L.orc_attention_supers.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                            C.c_void_p, C.c_int]
+        L.orc_attention_supers_shard.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                 C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]
         L.orc_attention_final.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
         L.orc_sample.restype = C.c_int32
         L.orc_sample.argtypes = [_u16p, C.c_int64, C.c_void_p, C.c_int, C.c_void_p, _f32p]
@@ -100,6 +103,14 @@ def exp(x: np.ndarray) -> np.ndarray:
     x = np.ascontiguousarray(x, dtype=np.float32)
     y = np.empty_like(x)
     lib().orc_exp_n(x.ravel(), y.ravel(), x.size)
+    return y
+
+
+def aexp(x: np.ndarray) -> np.ndarray:
+    """The attention softmax exp (x <= 0; 0 at and below -87)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    lib().orc_aexp_n(x.ravel(), y.ravel(), x.size)
     return y
 
 
@@ -233,6 +244,25 @@ def attention_supers(q_bf16, kv: dict, n_kv_heads: int, capacity: int, bits: int
     assert L.orc_partial_bytes() == PARTIAL_FLOATS * 4
     L.orc_attention_supers(q.ctypes.data, C.addressof(rec), hq, n_kv_heads, capacity, bits, T, out.ctypes.data,
                            n_super)
+    return out
+
+
+def attention_supers_shard(q_bf16, kv: dict, n_kv_heads: int, capacity: int, bits: int, T: int, base: int,
+                           s_lo: int, s_hi: int):
+    """Super-chunk partials [Hq, s_hi - s_lo, 130] of super-chunks [s_lo, s_hi)
+    of a T-token context, from a cache slice holding tokens base, base+1, ...
+    (kv arrays [Hkv, capacity, ...]): what one rank of a split session owns."""
+    from rec_b200 import abi
+
+    q = np.ascontiguousarray(q_bf16, np.uint16)
+    hq = q.size // 128
+    arrs = [np.ascontiguousarray(kv[n]) for n in ("k_codes", "k_scales", "k_biases", "v_codes", "v_scales",
+                                                  "v_biases")]
+    rec = abi.RecKVLayer(*(a.ctypes.data for a in arrs))
+    out = np.zeros((hq, max(0, s_hi - s_lo), PARTIAL_FLOATS), np.float32)
+    if s_hi > s_lo:
+        lib().orc_attention_supers_shard(q.ctypes.data, C.addressof(rec), hq, n_kv_heads, capacity, bits, T, base,
+                                         s_lo, s_hi, out.ctypes.data)
     return out
 
 

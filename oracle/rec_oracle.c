@@ -122,6 +122,30 @@ static inline float rexp(float x) { return orc_exp(x); }
 ORC_API void orc_exp_n(const float* x, float* y, int64_t n) {
   for (int64_t i = 0; i < n; ++i) y[i] = orc_exp(x[i]);
 }
+/* Attention exp for x <= 0 (rec_b200/csrc/attn_core.cuh aexp): n from
+ * fma(x, log2e, 1.5*2^23), the same reduction and polynomial as orc_exp,
+ * 2^n in one step; x <= -87 (and -inf) gives 0. */
+ORC_API float orc_aexp(float x) {
+  if (!(x > -87.0f)) return 0.0f;
+  const float t = fmaf(x, 1.44269504088896341f, 12582912.0f);
+  const float n = t - 12582912.0f;
+  float r = fmaf(-n, 0.693145751953125f, x);
+  r = fmaf(-n, 1.42860682030941723e-6f, r);
+  float p = 1.98412698412698413e-4f;
+  p = fmaf(p, r, 1.38888888888888889e-3f);
+  p = fmaf(p, r, 8.33333333333333333e-3f);
+  p = fmaf(p, r, 4.16666666666666667e-2f);
+  p = fmaf(p, r, 1.66666666666666667e-1f);
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  const uint32_t sc = (f2u(t) + (uint32_t)(127 - 0x4B400000)) << 23;
+  return p * u2f(sc);
+}
+static inline float aexp(float x) { return orc_aexp(x); }
+ORC_API void orc_aexp_n(const float* x, float* y, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) y[i] = orc_aexp(x[i]);
+}
 static inline float rsigmoid(float g) {
   float tail = 1.0f / (1.0f + rexp(fabsf(g)));
   return g < 0.0f ? tail : 1.0f - tail;
@@ -419,7 +443,7 @@ static inline uint32_t kv_code(const uint32_t* row, int bits, int d) {
 }
 
 /* Prepared query of one head: qs = bf16(q / sqrt(128)); 16-bit fixed point
- * qi = rint(qs * 2^F), F = min(14 - exponent(max|qs|), 100); QS[g] = float of
+ * qi = rint(qs * 2^F), F = min(14 - exponent(max|qs| * (1 + 2^-7)), 100); QS[g] = float of
  * the exact sum of qi over group g; down = 2^-F. */
 typedef struct {
   int32_t qi[128];
@@ -434,8 +458,8 @@ static void prep_query(const uint16_t* q, QPrep* Q) {
     float a = fabsf(qs[d]);
     mx = a > mx ? a : mx;
   }
-  uint32_t u;
-  memcpy(&u, &mx, 4);
+  /* the factor 1 + 2^-7 keeps |qi| <= 32512: both byte limbs are signed */
+  uint32_t u = f2u(mx * 1.0078125f);
   int E = (int)((u >> 23) & 0xFF) - 127;
   int F = 14 - E;
   if (F > 100) F = 100;
@@ -461,15 +485,29 @@ static float att_score(const QPrep* Q, const uint32_t* krow, const uint16_t* ks,
   return rbf(t * Q->down);
 }
 
-/* Tile partial of one q head over tokens [t0, t0+32) ∩ [0, T), in the
- * kernels' fragment order (rec_b200/csrc/attn_core.cuh):
- *   m = max score; p_j = exp(s_j - m) (0 beyond T);
- *   l: v[gq] = (p[gq] + p[gq+8]) + (p[16+gq] + p[24+gq]), then a butterfly
- *      over gq = 0..7 (offsets 4, 2, 1);
- *   per V group (64 dims): w_j = p_j * scale_j; F = min(13 - exponent(max|w|),
- *      100); wq_j = rint(w_j * 2^F); acc_int_d = sum_j wq_j * code_jd (exact);
- *      B = sum of p_j * bias_j in the order of l; acc_d = fma(acc_int_d, 2^-F, B). */
-static void att_tile(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bits, int t0, int T, Partial* out) {
+/* Canonical tile sum (attn_core.cuh tile_sum): thread tq of a head holds
+ * v[2nt + j] = x[8nt + 2tq + j]; S_tq = ((v0+v1)+(v2+v3))+((v4+v5)+(v6+v7));
+ * result (S0+S1)+(S2+S3). */
+static float tile_sum(const float* x) {
+  float S[4];
+  for (int tq = 0; tq < 4; ++tq) {
+    float v[8];
+    for (int nt = 0; nt < 4; ++nt)
+      for (int j = 0; j < 2; ++j) v[2 * nt + j] = x[8 * nt + 2 * tq + j];
+    S[tq] = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+  }
+  return (S[0] + S[1]) + (S[2] + S[3]);
+}
+
+/* Folds the tile of one q head over tokens [t0, t0+32) ∩ [0, T) into the
+ * running state st (attn_core.cuh tile_fold):
+ *   m' = max(m, max score); alpha = aexp(m - m'); p_j = aexp(s_j - m') (0 beyond T);
+ *   l' = fma(l, alpha, tile_sum(p));
+ *   per V group (64 dims): w_j = p_j * scale_j, x_j = p_j * bias_j (0 beyond T);
+ *      F = min(14 - exponent(max|w| * (1 + 2^-7)), 100); wq_j = rint(w_j * 2^F);
+ *      acc_d' = fma(acc_d, alpha, fma(float(sum_j wq_j * code_jd), 2^-F, tile_sum(x))). */
+static void att_tile(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bits, int t0, int T, int base,
+                     Partial* st) {
   int words = 128 * bits / 32;
   const uint32_t* KC = (const uint32_t*)kv->k_codes;
   const uint32_t* VC = (const uint32_t*)kv->v_codes;
@@ -477,59 +515,51 @@ static void att_tile(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bit
   const uint16_t *VS = (const uint16_t*)kv->v_scales, *VB = (const uint16_t*)kv->v_biases;
   int nvalid = T - t0;
   if (nvalid > ATT_TILE) nvalid = ATT_TILE;
-  if (nvalid <= 0) {
-    p_empty(out);
-    return;
-  }
+  if (nvalid <= 0) return;
   float s[ATT_TILE], p[ATT_TILE];
-  float m = NEG_INF;
-  for (int j = 0; j < nvalid; ++j) {
-    int64_t slot = (int64_t)g * C + t0 + j;
-    s[j] = att_score(Q, KC + slot * words, KS + slot * 2, KB + slot * 2, bits);
-    m = s[j] > m ? s[j] : m;
+  float mt = NEG_INF;
+  for (int j = 0; j < ATT_TILE; ++j) {
+    int64_t slot = (int64_t)g * C + t0 - base + j;
+    s[j] = j < nvalid ? att_score(Q, KC + slot * words, KS + slot * 2, KB + slot * 2, bits) : NEG_INF;
+    mt = fmaxf(mt, s[j]);
   }
-  for (int j = 0; j < ATT_TILE; ++j) p[j] = j < nvalid ? rexp(s[j] - m) : 0.0f;
-  float v[8];
-  for (int q = 0; q < 8; ++q) v[q] = (p[q] + p[q + 8]) + (p[16 + q] + p[24 + q]);
-  bfly(v, 8);
-  out->m = m;
-  out->l = v[0];
+  const float mn = fmaxf(st->m, mt);
+  const float alpha = aexp(st->m - mn);
+  for (int j = 0; j < ATT_TILE; ++j) p[j] = aexp(s[j] - mn);
+  st->l = fmaf(st->l, alpha, tile_sum(p));
   for (int gr = 0; gr < 2; ++gr) {
     float w[ATT_TILE], x[ATT_TILE];
     float mx = 0.0f;
     for (int j = 0; j < ATT_TILE; ++j) {
-      int64_t slot = (int64_t)g * C + t0 + j;
+      int64_t slot = (int64_t)g * C + t0 - base + j;
       w[j] = j < nvalid ? p[j] * bf(VS[slot * 2 + gr]) : 0.0f;
       x[j] = j < nvalid ? p[j] * bf(VB[slot * 2 + gr]) : 0.0f;
-      float a = fabsf(w[j]);
-      mx = a > mx ? a : mx;
+      mx = fmaxf(mx, fabsf(w[j]));
     }
-    uint32_t u;
-    memcpy(&u, &mx, 4);
-    int E = (int)((u >> 23) & 0xFF) - 127;
-    int F = 13 - E;
+    int E = (int)((f2u(mx * 1.0078125f) >> 23) & 0xFF) - 127;
+    int F = 14 - E;
     if (F > 100) F = 100;
     float up = ldexpf(1.0f, F), down = ldexpf(1.0f, -F);
     int32_t wq[ATT_TILE];
     for (int j = 0; j < ATT_TILE; ++j) wq[j] = (int32_t)rintf(w[j] * up);
-    for (int q = 0; q < 8; ++q) v[q] = (x[q] + x[q + 8]) + (x[16 + q] + x[24 + q]);
-    bfly(v, 8);
-    const float B = v[0];
+    const float B = tile_sum(x);
     for (int d = 64 * gr; d < 64 * gr + 64; ++d) {
       int32_t acc = 0;
       for (int j = 0; j < nvalid; ++j) {
-        int64_t slot = (int64_t)g * C + t0 + j;
+        int64_t slot = (int64_t)g * C + t0 - base + j;
         acc += wq[j] * (int32_t)kv_code(VC + slot * words, bits, d);
       }
-      out->acc[d] = fmaf((float)acc, down, B);
+      st->acc[d] = fmaf(st->acc[d], alpha, fmaf((float)acc, down, B));
     }
   }
+  st->m = mn;
 }
 
 /* Partial of one q head over item it (blocks [nbi*it, nbi*it+nbi) ∩ blocks < T):
- * warp w folds tiles 8b + w of the item's blocks in order; the eight warp
- * states are folded as a tree ((w0 w1)(w2 w3))((w4 w5)(w6 w7)). */
-static void att_item(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bits, int it, int T, Partial* out) {
+ * warp w folds tiles 8b + w of the item's blocks in order into its running
+ * state; the eight warp states are folded as a tree ((w0 w1)(w2 w3))((w4 w5)(w6 w7)). */
+static void att_item(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bits, int it, int T, int base,
+                     Partial* out) {
   const int nbi = att_item_blocks((T + ATT_BLOCK - 1) / ATT_BLOCK);
   Partial st[ATT_WARPS];
   for (int w = 0; w < ATT_WARPS; ++w) {
@@ -537,9 +567,7 @@ static void att_item(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bit
     for (int b = it * nbi; b < (it + 1) * nbi; ++b) {
       int t0 = b * ATT_BLOCK + w * ATT_TILE;
       if (t0 >= T) break;
-      Partial P;
-      att_tile(Q, kv, g, C, bits, t0, T, &P);
-      p_merge(&st[w], &P);
+      att_tile(Q, kv, g, C, bits, t0, T, base, &st[w]);
     }
   }
   for (int step = 1; step < ATT_WARPS; step *= 2)
@@ -547,29 +575,39 @@ static void att_item(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bit
   *out = st[0];
 }
 
-/* Super-chunk partials of every q head: supers[h * n_super + s] = items of
- * super s (64 blocks) merged in order.  Tokens [0, T) of one
- * layer's cache. */
-ORC_API void orc_attention_supers(const uint16_t* q, const RecKVLayer* kv, int Hq, int Hkv, int C,
-                                  int bits, int T, Partial* supers, int n_super) {
+/* Super-chunk partials of every q head for super-chunks [s_lo, s_hi) of a
+ * context of T tokens (items and blocks numbered as for the whole context):
+ * supers[h * (s_hi - s_lo) + s - s_lo] = items of super s (64 blocks) merged
+ * in order.  The cache holds tokens from `base` on (token t in slot t - base
+ * of each head's C rows): a rank of a split session passes its own slice. */
+ORC_API void orc_attention_supers_shard(const uint16_t* q, const RecKVLayer* kv, int Hq, int Hkv, int C, int bits,
+                                        int T, int base, int s_lo, int s_hi, Partial* supers) {
   int nblocks = (T + ATT_BLOCK - 1) / ATT_BLOCK;
   int nbi = att_item_blocks(nblocks), per_super = ATT_SUPER / nbi;
   int nitems = (nblocks + nbi - 1) / nbi;
+  int ns = s_hi - s_lo;
 #pragma omp parallel for schedule(dynamic)
   for (int h = 0; h < Hq; ++h) {
     QPrep Q;
     prep_query(q + h * 128, &Q);
     int g = h / (Hq / Hkv);
-    for (int s = 0; s < n_super; ++s) {
-      Partial* S = &supers[h * n_super + s];
+    for (int s = s_lo; s < s_hi; ++s) {
+      Partial* S = &supers[h * ns + s - s_lo];
       p_empty(S);
       for (int it = s * per_super; it < (s + 1) * per_super && it < nitems; ++it) {
         Partial P;
-        att_item(&Q, kv, g, C, bits, it, T, &P);
+        att_item(&Q, kv, g, C, bits, it, T, base, &P);
         p_merge(S, &P);
       }
     }
   }
+}
+
+/* Super-chunk partials of every q head over tokens [0, T) of one layer's
+ * cache: supers[h * n_super + s]. */
+ORC_API void orc_attention_supers(const uint16_t* q, const RecKVLayer* kv, int Hq, int Hkv, int C,
+                                  int bits, int T, Partial* supers, int n_super) {
+  orc_attention_supers_shard(q, kv, Hq, Hkv, C, bits, T, 0, 0, n_super, supers);
 }
 
 ORC_API void orc_attention_final(const Partial* supers, int Hq, int n_super, const uint16_t* sinks,

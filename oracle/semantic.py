@@ -45,11 +45,13 @@ def rope(x: np.ndarray, pos: int, theta: float) -> np.ndarray:
     return np.concatenate([a * c - b * s, a * s + b * c], axis=1).astype(np.float32)
 
 
-def attention(q_bf16: np.ndarray, k: np.ndarray, v: np.ndarray, sinks=None) -> np.ndarray:
+def attention(q_bf16: np.ndarray, k: np.ndarray, v: np.ndarray, sinks=None, bf16_probs: bool = True) -> np.ndarray:
     """quantized_attention_with_sinks (model.py:108-139) for one query token.
     q: [Hq, 128] bf16 (post-RoPE); k, v: dequantised float [Hkv, T, 128].
     Scores are rounded to bf16 (the quantized matmul returns bf16), softmax in
-    fp32 over [scores, sink], probabilities rounded to bf16 before P*V."""
+    fp32 over [scores, sink], probabilities rounded to bf16 before P*V
+    (bf16_probs=False keeps them in float64: the exact softmax of the bf16
+    scores)."""
     hq = q_bf16.shape[0]
     hkv = k.shape[0]
     rep = hq // hkv
@@ -62,7 +64,7 @@ def attention(q_bf16: np.ndarray, k: np.ndarray, v: np.ndarray, sinks=None) -> n
         allv = np.concatenate([sc, sink])
         p = np.exp(allv - allv.max())
         p = p / p.sum()
-        p = rbf(p[: sc.size].astype(np.float32)).astype(np.float64)
+        p = rbf(p[: sc.size].astype(np.float32)).astype(np.float64) if bf16_probs else p[: sc.size]
         out[h] = (p @ v[g].astype(np.float64)).astype(np.float32)
     return out
 

@@ -53,9 +53,9 @@ __host__ __device__ inline int items_cap(int capacity) { return capacity / kAttB
 
 // Shared-memory scratch of the attention items of one CTA.
 struct AttnScratch {
-  QHead qh[kHeadsPerKv];
+  QFrags qf;                               // queries of the 8 heads
   union alignas(16) {
-    uint8_t wbuf[kAttWarps][1024];         // per-warp fixed-point PV weights
+    uint8_t wbuf[kAttWarps][1024];         // per-warp scratch of the query / new-row preparation
     float tree[kAttWarps / 2][36][32];     // warp states during the tree fold
     float stage[kAttWarps][4][kPartialFloats];  // per-warp partials being merged
   } u;
@@ -76,8 +76,7 @@ __device__ __forceinline__ void prep_q_heads(const uint16_t* qkv, int g, const f
   if (q_norm) head_norm4(x, q_norm, eps);
   float* scratch = reinterpret_cast<float*>(sc.u.wbuf[warp]);
   rope4(x, cs, scratch);
-  prep_qhead<BITS>(x, sc.qh[warp], scratch);
-  __syncwarp();
+  prep_qhead<BITS>(x, sc.qf, warp, reinterpret_cast<int*>(scratch));
 }
 
 // The new token's K and V of kv head g, RoPE'd (K) and quantized into the
@@ -159,25 +158,19 @@ __device__ __forceinline__ void warps_fold(WarpState& st, int warp, AttnScratch&
     auto slot = [&](int recv) { return step == 1 ? recv / 2 : (step == 2 ? recv / 2 + 1 : 3); };
     if ((warp & (2 * step - 1)) == step) {
       float(*d)[32] = sc.u.tree[slot(warp - step)];
+      d[0][lane] = st.m;
+      d[1][lane] = st.l;
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        d[hh][lane] = st.m[hh];
-        d[2 + hh][lane] = st.l[hh];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) d[4 + 16 * hh + i][lane] = st.acc[hh][i];
-      }
+      for (int i = 0; i < 32; ++i) d[2 + i][lane] = st.acc[i];
     }
     sync();
     if ((warp & (2 * step - 1)) == 0) {
       const float(*d)[32] = sc.u.tree[slot(warp)];
       WarpState y;
+      y.m = d[0][lane];
+      y.l = d[1][lane];
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        y.m[hh] = d[hh][lane];
-        y.l[hh] = d[2 + hh][lane];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) y.acc[hh][i] = d[4 + 16 * hh + i][lane];
-      }
+      for (int i = 0; i < 32; ++i) y.acc[i] = d[2 + i][lane];
       state_merge(st, y);
     }
   }
@@ -188,15 +181,16 @@ __device__ __forceinline__ void warps_fold(WarpState& st, int warp, AttnScratch&
 template <int BITS>
 __device__ __forceinline__ void store_item(const WarpState& st, float* dst, size_t head_stride) {
   const int lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
+  float* d = dst + size_t(gq) * head_stride;
+  if (tq == 0) {
+    d[0] = st.m;
+    d[1] = st.l;
+  }
 #pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    float* d = dst + size_t(2 * tq + hh) * head_stride;
-    if (gq == 0) {
-      d[0] = st.m[hh];
-      d[1] = st.l[hh];
-    }
-#pragma unroll
-    for (int li = 0; li < 16; ++li) d[4 + dim_of<BITS>(li, gq)] = st.acc[hh][li];
+  for (int r = 0; r < 4; ++r) {  // dims 64(r>>1) + 16tq + 8(r&1) + 0..7
+    float4* o = reinterpret_cast<float4*>(d + 4 + 64 * (r >> 1) + 16 * tq + 8 * (r & 1));
+    o[0] = make_float4(st.acc[8 * r], st.acc[8 * r + 1], st.acc[8 * r + 2], st.acc[8 * r + 3]);
+    o[1] = make_float4(st.acc[8 * r + 4], st.acc[8 * r + 5], st.acc[8 * r + 6], st.acc[8 * r + 7]);
   }
 }
 
@@ -204,15 +198,15 @@ __device__ __forceinline__ void store_item(const WarpState& st, float* dst, size
 // (n tokens of the block valid; new_row >= 0: that row is the new token).
 template <int BITS>
 __device__ __forceinline__ void block_tiles(uint32_t* kc, uint16_t* ks, uint16_t* kb, uint32_t* vc, uint16_t* vs,
-                                            uint16_t* vb, int n, int new_row, const AttnScratch& sc, uint8_t* wbuf,
-                                            int warp, WarpState& st) {
+                                            uint16_t* vb, int n, int new_row, const AttnScratch& sc, int warp,
+                                            WarpState& st) {
   constexpr int RW = 128 * BITS / 32;
   const int t0 = warp * kAttTile;
   const int nvalid = min(kAttTile, n - t0);
   if (nvalid <= 0) return;
   if (new_row >= t0 && new_row < t0 + kAttTile) patch_row<BITS>(kc, ks, kb, vc, vs, vb, new_row, sc);
-  tile_fold<BITS>(kc + t0 * RW, ks + 2 * t0, kb + 2 * t0, vc + t0 * RW, vs + 2 * t0, vb + 2 * t0, nvalid, sc.qh,
-                  wbuf, st);
+  tile_fold<BITS>(kc + t0 * RW, ks + 2 * t0, kb + 2 * t0, vc + t0 * RW, vs + 2 * t0, vb + 2 * t0, nvalid, sc.qf,
+                  st);
 }
 
 // ---------------------------------------------------------------------------
@@ -311,7 +305,7 @@ __global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnAr
       const int n = min(kAttBlock, T - b * kAttBlock);
       const int new_row = (has_new && p / kAttBlock == b) ? p - b * kAttBlock : -1;
       AttnStage<BITS>& S = sm.st[s];
-      block_tiles<BITS>(S.kc, S.ks, S.kb, S.vc, S.vs, S.vb, n, new_row, sm.sc, sm.sc.u.wbuf[warp], warp, st);
+      block_tiles<BITS>(S.kc, S.ks, S.kb, S.vc, S.vs, S.vb, n, new_row, sm.sc, warp, st);
       // the tile may have been patched through the generic proxy, and the
       // next bulk copy into this stage must not overtake this block's reads
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -5,17 +5,19 @@
 // Canonical order (restated by oracle/rec_oracle.c):
 //   * q is RoPE'd (pairs (i, i+64), fp32 cos/sin table), scaled and rounded:
 //     qs = bf16(q * 1/sqrt(128)).  Each head gets a 16-bit fixed point:
-//     F = min(14 - exponent(max|qs|), 100), qi = rint(qs * 2^F);
+//     F = min(14 - exponent(max|qs| * (1 + 2^-7)), 100), qi = rint(qs * 2^F);
 //     QS_g = sum of qi over group g (64 dims), exact.
 //   * score(t) = bf16(fma(b1, QS1, fma(s1, D1, fma(b0, QS0, s0*D0))) * 2^-F)
 //     with D_g = sum_d qi_d * code_d exact (int32) and s, b the token's K
 //     scale/bias of group g.
-//   * a block of 256 tokens is 8 tiles of 32; warp w of 8 owns tile w:
-//     m = tile max; p_t = exp(s_t - m); l = butterfly-sum(p);
-//     acc = sum_t fma(p_t, v_t, acc) in token order, v = fma(scale, code, bias).
-//   * block partial = warps merged in order; super-chunk = 64 blocks merged in
-//     order; final = [sink (sink, 1, 0)] then super-chunks in order;
-//     merge: m = max; a_i = exp(m_i - m); l = fma(l1, a1, l2*a2);
+//   * a block of 256 tokens is 8 tiles of 32; warp w folds tile w of each
+//     block of a work item into a running (m, l, acc) state (tile_fold):
+//     m' = max(m, tile max); alpha = aexp(m - m'); p = aexp(s - m');
+//     l' = fma(l, alpha, sum p); acc' = fma(acc, alpha, PV) with PV from
+//     fixed-point weights (exact integer dot, one rounding per dim).
+//   * item partial = the 8 warp states folded as a tree; super-chunk = its
+//     items merged in order; final = [sink (sink, 1, 0)] then super-chunks in
+//     order; merge: m = max; a_i = exp(m_i - m); l = fma(l1, a1, l2*a2);
 //     acc = fma(acc1, a1, acc2*a2); an empty side is the identity.
 //   * out = bf16(acc / l).
 // Reference: model.py:108-139 (scores, sink, softmax), megakernel.py:619-693
@@ -133,110 +135,85 @@ __device__ __forceinline__ void rope4(float (&x)[4], const float* cs, float* scr
   __syncwarp();
 }
 
-// Prepared query of one head in shared memory: byte limbs in the layout of
-// the K code words (8-bit: word w = dims 4w..4w+3; 4-bit: word w = dims
-// 8w..8w+7 split in even / odd nibble lanes).
-struct QHead {
-  uint32_t hi[32], lo[32];  // 8-bit: [w]; 4-bit: [2w] even, [2w+1] odd
-  float QS[2];              // float(sum qi) per group, exact
-  float down;               // 2^-F
-  float pad;
-};
-
-// One warp prepares head h: x = its (normed, RoPE'd) dims 4l..4l+3.
-template <int BITS>
-__device__ __forceinline__ void prep_qhead(const float (&x)[4], QHead& q, float* scratch) {
-  const int lane = threadIdx.x & 31;
-  float qs[4];
-  float mx = 0.0f;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    qs[j] = rbf(__fmul_rn(x[j], kQScale));
-    mx = fmaxf(mx, fabsf(qs[j]));
-  }
-  mx = bfly_max(mx);
-  const int E = int((__float_as_uint(mx) >> 23) & 0xFF) - 127;
-  int F = 14 - E;
-  F = F > 100 ? 100 : F;
-  const float up = __uint_as_float(uint32_t(F + 127) << 23);
-  int qi[4];
-  int part = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    qi[j] = __float2int_rn(__fmul_rn(qs[j], up));
-    part += qi[j];
-  }
-  // group sums: lanes 0..15 hold group 0, 16..31 group 1 (exact integers)
-#pragma unroll
-  for (int off = 8; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
-  if (lane == 0) q.QS[0] = float(part);
-  if (lane == 16) q.QS[1] = float(part);
-  if (lane == 0) q.down = __uint_as_float(uint32_t(127 - F) << 23);
-  if constexpr (BITS == 8) {
-    // lane l owns dims 4l..4l+3 = word l
-    uint32_t h = 0, lo = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      h |= (uint32_t(qi[j] >> 8) & 0xFFu) << (8 * j);
-      lo |= (uint32_t(qi[j]) & 0xFFu) << (8 * j);
-    }
-    q.hi[lane] = h;
-    q.lo[lane] = lo;
-  } else {
-    // word w = dims 8w..8w+7: even dims from lanes 2w (dims 0,2) and 2w+1
-    // (dims 4,6); odd dims likewise.  Exchange through the scratch.
-    int* si = reinterpret_cast<int*>(scratch);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) si[4 * lane + j] = qi[j];
-    __syncwarp();
-    if (lane < 16) {
-      const int w = lane;
-      uint32_t he = 0, ho = 0, le = 0, lo = 0;
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        const int ve = si[8 * w + 2 * q4], vo = si[8 * w + 2 * q4 + 1];
-        he |= (uint32_t(ve >> 8) & 0xFFu) << (8 * q4);
-        ho |= (uint32_t(vo >> 8) & 0xFFu) << (8 * q4);
-        le |= (uint32_t(ve) & 0xFFu) << (8 * q4);
-        lo |= (uint32_t(vo) & 0xFFu) << (8 * q4);
-      }
-      q.hi[2 * w] = he;
-      q.hi[2 * w + 1] = ho;
-      q.lo[2 * w] = le;
-      q.lo[2 * w + 1] = lo;
-    }
-    __syncwarp();
-  }
+// ---------------------------------------------------------------------------
+// Exp of the attention softmax, for x <= 0 (a score minus a running max, or
+// the difference of two running maxima).  Cody-Waite reduction with a 16-bit
+// head of ln2; the integer n = rint(x*log2e) comes from the fused
+// multiply-add fma(x, log2e, 1.5*2^23) (one rounding), whose bits also give
+// the scale 2^n; e^r by the degree-7 Taylor polynomial in Horner form.
+// Results below 2^-125 (x <= -87) are flushed to 0; exp(-inf) = 0.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float aexp(float x) {
+  if (!(x > -87.0f)) return 0.0f;
+  const float t = __fmaf_rn(x, 1.44269504088896341f, 12582912.0f);
+  const float n = __fsub_rn(t, 12582912.0f);
+  float r = __fmaf_rn(-n, 0.693145751953125f, x);
+  r = __fmaf_rn(-n, 1.42860682030941723e-6f, r);
+  float p = 1.98412698412698413e-4f;
+  p = __fmaf_rn(p, r, 1.38888888888888889e-3f);
+  p = __fmaf_rn(p, r, 8.33333333333333333e-3f);
+  p = __fmaf_rn(p, r, 4.16666666666666667e-2f);
+  p = __fmaf_rn(p, r, 1.66666666666666667e-1f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  // bits(t) = 0x4B400000 + n  ->  exponent field n + 127
+  const uint32_t sc = (__float_as_uint(t) + uint32_t(127 - 0x4B400000)) << 23;
+  return __fmul_rn(p, __uint_as_float(sc));
 }
 
 // ---------------------------------------------------------------------------
-// Tile computation on the tensor cores (integer mma.sync m16n8k32).  Scores
-// D_g = sum qi*code and the PV dot sum wq*code are exact int32 sums, so the
-// MMA gives the same bits as any other summation order.
-//
-// Fragment layout (lane = 4*gq + tq):
-//   A 16x32 (row): a0 = A[gq][4tq..], a1 = A[gq+8][4tq..], a2 = A[gq][16+4tq..],
-//                  a3 = A[gq+8][16+4tq..]  (four 8-bit values per register)
-//   B 32x8  (col): b0 = B[4tq..][gq], b1 = B[16+4tq..][gq]
+// Tile computation on the tensor cores (integer mma.sync m16n8k32, signed
+// A, unsigned B).  Fragment layout (lane = 4*gq + tq):
+//   A 16x32 (row): a0 = A[gq][4tq..+3], a1 = A[gq+8][4tq..+3],
+//                  a2 = A[gq][16+4tq..+3], a3 = A[gq+8][16+4tq..+3]
+//   B 32x8  (col): b0 = B[4tq..+3][gq], b1 = B[16+4tq..+3][gq]
 //   C 16x8:        c0 = C[gq][2tq], c1 = C[gq][2tq+1], c2 = C[gq+8][2tq],
 //                  c3 = C[gq+8][2tq+1]
-// A thread owns the tile's tokens gq, gq+8, 16+gq, 24+gq and the heads 2tq,
-// 2tq+1; for PV it owns 16 dims: dim_of(li) below.
+// (byte i of a register = k index 4tq+i, resp. 16+4tq+i).
+//
+// A rows gq and gq+8 carry the high and low signed byte limbs of head gq
+// (v = 256*hi + lo, hi = (v+128)>>8), so a thread owns one head: gq.
+//   scores:  A = query limbs, B = K codes of n-tile nt (tokens 8nt..8nt+7);
+//            the thread gets head gq, tokens 8nt+2tq, 8nt+2tq+1.
+//   PV:      A = fixed-point weights of the thread's own 8 tokens (k index
+//            4tq+i <-> token 8(i>>1)+2tq+(i&1), 16+4tq+i <-> that + 16),
+//            B = V codes (n-tile nt: column n = dim 8n+nt of group 0, nt < 8,
+//            or 64+8n+(nt-8)); the thread gets dims 16tq+{0..15} and
+//            64+16tq+{0..15} of head gq.
+// The K dims are permuted within a k-step (qk_dim) so that a thread's B
+// registers come straight from its code words; the query uses the same
+// permutation.  All integer sums are exact, so the permutations and the MMA
+// summation order do not change any result.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void mma_s8u8(int (&c)[4], const uint4& a, uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ void mma_u8u8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+
+// Dim of K/query k index (k-step ks, thread tq, side r: 0 = k 4tq+i, 1 = k
+// 16+4tq+i, byte i).  4-bit: word w = 8(ks>>1) + 2tq + (ks&1), low nibbles
+// (even dims) on side 0, high nibbles on side 1.  8-bit: words w0 = 16(ks>>1)
+// + 4tq + 2(ks&1) (side 0) and w0+1 (side 1).  k-steps 0,1 cover group 0.
+template <int BITS>
+__host__ __device__ __forceinline__ int qk_dim(int ks, int tq, int r, int i) {
+  if constexpr (BITS == 4) {
+    const int w = 8 * (ks >> 1) + 2 * tq + (ks & 1);
+    return 8 * w + 2 * i + r;
+  } else {
+    const int w = 16 * (ks >> 1) + 4 * tq + 2 * (ks & 1) + r;
+    return 4 * w + i;
+  }
 }
+
+// Prepared queries of the 8 heads of a kv head: A fragments per k-step and
+// lane (head lane>>2), and per head (QS0, QS1, 2^-F, 0).
+struct QFrags {
+  uint4 frag[4][32];
+  float4 meta[8];
+};
 
 // 4x4 byte transpose: r_k = byte k of w0..w3 (w0 in the low byte).
 __device__ __forceinline__ void transpose4(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, uint32_t& r0,
@@ -249,282 +226,266 @@ __device__ __forceinline__ void transpose4(uint32_t w0, uint32_t w1, uint32_t w2
   r3 = __byte_perm(x1, x3, 0x7632);
 }
 
-// PV dims of a thread: local index li (0..15) -> dim.
+// Signed byte limbs of v (|v| <= 32639): hi = (v + 128) >> 8, lo = v - 256 hi.
+__device__ __forceinline__ uint32_t limb_hi(int v) { return uint32_t((v + 128) >> 8) & 0xFFu; }
+__device__ __forceinline__ uint32_t limb_lo(int v) { return uint32_t(v) & 0xFFu; }
+
+// One warp prepares head `head` (0..7) of the kv head: x = its (normed,
+// RoPE'd) dims 4l..4l+3.  scratch: 512 bytes of the warp's shared memory.
+//   qs = bf16(x / sqrt(128)); F = min(14 - exponent(max|qs| * (1 + 2^-7)), 100)
+//   (keeps |qi| <= 32512, so both limbs are signed bytes); qi = rint(qs 2^F);
+//   QS_g = exact sum of qi over group g.
 template <int BITS>
-__device__ __forceinline__ int dim_of(int li, int gq) {
-  if constexpr (BITS == 8) return 32 * (li >> 2) + 4 * gq + (li & 3);
-  else return 64 * (li >> 3) + 8 * gq + (li & 7);
+__device__ __forceinline__ void prep_qhead(const float (&x)[4], QFrags& q, int head, int* scratch) {
+  const int lane = threadIdx.x & 31;
+  float qs[4];
+  float mx = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    qs[j] = rbf(__fmul_rn(x[j], kQScale));
+    mx = fmaxf(mx, fabsf(qs[j]));
+  }
+  mx = bfly_max(mx);
+  const int E = int((__float_as_uint(__fmul_rn(mx, 1.0078125f)) >> 23) & 0xFF) - 127;
+  int F = 14 - E;
+  F = F > 100 ? 100 : F;
+  const float up = __uint_as_float(uint32_t(F + 127) << 23);
+  int part = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int qi = __float2int_rn(__fmul_rn(qs[j], up));
+    scratch[4 * lane + j] = qi;
+    part += qi;
+  }
+  // group sums: lanes 0..15 hold group 0, 16..31 group 1 (exact integers)
+#pragma unroll
+  for (int off = 8; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+  const int qs1 = __shfl_sync(0xffffffffu, part, 16);
+  if (lane == 0) q.meta[head] = make_float4(float(part), float(qs1), __uint_as_float(uint32_t(127 - F) << 23), 0.0f);
+  __syncwarp();
+  if (lane < 16) {
+    const int ks = lane >> 2, tq = lane & 3;
+    uint32_t r[4] = {0, 0, 0, 0};  // a0 (hi, side 0), a1 (lo, side 0), a2, a3
+#pragma unroll
+    for (int side = 0; side < 2; ++side)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int v = scratch[qk_dim<BITS>(ks, tq, side, i)];
+        r[2 * side] |= limb_hi(v) << (8 * i);
+        r[2 * side + 1] |= limb_lo(v) << (8 * i);
+      }
+    q.frag[ks][4 * head + tq] = make_uint4(r[0], r[1], r[2], r[3]);
+  }
+  __syncwarp();
 }
 
-// Running (m, l, acc) of one warp for heads 2tq, 2tq+1 and the thread's dims.
+// Running state of one warp: head gq of the kv head, dims 16tq + (0..15) and
+// 64 + 16tq + (0..15): acc[16 grp + 8 c + k] = dim 64 grp + 16 tq + 8 c + k.
 struct WarpState {
-  float m[2], l[2];
-  float acc[2][16];
+  float m, l;
+  float acc[32];
 };
 __device__ __forceinline__ void state_empty(WarpState& s) {
+  s.m = -INFINITY;
+  s.l = 0.0f;
 #pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    s.m[hh] = -INFINITY;
-    s.l[hh] = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) s.acc[hh][i] = 0.0f;
-  }
+  for (int i = 0; i < 32; ++i) s.acc[i] = 0.0f;
 }
-// x <- x (+) y for one head (the merge rule of merge_into).
+// x <- x (+) y (the merge rule of merge_into).
 __device__ __forceinline__ void state_merge(WarpState& x, const WarpState& y) {
-#pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    if (y.m[hh] == -INFINITY) continue;
-    if (x.m[hh] == -INFINITY) {
-      x.m[hh] = y.m[hh];
-      x.l[hh] = y.l[hh];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) x.acc[hh][i] = y.acc[hh][i];
-      continue;
-    }
-    const float m = fmaxf(x.m[hh], y.m[hh]);
-    const float a1 = rexp(__fsub_rn(x.m[hh], m)), a2 = rexp(__fsub_rn(y.m[hh], m));
-    x.l[hh] = __fmaf_rn(x.l[hh], a1, __fmul_rn(y.l[hh], a2));
-#pragma unroll
-    for (int i = 0; i < 16; ++i) x.acc[hh][i] = __fmaf_rn(x.acc[hh][i], a1, __fmul_rn(y.acc[hh][i], a2));
-    x.m[hh] = m;
+  if (y.m == -INFINITY) return;
+  if (x.m == -INFINITY) {
+    x = y;
+    return;
   }
+  const float m = fmaxf(x.m, y.m);
+  const float a1 = rexp(__fsub_rn(x.m, m)), a2 = rexp(__fsub_rn(y.m, m));
+  x.l = __fmaf_rn(x.l, a1, __fmul_rn(y.l, a2));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) x.acc[i] = __fmaf_rn(x.acc[i], a1, __fmul_rn(y.acc[i], a2));
+  x.m = m;
 }
+__device__ __forceinline__ int state_dim(int i, int tq) { return 64 * (i >> 4) + 16 * tq + (i & 15); }
 
-__device__ __forceinline__ float sum_tokens(float v00, float v01, float v10, float v11) {
-  // (t[gq] + t[gq+8]) + (t[16+gq] + t[24+gq]), then a butterfly over gq
-  float s = __fadd_rn(__fadd_rn(v00, v01), __fadd_rn(v10, v11));
-  s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 16));
-  s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 8));
-  s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 4));
-  return s;
+// Sum over the 32 tokens of a tile of the values v[2nt + j] (token 8nt + 2tq
+// + j) of the 4 threads of a head: ((v0+v1)+(v2+v3)) + ((v4+v5)+(v6+v7)) per
+// thread, then (S0+S1)+(S2+S3) by a butterfly over tq.
+__device__ __forceinline__ float tile_sum(const float (&v)[8]) {
+  float s = __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3])),
+                      __fadd_rn(__fadd_rn(v[4], v[5]), __fadd_rn(v[6], v[7])));
+  s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 1));
+  return __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, 2));
 }
-__device__ __forceinline__ float max_tokens(float v) {
-  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
-  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
-  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
-  return v;
+__device__ __forceinline__ float tile_max(const float (&v)[8]) {
+  float m = fmaxf(fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3])), fmaxf(fmaxf(v[4], v[5]), fmaxf(v[6], v[7])));
+  m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+  return fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
 }
 
 // One tile of 32 tokens (rows of the K and V tiles in shared memory, row
-// stride RW words; scales/biases [token][2]) for the 8 q heads in qh, folded
-// into the warp state.  nvalid: tokens of the tile below T (1..32).
-// wbuf: 1 KB of the warp's shared memory.
+// stride RW words; scales/biases [token][2], 8-byte aligned) for the 8 q
+// heads, folded into the warp state (canonical order):
+//   s_t = score of token t (0..nvalid-1), -inf beyond;
+//   m' = max(m, max_t s_t); alpha = aexp(m - m'); p_t = aexp(s_t - m');
+//   l' = fma(l, alpha, tile_sum(p));
+//   per V group: w_t = p_t scale_t, x_t = p_t bias_t (0 beyond nvalid);
+//     F = min(14 - exponent(max|w| (1 + 2^-7)), 100); wq_t = rint(w_t 2^F)
+//     (|wq| <= 32514: signed byte limbs);
+//     acc_d' = fma(acc_d, alpha, fma(float(sum_t wq_t code_td), 2^-F, tile_sum(x))).
 template <int BITS>
 __device__ __forceinline__ void tile_fold(const uint32_t* kc, const uint16_t* ks, const uint16_t* kb,
                                           const uint32_t* vc, const uint16_t* vs, const uint16_t* vb, int nvalid,
-                                          const QHead* qh, uint8_t* wbuf, WarpState& st) {
+                                          const QFrags& qf, WarpState& st) {
   constexpr int RW = 128 * BITS / 32;
+  constexpr uint32_t M4 = 0x0F0F0F0Fu;
   const int lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
-  // ---- scores: C[group][half][limb]
-  int C[2][2][2][4];
+  // ---- scores: C[group][nt]
+  int C[2][4][4];
 #pragma unroll
   for (int g = 0; g < 2; ++g)
 #pragma unroll
-    for (int hf = 0; hf < 2; ++hf)
+    for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-      for (int lb = 0; lb < 2; ++lb)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) C[g][hf][lb][e] = 0;
-#pragma unroll
-  for (int kq = 0; kq < 4; ++kq) {
-    const uint32_t bh0 = qh[gq].hi[8 * kq + tq], bh1 = qh[gq].hi[8 * kq + 4 + tq];
-    const uint32_t bl0 = qh[gq].lo[8 * kq + tq], bl1 = qh[gq].lo[8 * kq + 4 + tq];
-#pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-      const uint32_t* r0 = kc + (16 * hf + gq) * RW;
-      const uint32_t* r1 = r0 + 8 * RW;
-      uint32_t a0, a1, a2, a3;
-      if constexpr (BITS == 8) {
-        a0 = r0[8 * kq + tq];
-        a1 = r1[8 * kq + tq];
-        a2 = r0[8 * kq + 4 + tq];
-        a3 = r1[8 * kq + 4 + tq];
-      } else {
-        const int w0 = 4 * kq + (tq >> 1), w2 = w0 + 2, sh = (tq & 1) * 4;
-        a0 = (r0[w0] >> sh) & 0x0F0F0F0Fu;
-        a1 = (r1[w0] >> sh) & 0x0F0F0F0Fu;
-        a2 = (r0[w2] >> sh) & 0x0F0F0F0Fu;
-        a3 = (r1[w2] >> sh) & 0x0F0F0F0Fu;
-      }
-      mma_u8s8(C[kq >> 1][hf][0], a0, a1, a2, a3, bh0, bh1);
-      mma_u8u8(C[kq >> 1][hf][1], a0, a1, a2, a3, bl0, bl1);
-    }
-  }
-  // ---- scores, tile max, p, l   (element e = 2r + hh: token 16hf + 8r + gq, head 2tq + hh)
-  float p[2][2][2];  // [hf][r][hh]
-  float mt[2];
+      for (int e = 0; e < 4; ++e) C[g][nt][e] = 0;
   {
-    float sc[2][2][2];
-    float QS0[2], QS1[2], dn[2];
+    uint4 A[4];
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      QS0[hh] = qh[2 * tq + hh].QS[0];
-      QS1[hh] = qh[2 * tq + hh].QS[1];
-      dn[hh] = qh[2 * tq + hh].down;
-    }
+    for (int k = 0; k < 4; ++k) A[k] = qf.frag[k][lane];
 #pragma unroll
-    for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int j = 16 * hf + 8 * r + gq;
-        const uint32_t sp = *reinterpret_cast<const uint32_t*>(ks + 2 * j);
-        const uint32_t bp = *reinterpret_cast<const uint32_t*>(kb + 2 * j);
-        const float s0 = __uint_as_float(sp << 16), s1 = __uint_as_float(sp & 0xFFFF0000u);
-        const float b0 = __uint_as_float(bp << 16), b1 = __uint_as_float(bp & 0xFFFF0000u);
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int e = 2 * r + hh;
-          const int D0 = C[0][hf][0][e] * 256 + C[0][hf][1][e];
-          const int D1 = C[1][hf][0][e] * 256 + C[1][hf][1][e];
-          float t = __fmaf_rn(b0, QS0[hh], __fmul_rn(s0, float(D0)));
-          t = __fmaf_rn(s1, float(D1), t);
-          t = __fmaf_rn(b1, QS1[hh], t);
-          sc[hf][r][hh] = j < nvalid ? rbf(__fmul_rn(t, dn[hh])) : -INFINITY;
-        }
+    for (int nt = 0; nt < 4; ++nt) {
+      const uint32_t* row = kc + (8 * nt + gq) * RW;
+      if constexpr (BITS == 4) {
+        const uint2 x = *reinterpret_cast<const uint2*>(row + 2 * tq);
+        const uint2 y = *reinterpret_cast<const uint2*>(row + 8 + 2 * tq);
+        mma_s8u8(C[0][nt], A[0], x.x & M4, (x.x >> 4) & M4);
+        mma_s8u8(C[0][nt], A[1], x.y & M4, (x.y >> 4) & M4);
+        mma_s8u8(C[1][nt], A[2], y.x & M4, (y.x >> 4) & M4);
+        mma_s8u8(C[1][nt], A[3], y.y & M4, (y.y >> 4) & M4);
+      } else {
+        const uint4 x = *reinterpret_cast<const uint4*>(row + 4 * tq);
+        const uint4 y = *reinterpret_cast<const uint4*>(row + 16 + 4 * tq);
+        mma_s8u8(C[0][nt], A[0], x.x, x.y);
+        mma_s8u8(C[0][nt], A[1], x.z, x.w);
+        mma_s8u8(C[1][nt], A[2], y.x, y.y);
+        mma_s8u8(C[1][nt], A[3], y.z, y.w);
       }
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      float m = fmaxf(fmaxf(sc[0][0][hh], sc[0][1][hh]), fmaxf(sc[1][0][hh], sc[1][1][hh]));
-      m = max_tokens(m);
-      mt[hh] = m;
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          const int j = 16 * hf + 8 * r + gq;
-          p[hf][r][hh] = j < nvalid ? rexp(__fsub_rn(sc[hf][r][hh], m)) : 0.0f;
-        }
     }
   }
-  float lt[2];
+  // ---- scores of head gq, tokens 8nt + 2tq + j  (v = 2nt + j)
+  float p[8];
+  float alpha;
+  {
+    const float4 meta = qf.meta[gq];
 #pragma unroll
-  for (int hh = 0; hh < 2; ++hh) lt[hh] = sum_tokens(p[0][0][hh], p[0][1][hh], p[1][0][hh], p[1][1][hh]);
-  // merge factors of the state and the tile
-  float as[2], at[2];
-  bool first[2];
+    for (int nt = 0; nt < 4; ++nt) {
+      const int t = 8 * nt + 2 * tq;
+      const uint2 sp = *reinterpret_cast<const uint2*>(ks + 2 * t);
+      const uint2 bp = *reinterpret_cast<const uint2*>(kb + 2 * t);
 #pragma unroll
-  for (int hh = 0; hh < 2; ++hh) {
-    first[hh] = st.m[hh] == -INFINITY;
-    const float m = first[hh] ? mt[hh] : fmaxf(st.m[hh], mt[hh]);
-    as[hh] = first[hh] ? 0.0f : rexp(__fsub_rn(st.m[hh], m));
-    at[hh] = first[hh] ? 1.0f : rexp(__fsub_rn(mt[hh], m));
-    st.l[hh] = first[hh] ? lt[hh] : __fmaf_rn(st.l[hh], as[hh], __fmul_rn(lt[hh], at[hh]));
-    st.m[hh] = m;
+      for (int j = 0; j < 2; ++j) {
+        const uint32_t sw = j ? sp.y : sp.x, bw = j ? bp.y : bp.x;
+        const float s0 = __uint_as_float(sw << 16), s1 = __uint_as_float(sw & 0xFFFF0000u);
+        const float b0 = __uint_as_float(bw << 16), b1 = __uint_as_float(bw & 0xFFFF0000u);
+        const int D0 = C[0][nt][j] * 256 + C[0][nt][2 + j];
+        const int D1 = C[1][nt][j] * 256 + C[1][nt][2 + j];
+        float u = __fmaf_rn(b0, meta.x, __fmul_rn(s0, float(D0)));
+        u = __fmaf_rn(s1, float(D1), u);
+        u = __fmaf_rn(b1, meta.y, u);
+        p[2 * nt + j] = t + j < nvalid ? rbf(__fmul_rn(u, meta.z)) : -INFINITY;
+      }
+    }
+    const float mt = tile_max(p);
+    const float mn = fmaxf(st.m, mt);
+    alpha = aexp(__fsub_rn(st.m, mn));
+    st.m = mn;
+#pragma unroll
+    for (int v = 0; v < 8; ++v) p[v] = aexp(__fsub_rn(p[v], mn));
+    st.l = __fmaf_rn(st.l, alpha, tile_sum(p));
   }
-  // ---- PV per V group: fixed-point weights, exact integer dot, fold
+  // ---- PV per V group
+  uint2 vsp[4], vbp[4];
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    const int t = 8 * nt + 2 * tq;
+    vsp[nt] = *reinterpret_cast<const uint2*>(vs + 2 * t);
+    vbp[nt] = *reinterpret_cast<const uint2*>(vb + 2 * t);
+  }
 #pragma unroll
   for (int g = 0; g < 2; ++g) {
-    float dnw[2], B[2];
-    float vsc[2][2], vbi[2][2];  // V scale / bias of the thread's tokens, group g
+    float w[8], x[8];
+    float mx = 0.0f;
 #pragma unroll
-    for (int hf = 0; hf < 2; ++hf)
+    for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int j = 16 * hf + 8 * r + gq;
-        vsc[hf][r] = bf(vs[2 * j + g]);
-        vbi[hf][r] = bf(vb[2 * j + g]);
+      for (int j = 0; j < 2; ++j) {
+        const int v = 2 * nt + j;
+        const uint32_t sw = j ? vsp[nt].y : vsp[nt].x, bw = j ? vbp[nt].y : vbp[nt].x;
+        const float sc = __uint_as_float(g ? (sw & 0xFFFF0000u) : (sw << 16));
+        const float bi = __uint_as_float(g ? (bw & 0xFFFF0000u) : (bw << 16));
+        const bool ok = 8 * nt + 2 * tq + j < nvalid;
+        w[v] = ok ? __fmul_rn(p[v], sc) : 0.0f;
+        x[v] = ok ? __fmul_rn(p[v], bi) : 0.0f;
+        mx = fmaxf(mx, fabsf(w[v]));
       }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const int E = int((__float_as_uint(__fmul_rn(mx, 1.0078125f)) >> 23) & 0xFF) - 127;
+    int F = 14 - E;
+    F = F > 100 ? 100 : F;
+    const float up = __uint_as_float(uint32_t(F + 127) << 23);
+    const float dn = __uint_as_float(uint32_t(127 - F) << 23);
+    const float B = tile_sum(x);
+    // wq = rint(w 2^F) as bits 0x4B400000 + wq of fma(w, 2^F, 1.5*2^23);
+    // byte 0 of those bits is the low limb, byte 1 of (bits + 128) the high.
+    uint32_t lo[8], hp[8];
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      float w[2][2], x[2][2];
-      float mx = 0.0f;
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          const int j = 16 * hf + 8 * r + gq;
-          const bool v = j < nvalid;
-          w[hf][r] = v ? __fmul_rn(p[hf][r][hh], vsc[hf][r]) : 0.0f;
-          x[hf][r] = v ? __fmul_rn(p[hf][r][hh], vbi[hf][r]) : 0.0f;
-          mx = fmaxf(mx, fabsf(w[hf][r]));
-        }
-      mx = max_tokens(mx);
-      const int E = int((__float_as_uint(mx) >> 23) & 0xFF) - 127;
-      int F = 13 - E;
-      F = F > 100 ? 100 : F;
-      const float up = __uint_as_float(uint32_t(F + 127) << 23);
-      dnw[hh] = __uint_as_float(uint32_t(127 - F) << 23);
-      B[hh] = sum_tokens(x[0][0], x[0][1], x[1][0], x[1][1]);
-      // limbs -> wbuf[limb][head][token] bytes
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          const int j = 16 * hf + 8 * r + gq, head = 2 * tq + hh;
-          const int q = __float2int_rn(__fmul_rn(w[hf][r], up));
-          wbuf[head * 32 + j] = uint8_t((q >> 8) & 0xFF);
-          wbuf[256 + head * 32 + j] = uint8_t(q & 0xFF);
-        }
+    for (int v = 0; v < 8; ++v) {
+      lo[v] = __float_as_uint(__fmaf_rn(w[v], up, 12582912.0f));
+      hp[v] = lo[v] + 128u;
     }
-    __syncwarp();
-    const uint32_t* wb32 = reinterpret_cast<const uint32_t*>(wbuf);
-    const uint32_t bh0 = wb32[gq * 8 + tq], bh1 = wb32[gq * 8 + 4 + tq];
-    const uint32_t bl0 = wb32[64 + gq * 8 + tq], bl1 = wb32[64 + gq * 8 + 4 + tq];
-    int P[4][2][4];  // [block][limb][e]
+    uint4 Aw;
+    Aw.x = __byte_perm(__byte_perm(hp[0], hp[1], 0x0051), __byte_perm(hp[2], hp[3], 0x0051), 0x5410);
+    Aw.y = __byte_perm(__byte_perm(lo[0], lo[1], 0x0040), __byte_perm(lo[2], lo[3], 0x0040), 0x5410);
+    Aw.z = __byte_perm(__byte_perm(hp[4], hp[5], 0x0051), __byte_perm(hp[6], hp[7], 0x0051), 0x5410);
+    Aw.w = __byte_perm(__byte_perm(lo[4], lo[5], 0x0040), __byte_perm(lo[6], lo[7], 0x0040), 0x5410);
+    // V codes of the thread's tokens: side 0 = tokens 2tq, 2tq+1, 8+2tq,
+    // 9+2tq; side 1 = those + 16.  Transposed to (dim, 4 tokens) bytes.
+    uint32_t bt[2][8];  // [side][nt & 7]
 #pragma unroll
-    for (int bk = 0; bk < 4; ++bk)
+    for (int side = 0; side < 2; ++side) {
+      const int tb = 16 * side + 2 * tq;
+      const int rows[4] = {tb, tb + 1, tb + 8, tb + 9};
+      if constexpr (BITS == 4) {
+        uint32_t wv[4];
 #pragma unroll
-      for (int lb = 0; lb < 2; ++lb)
+        for (int i = 0; i < 4; ++i) wv[i] = vc[rows[i] * RW + 8 * g + gq];
+        uint32_t r[4];
+        transpose4(wv[0], wv[1], wv[2], wv[3], r[0], r[1], r[2], r[3]);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) P[bk][lb][e] = 0;
-    if constexpr (BITS == 8) {
-      // 32-dim groups p = 2g, 2g+1: words (8p + gq) of tokens 4tq+i and 16+4tq+i
-#pragma unroll
-      for (int pp = 0; pp < 2; ++pp) {
-        const int wi = 8 * (2 * g + pp) + gq;
-        uint32_t r0, r1, r2, r3, s0, s1, s2, s3;
-        transpose4(vc[(4 * tq + 0) * RW + wi], vc[(4 * tq + 1) * RW + wi], vc[(4 * tq + 2) * RW + wi],
-                   vc[(4 * tq + 3) * RW + wi], r0, r1, r2, r3);
-        transpose4(vc[(16 + 4 * tq + 0) * RW + wi], vc[(16 + 4 * tq + 1) * RW + wi],
-                   vc[(16 + 4 * tq + 2) * RW + wi], vc[(16 + 4 * tq + 3) * RW + wi], s0, s1, s2, s3);
-        mma_u8s8(P[2 * pp][0], r0, r1, s0, s1, bh0, bh1);
-        mma_u8u8(P[2 * pp][1], r0, r1, s0, s1, bl0, bl1);
-        mma_u8s8(P[2 * pp + 1][0], r2, r3, s2, s3, bh0, bh1);
-        mma_u8u8(P[2 * pp + 1][1], r2, r3, s2, s3, bl0, bl1);
-      }
-    } else {
-      const int wi = 8 * g + gq;
-      uint32_t w4[4], z4[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        w4[i] = vc[(4 * tq + i) * RW + wi];
-        z4[i] = vc[(16 + 4 * tq + i) * RW + wi];
-      }
-      uint32_t e0, e1, e2, e3, o0, o1, o2, o3, f0, f1, f2, f3, q0, q1, q2, q3;
-      transpose4(w4[0] & 0x0F0F0F0Fu, w4[1] & 0x0F0F0F0Fu, w4[2] & 0x0F0F0F0Fu, w4[3] & 0x0F0F0F0Fu, e0, e1, e2, e3);
-      transpose4((w4[0] >> 4) & 0x0F0F0F0Fu, (w4[1] >> 4) & 0x0F0F0F0Fu, (w4[2] >> 4) & 0x0F0F0F0Fu,
-                 (w4[3] >> 4) & 0x0F0F0F0Fu, o0, o1, o2, o3);
-      transpose4(z4[0] & 0x0F0F0F0Fu, z4[1] & 0x0F0F0F0Fu, z4[2] & 0x0F0F0F0Fu, z4[3] & 0x0F0F0F0Fu, f0, f1, f2, f3);
-      transpose4((z4[0] >> 4) & 0x0F0F0F0Fu, (z4[1] >> 4) & 0x0F0F0F0Fu, (z4[2] >> 4) & 0x0F0F0F0Fu,
-                 (z4[3] >> 4) & 0x0F0F0F0Fu, q0, q1, q2, q3);
-      // blocks: dims (+0,+2), (+4,+6), (+1,+3), (+5,+7) of the thread's 8
-      mma_u8s8(P[0][0], e0, e1, f0, f1, bh0, bh1);
-      mma_u8u8(P[0][1], e0, e1, f0, f1, bl0, bl1);
-      mma_u8s8(P[1][0], e2, e3, f2, f3, bh0, bh1);
-      mma_u8u8(P[1][1], e2, e3, f2, f3, bl0, bl1);
-      mma_u8s8(P[2][0], o0, o1, q0, q1, bh0, bh1);
-      mma_u8u8(P[2][1], o0, o1, q0, q1, bl0, bl1);
-      mma_u8s8(P[3][0], o2, o3, q2, q3, bh0, bh1);
-      mma_u8u8(P[3][1], o2, o3, q2, q3, bl0, bl1);
-    }
-    __syncwarp();
-    // element (block bk, row r, head hh) -> local dim li
-#pragma unroll
-    for (int bk = 0; bk < 4; ++bk)
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        int li;
-        if constexpr (BITS == 8) li = 8 * g + 4 * (bk >> 1) + 2 * (bk & 1) + r;
-        else li = 8 * g + (bk == 0 ? 2 * r : bk == 1 ? 4 + 2 * r : bk == 2 ? 1 + 2 * r : 5 + 2 * r);
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int e = 2 * r + hh;
-          const int acc_int = P[bk][0][e] * 256 + P[bk][1][e];
-          const float v = __fmaf_rn(float(acc_int), dnw[hh], B[hh]);
-          st.acc[hh][li] = first[hh] ? v : __fmaf_rn(st.acc[hh][li], as[hh], __fmul_rn(v, at[hh]));
+        for (int k = 0; k < 4; ++k) {
+          bt[side][2 * k] = r[k] & M4;
+          bt[side][2 * k + 1] = (r[k] >> 4) & M4;
         }
+      } else {
+        uint2 wv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) wv[i] = *reinterpret_cast<const uint2*>(vc + rows[i] * RW + 16 * g + 2 * gq);
+        transpose4(wv[0].x, wv[1].x, wv[2].x, wv[3].x, bt[side][0], bt[side][1], bt[side][2], bt[side][3]);
+        transpose4(wv[0].y, wv[1].y, wv[2].y, wv[3].y, bt[side][4], bt[side][5], bt[side][6], bt[side][7]);
       }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      int P[4] = {0, 0, 0, 0};
+      mma_s8u8(P, Aw, bt[0][k], bt[1][k]);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int ai = P[c] * 256 + P[2 + c];
+        const float v = __fmaf_rn(float(ai), dn, B);
+        float& a = st.acc[16 * g + 8 * c + k];
+        a = __fmaf_rn(a, alpha, v);
+      }
+    }
   }
 }
 

@@ -742,8 +742,7 @@ struct Consumers {
       uint32_t* vc = reinterpret_cast<uint32_t*>(vt);
       uint16_t* vs = reinterpret_cast<uint16_t*>(vt + n4 * RW * 4);
       const int new_row = (has_new && pos / kAttBlock == b) ? pos - b * kAttBlock : -1;
-      block_tiles<BITS>(kc, ks, ks + n4 * 2, vc, vs, vs + n4 * 2, n, new_row, sm.att, sm.att.u.wbuf[warp], warp,
-                        st);
+      block_tiles<BITS>(kc, ks, ks + n4 * 2, vc, vs, vs + n4 * 2, n, new_row, sm.att, warp, st);
       if (warp == 0 && lane == 0 && b == b0) stamp(a, step_, layer_, 16);
       slot = kslot;
       release(true);

@@ -24,6 +24,54 @@ def test_exp_accuracy_and_edges():
     assert np.isnan(oracle.exp(np.array([np.nan], np.float32))[0])
 
 
+def test_attention_exp_accuracy_and_edges():
+    rng = np.random.default_rng(1)
+    x = np.concatenate([rng.uniform(-86.9, 0.0, 200000), rng.uniform(-1, 0, 100000),
+                        np.array([0.0, -0.0, -1e-30, -0.5, -86.99])]).astype(np.float32)
+    y = oracle.aexp(x).astype(np.float64)
+    ref = np.exp(x.astype(np.float64))
+    ulp = np.spacing(ref.astype(np.float32)).astype(np.float64)
+    err = np.abs(y - ref) / ulp
+    assert err.max() <= 2.0, err.max()
+    assert oracle.aexp(np.array([0.0], np.float32))[0] == 1.0
+    z = oracle.aexp(np.array([-87.0, -100.0, -np.inf], np.float32))
+    assert (z == 0.0).all()
+
+
+@pytest.mark.parametrize("T,bits,sinks", [(1, 4, False), (37, 8, True), (300, 4, True), (2049, 8, False),
+                                          (20000, 4, True)])
+def test_attention_canonical_vs_semantic(T, bits, sinks):
+    """The canonical fixed-point attention on a quantized cache against the
+    exact softmax of the bf16 scores (float64): per head, its rel-L2 error
+    stays within 2x the larger of the reference semantics' own error (bf16
+    probabilities) and the bf16 rounding of the exact output.  (Rounding the
+    scores to bf16 makes them sensitive to the fp32 summation order: any two
+    implementations differ in ~0.5% of the rounded scores at long contexts.)"""
+    hq, hkv = 16, 2
+    rng = np.random.default_rng(T + bits)
+    cap = (T + 255) // 256 * 256
+    kv, deq = {}, {}
+    for n in ("k", "v"):
+        x = oracle.bf16_to_f32(oracle.f32_to_bf16(rng.standard_normal((hkv, T, 128), dtype=np.float32)))
+        c, s, b = oracle.quantize(x, bits, 1)
+        kv[f"{n}_codes"] = np.zeros((hkv, cap, c.shape[-1]), np.uint32)
+        kv[f"{n}_scales"] = np.zeros((hkv, cap, 2), np.uint16)
+        kv[f"{n}_biases"] = np.zeros((hkv, cap, 2), np.uint16)
+        kv[f"{n}_codes"][:, :T], kv[f"{n}_scales"][:, :T], kv[f"{n}_biases"][:, :T] = c, s, b
+        deq[n] = oracle.dequantize(c, s, b, bits, 1).reshape(hkv, T, 128)
+    q = oracle.f32_to_bf16(3.0 * rng.standard_normal(hq * 128, dtype=np.float32))
+    sk = oracle.f32_to_bf16(rng.standard_normal(hq, dtype=np.float32)) if sinks else None
+    n_super = -(-((T + 255) // 256) // 64)
+    got = oracle.bf16_to_f32(oracle.attention_final(
+        oracle.attention_supers(q, kv, hkv, cap, bits, T, n_super), sk)).reshape(hq, 128)
+    sem = semantic.attention(q.reshape(hq, 128), deq["k"], deq["v"], sk)
+    exact = semantic.attention(q.reshape(hq, 128), deq["k"], deq["v"], sk, bf16_probs=False)
+    for h in range(hq):
+        bound = 2.0 * max(semantic.rel_l2(sem[h], exact[h]), semantic.rel_l2(semantic.rbf(exact[h]), exact[h]))
+        err = semantic.rel_l2(got[h], exact[h])
+        assert err <= bound, (h, err, bound)
+
+
 def _mlx_affine_numpy(w: np.ndarray, bits: int):
     """Vectorised numpy restatement of mx.quantize(mode='affine') in float32."""
     g = w.reshape(-1, 64).astype(np.float32)

@@ -68,15 +68,14 @@ def _worker(rank, world, port, q):
         qv = oracle.f32_to_bf16(rng.standard_normal(HQ * 128, dtype=np.float32))
         sinks = oracle.f32_to_bf16(rng.standard_normal(HQ, dtype=np.float32))
         p = shard.plan(world, rank, 16, CAP)
-        # attention over this rank's super-chunks only
+        # attention over this rank's super-chunks only (its own cache slice;
+        # items and tiles numbered as for the whole context)
         lo, hi = p.token_base, p.token_end
-        t_local = max(0, min(T, hi) - lo)
-        n_local = max(0, -(-t_local // shard.SUPER_TOKENS))
-        if n_local:
-            local = {n: np.ascontiguousarray(a[:, lo:hi]) for n, a in kv.items()}
-            sup = oracle.attention_supers(qv, local, HKV, hi - lo, BITS, t_local, n_local)
-        else:
-            sup = np.zeros((HQ, 0, oracle.PARTIAL_FLOATS), np.float32)
+        n_super = -(-T // shard.SUPER_TOKENS)
+        s_lo, s_hi = min(p.super_lo, n_super), min(p.super_hi, n_super)
+        n_local = s_hi - s_lo
+        local = {n: np.ascontiguousarray(a[:, lo:hi]) for n, a in kv.items()}
+        sup = oracle.attention_supers_shard(qv, local, HKV, hi - lo, BITS, T, lo, s_lo, s_hi)
         # exchange: every rank gathers every rank's super-chunk partials
         counts = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
         dist.all_gather(counts, torch.tensor([n_local]))
