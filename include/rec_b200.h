@@ -190,7 +190,7 @@ REC_API int rec_launch_kernel(RecCtx* ctx, int32_t kind, int32_t layer, void* st
  * (megakernel.py:151,1269-1299).  NULL disables. */
 REC_API int rec_set_profile(RecCtx* ctx, void* buf_dev, size_t entries);
 /* Optional stamps inside one layer (step 0 of a launch) of the persistent
- * kernel: uint64 [cta][32] %globaltimer values at fixed points of the
+ * kernel: uint64 [cta][64] %globaltimer values at fixed points of the
  * attention and expert phases (diagnostics; no reference counterpart). */
 REC_API int rec_set_layer_profile(RecCtx* ctx, void* buf_dev, int32_t layer);
 /* Reads the device status word (synchronises `stream`).  Non-zero marks the

@@ -144,54 +144,60 @@ __device__ __forceinline__ void patch_row(uint32_t* kc, uint16_t* ks, uint16_t* 
   __syncwarp();
 }
 
-// Tree fold of the 8 warp states; warp 0 ends with the item state.  All
-// warps call it (sync: a barrier over the 8 warps) after a barrier that ends
-// every warp's tiles: the tree scratch overlays the per-warp PV buffers.
-// Slots: level 1 senders w = 1,3,5,7 write slot w/2; level 2 senders 2, 6
-// write slots 1, 3 and level 3 sender 4 writes slot 3 -- each a slot that only
-// the sender itself read in the level before, so one barrier per level.
+// Tree fold of the 8 warp states ((w0 w1)(w2 w3))((w4 w5)(w6 w7)) and the
+// store of the item partial of heads 0..7 to dst + head * head_stride (m, l,
+// pad, pad, acc[128]).  All warps call it (sync: a barrier over the 8 warps)
+// after a barrier that ends every warp's tiles: the scratch overlays the
+// per-warp buffers.  Level 1 goes through the scratch in the thread layout
+// (senders 1,3,5,7 write slot w/2); receivers 0,2,4,6 rewrite their slot as
+// [head][m, l, pad, pad, dim]; then warp w folds head w's four level-1
+// states in registers (lane l: dims 4l..4l+3) and stores it.
 template <typename Sync>
-__device__ __forceinline__ void warps_fold(WarpState& st, int warp, AttnScratch& sc, Sync sync) {
-  const int lane = threadIdx.x & 31;
-  for (int step = 1; step < kAttWarps; step *= 2) {
-    // slot of the pair (receiver w, sender w + step) at this level
-    auto slot = [&](int recv) { return step == 1 ? recv / 2 : (step == 2 ? recv / 2 + 1 : 3); };
-    if ((warp & (2 * step - 1)) == step) {
-      float(*d)[32] = sc.u.tree[slot(warp - step)];
-      d[0][lane] = st.m;
-      d[1][lane] = st.l;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) d[2 + i][lane] = st.acc[i];
-    }
-    sync();
-    if ((warp & (2 * step - 1)) == 0) {
-      const float(*d)[32] = sc.u.tree[slot(warp)];
-      WarpState y;
-      y.m = d[0][lane];
-      y.l = d[1][lane];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) y.acc[i] = d[2 + i][lane];
-      state_merge(st, y);
-    }
-  }
-}
-
-// Warp 0: the item state of heads h0 .. h0+7 into dst + head * head_stride
-// (m, l, pad, pad, acc[128]).
-template <int BITS>
-__device__ __forceinline__ void store_item(const WarpState& st, float* dst, size_t head_stride) {
+__device__ __forceinline__ void warps_fold_store(WarpState& st, int warp, AttnScratch& sc, Sync sync, float* dst,
+                                                 size_t head_stride) {
   const int lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
-  float* d = dst + size_t(gq) * head_stride;
-  if (tq == 0) {
-    d[0] = st.m;
-    d[1] = st.l;
-  }
+  float(*d)[32] = sc.u.tree[warp >> 1];
+  if (warp & 1) {
+    d[0][lane] = st.m;
+    d[1][lane] = st.l;
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {  // dims 64(r>>1) + 16tq + 8(r&1) + 0..7
-    float4* o = reinterpret_cast<float4*>(d + 4 + 64 * (r >> 1) + 16 * tq + 8 * (r & 1));
-    o[0] = make_float4(st.acc[8 * r], st.acc[8 * r + 1], st.acc[8 * r + 2], st.acc[8 * r + 3]);
-    o[1] = make_float4(st.acc[8 * r + 4], st.acc[8 * r + 5], st.acc[8 * r + 6], st.acc[8 * r + 7]);
+    for (int i = 0; i < 32; ++i) d[2 + i][lane] = st.acc[i];
   }
+  sync();
+  if (!(warp & 1)) {
+    WarpState y;
+    y.m = d[0][lane];
+    y.l = d[1][lane];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) y.acc[i] = d[2 + i][lane];
+    state_merge(st, y);
+    __syncwarp();  // the slot is rewritten below: every lane has read it
+    float* hs = &d[0][0] + gq * kPartialFloats;
+    if (tq == 0) {
+      hs[0] = st.m;
+      hs[1] = st.l;
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {  // dims 64(r>>1) + 16tq + 8(r&1) + 0..7
+      float4* o = reinterpret_cast<float4*>(hs + 4 + 64 * (r >> 1) + 16 * tq + 8 * (r & 1));
+      o[0] = make_float4(st.acc[8 * r], st.acc[8 * r + 1], st.acc[8 * r + 2], st.acc[8 * r + 3]);
+      o[1] = make_float4(st.acc[8 * r + 4], st.acc[8 * r + 5], st.acc[8 * r + 6], st.acc[8 * r + 7]);
+    }
+  }
+  sync();
+  Partial4 q[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const float* hs = &sc.u.tree[r][0][0] + warp * kPartialFloats;
+    q[r].m = hs[0];
+    q[r].l = hs[1];
+    const float4 v = *reinterpret_cast<const float4*>(hs + 4 + 4 * lane);
+    q[r].a[0] = v.x; q[r].a[1] = v.y; q[r].a[2] = v.z; q[r].a[3] = v.w;
+  }
+  merge_into(q[0], q[1]);
+  merge_into(q[2], q[3]);
+  merge_into(q[0], q[2]);
+  store_partial(dst + size_t(warp) * head_stride, q[0]);
 }
 
 // This warp's tile (tile `warp`) of one block held in the given K / V tiles
@@ -278,7 +284,7 @@ __global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnAr
   const int items = n_items * a.hkv;
   const float* cs = a.rope + size_t(p) * 128;
   const int icap = items_cap(a.capacity);
-  uint32_t phase[2] = {0, 0};
+  uint32_t phase = 0;  // bit s: parity of stage s
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
     const int g = it % a.hkv, item = it / a.hkv;
     const int b0 = item * nbi, b1 = min(b0 + nbi, nblk);
@@ -299,8 +305,8 @@ __global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnAr
     for (int b = b0; b < b1; ++b) {
       const int s = (b - b0) & 1;
       if (threadIdx.x == 0 && b + 1 < b1) issue_block<BITS>(sm, s ^ 1, a, g, b + 1, T);
-      ok = mbar_wait(&sm.bar[s], phase[s]) && ok;
-      phase[s] ^= 1;
+      ok = mbar_wait(&sm.bar[s], (phase >> s) & 1u) && ok;
+      phase ^= 1u << s;
       if (!__syncthreads_and(ok)) break;
       const int n = min(kAttBlock, T - b * kAttBlock);
       const int new_row = (has_new && p / kAttBlock == b) ? p - b * kAttBlock : -1;
@@ -314,14 +320,12 @@ __global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnAr
     if (!ok) {
       if (threadIdx.x == 0) {
         report(a.status, kStatusBulkTimeout);
-        for (int s = 0; s < 2; ++s) mbar_wait(&sm.bar[s], phase[s]);
+        for (int s = 0; s < 2; ++s) mbar_wait(&sm.bar[s], (phase >> s) & 1u);
       }
       return;
     }
-    warps_fold(st, warp, sm.sc, CtaSync{});
-    if (warp == 0)
-      store_item<BITS>(st, a.partials + (size_t(g * kHeadsPerKv) * icap + item) * kPartialFloats,
-                       size_t(icap) * kPartialFloats);
+    warps_fold_store(st, warp, sm.sc, CtaSync{}, a.partials + (size_t(g * kHeadsPerKv) * icap + item) * kPartialFloats,
+                     size_t(icap) * kPartialFloats);
     __syncthreads();
   }
 }

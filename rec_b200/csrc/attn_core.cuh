@@ -51,8 +51,12 @@ struct Partial4 {  // lane-distributed partial: dims 4*lane .. 4*lane+3
 __device__ __forceinline__ void merge_into(Partial4& x, const Partial4& y) {
   if (y.m == -INFINITY) return;
   if (x.m == -INFINITY) { x = y; return; }
-  const float m = fmaxf(x.m, y.m);
-  const float a1 = rexp(__fsub_rn(x.m, m)), a2 = rexp(__fsub_rn(y.m, m));
+  // the factor of the side holding the max is exp(0) = 1: only the other
+  // one is computed
+  const bool xm = x.m >= y.m;
+  const float m = xm ? x.m : y.m;
+  const float e = rexp(__fsub_rn(xm ? y.m : x.m, m));
+  const float a1 = xm ? 1.0f : e, a2 = xm ? e : 1.0f;
   x.l = __fmaf_rn(x.l, a1, __fmul_rn(y.l, a2));
 #pragma unroll
   for (int j = 0; j < 4; ++j) x.a[j] = __fmaf_rn(x.a[j], a1, __fmul_rn(y.a[j], a2));
@@ -215,6 +219,19 @@ struct QFrags {
   float4 meta[8];
 };
 
+// 4x4 byte transpose with the pairs (w0, w1), (w2, w3) given in either
+// order: selectors (0x5140, 0x7362) for the natural order, (0x1504, 0x3726)
+// for swapped pairs.
+__device__ __forceinline__ void transpose4s(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, uint32_t sa,
+                                            uint32_t sb, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  const uint32_t x0 = __byte_perm(w0, w1, sa), x1 = __byte_perm(w0, w1, sb);
+  const uint32_t x2 = __byte_perm(w2, w3, sa), x3 = __byte_perm(w2, w3, sb);
+  r0 = __byte_perm(x0, x2, 0x5410);
+  r1 = __byte_perm(x0, x2, 0x7632);
+  r2 = __byte_perm(x1, x3, 0x5410);
+  r3 = __byte_perm(x1, x3, 0x7632);
+}
+
 // 4x4 byte transpose: r_k = byte k of w0..w3 (w0 in the low byte).
 __device__ __forceinline__ void transpose4(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, uint32_t& r0,
                                            uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -298,8 +315,10 @@ __device__ __forceinline__ void state_merge(WarpState& x, const WarpState& y) {
     x = y;
     return;
   }
-  const float m = fmaxf(x.m, y.m);
-  const float a1 = rexp(__fsub_rn(x.m, m)), a2 = rexp(__fsub_rn(y.m, m));
+  const bool xm = x.m >= y.m;
+  const float m = xm ? x.m : y.m;
+  const float e = rexp(__fsub_rn(xm ? y.m : x.m, m));
+  const float a1 = xm ? 1.0f : e, a2 = xm ? e : 1.0f;
   x.l = __fmaf_rn(x.l, a1, __fmul_rn(y.l, a2));
 #pragma unroll
   for (int i = 0; i < 32; ++i) x.acc[i] = __fmaf_rn(x.acc[i], a1, __fmul_rn(y.acc[i], a2));
@@ -456,11 +475,15 @@ __device__ __forceinline__ void tile_fold(const uint32_t* kc, const uint16_t* ks
       const int tb = 16 * side + 2 * tq;
       const int rows[4] = {tb, tb + 1, tb + 8, tb + 9};
       if constexpr (BITS == 4) {
+        // odd tq reads each row pair in swapped order: the four threads of a
+        // column then hit two rows of each parity (two bank halves)
+        const int odd = tq & 1;
         uint32_t wv[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) wv[i] = vc[rows[i] * RW + 8 * g + gq];
+        for (int i = 0; i < 4; ++i) wv[i] = vc[(tb + 8 * (i >> 1) + ((i & 1) ^ odd)) * RW + 8 * g + gq];
         uint32_t r[4];
-        transpose4(wv[0], wv[1], wv[2], wv[3], r[0], r[1], r[2], r[3]);
+        transpose4s(wv[0], wv[1], wv[2], wv[3], odd ? 0x1504u : 0x5140u, odd ? 0x3726u : 0x7362u, r[0], r[1], r[2],
+                    r[3]);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           bt[side][2 * k] = r[k] & M4;

@@ -35,6 +35,7 @@ constexpr int kMegaCons = 8;                        // consumer warps
 constexpr int kMegaThreads = 32 * (kMegaCons + 1);  // + producer warp
 constexpr int kSlotBytes = 36864;
 constexpr int kSlots = 4;
+constexpr int kMergeChunk = 8;  // partials per head in one merge slot (8 heads x 8 x 528 B)
 constexpr int kBarCons = 1;   // named barrier: all consumer warps
 constexpr int kBarTeam0 = 2;  // named barriers 2..5: warp pairs (K = 4096 rows)
 constexpr int kQRows = 32;    // rows per Q / H chunk (K = 2048)
@@ -125,7 +126,7 @@ struct MegaArgs {
   XchLayout xl;
   uint8_t* xch[kMaxWorld];
   unsigned long long* prof;  // optional: [barrier][cta] x (arrive, release) globaltimer stamps
-  unsigned long long* prof2; // optional: [cta][32] stamps inside layer prof_layer of step 0
+  unsigned long long* prof2; // optional: [cta][64] stamps inside layer prof_layer of step 0
   int prof_layer;
 };
 
@@ -146,8 +147,10 @@ struct MegaSmem {
   float seg_part[kMegaCons][4];
   float best_val[kMegaCons];
   int best_idx[kMegaCons];
-  float route_p[kMaxExperts];
-  float route_c[kMaxExperts];
+  float gX[kMaxTopK * 16];   // exact group sums of the shared fixed-point limbs
+  float dmax[kMaxTopK];      // D: max |activation| per selected expert
+  alignas(16) float route_p[kMaxExperts];
+  alignas(16) float route_c[kMaxExperts];
   int ids[kMaxTopK];
   float wts[kMaxTopK];
   int loc[kMaxTopK];   // selection slots whose expert is local, in slot order
@@ -158,9 +161,13 @@ struct MegaSmem {
   uint64_t full[kSlots], empty[kSlots];
   uint16_t hown[kDRowsMax];  // this CTA's rows of h (it owns them in embed, O and D)
   volatile int route_seq;
+  volatile int merge_seq;  // 2 (step n_layers + layer) + k: consumers passed merge barrier k
   int token;
   int token0, pos0;  // starting token / position, read once at kernel entry
 };
+
+// D stages the experts' fixed-point limbs (k * I * 2 bytes) in the attention scratch.
+static_assert(sizeof(decltype(AttnScratch::u)) >= kMaxTopK * 1024 * 2, "attention scratch too small for D limbs");
 
 __device__ __forceinline__ void cons_sync() { asm volatile("bar.sync %0, %1;" ::"r"(kBarCons), "r"(kMegaCons * 32)); }
 struct ConsSync {
@@ -242,11 +249,11 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 }
 
 __device__ __forceinline__ void stamp(const MegaArgs& a, int step, int layer, int slot) {
-  if (a.prof2 && step == 0 && layer == a.prof_layer) a.prof2[blockIdx.x * 32 + slot] = globaltimer();
+  if (a.prof2 && step == 0 && layer == a.prof_layer) a.prof2[blockIdx.x * 64 + slot] = globaltimer();
 }
 // Adds v to a per-CTA diagnostic slot of the same layer profile.
 __device__ __forceinline__ void prof_add(const MegaArgs& a, int step, int layer, int slot, unsigned long long v) {
-  if (a.prof2 && step == 0 && layer == a.prof_layer) a.prof2[blockIdx.x * 32 + slot] += v;
+  if (a.prof2 && step == 0 && layer == a.prof_layer) a.prof2[blockIdx.x * 64 + slot] += v;
 }
 
 // Grid barrier index of a phase: each step has 6 per layer + 1 (after H).
@@ -272,8 +279,9 @@ __device__ __forceinline__ bool grid_barrier(const MegaArgs& a, unsigned seq, un
   __shared__ int ok_flag;
   if (threadIdx.x == 32) {
     if (a.prof && idx != kNoStamp) a.prof[(size_t(idx) * gridDim.x + blockIdx.x) * 2] = globaltimer();
-    __threadfence();
-    atomicAdd(a.gbar, 1u);
+    // release: the CTA's writes (ordered before this thread by the barrier
+    // above) become visible to every CTA that acquires the count
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a.gbar), "r"(1u) : "memory");
     const unsigned target = gridDim.x * (seq + 1);
     int ok = 1;
     uint32_t spins = 0;
@@ -285,7 +293,6 @@ __device__ __forceinline__ bool grid_barrier(const MegaArgs& a, unsigned seq, un
         break;
       }
     }
-    __threadfence();
     if (a.prof && idx != kNoStamp) a.prof[(size_t(idx) * gridDim.x + blockIdx.x) * 2 + 1] = globaltimer();
     ok_flag = ok && !aborted(a);
   }
@@ -371,6 +378,16 @@ struct Producer {
     }
     issued(slot);
   }
+  // One router row (bf16 [H]) of expert e.
+  __device__ void router_chunk(const MegaLayer& L, int e) {
+    int slot;
+    uint8_t* dst = acquire(slot);
+    if (!dst) return;
+    const uint32_t bytes = uint32_t(a.H) * 2;
+    mbar_expect_tx(&sm.full[slot], bytes);
+    bulk_g2s(dst, L.router + size_t(e) * a.H, bytes, &sm.full[slot]);
+    issued(slot);
+  }
   __device__ void kv_chunk(const uint32_t* codes, const uint16_t* sc, const uint16_t* bi, int g, int b, int n) {
     int slot;
     uint8_t* dst = acquire(slot);
@@ -403,6 +420,64 @@ struct Producer {
     bulk_g2s(dst + half + cb, L.v_scales + s0 * 2, sbytes, &sm.full[slot]);
     bulk_g2s(dst + half + cb + sbytes, L.v_biases + s0 * 2, sbytes, &sm.full[slot]);
     issued(slot);
+  }
+
+  // 8 heads x n partials (kPartialFloats floats each): head h's run starts at
+  // src0 + h * head_stride; slot layout [head][n][kPartialFloats].
+  __device__ void partials_chunk(const float* src0, size_t head_stride, int n) {
+    int slot;
+    uint8_t* dst = acquire(slot);
+    if (!dst) return;
+    const uint32_t bytes = uint32_t(n) * kPartialFloats * 4;
+    mbar_expect_tx(&sm.full[slot], kHeadsPerKv * bytes);
+    for (int h = 0; h < kHeadsPerKv; ++h) bulk_g2s(dst + h * bytes, src0 + h * head_stride, bytes, &sm.full[slot]);
+    issued(slot);
+  }
+  // Waits (bounded) until the consumers have passed merge barrier `target`.
+  // The partials were written by other CTAs before it: order the async-proxy
+  // reads after the consumers' acquire.
+  __device__ void wait_merge(int target) {
+    uint32_t spins = 0;
+    while (sm.merge_seq < target) {
+      __nanosleep(32);
+      if (aborted(a)) { ok = false; return; }
+      if (++spins > kSpinLimit * 64) {
+        set_abort(a, kStatusCounterTimeout);
+        ok = false;
+        return;
+      }
+    }
+    stamp_cur(30);
+    __threadfence();
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    stamp_cur(25);
+  }
+  // The merge phases of one layer's attention (the consumers' merge_phase
+  // and final_phase take the same chunks in the same order).
+  int cur_step = 0, cur_layer = 0;  // for the diagnostics stamps
+  __device__ void stamp_cur(int slot) { stamp(a, cur_step, cur_layer, slot); }
+  __device__ void merge_chunks(const AttnPlan& AP, int step, int l) {
+    cur_step = step;
+    cur_layer = l;
+    const int seq = 2 * (step * a.n_layers + l);
+    wait_merge(seq + 1);
+    const int icap = items_cap(a.capacity);
+    const int item0 = a.token_base / (kAttBlock * AP.nbi);
+    const int n_local = max(0, min(a.super_hi, AP.n_super) - a.super_lo);
+    for (int t = blockIdx.x; t < n_local * a.hkv && ok; t += gridDim.x) {
+      const int g = t % a.hkv, s = a.super_lo + t / a.hkv;
+      const int lo = s * AP.per_super - item0, hi = min((s + 1) * AP.per_super, AP.n_items) - item0;
+      for (int i0 = lo; i0 < hi && ok; i0 += kMergeChunk)
+        partials_chunk(a.partials + (size_t(g * kHeadsPerKv) * icap + i0) * kPartialFloats,
+                       size_t(icap) * kPartialFloats, min(kMergeChunk, hi - i0));
+    }
+    if (AP.n_super > 1 && a.world == 1 && ok) {
+      wait_merge(seq + 2);
+      for (int c = blockIdx.x; c < a.hkv && ok; c += gridDim.x)
+        for (int s0 = 0; s0 < AP.n_super && ok; s0 += kMergeChunk)
+          partials_chunk(a.supers + (size_t(c * kHeadsPerKv) * a.n_super_max + s0) * kPartialFloats,
+                         size_t(a.n_super_max) * kPartialFloats, min(kMergeChunk, AP.n_super - s0));
+    }
   }
 
   __device__ void run() {
@@ -440,8 +515,11 @@ struct Producer {
             }
             stamp(a, step, l, 24);
           }
+          if (ok) merge_chunks(AP, step, l);
           // O rows
           for (int r = P.o0; r < P.o1 && ok; r += kORows) gemv_chunk(L.o, a.hq * 128, r, min(kORows, P.o1 - r));
+          // R: this CTA's router rows
+          for (int e = blockIdx.x; e < a.E && ok; e += gridDim.x) router_chunk(L, e);
           // G / D need this layer's routing: wait for the consumers' selection
           const int seq = step * a.n_layers + l + 1;
           uint32_t spins = 0;
@@ -534,6 +612,14 @@ struct Consumers {
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[slot]);
     ++chunk;
+  }
+
+  // The fixed-point limbs of x (n_groups groups of 64, one scale) shared by
+  // every lane of the CTA: prepared once, in place.
+  __device__ void share_limbs(uint16_t* x, int n_groups, const FixScale& fs) {
+    const float up = fs.up;
+    prep_limbs_inplace<2, kMegaCons * 32>(x, sm.gX, n_groups, threadIdx.x - 32, [up](int) { return up; },
+                                          ConsSync{});
   }
 
   // RMSNorm of src (bf16[2048], global or shared) into sm.xn, canonical
@@ -701,9 +787,10 @@ struct Consumers {
   }
 
   // --- attention ----------------------------------------------------------------
-  // All consumer warps: item `item` (4 blocks) of kv head g for its 8 q heads,
-  // blocks streamed through the ring (K slot, V slot per block); then the
-  // last-arriver merges of super-chunk and head.
+  // All consumer warps: item `item` (nbi blocks) of kv head g for its 8 q
+  // heads, blocks streamed through the ring (4-bit: K and V in one slot;
+  // 8-bit: a K slot and a V slot); the item partial is stored for
+  // merge_phase.
   template <int BITS>
   __device__ void attn_item(const MegaLayer& L, const AttnPlan& P, int pos, int g, int item, int step_,
                             int layer_) {
@@ -720,12 +807,16 @@ struct Consumers {
                         L.v_biases + sl * 2);
     }
     cons_sync();
-    if (warp == 0 && lane == 0) sm.att.qg = g;
+    if (warp == 0 && lane == 0) {
+      sm.att.qg = g;
+      stamp(a, step_, layer_, 19);
+    }
     WarpState st;
     state_empty(st);
     for (int b = b0; b < b1; ++b) {
       const int n = min(kAttBlock, P.T - b * kAttBlock), n4 = (n + 3) & ~3;
       uint8_t* kt = const_cast<uint8_t*>(take());
+      if (warp == 0 && lane == 0 && b == b0) stamp(a, step_, layer_, 29);
       const int kslot = slot;
       uint8_t* vt;
       int vslot = -1;
@@ -752,94 +843,88 @@ struct Consumers {
       }
     }
     if (warp == 0 && lane == 0) stamp(a, step_, layer_, 17);
-    cons_sync();  // the tree scratch overlays the per-warp PV buffers
-    warps_fold(st, warp, sm.att, ConsSync{});
-    // item partial of the 8 heads (local item index), then the merges
+    cons_sync();  // the fold scratch overlays the query-preparation buffers
+    // item partial of the 8 heads (local item index)
     const int icap = items_cap(a.capacity);
     const int item0 = a.token_base / (kAttBlock * P.nbi);
-    if (warp == 0)
-      store_item<BITS>(st, a.partials + (size_t(g * kHeadsPerKv) * icap + (item - item0)) * kPartialFloats,
-                       size_t(icap) * kPartialFloats);
-    if (warp == 0 && lane == 0) {
-      stamp(a, step_, layer_, 18);
-      prof_add(a, step_, layer_, 25, 1);
-    }
-    // several super-chunks: merged in a phase of their own (merge_phase)
-    if (P.n_super > 1) return;
-    __threadfence();
-    const int in_super = P.n_items;
-    cons_sync();
-    if (warp == 0 && lane == 0) {
-      const unsigned prev = atomicAdd(a.cnt + a.hq + g * a.n_super_max, 1u);
-      sm.xok = int(prev) == in_super - 1;
-      if (sm.xok) a.cnt[a.hq + g * a.n_super_max] = 0;
-    }
-    cons_sync();
-    if (!sm.xok) return;
-    // the last item of the only super-chunk: warp w merges head 8g + w
-    __threadfence();
-    super_done<BITS>(L, P, g, 0, item0, step_, layer_);
+    warps_fold_store(st, warp, sm.att, ConsSync{},
+                     a.partials + (size_t(g * kHeadsPerKv) * icap + (item - item0)) * kPartialFloats,
+                     size_t(icap) * kPartialFloats);
+    if (warp == 0 && lane == 0) stamp(a, step_, layer_, 18);
   }
 
-  // Warp w folds super-chunk s of head 8g + w (its items in order), then
-  // publishes it (several ranks) or merges the output (one rank: directly
-  // with one super-chunk, else through the per-head last arriver).
+  // Folds super-chunk s of the 8 heads of kv head g from the merge slots
+  // (items in order; warp w = head 8g + w), then finishes it: several ranks
+  // publish it, one rank with one super-chunk writes the output, otherwise
+  // it is stored for final_phase.
   template <int BITS>
-  __device__ void super_done(const MegaLayer& L, const AttnPlan& P, int g, int s, int item0, int step_, int layer_) {
-    const int icap = items_cap(a.capacity);
-    const int in_super = min(P.per_super, P.n_items - s * P.per_super);
-    const int h = g * kHeadsPerKv + warp;
-    const float* hpart = a.partials + size_t(h) * icap * kPartialFloats;
-    Partial4 S = empty_partial();
-    const Partial4 none = empty_partial();
-    merge_range(S, hpart, s * P.per_super - item0, s * P.per_super + in_super - item0, -1, none);
-    if (warp == 0 && lane == 0) prof_add(a, step_, layer_, 26, 1);
-    if (a.world > 1) {
-      // publish the super-chunk to every rank; each merges them itself
-      const int par = xch_parity(a, step_, layer_);
-      for (int q = 0; q < a.world; ++q) store_partial(xch_super(a.xch[q], a.xl, par, h, s), S);
-      __threadfence_system();
-      __syncwarp();
-      if (lane == 0)
-        for (int q = 0; q < a.world; ++q) atomicAdd_system(xch_head_cnt(a.xch[q], a.xl, par, h), 1u);
-      return;
+  __device__ void merge_phase(const MegaLayer& L, const AttnPlan& P, int step_, int layer_) {
+    const int n_local = max(0, min(a.super_hi, P.n_super) - a.super_lo);
+    const int item0 = a.token_base / (kAttBlock * P.nbi);
+    for (int t = blockIdx.x; t < n_local * a.hkv; t += gridDim.x) {
+      const int g = t % a.hkv, s = a.super_lo + t / a.hkv;
+      const int lo = s * P.per_super - item0, hi = min((s + 1) * P.per_super, P.n_items) - item0;
+      Partial4 S = empty_partial();
+      for (int i0 = lo; i0 < hi; i0 += kMergeChunk) {
+        const int n = min(kMergeChunk, hi - i0);
+        const float* st = reinterpret_cast<const float*>(take()) + warp * n * kPartialFloats;
+        if (warp == 0 && lane == 0 && i0 == lo) stamp(a, step_, layer_, 37);
+        for (int j = 0; j < n; ++j) merge_into(S, smem_partial(st + j * kPartialFloats));
+        release();
+      }
+      if (warp == 0 && lane == 0) stamp(a, step_, layer_, 38);
+      const int h = g * kHeadsPerKv + warp;
+      if (a.world > 1) {
+        // publish the super-chunk to every rank; each merges them itself
+        const int par = xch_parity(a, step_, layer_);
+        for (int q = 0; q < a.world; ++q) store_partial(xch_super(a.xch[q], a.xl, par, h, s), S);
+        __threadfence_system();
+        __syncwarp();
+        if (lane == 0)
+          for (int q = 0; q < a.world; ++q) atomicAdd_system(xch_head_cnt(a.xch[q], a.xl, par, h), 1u);
+      } else if (P.n_super == 1) {
+        Partial4 F = sink_partial(L, h);
+        merge_into(F, S);
+        write_attn(h, F);
+        if (warp == 0 && lane == 0) stamp(a, step_, layer_, 31);
+      } else {
+        store_partial(a.supers + (size_t(h) * a.n_super_max + s) * kPartialFloats, S);
+      }
     }
+  }
+
+  // One rank, several super-chunks: heads 8c + w fold [sink] and the
+  // super-chunks in order from the merge slots.
+  __device__ void final_phase(const MegaLayer& L, const AttnPlan& P, int step_, int layer_) {
+    for (int c = blockIdx.x; c < a.hkv; c += gridDim.x) {
+      const int h = c * kHeadsPerKv + warp;
+      Partial4 F = sink_partial(L, h);
+      for (int s0 = 0; s0 < P.n_super; s0 += kMergeChunk) {
+        const int n = min(kMergeChunk, P.n_super - s0);
+        const float* st = reinterpret_cast<const float*>(take()) + warp * n * kPartialFloats;
+        for (int j = 0; j < n; ++j) merge_into(F, smem_partial(st + j * kPartialFloats));
+        release();
+      }
+      write_attn(h, F);
+      if (warp == 0 && lane == 0) stamp(a, step_, layer_, 31);
+    }
+  }
+
+  __device__ Partial4 smem_partial(const float* p) const {
+    Partial4 Q;
+    Q.m = p[0];
+    Q.l = p[1];
+    const float4 v = *reinterpret_cast<const float4*>(p + 4 + 4 * lane);
+    Q.a[0] = v.x; Q.a[1] = v.y; Q.a[2] = v.z; Q.a[3] = v.w;
+    return Q;
+  }
+  __device__ Partial4 sink_partial(const MegaLayer& L, int h) const {
     Partial4 F = empty_partial();
     if (L.sinks) {
       F.m = bf(L.sinks[h]);
       F.l = 1.0f;
     }
-    if (P.n_super == 1) {
-      merge_into(F, S);
-    } else {
-      store_partial(a.supers + (size_t(h) * a.n_super_max + s) * kPartialFloats, S);
-      __threadfence();
-      unsigned prev = 0;
-      if (lane == 0) prev = atomicAdd(a.cnt + h, 1u);
-      prev = __shfl_sync(0xffffffffu, prev, 0);
-      if (int(prev) != P.n_super - 1) return;
-      __threadfence();
-      merge_range(F, a.supers + size_t(h) * a.n_super_max * kPartialFloats, 0, P.n_super, s, S);
-      if (lane == 0) a.cnt[h] = 0;
-      if (lane == 0) prof_add(a, step_, layer_, 28, 1);
-    }
-    write_attn(h, F);
-  }
-
-  // Several super-chunks (long contexts): after a grid barrier, task
-  // (kv head g, local super-chunk s) goes to CTA task % grid, so the folds
-  // spread over the grid instead of landing on the items' last arrivers.
-  template <int BITS>
-  __device__ void merge_phase(const MegaLayer& L, const AttnPlan& P, int step_, int layer_) {
-    const int s_hi = min(a.super_hi, P.n_super);
-    const int n_local = max(0, s_hi - a.super_lo);
-    const int tasks = n_local * a.hkv;
-    const int item0 = a.token_base / (kAttBlock * P.nbi);
-    for (int t = blockIdx.x; t < tasks; t += gridDim.x) {
-      const int g = t % a.hkv, s = a.super_lo + t / a.hkv;
-      cons_sync();  // merge_range stages through the attention scratch
-      super_done<BITS>(L, P, g, s, item0, step_, layer_);
-    }
+    return F;
   }
 
   // world > 1: send this rank's expert slots of rows [o0, o1) to every other
@@ -975,34 +1060,27 @@ struct Consumers {
     cons_sync();
     if (warp == 0 && lane == 0) stamp(a, step_, layer_, 14);
     if (a.router_mode == 0) {
-      // max and the canonical sum of exp(l - max): lane l of warp 0 adds
-      // experts l, l+32, ... in order, then a butterfly
+      // warp 0: max; exp(l - max); the canonical sum (lane l adds experts l,
+      // l+32, ... in order, then a butterfly); p = exp / sum
       if (warp == 0) {
         float mx = -INFINITY;
 #pragma unroll 1
         for (int i = lane; i < E; i += 32) mx = fmaxf(mx, sm.route_p[i]);
         mx = bfly_max(mx);
-        if (lane == 0) sm.red[34] = mx;
-      }
-      cons_sync();
-      const float mx = sm.red[34];
-#pragma unroll 1
-      for (int i = t; i < E; i += nt) sm.route_c[i] = rexp(__fsub_rn(sm.route_p[i], mx));
-      cons_sync();
-      if (warp == 0) {
         float sum = 0.0f;
 #pragma unroll 1
-        for (int i = lane; i < E; i += 32) sum = __fadd_rn(sum, sm.route_c[i]);
+        for (int i = lane; i < E; i += 32) {
+          const float c = rexp(__fsub_rn(sm.route_p[i], mx));
+          sm.route_c[i] = c;
+          sum = __fadd_rn(sum, c);
+        }
         sum = bfly_sum(sum);
-        if (lane == 0) sm.red[35] = sum;
-      }
-      cons_sync();
-      const float sum = sm.red[35];
 #pragma unroll 1
-      for (int i = t; i < E; i += nt) {
-        const float pi = __fdiv_rn(sm.route_c[i], sum);
-        sm.route_p[i] = pi;
-        sm.route_c[i] = pi;
+        for (int i = lane; i < E; i += 32) {
+          const float pi = __fdiv_rn(sm.route_c[i], sum);
+          sm.route_p[i] = pi;
+          sm.route_c[i] = pi;
+        }
       }
     } else {
 #pragma unroll 1
@@ -1015,17 +1093,44 @@ struct Consumers {
     cons_sync();
     if (warp == 0 && lane == 0) stamp(a, step_, layer_, 15);
     // rank of i = #{j : c_j > c_i or (c_j == c_i and j < i)}; ranks < k are
-    // the selection, in rank order (largest first, lowest index on ties)
-#pragma unroll 1
-    for (int i = t; i < E; i += nt) {
+    // the selection, in rank order (largest first, lowest index on ties).
+    // Pairs of threads split the comparisons of one expert when 2E fits the
+    // consumer threads and E is a multiple of 8 (float4 reads of each half).
+    auto rank_of = [&](int i, int j0, int j1) {
       const float ci = sm.route_c[i];
       int rank = 0;
+      if (((j1 - j0) & 3) == 0) {
+        const float4* c4 = reinterpret_cast<const float4*>(sm.route_c + j0);
 #pragma unroll 4
-      for (int j = 0; j < E; ++j) {
-        const float cj = sm.route_c[j];
-        rank += (cj > ci || (cj == ci && j < i)) ? 1 : 0;
+        for (int q = 0; q < (j1 - j0) / 4; ++q) {
+          const float4 cv = c4[q];
+          const int j = j0 + 4 * q;
+          rank += (cv.x > ci || (cv.x == ci && j < i)) ? 1 : 0;
+          rank += (cv.y > ci || (cv.y == ci && j + 1 < i)) ? 1 : 0;
+          rank += (cv.z > ci || (cv.z == ci && j + 2 < i)) ? 1 : 0;
+          rank += (cv.w > ci || (cv.w == ci && j + 3 < i)) ? 1 : 0;
+        }
+      } else {
+#pragma unroll 4
+        for (int j = j0; j < j1; ++j) {
+          const float cj = sm.route_c[j];
+          rank += (cj > ci || (cj == ci && j < i)) ? 1 : 0;
+        }
       }
-      if (rank < a.k) sm.ids[rank] = i;
+      return rank;
+    };
+    if (2 * E <= nt && (E & 7) == 0) {
+      const bool act = t < 2 * E;  // threads t, t^1 share expert t/2
+      const int i = t >> 1, half = t & 1;
+      int rank = act ? rank_of(i, half * (E / 2), (half + 1) * (E / 2)) : 0;
+      rank += __shfl_xor_sync(0xffffffffu, rank, 1);
+      if (act && half == 0 && rank < a.k) sm.ids[rank] = i;
+    } else {
+#pragma unroll 1
+      for (int i = t; i < E; i += nt) {
+        const int rank = rank_of(i, 0, E);
+        if (rank < a.k) sm.ids[rank] = i;
+      }
     }
     cons_sync();
     if (warp == 0) {
@@ -1088,7 +1193,8 @@ struct Consumers {
         const FixScale fq = norm(l == 0 ? sm.h0 : a.h, L.input_norm, l == 0);
         {
           GroupX gx[1];
-          prep_lane_x<2048>(sm.xn, fq, 0, lane, gx);
+          share_limbs(sm.xn, 32, fq);
+          load_limbs(sm.xn, sm.gX, 32, lane, gx[0]);
           const int qrows[3] = {a.hq * 128, a.hkv * 128, a.hkv * 128};
           for (int r = P.q0; r < P.q1;) {
             int m = 0, base = 0;
@@ -1112,18 +1218,37 @@ struct Consumers {
           attn_item<BITS>(L, AP, pos, g, item, step, l);
           if (warp == 0 && lane == 0) stamp(a, step, l, 13);
         }
-        if (AP.n_super > 1) {
+        {
+          // item partials -> super-chunks (-> output); the producer stages
+          // the partials into the ring once every CTA has stored its items
+          const int seq = 2 * (step * a.n_layers + l);
           if (!gbar(kNoStamp)) return;
+          if (warp == 0 && lane == 0) {
+            sm.merge_seq = seq + 1;
+            stamp(a, step, l, 26);
+          }
           merge_phase<BITS>(L, AP, step, l);
+          if (warp == 0 && lane == 0) stamp(a, step, l, 27);
+          if (AP.n_super > 1 && a.world == 1) {
+            if (!gbar(kNoStamp)) return;
+            if (warp == 0 && lane == 0) {
+              sm.merge_seq = seq + 2;
+              stamp(a, step, l, 28);
+            }
+            final_phase(L, AP, step, l);
+          }
         }
         if (a.world > 1 && warp == 0) attn_final_sharded(L, AP, xch_parity(a, step, l));
         if (!gbar(bar_index(a, step, l, 1))) return;
         // ---- O
         {
+          if (warp == 0 && lane == 0) stamp(a, step, l, 40);
           const FixScale fo = load_x(a.attn, a.hq * 128);
+          if (warp == 0 && lane == 0) stamp(a, step, l, 41);
           GroupX gx[1];
           if (a.hq * 128 == 4096) {
-            prep_lane_x<4096>(sm.xn, fo, warp & 1, lane, gx);
+            share_limbs(sm.xn, 64, fo);
+            load_limbs(sm.xn, sm.gX, 64, KCfg<4096>::group(warp & 1, lane, 0), gx[0]);
             for (int r = P.o0; r < P.o1; r += kORows) {
               const int n = min(kORows, P.o1 - r);
               const uint8_t* st = take();
@@ -1131,7 +1256,8 @@ struct Consumers {
               release();
             }
           } else {
-            prep_lane_x<2048>(sm.xn, fo, 0, lane, gx);
+            share_limbs(sm.xn, 32, fo);
+            load_limbs(sm.xn, sm.gX, 32, lane, gx[0]);
             for (int r = P.o0; r < P.o1; r += kORows) {
               const int n = min(kORows, P.o1 - r);
               const uint8_t* st = take();
@@ -1139,18 +1265,26 @@ struct Consumers {
               release();
             }
           }
+          if (warp == 0 && lane == 0) stamp(a, step, l, 42);
         }
         if (!gbar(bar_index(a, step, l, 2))) return;
         // ---- R
+        if (warp == 0 && lane == 0) stamp(a, step, l, 43);
         const FixScale fr = norm(a.h, L.post_norm);
+        if (warp == 0 && lane == 0) stamp(a, step, l, 44);
         {
           int j = 0;
           for (int e = blockIdx.x; e < a.E; e += gridDim.x, ++j) {
-            if ((j % kMegaCons) != warp) continue;
+            // the row was staged by the producer; warp j % 8 computes it
+            const uint16_t* wrow = reinterpret_cast<const uint16_t*>(take());
+            if ((j % kMegaCons) != warp) {
+              release();
+              continue;
+            }
             float acc = 0.0f;
             for (int mm = 0; mm < H / 256; ++mm) {
               const int c = lane + 32 * mm;
-              const uint4 wv = ldg128_nc(L.router + size_t(e) * H + c * 8);
+              const uint4 wv = *reinterpret_cast<const uint4*>(wrow + c * 8);
               const uint4 xv = *reinterpret_cast<const uint4*>(sm.xn + c * 8);
               const uint32_t ws_[4] = {wv.x, wv.y, wv.z, wv.w};
               const uint32_t xs_[4] = {xv.x, xv.y, xv.z, xv.w};
@@ -1162,7 +1296,9 @@ struct Consumers {
             }
             acc = bfly_sum(acc);
             if (lane == 0) a.router_logits[e] = rbf(acc);
+            release();
           }
+          if (warp == 0 && lane == 0) stamp(a, step, l, 45);
         }
         if (!gbar(bar_index(a, step, l, 3))) return;
         // ---- G: selection (same on every CTA), then gate/up pairs
@@ -1176,7 +1312,8 @@ struct Consumers {
         cons_sync();
         {
           GroupX gx[1];
-          prep_lane_x<2048>(sm.xn, fr, 0, lane, gx);
+          share_limbs(sm.xn, 32, fr);
+          load_limbs(sm.xn, sm.gX, 32, lane, gx[0]);
           int g0, g1;
           split_range(sm.n_loc * a.I / 2, gridDim.x, blockIdx.x, g0, g1);
           g0 *= 2;
@@ -1218,13 +1355,27 @@ struct Consumers {
         if (!gbar(bar_index(a, step, l, 4))) return;
         // ---- D: down rows of all k experts, mix, residual
         {
+          if (warp == 0 && lane == 0) stamp(a, step, l, 39);
           load_vec(sm.act, a.act, a.k * I);
+          // per selected expert: fixed-point scale, then the shared limbs
+          for (int r = warp; r < a.k; r += kMegaCons) {
+            const float m = warp_maxabs(sm.act + r * I, I);
+            if (lane == 0) sm.dmax[r] = m;
+          }
+          cons_sync();
+          // limbs into the attention scratch (free during D)
+          uint16_t* dl = reinterpret_cast<uint16_t*>(&sm.att.u);
+          prep_limbs_to<kMegaCons * 32>(sm.act, dl, sm.gX, a.k * (I / 64), threadIdx.x - 32,
+                                        [&](int g) { return fix_scale_from_max(sm.dmax[g / (I / 64)]).up; });
+          cons_sync();
+          if (warp == 0 && lane == 0) stamp(a, step, l, 33);
           const int n = P.o1 - P.o0;
           const int nl = sm.n_loc;
           if (n > 0) {
             for (int j0 = 0; j0 < nl; j0 += kDExperts) {
               const int j1 = min(nl, j0 + kDExperts);
               const uint8_t* st = take();
+              if (warp == 0 && lane == 0 && j0 == 0) stamp(a, step, l, 34);
               // warp w: local expert j0 + (w % 4), rows of half (w / 4)
               const int jj = j0 + (warp % kDExperts), half = warp / kDExperts;
               if (jj < j1) {
@@ -1235,10 +1386,8 @@ struct Consumers {
                 const uint8_t* e0 = st + (jj - j0) * per;
                 const uint16_t* sbase = reinterpret_cast<const uint16_t*>(e0 + wb);
                 const uint16_t* bbase = reinterpret_cast<const uint16_t*>(e0 + wb + ((sbytes + 15) & ~15u));
-                const FixScale fd = fix_scale_from_max(warp_maxabs(sm.act + rr * I, I));
-                GroupX gx[C::GPL];
+                const FixScale fd = fix_scale_from_max(sm.dmax[rr]);
                 const int sub = lane >> 2, l4 = lane & 3;  // 8 rows per pass, 4 lanes per row
-                prep_lane_x<I>(sm.act + rr * I, fd, 0, l4, gx);
                 const int rbeg = half * ((n + 1) / 2), rend = half == 0 ? (n + 1) / 2 : n;
                 for (int rb = rbeg; rb < rend; rb += 8) {
                   int rows[1];
@@ -1246,15 +1395,18 @@ struct Consumers {
                   const bool valid = x < rend;
                   rows[0] = valid ? x : rbeg;
                   float v[1];
-                  lane_rows_partial<I, 2, 1>(e0, sbase, bbase, rows, 0, l4, gx, v, a.sd);
+                  lane_rows_partial_shared<I, 2, 1>(e0, sbase, bbase, rows, l4, dl, sm.gX, a.k * (I / 64),
+                                                    rr * (I / 64), v, a.sd);
                   v[0] = bfly_sum<4>(valid ? v[0] : 0.0f);
                   if (valid && l4 == 0) sm.dsm[rr][rows[0]] = rbf(__fmul_rn(v[0], fd.down));
                 }
               }
+              if (warp == 0 && lane == 0) stamp(a, step, l, j0 == 0 ? 46 : 47);
               release();
             }
             cons_sync();
           }
+          if (warp == 0 && lane == 0) stamp(a, step, l, 35);
           if (a.world > 1 && !exchange_down(P, n, xch_parity(a, step, l))) return;
           if (n > 0) {
             for (int i = threadIdx.x - 32; i < n; i += kMegaCons * 32) {
@@ -1269,6 +1421,7 @@ struct Consumers {
               a.trace[size_t(l + 1) * H + P.o0 + i] = hn;
             }
           }
+          if (warp == 0 && lane == 0) stamp(a, step, l, 36);
         }
         if (!gbar(bar_index(a, step, l, 5))) return;
       }
@@ -1276,7 +1429,8 @@ struct Consumers {
       const FixScale fh = norm(a.h, a.final_norm);
       {
         GroupX gx[1];
-        prep_lane_x<2048>(sm.xn, fh, 0, lane, gx);
+        share_limbs(sm.xn, 32, fh);
+        load_limbs(sm.xn, sm.gX, 32, lane, gx[0]);
         best = -INFINITY;
         best_i = 0x7fffffff;
         int v0, v1;
@@ -1359,6 +1513,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_decode_mega(const MegaArgs 
       mbar_init(&sm.empty[s], kMegaCons);
     }
     sm.route_seq = 0;
+    sm.merge_seq = 0;
     sm.token0 = a.ctl[1];
     sm.pos0 = a.ctl[2];
     fence_barrier_init();

@@ -159,6 +159,116 @@ __device__ __forceinline__ void prep_lane_x(const uint16_t* x, FixScale fs, int 
   for (int m = 0; m < KCfg<K>::GPL; ++m) prep_group(x + KCfg<K>::group(seg, l, m) * 64, fs, gx[m]);
 }
 
+// Fixed-point limbs of n_groups groups of 64 bf16 values at x (shared
+// memory), prepared once for all lanes and written in place in the layout
+// [chunk 0..7][group] of uint4 (chunks 0,1 = hi_e, 2,3 = hi_o, 4,5 = lo_e,
+// 6,7 = lo_o), with X[g] = float(exact sum of the group's xi).  Group g uses
+// the up-scale upf(g).  Threads [0, NT) of the calling group call it (sync:
+// a barrier over them); n_groups * 8 <= MAXI * NT.  The values are those of
+// prep_group.
+template <int MAXI, int NT, class UpF, class Sync>
+__device__ __forceinline__ void prep_limbs_inplace(uint16_t* x, float* X, int n_groups, int t, UpF upf, Sync sync) {
+  uint32_t he[MAXI], ho[MAXI], le[MAXI], lo[MAXI];
+  const int n_items = n_groups * 8;
+#pragma unroll
+  for (int q = 0; q < MAXI; ++q) {
+    const int idx = t + q * NT;
+    int part = 0;
+    he[q] = ho[q] = le[q] = lo[q] = 0;
+    if (idx < n_items) {
+      const uint4 u = *reinterpret_cast<const uint4*>(x + idx * 8);
+      const float up = upf(idx >> 3);
+      const uint32_t us[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int a = __float2int_rn(__fmul_rn(__uint_as_float(us[k] << 16), up));
+        const int b = __float2int_rn(__fmul_rn(__uint_as_float(us[k] & 0xFFFF0000u), up));
+        he[q] |= (uint32_t(a >> 8) & 0xFFu) << (8 * k);
+        ho[q] |= (uint32_t(b >> 8) & 0xFFu) << (8 * k);
+        le[q] |= (uint32_t(a) & 0xFFu) << (8 * k);
+        lo[q] |= (uint32_t(b) & 0xFFu) << (8 * k);
+        part += a + b;
+      }
+    }
+    // the 8 items of a group are 8 consecutive lanes of one warp
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    part += __shfl_xor_sync(0xffffffffu, part, 4);
+    if (idx < n_items && (idx & 7) == 0) X[idx >> 3] = float(part);
+  }
+  sync();
+  uint32_t* L = reinterpret_cast<uint32_t*>(x);
+#pragma unroll
+  for (int q = 0; q < MAXI; ++q) {
+    const int idx = t + q * NT;
+    if (idx < n_items) {
+      const int g = idx >> 3, w = idx & 7, c = w >> 2, j = w & 3;
+      L[((0 + c) * n_groups + g) * 4 + j] = he[q];
+      L[((2 + c) * n_groups + g) * 4 + j] = ho[q];
+      L[((4 + c) * n_groups + g) * 4 + j] = le[q];
+      L[((6 + c) * n_groups + g) * 4 + j] = lo[q];
+    }
+  }
+  sync();
+}
+
+// The same limbs written to a separate buffer `out` (one pass; callers
+// synchronize before reading them).
+template <int NT, class UpF>
+__device__ __forceinline__ void prep_limbs_to(const uint16_t* x, uint16_t* out, float* X, int n_groups, int t,
+                                              UpF upf) {
+  const int n_items = n_groups * 8;
+  uint32_t* L = reinterpret_cast<uint32_t*>(out);
+  for (int base = 0; base < n_items; base += NT) {
+    const int idx = base + t;
+    int part = 0;
+    uint32_t he = 0, ho = 0, le = 0, lo = 0;
+    if (idx < n_items) {
+      const uint4 u = *reinterpret_cast<const uint4*>(x + idx * 8);
+      const float up = upf(idx >> 3);
+      const uint32_t us[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int a = __float2int_rn(__fmul_rn(__uint_as_float(us[k] << 16), up));
+        const int b = __float2int_rn(__fmul_rn(__uint_as_float(us[k] & 0xFFFF0000u), up));
+        he |= (uint32_t(a >> 8) & 0xFFu) << (8 * k);
+        ho |= (uint32_t(b >> 8) & 0xFFu) << (8 * k);
+        le |= (uint32_t(a) & 0xFFu) << (8 * k);
+        lo |= (uint32_t(b) & 0xFFu) << (8 * k);
+        part += a + b;
+      }
+      const int g = idx >> 3, w = idx & 7, c = w >> 2, j = w & 3;
+      L[((0 + c) * n_groups + g) * 4 + j] = he;
+      L[((2 + c) * n_groups + g) * 4 + j] = ho;
+      L[((4 + c) * n_groups + g) * 4 + j] = le;
+      L[((6 + c) * n_groups + g) * 4 + j] = lo;
+    }
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    part += __shfl_xor_sync(0xffffffffu, part, 4);
+    if (idx < n_items && (idx & 7) == 0) X[idx >> 3] = float(part);
+  }
+}
+
+// A lane's prepared group g from the shared limbs of prep_limbs_inplace.
+__device__ __forceinline__ void load_limbs(const uint16_t* x, const float* X, int n_groups, int g, GroupX& gx) {
+  const uint4* L = reinterpret_cast<const uint4*>(x);
+  uint4 c[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) c[k] = L[k * n_groups + g];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    gx.hi_e[4 * k] = c[k].x; gx.hi_e[4 * k + 1] = c[k].y; gx.hi_e[4 * k + 2] = c[k].z; gx.hi_e[4 * k + 3] = c[k].w;
+    gx.hi_o[4 * k] = c[2 + k].x; gx.hi_o[4 * k + 1] = c[2 + k].y; gx.hi_o[4 * k + 2] = c[2 + k].z;
+    gx.hi_o[4 * k + 3] = c[2 + k].w;
+    gx.lo_e[4 * k] = c[4 + k].x; gx.lo_e[4 * k + 1] = c[4 + k].y; gx.lo_e[4 * k + 2] = c[4 + k].z;
+    gx.lo_e[4 * k + 3] = c[4 + k].w;
+    gx.lo_o[4 * k] = c[6 + k].x; gx.lo_o[4 * k + 1] = c[6 + k].y; gx.lo_o[4 * k + 2] = c[6 + k].z;
+    gx.lo_o[4 * k + 3] = c[6 + k].w;
+  }
+  gx.X = X[g];
+}
+
 // Lane partials of ILP rows at once (independent chains for the scheduler).
 template <int K, int SD, int ILP>
 __device__ __forceinline__ void lane_rows_partial(const uint8_t* wbase, const uint16_t* sbase,
@@ -186,6 +296,40 @@ __device__ __forceinline__ void lane_rows_partial(const uint8_t* wbase, const ui
       const float s = sb<SD>(sbase[rows[i] * KCfg<K>::GROUPS + g], sd_rt);
       const float b = sb<SD>(bbase[rows[i] * KCfg<K>::GROUPS + g], sd_rt);
       acc[i] = fold_group(acc[i], D[i], gx[m].X, s, b);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < ILP; ++i) out[i] = acc[i];
+}
+
+// lane_rows_partial with the lane's groups read from the shared limbs of
+// prep_limbs_inplace one at a time (group index g0 + KCfg<K>::group(0, l, m)).
+template <int K, int SD, int ILP>
+__device__ __forceinline__ void lane_rows_partial_shared(const uint8_t* wbase, const uint16_t* sbase,
+                                                         const uint16_t* bbase, const int (&rows)[ILP], int l,
+                                                         const uint16_t* limbs, const float* X, int n_groups,
+                                                         int g0, float (&out)[ILP], int sd_rt = 0) {
+  float acc[ILP];
+#pragma unroll
+  for (int i = 0; i < ILP; ++i) acc[i] = 0.0f;
+#pragma unroll
+  for (int m = 0; m < KCfg<K>::GPL; ++m) {
+    const int g = KCfg<K>::group(0, l, m);
+    GroupX gx;
+    load_limbs(limbs, X, n_groups, g0 + g, gx);
+    uint4 w[ILP][2];
+#pragma unroll
+    for (int i = 0; i < ILP; ++i) {
+      const uint8_t* p = wbase + rows[i] * KCfg<K>::ROW_BYTES + g * 32;
+      w[i][0] = lds128(p);
+      w[i][1] = lds128(p + 16);
+    }
+#pragma unroll
+    for (int i = 0; i < ILP; ++i) {
+      const int D = group_dot(w[i], gx);
+      const float s = sb<SD>(sbase[rows[i] * KCfg<K>::GROUPS + g], sd_rt);
+      const float b = sb<SD>(bbase[rows[i] * KCfg<K>::GROUPS + g], sd_rt);
+      acc[i] = fold_group(acc[i], D, gx.X, s, b);
     }
   }
 #pragma unroll
