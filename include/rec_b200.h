@@ -183,6 +183,18 @@ enum {
  * state (profiling and per-kernel timing; no reference counterpart: the
  * reference's step is a single Metal dispatch). */
 REC_API int rec_launch_kernel(RecCtx* ctx, int32_t kind, int32_t layer, void* stream);
+/* The MoE block of one layer on a residual vector, with the session's
+ * weights: x = RMSNorm(h, post_norm); logits = bf16(Wr x); softmax or
+ * sigmoid + bias selection of top_k experts, weights renormalised;
+ * h <- bf16(h + mix), mix = the selected experts' bf16 SwiGLU FFN outputs
+ * times bf16(weight), summed in bf16 in selection order.  h_dev (bf16
+ * [hidden]) is read and overwritten; ids_dev (int32 [top_k]) and weights_dev
+ * (float [top_k]) receive the selection when non-NULL.  Replaces Router /
+ * SparseMoeBlock.__call__ (engine/src/rec_mlx/model.py:227-254), mlx-lm's
+ * SwitchGLU and the reference's route/expert kernels (megakernel.py:406-435,
+ * 696-798; mixed_bits.py:32-54).  Unsharded sessions only. */
+REC_API int rec_router_moe(RecCtx* ctx, int32_t layer, void* h_dev, int32_t* ids_dev, float* weights_dev,
+                           void* stream);
 /* Optional phase timeline of the persistent decode kernel: when set, every
  * CTA stamps %globaltimer (ns) at each grid-barrier arrival and release into
  * buf_dev as uint64 [barrier][cta][2]; a step has 6*n_layers + 1 barriers.
@@ -197,6 +209,18 @@ REC_API int rec_set_layer_profile(RecCtx* ctx, void* buf_dev, int32_t layer);
  * session unusable. */
 REC_API int rec_check_status(RecCtx* ctx, void* stream);
 REC_API int rec_last_error(char* buf, size_t len);
+
+/* Quantize-on-append of one token's K and V rows (bf16 [n_kv_heads * 128]
+ * each, K already RoPE'd) into row *position_dev of every head of a cache
+ * layer: MLX affine quantization, group 64 along head_dim, bf16 scale and
+ * bias.  Replaces the append of MixedQuantizedKVCache.update_and_fetch
+ * (engine/src/rec_mlx/model.py:45-82) and the KV write kernels
+ * (cache.py:6-46); the persistent decode kernel fuses the same step into its
+ * attention phase.  A position outside [0, capacity) sets *status_dev to 4
+ * and writes nothing. */
+REC_API int rec_kv_append(const RecKVLayer* kv, int32_t n_kv_heads, int32_t capacity, int32_t kv_bits,
+                          const void* k_dev, const void* v_dev, const int32_t* position_dev, int32_t* status_dev,
+                          void* stream);
 
 /* ---- kernel entry points used by the unit tests -------------------------- */
 /* y = W x (int4 g64) with an optional fused RMSNorm prologue on x. */
@@ -240,6 +264,16 @@ REC_API int rec_gemv_int4_argmax_noalloc(const RecQMat* w, int32_t scale_dtype, 
 REC_API int rec_sample_logits(const void* logits_dev, int32_t batch, int32_t vocab, int64_t stride,
                               const int32_t* history_dev, int32_t history_len, const RecSampling* params,
                               const float* uniforms_dev, int32_t* ids_dev, void* stream);
+/* The sampling head for `batch` hidden rows (bf16 [batch, hidden]):
+ * logits[b] = lm_head . RMSNorm(h[b], final_norm) (int4 g64 GEMV into
+ * logits_dev, bf16 [batch, vocab]), then rec_sample_logits on those rows with
+ * the history, parameters and uniforms as documented there.  Replaces the
+ * final norm + lm_head of Model.__call__ (engine/src/rec_mlx/model.py:324-327)
+ * followed by the reference's sampler step (engine.py:279-301). */
+REC_API int rec_lmhead_sample(const RecQMat* lm_head, int32_t scale_dtype, int32_t vocab, int32_t hidden,
+                              const void* h_dev, int32_t batch, const void* final_norm_dev, float eps,
+                              const int32_t* history_dev, int32_t history_len, const RecSampling* params,
+                              const float* uniforms_dev, void* logits_dev, int32_t* ids_dev, void* stream);
 /* Decode attention of one layer alone (unit tests, the attention sweep):
  * quantizes the new K / V of `*position_dev` from qkv_dev (bf16 [Hq*128 |
  * Hkv*128 | Hkv*128], RoPE from rope_dev [positions][cos 64 | sin 64]) into

@@ -35,7 +35,53 @@ cudaError_t launch_smem(K kern, int threads, size_t smem, cudaStream_t st, const
   return cudaGetLastError();
 }
 
+// Quantize-on-append: one warp per (kv head, K or V, group of 64 dims) of
+// the new token's rows, stored at row *position of each head.
+__global__ void k_kv_append(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v, RecKVLayer kv, int hkv,
+                            int capacity, int bits, const int* __restrict__ position, int* status) {
+  const int lane = threadIdx.x & 31;
+  const int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (task >= hkv * 4) return;
+  const int p = *position;
+  if (p < 0 || p >= capacity) {
+    if (task == 0 && lane == 0) report(status, kStatusBadPosition);
+    return;
+  }
+  const int g = task >> 2, is_v = (task >> 1) & 1, grp = task & 1;
+  const uint32_t pair = reinterpret_cast<const uint32_t*>((is_v ? v : k) + g * 128 + 64 * grp)[lane];
+  const float v0 = bf(uint16_t(pair & 0xFFFFu)), v1 = bf(uint16_t(pair >> 16));
+  const QGroupParams qp = warp_group_params(v0, v1, bits);
+  const uint32_t word = warp_pack(quant_code(v0, qp, bits), quant_code(v1, qp, bits), bits);
+  const int gw = 64 * bits / 32, rw = 2 * gw;
+  const size_t slot = size_t(g) * capacity + size_t(p);
+  uint32_t* codes = static_cast<uint32_t*>(is_v ? kv.v_codes : kv.k_codes);
+  uint16_t* sc = static_cast<uint16_t*>(is_v ? kv.v_scales : kv.k_scales);
+  uint16_t* bi = static_cast<uint16_t*>(is_v ? kv.v_biases : kv.k_biases);
+  if (lane < gw) codes[slot * rw + grp * gw + lane] = word;
+  if (lane == 0) {
+    sc[slot * 2 + grp] = to_bf(qp.scale);
+    bi[slot * 2 + grp] = to_bf(qp.bias);
+  }
+}
+
 }  // namespace
+
+REC_API int rec_kv_append(const RecKVLayer* kv, int32_t n_kv_heads, int32_t capacity, int32_t kv_bits,
+                          const void* k_dev, const void* v_dev, const int32_t* position_dev, int32_t* status_dev,
+                          void* stream) {
+  REC_CHECK_ARG(kv && k_dev && v_dev && position_dev && status_dev, "rec_kv_append: null pointer");
+  REC_CHECK_ARG(n_kv_heads > 0 && capacity > 0, "rec_kv_append: n_kv_heads and capacity must be positive");
+  REC_CHECK_ARG(kv_bits == 4 || kv_bits == 8, "kv_bits must be 4 or 8");
+  REC_CHECK_ARG(kv->k_codes && kv->k_scales && kv->k_biases && kv->v_codes && kv->v_scales && kv->v_biases &&
+                    aligned16(kv->k_codes) && aligned16(kv->v_codes) && aligned16(k_dev) && aligned16(v_dev),
+                "rec_kv_append: KV buffers and k/v rows must be non-null and 16-byte aligned");
+  const int warps = n_kv_heads * 4;
+  k_kv_append<<<(warps + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(k_dev), static_cast<const uint16_t*>(v_dev), *kv, n_kv_heads, capacity, kv_bits,
+      position_dev, status_dev);
+  REC_CHECK_CUDA(cudaGetLastError());
+  return REC_OK;
+}
 
 REC_API size_t rec_attn_scratch_bytes(int32_t n_q_heads, int32_t capacity) {
   if (n_q_heads <= 0 || capacity <= 0) return 0;

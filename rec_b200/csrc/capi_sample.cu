@@ -42,3 +42,23 @@ REC_API int rec_sample_logits(const void* logits_dev, int32_t batch, int32_t voc
   REC_CHECK_CUDA(cudaGetLastError());
   return REC_OK;
 }
+
+REC_API int rec_lmhead_sample(const RecQMat* lm_head, int32_t scale_dtype, int32_t vocab, int32_t hidden,
+                              const void* h_dev, int32_t batch, const void* final_norm_dev, float eps,
+                              const int32_t* history_dev, int32_t history_len, const RecSampling* params,
+                              const float* uniforms_dev, void* logits_dev, int32_t* ids_dev, void* stream) {
+  REC_CHECK_ARG(lm_head && h_dev && final_norm_dev && params && logits_dev && ids_dev,
+                "rec_lmhead_sample: null pointer");
+  REC_CHECK_ARG(batch >= 1 && batch <= 64, "rec_lmhead_sample: batch %d outside 1..64", batch);
+  REC_CHECK_ARG(hidden > 0 && vocab > 0, "rec_lmhead_sample: bad shape");
+  const uint16_t* h = static_cast<const uint16_t*>(h_dev);
+  uint16_t* lg = static_cast<uint16_t*>(logits_dev);
+  for (int b = 0; b < batch; ++b) {
+    const int rc = rec_gemv_int4(lm_head, scale_dtype, vocab, hidden, h + size_t(b) * hidden, final_norm_dev, eps,
+                                 lg + size_t(b) * vocab, stream);
+    if (rc) return rc;
+  }
+  return rec_sample_logits(logits_dev, batch, vocab, vocab, history_dev, history_len, params, uniforms_dev, ids_dev,
+                           stream);
+}
+

@@ -828,6 +828,29 @@ REC_API int rec_launch_kernel(RecCtx* c, int32_t kind, int32_t layer, void* stre
   return REC_OK;
 }
 
+REC_API int rec_router_moe(RecCtx* c, int32_t layer, void* h_dev, int32_t* ids_dev, float* weights_dev,
+                           void* stream) {
+  int rc = check_ready(c);
+  if (rc) return rc;
+  REC_CHECK_ARG(h_dev, "rec_router_moe: null residual");
+  REC_CHECK_ARG(layer >= 0 && layer < c->d.n_layers, "layer %d out of range", layer);
+  REC_CHECK_ARG(c->world == 1, "rec_router_moe runs on an unsharded session");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t hb = size_t(c->d.hidden) * 2;
+  REC_CHECK_CUDA(cudaMemcpyAsync(c->h, h_dev, hb, cudaMemcpyDeviceToDevice, st));
+  for (int k = kKRouter; k <= kKDown; ++k) {
+    cudaError_t e = c->d.scale_dtype == REC_SCALE_FP16 ? enqueue_kernel_sd<0>(c, k, layer, st, false)
+                                                       : enqueue_kernel_sd<1>(c, k, layer, st, false);
+    REC_CHECK_CUDA(e);
+  }
+  REC_CHECK_CUDA(cudaMemcpyAsync(h_dev, c->h, hb, cudaMemcpyDeviceToDevice, st));
+  if (ids_dev)
+    REC_CHECK_CUDA(cudaMemcpyAsync(ids_dev, c->ids, size_t(c->d.top_k) * 4, cudaMemcpyDeviceToDevice, st));
+  if (weights_dev)
+    REC_CHECK_CUDA(cudaMemcpyAsync(weights_dev, c->wts, size_t(c->d.top_k) * 4, cudaMemcpyDeviceToDevice, st));
+  return REC_OK;
+}
+
 REC_API int rec_set_profile(RecCtx* c, void* buf_dev, size_t entries) {
   REC_CHECK_ARG(c, "null context");
   c->prof = static_cast<unsigned long long*>(buf_dev);

@@ -59,21 +59,32 @@ def sample_logits(logits: torch.Tensor, p: abi.RecSampling, u: torch.Tensor | No
 def sample_head(h: torch.Tensor, final_norm: torch.Tensor, lm_head, scale_dtype: torch.dtype, p: abi.RecSampling,
                 u: torch.Tensor | None = None, history: torch.Tensor | None = None, eps: float = 1e-6):
     """Final RMSNorm + int4 lm_head GEMV + sampler for B hidden rows
-    Returns (ids int32 [B], logits bf16 [B, V])."""
+    (config 5) through rec_lmhead_sample.  Returns (ids int32 [B], logits
+    bf16 [B, V])."""
     from .ops import scale_dtype_code
 
-    hb = h.reshape(-1, h.shape[-1])
+    hb = h.reshape(-1, h.shape[-1]).contiguous()
     B, H = hb.shape
     V = lm_head.w.shape[0]
     logits = torch.empty(B, V, dtype=torch.bfloat16, device=h.device)
+    ids = torch.empty(B, dtype=torch.int32, device=h.device)
     m = abi.RecQMat(lm_head.w.data_ptr(), lm_head.s.data_ptr(), lm_head.b.data_ptr())
     stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
-    for b in range(B):
-        row = hb[b].contiguous()
-        check(lib().rec_gemv_int4(C.byref(m), scale_dtype_code(scale_dtype), V, H, C.c_void_p(row.data_ptr()),
-                                  C.c_void_p(final_norm.data_ptr()), float(eps), C.c_void_p(logits[b].data_ptr()),
-                                  stream), "rec_gemv_int4")
-    return sample_logits(logits, p, u, history), logits
+    hist = None
+    hist_len = 0
+    if history is not None and history.numel():
+        hist = history.to(torch.int32).reshape(B, -1).contiguous()
+        hist_len = hist.shape[1]
+    if p.temperature > 0 and u is None:
+        raise ValueError("temperature > 0 needs uniforms")
+    uu = None if u is None else u.to(torch.float32).reshape(B, -1).contiguous()
+    check(lib().rec_lmhead_sample(C.byref(m), scale_dtype_code(scale_dtype), V, H, C.c_void_p(hb.data_ptr()), B,
+                                  C.c_void_p(final_norm.data_ptr()), float(eps),
+                                  C.c_void_p(hist.data_ptr()) if hist is not None else None, hist_len, C.byref(p),
+                                  C.c_void_p(uu.data_ptr()) if uu is not None else None,
+                                  C.c_void_p(logits.data_ptr()), C.c_void_p(ids.data_ptr()), stream),
+          "rec_lmhead_sample")
+    return ids, logits
 
 
 def sampled_block(engine, state, token, count, seed, *, temperature, top_p, top_k, presence_penalty, eos=()):

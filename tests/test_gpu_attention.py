@@ -93,3 +93,41 @@ def test_attention_matches_oracle(cuda, T, bits, heads):
     got = _host(out, np.uint16)
     bad = np.flatnonzero(got != want)
     assert bad.size == 0, (bad[:8], got[bad[:8]], want[bad[:8]])
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_kv_append_matches_oracle(cuda, bits):
+    """rec_kv_append (quantize-on-append alone) against the oracle's append,
+    bit for bit, and an out-of-range position reported without a write."""
+    from rec_b200._lib import check, lib
+
+    hkv, cap, pos = 4, 512, 301
+    rng = np.random.default_rng(bits)
+    words = 128 * bits // 32
+    kv = {}
+    for n in ("k", "v"):
+        kv[f"{n}_codes"] = np.zeros((hkv, cap, words), np.uint32)
+        kv[f"{n}_scales"] = np.zeros((hkv, cap, 2), np.uint16)
+        kv[f"{n}_biases"] = np.zeros((hkv, cap, 2), np.uint16)
+    k_new = oracle.f32_to_bf16(3.0 * rng.standard_normal(hkv * 128, dtype=np.float32))
+    v_new = oracle.f32_to_bf16(rng.standard_normal(hkv * 128, dtype=np.float32))
+    dev = {n: _dev(a) for n, a in kv.items()}
+    rec = abi.RecKVLayer(*(dev[n].data_ptr() for n in ("k_codes", "k_scales", "k_biases", "v_codes", "v_scales",
+                                                      "v_biases")))
+    kd, vd = _dev(k_new), _dev(v_new)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for p, want_status in ((pos, 0), (cap, 4)):
+        pd = torch.tensor([p], dtype=torch.int32, device="cuda")
+        check(lib().rec_kv_append(C.byref(rec), hkv, cap, bits, C.c_void_p(kd.data_ptr()), C.c_void_p(vd.data_ptr()),
+                                  C.c_void_p(pd.data_ptr()), C.c_void_p(status.data_ptr()), stream), "rec_kv_append")
+        torch.cuda.synchronize()
+        assert int(status.item()) == want_status
+    lay = {n: a.copy() for n, a in kv.items()}
+    arrs = [lay[n] for n in ("k_codes", "k_scales", "k_biases", "v_codes", "v_scales", "v_biases")]
+    orec = abi.RecKVLayer(*(a.ctypes.data for a in arrs))
+    L = oracle.lib()
+    L.orc_kv_store.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+    L.orc_kv_store(C.addressof(orec), hkv, cap, bits, pos, k_new.ctypes.data, v_new.ctypes.data)
+    for n in lay:
+        assert np.array_equal(_host(dev[n], lay[n].dtype), lay[n]), n

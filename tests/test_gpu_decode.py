@@ -115,3 +115,48 @@ def test_long_context_step_bitexact(cuda, schedule, context, bits):
         ref_logits, ref_trace = host.step(hkv, 100 + i, pos)
         assert np.array_equal(_u16(trace), ref_trace), pos
         assert np.array_equal(_u16(logits), ref_logits), pos
+
+
+@pytest.mark.parametrize("variant", ["tiny_kv8_fp16", "tiny_kv4_bf16_sigmoid"])
+def test_router_moe_entry_bitexact(cuda, variant):
+    """rec_router_moe (the MoE block of one layer alone) against the oracle's
+    RMSNorm -> router -> top-k -> SwiGLU experts -> bf16 mix -> residual."""
+    import ctypes as C
+
+    from rec_b200._lib import check, lib
+
+    cfg = VARIANTS[variant]
+    w, kv, sess, host, hkv = _setup(cfg, 512, seed=11)
+    sd = 1 if cfg.scale_dtype == torch.bfloat16 else 0
+    rng = np.random.default_rng(13)
+    layer = 1 if cfg.n_layers > 1 else 0
+    h = oracle.f32_to_bf16(rng.standard_normal(cfg.hidden, dtype=np.float32))
+    h_dev = torch.from_numpy(h.view(np.int16)).cuda()
+    ids_dev = torch.zeros(cfg.top_k, dtype=torch.int32, device="cuda")
+    wts_dev = torch.zeros(cfg.top_k, dtype=torch.float32, device="cuda")
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    check(lib().rec_router_moe(sess.ctx, layer, C.c_void_p(h_dev.data_ptr()), C.c_void_p(ids_dev.data_ptr()),
+                               C.c_void_p(wts_dev.data_ptr()), stream), "rec_router_moe")
+    torch.cuda.synchronize()
+    L = w.layers[layer]
+    xn = oracle.rmsnorm(h, _np(L.post_norm), cfg.rms_eps)
+    logits = oracle.router_logits(_np(L.router), xn)
+    bias = None if L.expert_bias is None else _np(L.expert_bias)
+    ids, wts = oracle.route(logits, cfg.top_k, cfg.router_mode, bias)
+    I, H = cfg.moe_inter, cfg.hidden
+    gw, gs, gb = _np(L.gate.w), _np(L.gate.s), _np(L.gate.b)
+    uw, us, ub = _np(L.up.w), _np(L.up.s), _np(L.up.b)
+    dw, ds, db = _np(L.down.w), _np(L.down.s), _np(L.down.b)
+    downs = []
+    for e in ids:
+        rows = slice(int(e) * I, (int(e) + 1) * I)
+        g = oracle.gemv(gw[rows], gs[rows], gb[rows], xn, sd)
+        u = oracle.gemv(uw[rows], us[rows], ub[rows], xn, sd)
+        act = np.array([oracle.swiglu(int(a), int(b)) for a, b in zip(g, u)], np.uint16)
+        drows = slice(int(e) * H, (int(e) + 1) * H)
+        downs.append(oracle.gemv(dw[drows], ds[drows], db[drows], act, sd))
+    mix = oracle.mix(np.stack(downs), wts)
+    want = oracle.f32_to_bf16(oracle.bf16_to_f32(h) + oracle.bf16_to_f32(mix))
+    assert np.array_equal(ids_dev.cpu().numpy(), ids)
+    assert np.array_equal(wts_dev.cpu().numpy().view(np.uint32), wts.view(np.uint32))
+    assert np.array_equal(_u16(h_dev), want)
