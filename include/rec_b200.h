@@ -274,6 +274,17 @@ REC_API int rec_lmhead_sample(const RecQMat* lm_head, int32_t scale_dtype, int32
                               const void* h_dev, int32_t batch, const void* final_norm_dev, float eps,
                               const int32_t* history_dev, int32_t history_len, const RecSampling* params,
                               const float* uniforms_dev, void* logits_dev, int32_t* ids_dev, void* stream);
+/* Prefill projection on the tensor cores: Y[t, n] = X[t, k] . W[n, k]^T with
+ * X bf16 [t, k] row-major (16-byte aligned), W int4 g64 (MLX affine layout,
+ * scale_dtype scales and biases), Y bf16 [t, n].  n a multiple of 256, k a
+ * multiple of 64.  tcgen05 MMAs accumulate in fp32 in tensor memory from bf16
+ * operands (the weights are dequantized to bf16), so results match an fp32
+ * GEMM of the dequantized weights within bf16 rounding, not bit for bit.
+ * *status_dev is set to 1 if a bounded device wait ran out.  Replaces the
+ * quantized projections of the reference's chunked prefill
+ * (engine/src/rec_mlx/quantized.py:102-148, kernels/m4_max_prefill.py:49-144). */
+REC_API int rec_prefill_gemm(const RecQMat* w, int32_t scale_dtype, int64_t n, int32_t k, const void* x_dev,
+                             int64_t t, void* y_dev, int32_t* status_dev, void* stream);
 /* Decode attention of one layer alone (unit tests, the attention sweep):
  * quantizes the new K / V of `*position_dev` from qkv_dev (bf16 [Hq*128 |
  * Hkv*128 | Hkv*128], RoPE from rope_dev [positions][cos 64 | sin 64]) into

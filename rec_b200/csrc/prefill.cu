@@ -1,0 +1,272 @@
+// Prefill projection GEMM on the 5th-generation tensor cores (tcgen05):
+//   Y[T, N] = X[T, K] . W[N, K]^T
+// X bf16 row-major (the prompt's activations), W int4 g64 in the MLX affine
+// layout (uint32 nibbles, fp16 or bf16 scale and bias per 64 weights), Y bf16.
+// Reference: the prefill of QATSession.prefill / m4_max_prefill
+// (engine/src/rec_mlx/quantized.py:102-148, kernels/m4_max_prefill.py:49-144),
+// whose projections are mx.quantized_matmul over the prompt's tokens.
+//
+// One CTA computes a 128 x 256 tile of Y with K walked in steps of 64 (one
+// quantization group), through a 3-stage shared-memory ring:
+//   * the X tile (128 tokens x 64) arrives by TMA (cp.async.bulk.tensor, 128B
+//     swizzle) on the stage's mbarrier;
+//   * the W tile (256 rows x 64) is dequantized by the 128 threads,
+//     w = bf16(fma(scale, q, bias)), and written in the same 128B-swizzled
+//     K-major layout;
+//   * thread 0 issues four tcgen05.mma kind::f16 (M 128, N 256, K 16, bf16 in,
+//     fp32 accumulate in tensor memory) and commits them to the stage's
+//     "empty" mbarrier, which frees the stage for the next K step;
+//   * after the last step the accumulator (128 lanes x 256 columns of TMEM) is
+//     read with tcgen05.ld, rounded to bf16 and stored.
+// Every wait is bounded: a wait that runs out records kStatusBulkTimeout, the
+// CTA drains what it issued, frees its tensor memory and returns.
+//
+// Numerics: the products are exact (bf16 x bf16 in fp32) and the tensor core
+// accumulates in fp32 in its own order, so results are compared with a
+// tolerance (rounding the dequantized weights to bf16 costs ~2^-9 relative per
+// weight; the reference dequantizes in fp32).
+#include <cuda.h>
+
+#include "capi_common.h"
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace rec {
+namespace {
+
+constexpr int kPBM = 128, kPBN = 256, kPBK = 64, kPStages = 3, kPThreads = 128;
+constexpr uint32_t kATileBytes = kPBM * kPBK * 2;  // 16 KB
+constexpr uint32_t kBTileBytes = kPBN * kPBK * 2;  // 32 KB
+constexpr uint32_t kTmemCols = kPBN;               // fp32 accumulator columns
+
+struct PrefillSmem {
+  alignas(1024) uint8_t a[kPStages][kATileBytes];
+  alignas(1024) uint8_t b[kPStages][kBTileBytes];
+  uint64_t full[kPStages], empty[kPStages], done;
+  uint32_t tmem_base;
+};
+
+// Shared-memory matrix descriptor of a K-major, 128B-swizzled operand whose
+// rows are 128 bytes (64 bf16) and whose 8-row groups are 1,024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = uint64_t((saddr >> 4) & 0x3FFFu);  // start address
+  d |= uint64_t(1) << 16;                          // leading byte offset (unused for this layout)
+  d |= uint64_t(1024 >> 4) << 32;                  // stride byte offset: 8 rows x 128 B
+  d |= uint64_t(1) << 46;                          // descriptor version
+  d |= uint64_t(2) << 61;                          // 128-byte swizzle
+  return d;
+}
+// Instruction descriptor: bf16 A and B, fp32 D, both K-major, M = 128, N = 256.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kPBN >> 3) << 17) |
+                            (uint32_t(kPBM >> 4) << 24);
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cta(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int SD>
+__global__ void __launch_bounds__(kPThreads, 1)
+    k_prefill_gemm(const __grid_constant__ CUtensorMap xmap, const QMatDev w, int K, int N, int T,
+                   uint16_t* __restrict__ y, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                    ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * kPBN, m0 = blockIdx.y * kPBM;
+  const int KT = K / kPBK;
+  if (tid == 0) {
+    for (int s = 0; s < kPStages; ++s) {
+      mbar_init(&sm.full[s], kPThreads + 1);  // every thread's W rows + the X bytes
+      mbar_init(&sm.empty[s], 1);             // the MMAs that read the stage
+    }
+    mbar_init(&sm.done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&sm.tmem_base)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  bool ok = true;
+  int issued = 0;  // K steps whose MMAs thread 0 issued
+  for (int kt = 0; kt < KT && ok; ++kt) {
+    const int s = kt % kPStages;
+    const uint32_t use = uint32_t(kt / kPStages);
+    if (kt >= kPStages && !mbar_wait(&sm.empty[s], (use - 1) & 1u)) {
+      ok = false;
+      break;
+    }
+    if (tid == 0) {
+      mbar_expect_tx(&sm.full[s], kATileBytes);
+      tma_load_2d(sm.a[s], &xmap, kt * kPBK, m0, &sm.full[s]);
+    }
+    // this thread's W rows tid and tid + 128, group kt: dequantize to bf16
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const int r = tid + rr * kPThreads;
+      const size_t row = size_t(n0 + r);
+      const uint4* src = reinterpret_cast<const uint4*>(w.w + row * (K / 8) + size_t(kt) * 8);
+      const uint4 c0 = ldg128_nc(src), c1 = ldg128_nc(src + 1);
+      const float sc = sb<SD>(w.s[row * (K / 64) + kt]), bi = sb<SD>(w.b[row * (K / 64) + kt]);
+      const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      uint8_t* brow = sm.b[s] + r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // word c = elements 8c .. 8c+7 = one 16-byte chunk
+        uint32_t p[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float v0 = __fmaf_rn(sc, float((words[c] >> (8 * j)) & 15u), bi);
+          const float v1 = __fmaf_rn(sc, float((words[c] >> (8 * j + 4)) & 15u), bi);
+          p[j] = uint32_t(to_bf(v0)) | (uint32_t(to_bf(v1)) << 16);
+        }
+        *reinterpret_cast<uint4*>(brow + ((c ^ (r & 7)) << 4)) = make_uint4(p[0], p[1], p[2], p[3]);
+      }
+    }
+    fence_proxy_async_smem();  // the tensor core reads these writes through the async proxy
+    mbar_arrive_cta(&sm.full[s]);
+    if (tid == 0) {
+      if (!mbar_wait(&sm.full[s], use & 1u)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t a0 = smem_addr(sm.a[s]), b0 = smem_addr(sm.b[s]);
+#pragma unroll
+      for (int ks = 0; ks < kPBK / 16; ++ks)
+        umma_bf16(tmem, sw128_desc(a0 + ks * 32), sw128_desc(b0 + ks * 32), (kt | ks) != 0);
+      umma_commit(&sm.empty[s]);
+      ++issued;
+    }
+  }
+  // the accumulator is complete once every issued MMA has finished
+  if (tid == 0) umma_commit(&sm.done);
+  const bool done = mbar_wait(&sm.done, 0);
+  tc_fence_after();
+  ok = __syncthreads_and(ok && done && (tid != 0 || issued == KT));
+  if (ok) {
+    const int row = m0 + warp * 32 + lane;
+#pragma unroll 1
+    for (int c = 0; c < kPBN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c * 32), r);
+      if (row < T) {
+        uint4* dst = reinterpret_cast<uint4*>(y + size_t(row) * N + n0 + c * 32);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            o[j] = uint32_t(to_bf(__uint_as_float(r[8 * q + 2 * j]))) |
+                   (uint32_t(to_bf(__uint_as_float(r[8 * q + 2 * j + 1]))) << 16);
+          dst[q] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+    }
+  } else if (tid == 0) {
+    report(status, kStatusBulkTimeout);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+  static EncodeTiled fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  }
+  return fn;
+}
+
+template <int SD>
+cudaError_t launch_prefill(const CUtensorMap& map, const QMatDev& w, int K, int N, int T, uint16_t* y, int* status,
+                           cudaStream_t st) {
+  const size_t smem = sizeof(PrefillSmem) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(k_prefill_gemm<SD>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return e;
+  dim3 grid(N / kPBN, (T + kPBM - 1) / kPBM);
+  k_prefill_gemm<SD><<<grid, kPThreads, smem, st>>>(map, w, K, N, T, y, status);
+  return cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace rec
+
+using namespace rec;
+
+REC_API int rec_prefill_gemm(const RecQMat* w, int32_t scale_dtype, int64_t n, int32_t k, const void* x_dev,
+                             int64_t t, void* y_dev, int32_t* status_dev, void* stream) {
+  REC_CHECK_ARG(w && w->w && w->scales && w->biases && x_dev && y_dev && status_dev, "rec_prefill_gemm: null pointer");
+  REC_CHECK_ARG(n > 0 && n % kPBN == 0 && n < (1ll << 30), "rec_prefill_gemm: N=%lld must be a multiple of %d",
+                (long long)n, kPBN);
+  REC_CHECK_ARG(k >= kPBK && k % kPBK == 0, "rec_prefill_gemm: K=%d must be a positive multiple of %d", k, kPBK);
+  REC_CHECK_ARG(t > 0 && t < (1ll << 31), "rec_prefill_gemm: bad token count");
+  REC_CHECK_ARG(aligned16(x_dev) && aligned16(y_dev) && aligned16(w->w), "rec_prefill_gemm: buffers must be 16-byte aligned");
+  REC_CHECK_ARG(scale_dtype == REC_SCALE_FP16 || scale_dtype == REC_SCALE_BF16, "bad scale dtype");
+  EncodeTiled enc = encode_fn();
+  REC_CHECK_ARG(enc, "rec_prefill_gemm: cuTensorMapEncodeTiled is unavailable");
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(t)};
+  const cuuint64_t strides[1] = {cuuint64_t(k) * 2};
+  const cuuint32_t box[2] = {kPBK, kPBM};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x_dev), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  REC_CHECK_ARG(r == CUDA_SUCCESS, "rec_prefill_gemm: tensor map encoding failed (%d)", int(r));
+  const QMatDev wd = {static_cast<const uint32_t*>(w->w), static_cast<const uint16_t*>(w->scales),
+                      static_cast<const uint16_t*>(w->biases)};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = scale_dtype == REC_SCALE_FP16
+                      ? launch_prefill<0>(map, wd, k, int(n), int(t), static_cast<uint16_t*>(y_dev), status_dev, st)
+                      : launch_prefill<1>(map, wd, k, int(n), int(t), static_cast<uint16_t*>(y_dev), status_dev, st);
+  REC_CHECK_CUDA(e);
+  return REC_OK;
+}
