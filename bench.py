@@ -50,6 +50,9 @@ def parse():
     p.add_argument("--attn-sweep", action="store_true",
                    help="config 2: time the attention kernels alone over --contexts (4-bit cache unless --kv-bits 8)")
     p.add_argument("--contexts", default="1024,8192,32768,131072,258048")
+    p.add_argument("--prefill", action="store_true",
+                   help="the tensor-core prefill projections (rec_prefill_gemm) of one config-3 layer")
+    p.add_argument("--tokens", default="1024,4096", help="prompt lengths for --prefill")
     p.add_argument("--shard", action="store_true",
                    help="with N GPUs: one session split over the GPUs (expert parallelism + split-KV, the "
                         "config-4 partitioning) instead of N independent sessions (config 3 replicas)")
@@ -514,9 +517,65 @@ def run_attn_sweep(args):
           flush=True)
 
 
+def run_prefill(args):
+    """The prefill projections of one config-3 layer on the tensor cores
+    (rec_prefill_gemm: QKV 5,120 x 2,048, O 2,048 x 4,096, one expert's
+    gate/up 1,536 x 2,048 and down 2,048 x 768 over all T tokens) at each
+    prompt length; TFLOP/s against the measured dense bf16 peak."""
+    import ctypes as C
+
+    import torch
+
+    from rec_b200 import abi
+    from rec_b200._lib import check, lib
+
+    torch.cuda.set_device(0)
+    f = ROOT / "MEASURED_PEAKS.json"
+    peak, kind = (json.loads(f.read_text())["bf16_tflops"], "measured") if f.exists() else (1590.0, "fallback")
+    shapes = [("qkv", 5120, 2048), ("o_proj", 2048, 4096), ("expert_gate_up", 1536, 2048), ("expert_down", 2048, 768)]
+    rows = []
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for T in [int(t) for t in args.tokens.split(",")]:
+        for name, N, K in shapes:
+            g = torch.Generator(device="cuda").manual_seed(N + K + T)
+            w = torch.randint(-2**31, 2**31 - 1, (N, K // 8), generator=g, device="cuda", dtype=torch.int32)
+            sc = (torch.rand(N, K // 64, generator=g, device="cuda") * 0.01).to(torch.float16)
+            bi = (torch.rand(N, K // 64, generator=g, device="cuda") - 0.5).mul(0.1).to(torch.float16)
+            x = torch.randn(T, K, generator=g, device="cuda").to(torch.bfloat16)
+            y = torch.empty(T, N, dtype=torch.bfloat16, device="cuda")
+            status = torch.zeros(1, dtype=torch.int32, device="cuda")
+            m = abi.RecQMat(w.data_ptr(), sc.data_ptr(), bi.data_ptr())
+
+            def call():
+                check(lib().rec_prefill_gemm(C.byref(m), abi.REC_SCALE_FP16, N, K, C.c_void_p(x.data_ptr()), T,
+                                             C.c_void_p(y.data_ptr()), C.c_void_p(status.data_ptr()), stream),
+                      "rec_prefill_gemm")
+
+            for _ in range(max(3, args.warmup)):
+                call()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(args.steps):
+                call()
+            b.record()
+            torch.cuda.synchronize()
+            if int(status.item()) != 0:
+                raise RuntimeError(f"prefill GEMM reported device status {int(status.item())}")
+            us = a.elapsed_time(b) / args.steps * 1e3
+            tf = 2.0 * T * N * K / us / 1e6
+            rows.append({"tokens": T, "gemm": name, "N": N, "K": K, "us": round(us, 2), "TFLOPs": round(tf, 1),
+                         "frac": round(tf / peak, 4)})
+    print(json.dumps({"workload": "prefill_projections_tcgen05", "peak_TFLOPs": peak, "peak_source": kind,
+                      "steps": args.steps, "dtype": "bf16 x bf16 -> fp32 (int4 g64 weights dequantized in smem)",
+                      "rows": rows}), flush=True)
+
+
 def main():
     args = parse()
-    if args.attn_sweep:
+    if args.prefill:
+        run_prefill(args)
+    elif args.attn_sweep:
         run_attn_sweep(args)
     elif args.impl == "reference":
         run_reference(args)

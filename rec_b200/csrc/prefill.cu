@@ -10,7 +10,8 @@
 // quantization group), through a 3-stage shared-memory ring:
 //   * the X tile (128 tokens x 64) arrives by TMA (cp.async.bulk.tensor, 128B
 //     swizzle) on the stage's mbarrier;
-//   * the W tile (256 rows x 64) is dequantized by the 128 threads,
+//   * the W tile (256 rows x 64) is dequantized by the 256 threads (one row
+//     each, its codes fetched one K step ahead),
 //     w = bf16(fma(scale, q, bias)), and written in the same 128B-swizzled
 //     K-major layout;
 //   * thread 0 issues four tcgen05.mma kind::f16 (M 128, N 256, K 16, bf16 in,
@@ -34,7 +35,7 @@
 namespace rec {
 namespace {
 
-constexpr int kPBM = 128, kPBN = 256, kPBK = 64, kPStages = 3, kPThreads = 128;
+constexpr int kPBM = 128, kPBN = 256, kPBK = 64, kPStages = 3, kPThreads = 256;
 constexpr uint32_t kATileBytes = kPBM * kPBK * 2;  // 16 KB
 constexpr uint32_t kBTileBytes = kPBN * kPBK * 2;  // 32 KB
 constexpr uint32_t kTmemCols = kPBN;               // fp32 accumulator columns
@@ -128,9 +129,36 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
   bool ok = true;
   int issued = 0;  // K steps whose MMAs thread 0 issued
+  // this thread's W row (tid): codes, scale and bias of the next K step are
+  // loaded one step ahead
+  constexpr int RPT = kPBN / kPThreads;  // rows per thread
+  uint4 nc[RPT][2];
+  uint16_t ns[RPT], nb[RPT];
+  auto fetch = [&](int kt) {
+#pragma unroll
+    for (int rr = 0; rr < RPT; ++rr) {
+      const size_t row = size_t(n0 + tid + rr * kPThreads);
+      const uint4* src = reinterpret_cast<const uint4*>(w.w + row * (K / 8) + size_t(kt) * 8);
+      nc[rr][0] = ldg128_nc(src);
+      nc[rr][1] = ldg128_nc(src + 1);
+      ns[rr] = w.s[row * (K / 64) + kt];
+      nb[rr] = w.b[row * (K / 64) + kt];
+    }
+  };
+  fetch(0);
   for (int kt = 0; kt < KT && ok; ++kt) {
     const int s = kt % kPStages;
     const uint32_t use = uint32_t(kt / kPStages);
+    uint4 cc[RPT][2];
+    uint16_t cs[RPT], cb[RPT];
+#pragma unroll
+    for (int rr = 0; rr < RPT; ++rr) {
+      cc[rr][0] = nc[rr][0];
+      cc[rr][1] = nc[rr][1];
+      cs[rr] = ns[rr];
+      cb[rr] = nb[rr];
+    }
+    if (kt + 1 < KT) fetch(kt + 1);
     if (kt >= kPStages && !mbar_wait(&sm.empty[s], (use - 1) & 1u)) {
       ok = false;
       break;
@@ -139,24 +167,24 @@ __global__ void __launch_bounds__(kPThreads, 1)
       mbar_expect_tx(&sm.full[s], kATileBytes);
       tma_load_2d(sm.a[s], &xmap, kt * kPBK, m0, &sm.full[s]);
     }
-    // this thread's W rows tid and tid + 128, group kt: dequantize to bf16
+    // dequantize: float(q) from the bits 0x4B000000 | q minus 2^23 (exact),
+    // w = fma(scale, q, bias), two values per packed bf16 conversion
 #pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
+    for (int rr = 0; rr < RPT; ++rr) {
       const int r = tid + rr * kPThreads;
-      const size_t row = size_t(n0 + r);
-      const uint4* src = reinterpret_cast<const uint4*>(w.w + row * (K / 8) + size_t(kt) * 8);
-      const uint4 c0 = ldg128_nc(src), c1 = ldg128_nc(src + 1);
-      const float sc = sb<SD>(w.s[row * (K / 64) + kt]), bi = sb<SD>(w.b[row * (K / 64) + kt]);
-      const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const float sc = sb<SD>(cs[rr]), bi = sb<SD>(cb[rr]);
+      const uint32_t words[8] = {cc[rr][0].x, cc[rr][0].y, cc[rr][0].z, cc[rr][0].w,
+                                 cc[rr][1].x, cc[rr][1].y, cc[rr][1].z, cc[rr][1].w};
       uint8_t* brow = sm.b[s] + r * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {  // word c = elements 8c .. 8c+7 = one 16-byte chunk
         uint32_t p[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float v0 = __fmaf_rn(sc, float((words[c] >> (8 * j)) & 15u), bi);
-          const float v1 = __fmaf_rn(sc, float((words[c] >> (8 * j + 4)) & 15u), bi);
-          p[j] = uint32_t(to_bf(v0)) | (uint32_t(to_bf(v1)) << 16);
+          const float q0 = __fsub_rn(__uint_as_float(((words[c] >> (8 * j)) & 15u) | 0x4B000000u), 8388608.0f);
+          const float q1 = __fsub_rn(__uint_as_float(((words[c] >> (8 * j + 4)) & 15u) | 0x4B000000u), 8388608.0f);
+          const __nv_bfloat162 v = __floats2bfloat162_rn(__fmaf_rn(sc, q0, bi), __fmaf_rn(sc, q1, bi));
+          p[j] = *reinterpret_cast<const uint32_t*>(&v);
         }
         *reinterpret_cast<uint4*>(brow + ((c ^ (r & 7)) << 4)) = make_uint4(p[0], p[1], p[2], p[3]);
       }
@@ -183,11 +211,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
   tc_fence_after();
   ok = __syncthreads_and(ok && done && (tid != 0 || issued == KT));
   if (ok) {
-    const int row = m0 + warp * 32 + lane;
+    // warp w reads TMEM lanes 32 (w % 4) .. +31 (its lane quarter) and the
+    // column half w / 4
+    const int quarter = warp & 3, half = warp >> 2;
+    const int row = m0 + quarter * 32 + lane;
 #pragma unroll 1
-    for (int c = 0; c < kPBN / 32; ++c) {
+    for (int c = half * (kPBN / 64); c < (half + 1) * (kPBN / 64); ++c) {
       uint32_t r[32];
-      tmem_ld32(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c * 32), r);
+      tmem_ld32(tmem + (uint32_t(quarter * 32) << 16) + uint32_t(c * 32), r);
       if (row < T) {
         uint4* dst = reinterpret_cast<uint4*>(y + size_t(row) * N + n0 + c * 32);
 #pragma unroll
