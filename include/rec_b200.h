@@ -203,7 +203,9 @@ REC_API int rec_router_moe(RecCtx* ctx, int32_t layer, void* h_dev, int32_t* ids
 REC_API int rec_set_profile(RecCtx* ctx, void* buf_dev, size_t entries);
 /* Optional stamps inside one layer (step 0 of a launch) of the persistent
  * kernel: uint64 [cta][64] %globaltimer values at fixed points of the
- * attention and expert phases (diagnostics; no reference counterpart). */
+ * attention and expert phases (diagnostics; no reference counterpart).  The
+ * stamps exist only in a library built with REC_LAYER_STAMPS=1 (see
+ * rec_b200/build.py); otherwise the buffer is left untouched. */
 REC_API int rec_set_layer_profile(RecCtx* ctx, void* buf_dev, int32_t layer);
 /* Reads the device status word (synchronises `stream`).  Non-zero marks the
  * session unusable. */

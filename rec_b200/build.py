@@ -26,6 +26,12 @@ NVCC_FLAGS = [
 ]
 
 
+if os.environ.get("REC_LAYER_STAMPS"):
+    # diagnostic build: the persistent kernel's in-layer stamps
+    # (rec_set_layer_profile); remove _build/ to rebuild with a new setting
+    NVCC_FLAGS.append("-DREC_LAYER_STAMPS")
+
+
 def _nvcc() -> str:
     for cand in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", shutil.which("nvcc")):
         if cand and Path(cand).exists():

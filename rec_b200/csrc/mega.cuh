@@ -248,12 +248,18 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   return v;
 }
 
+// In-layer stamps are compiled in only with -DREC_LAYER_STAMPS (diagnostic
+// builds): each site costs instructions in code that runs once per layer.
 __device__ __forceinline__ void stamp(const MegaArgs& a, int step, int layer, int slot) {
+#ifdef REC_LAYER_STAMPS
   if (a.prof2 && step == 0 && layer == a.prof_layer) a.prof2[blockIdx.x * 64 + slot] = globaltimer();
+#endif
 }
 // Adds v to a per-CTA diagnostic slot of the same layer profile.
 __device__ __forceinline__ void prof_add(const MegaArgs& a, int step, int layer, int slot, unsigned long long v) {
+#ifdef REC_LAYER_STAMPS
   if (a.prof2 && step == 0 && layer == a.prof_layer) a.prof2[blockIdx.x * 64 + slot] += v;
+#endif
 }
 
 // Grid barrier index of a phase: each step has 6 per layer + 1 (after H).
@@ -974,7 +980,7 @@ struct Consumers {
     return true;
   }
 
-  __device__ void write_attn(int h, const Partial4& F) {
+  __device__ __noinline__ void write_attn(int h, const Partial4& F) {
     uint2 o;
     o.x = uint32_t(to_bf(__fdiv_rn(F.a[0], F.l))) | (uint32_t(to_bf(__fdiv_rn(F.a[1], F.l))) << 16);
     o.y = uint32_t(to_bf(__fdiv_rn(F.a[2], F.l))) | (uint32_t(to_bf(__fdiv_rn(F.a[3], F.l))) << 16);
@@ -1053,6 +1059,32 @@ struct Consumers {
   // Routing, computed by all consumer warps of every CTA (one thread per
   // expert; the sums keep the canonical lane order).  The code is compact
   // (runtime loops): it runs once per layer and is fetched cold.
+  // Rank of expert i among choices [j0, j1): #{j : c_j > c_i or (c_j == c_i
+  // and j < i)}.
+  __device__ __noinline__ int rank_of(int i, int j0, int j1) const {
+    const float ci = sm.route_c[i];
+    int rank = 0;
+    if (((j1 - j0) & 3) == 0) {
+      const float4* c4 = reinterpret_cast<const float4*>(sm.route_c + j0);
+#pragma unroll 2
+      for (int q = 0; q < (j1 - j0) / 4; ++q) {
+        const float4 cv = c4[q];
+        const int j = j0 + 4 * q;
+        rank += (cv.x > ci || (cv.x == ci && j < i)) ? 1 : 0;
+        rank += (cv.y > ci || (cv.y == ci && j + 1 < i)) ? 1 : 0;
+        rank += (cv.z > ci || (cv.z == ci && j + 2 < i)) ? 1 : 0;
+        rank += (cv.w > ci || (cv.w == ci && j + 3 < i)) ? 1 : 0;
+      }
+    } else {
+#pragma unroll 1
+      for (int j = j0; j < j1; ++j) {
+        const float cj = sm.route_c[j];
+        rank += (cj > ci || (cj == ci && j < i)) ? 1 : 0;
+      }
+    }
+    return rank;
+  }
+
   __device__ void route(const MegaLayer& L, int step_, int layer_) {
     const int E = a.E, t = threadIdx.x - 32, nt = kMegaCons * 32;
 #pragma unroll 1
@@ -1096,29 +1128,6 @@ struct Consumers {
     // the selection, in rank order (largest first, lowest index on ties).
     // Pairs of threads split the comparisons of one expert when 2E fits the
     // consumer threads and E is a multiple of 8 (float4 reads of each half).
-    auto rank_of = [&](int i, int j0, int j1) {
-      const float ci = sm.route_c[i];
-      int rank = 0;
-      if (((j1 - j0) & 3) == 0) {
-        const float4* c4 = reinterpret_cast<const float4*>(sm.route_c + j0);
-#pragma unroll 4
-        for (int q = 0; q < (j1 - j0) / 4; ++q) {
-          const float4 cv = c4[q];
-          const int j = j0 + 4 * q;
-          rank += (cv.x > ci || (cv.x == ci && j < i)) ? 1 : 0;
-          rank += (cv.y > ci || (cv.y == ci && j + 1 < i)) ? 1 : 0;
-          rank += (cv.z > ci || (cv.z == ci && j + 2 < i)) ? 1 : 0;
-          rank += (cv.w > ci || (cv.w == ci && j + 3 < i)) ? 1 : 0;
-        }
-      } else {
-#pragma unroll 4
-        for (int j = j0; j < j1; ++j) {
-          const float cj = sm.route_c[j];
-          rank += (cj > ci || (cj == ci && j < i)) ? 1 : 0;
-        }
-      }
-      return rank;
-    };
     if (2 * E <= nt && (E & 7) == 0) {
       const bool act = t < 2 * E;  // threads t, t^1 share expert t/2
       const int i = t >> 1, half = t & 1;
