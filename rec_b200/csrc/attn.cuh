@@ -17,6 +17,7 @@
 namespace rec {
 
 constexpr int kHeadsPerKv = 8;                          // q heads per kv head
+constexpr int kShortItems = 6;  // item partials per head folded by the last item's CTA (one super-chunk)
 
 // Blocks per work item: 1 while the context fits one super-chunk (short
 // contexts want many small items), 4 beyond (fewer per-item overheads).
@@ -58,6 +59,7 @@ struct AttnScratch {
     uint8_t wbuf[kAttWarps][1024];         // per-warp scratch of the query / new-row preparation
     float tree[kAttWarps / 2][36][32];     // warp states during the tree fold
     float stage[kAttWarps][4][kPartialFloats];  // per-warp partials being merged
+    float items[kHeadsPerKv][kShortItems][kPartialFloats];  // a head group's item partials (short contexts)
   } u;
   uint32_t kpatch[32], vpatch[32];         // quantized K / V row of the new token
   uint16_t kps[2], kpb[2], vps[2], vpb[2];

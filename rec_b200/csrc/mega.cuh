@@ -159,6 +159,8 @@ struct MegaSmem {
   int xok;             // world > 1: the expert-output exchange completed
   float dsm[kMaxTopK][kDRowsMax];
   uint64_t full[kSlots], empty[kSlots];
+  uint64_t mfull;      // a short-context head group's item partials have landed
+  unsigned mpar;       // its phase parity
   uint16_t hown[kDRowsMax];  // this CTA's rows of h (it owns them in embed, O and D)
   volatile int route_seq;
   volatile int merge_seq;  // 2 (step n_layers + layer) + k: consumers passed merge barrier k
@@ -232,6 +234,13 @@ __device__ __forceinline__ AttnPlan attn_plan(const MegaArgs& a, int pos) {
   p.i_hi = min(a.super_hi * p.per_super, p.n_items);
   p.items = (p.i_hi - p.i_lo) * a.hkv;
   return p;
+}
+// One rank, one super-chunk of at most kShortItems items per head: the CTA
+// that stores a head group's last item partial folds the group itself
+// (Consumers::short_tail); otherwise the folds run after a grid barrier from
+// partials the producer stages (merge_phase, final_phase).
+__device__ __forceinline__ bool short_merge(const MegaArgs& a, const AttnPlan& P) {
+  return a.world == 1 && P.n_super == 1 && P.n_items <= kShortItems;
 }
 // Work item it of this rank: kv head g and global item index.
 __device__ __forceinline__ void attn_coords(const AttnPlan& P, int hkv, int it, int& g, int& item) {
@@ -463,6 +472,7 @@ struct Producer {
   int cur_step = 0, cur_layer = 0;  // for the diagnostics stamps
   __device__ void stamp_cur(int slot) { stamp(a, cur_step, cur_layer, slot); }
   __device__ void merge_chunks(const AttnPlan& AP, int step, int l) {
+    if (short_merge(a, AP)) return;
     cur_step = step;
     cur_layer = l;
     const int seq = 2 * (step * a.n_layers + l);
@@ -857,6 +867,45 @@ struct Consumers {
                      a.partials + (size_t(g * kHeadsPerKv) * icap + (item - item0)) * kPartialFloats,
                      size_t(icap) * kPartialFloats);
     if (warp == 0 && lane == 0) stamp(a, step_, layer_, 18);
+    if (short_merge(a, P)) short_tail(L, P, g, step_, layer_);
+  }
+
+  // Short contexts: an acq_rel counter per kv head finds the CTA that stored
+  // the group's last item partial; it bulk-copies the group's partials into
+  // its scratch and warp w folds head 8g + w: [sink], then the items in order.
+  __device__ void short_tail(const MegaLayer& L, const AttnPlan& P, int g, int step_, int layer_) {
+    cons_sync();  // every warp's partial stores precede the counter update
+    if (warp == 0 && lane == 0) {
+      unsigned* cnt = a.cnt + a.hq + g * a.n_super_max;
+      unsigned prev;
+      asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(prev) : "l"(cnt) : "memory");
+      const bool last = prev == unsigned(P.n_items - 1);
+      sm.xok = last ? 1 : 0;
+      if (last) {
+        *cnt = 0u;  // the next layer's items come after grid barriers
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        const int icap = items_cap(a.capacity);
+        const uint32_t bytes = uint32_t(P.n_items) * kPartialFloats * 4;
+        mbar_expect_tx(&sm.mfull, kHeadsPerKv * bytes);
+        for (int h = 0; h < kHeadsPerKv; ++h)
+          bulk_g2s(&sm.att.u.items[h][0][0], a.partials + size_t(g * kHeadsPerKv + h) * icap * kPartialFloats,
+                   bytes, &sm.mfull);
+      }
+    }
+    cons_sync();
+    if (!sm.xok) return;
+    const bool ok = mbar_wait(&sm.mfull, sm.mpar & 1u);
+    if (ok) {
+      const int h = g * kHeadsPerKv + warp;
+      Partial4 F = sink_partial(L, h);
+      for (int j = 0; j < P.n_items; ++j) merge_into(F, smem_partial(&sm.att.u.items[warp][j][0]));
+      write_attn(h, F);
+      if (warp == 0 && lane == 0) stamp(a, step_, layer_, 31);
+    } else if (warp == 0 && lane == 0) {
+      set_abort(a, kStatusBulkTimeout);
+    }
+    cons_sync();
+    if (warp == 0 && lane == 0) sm.mpar += 1;
   }
 
   // Folds super-chunk s of the 8 heads of kv head g from the merge slots
@@ -1227,7 +1276,7 @@ struct Consumers {
           attn_item<BITS>(L, AP, pos, g, item, step, l);
           if (warp == 0 && lane == 0) stamp(a, step, l, 13);
         }
-        {
+        if (!short_merge(a, AP)) {
           // item partials -> super-chunks (-> output); the producer stages
           // the partials into the ring once every CTA has stored its items
           const int seq = 2 * (step * a.n_layers + l);
@@ -1523,6 +1572,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_decode_mega(const MegaArgs 
     }
     sm.route_seq = 0;
     sm.merge_seq = 0;
+    mbar_init(&sm.mfull, 1);
+    sm.mpar = 0;
     sm.token0 = a.ctl[1];
     sm.pos0 = a.ctl[2];
     fence_barrier_init();
