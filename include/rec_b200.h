@@ -148,6 +148,20 @@ REC_API int rec_decode_step(RecCtx* ctx, int32_t token, int32_t position, void* 
 REC_API int rec_decode_greedy(RecCtx* ctx, int32_t token, int32_t position, int32_t count,
                               const int32_t* eos, int32_t n_eos, int32_t* ids_dev,
                               int32_t* produced_dev, void* stream);
+/* A packet of up to 64 tokens sampled on the device (temperature > 0):
+ * each step decodes one token and samples the next id from the logits with
+ * that step's uniforms (fp32 [count, vocab]; the rules of rec_sample_logits),
+ * and the id is fed back without a host round trip.  history_dev (int32
+ * [history_cap]) holds *history_len_dev ids that the penalties apply to; each
+ * sampled id is appended (up to history_cap).  Ids are recorded until an EOS
+ * id (included); ids_dev / produced_dev as for rec_decode_greedy.  Replaces
+ * ResidentSampler.block at temperature > 0 with its device-side Gumbel
+ * feedback (engine/src/rec_mlx/kernels/sampling.py:17-60,62-169,
+ * resident_block.py:62-88). */
+REC_API int rec_decode_sampled(RecCtx* ctx, int32_t token, int32_t position, int32_t count,
+                               const RecSampling* params, const float* uniforms_dev, int32_t* history_dev,
+                               int32_t* history_len_dev, int32_t history_cap, const int32_t* eos, int32_t n_eos,
+                               int32_t* ids_dev, int32_t* produced_dev, void* stream);
 /* ---- one session over several GPUs (one process per GPU) ----------------
  * Expert parallelism + split-KV along the sequence: rank r holds experts
  * [expert_lo, expert_hi) (its layer weights' gate/up/down hold only those,

@@ -19,6 +19,7 @@
 #include "capi_common.h"
 #include "mega.cuh"
 #include "moe.cuh"
+#include "sample.cuh"
 
 namespace rec {
 
@@ -34,14 +35,17 @@ enum Ctrl : int {
   kCtlArgmax = 7,
   kCtlEos = 8,       // 8 slots
   kCtlRecorded = 16, // 64 slots: ids produced by the current packet
-  kCtlInts = 80,
+  kCtlSampled = 80,  // 1: a sampled packet; the sampler feeds the next token back
+  kCtlInts = 96,
 };
 constexpr int kMaxPacket = 64;
 constexpr int kMaxEos = 8;
 
 // token < 0: continue from the token and position held on the device.
-__global__ void k_set_step(int* ctl, int token, int position, int n_eos, const int4 eos_lo, const int4 eos_hi) {
+__global__ void k_set_step(int* ctl, int token, int position, int n_eos, const int4 eos_lo, const int4 eos_hi,
+                           int sampled) {
   if (threadIdx.x == 0) {
+    ctl[kCtlSampled] = sampled;
     if (token >= 0) {
       ctl[kCtlToken] = token;
       ctl[kCtlPosition] = position;
@@ -85,6 +89,11 @@ __global__ void k_step_end(int* ctl) {
   if (threadIdx.x == 0) {
     const int t = ctl[kCtlArgmax];
     const int step = ctl[kCtlStep];
+    if (ctl[kCtlSampled]) {  // the sampler records the id and feeds it back
+      ctl[kCtlPosition] += 1;
+      ctl[kCtlStep] = step + 1;
+      return;
+    }
     if (ctl[kCtlActive]) {
       if (step < kMaxPacket) ctl[kCtlRecorded + step] = t;
       ctl[kCtlProduced] += 1;
@@ -775,7 +784,7 @@ REC_API int rec_decode_step(RecCtx* c, int32_t token, int32_t position, void* lo
   }
   REC_CHECK_ARG(token >= 0 && token < c->d.vocab, "token %d outside the vocabulary", token);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  k_set_step<<<1, 32, 0, st>>>(c->ctl, token, position, 0, make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0));
+  k_set_step<<<1, 32, 0, st>>>(c->ctl, token, position, 0, make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0), 0);
   REC_CHECK_CUDA(cudaGetLastError());
   if (c->use_mega) REC_CHECK_CUDA(launch_mega(c, 1, st));
   else REC_CHECK_CUDA(cudaGraphLaunch(c->step_exec, st));
@@ -802,11 +811,74 @@ REC_API int rec_decode_greedy(RecCtx* c, int32_t token, int32_t position, int32_
   for (int i = 0; i < n_eos; ++i) e8[i] = eos[i];
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   k_set_step<<<1, 32, 0, st>>>(c->ctl, token, position, n_eos, make_int4(e8[0], e8[1], e8[2], e8[3]),
-                               make_int4(e8[4], e8[5], e8[6], e8[7]));
+                               make_int4(e8[4], e8[5], e8[6], e8[7]), 0);
   REC_CHECK_CUDA(cudaGetLastError());
   if (c->use_mega) REC_CHECK_CUDA(launch_mega(c, count, st));
   else
     for (int i = 0; i < count; ++i) REC_CHECK_CUDA(cudaGraphLaunch(c->step_exec, st));
+  if (ids_dev)
+    REC_CHECK_CUDA(cudaMemcpyAsync(ids_dev, c->ctl + kCtlRecorded, size_t(count) * 4, cudaMemcpyDeviceToDevice, st));
+  if (produced_dev)
+    REC_CHECK_CUDA(cudaMemcpyAsync(produced_dev, c->ctl + kCtlProduced, 4, cudaMemcpyDeviceToDevice, st));
+  return REC_OK;
+}
+
+REC_API int rec_decode_sampled(RecCtx* c, int32_t token, int32_t position, int32_t count,
+                               const RecSampling* params, const float* uniforms_dev, int32_t* history_dev,
+                               int32_t* history_len_dev, int32_t history_cap, const int32_t* eos, int32_t n_eos,
+                               int32_t* ids_dev, int32_t* produced_dev, void* stream) {
+  int rc = check_ready(c);
+  if (rc) return rc;
+  const int V = c->d.vocab;
+  REC_CHECK_ARG(params && uniforms_dev, "rec_decode_sampled: null parameters or uniforms");
+  REC_CHECK_ARG(count >= 1 && count <= kMaxPacket, "packet must contain between 1 and %d tokens", kMaxPacket);
+  REC_CHECK_ARG(n_eos >= 0 && n_eos <= kMaxEos && (n_eos == 0 || eos), "between 0 and %d EOS ids", kMaxEos);
+  REC_CHECK_ARG(token >= 0 && token < V, "token %d outside the vocabulary", token);
+  REC_CHECK_ARG(V <= kSampleMaxVocab, "vocabulary above %d", kSampleMaxVocab);
+  const RecSampling& p = *params;
+  REC_CHECK_ARG(p.temperature > 0.0f && p.temperature < 1e30f, "rec_decode_sampled: temperature must be positive");
+  REC_CHECK_ARG(p.repetition_penalty > 0.0f, "repetition penalty must be positive");
+  REC_CHECK_ARG(p.top_k >= 0 && p.top_k < V && p.top_k <= kSampleMaxTopK, "top_k must be between 0 and %d",
+                V - 1 < kSampleMaxTopK ? V - 1 : kSampleMaxTopK);
+  REC_CHECK_ARG(p.top_p > 0.0f, "top_p must be positive");
+  REC_CHECK_ARG(p.top_k > 0 || p.top_p >= 1.0f, "top_p < 1 needs top_k > 0");
+  REC_CHECK_ARG(history_cap >= 0 && (history_cap == 0 || (history_dev && history_len_dev)),
+                "rec_decode_sampled: a history needs its buffer and length");
+  if (position < 0 || position + count > position_limit(c)) {
+    set_error("Decode context limit exhausted");
+    return REC_ELIMIT;
+  }
+  int e8[8] = {-1, -1, -1, -1, -1, -1, -1, -1};
+  for (int i = 0; i < n_eos; ++i) e8[i] = eos[i];
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  k_set_step<<<1, 32, 0, st>>>(c->ctl, token, position, n_eos, make_int4(e8[0], e8[1], e8[2], e8[3]),
+                               make_int4(e8[4], e8[5], e8[6], e8[7]), 1);
+  REC_CHECK_CUDA(cudaGetLastError());
+  SampleArgs sa = {};
+  sa.logits = c->logits;
+  sa.stride = V;
+  sa.V = V;
+  sa.history = history_cap ? history_dev : nullptr;
+  sa.n_hist = 0;
+  sa.temperature = p.temperature;
+  sa.top_k = p.top_k;
+  sa.top_p = p.top_p;
+  sa.rep = p.repetition_penalty;
+  sa.presence = p.presence_penalty;
+  sa.ids = c->ctl + kCtlArgmax;  // the id also lands in the packet's record and next-token slots
+  sa.ctl = c->ctl;
+  sa.hist_len = history_cap ? history_len_dev : nullptr;
+  sa.hist_out = history_cap ? history_dev : nullptr;
+  sa.hist_cap = history_cap;
+  const size_t dyn = size_t((V + 31) / 32) * 4;
+  REC_CHECK_CUDA(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, int(dyn)));
+  for (int i = 0; i < count; ++i) {
+    if (c->use_mega) REC_CHECK_CUDA(launch_mega(c, 1, st));
+    else REC_CHECK_CUDA(cudaGraphLaunch(c->step_exec, st));
+    sa.uniforms = uniforms_dev + size_t(i) * V;
+    k_sample<<<1, kSampleThreads, dyn, st>>>(sa);
+    REC_CHECK_CUDA(cudaGetLastError());
+  }
   if (ids_dev)
     REC_CHECK_CUDA(cudaMemcpyAsync(ids_dev, c->ctl + kCtlRecorded, size_t(count) * 4, cudaMemcpyDeviceToDevice, st));
   if (produced_dev)

@@ -1540,7 +1540,12 @@ struct Consumers {
         }
         if (lane == 0) {
           sm.token = bi;
-          if (blockIdx.x == 0) {
+          if (blockIdx.x == 0 && a.ctl[80]) {
+            // sampled packet: the sampler records the id and feeds it back
+            a.ctl[7] = bi;
+            a.ctl[2] = pos + 1;
+            a.ctl[5] += 1;
+          } else if (blockIdx.x == 0) {
             int* ctl = a.ctl;
             if (ctl[3]) {  // active
               if (ctl[5] < 64) ctl[16 + ctl[5]] = bi;

@@ -44,7 +44,39 @@ struct SampleArgs {
   int top_k;
   const float* uniforms;   // fp32 [B, V] (temperature > 0)
   int* ids;                // int32 [B]; -1: more than kSampleMaxCand ties at the threshold
+  // feedback mode (batch 1, a decode packet on the device): when ctl is set,
+  // the history length is read from *hist_len, and the sampled id becomes
+  // the session's next token, is recorded for the packet (with the EOS stop)
+  // and is appended to history (up to hist_cap ids)
+  int* ctl;
+  int* hist_len;
+  int* hist_out;
+  int hist_cap;
 };
+
+// The control-block slots of a decode packet (decode.cu's Ctrl).
+constexpr int kCtlSlotToken = 1, kCtlSlotActive = 3, kCtlSlotProduced = 4, kCtlSlotStep = 5, kCtlSlotNEos = 6,
+              kCtlSlotEos = 8, kCtlSlotRecorded = 16, kCtlMaxRecorded = 64;
+
+// Row b's sampled id (one thread): the output, and in feedback mode the
+// packet bookkeeping that the decode step leaves to the sampler.
+__device__ __forceinline__ void sample_finish(const SampleArgs& a, int b, int id) {
+  a.ids[b] = id;
+  if (!a.ctl) return;
+  int* ctl = a.ctl;
+  const int step = ctl[kCtlSlotStep] - 1;  // the decode step already advanced it
+  if (ctl[kCtlSlotActive]) {
+    if (step >= 0 && step < kCtlMaxRecorded) ctl[kCtlSlotRecorded + step] = id;
+    ctl[kCtlSlotProduced] += 1;
+    for (int i = 0; i < ctl[kCtlSlotNEos]; ++i)
+      if (ctl[kCtlSlotEos + i] == id) ctl[kCtlSlotActive] = 0;
+  }
+  ctl[kCtlSlotToken] = id < 0 ? 0 : id;
+  if (id >= 0 && a.hist_len && *a.hist_len < a.hist_cap) {
+    a.hist_out[*a.hist_len] = id;
+    *a.hist_len += 1;
+  }
+}
 
 // Order-preserving unsigned key of a non-NaN float (-0 must be canonicalised).
 __device__ __forceinline__ uint32_t float_key(float x) {
@@ -98,19 +130,20 @@ __device__ __forceinline__ void block_argmax(float& v, int& i, SampleSmem& s) {
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const SampleArgs a) {
+static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const SampleArgs a) {
   extern __shared__ uint32_t seen[];  // history bitmap [ceil(V/32)]
   __shared__ SampleSmem s;
   const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int V = a.V;
   const uint16_t* lg = a.logits + size_t(b) * a.stride;
   const bool pen = a.rep != 1.0f || a.presence != 0.0f;
+  const int n_hist = a.hist_len ? *a.hist_len : a.n_hist;
   const int nw = (V + 31) >> 5;
   if (pen) {
     for (int i = t; i < nw; i += kSampleThreads) seen[i] = 0u;
     __syncthreads();
-    for (int i = t; i < a.n_hist; i += kSampleThreads) {
-      const int id = a.history[size_t(b) * a.n_hist + i];
+    for (int i = t; i < n_hist; i += kSampleThreads) {
+      const int id = a.history[size_t(b) * n_hist + i];
       if (id >= 0 && id < V) atomicOr(&seen[id >> 5], 1u << (id & 31));
     }
     __syncthreads();
@@ -139,7 +172,7 @@ __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const SampleArgs a
   }
   block_argmax(mx, mi, s);
   if (a.temperature == 0.0f) {
-    if (t == 0) a.ids[b] = mi;
+    if (t == 0) sample_finish(a, b, mi);
     return;
   }
   const float M = mx;
@@ -203,7 +236,7 @@ __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const SampleArgs a
       if (z > bv) { bv = z; bi = i; }
     }
     block_argmax(bv, bi, s);
-    if (t == 0) a.ids[b] = bi;
+    if (t == 0) sample_finish(a, b, bi);
     return;
   }
 
@@ -215,7 +248,7 @@ __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const SampleArgs a
   const int greater = a.top_k - 1 - s.rank;
   const int n = greater + s.tied;
   if (n > kSampleMaxCand) {
-    if (t == 0) a.ids[b] = -1;
+    if (t == 0) sample_finish(a, b, -1);
     return;
   }
   // ---- collect the elements >= theta
@@ -286,7 +319,7 @@ __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const SampleArgs a
       const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
       if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
     }
-    if (lane == 0) a.ids[b] = bi;
+    if (lane == 0) sample_finish(a, b, bi);
   }
 }
 

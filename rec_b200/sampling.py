@@ -88,38 +88,48 @@ def sample_head(h: torch.Tensor, final_norm: torch.Tensor, lm_head, scale_dtype:
 
 
 def sampled_block(engine, state, token, count, seed, *, temperature, top_p, top_k, presence_penalty, eos=()):
-    """ResidentSampler.block for temperature > 0: each step decodes on the
-    device, samples with the step's uniforms and feeds the id back.
-    state["presence_mask"] (float [V], the reference's key) marks the ids the
-    presence penalty applies to."""
+    """ResidentSampler.block for temperature > 0 through rec_decode_sampled:
+    the packet decodes and samples on the device with the step's uniforms,
+    feeding each id back without a host round trip.  state["presence_mask"]
+    (float [V], the reference's key) marks the ids the presence penalty
+    applies to; the packet's ids are added to it afterwards."""
     sess = engine._session(state)
     V = engine.weights.cfg.vocab
     dev = sess.logits.device
     p = params(temperature, top_k, top_p, 1.0, presence_penalty)
-    u = uniforms(count, V, seed, dev)
+    u = uniforms(count, V, seed, dev).contiguous()
     mask = state.get("presence_mask")
     if presence_penalty and mask is None:
         mask = torch.zeros(V, dtype=torch.float32, device=dev)
         state["presence_mask"] = mask
-    ids = []
-    ids_dev = torch.empty(1, dtype=torch.int32, device=dev)
+    hist = hist_len = None
+    cap = 0
+    if presence_penalty:
+        seen = torch.nonzero(mask).to(torch.int32).reshape(-1)
+        cap = int(seen.numel()) + count
+        hist = torch.zeros(cap, dtype=torch.int32, device=dev)
+        hist[: seen.numel()] = seen
+        hist_len = torch.tensor([seen.numel()], dtype=torch.int32, device=dev)
+    eos_ids = list(eos)[:8]
+    eos_arr = (C.c_int32 * max(1, len(eos_ids)))(*eos_ids) if eos_ids else None
+    ids_dev = torch.zeros(count, dtype=torch.int32, device=dev)
+    produced = torch.zeros(1, dtype=torch.int32, device=dev)
     pos = state["position"]
 
     def run():
-        tok = int(token)
-        for i in range(count):
-            logits, _ = sess.step(tok, pos + i)
-            hist = torch.nonzero(mask).to(torch.int32).reshape(-1) if presence_penalty else None
-            sample_logits(logits, p, u[i], hist, out=ids_dev)
-            tok = int(ids_dev.item())
-            if tok < 0:
-                raise RuntimeError("Invalid sampled chain")
-            ids.append(tok)
-            if presence_penalty:
-                mask[tok] = 1.0
-            if tok in eos:
-                break
+        stream = C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        check(lib().rec_decode_sampled(sess.ctx, int(token), pos, count, C.byref(p), C.c_void_p(u.data_ptr()),
+                                       C.c_void_p(hist.data_ptr()) if hist is not None else None,
+                                       C.c_void_p(hist_len.data_ptr()) if hist_len is not None else None, cap,
+                                       eos_arr, len(eos_ids), C.c_void_p(ids_dev.data_ptr()),
+                                       C.c_void_p(produced.data_ptr()), stream), "rec_decode_sampled")
         sess.check_status()
+        n = int(produced.item())
+        ids = ids_dev[:n].tolist()
+        if any(t < 0 for t in ids):
+            raise RuntimeError("Invalid sampled chain")
+        if presence_penalty and ids:
+            mask[torch.tensor(ids, dtype=torch.long, device=dev)] = 1.0
         return ids
 
     return engine._guard(state, run)

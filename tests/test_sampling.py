@@ -224,3 +224,29 @@ def test_gpu_resident_sampler_block(cuda):
         want.append(tok)
         seen.append(tok)
     assert ids == want
+
+
+@pytest.mark.parametrize("schedule", ["mega", "graph"])
+def test_gpu_resident_sampler_eos(cuda, schedule, monkeypatch):
+    """A sampled packet stops recording at an EOS id (included), on both
+    schedules, and the ids before it equal the packet without EOS."""
+    monkeypatch.setenv("REC_SCHEDULE", schedule)
+    from rec_b200.engine import build_decoder
+    from rec_b200.model import TINY, generate_weights
+
+    w = generate_weights(TINY, seed=5, device="cuda")
+
+    def packet(eos):
+        engine, sampler = build_decoder(w, eos_tokens=eos)
+        state = engine.prefill_state(256)
+        for t in (9, 40):
+            engine.forward(state, t)
+        return sampler.block(state, 7, 8, 99, temperature=1.0, top_k=20, top_p=0.95, presence_penalty=0.2), state
+
+    full, _ = packet(())
+    assert len(full) == 8
+    stop = full[4]
+    cut, state = packet((stop,))
+    k = full.index(stop)
+    assert cut == full[: k + 1]
+    assert state["position"] == 2 + len(cut)
