@@ -280,6 +280,16 @@ REC_API int rec_gemv_int4_argmax_noalloc(const RecQMat* w, int32_t scale_dtype, 
 REC_API int rec_sample_logits(const void* logits_dev, int32_t batch, int32_t vocab, int64_t stride,
                               const int32_t* history_dev, int32_t history_len, const RecSampling* params,
                               const float* uniforms_dev, int32_t* ids_dev, void* stream);
+/* rec_sample_logits with a grammar allow-mask: allow_dev (uint32 [batch,
+ * allow_stride], allow_stride >= ceil(vocab / 32)) has bit (i & 31) of word
+ * i >> 5 set for each allowed id i of the row.  Disallowed ids get -inf after
+ * the penalties (the reference's grammar handoff, masked_sampling.py:101-110);
+ * top-k counts allowed ids only; a row with no allowed id gives -1.  NULL
+ * allow_dev is rec_sample_logits. */
+REC_API int rec_sample_logits_masked(const void* logits_dev, int32_t batch, int32_t vocab, int64_t stride,
+                                     const int32_t* history_dev, int32_t history_len, const RecSampling* params,
+                                     const float* uniforms_dev, const uint32_t* allow_dev, int64_t allow_stride,
+                                     int32_t* ids_dev, void* stream);
 /* The sampling head for `batch` hidden rows (bf16 [batch, hidden]):
  * logits[b] = lm_head . RMSNorm(h[b], final_norm) (int4 g64 GEMV into
  * logits_dev, bf16 [batch, vocab]), then rec_sample_logits on those rows with

@@ -62,6 +62,8 @@ def lib() -> C.CDLL:
         L.orc_attention_final.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
         L.orc_sample.restype = C.c_int32
         L.orc_sample.argtypes = [_u16p, C.c_int64, C.c_void_p, C.c_int, C.c_void_p, _f32p]
+        L.orc_sample_masked.restype = C.c_int32
+        L.orc_sample_masked.argtypes = [_u16p, C.c_int64, C.c_void_p, C.c_int, C.c_void_p, _f32p, C.c_void_p]
         L.orc_log.restype = C.c_float
         L.orc_log.argtypes = [C.c_float]
         L.orc_log_n.argtypes = [_f32p, _f32p, C.c_int64]
@@ -213,17 +215,31 @@ def log(x: np.ndarray) -> np.ndarray:
     return y
 
 
-def sample(logits_bf16, history, params, uniforms) -> int:
+def sample(logits_bf16, history, params, uniforms, allow=None) -> int:
     """orc_sample on one row: logits uint16[V] (bf16 bits), history int32 ids,
     params a rec_b200.abi.RecSampling, uniforms float32[V] (or None when the
-    temperature is 0)."""
+    temperature is 0), allow an optional grammar mask (uint32[ceil(V/32)],
+    bit i & 31 of word i >> 5 set = id i allowed; orc_sample_masked)."""
     from rec_b200 import abi
 
     lg = np.ascontiguousarray(logits_bf16, np.uint16)
     h = np.ascontiguousarray(history if history is not None else np.zeros(0), np.int32)
     u = np.ascontiguousarray(uniforms if uniforms is not None else np.zeros(lg.size), np.float32)
     assert isinstance(params, abi.RecSampling)
-    return int(lib().orc_sample(lg, lg.size, h.ctypes.data if h.size else None, h.size, C.byref(params), u))
+    hp = h.ctypes.data if h.size else None
+    if allow is None:
+        return int(lib().orc_sample(lg, lg.size, hp, h.size, C.byref(params), u))
+    m = np.ascontiguousarray(allow, np.uint32)
+    assert m.size >= (lg.size + 31) // 32
+    return int(lib().orc_sample_masked(lg, lg.size, hp, h.size, C.byref(params), u, m.ctypes.data))
+
+
+def pack_allow(allowed_ids, vocab: int) -> np.ndarray:
+    """Grammar mask words (uint32[ceil(vocab/32)]) from a list of allowed ids."""
+    m = np.zeros((vocab + 31) // 32, np.uint32)
+    for i in np.asarray(allowed_ids, np.int64).ravel():
+        m[i >> 5] |= np.uint32(1) << np.uint32(i & 31)
+    return m
 
 
 PARTIAL_FLOATS = 130  # (m, l, acc[128]) of one head's attention partial

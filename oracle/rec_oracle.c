@@ -836,11 +836,22 @@ static int cand_desc(const void* pa, const void* pb) {
  * penalties over the history, then greedy argmax, or Gumbel-max with the
  * injected uniforms u[V] over all logits (top_k = 0) or over the reference's
  * joint top-k / top-p filter (engine.py:279-301, masked_sampling.py:98-125,
- * filtered_sampling.py:7-22, sampling.py:48-52).  Returns -1 when more than
- * 1,024 logits tie at the top-k threshold. */
-ORC_API int32_t orc_sample(const uint16_t* logits, int64_t V, const int32_t* hist, int n_hist,
-                           const RecSampling* sp, const float* u) {
+ * filtered_sampling.py:7-22, sampling.py:48-52).  allow (optional, bit i & 31
+ * of word i >> 5 per id) is the grammar mask.  Returns -1 when more than
+ * 1,024 logits tie at the top-k threshold, no id is allowed, or no candidate
+ * is finite. */
+ORC_API int32_t orc_sample_masked(const uint16_t* logits, int64_t V, const int32_t* hist, int n_hist,
+                                  const RecSampling* sp, const float* u, const uint32_t* allow) {
   const int pen = sp->repetition_penalty != 1.0f || sp->presence_penalty != 0.0f;
+  /* grammar mask: disallowed ids are -inf after the penalties; top-k counts
+   * the allowed ids (rec_b200/csrc/sample.cuh) */
+  int top_k = sp->top_k;
+  if (allow) {
+    int64_t n_allowed = 0;
+    for (int64_t i = 0; i < V; ++i) n_allowed += (allow[i >> 5] >> (i & 31)) & 1u;
+    if (n_allowed == 0) return -1;
+    if (n_allowed < top_k) top_k = (int)n_allowed;
+  }
   uint8_t* seen = (uint8_t*)calloc((size_t)V, 1);
   if (pen)
     for (int i = 0; i < n_hist; ++i)
@@ -854,10 +865,11 @@ ORC_API int32_t orc_sample(const uint16_t* logits, int64_t V, const int32_t* his
       if (sp->presence_penalty != 0.0f) v = v - sp->presence_penalty;
     }
     x[i] = v + 0.0f;
+    if (allow && !((allow[i >> 5] >> (i & 31)) & 1u)) x[i] = -INFINITY;
   }
   free(seen);
   float M = -INFINITY;
-  int32_t Mi = 0;
+  int32_t Mi = -1; /* -1: no finite candidate */
   for (int64_t i = 0; i < V; ++i)
     if (x[i] > M) {
       M = x[i];
@@ -882,7 +894,7 @@ ORC_API int32_t orc_sample(const uint16_t* logits, int64_t V, const int32_t* his
   const float lse = M + rlog(tot);
   const float inv_t = 1.0f / sp->temperature;
   int32_t out = -1;
-  if (sp->top_k == 0) {
+  if (top_k == 0) {
     const int t1 = sp->temperature == 1.0f && sp->top_p >= 1.0f;
     float bv = -INFINITY;
     int32_t bi = 0x7fffffff;
@@ -894,7 +906,7 @@ ORC_API int32_t orc_sample(const uint16_t* logits, int64_t V, const int32_t* his
       }
     }
     free(x);
-    return bi;
+    return bi == 0x7fffffff ? -1 : bi;
   }
   /* top-k threshold: the k-th largest x */
   Cand* all = (Cand*)malloc(sizeof(Cand) * V);
@@ -903,7 +915,7 @@ ORC_API int32_t orc_sample(const uint16_t* logits, int64_t V, const int32_t* his
     all[i].i = (int32_t)i;
   }
   qsort(all, (size_t)V, sizeof(Cand), cand_desc);
-  const float theta = all[sp->top_k - 1].x;
+  const float theta = all[top_k - 1].x;
   int greater = 0, n = 0;
   while (n < V && all[n].x >= theta) {
     if (all[n].x > theta) ++greater;
@@ -930,7 +942,7 @@ ORC_API int32_t orc_sample(const uint16_t* logits, int64_t V, const int32_t* his
       first = q;
       break;
     }
-  const int allowed = sp->top_k - greater;
+  const int allowed = top_k - greater;
   const int lo = first < 0 ? n : (first - allowed + 1 > greater ? first - allowed + 1 : greater);
   float bv = -INFINITY;
   int32_t bi = 0x7fffffff;
@@ -943,12 +955,17 @@ ORC_API int32_t orc_sample(const uint16_t* logits, int64_t V, const int32_t* his
       bi = all[q].i;
     }
   }
-  out = bi;
+  out = bi == 0x7fffffff ? -1 : bi;
   free(keep_p);
   free(lp);
   free(all);
   free(x);
   return out;
+}
+
+ORC_API int32_t orc_sample(const uint16_t* logits, int64_t V, const int32_t* hist, int n_hist,
+                           const RecSampling* sp, const float* u) {
+  return orc_sample_masked(logits, V, hist, n_hist, sp, u, NULL);
 }
 
 /* --------------------------------------------------------- decode step */

@@ -24,6 +24,9 @@ _SIGNATURES = {
                                     C.POINTER(abi.RecSampling), C.c_void_p, C.c_void_p, C.c_void_p]),
     "rec_set_shard": (C.c_int, [C.c_void_p, C.POINTER(abi.RecShard)]),
     "rec_exchange_bytes": (C.c_size_t, [C.c_void_p]),
+    "rec_sample_logits_masked": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int64, C.c_void_p, C.c_int32,
+                                           C.POINTER(abi.RecSampling), C.c_void_p, C.c_void_p, C.c_int64,
+                                           C.c_void_p, C.c_void_p]),
     "rec_lmhead_sample": (C.c_int, [C.POINTER(abi.RecQMat), C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int32,
                                     C.c_void_p, C.c_float, C.c_void_p, C.c_int32, C.POINTER(abi.RecSampling),
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),

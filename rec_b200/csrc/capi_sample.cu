@@ -4,9 +4,11 @@
 
 using namespace rec;
 
-REC_API int rec_sample_logits(const void* logits_dev, int32_t batch, int32_t vocab, int64_t stride,
-                              const int32_t* history_dev, int32_t history_len, const RecSampling* params,
-                              const float* uniforms_dev, int32_t* ids_dev, void* stream) {
+REC_API int rec_sample_logits_masked(const void* logits_dev, int32_t batch, int32_t vocab, int64_t stride,
+                                     const int32_t* history_dev, int32_t history_len, const RecSampling* params,
+                                     const float* uniforms_dev, const uint32_t* allow_dev, int64_t allow_stride,
+                                     int32_t* ids_dev, void* stream) {
+  REC_CHECK_ARG(!allow_dev || allow_stride >= (vocab + 31) / 32, "rec_sample_logits_masked: allow rows too short");
   REC_CHECK_ARG(logits_dev && ids_dev && params, "rec_sample_logits: null pointer");
   REC_CHECK_ARG(batch >= 1 && batch <= 64, "rec_sample_logits: batch %d outside 1..64", batch);
   REC_CHECK_ARG(vocab >= 2 && vocab <= kSampleMaxVocab, "rec_sample_logits: vocab %d outside 2..%d", vocab,
@@ -35,12 +37,21 @@ REC_API int rec_sample_logits(const void* logits_dev, int32_t batch, int32_t voc
   a.rep = p.repetition_penalty;
   a.presence = p.presence_penalty;
   a.uniforms = uniforms_dev;
+  a.allow = allow_dev;
+  a.allow_stride = allow_stride;
   a.ids = ids_dev;
   const size_t dyn = size_t((vocab + 31) / 32) * 4;
   REC_CHECK_CUDA(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, int(dyn)));
   k_sample<<<batch, kSampleThreads, dyn, static_cast<cudaStream_t>(stream)>>>(a);
   REC_CHECK_CUDA(cudaGetLastError());
   return REC_OK;
+}
+
+REC_API int rec_sample_logits(const void* logits_dev, int32_t batch, int32_t vocab, int64_t stride,
+                              const int32_t* history_dev, int32_t history_len, const RecSampling* params,
+                              const float* uniforms_dev, int32_t* ids_dev, void* stream) {
+  return rec_sample_logits_masked(logits_dev, batch, vocab, stride, history_dev, history_len, params, uniforms_dev,
+                                  nullptr, 0, ids_dev, stream);
 }
 
 REC_API int rec_lmhead_sample(const RecQMat* lm_head, int32_t scale_dtype, int32_t vocab, int32_t hidden,

@@ -24,6 +24,10 @@
 //           lp * (1/T) + g, lowest index on ties.
 //   g_i   = -log(-log(u_i)) with the injected uniform u_i (the reference draws it
 //           with mx.random.gumbel; fixing u makes the ids comparable).
+//   grammar mask (optional): x_i = -inf for every id whose allow bit is clear,
+//           after the penalties (the reference's handoff, masked_sampling.py:101-110);
+//           top_k = min(top_k, #allowed); no allowed id, or no finite candidate,
+//           gives -1.
 #pragma once
 #include "common.cuh"
 
@@ -43,7 +47,10 @@ struct SampleArgs {
   float temperature, top_p, rep, presence;
   int top_k;
   const float* uniforms;   // fp32 [B, V] (temperature > 0)
-  int* ids;                // int32 [B]; -1: more than kSampleMaxCand ties at the threshold
+  const uint32_t* allow;   // optional grammar mask: bit (i & 31) of word i >> 5 of row b set = id i allowed
+  int64_t allow_stride;    // words per row of allow
+  int* ids;                // int32 [B]; -1: more than kSampleMaxCand ties at the threshold, no id
+                           // allowed, or no finite candidate
   // feedback mode (batch 1, a decode packet on the device): when ctl is set,
   // the history length is read from *hist_len, and the sampled id becomes
   // the session's next token, is recorded for the packet (with the EOS stop)
@@ -139,6 +146,7 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
   const bool pen = a.rep != 1.0f || a.presence != 0.0f;
   const int n_hist = a.hist_len ? *a.hist_len : a.n_hist;
   const int nw = (V + 31) >> 5;
+  const uint32_t* allow = a.allow ? a.allow + size_t(b) * a.allow_stride : nullptr;
   if (pen) {
     for (int i = t; i < nw; i += kSampleThreads) seen[i] = 0u;
     __syncthreads();
@@ -149,6 +157,7 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
     __syncthreads();
   }
   auto X = [&](int i) -> float {
+    if (allow && !((allow[i >> 5] >> (i & 31)) & 1u)) return -INFINITY;  // grammar: not allowed
     float x = bf(lg[i]);
     if (pen && ((seen[i >> 5] >> (i & 31)) & 1u)) {
       if (a.rep != 1.0f) x = x < 0.0f ? __fmul_rn(x, a.rep) : __fdiv_rn(x, a.rep);
@@ -156,7 +165,28 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
     }
     return __fadd_rn(x, 0.0f);
   };
-  const bool filtered = a.temperature != 0.0f && a.top_k > 0;
+  // with a grammar mask, top-k counts the allowed ids only
+  int top_k = a.top_k;
+  if (allow) {
+    int c = 0;
+    for (int w = t; w < nw; w += kSampleThreads) {
+      uint32_t m = allow[w];
+      if (w == nw - 1 && (V & 31)) m &= (1u << (V & 31)) - 1u;
+      c += __popc(m);
+    }
+    c = __reduce_add_sync(0xffffffffu, c);
+    if (lane == 0) s.red_i[warp] = c;
+    __syncthreads();
+    int n_allowed = 0;
+    for (int w = 0; w < kSampleThreads / 32; ++w) n_allowed += s.red_i[w];
+    __syncthreads();
+    if (n_allowed == 0) {
+      if (t == 0) sample_finish(a, b, -1);
+      return;
+    }
+    top_k = top_k < n_allowed ? top_k : n_allowed;
+  }
+  const bool filtered = a.temperature != 0.0f && top_k > 0;
 
   // ---- pass 1: max (argmax for greedy) and the top digit's histogram
   if (filtered) {
@@ -171,8 +201,8 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
     if (filtered) atomicAdd(&s.hist[float_key(x) >> 24], 1u);
   }
   block_argmax(mx, mi, s);
-  if (a.temperature == 0.0f) {
-    if (t == 0) sample_finish(a, b, mi);
+  if (a.temperature == 0.0f) {  // no finite candidate (all masked or -inf): -1
+    if (t == 0) sample_finish(a, b, mi == 0x7fffffff ? -1 : mi);
     return;
   }
   const float M = mx;
@@ -181,7 +211,7 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
   auto resolve = [&](int level) {
     if (t == 0) {
       const int shift = 24 - 8 * level;
-      int rank = level == 0 ? a.top_k - 1 : s.rank;
+      int rank = level == 0 ? top_k - 1 : s.rank;
       unsigned c = 0;
       int d = 255;
       for (; d > 0; --d) {
@@ -236,7 +266,7 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
       if (z > bv) { bv = z; bi = i; }
     }
     block_argmax(bv, bi, s);
-    if (t == 0) sample_finish(a, b, bi);
+    if (t == 0) sample_finish(a, b, bi == 0x7fffffff ? -1 : bi);
     return;
   }
 
@@ -245,7 +275,7 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
     resolve(level);
   }
   const uint32_t theta = s.prefix;
-  const int greater = a.top_k - 1 - s.rank;
+  const int greater = top_k - 1 - s.rank;
   const int n = greater + s.tied;
   if (n > kSampleMaxCand) {
     if (t == 0) sample_finish(a, b, -1);
@@ -298,7 +328,7 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
     int first = -1;
     for (int q = n - 1; q >= greater; --q)
       if (s.cx[q] != 0.0f) { first = q; break; }
-    const int allowed = a.top_k - greater;
+    const int allowed = top_k - greater;
     s.keep_lo = first < 0 ? n : max(greater, first - allowed + 1);
     s.keep_hi = first;  // tied kept: q in [keep_lo, keep_hi]
   }
@@ -319,7 +349,7 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
       const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
       if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
     }
-    if (lane == 0) sample_finish(a, b, bi);
+    if (lane == 0) sample_finish(a, b, bi == 0x7fffffff ? -1 : bi);
   }
 }
 

@@ -185,9 +185,14 @@ class ResidentSampler:
         if not 1 <= count <= WIDTH:
             raise ValueError("Resident packet must contain between one and eight tokens")
         self.engine.ensure_capacity(state, count)
-        if grammar is not None or logprobs is not None:
-            raise NotImplementedError("grammar masks and logprobs are outside the decode hot path")
-        if temperature != 0:
+        if logprobs is not None:
+            raise NotImplementedError("logprobs are outside the decode hot path")
+        if grammar is not None:
+            from .sampling import grammar_block
+
+            ids = grammar_block(self.engine, state, token, count, seed, grammar, temperature=temperature,
+                                top_p=top_p, top_k=top_k, presence_penalty=presence_penalty)
+        elif temperature != 0:
             from .sampling import sampled_block
 
             ids = sampled_block(self.engine, state, token, count, seed, temperature=temperature, top_p=top_p,

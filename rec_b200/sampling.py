@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import ctypes as C
 
+import numpy as np
 import torch
 
 from . import abi
@@ -30,9 +31,13 @@ def uniforms(batch: int, vocab: int, seed: int, device) -> torch.Tensor:
 
 
 def sample_logits(logits: torch.Tensor, p: abi.RecSampling, u: torch.Tensor | None = None,
-                  history: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+                  history: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                  allow: torch.Tensor | None = None) -> torch.Tensor:
     """ids int32 [B] for bf16 logits [B, V] (or [V]); history int32 [B, n]
-    (or [n]); u fp32 [B, V] (required when temperature > 0)."""
+    (or [n]); u fp32 [B, V] (required when temperature > 0); allow an
+    optional grammar mask, int32/uint32 words [B, W] (or [W]) with
+    W >= ceil(V / 32), bit i & 31 of word i >> 5 set for each allowed id
+    (rec_sample_logits_masked; a row with no allowed id gives -1)."""
     if logits.dtype != torch.bfloat16 or not logits.is_cuda:
         raise ValueError("logits must be a bf16 CUDA tensor")
     lg = logits.reshape(1, -1) if logits.dim() == 1 else logits
@@ -46,13 +51,21 @@ def sample_logits(logits: torch.Tensor, p: abi.RecSampling, u: torch.Tensor | No
         u = u.reshape(B, V).contiguous()
         if u.dtype != torch.float32:
             raise ValueError("uniforms must be float32")
+    if allow is not None:
+        allow = allow.reshape(B, -1) if allow.dim() == 1 else allow
+        if allow.element_size() != 4 or allow.device != lg.device or allow.stride(1) != 1:
+            raise ValueError("allow must be 32-bit words on the logits' device, rows contiguous")
+        if allow.shape[1] < (V + 31) // 32:
+            raise ValueError("allow rows must hold ceil(V / 32) words")
     ids = out if out is not None else torch.empty(B, dtype=torch.int32, device=lg.device)
     stream = torch.cuda.current_stream().cuda_stream
-    check(lib().rec_sample_logits(C.c_void_p(lg.data_ptr()), B, V, lg.stride(0),
-                                  C.c_void_p(history.data_ptr()) if history is not None else None,
-                                  history.shape[1] if history is not None else 0, C.byref(p),
-                                  C.c_void_p(u.data_ptr()) if u is not None else None, C.c_void_p(ids.data_ptr()),
-                                  C.c_void_p(stream)), "rec_sample_logits")
+    check(lib().rec_sample_logits_masked(C.c_void_p(lg.data_ptr()), B, V, lg.stride(0),
+                                         C.c_void_p(history.data_ptr()) if history is not None else None,
+                                         history.shape[1] if history is not None else 0, C.byref(p),
+                                         C.c_void_p(u.data_ptr()) if u is not None else None,
+                                         C.c_void_p(allow.data_ptr()) if allow is not None else None,
+                                         allow.stride(0) if allow is not None else 0, C.c_void_p(ids.data_ptr()),
+                                         C.c_void_p(stream)), "rec_sample_logits_masked")
     return ids
 
 
@@ -133,3 +146,73 @@ def sampled_block(engine, state, token, count, seed, *, temperature, top_p, top_
         return ids
 
     return engine._guard(state, run)
+
+
+def _grammar_words(mask, words: int, device) -> torch.Tensor | None:
+    """The allow words of a grammar mask (uint32 words + a trailing active
+    flag word, the reference's state["grammar_mask"], grammar.py:86-88), as
+    int32 [words] on `device`; None when the flag word is 0 (inactive).  Ids
+    past the grammar's words are not allowed."""
+    m = torch.as_tensor(np.asarray(mask, dtype=np.uint32).view(np.int32))
+    if m.numel() < 2:
+        raise ValueError("grammar_mask must hold the allow words and the active flag word")
+    if int(m[-1]) == 0:
+        return None
+    out = torch.zeros(words, dtype=torch.int32)
+    n = min(words, m.numel() - 1)
+    out[:n] = m[:n]
+    return out.to(device)
+
+
+def grammar_block(engine, state, token, count, seed, grammar, *, temperature, top_p, top_k, presence_penalty):
+    """ResidentSampler.block with a grammar constraint (reference
+    masked_sampling.py:33-212 with grammar.py:46-104): every step decodes one
+    token, masks its logits with the grammar's allow words after the presence
+    penalty, samples on the device (greedy at temperature 0), and hands the
+    id to the grammar on the host, whose matcher returns the next step's mask
+    (grammar._advance(token, active), stored in state["grammar_mask"]).  The
+    packet stops after one of grammar.stops.  The matcher runs on the CPU, so
+    each token makes one host round trip (the reference orders its GPU work
+    behind the same callback)."""
+    sess = engine._session(state)
+    V = engine.weights.cfg.vocab
+    dev = sess.logits.device
+    words = (V + 31) // 32
+    p = params(temperature, top_k, top_p, 1.0, presence_penalty)
+    u = uniforms(count, V, seed, dev) if temperature > 0 else None
+    mask = state.get("presence_mask")
+    if presence_penalty and mask is None:
+        mask = torch.zeros(V, dtype=torch.float32, device=dev)
+        state["presence_mask"] = mask
+    stops = set(int(t) for t in getattr(grammar, "stops", ()))
+    ids_dev = torch.zeros(1, dtype=torch.int32, device=dev)
+    pos = state["position"]
+
+    def run():
+        out = []
+        tok = int(token)
+        for i in range(count):
+            allow = _grammar_words(state["grammar_mask"], words, dev)
+            if allow is None:
+                break
+            logits, _ = sess.step(tok, pos + i)
+            hist = torch.nonzero(mask).to(torch.int32).reshape(1, -1) if presence_penalty else None
+            sample_logits(logits.reshape(1, V), p, u[i] if u is not None else None, hist, out=ids_dev,
+                          allow=allow)
+            sess.check_status()
+            tok = int(ids_dev.item())
+            if tok < 0:
+                raise RuntimeError("Grammar allows no token")
+            out.append(tok)
+            if presence_penalty:
+                mask[tok] = 1.0
+            nxt = np.asarray(grammar._advance(tok, True), dtype=np.uint32)
+            state["grammar_mask"] = np.concatenate([nxt, np.ones(1, np.uint32)])
+            if tok in stops:
+                break
+        return out
+
+    ids = engine._guard(state, run)
+    if not ids:
+        raise RuntimeError("Grammar session is inactive")
+    return ids
