@@ -171,6 +171,7 @@ struct RecCtx {
   // persistent schedule
   bool use_mega = true;
   MegaLayer* mega_layers = nullptr;  // device table, in the workspace
+  unsigned long long* router_ll = nullptr;  // [2][E] flag+value router logits of the persistent kernel
   unsigned* mega_cnt = nullptr;      // [2] grid barrier + abort, [Hq] heads, [Hq*n_super] supers
   unsigned long long* prof = nullptr;  // optional phase timeline
   size_t prof_entries = 0;
@@ -190,7 +191,7 @@ struct Layout {
 };
 
 enum Region {
-  rCtl, rCounters, rMegaCnt, rH, rQkv, rAttn, rXn, rAct, rLogits, rTrace, rRouter, rIds, rWts, rCandV, rCandI,
+  rCtl, rCounters, rMegaCnt, rRouterLL, rH, rQkv, rAttn, rXn, rAct, rLogits, rTrace, rRouter, rIds, rWts, rCandV, rCandI,
   rPartials, rSupers, rMegaLayers, rRope, rCount
 };
 
@@ -207,6 +208,7 @@ Layout layout_of(const RecCtx* c) {
   sz[rCtl] = kCtlInts * 4;
   sz[rCounters] = (64 + d.n_q_heads) * 4;
   sz[rMegaCnt] = size_t(2 + d.n_q_heads + d.n_q_heads * nsup) * 4;
+  sz[rRouterLL] = size_t(2) * d.n_experts * 8;  // zeroed with the control block
   sz[rMegaLayers] = size_t(d.n_layers) * sizeof(MegaLayer);
   sz[rH] = size_t(d.hidden) * 2;
   sz[rQkv] = size_t(d.n_q_heads + 2 * d.n_kv_heads) * 128 * 2;
@@ -606,6 +608,7 @@ REC_API int rec_set_workspace(RecCtx* c, void* ws, size_t bytes) {
   c->logits = reinterpret_cast<uint16_t*>(b + L.off[rLogits]);
   c->trace = reinterpret_cast<uint16_t*>(b + L.off[rTrace]);
   c->router_logits = reinterpret_cast<float*>(b + L.off[rRouter]);
+  c->router_ll = reinterpret_cast<unsigned long long*>(b + L.off[rRouterLL]);
   c->ids = reinterpret_cast<int*>(b + L.off[rIds]);
   c->wts = reinterpret_cast<float*>(b + L.off[rWts]);
   c->cand_val = reinterpret_cast<float*>(b + L.off[rCandV]);
@@ -665,9 +668,9 @@ static int check_ready(RecCtx* c) {
     return REC_ESTATE;
   }
   const char* sched = std::getenv("REC_SCHEDULE");
-  c->use_mega = !(sched && std::strcmp(sched, "graph") == 0);
+  c->use_mega = !(sched && std::strcmp(sched, "graph") == 0) && c->d.n_experts <= kMegaMaxExperts;
   if (c->world > 1) {
-    REC_CHECK_ARG(c->use_mega, "a session split over ranks runs on the persistent kernel only");
+    REC_CHECK_ARG(c->use_mega, "a session split over ranks runs on the persistent kernel only (no REC_SCHEDULE=graph, n_experts <= %d)", kMegaMaxExperts);
     for (int q = 0; q < c->world; ++q)
       if (!c->xch[q]) {
         set_error("rec_set_shard: exchange buffer of rank %d not set", q);
@@ -717,6 +720,7 @@ static cudaError_t launch_mega_t(RecCtx* c, int steps, cudaStream_t st) {
   A.partials = c->partials;
   A.supers = c->supers;
   A.router_logits = c->router_logits;
+  A.router_ll = c->router_ll;
   A.cand_val = c->cand_val;
   A.cand_idx = c->cand_idx;
   A.steps = steps;

@@ -5,18 +5,21 @@
 // weight (and KV) chunks for this CTA and streams them with cp.async.bulk into
 // a ring of shared-memory slots (full/empty mbarriers).  Weights do not depend
 // on activations, so the producer runs ahead across phase and layer
-// boundaries; only the expert chunks wait for this layer's routing.  Warps
+// boundaries; only the expert chunks wait for this layer's routing, which
+// the producer warp computes itself from the router logits as they land
+// (flag+value words, no grid barrier before G).  Warps
 // 1..8 are consumers: they take the chunks in the same order and run the same
 // math as the standalone kernels (gemv.cuh, attn.cuh, moe.cuh), in the same
 // canonical order, so results are bit-identical to them and to the oracle.
 //
-// Phases of a layer, separated by bounded software grid barriers:
+// Phases of a layer, separated by bounded software grid barriers (except
+// R -> G):
 //   Q  RMSNorm + QKV rows                       -> qkv
 //   A  split-KV attention items (+RoPE, quantize-on-append); the last CTA to
 //      finish a super-chunk / head merges it (log-sum-exp)   -> attn
 //   O  O rows + residual (rows owned like D)   -> h
-//   R  RMSNorm + router logits                 -> router_logits
-//   G  expert gate/up pairs + SwiGLU (selection recomputed per CTA) -> act
+//   R  RMSNorm + router logits                 -> router_ll (flag + value)
+//   G  expert gate/up pairs + SwiGLU (selection by each CTA's producer) -> act
 //   D  expert down rows for all k experts + bf16 mix + residual -> h, trace
 // then H (final RMSNorm + lm_head + CTA argmax) and E (global argmax, done
 // redundantly by every CTA, so the next token needs no extra barrier).
@@ -44,6 +47,7 @@ constexpr int kGPairs = 16;   // gate/up pairs per G chunk
 constexpr int kDExperts = 4;  // experts per D chunk
 constexpr int kDRowsMax = 16; // output rows per CTA in O / D
 constexpr int kMaxLayers = 64;  // layer descriptors kept in shared memory
+constexpr int kMegaMaxExperts = 256;  // the producer warp's routing holds 8 experts per lane
 
 struct MegaLayer {
   QMatDev q, k, v, o, gate, up, down;
@@ -116,6 +120,10 @@ struct MegaArgs {
   unsigned* cnt;       // [Hq] head counters, then [Hq * n_super_max] super counters
   uint16_t *h, *qkv, *attn, *act, *logits, *trace;
   float *partials, *supers, *router_logits, *cand_val;
+  // router logits as (flag << 32 | value bits) words, [2][E] by flag parity:
+  // the flag is the layer's running sequence number (route_flag), so the
+  // producer warps see each logit land without a grid barrier
+  unsigned long long* router_ll;
   int* cand_idx;
   int steps;
   // one session over several GPUs (world > 1): experts [e_lo, e_hi) and
@@ -149,8 +157,8 @@ struct MegaSmem {
   int best_idx[kMegaCons];
   float gX[kMaxTopK * 16];   // exact group sums of the shared fixed-point limbs
   float dmax[kMaxTopK];      // D: max |activation| per selected expert
-  alignas(16) float route_p[kMaxExperts];
-  alignas(16) float route_c[kMaxExperts];
+  float route_p[kMegaMaxExperts];     // the producer's routing: logits, then p
+  unsigned route_k[kMegaMaxExperts];  // selection keys (0 = taken)
   int ids[kMaxTopK];
   float wts[kMaxTopK];
   int loc[kMaxTopK];   // selection slots whose expert is local, in slot order
@@ -190,6 +198,15 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+// 64-bit flag+value words (single-copy atomic: aligned scalar 64-bit accesses)
+__device__ __forceinline__ unsigned long long ld_relaxed64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -272,8 +289,20 @@ __device__ __forceinline__ void prof_add(const MegaArgs& a, int step, int layer,
 }
 
 // Grid barrier index of a phase: each step has 6 per layer + 1 (after H).
+// Phase 3 (router logits -> selection) is not a grid barrier: its timeline
+// slot records when the CTA's selection became ready.
 __device__ __forceinline__ unsigned bar_index(const MegaArgs& a, int step, int layer, int ph) {
   return unsigned(step * (6 * a.n_layers + 1) + 6 * layer + ph);
+}
+// Flag of a layer's router-logit words: unique over the context's launches
+// (never 0, the value of a cleared word).
+__device__ __forceinline__ unsigned route_flag(const MegaArgs& a, int step, int layer) {
+  return a.layer_seq0 + unsigned(step) * unsigned(a.n_layers) + unsigned(layer) + 1u;
+}
+// Order-preserving key of a non-NaN float (+0 and -0 canonicalised first).
+__device__ __forceinline__ unsigned route_key(float x) {
+  const unsigned u = __float_as_uint(__fadd_rn(x, 0.0f));
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
 __device__ __forceinline__ bool aborted(const MegaArgs& a) {
@@ -496,6 +525,126 @@ struct Producer {
     }
   }
 
+  // Routing in the producer warp (all lanes): the router logits arrive as
+  // flag+value words, so the selection needs no grid barrier, and the
+  // expert copies are issued right after it.  Lane l handles experts l,
+  // l+32, ...  Softmax (router_mode 0: max, exp(l - max), the sum lane by
+  // lane in that order then a butterfly, p = exp / sum) or sigmoid + bias
+  // (1: p = sigmoid(l), c = p + bias); the top-k by c, lowest index on ties,
+  // in k rounds of a warp arg-max; weights p / (sum of the selected p in
+  // rank order + 1e-20).  Publishes ids, wts and the local-expert lists in
+  // shared memory, then route_seq = seq.  Compact loops: this code runs
+  // once per layer, so its size (instruction fetch) matters more than ILP.
+  __device__ bool route_ll(const MegaLayer& L, int step, int l, int lane) {
+    constexpr int J = kMegaMaxExperts / 32;
+    const unsigned flag = route_flag(a, step, l);
+    const int E = a.E;
+    const unsigned long long* buf = a.router_ll + size_t(flag & 1u) * E;
+    unsigned pending = 0;
+#pragma unroll 1
+    for (int j = 0; j < J; ++j)
+      if (lane + 32 * j < E) pending |= 1u << j;
+    const unsigned valid = pending;
+    uint32_t spins = 0;
+    while (true) {
+      unsigned long long v[J];
+#pragma unroll
+      for (int j = 0; j < J; ++j) v[j] = ((pending >> j) & 1u) ? ld_relaxed64(buf + lane + 32 * j) : 0ull;
+#pragma unroll
+      for (int j = 0; j < J; ++j)
+        if (((pending >> j) & 1u) && unsigned(v[j] >> 32) == flag) {
+          sm.route_p[lane + 32 * j] = __uint_as_float(unsigned(v[j]));
+          pending &= ~(1u << j);
+        }
+      if (__all_sync(0xffffffffu, pending == 0)) break;
+      if (__any_sync(0xffffffffu, aborted(a))) return false;
+      if (++spins > kSpinLimit * 4) {
+        if (lane == 0) set_abort(a, kStatusCounterTimeout);
+        return false;
+      }
+    }
+    if (lane == 0) stamp(a, step, l, 14);
+    if (a.router_mode == 0) {
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int i = lane; i < E; i += 32) mx = fmaxf(mx, sm.route_p[i]);
+      mx = bfly_max(mx);
+      float sum = 0.0f;
+#pragma unroll 1
+      for (int i = lane; i < E; i += 32) {
+        const float c = rexp(__fsub_rn(sm.route_p[i], mx));
+        sm.route_p[i] = c;
+        sum = __fadd_rn(sum, c);
+      }
+      sum = bfly_sum(sum);
+#pragma unroll 1
+      for (int i = lane; i < E; i += 32) {
+        const float pi = __fdiv_rn(sm.route_p[i], sum);
+        sm.route_p[i] = pi;
+        sm.route_k[i] = route_key(pi);
+      }
+    } else {
+#pragma unroll 1
+      for (int i = lane; i < E; i += 32) {
+        const float pi = rsigmoid(sm.route_p[i]);
+        sm.route_p[i] = pi;
+        sm.route_k[i] = route_key(__fadd_rn(pi, L.expert_bias[i]));
+      }
+    }
+    __syncwarp();
+    unsigned key[J];  // this lane's keys in registers for the k rounds (0 = absent or taken)
+#pragma unroll
+    for (int j = 0; j < J; ++j) key[j] = ((valid >> j) & 1u) ? sm.route_k[lane + 32 * j] : 0u;
+    float s2 = 0.0f, my_p = 0.0f;
+    int my_id = 0;
+#pragma unroll 1
+    for (int r = 0; r < a.k; ++r) {
+      unsigned best = 0;
+      int bj = 0;
+#pragma unroll
+      for (int j = 0; j < J; ++j)
+        if (key[j] > best) {
+          best = key[j];
+          bj = j;
+        }
+      const unsigned wbest = __reduce_max_sync(0xffffffffu, best);
+      const int widx = int(__reduce_min_sync(0xffffffffu, (best == wbest && best) ? unsigned(lane + 32 * bj) : ~0u));
+      const float pw = sm.route_p[widx];
+      if (lane == (widx & 31)) {
+#pragma unroll
+        for (int j = 0; j < J; ++j)
+          if (j == (widx >> 5)) key[j] = 0u;  // taken
+      }
+      if (lane == r) {
+        my_id = widx;
+        my_p = pw;
+      }
+      s2 = __fadd_rn(s2, pw);
+    }
+    s2 = __fadd_rn(s2, 1e-20f);
+    const bool sel = lane < a.k;
+    const bool local = sel && my_id >= a.e_lo && my_id < a.e_hi;
+    const unsigned lm = __ballot_sync(0xffffffffu, local);
+    if (sel) {
+      sm.ids[lane] = my_id;
+      sm.wts[lane] = __fdiv_rn(my_p, s2);
+    }
+    if (local) {
+      const int at = __popc(lm & ((1u << lane) - 1u));
+      sm.loc[at] = lane;
+      sm.lids[at] = my_id - a.e_lo;
+    }
+    if (lane == 0) sm.n_loc = __popc(lm);
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();
+      sm.route_seq = step * a.n_layers + l + 1;
+      stamp(a, step, l, 15);
+    }
+    __syncwarp();
+    return true;
+  }
+
   __device__ void run() {
     const int lane = threadIdx.x & 31;
     const Part P = partition(a);
@@ -536,20 +685,12 @@ struct Producer {
           for (int r = P.o0; r < P.o1 && ok; r += kORows) gemv_chunk(L.o, a.hq * 128, r, min(kORows, P.o1 - r));
           // R: this CTA's router rows
           for (int e = blockIdx.x; e < a.E && ok; e += gridDim.x) router_chunk(L, e);
-          // G / D need this layer's routing: wait for the consumers' selection
-          const int seq = step * a.n_layers + l + 1;
-          uint32_t spins = 0;
-          while (sm.route_seq < seq) {
-            __nanosleep(64);  // a hot spin would take issue slots from the consumer warps
-            if (aborted(a)) { ok = false; break; }
-            if (++spins > kSpinLimit * 64) {
-              set_abort(a, kStatusCounterTimeout);
-              ok = false;
-              break;
-            }
-          }
         }
         __syncwarp();
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        // G / D need this layer's routing: the warp selects the experts as
+        // soon as every router logit has landed
+        if (ok) ok = route_ll(L, step, l, lane);
         if (lane == 0) stamp(a, step, l, 20);
         if (lane == 0 && ok) {
           // this rank's selected experts only (all of them when world == 1)
@@ -1104,115 +1245,29 @@ struct Consumers {
     }
   }
 
-  // --- routing (every CTA, consumer warp 0) -----------------------------------
-  // Routing, computed by all consumer warps of every CTA (one thread per
-  // expert; the sums keep the canonical lane order).  The code is compact
-  // (runtime loops): it runs once per layer and is fetched cold.
-  // Rank of expert i among choices [j0, j1): #{j : c_j > c_i or (c_j == c_i
-  // and j < i)}.
-  __device__ __noinline__ int rank_of(int i, int j0, int j1) const {
-    const float ci = sm.route_c[i];
-    int rank = 0;
-    if (((j1 - j0) & 3) == 0) {
-      const float4* c4 = reinterpret_cast<const float4*>(sm.route_c + j0);
-#pragma unroll 2
-      for (int q = 0; q < (j1 - j0) / 4; ++q) {
-        const float4 cv = c4[q];
-        const int j = j0 + 4 * q;
-        rank += (cv.x > ci || (cv.x == ci && j < i)) ? 1 : 0;
-        rank += (cv.y > ci || (cv.y == ci && j + 1 < i)) ? 1 : 0;
-        rank += (cv.z > ci || (cv.z == ci && j + 2 < i)) ? 1 : 0;
-        rank += (cv.w > ci || (cv.w == ci && j + 3 < i)) ? 1 : 0;
-      }
-    } else {
-#pragma unroll 1
-      for (int j = j0; j < j1; ++j) {
-        const float cj = sm.route_c[j];
-        rank += (cj > ci || (cj == ci && j < i)) ? 1 : 0;
-      }
-    }
-    return rank;
-  }
-
-  __device__ void route(const MegaLayer& L, int step_, int layer_) {
-    const int E = a.E, t = threadIdx.x - 32, nt = kMegaCons * 32;
-#pragma unroll 1
-    for (int i = t; i < E; i += nt) sm.route_p[i] = __ldcg(a.router_logits + i);
-    cons_sync();
-    if (warp == 0 && lane == 0) stamp(a, step_, layer_, 14);
-    if (a.router_mode == 0) {
-      // warp 0: max; exp(l - max); the canonical sum (lane l adds experts l,
-      // l+32, ... in order, then a butterfly); p = exp / sum
-      if (warp == 0) {
-        float mx = -INFINITY;
-#pragma unroll 1
-        for (int i = lane; i < E; i += 32) mx = fmaxf(mx, sm.route_p[i]);
-        mx = bfly_max(mx);
-        float sum = 0.0f;
-#pragma unroll 1
-        for (int i = lane; i < E; i += 32) {
-          const float c = rexp(__fsub_rn(sm.route_p[i], mx));
-          sm.route_c[i] = c;
-          sum = __fadd_rn(sum, c);
-        }
-        sum = bfly_sum(sum);
-#pragma unroll 1
-        for (int i = lane; i < E; i += 32) {
-          const float pi = __fdiv_rn(sm.route_c[i], sum);
-          sm.route_p[i] = pi;
-          sm.route_c[i] = pi;
+  // Waits (thread 32, bounded) until the producer warp has published this
+  // layer's selection (route_ll); the timeline slot of phase 3 records the
+  // wait.  Returns false on abort.
+  __device__ bool wait_route(int seq, unsigned idx) {
+    __shared__ int ok_route;
+    if (threadIdx.x == 32) {
+      if (a.prof) a.prof[(size_t(idx) * gridDim.x + blockIdx.x) * 2] = globaltimer();
+      int ok = 1;
+      uint32_t spins = 0;
+      while (sm.route_seq < seq) {
+        if (aborted(a)) { ok = 0; break; }
+        if (++spins > kSpinLimit * 4) {
+          set_abort(a, kStatusCounterTimeout);
+          ok = 0;
+          break;
         }
       }
-    } else {
-#pragma unroll 1
-      for (int i = t; i < E; i += nt) {
-        const float pi = rsigmoid(sm.route_p[i]);
-        sm.route_p[i] = pi;
-        sm.route_c[i] = __fadd_rn(pi, L.expert_bias[i]);
-      }
+      __threadfence_block();
+      if (a.prof) a.prof[(size_t(idx) * gridDim.x + blockIdx.x) * 2 + 1] = globaltimer();
+      ok_route = ok;
     }
     cons_sync();
-    if (warp == 0 && lane == 0) stamp(a, step_, layer_, 15);
-    // rank of i = #{j : c_j > c_i or (c_j == c_i and j < i)}; ranks < k are
-    // the selection, in rank order (largest first, lowest index on ties).
-    // Pairs of threads split the comparisons of one expert when 2E fits the
-    // consumer threads and E is a multiple of 8 (float4 reads of each half).
-    if (2 * E <= nt && (E & 7) == 0) {
-      const bool act = t < 2 * E;  // threads t, t^1 share expert t/2
-      const int i = t >> 1, half = t & 1;
-      int rank = act ? rank_of(i, half * (E / 2), (half + 1) * (E / 2)) : 0;
-      rank += __shfl_xor_sync(0xffffffffu, rank, 1);
-      if (act && half == 0 && rank < a.k) sm.ids[rank] = i;
-    } else {
-#pragma unroll 1
-      for (int i = t; i < E; i += nt) {
-        const int rank = rank_of(i, 0, E);
-        if (rank < a.k) sm.ids[rank] = i;
-      }
-    }
-    cons_sync();
-    if (warp == 0) {
-      // renormalise: lane r holds p of rank r; the sum runs in rank order
-      const float pr = lane < a.k ? sm.route_p[sm.ids[lane]] : 0.0f;
-      float s2 = 0.0f;
-#pragma unroll 1
-      for (int r = 0; r < a.k; ++r) s2 = __fadd_rn(s2, __shfl_sync(0xffffffffu, pr, r));
-      s2 = __fadd_rn(s2, 1e-20f);
-      if (lane < a.k) sm.wts[lane] = __fdiv_rn(pr, s2);
-      if (lane == 0) {
-        int n = 0;
-        for (int r = 0; r < a.k; ++r) {
-          const int e = sm.ids[r];
-          if (e >= a.e_lo && e < a.e_hi) {
-            sm.loc[n] = r;
-            sm.lids[n] = e - a.e_lo;
-            ++n;
-          }
-        }
-        sm.n_loc = n;
-      }
-    }
-    cons_sync();
+    return ok_route != 0;
   }
 
   template <int I, int BITS>
@@ -1353,21 +1408,19 @@ struct Consumers {
               }
             }
             acc = bfly_sum(acc);
-            if (lane == 0) a.router_logits[e] = rbf(acc);
+            if (lane == 0) {
+              const unsigned flag = route_flag(a, step, l);
+              st_relaxed64(a.router_ll + size_t(flag & 1u) * a.E + e,
+                           (static_cast<unsigned long long>(flag) << 32) | __float_as_uint(rbf(acc)));
+            }
             release();
           }
           if (warp == 0 && lane == 0) stamp(a, step, l, 45);
         }
-        if (!gbar(bar_index(a, step, l, 3))) return;
-        // ---- G: selection (same on every CTA), then gate/up pairs
+        // ---- G: the selection (the producer's route_ll), then gate/up pairs
         if (warp == 0 && lane == 0) stamp(a, step, l, 0);
-        route(L, step, l);
+        if (!wait_route(step * a.n_layers + l + 1, bar_index(a, step, l, 3))) return;
         if (warp == 0 && lane == 0) stamp(a, step, l, 1);
-        if (warp == 0 && lane == 0) {
-          __threadfence_block();
-          sm.route_seq = step * a.n_layers + l + 1;
-        }
-        cons_sync();
         {
           GroupX gx[1];
           share_limbs(sm.xn, 32, fr);

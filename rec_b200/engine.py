@@ -147,23 +147,44 @@ class QATSession:
         self._state = None
         self.cached_tokens = 0
         self.common_prefix_tokens = 0
+        self.prompt_cache = None
 
     def prefill(self, tokens, *, prefix=None, should_stop=lambda: False, interrupt_between_layers=False):
-        if prefix is not None:
-            raise NotImplementedError("prompt-prefix reuse is outside the decode hot path")
+        """Chunked prefill (quantized.py:102-148).  `prefix` is the
+        `prompt_cache` of an earlier session: its K/V rows for the common
+        prompt prefix are reused in place (prefix.py:83-118), and only the
+        rest of the prompt runs.  `should_stop` is polled before each chunk
+        (PrefillCancelled)."""
+        from .errors import PrefillCancelled
+        from .prefix import PromptCache, select_prefix
+
+        tokens = [int(t) for t in tokens]
         limit = len(tokens) + self.maximum
         if limit > self.context_limit:
             raise ValueError("prompt plus output allowance exceeds the context limit")
-        state = self.engine.prefill_state(len(tokens) + 1, limit=limit)
+        prefix, self.common_prefix_tokens = select_prefix(prefix, tokens)
+        self.cached_tokens = 0 if prefix is None else len(prefix.tokens)
+        storage = None if prefix is None else prefix.storage
+        state = self.engine.prefill_state(len(tokens) + 1, limit=limit, storage=storage)
+        self.prompt_cache = prefix or PromptCache([], state["kv"])
         sess = self.engine._session(state)
-        logits = None
-        for i, t in enumerate(tokens):
-            if should_stop() and i % self.engine.prefill_chunk_size == 0:
-                from .errors import PrefillCancelled
-
+        logits = self.prompt_cache.logits
+        chunk = self.engine.prefill_chunk_size
+        for begin in range(self.cached_tokens, len(tokens), chunk):
+            if should_stop():
                 raise PrefillCancelled()
-            logits, _ = sess.step(int(t), i)
-        self.engine._guard(state, sess.check_status)
+            self.prompt_cache.checkpoint()
+            part = tokens[begin:begin + chunk]
+            for i, t in enumerate(part):
+                out, _ = sess.step(t, begin + i, want_logits=i == len(part) - 1)
+            self.engine._guard(state, sess.check_status)
+            logits = out.clone()
+            self.prompt_cache.advance(part, logits)
+        if should_stop():
+            raise PrefillCancelled()
+        if logits is None:
+            raise ValueError("prefill needs at least one prompt token")
+        state["capacity"] = state["kv"].capacity
         state["position"] = state["initial"] = len(tokens)
         self._state = state
         return logits.clone()
