@@ -390,19 +390,29 @@ struct Producer {
     bulk_g2s(dst + boff, m.b + size_t(row0) * (K / 64), sbytes, &sm.full[slot]);
     issued(slot);
   }
-  __device__ void pair_chunk(const MegaLayer& L, int expert, int i0, int n) {
+  // G chunk: n gate/up pairs, rows [i0, i0 + nA) of expert eA then rows
+  // [0, n - nA) of expert eB (a chunk may span two experts, so every CTA's
+  // share of pairs takes the same number of chunks).  Slot layout: gate rows,
+  // up rows, gate scales, up scales, gate biases, up biases (pair q = row q).
+  __device__ void pair_chunk(const MegaLayer& L, int eA, int i0, int nA, int eB, int n) {
     int slot;
     uint8_t* dst = acquire(slot);
     if (!dst) return;
-    const size_t row = size_t(expert) * a.I + i0;
     const uint32_t wb = uint32_t(n) * 1024, sbytes = uint32_t(n) * 64;
     mbar_expect_tx(&sm.full[slot], 2 * wb + 4 * sbytes);
-    bulk_g2s(dst, reinterpret_cast<const uint8_t*>(L.gate.w) + row * 1024, wb, &sm.full[slot]);
-    bulk_g2s(dst + wb, reinterpret_cast<const uint8_t*>(L.up.w) + row * 1024, wb, &sm.full[slot]);
-    bulk_g2s(dst + 2 * wb, L.gate.s + row * 32, sbytes, &sm.full[slot]);
-    bulk_g2s(dst + 2 * wb + sbytes, L.up.s + row * 32, sbytes, &sm.full[slot]);
-    bulk_g2s(dst + 2 * wb + 2 * sbytes, L.gate.b + row * 32, sbytes, &sm.full[slot]);
-    bulk_g2s(dst + 2 * wb + 3 * sbytes, L.up.b + row * 32, sbytes, &sm.full[slot]);
+    for (int part = 0; part < 2; ++part) {
+      const int np = part ? n - nA : nA;
+      if (np == 0) continue;
+      const size_t row = part ? size_t(eB) * a.I : size_t(eA) * a.I + i0;
+      const uint32_t q0 = part ? uint32_t(nA) : 0u;  // first pair of this part
+      const uint32_t pw = uint32_t(np) * 1024, ps = uint32_t(np) * 64;
+      bulk_g2s(dst + q0 * 1024, reinterpret_cast<const uint8_t*>(L.gate.w) + row * 1024, pw, &sm.full[slot]);
+      bulk_g2s(dst + wb + q0 * 1024, reinterpret_cast<const uint8_t*>(L.up.w) + row * 1024, pw, &sm.full[slot]);
+      bulk_g2s(dst + 2 * wb + q0 * 64, L.gate.s + row * 32, ps, &sm.full[slot]);
+      bulk_g2s(dst + 2 * wb + sbytes + q0 * 64, L.up.s + row * 32, ps, &sm.full[slot]);
+      bulk_g2s(dst + 2 * wb + 2 * sbytes + q0 * 64, L.gate.b + row * 32, ps, &sm.full[slot]);
+      bulk_g2s(dst + 2 * wb + 3 * sbytes + q0 * 64, L.up.b + row * 32, ps, &sm.full[slot]);
+    }
     issued(slot);
   }
   // D chunk: experts ids[r0..r1) rows [o0, o0+n) of the down matrices (K = I)
@@ -703,8 +713,8 @@ struct Producer {
           g1 *= 2;
           for (int u = g0; u < g1 && ok;) {
             const int j = u / a.I, i0 = u % a.I;
-            const int n = min(min(kGPairs, g1 - u), a.I - i0);
-            pair_chunk(L, lids[j], i0, n);
+            const int n = min(kGPairs, g1 - u), nA = min(n, a.I - i0);
+            pair_chunk(L, lids[j], i0, nA, nA < n ? lids[j + 1] : 0, n);
             stamp(a, step, l, 21 + min((u - g0) / kGPairs, 3));
             u += n;
           }
@@ -1430,8 +1440,7 @@ struct Consumers {
           g0 *= 2;
           g1 *= 2;
           for (int u = g0; u < g1;) {
-            const int r = sm.loc[u / a.I], i0 = u % a.I;
-            const int n = min(min(kGPairs, g1 - u), a.I - i0);
+            const int n = min(kGPairs, g1 - u);  // pairs u .. u + n - 1 (at most two experts)
             const uint8_t* st = take();
             if (warp == 0 && lane == 0) stamp(a, step, l, 2 + 2 * min((u - g0) / kGPairs, 3));
             {
@@ -1447,13 +1456,18 @@ struct Consumers {
 #pragma unroll
               for (int q = 0; q < 4; ++q) v[q] = __fmul_rn(bfly_sum(v[q]), fr.down);
               if (lane == 0) {
+                // pair u + q: selection slot loc[(u + q) / I], row (u + q) % I
                 if (va) {
                   const float gg = rbf(v[0]), uu = rbf(v[1]);
-                  a.act[r * a.I + i0 + pa] = to_bf(__fmul_rn(rbf(__fmul_rn(gg, rbf(rsigmoid(gg)))), uu));
+                  const int gu = u + pa;
+                  a.act[sm.loc[gu / a.I] * a.I + gu % a.I] =
+                      to_bf(__fmul_rn(rbf(__fmul_rn(gg, rbf(rsigmoid(gg)))), uu));
                 }
                 if (vc) {
                   const float gg = rbf(v[2]), uu = rbf(v[3]);
-                  a.act[r * a.I + i0 + pc] = to_bf(__fmul_rn(rbf(__fmul_rn(gg, rbf(rsigmoid(gg)))), uu));
+                  const int gu = u + pc;
+                  a.act[sm.loc[gu / a.I] * a.I + gu % a.I] =
+                      to_bf(__fmul_rn(rbf(__fmul_rn(gg, rbf(rsigmoid(gg)))), uu));
                 }
               }
             }
