@@ -188,6 +188,15 @@ typedef struct RecShard {
 REC_API int rec_set_shard(RecCtx* ctx, const RecShard* shard);
 REC_API size_t rec_exchange_bytes(const RecCtx* ctx);
 
+/* Schedule of a decode step at `position`: 0 = one persistent cooperative
+ * kernel per call, 1 = a CUDA graph of separate kernels per step (7 per layer
+ * + 3).  REC_SCHEDULE=mega / graph forces one; otherwise the persistent
+ * kernel runs while a layer's attended KV is below 36 MiB (about 64K tokens
+ * with a 4-bit cache, 32K with an 8-bit one) and the graph above it, where
+ * the standalone attention kernel is faster.  Sessions split over ranks run
+ * on the persistent kernel.  -1 for a null context.  (The reference's step is
+ * always its single Metal dispatch, megakernel.py:1224-1301.) */
+REC_API int32_t rec_schedule_for(const RecCtx* ctx, int32_t position);
 /* Kernels of one step, in launch order; layer kernels repeat per layer. */
 enum {
   REC_K_EMBED = 0, REC_K_QKV = 1, REC_K_ATTN = 2, REC_K_COMBINE = 3, REC_K_OPROJ = 4, REC_K_ROUTER = 5,

@@ -56,6 +56,7 @@ _SIGNATURES = {
                                     C.c_void_p, C.c_void_p, C.c_void_p]),
     "rec_check_status": (C.c_int, [C.c_void_p, C.c_void_p]),
     "rec_launch_kernel": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
+    "rec_schedule_for": (C.c_int32, [C.c_void_p, C.c_int32]),
     "rec_set_profile": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
     "rec_set_layer_profile": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32]),
 }

@@ -657,6 +657,24 @@ REC_API int rec_set_workspace(RecCtx* c, void* ws, size_t bytes) {
   return REC_OK;
 }
 
+// Schedule of a step at `position`: the persistent kernel, or the CUDA graph
+// of separate kernels.  REC_SCHEDULE=graph / mega forces one; otherwise the
+// persistent kernel runs while a layer's attended KV is below
+// kMegaAttnBytes, and the graph above it: at long contexts attention
+// dominates, and its standalone kernel (two 8-warp CTAs per SM) outruns the
+// persistent kernel's 8 consumer warps per SM (measured crossover: about
+// 64K tokens with a 4-bit cache, 32K with an 8-bit one).  A session split
+// over ranks always runs on the persistent kernel.
+constexpr double kMegaAttnBytes = 36.0 * 1024 * 1024;
+static bool mega_for(const RecCtx* c, int position) {
+  const char* sched = std::getenv("REC_SCHEDULE");
+  if (sched && std::strcmp(sched, "graph") == 0) return false;
+  if (c->d.n_experts > kMegaMaxExperts) return false;
+  if ((sched && std::strcmp(sched, "mega") == 0) || c->world > 1) return true;
+  const double per_token = double(c->d.n_kv_heads) * (c->d.kv_bits == 4 ? 144.0 : 272.0);
+  return double(position + 1) * per_token < kMegaAttnBytes;
+}
+
 static int check_ready(RecCtx* c) {
   REC_CHECK_ARG(c, "null context");
   if (!c->usable) {
@@ -667,16 +685,21 @@ static int check_ready(RecCtx* c) {
     set_error("session not configured (weights, KV and workspace are required)");
     return REC_ESTATE;
   }
-  const char* sched = std::getenv("REC_SCHEDULE");
-  c->use_mega = !(sched && std::strcmp(sched, "graph") == 0) && c->d.n_experts <= kMegaMaxExperts;
   if (c->world > 1) {
-    REC_CHECK_ARG(c->use_mega, "a session split over ranks runs on the persistent kernel only (no REC_SCHEDULE=graph, n_experts <= %d)", kMegaMaxExperts);
+    REC_CHECK_ARG(mega_for(c, 0), "a session split over ranks runs on the persistent kernel only (no REC_SCHEDULE=graph, n_experts <= %d)", kMegaMaxExperts);
     for (int q = 0; q < c->world; ++q)
       if (!c->xch[q]) {
         set_error("rec_set_shard: exchange buffer of rank %d not set", q);
         return REC_ESTATE;
       }
   }
+  return REC_OK;
+}
+
+// Picks the schedule of a call whose last step runs at `last_position` and
+// builds the CUDA graph on first use.
+static int select_schedule(RecCtx* c, int last_position) {
+  c->use_mega = mega_for(c, last_position);
   return c->use_mega ? REC_OK : ensure_graph(c);
 }
 
@@ -787,6 +810,8 @@ REC_API int rec_decode_step(RecCtx* c, int32_t token, int32_t position, void* lo
     return REC_ELIMIT;
   }
   REC_CHECK_ARG(token >= 0 && token < c->d.vocab, "token %d outside the vocabulary", token);
+  rc = select_schedule(c, position);
+  if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   k_set_step<<<1, 32, 0, st>>>(c->ctl, token, position, 0, make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0), 0);
   REC_CHECK_CUDA(cudaGetLastError());
@@ -811,6 +836,8 @@ REC_API int rec_decode_greedy(RecCtx* c, int32_t token, int32_t position, int32_
     set_error("Decode context limit exhausted");
     return REC_ELIMIT;
   }
+  rc = select_schedule(c, position + count - 1);
+  if (rc) return rc;
   int e8[8] = {-1, -1, -1, -1, -1, -1, -1, -1};
   for (int i = 0; i < n_eos; ++i) e8[i] = eos[i];
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -852,6 +879,8 @@ REC_API int rec_decode_sampled(RecCtx* c, int32_t token, int32_t position, int32
     set_error("Decode context limit exhausted");
     return REC_ELIMIT;
   }
+  rc = select_schedule(c, position + count - 1);
+  if (rc) return rc;
   int e8[8] = {-1, -1, -1, -1, -1, -1, -1, -1};
   for (int i = 0; i < n_eos; ++i) e8[i] = eos[i];
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -888,6 +917,11 @@ REC_API int rec_decode_sampled(RecCtx* c, int32_t token, int32_t position, int32
   if (produced_dev)
     REC_CHECK_CUDA(cudaMemcpyAsync(produced_dev, c->ctl + kCtlProduced, 4, cudaMemcpyDeviceToDevice, st));
   return REC_OK;
+}
+
+REC_API int32_t rec_schedule_for(const RecCtx* c, int32_t position) {
+  if (!c) return -1;
+  return mega_for(c, position) ? 0 : 1;
 }
 
 REC_API int rec_launch_kernel(RecCtx* c, int32_t kind, int32_t layer, void* stream) {

@@ -67,3 +67,38 @@ def test_argument_errors_need_no_device():
                             top_k=2, moe_inter=256, vocab=64, group_size=64)
     assert lib.rec_create(C.byref(desc), C.byref(out)) == abi.REC_EINVAL
     assert "hidden" in _lib.last_error().lower()
+
+
+def test_schedule_rule_needs_no_device(monkeypatch):
+    """rec_schedule_for: the persistent kernel below 36 MiB of attended KV per
+    layer, the CUDA graph above it; REC_SCHEDULE forces either; more than 256
+    experts always take the graph."""
+    lib = _lib_or_skip()
+
+    def ctx(kv_bits, n_experts=128):
+        desc = abi.RecModelDesc(hidden=2048, n_layers=2, n_q_heads=32, n_kv_heads=4, head_dim=128,
+                                n_experts=n_experts, top_k=8, moe_inter=768, vocab=4096, group_size=64,
+                                kv_bits=kv_bits)
+        out = C.c_void_p()
+        assert lib.rec_create(C.byref(desc), C.byref(out)) == abi.REC_OK, _lib.last_error()
+        return out
+
+    monkeypatch.delenv("REC_SCHEDULE", raising=False)
+    c4, c8 = ctx(4), ctx(8)
+    limit = 36 * 1024 * 1024
+    for c, per_token in ((c4, 4 * 144), (c8, 4 * 272)):
+        edge = limit // per_token  # positions below it: (edge) * per_token < limit
+        assert lib.rec_schedule_for(c, 1023) == 0
+        assert lib.rec_schedule_for(c, edge - 2) == 0
+        assert lib.rec_schedule_for(c, edge + 1) == 1
+        assert lib.rec_schedule_for(c, 258047) == 1
+    monkeypatch.setenv("REC_SCHEDULE", "mega")
+    assert lib.rec_schedule_for(c4, 258047) == 0
+    monkeypatch.setenv("REC_SCHEDULE", "graph")
+    assert lib.rec_schedule_for(c4, 10) == 1
+    monkeypatch.delenv("REC_SCHEDULE")
+    c512 = ctx(8, n_experts=512)
+    assert lib.rec_schedule_for(c512, 10) == 1
+    assert lib.rec_schedule_for(None, 10) == -1
+    for c in (c4, c8, c512):
+        lib.rec_destroy(c)
