@@ -213,12 +213,15 @@ def run_rec(args):
     t_max = float(t.item())
     value = K / t_max if sharded else K * world / t_max
     # schedule of the timed steps (rec_schedule_for): the persistent kernel
-    # (per packet: k_set_step + k_decode_mega) or, at long contexts, the CUDA
-    # graph of 7 kernels per layer + 3 per step (per packet: k_set_step + the
-    # graph per step)
-    graph_sched = lib().rec_schedule_for(sess.ctx, pos + K - 1) == 1
-    if graph_sched:
+    # (per packet: k_set_step + k_decode_mega); the CUDA graph (7 kernels per
+    # layer + 3 per step); or, at long contexts, the split schedule
+    # (persistent segments around each layer's attention kernels)
+    sched = lib().rec_schedule_for(sess.ctx, pos + K - 1)
+    graph_sched = sched in (1, 2)  # the attention runs as standalone kernels
+    if sched == 1:
         launches = len(packets) + sum(packets) * (7 * cfg.n_layers + 3)
+    elif sched == 2:  # split: L + 1 persistent segments + 2 attention kernels per layer
+        launches = len(packets) + sum(packets) * (3 * cfg.n_layers + 1)
     else:
         launches = 2 * len(packets)
     launch_s = [a.elapsed_time(b) / 1e3 for a, b in launch_events]
@@ -297,7 +300,7 @@ def run_rec(args):
                 "algorithmic_bytes_per_launch": int(launch_bytes), "tokens_per_launch": sum(packets) / len(packets),
                 "mean_launch_ms": round(mean_launch * 1e3, 3), "peak_source": peak_kind}
     if graph_sched and "attn_partial" in per_kernel:
-        # graph schedule: the dominant kernel is the attention partial pass
+        # attention as standalone kernels: the dominant kernel is the attention partial pass
         # (one launch per layer), timed above with CUDA events over 50
         # back-to-back launches of the same state
         ab = kernel_bytes["attn_partial"]
@@ -368,7 +371,8 @@ def run_rec(args):
                    "context_at_timing": ctx0 + W, "kv_bits": cfg.kv_bits,
                    "parallelism": (f"one session: ep{world} + split-kv{world}" if sharded
                                    else (f"replicas{world}" if world > 1 else "single")),
-                   "schedule": "graph (7 kernels per layer)" if graph_sched else "persistent kernel",
+                   "schedule": {0: "persistent kernel", 1: "graph (7 kernels per layer)",
+                                2: "split (persistent segments around the attention kernels)"}[sched],
                    "cache": "synthetic K, V ~ N(0,1) quantized" if fill else "prefilled by decode steps",
                    "l2_flush": "none needed: 1.78 GB streamed per step > 126 MB L2"},
         "clocks": clk,

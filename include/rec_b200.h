@@ -189,13 +189,18 @@ REC_API int rec_set_shard(RecCtx* ctx, const RecShard* shard);
 REC_API size_t rec_exchange_bytes(const RecCtx* ctx);
 
 /* Schedule of a decode step at `position`: 0 = one persistent cooperative
- * kernel per call, 1 = a CUDA graph of separate kernels per step (7 per layer
- * + 3).  REC_SCHEDULE=mega / graph forces one; otherwise the persistent
- * kernel runs while a layer's attended KV is below 36 MiB (about 64K tokens
- * with a 4-bit cache, 32K with an 8-bit one) and the graph above it, where
- * the standalone attention kernel is faster.  Sessions split over ranks run
- * on the persistent kernel.  -1 for a null context.  (The reference's step is
- * always its single Metal dispatch, megakernel.py:1224-1301.) */
+ * kernel per call; 1 = a CUDA graph of separate kernels per step (7 per layer
+ * + 3); 2 = split: per step, persistent-kernel segments (embedding + Q of
+ * layer 0; then per layer O, router, experts and the next layer's Q, the
+ * last with the lm_head) around each layer's standalone attention kernels
+ * (3 per layer + 1 launches).  REC_SCHEDULE=mega / graph / split forces one;
+ * otherwise by one layer's attended KV: 0 below 30 MiB, 2 up to 60 MiB, 1
+ * above (with a 4-bit cache: up to ~54K tokens, ~109K, then the graph; with
+ * an 8-bit one ~29K, ~58K), where the standalone attention kernel is faster.
+ * More than 256 experts always take 1; sessions split over ranks run on 0.
+ * -1 for a null context.  (The
+ * reference's step is always its single Metal dispatch,
+ * megakernel.py:1224-1301.) */
 REC_API int32_t rec_schedule_for(const RecCtx* ctx, int32_t position);
 /* Kernels of one step, in launch order; layer kernels repeat per layer. */
 enum {

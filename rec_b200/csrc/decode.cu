@@ -169,7 +169,7 @@ struct RecCtx {
   cudaStream_t cap_stream = nullptr;
   cudaGraphExec_t step_exec = nullptr;
   // persistent schedule
-  bool use_mega = true;
+  int sched = 0;  // kSchedMega / kSchedGraph / kSchedSplit of the current call
   MegaLayer* mega_layers = nullptr;  // device table, in the workspace
   unsigned long long* router_ll = nullptr;  // [2][E] flag+value router logits of the persistent kernel
   unsigned* mega_cnt = nullptr;      // [2] grid barrier + abort, [Hq] heads, [Hq*n_super] supers
@@ -184,6 +184,8 @@ namespace {
 constexpr int kSuperTokens = kAttBlock * kAttSuper;  // tokens per super-chunk
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+enum { kSchedMega = 0, kSchedGraph = 1, kSchedSplit = 2 };
 
 struct Layout {
   size_t off[24];
@@ -657,23 +659,34 @@ REC_API int rec_set_workspace(RecCtx* c, void* ws, size_t bytes) {
   return REC_OK;
 }
 
-// Schedule of a step at `position`: the persistent kernel, or the CUDA graph
-// of separate kernels.  REC_SCHEDULE=graph / mega forces one; otherwise the
-// persistent kernel runs while a layer's attended KV is below
-// kMegaAttnBytes, and the graph above it: at long contexts attention
-// dominates, and its standalone kernel (two 8-warp CTAs per SM) outruns the
-// persistent kernel's 8 consumer warps per SM (measured crossover: about
-// 64K tokens with a 4-bit cache, 32K with an 8-bit one).  A session split
-// over ranks always runs on the persistent kernel.
-constexpr double kMegaAttnBytes = 36.0 * 1024 * 1024;
-static bool mega_for(const RecCtx* c, int position) {
+// Schedule of a step at `position`: the persistent kernel (kSchedMega), the
+// CUDA graph of separate kernels (kSchedGraph), or the split schedule
+// (kSchedSplit: persistent-kernel segments around the standalone attention
+// kernels of each layer).  REC_SCHEDULE=mega / graph / split forces one;
+// otherwise it follows one layer's attended KV bytes: the persistent kernel
+// below kMegaAttnBytes, the split schedule up to kSplitAttnBytes, the graph
+// above.  At long contexts attention dominates, and its standalone kernel
+// (two 8-warp CTAs per SM) outruns the persistent kernel's 8 consumer warps
+// per SM; the split schedule keeps the persistent kernel's projection,
+// routing and expert phases but loses their prefetch across the attention
+// launches, and past ~60 MiB the graph's overlap of consecutive kernels
+// (programmatic dependent launch) wins.  Measured tok/s (mega / split /
+// graph): 8-bit 16K 344 / 346 / 299; 8-bit 32K 315 / 320 / 287; 4-bit 64K
+// 271 / 298 / 275; 8-bit 64K 235 / 237 / 248; 4-bit 128K 190 / 217 / 219;
+// 4-bit 252K 149 / 161 / 175.  More than kMegaMaxExperts experts take the
+// graph; a session split over ranks always runs on the persistent kernel.
+constexpr double kMegaAttnBytes = 30.0 * 1024 * 1024;
+constexpr double kSplitAttnBytes = 60.0 * 1024 * 1024;
+static int schedule_for(const RecCtx* c, int position) {
   const char* sched = std::getenv("REC_SCHEDULE");
-  if (sched && std::strcmp(sched, "graph") == 0) return false;
-  if (c->d.n_experts > kMegaMaxExperts) return false;
-  if ((sched && std::strcmp(sched, "mega") == 0) || c->world > 1) return true;
-  const double per_token = double(c->d.n_kv_heads) * (c->d.kv_bits == 4 ? 144.0 : 272.0);
-  return double(position + 1) * per_token < kMegaAttnBytes;
+  if (sched && std::strcmp(sched, "graph") == 0) return kSchedGraph;
+  if (c->d.n_experts > kMegaMaxExperts) return kSchedGraph;
+  if ((sched && std::strcmp(sched, "mega") == 0) || c->world > 1) return kSchedMega;
+  if (sched && std::strcmp(sched, "split") == 0) return kSchedSplit;
+  const double bytes = double(position + 1) * double(c->d.n_kv_heads) * (c->d.kv_bits == 4 ? 144.0 : 272.0);
+  return bytes < kMegaAttnBytes ? kSchedMega : (bytes < kSplitAttnBytes ? kSchedSplit : kSchedGraph);
 }
+static bool mega_for(const RecCtx* c, int position) { return schedule_for(c, position) == kSchedMega; }
 
 static int check_ready(RecCtx* c) {
   REC_CHECK_ARG(c, "null context");
@@ -699,8 +712,10 @@ static int check_ready(RecCtx* c) {
 // Picks the schedule of a call whose last step runs at `last_position` and
 // builds the CUDA graph on first use.
 static int select_schedule(RecCtx* c, int last_position) {
-  c->use_mega = mega_for(c, last_position);
-  return c->use_mega ? REC_OK : ensure_graph(c);
+  c->sched = schedule_for(c, last_position);
+  // the split schedule launches the graph's attention kernels, whose set-up
+  // the capture does
+  return c->sched == kSchedMega ? REC_OK : ensure_graph(c);
 }
 
 // Position limit of the session (global when split over ranks).
@@ -708,9 +723,10 @@ static int position_limit(const RecCtx* c) { return c->world > 1 ? c->cap_total 
 
 // One cooperative launch of the persistent kernel for `steps` tokens.
 template <int I, int BITS>
-static cudaError_t launch_mega_t(RecCtx* c, int steps, cudaStream_t st) {
+static cudaError_t launch_mega_t(RecCtx* c, int steps, cudaStream_t st, int seg) {
   const RecModelDesc& d = c->d;
   MegaArgs A = {};
+  A.seg = seg;
   A.layers = c->mega_layers;
   A.n_layers = d.n_layers;
   A.H = d.hidden;
@@ -758,7 +774,7 @@ static cudaError_t launch_mega_t(RecCtx* c, int steps, cudaStream_t st) {
   A.xl = xch_layout(d.n_q_heads, c->world > 1 ? (c->cap_total + kSuperTokens - 1) / kSuperTokens : 1, d.hidden);
   for (int q = 0; q < kMaxWorld; ++q) A.xch[q] = c->xch[q];
   const size_t need = size_t(steps) * (6 * d.n_layers + 1) * c->grid * 2;
-  A.prof = (c->prof && c->prof_entries >= need) ? c->prof : nullptr;
+  A.prof = (c->prof && c->prof_entries >= need && seg == kSegAll) ? c->prof : nullptr;
   A.prof2 = c->prof2;
   A.prof_layer = c->prof_layer;
   auto kern = k_decode_mega<I, BITS>;
@@ -786,19 +802,49 @@ static cudaError_t launch_mega_t(RecCtx* c, int steps, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, kern, A);
-  if (e == cudaSuccess) c->layer_seq += unsigned(steps) * unsigned(d.n_layers);
+  // a segmented step advances the layer sequence once, after its last segment
+  if (e == cudaSuccess && seg == kSegAll) c->layer_seq += unsigned(steps) * unsigned(d.n_layers);
   return e;
 }
 
-static cudaError_t launch_mega(RecCtx* c, int steps, cudaStream_t st) {
+static cudaError_t launch_mega(RecCtx* c, int steps, cudaStream_t st, int seg = kSegAll) {
   const bool kv4 = c->d.kv_bits == 4;
   switch (c->d.moe_inter) {
-    case 256: return kv4 ? launch_mega_t<256, 4>(c, steps, st) : launch_mega_t<256, 8>(c, steps, st);
-    case 512: return kv4 ? launch_mega_t<512, 4>(c, steps, st) : launch_mega_t<512, 8>(c, steps, st);
-    case 768: return kv4 ? launch_mega_t<768, 4>(c, steps, st) : launch_mega_t<768, 8>(c, steps, st);
-    case 1024: return kv4 ? launch_mega_t<1024, 4>(c, steps, st) : launch_mega_t<1024, 8>(c, steps, st);
+    case 256: return kv4 ? launch_mega_t<256, 4>(c, steps, st, seg) : launch_mega_t<256, 8>(c, steps, st, seg);
+    case 512: return kv4 ? launch_mega_t<512, 4>(c, steps, st, seg) : launch_mega_t<512, 8>(c, steps, st, seg);
+    case 768: return kv4 ? launch_mega_t<768, 4>(c, steps, st, seg) : launch_mega_t<768, 8>(c, steps, st, seg);
+    case 1024: return kv4 ? launch_mega_t<1024, 4>(c, steps, st, seg) : launch_mega_t<1024, 8>(c, steps, st, seg);
     default: return cudaErrorInvalidValue;
   }
+}
+
+// One step on the split schedule: persistent-kernel segments for everything
+// but attention (embedding + Q of layer 0, then per layer O, R, G, D and the
+// next layer's Q, the last one ending with H and E), and the standalone
+// attention kernels of each layer between them.
+static cudaError_t launch_split_step(RecCtx* c, cudaStream_t st) {
+  const int L = c->d.n_layers;
+  cudaError_t e = launch_mega(c, 1, st, -1);
+  for (int l = 0; l < L && e == cudaSuccess; ++l) {
+    e = c->d.scale_dtype == REC_SCALE_FP16 ? enqueue_kernel_sd<0>(c, kKAttn, l, st, true)
+                                           : enqueue_kernel_sd<1>(c, kKAttn, l, st, true);
+    if (e == cudaSuccess)
+      e = c->d.scale_dtype == REC_SCALE_FP16 ? enqueue_kernel_sd<0>(c, kKCombine, l, st, true)
+                                             : enqueue_kernel_sd<1>(c, kKCombine, l, st, true);
+    if (e == cudaSuccess) e = launch_mega(c, 1, st, l);
+  }
+  if (e == cudaSuccess) c->layer_seq += unsigned(L);
+  return e;
+}
+
+// One step (graph schedule or split schedule) or a packet of steps
+// (persistent kernel) on the schedule chosen for the call.
+static cudaError_t launch_steps(RecCtx* c, int steps, cudaStream_t st) {
+  cudaError_t e = cudaSuccess;
+  if (c->sched == kSchedMega) return launch_mega(c, steps, st);
+  for (int i = 0; i < steps && e == cudaSuccess; ++i)
+    e = c->sched == kSchedGraph ? cudaGraphLaunch(c->step_exec, st) : launch_split_step(c, st);
+  return e;
 }
 
 REC_API int rec_decode_step(RecCtx* c, int32_t token, int32_t position, void* logits_dev, void* trace_dev,
@@ -815,8 +861,7 @@ REC_API int rec_decode_step(RecCtx* c, int32_t token, int32_t position, void* lo
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   k_set_step<<<1, 32, 0, st>>>(c->ctl, token, position, 0, make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0), 0);
   REC_CHECK_CUDA(cudaGetLastError());
-  if (c->use_mega) REC_CHECK_CUDA(launch_mega(c, 1, st));
-  else REC_CHECK_CUDA(cudaGraphLaunch(c->step_exec, st));
+  REC_CHECK_CUDA(launch_steps(c, 1, st));
   if (logits_dev)
     REC_CHECK_CUDA(cudaMemcpyAsync(logits_dev, c->logits, size_t(c->d.vocab) * 2, cudaMemcpyDeviceToDevice, st));
   if (trace_dev)
@@ -844,9 +889,7 @@ REC_API int rec_decode_greedy(RecCtx* c, int32_t token, int32_t position, int32_
   k_set_step<<<1, 32, 0, st>>>(c->ctl, token, position, n_eos, make_int4(e8[0], e8[1], e8[2], e8[3]),
                                make_int4(e8[4], e8[5], e8[6], e8[7]), 0);
   REC_CHECK_CUDA(cudaGetLastError());
-  if (c->use_mega) REC_CHECK_CUDA(launch_mega(c, count, st));
-  else
-    for (int i = 0; i < count; ++i) REC_CHECK_CUDA(cudaGraphLaunch(c->step_exec, st));
+  REC_CHECK_CUDA(launch_steps(c, count, st));
   if (ids_dev)
     REC_CHECK_CUDA(cudaMemcpyAsync(ids_dev, c->ctl + kCtlRecorded, size_t(count) * 4, cudaMemcpyDeviceToDevice, st));
   if (produced_dev)
@@ -906,8 +949,7 @@ REC_API int rec_decode_sampled(RecCtx* c, int32_t token, int32_t position, int32
   const size_t dyn = size_t((V + 31) / 32) * 4;
   REC_CHECK_CUDA(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, int(dyn)));
   for (int i = 0; i < count; ++i) {
-    if (c->use_mega) REC_CHECK_CUDA(launch_mega(c, 1, st));
-    else REC_CHECK_CUDA(cudaGraphLaunch(c->step_exec, st));
+    REC_CHECK_CUDA(launch_steps(c, 1, st));
     sa.uniforms = uniforms_dev + size_t(i) * V;
     k_sample<<<1, kSampleThreads, dyn, st>>>(sa);
     REC_CHECK_CUDA(cudaGetLastError());
@@ -921,7 +963,7 @@ REC_API int rec_decode_sampled(RecCtx* c, int32_t token, int32_t position, int32
 
 REC_API int32_t rec_schedule_for(const RecCtx* c, int32_t position) {
   if (!c) return -1;
-  return mega_for(c, position) ? 0 : 1;
+  return schedule_for(c, position);
 }
 
 REC_API int rec_launch_kernel(RecCtx* c, int32_t kind, int32_t layer, void* stream) {

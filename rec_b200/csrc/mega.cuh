@@ -133,6 +133,11 @@ struct MegaArgs {
   unsigned layer_seq0;  // layer steps run before this launch (exchange parity)
   XchLayout xl;
   uint8_t* xch[kMaxWorld];
+  // kSegAll: the whole step(s).  Otherwise one segment of a step whose
+  // attention runs as separate kernels (steps == 1): seg == -1 is the
+  // embedding + Q of layer 0; seg == l >= 0 is O, R, G, D of layer l, then
+  // Q of layer l + 1 (or H and E after the last layer)
+  int seg;
   unsigned long long* prof;  // optional: [barrier][cta] x (arrive, release) globaltimer stamps
   unsigned long long* prof2; // optional: [cta][64] stamps inside layer prof_layer of step 0
   int prof_layer;
@@ -287,6 +292,15 @@ __device__ __forceinline__ void prof_add(const MegaArgs& a, int step, int layer,
   if (a.prof2 && step == 0 && layer == a.prof_layer) a.prof2[blockIdx.x * 64 + slot] += v;
 #endif
 }
+
+constexpr int kSegAll = -2;
+__device__ __forceinline__ int seg_l0(const MegaArgs& a) { return a.seg == kSegAll ? 0 : max(0, a.seg); }
+__device__ __forceinline__ int seg_l1(const MegaArgs& a) {
+  return a.seg == kSegAll ? a.n_layers : min(a.n_layers, a.seg + 2);
+}
+__device__ __forceinline__ bool seg_q(const MegaArgs& a, int l) { return a.seg == kSegAll || l == a.seg + 1; }
+__device__ __forceinline__ bool seg_orgd(const MegaArgs& a, int l) { return a.seg == kSegAll || l == a.seg; }
+__device__ __forceinline__ bool seg_h(const MegaArgs& a) { return a.seg == kSegAll || a.seg == a.n_layers - 1; }
 
 // Grid barrier index of a phase: each step has 6 per layer + 1 (after H).
 // Phase 3 (router logits -> selection) is not a grid barrier: its timeline
@@ -660,14 +674,16 @@ struct Producer {
     const Part P = partition(a);
     const int pos0 = sm.pos0;
     const int qrows[3] = {a.hq * 128, a.hkv * 128, a.hkv * 128};
+    const bool attn_in = a.seg == kSegAll;
     for (int step = 0; step < a.steps && ok; ++step) {
       const int pos = pos0 + step;
       const AttnPlan AP = attn_plan(a, pos);
-      for (int l = 0; l < a.n_layers && ok; ++l) {
+      for (int l = seg_l0(a); l < seg_l1(a) && ok; ++l) {
         const MegaLayer& L = sm.layers[l];
+        const bool orgd = seg_orgd(a, l);
         if (lane == 0) {
           // Q rows (q | k | v), chunks never cross matrices
-          for (int r = P.q0; r < P.q1 && ok;) {
+          for (int r = P.q0; r < P.q1 && ok && seg_q(a, l);) {
             int m = 0, base = 0;
             while (m < 2 && r >= base + qrows[m]) base += qrows[m++];
             const int n = min(min(kQRows, P.q1 - r), base + qrows[m] - r);
@@ -675,7 +691,7 @@ struct Producer {
             r += n;
           }
           // A: K and V tiles of this CTA's items
-          for (int it = blockIdx.x; it < AP.items && ok; it += gridDim.x) {
+          for (int it = blockIdx.x; it < AP.items && ok && attn_in; it += gridDim.x) {
             int g, item;
             attn_coords(AP, a.hkv, it, g, item);
             const int b1 = min(item * AP.nbi + AP.nbi, AP.nblk);
@@ -690,14 +706,16 @@ struct Producer {
             }
             stamp(a, step, l, 24);
           }
-          if (ok) merge_chunks(AP, step, l);
+          if (ok && attn_in) merge_chunks(AP, step, l);
           // O rows
-          for (int r = P.o0; r < P.o1 && ok; r += kORows) gemv_chunk(L.o, a.hq * 128, r, min(kORows, P.o1 - r));
+          for (int r = P.o0; r < P.o1 && ok && orgd; r += kORows)
+            gemv_chunk(L.o, a.hq * 128, r, min(kORows, P.o1 - r));
           // R: this CTA's router rows
-          for (int e = blockIdx.x; e < a.E && ok; e += gridDim.x) router_chunk(L, e);
+          for (int e = blockIdx.x; e < a.E && ok && orgd; e += gridDim.x) router_chunk(L, e);
         }
         __syncwarp();
         ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!orgd) continue;
         // G / D need this layer's routing: the warp selects the experts as
         // soon as every router logit has landed
         if (ok) ok = route_ll(L, step, l, lane);
@@ -725,7 +743,7 @@ struct Producer {
         __syncwarp();
         ok = __shfl_sync(0xffffffffu, ok, 0);
       }
-      if (lane == 0) {
+      if (lane == 0 && seg_h(a)) {
         int v0, v1;
         split_range(a.V / 2, gridDim.x, blockIdx.x, v0, v1);
         v0 *= 2;
@@ -1292,7 +1310,12 @@ struct Consumers {
       const int pos = pos0 + step;
       const AttnPlan AP = attn_plan(a, pos);
       // embedding (every CTA, for its own layer-0 norm); owners publish rows
-      {
+      if (a.seg != kSegAll && a.seg >= 0) {
+        // a later segment of the step: this CTA's rows of h from the
+        // previous segment (same partition)
+        for (int i = threadIdx.x - 32; i < P.o1 - P.o0; i += kMegaCons * 32) sm.hown[i] = __ldcg(a.h + P.o0 + i);
+        cons_sync();
+      } else {
         const int tok = (token >= 0 && token < a.V) ? token : 0;
         if (tok != token && blockIdx.x == 0 && warp == 0 && lane == 0) report(a.ctl + 0, kStatusBadToken);
         const uint32_t* w = a.embed.w + size_t(tok) * (H / 8);
@@ -1310,11 +1333,12 @@ struct Consumers {
         }
         cons_sync();
       }
-      for (int l = 0; l < a.n_layers; ++l) {
+      const bool attn_in = a.seg == kSegAll;
+      for (int l = seg_l0(a); l < seg_l1(a); ++l) {
         const MegaLayer& L = sm.layers[l];
         // ---- Q
-        const FixScale fq = norm(l == 0 ? sm.h0 : a.h, L.input_norm, l == 0);
-        {
+        if (seg_q(a, l)) {
+          const FixScale fq = norm(l == 0 ? sm.h0 : a.h, L.input_norm, l == 0);
           GroupX gx[1];
           share_limbs(sm.xn, 32, fq);
           load_limbs(sm.xn, sm.gX, 32, lane, gx[0]);
@@ -1328,9 +1352,11 @@ struct Consumers {
             release();
             r += n;
           }
+          if (!attn_in) continue;  // a segment ends with Q: attention runs as separate kernels
+          if (!gbar(bar_index(a, step, l, 0))) return;
         }
-        if (!gbar(bar_index(a, step, l, 0))) return;
         // ---- A
+        if (attn_in) {
         if (warp == 0 && lane == 0) stamp(a, step, l, 11);
         if (warp == 0 && lane == 0) sm.att.qg = -1;  // queries change every layer
         cons_sync();
@@ -1363,6 +1389,8 @@ struct Consumers {
         }
         if (a.world > 1 && warp == 0) attn_final_sharded(L, AP, xch_parity(a, step, l));
         if (!gbar(bar_index(a, step, l, 1))) return;
+        }
+        if (!seg_orgd(a, l)) continue;
         // ---- O
         {
           if (warp == 0 && lane == 0) stamp(a, step, l, 40);
@@ -1550,6 +1578,7 @@ struct Consumers {
         }
         if (!gbar(bar_index(a, step, l, 5))) return;
       }
+      if (!seg_h(a)) continue;  // a segment that ends before the last layer's D
       // ---- H: final norm + lm_head + CTA argmax
       const FixScale fh = norm(a.h, a.final_norm);
       {
@@ -1653,8 +1682,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_decode_mega(const MegaArgs 
   {
     const uint32_t* src = reinterpret_cast<const uint32_t*>(a.layers);
     uint32_t* dst = reinterpret_cast<uint32_t*>(sm.layers);
-    const int words = a.n_layers * int(sizeof(MegaLayer) / 4);
-    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+    // the layers this launch runs (all of them, or a segment's one or two)
+    constexpr int per = int(sizeof(MegaLayer) / 4);
+    for (int i = seg_l0(a) * per + threadIdx.x; i < seg_l1(a) * per; i += blockDim.x) dst[i] = src[i];
   }
   __syncthreads();
   if (threadIdx.x < 32) {

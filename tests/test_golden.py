@@ -81,7 +81,7 @@ def _device_weights(m, dev):
     return ModelWeights(m.cfg, layers, q(m.embed), bf(m.final_norm), q(m.lm_head))
 
 
-@pytest.fixture(params=["mega", "graph"])
+@pytest.fixture(params=["mega", "graph", "split"])
 def schedule(request, monkeypatch):
     monkeypatch.setenv("REC_SCHEDULE", request.param)
     return request.param

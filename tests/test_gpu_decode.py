@@ -16,7 +16,7 @@ from rec_b200.session import DecodeSession
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["mega", "graph"])
+@pytest.fixture(params=["mega", "graph", "split"])
 def schedule(request, monkeypatch):
     """The persistent kernel (default) and the per-kernel CUDA graph."""
     monkeypatch.setenv("REC_SCHEDULE", request.param)

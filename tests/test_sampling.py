@@ -321,7 +321,7 @@ def test_gpu_resident_sampler_block(cuda):
     assert ids == want
 
 
-@pytest.mark.parametrize("schedule", ["mega", "graph"])
+@pytest.mark.parametrize("schedule", ["mega", "graph", "split"])
 def test_gpu_resident_sampler_eos(cuda, schedule, monkeypatch):
     """A sampled packet stops recording at an EOS id (included), on both
     schedules, and the ids before it equal the packet without EOS."""
