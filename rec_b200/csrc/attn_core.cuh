@@ -84,7 +84,7 @@ __device__ __forceinline__ void store_partial(float* dst, const Partial4& P) {
 // Folds partials [i0, i1) of a [*, kPartialFloats] array (L2 reads) into P in
 // order, with kBatch loads in flight.
 __device__ __forceinline__ void fold_partials(Partial4& P, const float* base, int i0, int i1) {
-  constexpr int kBatch = 4;
+  constexpr int kBatch = 16;  // loads in flight before the in-order merges
   const int lane = threadIdx.x & 31;
   for (int i = i0; i < i1; i += kBatch) {
     Partial4 Q[kBatch];

@@ -211,6 +211,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
           }
           asm volatile("bar.sync %0, %1;" ::"r"(1 + team), "r"(TEAM * 32));
         }
+        // residual rows read before any store, so the loads are in flight together
+        float res[ILP];
+#pragma unroll
+        for (int i = 0; i < ILP; ++i) {
+          res[i] = 0.0f;
+          if constexpr (EPI == kEpiResidual)
+            if (valid[i] && (C::wide ? (lane == 0 && seg == 0) : (l == 0))) res[i] = bf(a.resid[g0 + rows[i]]);
+        }
 #pragma unroll
         for (int i = 0; i < ILP; ++i) {
           const bool writer = valid[i] && (C::wide ? (lane == 0 && seg == 0) : (l == 0));
@@ -220,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
             if constexpr (EPI == kEpiStore) {
               a.out[grow] = to_bf(v[i]);
             } else if constexpr (EPI == kEpiResidual) {
-              a.resid[grow] = to_bf(__fadd_rn(bf(a.resid[grow]), rbf(v[i])));
+              a.resid[grow] = to_bf(__fadd_rn(res[i], rbf(v[i])));
             } else {
               uint16_t o = to_bf(v[i]);
               a.out[grow] = o;

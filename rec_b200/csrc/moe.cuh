@@ -86,21 +86,28 @@ __global__ void __launch_bounds__(kThreads) k_router(const RouterArgs a) {
   if (!sm.is_last || warp != 0) return;
   __threadfence();
   const int E = a.E;
+  // the logits once into shared memory (all loads in flight together)
+  for (int i = lane; i < E; i += 32) sm.p[i] = __ldcg(a.logits + i);
+  __syncwarp();
   if (a.mode == 0) {
     float mx = -INFINITY;
-    for (int i = lane; i < E; i += 32) mx = fmaxf(mx, __ldcg(a.logits + i));
+    for (int i = lane; i < E; i += 32) mx = fmaxf(mx, sm.p[i]);
     mx = bfly_max(mx);
     float s = 0.0f;
-    for (int i = lane; i < E; i += 32) s = __fadd_rn(s, rexp(__fsub_rn(__ldcg(a.logits + i), mx)));
+    for (int i = lane; i < E; i += 32) {
+      const float c = rexp(__fsub_rn(sm.p[i], mx));
+      sm.choice[i] = c;
+      s = __fadd_rn(s, c);
+    }
     s = bfly_sum(s);
     for (int i = lane; i < E; i += 32) {
-      const float pi = __fdiv_rn(rexp(__fsub_rn(__ldcg(a.logits + i), mx)), s);
+      const float pi = __fdiv_rn(sm.choice[i], s);
       sm.p[i] = pi;
       sm.choice[i] = pi;
     }
   } else {
     for (int i = lane; i < E; i += 32) {
-      const float pi = rsigmoid(__ldcg(a.logits + i));
+      const float pi = rsigmoid(sm.p[i]);
       sm.p[i] = pi;
       sm.choice[i] = __fadd_rn(pi, a.expert_bias[i]);
     }
