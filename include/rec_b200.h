@@ -194,11 +194,11 @@ REC_API size_t rec_exchange_bytes(const RecCtx* ctx);
  * layer 0; then per layer O, router, experts and the next layer's Q, the
  * last with the lm_head) around each layer's standalone attention kernels
  * (3 per layer + 1 launches).  REC_SCHEDULE=mega / graph / split forces one;
- * otherwise by one layer's attended KV: 0 below 30 MiB, 2 up to 60 MiB, 1
- * above (with a 4-bit cache: up to ~54K tokens, ~109K, then the graph; with
- * an 8-bit one ~29K, ~58K), where the standalone attention kernel is faster.
- * More than 256 experts always take 1; sessions split over ranks run on 0.
- * -1 for a null context.  (The
+ * otherwise 0 while one layer's attended KV is below 24 MiB (about 43K
+ * tokens with a 4-bit cache, 23K with an 8-bit one) and 1 above it, where
+ * the standalone attention kernel is faster; 2 runs only when forced.  More
+ * than 256 experts always take 1; sessions split over ranks run on 0.  -1
+ * for a null context.  (The
  * reference's step is always its single Metal dispatch,
  * megakernel.py:1224-1301.) */
 REC_API int32_t rec_schedule_for(const RecCtx* ctx, int32_t position);

@@ -663,20 +663,18 @@ REC_API int rec_set_workspace(RecCtx* c, void* ws, size_t bytes) {
 // CUDA graph of separate kernels (kSchedGraph), or the split schedule
 // (kSchedSplit: persistent-kernel segments around the standalone attention
 // kernels of each layer).  REC_SCHEDULE=mega / graph / split forces one;
-// otherwise it follows one layer's attended KV bytes: the persistent kernel
-// below kMegaAttnBytes, the split schedule up to kSplitAttnBytes, the graph
-// above.  At long contexts attention dominates, and its standalone kernel
-// (two 8-warp CTAs per SM) outruns the persistent kernel's 8 consumer warps
-// per SM; the split schedule keeps the persistent kernel's projection,
-// routing and expert phases but loses their prefetch across the attention
-// launches, and past ~60 MiB the graph's overlap of consecutive kernels
-// (programmatic dependent launch) wins.  Measured tok/s (mega / split /
-// graph): 8-bit 16K 344 / 346 / 299; 8-bit 32K 315 / 320 / 287; 4-bit 64K
-// 271 / 298 / 275; 8-bit 64K 235 / 237 / 248; 4-bit 128K 190 / 217 / 219;
-// 4-bit 252K 149 / 161 / 175.  More than kMegaMaxExperts experts take the
-// graph; a session split over ranks always runs on the persistent kernel.
-constexpr double kMegaAttnBytes = 30.0 * 1024 * 1024;
-constexpr double kSplitAttnBytes = 60.0 * 1024 * 1024;
+// otherwise the persistent kernel runs while one layer's attended KV is
+// below kMegaAttnBytes and the graph above it.  At long contexts attention
+// dominates, and its standalone kernel (two 8-warp CTAs per SM) outruns the
+// persistent kernel's 8 consumer warps per SM, while the graph overlaps
+// consecutive kernels (programmatic dependent launch).  Measured tok/s
+// (mega / split / graph): 8-bit 16K 347 / 344 / 330; 8-bit 32K 311 / 313 /
+// 326; 4-bit 64K 268 / 292 / 307; 4-bit 128K 188 / 206 / 242.  The split
+// schedule (each segment starts cold, without the weight prefetch across
+// the attention launches) is never the fastest and runs only when forced.
+// More than kMegaMaxExperts experts take the graph; a session split over
+// ranks always runs on the persistent kernel.
+constexpr double kMegaAttnBytes = 24.0 * 1024 * 1024;
 static int schedule_for(const RecCtx* c, int position) {
   const char* sched = std::getenv("REC_SCHEDULE");
   if (sched && std::strcmp(sched, "graph") == 0) return kSchedGraph;
@@ -684,7 +682,7 @@ static int schedule_for(const RecCtx* c, int position) {
   if ((sched && std::strcmp(sched, "mega") == 0) || c->world > 1) return kSchedMega;
   if (sched && std::strcmp(sched, "split") == 0) return kSchedSplit;
   const double bytes = double(position + 1) * double(c->d.n_kv_heads) * (c->d.kv_bits == 4 ? 144.0 : 272.0);
-  return bytes < kMegaAttnBytes ? kSchedMega : (bytes < kSplitAttnBytes ? kSchedSplit : kSchedGraph);
+  return bytes < kMegaAttnBytes ? kSchedMega : kSchedGraph;
 }
 static bool mega_for(const RecCtx* c, int position) { return schedule_for(c, position) == kSchedMega; }
 

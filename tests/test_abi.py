@@ -70,9 +70,9 @@ def test_argument_errors_need_no_device():
 
 
 def test_schedule_rule_needs_no_device(monkeypatch):
-    """rec_schedule_for: the persistent kernel below 30 MiB of attended KV per
-    layer, the split schedule up to 60 MiB, the graph above; REC_SCHEDULE
-    forces any of the three; more than 256 experts always take the graph."""
+    """rec_schedule_for: the persistent kernel below 24 MiB of attended KV per
+    layer, the graph above; REC_SCHEDULE forces any of the three (split only
+    when forced); more than 256 experts always take the graph."""
     lib = _lib_or_skip()
 
     def ctx(kv_bits, n_experts=128):
@@ -86,13 +86,10 @@ def test_schedule_rule_needs_no_device(monkeypatch):
     monkeypatch.delenv("REC_SCHEDULE", raising=False)
     c4, c8 = ctx(4), ctx(8)
     for c, per_token in ((c4, 4 * 144), (c8, 4 * 272)):
-        mega_edge = 30 * 1024 * 1024 // per_token  # tokens at which the persistent kernel stops
-        split_edge = 60 * 1024 * 1024 // per_token
+        edge = 24 * 1024 * 1024 // per_token  # tokens at which the persistent kernel stops
         assert lib.rec_schedule_for(c, 1023) == 0
-        assert lib.rec_schedule_for(c, mega_edge - 2) == 0
-        assert lib.rec_schedule_for(c, mega_edge + 1) == 2
-        assert lib.rec_schedule_for(c, split_edge - 2) == 2
-        assert lib.rec_schedule_for(c, split_edge + 1) == 1
+        assert lib.rec_schedule_for(c, edge - 2) == 0
+        assert lib.rec_schedule_for(c, edge + 1) == 1
         assert lib.rec_schedule_for(c, 258047) == 1
     monkeypatch.setenv("REC_SCHEDULE", "mega")
     assert lib.rec_schedule_for(c4, 258047) == 0
