@@ -53,6 +53,8 @@ def parse():
     p.add_argument("--prefill", action="store_true",
                    help="the tensor-core prefill projections (rec_prefill_gemm) of one config-3 layer")
     p.add_argument("--tokens", default="1024,4096", help="prompt lengths for --prefill")
+    p.add_argument("--sample-head", action="store_true",
+                   help="config 5: final RMSNorm + int4 lm_head + penalty/top-k/top-p sampler, batch 1 and 8")
     p.add_argument("--shard", action="store_true",
                    help="with N GPUs: one session split over the GPUs (expert parallelism + split-KV, the "
                         "config-4 partitioning) instead of N independent sessions (config 3 replicas)")
@@ -599,9 +601,62 @@ def run_prefill(args):
                       "rows": rows}), flush=True)
 
 
+def run_sample_head(args):
+    """Config 5: rec_lmhead_sample (final RMSNorm + int4 g64 lm_head 2,048 ->
+    151,936 + repetition penalty 1.1 over 4,096 history ids, T 0.7, top-k 40,
+    top-p 0.95, injected Philox uniforms) at batch 1 and 8.  Each call is
+    timed with CUDA events over `steps` back-to-back calls on the launching
+    stream; the lm_head (175 MB, more than the 126 MB L2) is re-read from HBM
+    every call.  GB/s counts the algorithmic bytes of one call: the weights
+    once, plus per row its hidden vector, logits (written and re-read by the
+    sampler), history and uniforms."""
+    import torch
+
+    from rec_b200 import ops, sampling
+    from rec_b200.model import QTensor
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    V, H = 151936, 2048
+    g = torch.Generator(device=dev).manual_seed(5)
+    w = torch.randn(V, H, generator=g, device=dev) * 0.02
+    lm = QTensor(*ops.quantize_affine(w, 4, torch.float16))
+    del w
+    fn = (1 + 0.1 * torch.randn(H, generator=g, device=dev)).to(torch.bfloat16)
+    p = sampling.params(0.7, 40, 0.95, 1.1)
+    peak, kind = measured_peaks()
+    wbytes = lm.w.numel() * lm.w.element_size() + lm.s.numel() * 2 + lm.b.numel() * 2
+    rows = []
+    for batch in (1, 8):
+        h = torch.randn(batch, H, generator=g, device=dev).to(torch.bfloat16)
+        hist = torch.randint(0, V, (batch, 4096), generator=g, device=dev, dtype=torch.int32)
+        u = sampling.uniforms(batch, V, 11, dev)
+        for _ in range(max(3, args.warmup)):
+            sampling.sample_head(h, fn, lm, torch.float16, p, u, hist)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            sampling.sample_head(h, fn, lm, torch.float16, p, u, hist)
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) / args.steps * 1e3
+        alg = wbytes + batch * (H * 2 + 2 * V * 2 + 4096 * 4 + V * 4)
+        rows.append({"batch": batch, "us_per_call": round(us, 2), "rows_per_s": round(batch / (us * 1e-6), 1),
+                     "algorithmic_bytes": int(alg), "GBps": round(alg / (us * 1e-6) / 1e9, 1),
+                     "frac": round(alg / (us * 1e-6) / 1e9 / peak, 4),
+                     "lm_head": ("k_gemv (one pass over the weights)" if batch == 1
+                                 else "k_gemv_batch (tensor cores, one pass for 8 rows)")})
+    print(json.dumps({"workload": "config5_sampling_head", "peak_GBps": peak, "peak_source": kind,
+                      "steps": args.steps, "sampler": "rep 1.1 over 4,096 ids, T 0.7, top-k 40, top-p 0.95",
+                      "rows": rows}), flush=True)
+
+
 def main():
     args = parse()
-    if args.prefill:
+    if args.sample_head:
+        run_sample_head(args)
+    elif args.prefill:
         run_prefill(args)
     elif args.attn_sweep:
         run_attn_sweep(args)

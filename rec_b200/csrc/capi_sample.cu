@@ -4,6 +4,11 @@
 
 using namespace rec;
 
+namespace rec {
+int lmhead_batch(const RecQMat* w, int sd, int V, const void* h, int B, const void* norm, float eps, void* out,
+                 int* status, cudaStream_t st);  // lmhead_batch.cu
+}
+
 REC_API int rec_sample_logits_masked(const void* logits_dev, int32_t batch, int32_t vocab, int64_t stride,
                                      const int32_t* history_dev, int32_t history_len, const RecSampling* params,
                                      const float* uniforms_dev, const uint32_t* allow_dev, int64_t allow_stride,
@@ -64,10 +69,25 @@ REC_API int rec_lmhead_sample(const RecQMat* lm_head, int32_t scale_dtype, int32
   REC_CHECK_ARG(hidden > 0 && vocab > 0, "rec_lmhead_sample: bad shape");
   const uint16_t* h = static_cast<const uint16_t*>(h_dev);
   uint16_t* lg = static_cast<uint16_t*>(logits_dev);
-  for (int b = 0; b < batch; ++b) {
-    const int rc = rec_gemv_int4(lm_head, scale_dtype, vocab, hidden, h + size_t(b) * hidden, final_norm_dev, eps,
-                                 lg + size_t(b) * vocab, stream);
-    if (rc) return rc;
+  const bool batched = batch > 1 && hidden == 2048 && vocab % 8 == 0 && lm_head->w && lm_head->scales &&
+                       lm_head->biases && aligned16(lm_head->w) && aligned16(lm_head->scales) &&
+                       aligned16(lm_head->biases) && aligned16(h_dev) && (reinterpret_cast<uintptr_t>(lg) & 3u) == 0;
+  if (batched) {
+    // up to 8 rows per pass over the weights, on the tensor cores
+    // (bit-identical to the per-row GEMV)
+    REC_CHECK_ARG(scale_dtype == REC_SCALE_FP16 || scale_dtype == REC_SCALE_BF16, "bad scale dtype");
+    for (int b0 = 0; b0 < batch; b0 += 8) {
+      const int rc = lmhead_batch(lm_head, scale_dtype, vocab, h + size_t(b0) * hidden,
+                                  batch - b0 < 8 ? batch - b0 : 8, final_norm_dev, eps, lg + size_t(b0) * vocab,
+                                  nullptr, static_cast<cudaStream_t>(stream));
+      if (rc) return rc;
+    }
+  } else {
+    for (int b = 0; b < batch; ++b) {
+      const int rc = rec_gemv_int4(lm_head, scale_dtype, vocab, hidden, h + size_t(b) * hidden, final_norm_dev, eps,
+                                   lg + size_t(b) * vocab, stream);
+      if (rc) return rc;
+    }
   }
   return rec_sample_logits(logits_dev, batch, vocab, vocab, history_dev, history_len, params, uniforms_dev, ids_dev,
                            stream);

@@ -257,7 +257,7 @@ def test_gpu_sampler_threshold_ties(cuda):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("batch", [1, 8])
+@pytest.mark.parametrize("batch", [1, 3, 8])
 def test_gpu_sample_head_config5(cuda, batch):
     """Config 5: final RMSNorm + int4 lm_head 2048 -> 151,936 + penalty 1.1
     over 4,096 history ids, T 0.7, top-k 40, top-p 0.95, Philox uniforms."""
