@@ -830,6 +830,7 @@ static int cand_desc(const void* pa, const void* pb) {
 }
 
 #define SAMPLE_THREADS 1024
+#define SAMPLE_CLUSTER 8
 #define SAMPLE_MAX_CAND 1024
 
 /* Sampling head of one row (rec_b200/csrc/sample.cuh states the rule):
@@ -879,17 +880,25 @@ ORC_API int32_t orc_sample_masked(const uint16_t* logits, int64_t V, const int32
     free(x);
     return Mi;
   }
-  /* S: thread t sums i = t, t+1024, ...; warp butterflies; warps in order */
+  /* S: 8 chunks of Q = ceil(V / 8192) * 1024 ids; in chunk c thread t sums
+   * ids cQ + t, cQ + t + 1024, ...; warp butterflies; warps in order; chunks
+   * in order (one CTA of a cluster per chunk on the GPU) */
+  const int64_t Q = (V + SAMPLE_CLUSTER * SAMPLE_THREADS - 1) / (SAMPLE_CLUSTER * SAMPLE_THREADS) * SAMPLE_THREADS;
   float tot = 0.0f;
-  for (int w = 0; w < SAMPLE_THREADS / 32; ++w) {
-    float lanes[32];
-    for (int l = 0; l < 32; ++l) {
-      float acc = 0.0f;
-      for (int64_t i = w * 32 + l; i < V; i += SAMPLE_THREADS) acc = acc + rexp(x[i] - M);
-      lanes[l] = acc;
+  for (int c = 0; c < SAMPLE_CLUSTER; ++c) {
+    const int64_t lo = c * Q < V ? c * Q : V, hi = lo + Q < V ? lo + Q : V;
+    float part = 0.0f;
+    for (int w = 0; w < SAMPLE_THREADS / 32; ++w) {
+      float lanes[32];
+      for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int64_t i = lo + w * 32 + l; i < hi; i += SAMPLE_THREADS) acc = acc + rexp(x[i] - M);
+        lanes[l] = acc;
+      }
+      bfly(lanes, 32);
+      part = part + lanes[0];
     }
-    bfly(lanes, 32);
-    tot = tot + lanes[0];
+    tot = tot + part;
   }
   const float lse = M + rlog(tot);
   const float inv_t = 1.0f / sp->temperature;

@@ -45,10 +45,7 @@ REC_API int rec_sample_logits_masked(const void* logits_dev, int32_t batch, int3
   a.allow = allow_dev;
   a.allow_stride = allow_stride;
   a.ids = ids_dev;
-  const size_t dyn = size_t((vocab + 31) / 32) * 4;
-  REC_CHECK_CUDA(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, int(dyn)));
-  k_sample<<<batch, kSampleThreads, dyn, static_cast<cudaStream_t>(stream)>>>(a);
-  REC_CHECK_CUDA(cudaGetLastError());
+  REC_CHECK_CUDA(launch_sample(a, batch, static_cast<cudaStream_t>(stream)));
   return REC_OK;
 }
 

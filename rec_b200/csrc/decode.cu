@@ -944,13 +944,10 @@ REC_API int rec_decode_sampled(RecCtx* c, int32_t token, int32_t position, int32
   sa.hist_len = history_cap ? history_len_dev : nullptr;
   sa.hist_out = history_cap ? history_dev : nullptr;
   sa.hist_cap = history_cap;
-  const size_t dyn = size_t((V + 31) / 32) * 4;
-  REC_CHECK_CUDA(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, int(dyn)));
   for (int i = 0; i < count; ++i) {
     REC_CHECK_CUDA(launch_steps(c, 1, st));
     sa.uniforms = uniforms_dev + size_t(i) * V;
-    k_sample<<<1, kSampleThreads, dyn, st>>>(sa);
-    REC_CHECK_CUDA(cudaGetLastError());
+    REC_CHECK_CUDA(launch_sample(sa, 1, st));
   }
   if (ids_dev)
     REC_CHECK_CUDA(cudaMemcpyAsync(ids_dev, c->ctl + kCtlRecorded, size_t(count) * 4, cudaMemcpyDeviceToDevice, st));

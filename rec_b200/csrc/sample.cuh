@@ -1,6 +1,9 @@
 // Sampling head over bf16 logits: repetition / presence penalty, temperature,
-// top-k and top-p with injected uniforms, or greedy argmax.  One CTA of 1024
-// threads per batch row; the row's logits are re-read from L2 by each pass.
+// top-k and top-p with injected uniforms, or greedy argmax.  One cluster of 8
+// CTAs of 1024 threads per batch row, each CTA over one eighth of the
+// vocabulary; the row's logits are re-read from L2 by each pass, and the
+// CTAs' partial results (max, exp sums, radix histograms, candidates) meet in
+// distributed shared memory at cluster barriers.
 //
 // Canonical rule (restated by oracle/rec_oracle.c:orc_sample):
 //   x_i   = float(logit_i); for ids in the row's history: x = x<0 ? x*rho : x/rho
@@ -8,8 +11,10 @@
 //           (alpha != 0; the reference's presence mask, masked_sampling.py:99-100);
 //           -0 is canonicalised to +0.
 //   T = 0 : argmax x, lowest index among equal maxima (engine.py:284-285).
-//   lse   = M + log(S), M = max x, S = sum exp(x - M): thread t sums i = t,
-//           t+1024, ... in order, then a warp butterfly, then the 32 warp sums in
+//   lse   = M + log(S), M = max x, S = sum exp(x - M) in this order: the ids
+//           are cut into 8 chunks of Q = ceil(V / 8192) * 1024; in chunk c,
+//           thread t sums ids cQ + t, cQ + t + 1024, ... in order, then a warp
+//           butterfly, then the 32 warp sums in order; S = the 8 chunk sums in
 //           order.  lp_i = x_i - lse.
 //   (T, top_p, top_k) = (1, 1, 0): id = argmax(x_i + g_i)      (sampling.py:48-52)
 //   top_k = 0 (top_p = 1): id = argmax(lp_i * (1/T) + g_i)     (mlx-lm categorical)
@@ -93,12 +98,22 @@ __device__ __forceinline__ uint32_t float_key(float x) {
 
 __device__ __forceinline__ float gumbel(float u) { return -rlog(-rlog(u)); }
 
+// Cluster of kSampleCluster CTAs per row; CTA r owns the ids
+// [r Q, (r + 1) Q) with Q = ceil(V / (kSampleCluster * 1024)) * 1024, and
+// thread t of it the ids r Q + t + 1024 j.  Partial results meet through
+// distributed shared memory at cluster barriers (no global scratch).
+constexpr int kSampleCluster = 8;
+constexpr int kSampleChunkWords = kSampleMaxVocab / kSampleCluster / 32;  // history bitmap words per CTA
+
 struct SampleSmem {
   float red_v[32];
   int red_i[32];
   unsigned hist[256];
-  float cx[kSampleMaxCand];
+  unsigned seen[kSampleChunkWords];  // history bitmap of this CTA's ids
+  float cx[kSampleMaxCand];          // this CTA's candidates
   int ci[kSampleMaxCand];
+  float gx[kSampleMaxCand];          // all candidates (CTA 0)
+  int gi[kSampleMaxCand];
   float sx[kSampleMaxCand];
   int si[kSampleMaxCand];
   float sp[kSampleMaxCand];
@@ -109,7 +124,29 @@ struct SampleSmem {
   float lse;
   float M;
   int Mi;
+  // published to the cluster (read by the other CTAs after a cluster barrier)
+  float pub_v[2];
+  int pub_i[2];
+  unsigned pub_hist[2][256];
+  float pub_S;
+  int pub_n;
 };
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of `p` (this CTA's shared memory) in the shared memory of cluster CTA `rank`.
+template <class T>
+__device__ __forceinline__ const T* peer(const T* p, int rank) {
+  uint64_t out;
+  asm volatile("mapa.u64 %0, %1, %2;" : "=l"(out) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
+  return reinterpret_cast<const T*>(out);
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
 
 // Block-wide argmax (value desc, index asc) of one value per thread; all
 // threads return the result.
@@ -137,29 +174,49 @@ __device__ __forceinline__ void block_argmax(float& v, int& i, SampleSmem& s) {
   __syncthreads();
 }
 
-static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const SampleArgs a) {
-  extern __shared__ uint32_t seen[];  // history bitmap [ceil(V/32)]
+// (value desc, index asc) arg-max over the cluster's published pub_v[k],
+// pub_i[k] (after a cluster barrier); thread 0 writes s.M / s.Mi.
+__device__ __forceinline__ void cluster_argmax(SampleSmem& s, int k) {
+  if (threadIdx.x == 0) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int r = 0; r < kSampleCluster; ++r) {
+      const float v = *peer(&s.pub_v[k], r);
+      const int i = *peer(&s.pub_i[k], r);
+      if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    }
+    s.M = bv;
+    s.Mi = bi;
+  }
+  __syncthreads();
+}
+
+static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSampleThreads, 1)
+    k_sample(const SampleArgs a) {
   __shared__ SampleSmem s;
-  const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int crank = int(cluster_rank());
+  const int b = blockIdx.x / kSampleCluster, t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int V = a.V;
+  const int Q = (V + kSampleCluster * kSampleThreads - 1) / (kSampleCluster * kSampleThreads) * kSampleThreads;
+  const int lo = min(V, crank * Q), hi = min(V, lo + Q);
   const uint16_t* lg = a.logits + size_t(b) * a.stride;
   const bool pen = a.rep != 1.0f || a.presence != 0.0f;
   const int n_hist = a.hist_len ? *a.hist_len : a.n_hist;
-  const int nw = (V + 31) >> 5;
   const uint32_t* allow = a.allow ? a.allow + size_t(b) * a.allow_stride : nullptr;
+  const bool lead = crank == 0;
   if (pen) {
-    for (int i = t; i < nw; i += kSampleThreads) seen[i] = 0u;
+    for (int i = t; i < kSampleChunkWords; i += kSampleThreads) s.seen[i] = 0u;
     __syncthreads();
     for (int i = t; i < n_hist; i += kSampleThreads) {
       const int id = a.history[size_t(b) * n_hist + i];
-      if (id >= 0 && id < V) atomicOr(&seen[id >> 5], 1u << (id & 31));
+      if (id >= lo && id < hi) atomicOr(&s.seen[(id - lo) >> 5], 1u << ((id - lo) & 31));
     }
     __syncthreads();
   }
   auto X = [&](int i) -> float {
     if (allow && !((allow[i >> 5] >> (i & 31)) & 1u)) return -INFINITY;  // grammar: not allowed
     float x = bf(lg[i]);
-    if (pen && ((seen[i >> 5] >> (i & 31)) & 1u)) {
+    if (pen && ((s.seen[(i - lo) >> 5] >> ((i - lo) & 31)) & 1u)) {
       if (a.rep != 1.0f) x = x < 0.0f ? __fmul_rn(x, a.rep) : __fdiv_rn(x, a.rep);
       if (a.presence != 0.0f) x = __fsub_rn(x, a.presence);
     }
@@ -169,19 +226,32 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
   int top_k = a.top_k;
   if (allow) {
     int c = 0;
-    for (int w = t; w < nw; w += kSampleThreads) {
+    for (int w = (lo >> 5) + t; w < ((hi + 31) >> 5); w += kSampleThreads) {
       uint32_t m = allow[w];
-      if (w == nw - 1 && (V & 31)) m &= (1u << (V & 31)) - 1u;
+      const int w0 = w << 5;
+      if (w0 < lo) m &= ~0u << (lo - w0);
+      if (w0 + 32 > hi) m &= (hi - w0 >= 32) ? ~0u : ((1u << (hi - w0)) - 1u);
       c += __popc(m);
     }
     c = __reduce_add_sync(0xffffffffu, c);
     if (lane == 0) s.red_i[warp] = c;
     __syncthreads();
-    int n_allowed = 0;
-    for (int w = 0; w < kSampleThreads / 32; ++w) n_allowed += s.red_i[w];
+    if (t == 0) {
+      int n = 0;
+      for (int w = 0; w < kSampleThreads / 32; ++w) n += s.red_i[w];
+      s.pub_n = n;
+    }
+    cluster_sync_all();
+    if (t == 0) {
+      int n = 0;
+      for (int r = 0; r < kSampleCluster; ++r) n += *peer(&s.pub_n, r);
+      s.n_cand = n;
+    }
     __syncthreads();
+    const int n_allowed = s.n_cand;
+    cluster_sync_all();  // every CTA has read pub_n
     if (n_allowed == 0) {
-      if (t == 0) sample_finish(a, b, -1);
+      if (lead && t == 0) sample_finish(a, b, -1);
       return;
     }
     top_k = top_k < n_allowed ? top_k : n_allowed;
@@ -195,17 +265,36 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
   }
   float mx = -INFINITY;
   int mi = 0x7fffffff;
-  for (int i = t; i < V; i += kSampleThreads) {
+  for (int i = lo + t; i < hi; i += kSampleThreads) {
     const float x = X(i);
     if (x > mx) { mx = x; mi = i; }
     if (filtered) atomicAdd(&s.hist[float_key(x) >> 24], 1u);
   }
   block_argmax(mx, mi, s);
+  if (t == 0) {
+    s.pub_v[0] = mx;
+    s.pub_i[0] = mi;
+  }
+  if (filtered)
+    for (int i = t; i < 256; i += kSampleThreads) s.pub_hist[0][i] = s.hist[i];
+  cluster_sync_all();
+  cluster_argmax(s, 0);
+  // cluster-wide histogram of a level from pub_hist[p]
+  auto gather_hist = [&](int p) {
+    for (int i = t; i < 256; i += kSampleThreads) {
+      unsigned c = 0;
+      for (int r = 0; r < kSampleCluster; ++r) c += *peer(&s.pub_hist[p][i], r);
+      s.hist[i] = c;
+    }
+    __syncthreads();
+  };
+  if (filtered) gather_hist(0);
+  const float M = s.M;
   if (a.temperature == 0.0f) {  // no finite candidate (all masked or -inf): -1
-    if (t == 0) sample_finish(a, b, mi == 0x7fffffff ? -1 : mi);
+    if (lead && t == 0) sample_finish(a, b, s.Mi == 0x7fffffff ? -1 : s.Mi);
+    cluster_sync_all();  // the peers' published values stay readable until every CTA is done
     return;
   }
-  const float M = mx;
 
   // radix select of the k-th largest key: resolve one digit from s.hist
   auto resolve = [&](int level) {
@@ -225,12 +314,12 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
     }
     __syncthreads();
   };
-  auto histogram = [&](int level) {  // elements matching the prefix of levels < level
+  auto local_hist = [&](int level) {  // this CTA's elements matching the prefix of levels < level
     for (int i = t; i < 256; i += kSampleThreads) s.hist[i] = 0u;
     __syncthreads();
     const uint32_t pre = s.prefix, msk = s.mask;
     const int shift = 24 - 8 * level;
-    for (int i = t; i < V; i += kSampleThreads) {
+    for (int i = lo + t; i < hi; i += kSampleThreads) {
       const uint32_t k = float_key(X(i));
       if ((k & msk) == pre) atomicAdd(&s.hist[(k >> shift) & 255u], 1u);
     }
@@ -238,19 +327,33 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
   };
   if (filtered) resolve(0);
 
-  // ---- pass 2: log-sum-exp (canonical order) [+ next digit]
+  // ---- pass 2: this CTA's share of S (canonical order) [+ next digit]
   {
     float sum = 0.0f;
-    for (int i = t; i < V; i += kSampleThreads) sum = __fadd_rn(sum, rexp(__fsub_rn(X(i), M)));
+    for (int i = lo + t; i < hi; i += kSampleThreads) sum = __fadd_rn(sum, rexp(__fsub_rn(X(i), M)));
     sum = bfly_sum(sum);
     if (lane == 0) s.red_v[warp] = sum;
     __syncthreads();
     if (t == 0) {
       float tot = 0.0f;
       for (int w = 0; w < 32; ++w) tot = __fadd_rn(tot, s.red_v[w]);
+      s.pub_S = tot;
+    }
+    if (filtered) {
+      local_hist(1);
+      for (int i = t; i < 256; i += kSampleThreads) s.pub_hist[1][i] = s.hist[i];
+    }
+    cluster_sync_all();
+    if (t == 0) {
+      float tot = 0.0f;  // S = the CTAs' shares in cluster order
+      for (int r = 0; r < kSampleCluster; ++r) tot = __fadd_rn(tot, *peer(&s.pub_S, r));
       s.lse = __fadd_rn(M, rlog(tot));
     }
     __syncthreads();
+    if (filtered) {
+      gather_hist(1);
+      resolve(1);
+    }
   }
   const float lse = s.lse;
   const float inv_t = __fdiv_rn(1.0f, a.temperature);
@@ -260,31 +363,42 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
     const bool t1 = a.temperature == 1.0f && a.top_p >= 1.0f;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = t; i < V; i += kSampleThreads) {
+    for (int i = lo + t; i < hi; i += kSampleThreads) {
       const float x = X(i);
       const float z = t1 ? __fadd_rn(x, gumbel(u[i])) : __fadd_rn(__fmul_rn(__fsub_rn(x, lse), inv_t), gumbel(u[i]));
       if (z > bv) { bv = z; bi = i; }
     }
     block_argmax(bv, bi, s);
-    if (t == 0) sample_finish(a, b, bi == 0x7fffffff ? -1 : bi);
+    if (t == 0) {
+      s.pub_v[1] = bv;
+      s.pub_i[1] = bi;
+    }
+    cluster_sync_all();
+    cluster_argmax(s, 1);
+    if (lead && t == 0) sample_finish(a, b, s.Mi == 0x7fffffff ? -1 : s.Mi);
+    cluster_sync_all();
     return;
   }
 
-  for (int level = 1; level < 4; ++level) {
-    histogram(level);
+  for (int level = 2; level < 4; ++level) {
+    local_hist(level);
+    for (int i = t; i < 256; i += kSampleThreads) s.pub_hist[level & 1][i] = s.hist[i];
+    cluster_sync_all();
+    gather_hist(level & 1);
     resolve(level);
   }
   const uint32_t theta = s.prefix;
   const int greater = top_k - 1 - s.rank;
   const int n = greater + s.tied;
   if (n > kSampleMaxCand) {
-    if (t == 0) sample_finish(a, b, -1);
+    if (lead && t == 0) sample_finish(a, b, -1);
+    cluster_sync_all();
     return;
   }
-  // ---- collect the elements >= theta
+  // ---- collect this CTA's elements >= theta, then CTA 0 gathers them
   if (t == 0) s.n_cand = 0;
   __syncthreads();
-  for (int i = t; i < V; i += kSampleThreads) {
+  for (int i = lo + t; i < hi; i += kSampleThreads) {
     const float x = X(i);
     if (float_key(x) >= theta) {
       const int slot = atomicAdd(&s.n_cand, 1);
@@ -295,14 +409,32 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
     }
   }
   __syncthreads();
+  if (t == 0) s.pub_n = s.n_cand;
+  cluster_sync_all();
+  if (lead) {
+    // CTA r's candidates go to [off_r, off_r + n_r); the order is irrelevant
+    // (they are ranked by value and index below)
+    int off = 0;
+    for (int r = 0; r < kSampleCluster; ++r) {
+      const int nr = *peer(&s.pub_n, r);
+      for (int q = t; q < nr && off + q < kSampleMaxCand; q += kSampleThreads) {
+        s.gx[off + q] = *peer(&s.cx[q], r);
+        s.gi[off + q] = *peer(&s.ci[q], r);
+      }
+      off += nr;
+    }
+  }
+  cluster_sync_all();  // the other CTAs may exit once CTA 0 has read their candidates
+  if (!lead) return;
+  __syncthreads();
   // descending (x desc, index desc) by rank counting
   if (t < n) {
-    const float xi = s.cx[t];
-    const int ii = s.ci[t];
+    const float xi = s.gx[t];
+    const int ii = s.gi[t];
     int r = 0;
     for (int j = 0; j < n; ++j) {
-      const float xj = s.cx[j];
-      const int ij = s.ci[j];
+      const float xj = s.gx[j];
+      const int ij = s.gi[j];
       r += (xj > xi || (xj == xi && ij > ii)) ? 1 : 0;
     }
     s.sx[r] = xi;
@@ -351,6 +483,12 @@ static __global__ void __launch_bounds__(kSampleThreads, 1) k_sample(const Sampl
     }
     if (lane == 0) sample_finish(a, b, bi == 0x7fffffff ? -1 : bi);
   }
+}
+
+// B rows, one cluster of kSampleCluster CTAs each.
+__host__ inline cudaError_t launch_sample(const SampleArgs& a, int batch, cudaStream_t st) {
+  k_sample<<<batch * kSampleCluster, kSampleThreads, 0, st>>>(a);
+  return cudaGetLastError();
 }
 
 }  // namespace rec
