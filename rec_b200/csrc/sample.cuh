@@ -148,6 +148,13 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   return r;
 }
 
+// Histogram increment aggregated over the warp's lanes with the same bucket
+// (the top digits of nearby logits collide heavily).
+__device__ __forceinline__ void hist_add(unsigned* h, unsigned bucket) {
+  const unsigned grp = __match_any_sync(__activemask(), bucket);
+  if (int(threadIdx.x & 31) == __ffs(grp) - 1) atomicAdd(&h[bucket], unsigned(__popc(grp)));
+}
+
 // Block-wide argmax (value desc, index asc) of one value per thread; all
 // threads return the result.
 __device__ __forceinline__ void block_argmax(float& v, int& i, SampleSmem& s) {
@@ -194,6 +201,7 @@ __device__ __forceinline__ void cluster_argmax(SampleSmem& s, int k) {
 static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSampleThreads, 1)
     k_sample(const SampleArgs a) {
   __shared__ SampleSmem s;
+  extern __shared__ float xs[];  // x of this CTA's ids (pass 1 fills it; later passes read it)
   const int crank = int(cluster_rank());
   const int b = blockIdx.x / kSampleCluster, t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int V = a.V;
@@ -265,10 +273,12 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
   }
   float mx = -INFINITY;
   int mi = 0x7fffffff;
+#pragma unroll 4
   for (int i = lo + t; i < hi; i += kSampleThreads) {
     const float x = X(i);
+    xs[i - lo] = x;
     if (x > mx) { mx = x; mi = i; }
-    if (filtered) atomicAdd(&s.hist[float_key(x) >> 24], 1u);
+    if (filtered) hist_add(s.hist, float_key(x) >> 24);
   }
   block_argmax(mx, mi, s);
   if (t == 0) {
@@ -319,9 +329,9 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
     __syncthreads();
     const uint32_t pre = s.prefix, msk = s.mask;
     const int shift = 24 - 8 * level;
-    for (int i = lo + t; i < hi; i += kSampleThreads) {
-      const uint32_t k = float_key(X(i));
-      if ((k & msk) == pre) atomicAdd(&s.hist[(k >> shift) & 255u], 1u);
+    for (int i = t; i < hi - lo; i += kSampleThreads) {
+      const uint32_t k = float_key(xs[i]);
+      if ((k & msk) == pre) hist_add(s.hist, (k >> shift) & 255u);
     }
     __syncthreads();
   };
@@ -330,7 +340,7 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
   // ---- pass 2: this CTA's share of S (canonical order) [+ next digit]
   {
     float sum = 0.0f;
-    for (int i = lo + t; i < hi; i += kSampleThreads) sum = __fadd_rn(sum, rexp(__fsub_rn(X(i), M)));
+    for (int i = t; i < hi - lo; i += kSampleThreads) sum = __fadd_rn(sum, rexp(__fsub_rn(xs[i], M)));
     sum = bfly_sum(sum);
     if (lane == 0) s.red_v[warp] = sum;
     __syncthreads();
@@ -363,8 +373,9 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
     const bool t1 = a.temperature == 1.0f && a.top_p >= 1.0f;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
+#pragma unroll 4
     for (int i = lo + t; i < hi; i += kSampleThreads) {
-      const float x = X(i);
+      const float x = xs[i - lo];
       const float z = t1 ? __fadd_rn(x, gumbel(u[i])) : __fadd_rn(__fmul_rn(__fsub_rn(x, lse), inv_t), gumbel(u[i]));
       if (z > bv) { bv = z; bi = i; }
     }
@@ -399,7 +410,7 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
   if (t == 0) s.n_cand = 0;
   __syncthreads();
   for (int i = lo + t; i < hi; i += kSampleThreads) {
-    const float x = X(i);
+    const float x = xs[i - lo];
     if (float_key(x) >= theta) {
       const int slot = atomicAdd(&s.n_cand, 1);
       if (slot < kSampleMaxCand) {
@@ -487,7 +498,11 @@ static __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(
 
 // B rows, one cluster of kSampleCluster CTAs each.
 __host__ inline cudaError_t launch_sample(const SampleArgs& a, int batch, cudaStream_t st) {
-  k_sample<<<batch * kSampleCluster, kSampleThreads, 0, st>>>(a);
+  const int Q = (a.V + kSampleCluster * kSampleThreads - 1) / (kSampleCluster * kSampleThreads) * kSampleThreads;
+  const size_t dyn = size_t(Q) * sizeof(float);
+  cudaError_t e = cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, int(dyn));
+  if (e != cudaSuccess) return e;
+  k_sample<<<batch * kSampleCluster, kSampleThreads, dyn, st>>>(a);
   return cudaGetLastError();
 }
 
