@@ -596,6 +596,49 @@ def run_prefill(args):
             tf = 2.0 * T * N * K / us / 1e6
             rows.append({"tokens": T, "gemm": name, "N": N, "K": K, "us": round(us, 2), "TFLOPs": round(tf, 1),
                          "frac": round(tf / peak, 4)})
+        # the MoE block of the chunk: 128 experts, top-8, grouped GEMMs (rec_prefill_moe)
+        E, k, H, I = 128, 8, 2048, 768
+        g = torch.Generator(device="cuda").manual_seed(T)
+
+        def qm(rows_, cols):
+            w = torch.randint(-2**31, 2**31 - 1, (rows_, cols // 8), generator=g, device="cuda", dtype=torch.int32)
+            sc = (torch.rand(rows_, cols // 64, generator=g, device="cuda") * 0.01).to(torch.float16)
+            bi = (torch.rand(rows_, cols // 64, generator=g, device="cuda") - 0.5).mul(0.1).to(torch.float16)
+            return (w, sc, bi), abi.RecQMat(w.data_ptr(), sc.data_ptr(), bi.data_ptr())
+
+        (gt, gm), (ut, um), (dt, dm) = qm(E * I, H), qm(E * I, H), qm(E * H, I)
+        x = torch.randn(T, H, generator=g, device="cuda").to(torch.bfloat16)
+        ids = torch.argsort(torch.rand(T, E, generator=g, device="cuda"), dim=1)[:, :k].to(torch.int32).contiguous()
+        wts = torch.rand(T, k, generator=g, device="cuda")
+        wts = (wts / wts.sum(dim=1, keepdim=True)).contiguous()
+        y = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        nb = lib().rec_prefill_moe_workspace_bytes(T, k, H, I, E)
+        ws = torch.empty(nb + 256, dtype=torch.uint8, device="cuda")
+        base = (ws.data_ptr() + 255) // 256 * 256
+
+        def moe():
+            check(lib().rec_prefill_moe(C.byref(gm), C.byref(um), C.byref(dm), abi.REC_SCALE_FP16, E, I, H,
+                                        C.c_void_p(x.data_ptr()), T, k, C.c_void_p(ids.data_ptr()),
+                                        C.c_void_p(wts.data_ptr()), None, C.c_void_p(y.data_ptr()), C.c_void_p(base),
+                                        nb, C.c_void_p(status.data_ptr()), stream), "rec_prefill_moe")
+
+        for _ in range(max(3, args.warmup)):
+            moe()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            moe()
+        b.record()
+        torch.cuda.synchronize()
+        if int(status.item()) != 0:
+            raise RuntimeError(f"prefill MoE reported device status {int(status.item())}")
+        us = a.elapsed_time(b) / args.steps * 1e3
+        tf = 2.0 * T * k * 3 * I * H / us / 1e6
+        rows.append({"tokens": T, "gemm": "moe_block_grouped (E 128, top-8, gate+up+down, gather, SwiGLU, mix)",
+                     "us": round(us, 2), "TFLOPs": round(tf, 1), "frac": round(tf / peak, 4)})
+        del gt, ut, dt, ws
     print(json.dumps({"workload": "prefill_projections_tcgen05", "peak_TFLOPs": peak, "peak_source": kind,
                       "steps": args.steps, "dtype": "bf16 x bf16 -> fp32 (int4 g64 weights dequantized in smem)",
                       "rows": rows}), flush=True)

@@ -325,6 +325,31 @@ REC_API int rec_lmhead_sample(const RecQMat* lm_head, int32_t scale_dtype, int32
  * (engine/src/rec_mlx/quantized.py:102-148, kernels/m4_max_prefill.py:49-144). */
 REC_API int rec_prefill_gemm(const RecQMat* w, int32_t scale_dtype, int64_t n, int32_t k, const void* x_dev,
                              int64_t t, void* y_dev, int32_t* status_dev, void* stream);
+/* Workspace (bytes) of rec_prefill_moe for t tokens, k experts per token, the
+ * hidden and expert-intermediate sizes and the expert count; 0 for bad sizes. */
+REC_API size_t rec_prefill_moe_workspace_bytes(int64_t t, int32_t k, int32_t hidden, int32_t inter,
+                                               int32_t n_experts);
+/* MoE block of a prefill chunk on the tensor cores.  x bf16 [t, hidden]: the
+ * post-attention RMSNorm of the tokens; ids int32 [t, k] and weights fp32
+ * [t, k]: each token's experts in rank order and their renormalised weights
+ * (the router's output); gate, up int4 g64 [n_experts * inter, hidden] and
+ * down [n_experts * hidden, inter] (the layer's stacked expert matrices).
+ * The (token, rank) pairs are grouped by expert and each expert's rows go
+ * through one grouped tcgen05 GEMM per matrix (rec_prefill_gemm's kernel,
+ * one 128-row tile table for all experts); act = bf16(bf16(g * bf16(
+ * sigmoid(g))) * u); y[t] = resid[t] + the pairs' d * bf16(w) summed in rank
+ * order with a bf16 rounding after each add (resid may be null: y = the
+ * mix).  hidden and inter multiples of 256.  workspace: 256-byte aligned,
+ * rec_prefill_moe_workspace_bytes of it; *status_dev is set when a bounded
+ * wait runs out or an expert id is outside [0, n_experts) (that pair is
+ * skipped).  Replaces the grouped expert GEMMs of the reference's prefill
+ * (engine/src/rec_mlx/m4_max_prefill.py:27-46 PrefillSwitchGLU,
+ * kernels/m4_max_prefill.py:111-144 gate_up) and the SwitchGLU of
+ * model.py:242-254 over the prompt's tokens. */
+REC_API int rec_prefill_moe(const RecQMat* gate, const RecQMat* up, const RecQMat* down, int32_t scale_dtype,
+                            int32_t n_experts, int32_t inter, int32_t hidden, const void* x_dev, int64_t t,
+                            int32_t k, const int32_t* ids_dev, const float* weights_dev, const void* resid_dev,
+                            void* y_dev, void* workspace, size_t workspace_bytes, int32_t* status_dev, void* stream);
 /* Decode attention of one layer alone (unit tests, the attention sweep):
  * quantizes the new K / V of `*position_dev` from qkv_dev (bf16 [Hq*128 |
  * Hkv*128 | Hkv*128], RoPE from rope_dev [positions][cos 64 | sin 64]) into

@@ -32,6 +32,11 @@ _SIGNATURES = {
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "rec_prefill_gemm": (C.c_int, [C.POINTER(abi.RecQMat), C.c_int32, C.c_int64, C.c_int32, C.c_void_p, C.c_int64,
                                    C.c_void_p, C.c_void_p, C.c_void_p]),
+    "rec_prefill_moe_workspace_bytes": (C.c_size_t, [C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
+    "rec_prefill_moe": (C.c_int, [C.POINTER(abi.RecQMat), C.POINTER(abi.RecQMat), C.POINTER(abi.RecQMat), C.c_int32,
+                                  C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_int64, C.c_int32, C.c_void_p,
+                                  C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p,
+                                  C.c_void_p]),
     "rec_decode_sampled": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.POINTER(abi.RecSampling),
                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_int32,
                                      C.c_void_p, C.c_void_p, C.c_void_p]),

@@ -99,15 +99,28 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// tiles (grouped mode, one matrix per expert): tile blockIdx.y is rows
+// [row0, row0 + rows) of X and Y multiplied by expert e's W (rows e N ..);
+// {e, row0, rows, 0}, rows 0 = no tile.  tiles null: dense, tile blockIdx.y =
+// rows 128 blockIdx.y .. of X.
 template <int SD>
 __global__ void __launch_bounds__(kPThreads, 1)
     k_prefill_gemm(const __grid_constant__ CUtensorMap xmap, const QMatDev w, int K, int N, int T,
-                   uint16_t* __restrict__ y, int* status) {
+                   uint16_t* __restrict__ y, int* status, const int4* __restrict__ tiles) {
   extern __shared__ uint8_t smem_raw[];
   PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                     ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * kPBN, m0 = blockIdx.y * kPBM;
+  const int n0 = blockIdx.x * kPBN;
+  int m0 = blockIdx.y * kPBM, mrows = kPBM;
+  size_t wrow0 = 0;
+  if (tiles) {
+    const int4 tl = tiles[blockIdx.y];
+    if (tl.z <= 0) return;  // the whole CTA, before any barrier or tensor memory
+    m0 = tl.y;
+    mrows = tl.z;
+    wrow0 = size_t(tl.x) * N;
+  }
   const int KT = K / kPBK;
   if (tid == 0) {
     for (int s = 0; s < kPStages; ++s) {
@@ -137,7 +150,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
   auto fetch = [&](int kt) {
 #pragma unroll
     for (int rr = 0; rr < RPT; ++rr) {
-      const size_t row = size_t(n0 + tid + rr * kPThreads);
+      const size_t row = wrow0 + size_t(n0 + tid + rr * kPThreads);
       const uint4* src = reinterpret_cast<const uint4*>(w.w + row * (K / 8) + size_t(kt) * 8);
       nc[rr][0] = ldg128_nc(src);
       nc[rr][1] = ldg128_nc(src + 1);
@@ -219,7 +232,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     for (int c = half * (kPBN / 64); c < (half + 1) * (kPBN / 64); ++c) {
       uint32_t r[32];
       tmem_ld32(tmem + (uint32_t(quarter * 32) << 16) + uint32_t(c * 32), r);
-      if (row < T) {
+      if (row < T && quarter * 32 + lane < mrows) {
         uint4* dst = reinterpret_cast<uint4*>(y + size_t(row) * N + n0 + c * 32);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -244,6 +257,10 @@ using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, 
                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+bool valid_qmat3(const RecQMat& m) {
+  return m.w && m.scales && m.biases && aligned16(m.w) && aligned16(m.scales) && aligned16(m.biases);
+}
+
 EncodeTiled encode_fn() {
   static EncodeTiled fn = nullptr;
   if (!fn) {
@@ -258,19 +275,212 @@ EncodeTiled encode_fn() {
 
 template <int SD>
 cudaError_t launch_prefill(const CUtensorMap& map, const QMatDev& w, int K, int N, int T, uint16_t* y, int* status,
-                           cudaStream_t st) {
+                           cudaStream_t st, const int4* tiles = nullptr, int n_tiles = 0) {
   const size_t smem = sizeof(PrefillSmem) + 1024;
   cudaError_t e = cudaFuncSetAttribute(k_prefill_gemm<SD>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   if (e != cudaSuccess) return e;
-  dim3 grid(N / kPBN, (T + kPBM - 1) / kPBM);
-  k_prefill_gemm<SD><<<grid, kPThreads, smem, st>>>(map, w, K, N, T, y, status);
+  dim3 grid(N / kPBN, tiles ? n_tiles : (T + kPBM - 1) / kPBM);
+  k_prefill_gemm<SD><<<grid, kPThreads, smem, st>>>(map, w, K, N, T, y, status, tiles);
   return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// MoE block of a prefill chunk: the (token, rank) pairs of the routing are
+// grouped by expert, each expert's rows multiply its gate / up / down
+// matrices in one grouped GEMM launch each, and the expert outputs are mixed
+// per token in rank order (the decode path's bf16 rounding points).
+// ---------------------------------------------------------------------------
+constexpr int kMoeThreads = 256;
+
+__global__ void k_moe_count(const int* __restrict__ ids, int n_pairs, int E, int* counts, int* status) {
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < n_pairs; p += gridDim.x * blockDim.x) {
+    const int e = ids[p];
+    if (e < 0 || e >= E) {
+      report(status, kStatusBadToken);
+      continue;
+    }
+    atomicAdd(&counts[e], 1);
+  }
+}
+
+// Offsets of the experts' row groups, the grouped GEMMs' tile table (rows
+// 128 at a time inside each group; unused entries have 0 rows) and zeroed
+// cursors.  One thread: E and the tile count are small.
+__global__ void k_moe_plan(const int* __restrict__ counts, int E, int* off, int* cursor, int4* tiles,
+                           int n_tiles_max) {
+  if (threadIdx.x != 0) return;
+  int o = 0, ti = 0;
+  for (int e = 0; e < E; ++e) {
+    const int n = counts[e];
+    off[e] = o;
+    cursor[e] = 0;
+    for (int m = 0; m < n && ti < n_tiles_max; m += kPBM) tiles[ti++] = make_int4(e, o + m, min(kPBM, n - m), 0);
+    o += n;
+  }
+  for (; ti < n_tiles_max; ++ti) tiles[ti] = make_int4(0, 0, 0, 0);
+}
+
+// One warp per pair (t, r): its slot in expert e's group (the order inside a
+// group does not change any result) and the copy of x row t there.
+__global__ void k_moe_gather(const int* __restrict__ ids, int n_pairs, int k, int E, const uint16_t* __restrict__ x,
+                             int H, const int* __restrict__ off, int* cursor, int* pos, uint16_t* __restrict__ xg) {
+  const int lane = threadIdx.x & 31;
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  for (int p = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < n_pairs; p += nw) {
+    const int e = ids[p];
+    int slot = -1;
+    if (lane == 0 && e >= 0 && e < E) slot = off[e] + atomicAdd(&cursor[e], 1);
+    slot = __shfl_sync(0xffffffffu, slot, 0);
+    if (lane == 0) pos[p] = slot;
+    if (slot < 0) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(x + size_t(p / k) * H);
+    uint4* dst = reinterpret_cast<uint4*>(xg + size_t(slot) * H);
+    for (int i = lane; i < H / 8; i += 32) dst[i] = ldg128(src + i);
+  }
+}
+
+// act = bf16(bf16(g * bf16(sigmoid(g))) * u), in place over g (as the decode
+// path's gate/up epilogue).
+__global__ void k_moe_swiglu(uint16_t* __restrict__ g, const uint16_t* __restrict__ u, size_t n) {
+  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+    const float gg = bf(g[i]), uu = bf(u[i]);
+    g[i] = to_bf(__fmul_rn(rbf(__fmul_rn(gg, rbf(rsigmoid(gg)))), uu));
+  }
+}
+
+// y[t] = (resid[t] +) the pairs' outputs d * bf16(w) summed in rank order
+// with a bf16 rounding after each add (the decode path's mix).
+__global__ void k_moe_mix(const uint16_t* __restrict__ d, const int* __restrict__ pos, const float* __restrict__ wts,
+                          int T, int k, int H, const uint16_t* __restrict__ resid, uint16_t* __restrict__ y) {
+  const size_t n = size_t(T) * H;
+  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+    const int t = int(i / H), h = int(i % H);
+    float mix = 0.0f;
+    bool first = true;
+    for (int r = 0; r < k; ++r) {
+      const int slot = pos[size_t(t) * k + r];
+      if (slot < 0) continue;
+      const float term = __fadd_rn(rbf(__fmul_rn(bf(d[size_t(slot) * H + h]), rbf(wts[size_t(t) * k + r]))), 0.0f);
+      mix = first ? term : rbf(__fadd_rn(term, mix));
+      first = false;
+    }
+    y[i] = resid ? to_bf(__fadd_rn(bf(resid[i]), mix)) : to_bf(mix);
+  }
+}
+
+struct MoeLayout {
+  size_t counts, cursor, off, tiles, pos, xg, g, u, d, total;
+  int n_tiles_max;
+};
+MoeLayout moe_layout(int64_t T, int k, int H, int I, int E) {
+  MoeLayout L;
+  const int64_t P = T * k;
+  L.n_tiles_max = int((P + kPBM - 1) / kPBM) + E;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = (o + bytes + 255) / 256 * 256;
+    return at;
+  };
+  L.counts = take(size_t(E) * 4);
+  L.cursor = take(size_t(E) * 4);
+  L.off = take(size_t(E) * 4);
+  L.tiles = take(size_t(L.n_tiles_max) * 16);
+  L.pos = take(size_t(P) * 4);
+  L.xg = take(size_t(P) * H * 2);
+  L.g = take(size_t(P) * I * 2);
+  L.u = take(size_t(P) * I * 2);
+  L.d = take(size_t(P) * H * 2);
+  L.total = o;
+  return L;
+}
+
+int encode_rows(CUtensorMap* map, const void* base, int64_t rows, int cols) {
+  EncodeTiled enc = encode_fn();
+  if (!enc) return -1;
+  const cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(cols) * 2};
+  const cuuint32_t box[2] = {kPBK, kPBM};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? 0
+             : -1;
 }
 
 }  // namespace
 }  // namespace rec
 
 using namespace rec;
+
+REC_API size_t rec_prefill_moe_workspace_bytes(int64_t t, int32_t k, int32_t hidden, int32_t inter,
+                                               int32_t n_experts) {
+  if (t <= 0 || k <= 0 || hidden <= 0 || inter <= 0 || n_experts <= 0) return 0;
+  return moe_layout(t, k, hidden, inter, n_experts).total;
+}
+
+REC_API int rec_prefill_moe(const RecQMat* gate, const RecQMat* up, const RecQMat* down, int32_t scale_dtype,
+                            int32_t n_experts, int32_t inter, int32_t hidden, const void* x_dev, int64_t t,
+                            int32_t k, const int32_t* ids_dev, const float* weights_dev, const void* resid_dev,
+                            void* y_dev, void* workspace, size_t workspace_bytes, int32_t* status_dev, void* stream) {
+  REC_CHECK_ARG(gate && up && down && x_dev && ids_dev && weights_dev && y_dev && workspace && status_dev,
+                "rec_prefill_moe: null pointer");
+  REC_CHECK_ARG(valid_qmat3(*gate) && valid_qmat3(*up) && valid_qmat3(*down),
+                "rec_prefill_moe: expert matrices must be non-null and 16-byte aligned");
+  REC_CHECK_ARG(scale_dtype == REC_SCALE_FP16 || scale_dtype == REC_SCALE_BF16, "bad scale dtype");
+  REC_CHECK_ARG(n_experts > 0 && n_experts <= 4096, "rec_prefill_moe: n_experts %d outside 1..4096", n_experts);
+  REC_CHECK_ARG(k >= 1 && k <= 16 && k <= n_experts, "rec_prefill_moe: k %d outside 1..min(16, n_experts)", k);
+  REC_CHECK_ARG(hidden % kPBN == 0 && inter % kPBN == 0,
+                "rec_prefill_moe: hidden %d and inter %d must be multiples of %d", hidden, inter, kPBN);
+  REC_CHECK_ARG(t > 0 && t * k < (1ll << 31), "rec_prefill_moe: bad token count");
+  REC_CHECK_ARG(aligned16(x_dev) && aligned16(y_dev) && (!resid_dev || aligned16(resid_dev)) &&
+                    (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
+                "rec_prefill_moe: x, y, resid 16-byte and workspace 256-byte aligned");
+  const MoeLayout L = moe_layout(t, k, hidden, inter, n_experts);
+  REC_CHECK_ARG(workspace_bytes >= L.total, "rec_prefill_moe: workspace %zu < %zu bytes", workspace_bytes, L.total);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* counts = reinterpret_cast<int*>(ws + L.counts);
+  int* cursor = reinterpret_cast<int*>(ws + L.cursor);
+  int* off = reinterpret_cast<int*>(ws + L.off);
+  int4* tiles = reinterpret_cast<int4*>(ws + L.tiles);
+  int* pos = reinterpret_cast<int*>(ws + L.pos);
+  uint16_t* xg = reinterpret_cast<uint16_t*>(ws + L.xg);
+  uint16_t* g = reinterpret_cast<uint16_t*>(ws + L.g);
+  uint16_t* u = reinterpret_cast<uint16_t*>(ws + L.u);
+  uint16_t* d = reinterpret_cast<uint16_t*>(ws + L.d);
+  const int P = int(t * k);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CUtensorMap xmap, amap;
+  REC_CHECK_ARG(encode_rows(&xmap, xg, P, hidden) == 0 && encode_rows(&amap, g, P, inter) == 0,
+                "rec_prefill_moe: tensor map encoding failed");
+  const int blocks = 4 * sm_count();
+  REC_CHECK_CUDA(cudaMemsetAsync(counts, 0, size_t(n_experts) * 4, st));
+  k_moe_count<<<blocks, kMoeThreads, 0, st>>>(ids_dev, P, n_experts, counts, status_dev);
+  k_moe_plan<<<1, 32, 0, st>>>(counts, n_experts, off, cursor, tiles, L.n_tiles_max);
+  k_moe_gather<<<blocks, kMoeThreads, 0, st>>>(ids_dev, P, k, n_experts, static_cast<const uint16_t*>(x_dev), hidden,
+                                               off, cursor, pos, xg);
+  REC_CHECK_CUDA(cudaGetLastError());
+  const QMatDev wg = {static_cast<const uint32_t*>(gate->w), static_cast<const uint16_t*>(gate->scales),
+                      static_cast<const uint16_t*>(gate->biases)};
+  const QMatDev wu = {static_cast<const uint32_t*>(up->w), static_cast<const uint16_t*>(up->scales),
+                      static_cast<const uint16_t*>(up->biases)};
+  const QMatDev wd = {static_cast<const uint32_t*>(down->w), static_cast<const uint16_t*>(down->scales),
+                      static_cast<const uint16_t*>(down->biases)};
+  auto gemm = [&](const CUtensorMap& m, const QMatDev& w, int K, int N, uint16_t* out) {
+    return scale_dtype == REC_SCALE_FP16 ? launch_prefill<0>(m, w, K, N, P, out, status_dev, st, tiles, L.n_tiles_max)
+                                         : launch_prefill<1>(m, w, K, N, P, out, status_dev, st, tiles, L.n_tiles_max);
+  };
+  REC_CHECK_CUDA(gemm(xmap, wg, hidden, inter, g));
+  REC_CHECK_CUDA(gemm(xmap, wu, hidden, inter, u));
+  k_moe_swiglu<<<blocks, kMoeThreads, 0, st>>>(g, u, size_t(P) * inter);
+  REC_CHECK_CUDA(cudaGetLastError());
+  REC_CHECK_CUDA(gemm(amap, wd, inter, hidden, d));
+  k_moe_mix<<<blocks, kMoeThreads, 0, st>>>(d, pos, weights_dev, int(t), k, hidden,
+                                            static_cast<const uint16_t*>(resid_dev), static_cast<uint16_t*>(y_dev));
+  REC_CHECK_CUDA(cudaGetLastError());
+  return REC_OK;
+}
 
 REC_API int rec_prefill_gemm(const RecQMat* w, int32_t scale_dtype, int64_t n, int32_t k, const void* x_dev,
                              int64_t t, void* y_dev, int32_t* status_dev, void* stream) {
