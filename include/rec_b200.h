@@ -251,6 +251,14 @@ REC_API int rec_last_error(char* buf, size_t len);
 REC_API int rec_kv_append(const RecKVLayer* kv, int32_t n_kv_heads, int32_t capacity, int32_t kv_bits,
                           const void* k_dev, const void* v_dev, const int32_t* position_dev, int32_t* status_dev,
                           void* stream);
+/* rec_kv_append for a prefill chunk: the t tokens' K and V rows (bf16
+ * [t, n_kv_heads * 128] each, K already RoPE'd) into rows [position,
+ * position + t) of every head, with the same arithmetic per row (the bulk
+ * quantize-on-append of the reference's prefill: update_and_fetch over a
+ * chunk, model.py:45-82).  Rows outside [0, capacity) are an argument
+ * error. */
+REC_API int rec_kv_append_bulk(const RecKVLayer* kv, int32_t n_kv_heads, int32_t capacity, int32_t kv_bits,
+                               const void* k_dev, const void* v_dev, int32_t position, int32_t t, void* stream);
 
 /* ---- kernel entry points used by the unit tests -------------------------- */
 /* y = W x (int4 g64) with an optional fused RMSNorm prologue on x. */

@@ -41,6 +41,8 @@ _SIGNATURES = {
                                      C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_void_p, C.c_int32,
                                      C.c_void_p, C.c_void_p, C.c_void_p]),
     "rec_router_moe": (C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "rec_kv_append_bulk": (C.c_int, [C.POINTER(abi.RecKVLayer), C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
+                                     C.c_void_p, C.c_int32, C.c_int32, C.c_void_p]),
     "rec_kv_append": (C.c_int, [C.POINTER(abi.RecKVLayer), C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                                 C.c_void_p, C.c_void_p, C.c_void_p]),
     "rec_attn_scratch_bytes": (C.c_size_t, [C.c_int32, C.c_int32]),

@@ -64,7 +64,53 @@ __global__ void k_kv_append(const uint16_t* __restrict__ k, const uint16_t* __re
   }
 }
 
+// Bulk form for a prefill chunk: token j of k, v (bf16 [t, hkv * 128]) goes
+// to row p0 + j; one warp per (token, head, K or V, group), the same
+// arithmetic as k_kv_append.
+__global__ void k_kv_append_bulk(const uint16_t* __restrict__ k, const uint16_t* __restrict__ v, RecKVLayer kv,
+                                 int hkv, int capacity, int bits, int p0, int t) {
+  const int lane = threadIdx.x & 31;
+  const long long task = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (task >= (long long)t * hkv * 4) return;
+  const int j = int(task / (hkv * 4)), r = int(task % (hkv * 4));
+  const int g = r >> 2, is_v = (r >> 1) & 1, grp = r & 1;
+  const uint32_t pair =
+      reinterpret_cast<const uint32_t*>((is_v ? v : k) + (size_t(j) * hkv + g) * 128 + 64 * grp)[lane];
+  const float v0 = bf(uint16_t(pair & 0xFFFFu)), v1 = bf(uint16_t(pair >> 16));
+  const QGroupParams qp = warp_group_params(v0, v1, bits);
+  const uint32_t word = warp_pack(quant_code(v0, qp, bits), quant_code(v1, qp, bits), bits);
+  const int gw = 64 * bits / 32, rw = 2 * gw;
+  const size_t slot = size_t(g) * capacity + size_t(p0 + j);
+  uint32_t* codes = static_cast<uint32_t*>(is_v ? kv.v_codes : kv.k_codes);
+  uint16_t* sc = static_cast<uint16_t*>(is_v ? kv.v_scales : kv.k_scales);
+  uint16_t* bi = static_cast<uint16_t*>(is_v ? kv.v_biases : kv.k_biases);
+  if (lane < gw) codes[slot * rw + grp * gw + lane] = word;
+  if (lane == 0) {
+    sc[slot * 2 + grp] = to_bf(qp.scale);
+    bi[slot * 2 + grp] = to_bf(qp.bias);
+  }
+}
+
 }  // namespace
+
+REC_API int rec_kv_append_bulk(const RecKVLayer* kv, int32_t n_kv_heads, int32_t capacity, int32_t kv_bits,
+                               const void* k_dev, const void* v_dev, int32_t position, int32_t t, void* stream) {
+  REC_CHECK_ARG(kv && k_dev && v_dev, "rec_kv_append_bulk: null pointer");
+  REC_CHECK_ARG(n_kv_heads > 0 && capacity > 0, "rec_kv_append_bulk: n_kv_heads and capacity must be positive");
+  REC_CHECK_ARG(kv_bits == 4 || kv_bits == 8, "kv_bits must be 4 or 8");
+  REC_CHECK_ARG(t >= 1 && position >= 0 && int64_t(position) + t <= capacity,
+                "rec_kv_append_bulk: rows [%d, %lld) outside the capacity %d", position,
+                (long long)position + t, capacity);
+  REC_CHECK_ARG(kv->k_codes && kv->k_scales && kv->k_biases && kv->v_codes && kv->v_scales && kv->v_biases &&
+                    aligned16(kv->k_codes) && aligned16(kv->v_codes) && aligned16(k_dev) && aligned16(v_dev),
+                "rec_kv_append_bulk: KV buffers and k/v rows must be non-null and 16-byte aligned");
+  const long long warps = (long long)t * n_kv_heads * 4;
+  k_kv_append_bulk<<<unsigned((warps + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(k_dev), static_cast<const uint16_t*>(v_dev), *kv, n_kv_heads, capacity, kv_bits,
+      position, t);
+  REC_CHECK_CUDA(cudaGetLastError());
+  return REC_OK;
+}
 
 REC_API int rec_kv_append(const RecKVLayer* kv, int32_t n_kv_heads, int32_t capacity, int32_t kv_bits,
                           const void* k_dev, const void* v_dev, const int32_t* position_dev, int32_t* status_dev,

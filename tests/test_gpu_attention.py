@@ -131,3 +131,43 @@ def test_kv_append_matches_oracle(cuda, bits):
     L.orc_kv_store(C.addressof(orec), hkv, cap, bits, pos, k_new.ctypes.data, v_new.ctypes.data)
     for n in lay:
         assert np.array_equal(_host(dev[n], lay[n].dtype), lay[n]), n
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_kv_append_bulk_matches_oracle(cuda, bits):
+    """rec_kv_append_bulk (a prefill chunk's quantize-on-append) against the
+    oracle's per-row append, bit for bit, for 77 rows at an odd start; rows
+    past the capacity are refused before any write."""
+    from rec_b200._lib import check, lib
+
+    hkv, cap, p0, t = 4, 512, 123, 77
+    rng = np.random.default_rng(10 + bits)
+    words = 128 * bits // 32
+    kv = {}
+    for n in ("k", "v"):
+        kv[f"{n}_codes"] = np.zeros((hkv, cap, words), np.uint32)
+        kv[f"{n}_scales"] = np.zeros((hkv, cap, 2), np.uint16)
+        kv[f"{n}_biases"] = np.zeros((hkv, cap, 2), np.uint16)
+    k_new = oracle.f32_to_bf16(3.0 * rng.standard_normal((t, hkv * 128), dtype=np.float32))
+    v_new = oracle.f32_to_bf16(rng.standard_normal((t, hkv * 128), dtype=np.float32))
+    dev = {n: _dev(a) for n, a in kv.items()}
+    rec = abi.RecKVLayer(*(dev[n].data_ptr() for n in ("k_codes", "k_scales", "k_biases", "v_codes", "v_scales",
+                                                      "v_biases")))
+    kd, vd = _dev(k_new), _dev(v_new)
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    check(lib().rec_kv_append_bulk(C.byref(rec), hkv, cap, bits, C.c_void_p(kd.data_ptr()), C.c_void_p(vd.data_ptr()),
+                                   p0, t, stream), "rec_kv_append_bulk")
+    with pytest.raises(ValueError):
+        check(lib().rec_kv_append_bulk(C.byref(rec), hkv, cap, bits, C.c_void_p(kd.data_ptr()),
+                                       C.c_void_p(vd.data_ptr()), cap - 10, t, stream), "rec_kv_append_bulk")
+    torch.cuda.synchronize()
+    lay = {n: a.copy() for n, a in kv.items()}
+    arrs = [lay[n] for n in ("k_codes", "k_scales", "k_biases", "v_codes", "v_scales", "v_biases")]
+    orec = abi.RecKVLayer(*(a.ctypes.data for a in arrs))
+    L = oracle.lib()
+    L.orc_kv_store.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+    for j in range(t):
+        kj, vj = np.ascontiguousarray(k_new[j]), np.ascontiguousarray(v_new[j])
+        L.orc_kv_store(C.addressof(orec), hkv, cap, bits, p0 + j, kj.ctypes.data, vj.ctypes.data)
+    for n in lay:
+        assert np.array_equal(_host(dev[n], lay[n].dtype), lay[n]), n
