@@ -323,14 +323,17 @@ def run_rec(args):
                      "frac": round(step_bytes / (t_max / K) / 1e9 / peak, 4),
                      "ideal_tokens_per_s": round(peak * 1e9 / step_bytes, 1)}
 
-    # ---- e2e through the public API: packets of 8 with a host round trip
+    # ---- e2e through the public API: packets of 8 with a host round trip,
+    # over the same positions as the timed region (the cache rows from there
+    # on are rewritten; attention reads only rows below the position)
     engine = FullModel(weights)
     storage = KVStorage.wrap(weights, kv, sess)
-    state = {"usable": True, "kv": storage, "metadata": None, "position": pos, "initial": ctx0,
+    e2e_start = ctx0 + W - 8  # one warm packet, then the timed region's positions
+    state = {"usable": True, "kv": storage, "metadata": None, "position": e2e_start, "initial": ctx0,
              "capacity": capacity, "limit": capacity, "growth_count": 0, "growth_seconds": 0.0}
     sampler = ResidentSampler(engine)
     token = int(sess.ids[0].item())
-    e2e_packets = max(1, min(K // 2, capacity - pos - 16) // 8)
+    e2e_packets = max(1, min(K, capacity - e2e_start - 16) // 8)
     sampler.block(state, token, 8, 0, temperature=0)  # warm
     token_host = torch.tensor([token], dtype=torch.int32).pin_memory()
     barrier()
@@ -349,7 +352,8 @@ def run_rec(args):
     # per packet of 8: the start token goes in (4 B, kernel argument); status,
     # count and the 8 ids come back (4 + 4 + 32 B)
     e2e = {"value": round(float(te.item()) * (1 if sharded else world), 2), "unit": UNIT, "h2d_bytes_per_step": 4 / 8,
-           "d2h_bytes_per_step": 40 / 8, "packet_tokens": 8, "api": "rec_b200.engine.ResidentSampler.block"}
+           "d2h_bytes_per_step": 40 / 8, "packet_tokens": 8, "api": "rec_b200.engine.ResidentSampler.block",
+           "positions": [e2e_start + 8, e2e_start + 8 + produced]}
 
     # ---- CPU baseline: the oracle on this host's cores, same weights and cache
     cpu = None
