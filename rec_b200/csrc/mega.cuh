@@ -313,11 +313,6 @@ __device__ __forceinline__ unsigned bar_index(const MegaArgs& a, int step, int l
 __device__ __forceinline__ unsigned route_flag(const MegaArgs& a, int step, int layer) {
   return a.layer_seq0 + unsigned(step) * unsigned(a.n_layers) + unsigned(layer) + 1u;
 }
-// Order-preserving key of a non-NaN float (+0 and -0 canonicalised first).
-__device__ __forceinline__ unsigned route_key(float x) {
-  const unsigned u = __float_as_uint(__fadd_rn(x, 0.0f));
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
 
 __device__ __forceinline__ bool aborted(const MegaArgs& a) {
   return *reinterpret_cast<volatile unsigned*>(a.gbar + 1) != 0;

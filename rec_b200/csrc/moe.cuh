@@ -40,6 +40,12 @@ struct RouterSmem {
   int is_last;
 };
 
+// Order-preserving key of a non-NaN float (+0 and -0 canonicalised first).
+__device__ __forceinline__ unsigned route_key(float x) {
+  const unsigned u = __float_as_uint(__fadd_rn(x, 0.0f));
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
 // Canonical router logit: lane l owns 8-element chunks l, l+32, ...; fused
 // multiply-adds in order; butterfly; rounded to bf16 (mixed_bits.py:32-38).
 template <int H>
@@ -89,6 +95,8 @@ __global__ void __launch_bounds__(kThreads) k_router(const RouterArgs a) {
   // the logits once into shared memory (all loads in flight together)
   for (int i = lane; i < E; i += 32) sm.p[i] = __ldcg(a.logits + i);
   __syncwarp();
+  // selection keys (route_key order; 0 = taken) over the choice storage
+  unsigned* keys = reinterpret_cast<unsigned*>(sm.choice);
   if (a.mode == 0) {
     float mx = -INFINITY;
     for (int i = lane; i < E; i += 32) mx = fmaxf(mx, sm.p[i]);
@@ -103,43 +111,49 @@ __global__ void __launch_bounds__(kThreads) k_router(const RouterArgs a) {
     for (int i = lane; i < E; i += 32) {
       const float pi = __fdiv_rn(sm.choice[i], s);
       sm.p[i] = pi;
-      sm.choice[i] = pi;
+      keys[i] = route_key(pi);
     }
   } else {
     for (int i = lane; i < E; i += 32) {
       const float pi = rsigmoid(sm.p[i]);
       sm.p[i] = pi;
-      sm.choice[i] = __fadd_rn(pi, a.expert_bias[i]);
+      keys[i] = route_key(__fadd_rn(pi, a.expert_bias[i]));
     }
   }
   __syncwarp();
-  int sel[kMaxTopK];
+  // k rounds of (largest choice, lowest id among equals): each lane keeps the
+  // best of its own experts lane + 32 j; the warp reduces those, and only the
+  // lane that owned the winner rescans its experts
+  unsigned bk = 0u;
+  int bi = 0;
+  for (int i = lane; i < E; i += 32)
+    if (keys[i] > bk) { bk = keys[i]; bi = i; }
+  float s2 = 0.0f, my_p = 0.0f;
+  int my_id = 0;
   for (int r = 0; r < a.k; ++r) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = lane; i < E; i += 32) {
-      const float c = sm.choice[i];
-      if (c > bv || (c == bv && i < bi)) { bv = c; bi = i; }
+    const unsigned wbest = __reduce_max_sync(0xffffffffu, bk);
+    int widx = int(__reduce_min_sync(0xffffffffu, (bk == wbest && bk) ? unsigned(bi) : ~0u));
+    if (unsigned(widx) >= unsigned(E)) widx = 0;  // only for NaN choices
+    const float pw = sm.p[widx];
+    if (lane == (widx & 31)) {
+      keys[widx] = 0u;
+      bk = 0u;
+      bi = 0;
+      for (int i = lane; i < E; i += 32)
+        if (keys[i] > bk) { bk = keys[i]; bi = i; }
     }
-    for (int off = 16; off >= 1; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    if (lane == r) {
+      my_id = widx;
+      my_p = pw;
     }
-    sel[r] = bi;
-    if (lane == 0) sm.choice[bi] = -INFINITY;
-    __syncwarp();
+    s2 = __fadd_rn(s2, pw);
   }
-  if (lane == 0) {
-    float sum = 0.0f;
-    for (int r = 0; r < a.k; ++r) sum = __fadd_rn(sum, sm.p[sel[r]]);
-    sum = __fadd_rn(sum, 1e-20f);
-    for (int r = 0; r < a.k; ++r) {
-      a.ids[r] = sel[r];
-      a.wts[r] = __fdiv_rn(sm.p[sel[r]], sum);
-    }
-    *a.counter = 0;
+  s2 = __fadd_rn(s2, 1e-20f);
+  if (lane < a.k) {
+    a.ids[lane] = my_id;
+    a.wts[lane] = __fdiv_rn(my_p, s2);
   }
+  if (lane == 0) *a.counter = 0;
 }
 
 // --- expert gate/up + SwiGLU ---------------------------------------------------

@@ -117,10 +117,13 @@ def test_long_context_step_bitexact(cuda, schedule, context, bits):
         assert np.array_equal(_u16(logits), ref_logits), pos
 
 
+@pytest.mark.parametrize("ties", [False, True])
 @pytest.mark.parametrize("variant", ["tiny_kv8_fp16", "tiny_kv4_bf16_sigmoid"])
-def test_router_moe_entry_bitexact(cuda, variant):
+def test_router_moe_entry_bitexact(cuda, variant, ties):
     """rec_router_moe (the MoE block of one layer alone) against the oracle's
-    RMSNorm -> router -> top-k -> SwiGLU experts -> bf16 mix -> residual."""
+    RMSNorm -> router -> top-k -> SwiGLU experts -> bf16 mix -> residual.
+    With ties, odd router rows repeat the even ones, so every choice value
+    occurs twice and the lower expert id must win each tie."""
     import ctypes as C
 
     from rec_b200._lib import check, lib
@@ -130,6 +133,13 @@ def test_router_moe_entry_bitexact(cuda, variant):
     sd = 1 if cfg.scale_dtype == torch.bfloat16 else 0
     rng = np.random.default_rng(13)
     layer = 1 if cfg.n_layers > 1 else 0
+    if ties:
+        R = w.layers[layer].router
+        R[1::2] = R[0::2]
+        if w.layers[layer].expert_bias is not None:
+            bias = w.layers[layer].expert_bias
+            bias[1::2] = bias[0::2]
+        torch.cuda.synchronize()
     h = oracle.f32_to_bf16(rng.standard_normal(cfg.hidden, dtype=np.float32))
     h_dev = torch.from_numpy(h.view(np.int16)).cuda()
     ids_dev = torch.zeros(cfg.top_k, dtype=torch.int32, device="cuda")
