@@ -58,6 +58,8 @@ def parse():
     p.add_argument("--shard", action="store_true",
                    help="with N GPUs: one session split over the GPUs (expert parallelism + split-KV, the "
                         "config-4 partitioning) instead of N independent sessions (config 3 replicas)")
+    p.add_argument("--config1", action="store_true",
+                   help="config 1: one decoder layer (64 experts top-8, 1,024-token 8-bit cache) per decode step")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--profile-phases", action="store_true",
                    help="also record the persistent kernel's phase timeline (printed to stderr)")
@@ -168,7 +170,11 @@ def run_rec(args):
     pos = ctx0
 
     stream = torch.cuda.current_stream()
-    ids_dev, prod_dev = sess.ids, sess.produced
+    prod_dev = sess.produced
+    # every produced id is kept (warm-up ids at [0, W), timed ids at [W, W + K))
+    # so that the CPU leg can check the timed tokens
+    ids_all = torch.zeros(W + K + PACKET, dtype=torch.int32, device="cuda")
+    ids_off = [0]
 
     def decode(n, token, position, events=None):
         """n greedy steps in device-side packets of up to 64 tokens; token < 0
@@ -180,8 +186,10 @@ def run_rec(args):
             if events is not None:
                 a = torch.cuda.Event(enable_timing=True)
                 a.record(stream)
+            ids_ptr = ids_all.data_ptr() + 4 * ids_off[0]
             check(lib().rec_decode_greedy(sess.ctx, token if done == 0 else -1, position + done, c, None, 0,
-                                          ids_dev.data_ptr(), prod_dev.data_ptr(), stream.cuda_stream))
+                                          ids_ptr, prod_dev.data_ptr(), stream.cuda_stream))
+            ids_off[0] += c
             if events is not None:
                 b = torch.cuda.Event(enable_timing=True)
                 b.record(stream)
@@ -207,7 +215,16 @@ def run_rec(args):
     barrier()
     clk = clocks.stop()
     sess.check_status()
+    timed_start_token = int(ids_all[W - 1].item())
+    timed_ids = ids_all[W:W + K].tolist()
+    timed_pos = pos
     pos += K
+    # ---- CPU leg: the oracle on this host's cores, same weights and cache,
+    # decoding the timed region's token chain from its first position (taken
+    # now, before later calls rewrite cache rows from that position on)
+    cpu, parity = None, None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu, parity = cpu_leg_same_chain(weights, kv, cfg, timed_pos, timed_start_token, timed_ids)
     t_local = e0.elapsed_time(e1) / 1e3
     t = torch.tensor([t_local], device="cuda")
     if world > 1:
@@ -332,7 +349,7 @@ def run_rec(args):
     state = {"usable": True, "kv": storage, "metadata": None, "position": e2e_start, "initial": ctx0,
              "capacity": capacity, "limit": capacity, "growth_count": 0, "growth_seconds": 0.0}
     sampler = ResidentSampler(engine)
-    token = int(sess.ids[0].item())
+    token = int(timed_ids[-1]) if timed_ids else 1
     e2e_packets = max(1, min(K, capacity - e2e_start - 16) // 8)
     sampler.block(state, token, 8, 0, temperature=0)  # warm
     token_host = torch.tensor([token], dtype=torch.int32).pin_memory()
@@ -355,10 +372,6 @@ def run_rec(args):
            "d2h_bytes_per_step": 40 / 8, "packet_tokens": 8, "api": "rec_b200.engine.ResidentSampler.block",
            "positions": [e2e_start + 8, e2e_start + 8 + produced]}
 
-    # ---- CPU baseline: the oracle on this host's cores, same weights and cache
-    cpu = None
-    if world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_same_weights(weights, kv, cfg, state["position"])
 
     if world > 1:
         dist.barrier()
@@ -389,32 +402,46 @@ def run_rec(args):
         "graph_schedule_kernels_us": per_kernel,
         "phases_us": phases,
         "cpu_baseline": cpu,
+        "parity": parity,
     }
     print(json.dumps(out), flush=True)
 
 
-def cpu_baseline_same_weights(weights, kv, cfg, pos):
-    import torch
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
+
+def cpu_leg_same_chain(weights, kv, cfg, pos, token, timed_ids, budget_s=12.0, max_tokens=32):
+    """The oracle (oracle/rec_oracle.c, OpenMP over rows and attention items,
+    every host core) decodes greedily from the timed region's first position
+    and token with the same weights and cache.  Its throughput is the CPU
+    baseline; its ids are compared with the ids the GPU produced in the timed
+    region (parity of the measured tokens themselves)."""
     import oracle
     from oracle.host import HostKV, HostModel
 
-    threads = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
-    oracle.lib()
+    threads = oracle.set_threads(host_threads())
     host = HostModel(weights)
     hkv = HostKV.from_device(cfg, kv)
-    token = 1
+    got = []
     n, t0 = 0, time.perf_counter()
-    while n < 2 or (time.perf_counter() - t0 < 10 and n < 8):
+    while n < len(timed_ids) and n < max_tokens and (n < 2 or time.perf_counter() - t0 < budget_s):
         logits, _ = host.step(hkv, token, pos + n, want_trace=False)
         token = oracle.argmax_bf16(logits)
+        got.append(token)
         n += 1
     dt = time.perf_counter() - t0
-    del host
-    return {"value": round(n / dt, 4), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{n} full decode tokens of the same model and cache on the host (oracle/rec_oracle.c, "
-                      f"OpenMP over rows), {dt:.1f} s"}
+    del host, hkv
+    mismatch = next((i for i in range(n) if got[i] != timed_ids[i]), None)
+    cpu = {"value": round(n / dt, 4), "unit": UNIT, "cores": threads, "kind": "port",
+           "sample": f"{n} greedy decode tokens of the same model and cache from the timed region's first "
+                     f"position ({pos}) on the host (oracle/rec_oracle.c, {threads} OpenMP threads), {dt:.1f} s"}
+    parity = {"tokens_compared": n, "first_mismatch": mismatch, "start_position": pos,
+              "checker": "oracle/rec_oracle.c greedy chain vs the ids of the timed packets, bit-exact ids"}
+    return cpu, parity
 
 
 # ---------------------------------------------------------------------------- reference arm
@@ -424,17 +451,21 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
     import oracle
     from oracle.host import HostModel
-    from oracle.synthetic import random_model
-    from rec_b200.model import CONFIG3
+    from rec_b200.model import CONFIG3, generate_weights
 
+    threads = oracle.set_threads(host_threads())
     cfg = CONFIG3
-    oracle.lib()
-    model = random_model(cfg, seed=0)
-    host = HostModel(model)
+    # the GPU arm's model: the same seeded N(0, 0.02) weights, drawn and
+    # quantized with the same generator (set-up only; nothing on the device
+    # is timed), then held in host memory
+    import torch
+
+    dev_weights = generate_weights(cfg, seed=0, device="cuda")
+    host = HostModel(dev_weights)
+    del dev_weights
+    torch.cuda.empty_cache()
     ctx0 = args.context
     W, K = max(3, args.warmup), args.steps
     capacity = (ctx0 + 64 + 255) // 256 * 256
@@ -471,12 +502,13 @@ def run_reference(args):
         pos += 1
     dt = time.perf_counter() - t0
     value = n_exec / dt
-    sample = (f"{n_exec} of the {K} requested decode tokens executed (bounded sample), config-3 shapes with "
-              f"random int4 codes, {ctx0}-token 8-bit cache; oracle/rec_oracle.c with {threads} OpenMP threads")
+    sample = (f"{n_exec} of the {K} requested decode tokens executed (bounded sample), the config-3 model "
+              f"(bench.py's seeded weights), {ctx0}-token 8-bit cache of quantized synthetic K, V ~ N(0, 1); "
+              f"oracle/rec_oracle.c with {threads} OpenMP threads")
     out = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": 0,
            "steps": K, "warmup": W, "ms_per_step": round(dt / n_exec * 1e3, 2), "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-           "config": {"workload": cfg.name, "seq_len": ctx0, "kv_bits": cfg.kv_bits},
+           "config": {"workload": cfg.name, "seq_len": ctx0, "kv_bits": cfg.kv_bits, "same_weights": True},
            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
                             "sample": sample},
            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -699,9 +731,67 @@ def run_sample_head(args):
                       "rows": rows}), flush=True)
 
 
+def run_config1(args):
+    """Config 1: decode steps of one decoder layer (hidden 2048, GQA 32/4 x
+    128, 64 experts top-8 with I 768, int4 g64 weights, 1,024-token 8-bit
+    cache of quantized K, V ~ N(0, 1)) on the persistent kernel, in device-side
+    greedy packets of 64; the step also embeds the token and runs a 4,096-row
+    int4 lm_head with argmax.  CUDA events over K steps; the layer's
+    algorithmic bytes are weights + router + the attended KV."""
+    import torch
+
+    from rec_b200._lib import check, lib
+    from rec_b200.model import CONFIG1_LAYER, KVCache, generate_weights
+    from rec_b200.session import DecodeSession
+
+    torch.cuda.set_device(0)
+    cfg = CONFIG1_LAYER
+    ctx0, W, K = 1024, max(3, args.warmup), args.steps
+    cap = (ctx0 + W + K + 255) // 256 * 256
+    w = generate_weights(cfg, seed=0, device="cuda")
+    kv = KVCache.allocate(cfg, cap)
+    kv.fill_random(ctx0, seed=7)
+    sess = DecodeSession(w, kv)
+    stream = torch.cuda.current_stream()
+
+    def run(n, token, position):
+        done = 0
+        while done < n:
+            c = min(PACKET, n - done)
+            check(lib().rec_decode_greedy(sess.ctx, token if done == 0 else -1, position + done, c, None, 0,
+                                          sess.ids.data_ptr(), sess.produced.data_ptr(), stream.cuda_stream))
+            done += c
+
+    run(W, 5, ctx0)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    run(K, -1, ctx0 + W)
+    b.record(stream)
+    torch.cuda.synchronize()
+    sess.check_status()
+    us = a.elapsed_time(b) / K * 1e3
+    peak, kind = measured_peaks()
+    g64 = 0.5 + 4 / 64
+    H = cfg.hidden
+    layer_w = ((cfg.n_q_heads + 2 * cfg.n_kv_heads) * 128 * H + H * cfg.n_q_heads * 128
+               + cfg.top_k * 3 * cfg.moe_inter * H) * g64 + cfg.n_experts * H * 2 + 2 * H * 2
+    kv_b = cfg.kv_bytes_per_token(ctx0 + W + K // 2)
+    step_b = cfg.weight_bytes_per_token() + kv_b
+    print(json.dumps({"workload": "config1_one_decoder_layer", "context": ctx0 + W, "steps": K, "warmup": W,
+                      "us_per_step": round(us, 2), "layer_bytes": int(layer_w + kv_b),
+                      "step_bytes_incl_embed_and_4096_row_head": int(step_b),
+                      "GBps_step": round(step_b / (us * 1e-6) / 1e9, 1),
+                      "frac_step": round(step_b / (us * 1e-6) / 1e9 / peak, 4), "peak_GBps": peak,
+                      "peak_source": kind, "schedule": "persistent kernel, packets of 64 greedy steps"}),
+          flush=True)
+
+
 def main():
     args = parse()
-    if args.sample_head:
+    if args.config1:
+        run_config1(args)
+    elif args.sample_head:
         run_sample_head(args)
     elif args.prefill:
         run_prefill(args)

@@ -281,7 +281,9 @@ REC_API int rec_gemv_int4(const RecQMat* w, int32_t scale_dtype, int64_t n, int3
  * is NULL, the bf16 logits) is one static device array of 532,736 bytes per
  * device.  Limits: N <= 262,144 rows when y_dev is NULL (larger N is rejected
  * with REC_EINVAL; pass y_dev for a larger vocabulary); N even, K as in
- * rec_gemv_int4.  token_dev receives -1 if a bounded device wait ran out.
+ * rec_gemv_int4.  token_dev receives -1 if a bounded device wait ran out;
+ * the logits in y_dev (when given) are then undefined, possibly partly
+ * written.
  * The first call on each device looks up the array's device address (with
  * that device current) and sets the kernels' shared-memory limit; make that
  * first call before any stream capture.  Every call shares the array and it

@@ -74,8 +74,19 @@ def lib() -> C.CDLL:
         L.orc_hf.restype = C.c_float
         L.orc_hf.argtypes = [C.c_uint16]
         L.orc_decode_step.restype = C.c_int
+        L.orc_mix.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p]
+        L.orc_select_topk.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+        L.orc_kv_store.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+        L.orc_set_threads.restype = C.c_int
+        L.orc_set_threads.argtypes = [C.c_int]
         _lib = L
     return _lib
+
+
+def set_threads(n: int) -> int:
+    """Sets the oracle's OpenMP thread count (overrides OMP_NUM_THREADS);
+    returns the count now in use."""
+    return int(lib().orc_set_threads(int(n)))
 
 
 # ---------------------------------------------------------------- bf16 / fp16

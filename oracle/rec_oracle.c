@@ -37,6 +37,7 @@
  */
 #include <float.h>
 #include <math.h>
+#include <omp.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -651,9 +652,11 @@ ORC_API void orc_select_topk(const float* p, const float* choice, int E, int k, 
                              float* weights) {
   int taken[1024] = {0};
   for (int r = 0; r < k; ++r) {
+    /* a NaN choice ranks below every number; ties keep the lower index */
     int best = -1;
     for (int e = 0; e < E; ++e)
-      if (!taken[e] && (best < 0 || choice[e] > choice[best])) best = e;
+      if (!taken[e] && (best < 0 || (!isnan(choice[e]) && (isnan(choice[best]) || choice[e] > choice[best]))))
+        best = e;
     taken[best] = 1;
     ids[r] = best;
   }
@@ -980,6 +983,14 @@ ORC_API int32_t orc_sample(const uint16_t* logits, int64_t V, const int32_t* his
 /* --------------------------------------------------------- decode step */
 /* One full decode step.  kv: n_layers layer caches of capacity C; h_trace
  * (optional) bf16[L+1, H]; logits bf16[V]. */
+/* OpenMP threads of the oracle's parallel loops (rows, attention items).
+ * Set explicitly by the CPU timing legs: a launcher may have exported
+ * OMP_NUM_THREADS=1 before the runtime read it.  Returns the count in use. */
+ORC_API int orc_set_threads(int n) {
+  if (n > 0) omp_set_num_threads(n);
+  return omp_get_max_threads();
+}
+
 ORC_API int orc_decode_step(const RecModelDesc* md, const RecLayerWeights* layers,
                             const RecGlobalWeights* gw, const RecKVLayer* kv, int C, int token,
                             int pos, uint16_t* logits, uint16_t* trace) {

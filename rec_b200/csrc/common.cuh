@@ -11,7 +11,27 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <set>
+#include <utility>
+
 namespace rec {
+
+// Raises a kernel's dynamic shared-memory limit once per (device, kernel):
+// the attribute is per device, so a process that drives several GPUs sets it
+// on each of them.  Host only; thread safe.
+inline cudaError_t set_smem_limit(const void* kern, size_t smem) {
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> g(mu);
+  if (done.count({dev, kern})) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e == cudaSuccess) done.insert({dev, kern});
+  return e;
+}
 
 // ----------------------------------------------------------------------------
 // Status words.  Kernels never trap: a bounded wait that runs out records a

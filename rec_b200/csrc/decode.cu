@@ -109,16 +109,9 @@ __global__ void k_step_end(int* ctl) {
 // --- launch helper ----------------------------------------------------------------
 template <typename Kern, typename... Args>
 cudaError_t launch(Kern kern, int grid, int block, size_t smem, cudaStream_t st, bool pdl, Args... args) {
-  static std::mutex mu;
-  static std::set<const void*> configured;
-  {
-    std::lock_guard<std::mutex> g(mu);
-    const void* key = reinterpret_cast<const void*>(kern);
-    if (smem > 48 * 1024 && !configured.count(key)) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-      if (e != cudaSuccess) return e;
-      configured.insert(key);
-    }
+  if (smem > 48 * 1024) {
+    cudaError_t e = set_smem_limit(reinterpret_cast<const void*>(kern), smem);
+    if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -777,17 +770,9 @@ static cudaError_t launch_mega_t(RecCtx* c, int steps, cudaStream_t st, int seg)
   A.prof_layer = c->prof_layer;
   auto kern = k_decode_mega<I, BITS>;
   const size_t smem = sizeof(MegaSmem);
-  static std::mutex mu;
-  static std::set<const void*> configured;
-  {
-    std::lock_guard<std::mutex> g(mu);
-    if (!configured.count(reinterpret_cast<const void*>(kern))) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-      if (e != cudaSuccess) return e;
-      configured.insert(reinterpret_cast<const void*>(kern));
-    }
-  }
-  cudaError_t e = cudaMemsetAsync(c->mega_cnt, 0, 2 * sizeof(unsigned), st);
+  cudaError_t e = set_smem_limit(reinterpret_cast<const void*>(kern), smem);
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(c->mega_cnt, 0, 2 * sizeof(unsigned), st);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(c->grid);

@@ -314,11 +314,9 @@ template <int K, int SD, int RS, int NS, int EPI>
 inline cudaError_t launch_gemv(const GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
   auto kern = k_gemv<K, SD, RS, NS, EPI>;
   const size_t smem = sizeof(GemvSmem<K, RS, NS>);
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (smem > 48 * 1024) {
+    cudaError_t e = set_smem_limit(reinterpret_cast<const void*>(kern), smem);
     if (e != cudaSuccess) return e;
-    configured = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);

@@ -627,7 +627,8 @@ struct Producer {
           bj = j;
         }
       const unsigned wbest = __reduce_max_sync(0xffffffffu, best);
-      const int widx = int(__reduce_min_sync(0xffffffffu, (best == wbest && best) ? unsigned(lane + 32 * bj) : ~0u));
+      int widx = int(__reduce_min_sync(0xffffffffu, (best == wbest && best) ? unsigned(lane + 32 * bj) : ~0u));
+      if (unsigned(widx) >= unsigned(E)) widx = 0;  // no key left (top_k > E); never read outside route_p
       const float pw = sm.route_p[widx];
       if (lane == (widx & 31)) {
 #pragma unroll

@@ -40,9 +40,11 @@ struct RouterSmem {
   int is_last;
 };
 
-// Order-preserving key of a non-NaN float (+0 and -0 canonicalised first).
+// Order-preserving key of a float (+0 and -0 canonicalised first); NaN gets
+// key 1, below every number, so it is chosen last (lowest index among NaNs).
 __device__ __forceinline__ unsigned route_key(float x) {
   const unsigned u = __float_as_uint(__fadd_rn(x, 0.0f));
+  if ((u & 0x7fffffffu) > 0x7f800000u) return 1u;  // NaN ranks below every number (and -inf)
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 

@@ -13,8 +13,9 @@ from rec_b200 import abi
 
 pytestmark = pytest.mark.gpu
 
+# the last three are config 2's long contexts (131,072 and 258,048 tokens)
 CASES = [(1, 8), (37, 4), (256, 8), (257, 4), (1028, 8), (1028, 4), (4097, 8), (16384, 8), (16385, 4), (20000, 8),
-         (70000, 4)]
+         (70000, 4), (131072, 8), (258048, 4), (258048, 8)]
 
 
 def _dev(a):
