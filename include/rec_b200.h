@@ -139,6 +139,22 @@ REC_API int rec_set_workspace(RecCtx* ctx, void* workspace_dev, size_t bytes);
  * FullModel.forward (megakernel.py:1224-1301). */
 REC_API int rec_decode_step(RecCtx* ctx, int32_t token, int32_t position, void* logits_dev,
                             void* trace_dev, void* stream);
+/* rec_decode_step through the first layer_count layers only (1 <= layer_count
+ * <= n_layers): the final norm and lm_head follow the last layer run, the
+ * trace holds rows 0..layer_count, and the deeper layers' cache rows at this
+ * position are not written.  Runs on the persistent kernel (n_experts <=
+ * 256).  Replaces FullModel.forward(state, token, layer_count)
+ * (engine/src/rec_mlx/kernels/megakernel.py:824,861,1224-1233,1272). */
+REC_API int rec_decode_layers(RecCtx* ctx, int32_t token, int32_t position, int32_t layer_count, void* logits_dev,
+                              void* trace_dev, void* stream);
+/* Tests of the failure path only (no reference counterpart; the reference's
+ * spin-capped grid barrier is megakernel.py:137-159): the persistent
+ * kernel's grid-barrier poll bound (0 restores the default) and one CTA
+ * (index, or -1 for none) that never arrives at a grid barrier.  With a CTA
+ * skipping, every CTA's bounded wait runs out, the kernel sets device status
+ * REC_DEV_COUNTER_TIMEOUT and returns; the next rec_check_status reports it
+ * and marks the session unusable. */
+REC_API int rec_set_fault_injection(RecCtx* ctx, uint32_t barrier_spin_limit, int32_t skip_arrive_cta);
 /* Up to `count` greedy steps with the argmax fed back on the device; stops
  * after an EOS id.  ids_dev int32[count] receives the produced ids, produced_dev
  * int32[1] their number.  token = -1 continues from the token and position
@@ -314,6 +330,19 @@ REC_API int rec_sample_logits_masked(const void* logits_dev, int32_t batch, int3
                                      const int32_t* history_dev, int32_t history_len, const RecSampling* params,
                                      const float* uniforms_dev, const uint32_t* allow_dev, int64_t allow_stride,
                                      int32_t* ids_dev, void* stream);
+/* Log-probability of each row's chosen id (ids_dev int32 [batch]) as the
+ * reference reports it: report = x / T (temperature > 0) or x, x the logits
+ * after the penalties over the history and the optional grammar mask (the
+ * rules of rec_sample_logits_masked); logprob_dev[b] = report[id] -
+ * logsumexp(report) over the whole vocabulary (fp32, the library's own exp
+ * and log).  NaN for an id outside [0, vocab); -inf when no logit is finite.
+ * top_k / top_p do not enter.  Replaces the logprob report of the reference
+ * (engine/src/rec_mlx/engine.py:294-296; kernels/masked_sampling.py:126-128,
+ * 145-146, 205-206). */
+REC_API int rec_token_logprob(const void* logits_dev, int32_t batch, int32_t vocab, int64_t stride,
+                              const int32_t* history_dev, int32_t history_len, const RecSampling* params,
+                              const uint32_t* allow_dev, int64_t allow_stride, const int32_t* ids_dev,
+                              float* logprob_dev, void* stream);
 /* The sampling head for `batch` hidden rows (bf16 [batch, hidden]):
  * logits[b] = lm_head . RMSNorm(h[b], final_norm) (int4 g64 GEMV into
  * logits_dev, bf16 [batch, vocab]), then rec_sample_logits on those rows with

@@ -77,6 +77,8 @@ def lib() -> C.CDLL:
         L.orc_mix.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p]
         L.orc_select_topk.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
         L.orc_kv_store.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+        L.orc_token_logprob.restype = C.c_float
+        L.orc_token_logprob.argtypes = [_u16p, C.c_int64, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int32]
         L.orc_set_threads.restype = C.c_int
         L.orc_set_threads.argtypes = [C.c_int]
         _lib = L
@@ -243,6 +245,17 @@ def sample(logits_bf16, history, params, uniforms, allow=None) -> int:
     m = np.ascontiguousarray(allow, np.uint32)
     assert m.size >= (lg.size + 31) // 32
     return int(lib().orc_sample_masked(lg, lg.size, hp, h.size, C.byref(params), u, m.ctypes.data))
+
+
+def token_logprob(logits_bf16, history, params, token: int, allow=None) -> float:
+    """orc_token_logprob: the reference's reported log-probability of
+    `token` (report = penalised, masked logits / T; report[token] -
+    logsumexp(report)) in the GPU kernel's summation order."""
+    lg = np.ascontiguousarray(logits_bf16, np.uint16)
+    h = np.ascontiguousarray(history if history is not None else np.zeros(0), np.int32)
+    m = None if allow is None else np.ascontiguousarray(allow, np.uint32)
+    return float(lib().orc_token_logprob(lg, lg.size, h.ctypes.data if h.size else None, h.size, C.byref(params),
+                                         None if m is None else m.ctypes.data, int(token)))
 
 
 def pack_allow(allowed_ids, vocab: int) -> np.ndarray:

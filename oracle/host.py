@@ -64,11 +64,20 @@ class HostModel:
     def new_kv(self, capacity: int) -> "HostKV":
         return HostKV(self.cfg, capacity)
 
-    def step(self, kv: "HostKV", token: int, pos: int, want_trace: bool = True):
+    def step(self, kv: "HostKV", token: int, pos: int, want_trace: bool = True, layer_count: int | None = None):
+        """One decode step; with layer_count, only the first layer_count
+        layers run before the final norm and lm_head (FullModel.forward's
+        partial depth)."""
         cfg = self.cfg
+        desc = self.desc
+        n = cfg.n_layers
+        if layer_count is not None and layer_count != cfg.n_layers:
+            n = int(layer_count)
+            desc = abi.RecModelDesc.from_buffer_copy(self.desc)
+            desc.n_layers = n
         logits = np.zeros(cfg.vocab, np.uint16)
-        trace = np.zeros((cfg.n_layers + 1, cfg.hidden), np.uint16) if want_trace else None
-        rc = lib().orc_decode_step(C.byref(self.desc), self.layers, C.byref(self.glob), kv.rec, kv.capacity,
+        trace = np.zeros((n + 1, cfg.hidden), np.uint16) if want_trace else None
+        rc = lib().orc_decode_step(C.byref(desc), self.layers, C.byref(self.glob), kv.rec, kv.capacity,
                                    int(token), int(pos), logits.ctypes.data,
                                    trace.ctypes.data if trace is not None else None)
         if rc != 0:

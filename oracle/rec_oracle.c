@@ -975,6 +975,64 @@ ORC_API int32_t orc_sample_masked(const uint16_t* logits, int64_t V, const int32
   return out;
 }
 
+/* Log-probability of `id` as the reference reports it (engine.py:294-296,
+ * masked_sampling.py:126-128): report = x / T (T > 0) or x, x the penalised,
+ * grammar-masked logits of orc_sample_masked; logprob = report[id] -
+ * logsumexp(report).  Order of rec_b200/csrc/capi_logprob.cu: M = max;
+ * thread t of 1024 sums exp(report_i - M) over i = t, t + 1024, ... in
+ * order; a butterfly over each warp of 32 threads; the 32 warp sums in
+ * order; lse = M + log S.  NaN for an id outside [0, V); -inf when no logit
+ * is finite. */
+ORC_API float orc_token_logprob(const uint16_t* logits, int64_t V, const int32_t* hist, int n_hist,
+                                const RecSampling* sp, const uint32_t* allow, int32_t id) {
+  const int pen = sp->repetition_penalty != 1.0f || sp->presence_penalty != 0.0f;
+  uint8_t* seen = (uint8_t*)calloc((size_t)V, 1);
+  if (pen)
+    for (int i = 0; i < n_hist; ++i)
+      if (hist[i] >= 0 && hist[i] < V) seen[hist[i]] = 1;
+  float* y = (float*)malloc(sizeof(float) * V);
+  for (int64_t i = 0; i < V; ++i) {
+    float v;
+    if (allow && !((allow[i >> 5] >> (i & 31)) & 1u)) {
+      v = -INFINITY;
+    } else {
+      v = bf(logits[i]);
+      if (seen[i]) {
+        if (sp->repetition_penalty != 1.0f)
+          v = v < 0.0f ? v * sp->repetition_penalty : v / sp->repetition_penalty;
+        if (sp->presence_penalty != 0.0f) v = v - sp->presence_penalty;
+      }
+      v = v + 0.0f;
+      if (sp->temperature > 0.0f) v = v / sp->temperature;
+    }
+    y[i] = v;
+  }
+  free(seen);
+  float M = -INFINITY;
+  for (int64_t i = 0; i < V; ++i) M = y[i] > M ? y[i] : M;
+  float out;
+  if (id < 0 || id >= V) {
+    out = NAN;
+  } else if (M == -INFINITY) {
+    out = -INFINITY;
+  } else {
+    float S = 0.0f;
+    for (int w = 0; w < 32; ++w) {
+      float v[32];
+      for (int l = 0; l < 32; ++l) {
+        float a = 0.0f;
+        for (int64_t i = 32 * w + l; i < V; i += 1024) a = a + rexp(y[i] - M);
+        v[l] = a;
+      }
+      bfly(v, 32);
+      S = S + v[0];
+    }
+    out = y[id] - (M + rlog(S));
+  }
+  free(y);
+  return out;
+}
+
 ORC_API int32_t orc_sample(const uint16_t* logits, int64_t V, const int32_t* hist, int n_hist,
                            const RecSampling* sp, const float* u) {
   return orc_sample_masked(logits, V, hist, n_hist, sp, u, NULL);

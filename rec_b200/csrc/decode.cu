@@ -170,6 +170,11 @@ struct RecCtx {
   size_t prof_entries = 0;
   unsigned long long* prof2 = nullptr;  // optional stamps inside one layer
   int prof_layer = -1;
+  int layers_run = 0;  // > 0: the current call runs only the first layers_run layers (rec_decode_layers)
+  // failure-path tests (rec_set_fault_injection): the grid barrier's poll
+  // bound, and one CTA that never arrives at a grid barrier (-1: none)
+  uint32_t bar_spin_limit = kSpinLimit * 4;
+  int skip_arrive_cta = -1;
 };
 
 namespace {
@@ -719,7 +724,9 @@ static cudaError_t launch_mega_t(RecCtx* c, int steps, cudaStream_t st, int seg)
   MegaArgs A = {};
   A.seg = seg;
   A.layers = c->mega_layers;
-  A.n_layers = d.n_layers;
+  A.n_layers = c->layers_run > 0 ? c->layers_run : d.n_layers;
+  A.bar_spin_limit = c->bar_spin_limit;
+  A.skip_arrive_cta = c->skip_arrive_cta;
   A.H = d.hidden;
   A.hq = d.n_q_heads;
   A.hkv = d.n_kv_heads;
@@ -786,7 +793,7 @@ static cudaError_t launch_mega_t(RecCtx* c, int steps, cudaStream_t st, int seg)
   cfg.numAttrs = 1;
   e = cudaLaunchKernelEx(&cfg, kern, A);
   // a segmented step advances the layer sequence once, after its last segment
-  if (e == cudaSuccess && seg == kSegAll) c->layer_seq += unsigned(steps) * unsigned(d.n_layers);
+  if (e == cudaSuccess && seg == kSegAll) c->layer_seq += unsigned(steps) * unsigned(A.n_layers);
   return e;
 }
 
@@ -850,6 +857,44 @@ REC_API int rec_decode_step(RecCtx* c, int32_t token, int32_t position, void* lo
   if (trace_dev)
     REC_CHECK_CUDA(cudaMemcpyAsync(trace_dev, c->trace, size_t(c->d.n_layers + 1) * c->d.hidden * 2,
                                    cudaMemcpyDeviceToDevice, st));
+  return REC_OK;
+}
+
+REC_API int rec_decode_layers(RecCtx* c, int32_t token, int32_t position, int32_t layer_count, void* logits_dev,
+                              void* trace_dev, void* stream) {
+  int rc = check_ready(c);
+  if (rc) return rc;
+  REC_CHECK_ARG(layer_count >= 1 && layer_count <= c->d.n_layers, "layer_count %d outside 1..%d", layer_count,
+                c->d.n_layers);
+  if (layer_count == c->d.n_layers) return rec_decode_step(c, token, position, logits_dev, trace_dev, stream);
+  REC_CHECK_ARG(c->d.n_experts <= kMegaMaxExperts, "a partial-depth step needs at most %d experts", kMegaMaxExperts);
+  if (position < 0 || position >= position_limit(c)) {
+    set_error("position %d outside the KV capacity", position);
+    return REC_ELIMIT;
+  }
+  REC_CHECK_ARG(token >= 0 && token < c->d.vocab, "token %d outside the vocabulary", token);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  k_set_step<<<1, 32, 0, st>>>(c->ctl, token, position, 0, make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0), 0);
+  REC_CHECK_CUDA(cudaGetLastError());
+  // the persistent kernel with a shorter layer loop (its H phase follows the
+  // last layer run)
+  c->sched = kSchedMega;
+  c->layers_run = layer_count;
+  const cudaError_t e = launch_mega(c, 1, st);
+  c->layers_run = 0;
+  REC_CHECK_CUDA(e);
+  if (logits_dev)
+    REC_CHECK_CUDA(cudaMemcpyAsync(logits_dev, c->logits, size_t(c->d.vocab) * 2, cudaMemcpyDeviceToDevice, st));
+  if (trace_dev)
+    REC_CHECK_CUDA(cudaMemcpyAsync(trace_dev, c->trace, size_t(layer_count + 1) * c->d.hidden * 2,
+                                   cudaMemcpyDeviceToDevice, st));
+  return REC_OK;
+}
+
+REC_API int rec_set_fault_injection(RecCtx* c, uint32_t barrier_spin_limit, int32_t skip_arrive_cta) {
+  REC_CHECK_ARG(c, "null context");
+  c->bar_spin_limit = barrier_spin_limit ? barrier_spin_limit : kSpinLimit * 4;
+  c->skip_arrive_cta = skip_arrive_cta;
   return REC_OK;
 }
 

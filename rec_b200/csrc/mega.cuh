@@ -138,6 +138,10 @@ struct MegaArgs {
   // embedding + Q of layer 0; seg == l >= 0 is O, R, G, D of layer l, then
   // Q of layer l + 1 (or H and E after the last layer)
   int seg;
+  // poll bound of the grid barrier, and a CTA that skips its arrivals (-1:
+  // none): the failure path's tests make the bounded wait run out with them
+  unsigned bar_spin_limit;
+  int skip_arrive_cta;
   unsigned long long* prof;  // optional: [barrier][cta] x (arrive, release) globaltimer stamps
   unsigned long long* prof2; // optional: [cta][64] stamps inside layer prof_layer of step 0
   int prof_layer;
@@ -334,13 +338,14 @@ __device__ __forceinline__ bool grid_barrier(const MegaArgs& a, unsigned seq, un
     if (a.prof && idx != kNoStamp) a.prof[(size_t(idx) * gridDim.x + blockIdx.x) * 2] = globaltimer();
     // release: the CTA's writes (ordered before this thread by the barrier
     // above) become visible to every CTA that acquires the count
-    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a.gbar), "r"(1u) : "memory");
+    if (int(blockIdx.x) != a.skip_arrive_cta)
+      asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a.gbar), "r"(1u) : "memory");
     const unsigned target = gridDim.x * (seq + 1);
     int ok = 1;
     uint32_t spins = 0;
     while (ld_acquire(a.gbar) < target) {
       if (aborted(a)) { ok = 0; break; }
-      if (++spins > kSpinLimit * 4) {
+      if (++spins > a.bar_spin_limit) {
         set_abort(a, kStatusCounterTimeout);
         ok = 0;
         break;
@@ -1659,6 +1664,9 @@ struct Consumers {
 };
 
 template <int I, int BITS>
+// 168 registers per thread at most: the register file is split over the
+// SM's four schedulers, and nine warps put three on one of them
+// (3 x 32 x 170 <= 16,384).  The code is written to that budget.
 __global__ void __launch_bounds__(kMegaThreads, 1) k_decode_mega(const MegaArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   MegaSmem& sm = *reinterpret_cast<MegaSmem*>(smem_raw);

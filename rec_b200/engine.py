@@ -116,14 +116,21 @@ class FullModel:
 
     # -- one step -------------------------------------------------------------
     def forward(self, state, token, layer_count=None):
-        """One token; returns (logits bf16[V], trace bf16[L+1, H])."""
-        if layer_count is not None and layer_count != self.cfg.n_layers:
-            raise ValueError("partial-depth forward is not supported; use the full layer count")
+        """One token through the first `layer_count` layers (all of them by
+        default); returns (logits bf16[V], trace bf16[layer_count + 1, H]),
+        as megakernel.py:1224-1301: the final norm and lm_head follow the
+        last layer run."""
+        L = self.cfg.n_layers if layer_count is None else int(layer_count)
+        if not 1 <= L <= self.cfg.n_layers:
+            raise ValueError(f"layer_count must be between 1 and {self.cfg.n_layers}")
         self.ensure_capacity(state, 1)
         sess = self._session(state)
 
         def run():
-            logits, trace = sess.step(int(token), state["position"], want_trace=True)
+            if L == self.cfg.n_layers:
+                logits, trace = sess.step(int(token), state["position"], want_trace=True)
+            else:
+                logits, trace = sess.step_layers(int(token), state["position"], L, want_trace=True)
             sess.check_status()
             return logits.clone(), trace.clone()
 
@@ -206,13 +213,13 @@ class ResidentSampler:
         if not 1 <= count <= WIDTH:
             raise ValueError("Resident packet must contain between one and eight tokens")
         self.engine.ensure_capacity(state, count)
-        if logprobs is not None:
-            raise NotImplementedError("logprobs are outside the decode hot path")
-        if grammar is not None:
-            from .sampling import grammar_block
+        if grammar is not None or logprobs is not None or (presence_penalty and temperature == 0):
+            # the reference's filtered path (kernels/sampling.py:80-96)
+            from .sampling import filtered_block
 
-            ids = grammar_block(self.engine, state, token, count, seed, grammar, temperature=temperature,
-                                top_p=top_p, top_k=top_k, presence_penalty=presence_penalty)
+            ids = filtered_block(self.engine, state, token, count, seed, temperature=temperature, top_p=top_p,
+                                 top_k=top_k, presence_penalty=presence_penalty, grammar=grammar, logprobs=logprobs,
+                                 eos=self.eos_tokens)
         elif temperature != 0:
             from .sampling import sampled_block
 

@@ -164,16 +164,43 @@ def _grammar_words(mask, words: int, device) -> torch.Tensor | None:
     return out.to(device)
 
 
-def grammar_block(engine, state, token, count, seed, grammar, *, temperature, top_p, top_k, presence_penalty):
-    """ResidentSampler.block with a grammar constraint (reference
-    masked_sampling.py:33-212 with grammar.py:46-104): every step decodes one
-    token, masks its logits with the grammar's allow words after the presence
-    penalty, samples on the device (greedy at temperature 0), and hands the
-    id to the grammar on the host, whose matcher returns the next step's mask
-    (grammar._advance(token, active), stored in state["grammar_mask"]).  The
-    packet stops after one of grammar.stops.  The matcher runs on the CPU, so
-    each token makes one host round trip (the reference orders its GPU work
-    behind the same callback)."""
+def token_logprob(logits: torch.Tensor, p: abi.RecSampling, ids: torch.Tensor, history: torch.Tensor | None = None,
+                  allow: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The reference's reported log-probability of each row's id
+    (rec_token_logprob): report = penalised, grammar-masked logits / T (or
+    the logits at T = 0); report[id] - logsumexp(report), fp32 [B]."""
+    lg = logits.reshape(1, -1) if logits.dim() == 1 else logits
+    B, V = lg.shape
+    if history is not None:
+        history = history.reshape(B, -1) if history.dim() == 1 else history
+        history = history.to(torch.int32).contiguous()
+    if allow is not None:
+        allow = allow.reshape(B, -1) if allow.dim() == 1 else allow
+    res = out if out is not None else torch.empty(B, dtype=torch.float32, device=lg.device)
+    stream = torch.cuda.current_stream().cuda_stream
+    check(lib().rec_token_logprob(C.c_void_p(lg.data_ptr()), B, V, lg.stride(0),
+                                  C.c_void_p(history.data_ptr()) if history is not None else None,
+                                  history.shape[1] if history is not None else 0, C.byref(p),
+                                  C.c_void_p(allow.data_ptr()) if allow is not None else None,
+                                  allow.stride(0) if allow is not None else 0, C.c_void_p(ids.data_ptr()),
+                                  C.c_void_p(res.data_ptr()), C.c_void_p(stream)), "rec_token_logprob")
+    return res
+
+
+def filtered_block(engine, state, token, count, seed, *, temperature, top_p, top_k, presence_penalty, grammar=None,
+                   logprobs=None, eos=()):
+    """ResidentSampler.block on the reference's filtered path
+    (kernels/sampling.py:80-96 -> masked_sampling.py:33-212): taken with a
+    grammar, with logprobs, or with a presence penalty at temperature 0.
+    Every step decodes one token, applies the presence penalty (ids sampled
+    so far, state["presence_mask"]) and the grammar's allow words, samples on
+    the device (greedy at temperature 0; otherwise the step's row of the
+    seeded uniforms, the same draws as the device-side sampled packet), and,
+    when `logprobs` is a list, appends report[id] - logsumexp(report) with
+    report = the masked, penalised logits / T.  With a grammar the id goes to
+    its host matcher (grammar._advance), whose result is the next step's mask
+    (state["grammar_mask"]), and the packet stops after one of grammar.stops;
+    without one it stops after an EOS id.  One host round trip per token."""
     sess = engine._session(state)
     V = engine.weights.cfg.vocab
     dev = sess.logits.device
@@ -184,35 +211,55 @@ def grammar_block(engine, state, token, count, seed, grammar, *, temperature, to
     if presence_penalty and mask is None:
         mask = torch.zeros(V, dtype=torch.float32, device=dev)
         state["presence_mask"] = mask
-    stops = set(int(t) for t in getattr(grammar, "stops", ()))
+    stops = set(int(t) for t in (getattr(grammar, "stops", ()) if grammar is not None else eos))
     ids_dev = torch.zeros(1, dtype=torch.int32, device=dev)
+    lp_dev = torch.zeros(1, dtype=torch.float32, device=dev)
     pos = state["position"]
 
     def run():
-        out = []
+        out, lps = [], []
         tok = int(token)
         for i in range(count):
-            allow = _grammar_words(state["grammar_mask"], words, dev)
-            if allow is None:
-                break
+            allow = None
+            if grammar is not None:
+                allow = _grammar_words(state["grammar_mask"], words, dev)
+                if allow is None:
+                    break
             logits, _ = sess.step(tok, pos + i)
             hist = torch.nonzero(mask).to(torch.int32).reshape(1, -1) if presence_penalty else None
-            sample_logits(logits.reshape(1, V), p, u[i] if u is not None else None, hist, out=ids_dev,
-                          allow=allow)
+            sample_logits(logits.reshape(1, V), p, u[i] if u is not None else None, hist, out=ids_dev, allow=allow)
+            if logprobs is not None:
+                token_logprob(logits.reshape(1, V), p, ids_dev, hist, allow, out=lp_dev)
             sess.check_status()
             tok = int(ids_dev.item())
             if tok < 0:
-                raise RuntimeError("Grammar allows no token")
+                raise RuntimeError("Grammar allows no token" if grammar is not None else "Invalid sampled chain")
             out.append(tok)
+            if logprobs is not None:
+                lps.append(float(lp_dev.item()))
             if presence_penalty:
                 mask[tok] = 1.0
-            nxt = np.asarray(grammar._advance(tok, True), dtype=np.uint32)
-            state["grammar_mask"] = np.concatenate([nxt, np.ones(1, np.uint32)])
+            if grammar is not None:
+                nxt = np.asarray(grammar._advance(tok, True), dtype=np.uint32)
+                state["grammar_mask"] = np.concatenate([nxt, np.ones(1, np.uint32)])
             if tok in stops:
                 break
-        return out
+        return out, lps
 
-    ids = engine._guard(state, run)
+    ids, lps = engine._guard(state, run)
     if not ids:
         raise RuntimeError("Grammar session is inactive")
+    if logprobs is not None:
+        logprobs.extend(lps)
     return ids
+
+
+def grammar_block(engine, state, token, count, seed, grammar, *, temperature, top_p, top_k, presence_penalty,
+                  logprobs=None):
+    """ResidentSampler.block with a grammar constraint (reference
+    masked_sampling.py:33-212 with grammar.py:46-104): filtered_block with
+    the grammar's allow words after the presence penalty.  The matcher runs
+    on the CPU, so each token makes one host round trip (the reference orders
+    its GPU work behind the same callback)."""
+    return filtered_block(engine, state, token, count, seed, temperature=temperature, top_p=top_p, top_k=top_k,
+                          presence_penalty=presence_penalty, grammar=grammar, logprobs=logprobs)

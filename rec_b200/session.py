@@ -96,6 +96,16 @@ class DecodeSession:
               "rec_decode_step")
         return (self.logits if want_logits else None), (self.trace if want_trace else None)
 
+    def step_layers(self, token: int, position: int, layer_count: int, want_trace: bool = True):
+        """One decode step through the first `layer_count` layers only
+        (rec_decode_layers); returns (logits bf16[V], trace bf16[layer_count
+        + 1, H] or None)."""
+        check(lib().rec_decode_layers(self.ctx, int(token), int(position), int(layer_count),
+                                      C.c_void_p(self.logits.data_ptr()),
+                                      C.c_void_p(self.trace.data_ptr()) if want_trace else None, self._stream()),
+              "rec_decode_layers")
+        return self.logits, (self.trace[: layer_count + 1] if want_trace else None)
+
     def prefill(self, tokens, start: int = 0) -> None:
         """Runs tokens through the decode step at positions start.. (fills the
         cache exactly as decoding would)."""

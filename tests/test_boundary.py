@@ -1,0 +1,269 @@
+"""The drop-in API's remaining contracts (reference engine/src/rec_mlx):
+
+- logprobs through ResidentSampler.block (masked_sampling.py:126-128,
+  145-146, 205-206; engine.py:264,296): the reported value is
+  report[id] - logsumexp(report), report = penalised, masked logits / T;
+- FullModel.forward(state, token, layer_count) at partial depth
+  (megakernel.py:824,861,1224-1233,1272);
+- the failure contract (megakernel.py:137-159,1264-1268,1326-1331;
+  sampling.py:77-78): a bounded device wait that runs out gives
+  RuntimeError("GPU synchronization failed ...") and state["usable"] = False,
+  and the next call raises "... invalidated ..."; the context limit and the
+  packet size give ValueError.  The wait is made to run out by one CTA that
+  skips its grid-barrier arrivals (rec_set_fault_injection), with a short
+  poll bound: nothing faults, traps or hangs.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from rec_b200 import abi
+
+
+def P(temperature=0.0, top_k=0, top_p=1.0, rep=1.0, presence=0.0):
+    return abi.RecSampling(temperature, top_k, top_p, rep, presence)
+
+
+def _reference_logprob(logits_u16, history, p, token, allowed=None):
+    """float64 restatement: report = x / T (or x), x the penalised logits
+    with disallowed ids at -inf; report[token] - logsumexp(report)."""
+    x = oracle.bf16_to_f32(logits_u16).astype(np.float64)
+    seen = np.zeros(x.size, bool)
+    h = np.asarray(history, np.int64)
+    seen[h[(h >= 0) & (h < x.size)]] = True
+    if p.repetition_penalty != 1.0:
+        x[seen] = np.where(x[seen] < 0, x[seen] * p.repetition_penalty, x[seen] / p.repetition_penalty)
+    x[seen] -= p.presence_penalty
+    if allowed is not None:
+        x = np.where(allowed, x, -np.inf)
+    r = x / p.temperature if p.temperature else x
+    m = r.max()
+    return float(r[token] - (m + np.log(np.sum(np.exp(r - m)))))
+
+
+LP_CONFIGS = {"greedy": P(), "t07": P(0.7), "t1_presence": P(1.0, 0, 1.0, 1.0, 0.5),
+              "config5": P(0.7, 40, 0.95, 1.1), "t13_rep": P(1.3, 0, 1.0, 1.2, 0.0)}
+
+
+@pytest.mark.parametrize("name", list(LP_CONFIGS))
+def test_oracle_token_logprob_matches_reference(name):
+    p = LP_CONFIGS[name]
+    rng = np.random.default_rng(len(name))
+    V = 151936
+    logits = oracle.f32_to_bf16((rng.standard_normal(V) * 3).astype(np.float32))
+    hist = rng.integers(0, V, 4096).astype(np.int32)
+    for tok in [0, int(np.argmax(oracle.bf16_to_f32(logits))), int(rng.integers(V)), V - 1]:
+        got = oracle.token_logprob(logits, hist, p, tok)
+        want = _reference_logprob(logits, hist, p, tok)
+        assert abs(got - want) <= 1e-5 * max(1.0, abs(want)), (tok, got, want)
+    assert np.isnan(oracle.token_logprob(logits, hist, p, V))
+    allowed = np.zeros(V, bool)
+    allowed[rng.integers(0, V, 500)] = True
+    allow = oracle.pack_allow(np.flatnonzero(allowed), V)
+    tok = int(np.flatnonzero(allowed)[3])
+    got = oracle.token_logprob(logits, hist, p, tok, allow=allow)
+    want = _reference_logprob(logits, hist, p, tok, allowed)
+    assert abs(got - want) <= 1e-5 * max(1.0, abs(want))
+    assert oracle.token_logprob(logits, hist, p, int(np.flatnonzero(~allowed)[0]), allow=allow) == -np.inf
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", list(LP_CONFIGS))
+def test_gpu_token_logprob_bitexact(cuda, name):
+    """rec_token_logprob against the oracle, bit for bit, for 4 rows of
+    151,936 logits (one with a grammar mask)."""
+    from rec_b200 import sampling
+
+    p = LP_CONFIGS[name]
+    rng = np.random.default_rng(100 + len(name))
+    B, V = 4, 151936
+    logits = oracle.f32_to_bf16((rng.standard_normal((B, V)) * 3).astype(np.float32))
+    hist = rng.integers(0, V, (B, 2048)).astype(np.int32)
+    ids = np.array([int(rng.integers(V)) for _ in range(B)], np.int32)
+    ids[1] = int(np.argmax(oracle.bf16_to_f32(logits[1])))
+    lg = torch.from_numpy(logits.view(np.int16)).cuda().view(torch.bfloat16)
+    out = sampling.token_logprob(lg, p, torch.from_numpy(ids).cuda(), torch.from_numpy(hist).cuda())
+    got = out.cpu().numpy()
+    for b in range(B):
+        want = oracle.token_logprob(logits[b], hist[b], p, int(ids[b]))
+        assert np.float32(want).view(np.uint32) == got[b].view(np.uint32), (b, got[b], want)
+
+
+def _tiny_engine(seed=9):
+    from rec_b200.engine import build_decoder
+    from rec_b200.model import TINY, generate_weights
+
+    w = generate_weights(TINY, seed=seed, device="cuda")
+    engine, sampler = build_decoder(w)
+    return w, engine, sampler
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("temperature", [0.0, 0.8])
+def test_gpu_resident_sampler_logprobs(cuda, temperature):
+    """ResidentSampler.block(logprobs=list): the ids equal the packet's ids
+    without logprobs, and each reported value equals the oracle's on the
+    oracle's own decode chain, bit for bit."""
+    from oracle.host import HostKV, HostModel
+    from rec_b200 import sampling
+
+    w, engine, sampler = _tiny_engine()
+    cfg = w.cfg
+    prompt, count, seed = [3, 77, 1024, 5], 6, 4321
+    kw = dict(temperature=temperature, top_p=0.9 if temperature else 1.0, top_k=30 if temperature else 0,
+              presence_penalty=0.4 if temperature else 0.0)
+
+    def run(with_lp):
+        state = engine.prefill_state(256)
+        for t in prompt[:-1]:
+            engine.forward(state, t)
+        lps = [] if with_lp else None
+        ids = sampler.block(state, prompt[-1], count, seed, logprobs=lps, **kw)
+        return ids, lps, state
+
+    fast, _, _ = run(False)
+    ids, lps, state = run(True)
+    assert ids == fast
+    assert len(lps) == len(ids)
+    assert state["position"] == len(prompt) - 1 + len(ids)
+    host = HostModel(w)
+    hkv = HostKV(cfg, 256)
+    for i, t in enumerate(prompt[:-1]):
+        host.step(hkv, t, i, want_trace=False)
+    p = sampling.params(kw["temperature"], kw["top_k"], kw["top_p"], 1.0, kw["presence_penalty"])
+    u = sampling.uniforms(count, cfg.vocab, seed, cuda).cpu().numpy() if temperature else None
+    tok, seen = prompt[-1], []
+    for i in range(len(ids)):
+        logits, _ = host.step(hkv, tok, len(prompt) - 1 + i, want_trace=False)
+        tok = oracle.sample(logits, np.array(seen, np.int32), p, u[i] if u is not None else None)
+        assert tok == ids[i]
+        want = oracle.token_logprob(logits, np.array(seen, np.int32), p, tok)
+        assert np.float32(want).view(np.uint32) == np.float32(lps[i]).view(np.uint32), (i, lps[i], want)
+        seen.append(tok)
+
+
+@pytest.mark.gpu
+def test_gpu_greedy_presence_penalty_takes_filtered_path(cuda):
+    """Temperature 0 with a presence penalty: the penalty applies before the
+    argmax (the reference routes it through its filtered sampler)."""
+    from oracle.host import HostKV, HostModel
+    from rec_b200 import sampling
+
+    w, engine, sampler = _tiny_engine(seed=13)
+    state = engine.prefill_state(256)
+    engine.forward(state, 17)
+    ids = sampler.block(state, 40, 8, 0, temperature=0.0, presence_penalty=2.0)
+    host = HostModel(w)
+    hkv = HostKV(w.cfg, 256)
+    host.step(hkv, 17, 0, want_trace=False)
+    p = sampling.params(0.0, 0, 1.0, 1.0, 2.0)
+    tok, seen, want = 40, [], []
+    for i in range(8):
+        logits, _ = host.step(hkv, tok, 1 + i, want_trace=False)
+        tok = oracle.sample(logits, np.array(seen, np.int32), p, None)
+        want.append(tok)
+        seen.append(tok)
+    assert ids == want
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("layer_count", [1, 2, 3])
+def test_gpu_forward_partial_depth(cuda, layer_count):
+    """forward(state, token, layer_count): logits and the trace of the layers
+    run equal the oracle's partial-depth step; the cache rows of the layers
+    run are written; a full step afterwards still matches."""
+    from dataclasses import replace
+
+    from oracle.host import HostKV, HostModel
+    from rec_b200.engine import FullModel
+    from rec_b200.model import TINY, generate_weights
+
+    cfg = replace(TINY, n_layers=3)
+    w = generate_weights(cfg, seed=31, device="cuda")
+    engine = FullModel(w)
+    state = engine.prefill_state(256)
+    host = HostModel(w)
+    hkv = HostKV(cfg, 256)
+    for i, t in enumerate([5, 900, 77]):
+        logits, trace = engine.forward(state, t)
+        host.step(hkv, t, i, want_trace=False)
+    logits, trace = engine.forward(state, 1234, layer_count=layer_count)
+    assert trace.shape == (layer_count + 1, cfg.hidden)
+    ref_logits, ref_trace = host.step(hkv, 1234, 3, layer_count=layer_count)
+    u16 = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)  # noqa: E731
+    assert np.array_equal(u16(trace), ref_trace)
+    assert np.array_equal(u16(logits), ref_logits)
+    kv = state["kv"].cache
+    for li in range(layer_count):
+        for name in kv.layers[li]:
+            got = kv.layers[li][name][:, 3].contiguous()
+            got = got.view(torch.int16).cpu().numpy().view(np.uint16) if got.dtype == torch.bfloat16 else \
+                got.cpu().numpy().view(np.uint32)
+            assert np.array_equal(got, hkv.layers[li][name][:, 3]), (li, name)
+    # the next full step (the deeper layers' row 3 is whatever both wrote)
+    for li in range(layer_count, cfg.n_layers):
+        for name in kv.layers[li]:
+            src = kv.layers[li][name][:, 3].contiguous()
+            src = src.view(torch.int16).cpu().numpy().view(np.uint16) if src.dtype == torch.bfloat16 else \
+                src.cpu().numpy().view(np.uint32)
+            hkv.layers[li][name][:, 3] = src
+    logits, trace = engine.forward(state, 66)
+    ref_logits, ref_trace = host.step(hkv, 66, 4)
+    assert np.array_equal(u16(trace), ref_trace)
+    assert np.array_equal(u16(logits), ref_logits)
+    with pytest.raises(ValueError):
+        engine.forward(state, 1, layer_count=0)
+    with pytest.raises(ValueError):
+        engine.forward(state, 1, layer_count=cfg.n_layers + 1)
+
+
+@pytest.mark.gpu
+def test_gpu_failure_contract(cuda, monkeypatch):
+    """A grid-barrier wait that runs out (one CTA skips its arrivals, poll
+    bound 4,096) -> RuntimeError("GPU synchronization failed") and
+    usable = False; the next call -> "invalidated"; the device and other
+    sessions stay usable."""
+    import ctypes as C
+
+    from rec_b200._lib import check, lib
+
+    monkeypatch.setenv("REC_SCHEDULE", "mega")
+    w, engine, sampler = _tiny_engine(seed=3)
+    state = engine.prefill_state(256)
+    engine.forward(state, 5)
+    sess = engine._session(state)
+    check(lib().rec_set_fault_injection(sess.ctx, 4096, 1), "rec_set_fault_injection")
+    with pytest.raises(RuntimeError, match="GPU synchronization failed"):
+        engine.forward(state, 6)
+    assert state["usable"] is False
+    with pytest.raises(RuntimeError, match="invalidated"):
+        engine.forward(state, 7)
+    with pytest.raises(RuntimeError, match="invalidated"):
+        sampler.block(state, 7, 4, 0, temperature=0)
+    # the C session refuses further work too
+    assert lib().rec_decode_step(sess.ctx, 1, 2, None, None,
+                                 C.c_void_p(torch.cuda.current_stream().cuda_stream)) == abi.REC_ESTATE
+    # a fresh state on the same device decodes normally
+    fresh = engine.prefill_state(256)
+    logits, _ = engine.forward(fresh, 5)
+    assert torch.isfinite(logits.float()).all()
+
+
+@pytest.mark.gpu
+def test_gpu_limits_and_packet_size(cuda):
+    """ValueError("Decode context limit exhausted") past the state's limit,
+    and ValueError for packets outside 1..8 (sampling.py:77-78)."""
+    w, engine, sampler = _tiny_engine(seed=4)
+    state = engine.prefill_state(256, limit=3)
+    for t in (1, 2, 3):
+        engine.forward(state, t)
+    with pytest.raises(ValueError, match="Decode context limit exhausted"):
+        engine.forward(state, 4)
+    state = engine.prefill_state(256)
+    for bad in (0, 9):
+        with pytest.raises(ValueError, match="between one and eight"):
+            sampler.block(state, 1, bad, 0, temperature=0)
+    state = engine.prefill_state(256, limit=4)
+    with pytest.raises(ValueError, match="Decode context limit exhausted"):
+        sampler.block(state, 1, 5, 0, temperature=0)
