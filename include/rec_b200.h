@@ -132,6 +132,14 @@ REC_API int rec_set_weights(RecCtx* ctx, const RecLayerWeights* layers, int32_t 
                             const RecGlobalWeights* global);
 /* capacity: KV slots per layer (multiple of 256). */
 REC_API int rec_set_kv(RecCtx* ctx, const RecKVLayer* layers, int32_t n_layers, int32_t capacity);
+/* Rows [0, rows) of every head of the cache are backed by memory; positions
+ * at or above rows are refused (REC_ELIMIT) while `capacity` stays the head
+ * stride.  For a cache reserved at its final capacity in virtual memory and
+ * backed block by block as the context grows (no copy of the rows already
+ * written; rec_b200/vmm.py).  rows: a multiple of 256, at most the capacity;
+ * rec_set_kv resets it to the capacity.  Replaces the reference's KV growth by
+ * appended bank blocks (engine/src/rec_mlx/cache.py:47-84). */
+REC_API int rec_set_kv_rows(RecCtx* ctx, int32_t rows);
 REC_API size_t rec_workspace_bytes(const RecCtx* ctx);
 REC_API int rec_set_workspace(RecCtx* ctx, void* workspace_dev, size_t bytes);
 /* One decode step: embeds `token` at `position`, runs every layer, writes

@@ -107,5 +107,6 @@ class HostKV:
         h = cls(cfg, kvcache.capacity)
         for dst, src in zip(h.layers, kvcache.layers):
             for name in dst:
-                dst[name][...] = _np(src[name])
+                a = _np(src[name])  # a reserved cache's codes cover its backed rows only
+                dst[name][:, : a.shape[1]] = a
         return h

@@ -27,6 +27,7 @@ _SIGNATURES = {
     "rec_sample_logits_masked": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int64, C.c_void_p, C.c_int32,
                                            C.POINTER(abi.RecSampling), C.c_void_p, C.c_void_p, C.c_int64,
                                            C.c_void_p, C.c_void_p]),
+    "rec_set_kv_rows": (C.c_int, [C.c_void_p, C.c_int32]),
     "rec_decode_layers": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                                     C.c_void_p]),
     "rec_set_fault_injection": (C.c_int, [C.c_void_p, C.c_uint32, C.c_int32]),

@@ -170,6 +170,8 @@ struct RecCtx {
   size_t prof_entries = 0;
   unsigned long long* prof2 = nullptr;  // optional stamps inside one layer
   int prof_layer = -1;
+  int kv_rows = 0;     // cache rows backed by memory (rec_set_kv_rows; <= capacity, the head stride)
+  int rope_done = 0;   // RoPE table rows filled (the table grows with kv_rows)
   int layers_run = 0;  // > 0: the current call runs only the first layers_run layers (rec_decode_layers)
   // failure-path tests (rec_set_fault_injection): the grid barrier's poll
   // bound, and one CTA that never arrives at a grid barrier (-1: none)
@@ -574,6 +576,7 @@ REC_API int rec_set_kv(RecCtx* c, const RecKVLayer* layers, int32_t n_layers, in
   const bool grow = capacity != c->capacity;
   c->kv.assign(layers, layers + n_layers);
   c->capacity = capacity;
+  c->kv_rows = capacity;
   const int nblk = capacity / kAttBlock;
   c->n_super_max = (nblk + kAttSuper - 1) / kAttSuper;
   if (grow) {
@@ -584,12 +587,43 @@ REC_API int rec_set_kv(RecCtx* c, const RecKVLayer* layers, int32_t n_layers, in
   return REC_OK;
 }
 
+static int fill_rope(RecCtx* c, int rows);
+
+REC_API int rec_set_kv_rows(RecCtx* c, int32_t rows) {
+  REC_CHECK_ARG(c && c->capacity > 0, "rec_set_kv_rows: set the KV cache first");
+  REC_CHECK_ARG(c->world == 1, "rec_set_kv_rows: an unsharded session only");
+  REC_CHECK_ARG(rows > 0 && rows <= c->capacity && rows % kAttBlock == 0,
+                "rec_set_kv_rows: rows %d must be a multiple of %d in (0, %d]", rows, kAttBlock, c->capacity);
+  c->kv_rows = rows;
+  return fill_rope(c, rows);
+}
+
 REC_API size_t rec_workspace_bytes(const RecCtx* c) {
   if (!c || c->capacity <= 0) return 0;
   return layout_of(c).total;
 }
 
+// RoPE table rows [rope_done, rows): cos/sin of pos * theta^(-i/64) in
+// double, rounded to float (row p = absolute position p).
+static int fill_rope(RecCtx* c, int rows) {
+  rows = rows < rope_rows(c) ? rows : rope_rows(c);
+  if (!c->rope || rows <= c->rope_done) return REC_OK;
+  const int p0 = c->rope_done;
+  std::vector<float> cs(size_t(rows - p0) * 128);
+  for (int p = p0; p < rows; ++p)
+    for (int i = 0; i < 64; ++i) {
+      const double inv = std::pow(double(c->d.rope_theta), -double(i) / 64.0);
+      const double ang = double(p) * inv;
+      cs[size_t(p - p0) * 128 + i] = float(std::cos(ang));
+      cs[size_t(p - p0) * 128 + 64 + i] = float(std::sin(ang));
+    }
+  REC_CHECK_CUDA(cudaMemcpy(c->rope + size_t(p0) * 128, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+  c->rope_done = rows;
+  return REC_OK;
+}
+
 REC_API int rec_set_workspace(RecCtx* c, void* ws, size_t bytes) {
+  int rc_rope = 0;
   REC_CHECK_ARG(c && ws, "rec_set_workspace: null argument");
   REC_CHECK_ARG(c->capacity > 0, "call rec_set_kv before rec_set_workspace");
   const Layout L = layout_of(c);
@@ -640,18 +674,10 @@ REC_API int rec_set_workspace(RecCtx* c, void* ws, size_t bytes) {
     if (c->has_weights)
       REC_CHECK_CUDA(cudaMemcpy(c->mega_layers, t.data(), t.size() * sizeof(MegaLayer), cudaMemcpyHostToDevice));
   }
-  // RoPE table: cos/sin of pos * theta^(-i/64) in double, rounded to float
-  // (row p = absolute position p)
-  const int rows = rope_rows(c);
-  std::vector<float> cs(size_t(rows) * 128);
-  for (int p = 0; p < rows; ++p)
-    for (int i = 0; i < 64; ++i) {
-      const double inv = std::pow(double(c->d.rope_theta), -double(i) / 64.0);
-      const double ang = double(p) * inv;
-      cs[size_t(p) * 128 + i] = float(std::cos(ang));
-      cs[size_t(p) * 128 + 64 + i] = float(std::sin(ang));
-    }
-  REC_CHECK_CUDA(cudaMemcpy(c->rope, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+  // RoPE table rows for the positions the cache backs (more as it grows)
+  c->rope_done = 0;
+  rc_rope = fill_rope(c, c->world > 1 ? rope_rows(c) : c->kv_rows);
+  if (rc_rope) return rc_rope;
   c->usable = true;
   drop_graph(c);
   return REC_OK;
@@ -715,7 +741,9 @@ static int select_schedule(RecCtx* c, int last_position) {
 }
 
 // Position limit of the session (global when split over ranks).
-static int position_limit(const RecCtx* c) { return c->world > 1 ? c->cap_total : c->token_base + c->capacity; }
+static int position_limit(const RecCtx* c) {
+  return c->world > 1 ? c->cap_total : c->token_base + (c->kv_rows < c->capacity ? c->kv_rows : c->capacity);
+}
 
 // One cooperative launch of the persistent kernel for `steps` tokens.
 template <int I, int BITS>

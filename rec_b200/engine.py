@@ -27,15 +27,29 @@ WIDTH = 8  # resident packet size (sampling.py:8)
 
 
 class KVStorage:
-    """Growable quantized KV storage of a state (reference cache.py:52-119)."""
+    """Growable quantized KV storage of a state (reference cache.py:47-119).
 
-    def __init__(self, weights: ModelWeights, capacity: int, device):
+    The cache's codes are reserved in virtual memory for the state's limit
+    (rounded up to 65,536-token blocks, the reference's bank size) and backed
+    block by block as the context grows (rec_b200.vmm): a growth maps new
+    memory behind the rows already written, without copying them and without
+    a new session.  A state that outgrows its reservation (a prompt cache
+    reused under a larger limit) is moved once into a larger reservation."""
+
+    def __init__(self, weights: ModelWeights, capacity: int, device, limit: int | None = None):
         self.weights = weights
         self.device = device
         self.capacity = 0
         self.cache: KVCache | None = None
         self.session: DecodeSession | None = None
+        self.reserve_rows = self._reserve(max(capacity, limit or 0))
         self.grow(capacity)
+
+    @staticmethod
+    def _reserve(n: int) -> int:
+        from .vmm import BLOCK_TOKENS
+
+        return max(BLOCK_TOKENS, -(-n // BLOCK_TOKENS) * BLOCK_TOKENS)
 
     @classmethod
     def wrap(cls, weights: ModelWeights, cache: KVCache, session: DecodeSession) -> "KVStorage":
@@ -46,21 +60,25 @@ class KVStorage:
         obj.capacity = cache.capacity
         return obj
 
-    @staticmethod
-    def _round(n: int) -> int:
-        return max(256, (n + 4095) // 4096 * 4096)
-
     def grow(self, count: int) -> None:
-        need = self._round(count)
-        if self.cache is not None and need <= self.capacity:
+        """Backs at least `count` positions."""
+        if self.cache is not None and count <= self.capacity:
             return
-        new = KVCache.allocate(self.weights.cfg, need, self.device)
-        if self.cache is not None:
-            for dst, src in zip(new.layers, self.cache.layers):
+        if self.cache is not None and self.cache.reserved is not None and count <= self.cache.capacity:
+            self.cache.grow(count)  # in place: new blocks behind the written rows
+            self.session.set_rows(self.cache.rows)
+            self.capacity = self.cache.rows
+            return
+        old = self.cache
+        self.reserve_rows = max(self.reserve_rows, self._reserve(count))
+        new = KVCache.reserve(self.weights.cfg, self.reserve_rows, count, self.device)
+        if old is not None:  # outgrew the reservation: one move into the larger one
+            for dst, src in zip(new.layers, old.layers):
                 for name in dst:
-                    dst[name][:, : self.capacity].copy_(src[name])
+                    n = min(src[name].shape[1], dst[name].shape[1])
+                    dst[name][:, :n].copy_(src[name][:, :n])
         self.cache = new
-        self.capacity = need
+        self.capacity = new.rows
         self.session = DecodeSession(self.weights, new)
 
     @property
@@ -84,7 +102,7 @@ class FullModel:
     # -- state ---------------------------------------------------------------
     def prefill_state(self, capacity, *, limit=None, storage=None):
         if storage is None:
-            storage = KVStorage(self.weights, capacity, self.device)
+            storage = KVStorage(self.weights, capacity, self.device, limit=limit)
         else:
             storage.grow(capacity)
         return {"usable": True, "kv": storage, "metadata": None, "position": 0, "initial": 0,

@@ -197,10 +197,56 @@ def generate_weights(cfg: ModelConfig, seed: int = 0, device: str | torch.device
 
 @dataclass
 class KVCache:
-    """Quantized KV storage for every layer, capacity C (multiple of 256)."""
+    """Quantized KV storage for every layer, capacity C (multiple of 256).
+    A cache made by `reserve` has its codes in reserved virtual memory
+    (rec_b200.vmm): C is the head stride, only rows [0, rows) are backed, and
+    `grow` backs more rows in place; the tensors in `layers` then cover the
+    backed rows."""
     cfg: ModelConfig
     capacity: int
     layers: list[dict]
+    reserved: list | None = None  # per layer {"k_codes": ReservedCodes, "v_codes": ...}
+    rows: int = 0                 # backed rows (== capacity for an ordinary cache)
+
+    def __post_init__(self):
+        if not self.rows:
+            self.rows = self.capacity
+
+    @classmethod
+    def reserve(cls, cfg: ModelConfig, capacity: int, rows: int, device="cuda") -> "KVCache":
+        """Codes reserved for `capacity` rows (a multiple of 65,536) and backed
+        for `rows`; scales and biases allocated for the full capacity."""
+        from .vmm import ReservedCodes
+
+        words = 128 * cfg.kv_bits // 32
+        dev = torch.device(device)
+        layers, reserved = [], []
+        for _ in range(cfg.n_layers):
+            R = {n: ReservedCodes(cfg.n_kv_heads, capacity, words, dev) for n in ("k_codes", "v_codes")}
+            L = {}
+            for kv in ("k", "v"):
+                L[f"{kv}_codes"] = None
+                L[f"{kv}_scales"] = torch.zeros(cfg.n_kv_heads, capacity, 2, dtype=torch.bfloat16, device=dev)
+                L[f"{kv}_biases"] = torch.zeros(cfg.n_kv_heads, capacity, 2, dtype=torch.bfloat16, device=dev)
+            layers.append(L)
+            reserved.append(R)
+        obj = cls(cfg, capacity, layers, reserved, rows=1)
+        obj.rows = 0
+        obj.grow(rows)
+        return obj
+
+    def grow(self, rows: int) -> None:
+        """Backs rows [0, rows) of a reserved cache (rows already written stay
+        in place)."""
+        if self.reserved is None:
+            raise ValueError("only a reserved cache grows in place")
+        if rows <= self.rows:
+            return
+        for L, R in zip(self.layers, self.reserved):
+            for n, rc in R.items():
+                rc.grow(rows)
+                L[n] = rc.view()
+        self.rows = self.reserved[0]["k_codes"].rows
 
     @classmethod
     def allocate(cls, cfg: ModelConfig, capacity: int, device="cuda") -> "KVCache":
@@ -223,7 +269,15 @@ class KVCache:
                                                        "v_biases"))) for L in self.layers])
         return arr
 
+    def view(self, layer: int, name: str, upto: int | None = None) -> torch.Tensor:
+        """Tensor `name` of a layer restricted to rows [0, upto) (default: the
+        backed rows)."""
+        n = self.rows if upto is None else min(upto, self.rows)
+        return self.layers[layer][name][:, :n]
+
     def nbytes(self) -> int:
+        """Bytes of device memory the cache holds (backed rows only for
+        reserved codes)."""
         return sum(t.numel() * t.element_size() for L in self.layers for t in L.values())
 
     def fill_random(self, upto: int, seed: int = 0, start: int = 0) -> None:

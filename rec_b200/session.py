@@ -36,6 +36,8 @@ class DecodeSession:
               "rec_set_weights")
         self._kv = kv.rec()
         check(lib().rec_set_kv(self.ctx, self._kv, len(kv.layers), kv.capacity), "rec_set_kv")
+        if kv.rows < kv.capacity:
+            check(lib().rec_set_kv_rows(self.ctx, kv.rows), "rec_set_kv_rows")
         if plan is not None:
             self._setup_exchange(group)
         nbytes = lib().rec_workspace_bytes(self.ctx)
@@ -74,6 +76,11 @@ class DecodeSession:
             self._shard.exchange[q] = p
         check(lib().rec_set_shard(self.ctx, C.byref(self._shard)), "rec_set_shard")
         dist.barrier(group=group)
+
+    def set_rows(self, rows: int) -> None:
+        """The cache now backs rows [0, rows) (a reserved cache that grew in
+        place; rec_set_kv_rows)."""
+        check(lib().rec_set_kv_rows(self.ctx, int(rows)), "rec_set_kv_rows")
 
     def __del__(self):
         ctx = getattr(self, "ctx", None)
