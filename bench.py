@@ -53,6 +53,7 @@ def parse():
     p.add_argument("--prefill", action="store_true",
                    help="the tensor-core prefill projections (rec_prefill_gemm) of one config-3 layer")
     p.add_argument("--tokens", default="1024,4096", help="prompt lengths for --prefill")
+    p.add_argument("--ttft-tokens", default="1024,32768", help="prompt lengths of the --prefill time-to-first-token rows")
     p.add_argument("--sample-head", action="store_true",
                    help="config 5: final RMSNorm + int4 lm_head + penalty/top-k/top-p sampler, batch 1 and 8")
     p.add_argument("--shard", action="store_true",
@@ -675,9 +676,32 @@ def run_prefill(args):
         rows.append({"tokens": T, "gemm": "moe_block_grouped (E 128, top-8, gate+up+down, gather, SwiGLU, mix)",
                      "us": round(us, 2), "TFLOPs": round(tf, 1), "frac": round(tf / peak, 4)})
         del gt, ut, dt, ws
+    # time to first token of the config-3 model through the public API
+    # (QATSession.prefill: chunks of 1,024 tokens through rec_prefill_chunk)
+    from rec_b200.engine import FullModel
+    from rec_b200.model import CONFIG3, generate_weights
+
+    weights = generate_weights(CONFIG3, seed=0, device="cuda")
+    engine = FullModel(weights)
+    ttft = []
+    for T in [int(t) for t in args.ttft_tokens.split(",")]:
+        tokens = torch.randint(0, CONFIG3.vocab, (T,), generator=torch.Generator().manual_seed(1)).tolist()
+        engine.make_session(max_new_tokens=8).prefill(tokens[:1024])  # warm: workspace and code paths
+        torch.cuda.synchronize()
+        sess = engine.make_session(max_new_tokens=8)
+        t0 = time.perf_counter()
+        logits = sess.prefill(tokens)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        ttft.append({"prompt_tokens": T, "ttft_ms": round(dt * 1e3, 1), "prompt_tokens_per_s": round(T / dt, 1),
+                     "next_id": int(torch.argmax(logits.float()))})
+        del sess
+        torch.cuda.empty_cache()
     print(json.dumps({"workload": "prefill_projections_tcgen05", "peak_TFLOPs": peak, "peak_source": kind,
-                      "steps": args.steps, "dtype": "bf16 x bf16 -> fp32 (int4 g64 weights dequantized in smem)",
-                      "rows": rows}), flush=True)
+                      "steps": args.steps, "dtype": "bf16 activations x (bf16 w_hi + bf16 w_lo) -> fp32 "
+                      "(int4 g64 weights dequantized in smem)", "rows": rows,
+                      "ttft_config3": ttft, "ttft_api": "rec_b200.engine.QATSession.prefill (chunks of 1,024)"}),
+          flush=True)
 
 
 def run_sample_head(args):

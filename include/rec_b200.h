@@ -361,6 +361,35 @@ REC_API int rec_lmhead_sample(const RecQMat* lm_head, int32_t scale_dtype, int32
                               const void* h_dev, int32_t batch, const void* final_norm_dev, float eps,
                               const int32_t* history_dev, int32_t history_len, const RecSampling* params,
                               const float* uniforms_dev, void* logits_dev, int32_t* ids_dev, void* stream);
+/* Workspace (bytes) of rec_prefill_chunk for a chunk of t tokens. */
+REC_API size_t rec_prefill_workspace_bytes(const RecCtx* ctx, int32_t t);
+/* Chunked prompt prefill: the t tokens of tokens_dev (int32) at positions
+ * [position, position + t) through every layer of the session -- embedding,
+ * RMSNorm, q / k / v / o projections and the MoE block on the tensor cores
+ * (rec_prefill_gemm, rec_prefill_moe), q / k head norms and RoPE, the chunk's
+ * K / V quantized into the cache (rec_kv_append_bulk), causal attention of
+ * every token over the quantized cache at positions 0 .. its own, the
+ * router of every token -- and, when logits_dev is non-NULL, the bf16 logits
+ * of the last token (final norm + lm_head).  The cache rows then hold what
+ * the chunk wrote, and decoding continues at position + t.  Dense work
+ * accumulates in fp32 on the tensor cores, so results match the
+ * token-by-token decode within a tolerance, not bit for bit.  workspace:
+ * 256-byte aligned, rec_prefill_workspace_bytes(ctx, t) bytes.  Unsharded
+ * sessions, hidden 2048.  Replaces QATSession.prefill's chunk step
+ * (engine/src/rec_mlx/quantized.py:102-148; m4_max_prefill.py:6-104;
+ * kernels/m4_max_prefill.py:49-144). */
+REC_API int rec_prefill_chunk(RecCtx* ctx, const int32_t* tokens_dev, int32_t position, int32_t t, void* logits_dev,
+                              void* workspace, size_t workspace_bytes, void* stream);
+/* The causal attention step of rec_prefill_chunk alone: q_dev bf16 [t,
+ * n_q_heads, 128] (RoPE'd, not scaled) at positions [position, position + t)
+ * attends over cache rows 0 .. its own position (the chunk's rows already
+ * appended): scores bf16(bf16(q / sqrt(128)) . k), fp32 softmax with the
+ * optional sink logit, P . V with fp16 P and V, fp32 accumulation; out bf16
+ * [t, n_q_heads * 128].  Replaces the prefill path of
+ * quantized_attention_with_sinks (engine/src/rec_mlx/model.py:108-139). */
+REC_API int rec_prefill_attention(const void* q_dev, int32_t n_q_heads, int32_t n_kv_heads, const RecKVLayer* kv,
+                                  int32_t capacity, int32_t kv_bits, int32_t position, int32_t t, const void* sinks_dev,
+                                  void* out_dev, void* stream);
 /* Prefill projection on the tensor cores: Y[t, n] = X[t, k] . W[n, k]^T with
  * X bf16 [t, k] row-major (16-byte aligned), W int4 g64 (MLX affine layout,
  * scale_dtype scales and biases), Y bf16 [t, n].  n a multiple of 256, k a

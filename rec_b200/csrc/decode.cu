@@ -19,6 +19,7 @@
 #include "capi_common.h"
 #include "mega.cuh"
 #include "moe.cuh"
+#include "prefill_layer.h"
 #include "sample.cuh"
 
 namespace rec {
@@ -916,6 +917,125 @@ REC_API int rec_decode_layers(RecCtx* c, int32_t token, int32_t position, int32_
   if (trace_dev)
     REC_CHECK_CUDA(cudaMemcpyAsync(trace_dev, c->trace, size_t(layer_count + 1) * c->d.hidden * 2,
                                    cudaMemcpyDeviceToDevice, st));
+  return REC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Chunked prompt prefill (quantized.py:102-148): t tokens at positions
+// [position, position + t) through every layer, dense work on the tensor cores
+// (rec_prefill_gemm, rec_prefill_moe), causal attention over the quantized
+// cache (prefill_layer.cu), the chunk's K / V quantized into the cache
+// (rec_kv_append_bulk); optionally the last token's logits.
+// ---------------------------------------------------------------------------
+namespace {
+struct PrefillLayout {
+  size_t h, xn, q, k, v, att, o, ids, wts, moe, total;
+  size_t moe_bytes;
+};
+PrefillLayout prefill_layout(const RecModelDesc& d, int64_t t) {
+  PrefillLayout L;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align_up(off + bytes, 256);
+    return at;
+  };
+  const size_t H = size_t(d.hidden), Q = size_t(d.n_q_heads) * 128, KV = size_t(d.n_kv_heads) * 128;
+  L.h = take(size_t(t) * H * 2);
+  L.xn = take(size_t(t) * H * 2);
+  L.q = take(size_t(t) * Q * 2);
+  L.k = take(size_t(t) * KV * 2);
+  L.v = take(size_t(t) * KV * 2);
+  L.att = take(size_t(t) * Q * 2);
+  L.o = take(size_t(t) * H * 2);
+  L.ids = take(size_t(t) * d.top_k * 4);
+  L.wts = take(size_t(t) * d.top_k * 4);
+  L.moe_bytes = rec_prefill_moe_workspace_bytes(t, d.top_k, d.hidden, d.moe_inter, d.n_experts);
+  L.moe = take(L.moe_bytes);
+  L.total = off;
+  return L;
+}
+}  // namespace
+
+REC_API size_t rec_prefill_workspace_bytes(const RecCtx* c, int32_t t) {
+  if (!c || t <= 0) return 0;
+  return prefill_layout(c->d, t).total;
+}
+
+REC_API int rec_prefill_chunk(RecCtx* c, const int32_t* tokens_dev, int32_t position, int32_t t, void* logits_dev,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_ready(c);
+  if (rc) return rc;
+  const RecModelDesc& d = c->d;
+  REC_CHECK_ARG(tokens_dev && workspace, "rec_prefill_chunk: null pointer");
+  REC_CHECK_ARG(c->world == 1, "rec_prefill_chunk: an unsharded session only");
+  REC_CHECK_ARG(d.hidden == 2048 && d.moe_inter % 256 == 0, "rec_prefill_chunk: hidden 2048 and I a multiple of 256");
+  REC_CHECK_ARG(t >= 1 && t <= 16384, "rec_prefill_chunk: %d tokens outside 1..16384", t);
+  if (position < 0 || int64_t(position) + t > position_limit(c)) {
+    set_error("Decode context limit exhausted");
+    return REC_ELIMIT;
+  }
+  const PrefillLayout L = prefill_layout(d, t);
+  REC_CHECK_ARG(workspace_bytes >= L.total && (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
+                "rec_prefill_chunk: workspace must be 256-byte aligned and hold %zu bytes", L.total);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  uint16_t* h = reinterpret_cast<uint16_t*>(w + L.h);
+  uint16_t* xn = reinterpret_cast<uint16_t*>(w + L.xn);
+  uint16_t* q = reinterpret_cast<uint16_t*>(w + L.q);
+  uint16_t* k = reinterpret_cast<uint16_t*>(w + L.k);
+  uint16_t* v = reinterpret_cast<uint16_t*>(w + L.v);
+  uint16_t* att = reinterpret_cast<uint16_t*>(w + L.att);
+  uint16_t* o = reinterpret_cast<uint16_t*>(w + L.o);
+  int* ids = reinterpret_cast<int*>(w + L.ids);
+  float* wts = reinterpret_cast<float*>(w + L.wts);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int* status = c->ctl + kCtlStatus;
+  const int sd = d.scale_dtype;
+  const int H = d.hidden, Q = d.n_q_heads * 128, KV = d.n_kv_heads * 128;
+  const QMatDev emb = {(const uint32_t*)c->g.embed.w, (const uint16_t*)c->g.embed.scales,
+                       (const uint16_t*)c->g.embed.biases};
+  REC_CHECK_CUDA(pf_embed(emb, sd == REC_SCALE_BF16 ? 1 : 0, tokens_dev, t, H, d.vocab, h, status, st));
+  const bool qk = (d.flags & REC_FLAG_QK_NORM) != 0, sinks = (d.flags & REC_FLAG_SINKS) != 0;
+  for (int l = 0; l < d.n_layers; ++l) {
+    const RecLayerWeights& W = c->layers[l];
+    REC_CHECK_CUDA(pf_rmsnorm(h, (const uint16_t*)W.input_norm, t, d.rms_eps, xn, st));
+    if ((rc = rec_prefill_gemm(&W.q, sd, Q, H, xn, t, q, status, st))) return rc;
+    if ((rc = rec_prefill_gemm(&W.k, sd, KV, H, xn, t, k, status, st))) return rc;
+    if ((rc = rec_prefill_gemm(&W.v, sd, KV, H, xn, t, v, status, st))) return rc;
+    REC_CHECK_CUDA(pf_qk(q, d.n_q_heads, k, d.n_kv_heads, t, position, c->rope,
+                         qk ? (const uint16_t*)W.q_norm : nullptr, qk ? (const uint16_t*)W.k_norm : nullptr,
+                         d.rms_eps, st));
+    if ((rc = rec_kv_append_bulk(&c->kv[l], d.n_kv_heads, c->capacity, d.kv_bits, k, v, position, t, st)))
+      return rc;
+    REC_CHECK_CUDA(pf_attention(q, d.n_q_heads, d.n_kv_heads, c->kv[l], c->capacity, d.kv_bits, position, t,
+                                sinks ? (const uint16_t*)W.sinks : nullptr, att, st));
+    if ((rc = rec_prefill_gemm(&W.o, sd, H, Q, att, t, o, status, st))) return rc;
+    REC_CHECK_CUDA(pf_add(h, o, size_t(t) * H, st));
+    REC_CHECK_CUDA(pf_rmsnorm(h, (const uint16_t*)W.post_norm, t, d.rms_eps, xn, st));
+    REC_CHECK_CUDA(pf_router(xn, (const uint16_t*)W.router, (const float*)W.expert_bias, t, d.n_experts, d.top_k,
+                             d.router_mode, ids, wts, st));
+    if ((rc = rec_prefill_moe(&W.gate, &W.up, &W.down, sd, d.n_experts, d.moe_inter, H, xn, t, d.top_k, ids, wts, h,
+                              h, w + L.moe, L.moe_bytes, status, st)))
+      return rc;
+  }
+  if (logits_dev)
+    return rec_gemv_int4(&c->g.lm_head, sd, d.vocab, H, h + size_t(t - 1) * H, c->g.final_norm, d.rms_eps, logits_dev,
+                         st);
+  return REC_OK;
+}
+
+REC_API int rec_prefill_attention(const void* q_dev, int32_t n_q_heads, int32_t n_kv_heads, const RecKVLayer* kv,
+                                  int32_t capacity, int32_t kv_bits, int32_t position, int32_t t, const void* sinks_dev,
+                                  void* out_dev, void* stream) {
+  REC_CHECK_ARG(q_dev && kv && out_dev, "rec_prefill_attention: null pointer");
+  REC_CHECK_ARG(n_kv_heads >= 1 && n_q_heads == 8 * n_kv_heads, "rec_prefill_attention: 8 q heads per kv head");
+  REC_CHECK_ARG(kv_bits == 4 || kv_bits == 8, "rec_prefill_attention: kv_bits 4 or 8");
+  REC_CHECK_ARG(t >= 1 && position >= 0 && int64_t(position) + t <= capacity,
+                "rec_prefill_attention: positions [%d, %d) outside the capacity %d", position, position + t, capacity);
+  REC_CHECK_ARG(aligned16(kv->k_codes) && aligned16(kv->v_codes), "rec_prefill_attention: codes 16-byte aligned");
+  REC_CHECK_CUDA(pf_attention(static_cast<const uint16_t*>(q_dev), n_q_heads, n_kv_heads, *kv, capacity, kv_bits,
+                              position, t, static_cast<const uint16_t*>(sinks_dev), static_cast<uint16_t*>(out_dev),
+                              static_cast<cudaStream_t>(stream)));
   return REC_OK;
 }
 

@@ -453,7 +453,7 @@ struct MixArgs {
   int pdl;
 };
 
-__global__ void __launch_bounds__(kThreads) k_mix(const MixArgs a) {
+static __global__ void __launch_bounds__(kThreads) k_mix(const MixArgs a) {
   if (a.pdl) grid_wait();
   grid_launch_dependents();
   for (int i = blockIdx.x * kThreads + threadIdx.x; i < a.H; i += gridDim.x * kThreads) {

@@ -30,8 +30,8 @@ class KVStorage:
     """Growable quantized KV storage of a state (reference cache.py:47-119).
 
     The cache's codes are reserved in virtual memory for the state's limit
-    (rounded up to 65,536-token blocks, the reference's bank size) and backed
-    block by block as the context grows (rec_b200.vmm): a growth maps new
+    (rounded up to 32,768-token blocks; the reference's bank blocks hold
+    65,536) and backed block by block as the context grows (rec_b200.vmm): a growth maps new
     memory behind the rows already written, without copying them and without
     a new session.  A state that outgrows its reservation (a prompt cache
     reused under a larger limit) is moved once into a larger reservation."""
@@ -71,7 +71,14 @@ class KVStorage:
             return
         old = self.cache
         self.reserve_rows = max(self.reserve_rows, self._reserve(count))
-        new = KVCache.reserve(self.weights.cfg, self.reserve_rows, count, self.device)
+        from .vmm import BLOCK_TOKENS
+
+        if self.reserve_rows <= BLOCK_TOKENS:
+            # a limit within one block: the whole cache at once (one ordinary
+            # allocation, no mapping calls on the prefill's critical path)
+            new = KVCache.allocate(self.weights.cfg, self.reserve_rows, self.device)
+        else:
+            new = KVCache.reserve(self.weights.cfg, self.reserve_rows, count, self.device)
         if old is not None:  # outgrew the reservation: one move into the larger one
             for dst, src in zip(new.layers, old.layers):
                 for name in dst:
@@ -156,18 +163,26 @@ class FullModel:
         state["position"] += 1
         return out
 
-    def make_session(self, *, max_new_tokens=512) -> "QATSession":
-        return QATSession(self, max_new_tokens)
+    def make_session(self, *, max_new_tokens=512, prefill_mode: str = "chunked") -> "QATSession":
+        return QATSession(self, max_new_tokens, prefill_mode)
 
 
 class QATSession:
-    """Prefill + scalar decode (reference quantized.py:98-151).  Prefill runs
-    the prompt through the decode step token by token (exact: the cache holds
-    what decoding would have written)."""
+    """Prefill + scalar decode (reference quantized.py:98-151).  The prompt is
+    prefilled in chunks of engine.prefill_chunk_size tokens through
+    rec_prefill_chunk: projections and experts on the tensor cores, causal
+    attention over the quantized cache.  Its results match the token-by-token
+    decode path within a tolerance (fp32 tensor-core accumulation) and do not
+    depend on where the chunks are cut.  prefill_mode="decode" runs the prompt
+    through the decode step token by token instead (the cache then holds
+    exactly what decoding would have written)."""
 
     context_limit = 262144
 
-    def __init__(self, engine: FullModel, max_new_tokens: int):
+    def __init__(self, engine: FullModel, max_new_tokens: int, prefill_mode: str = "chunked"):
+        if prefill_mode not in ("chunked", "decode"):
+            raise ValueError("prefill_mode must be 'chunked' or 'decode'")
+        self.prefill_mode = prefill_mode
         self.engine, self.maximum = engine, max_new_tokens
         self._state = None
         self.cached_tokens = 0
@@ -200,8 +215,11 @@ class QATSession:
                 raise PrefillCancelled()
             self.prompt_cache.checkpoint()
             part = tokens[begin:begin + chunk]
-            for i, t in enumerate(part):
-                out, _ = sess.step(t, begin + i, want_logits=i == len(part) - 1)
+            if self.prefill_mode == "chunked":
+                out = self.engine._guard(state, lambda: sess.prefill_chunk(part, begin))
+            else:
+                for i, t in enumerate(part):
+                    out, _ = sess.step(t, begin + i, want_logits=i == len(part) - 1)
             self.engine._guard(state, sess.check_status)
             logits = out.clone()
             self.prompt_cache.advance(part, logits)

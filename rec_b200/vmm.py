@@ -7,7 +7,7 @@ reference appends separate 65,536-token bank blocks instead
 (engine/src/rec_mlx/cache.py:47-84) and its kernel indexes the block of each
 token.  Here the whole final capacity C is reserved as one virtual address
 range (cuMemAddressReserve), and physical memory is created and mapped for
-each head's rows one 65,536-token block at a time as the context grows
+each head's rows one 32,768-token block at a time as the context grows
 (cuMemCreate / cuMemMap / cuMemSetAccess).  The kernels keep their flat
 [Hkv, C, words] addressing with C as the head stride, no row already written
 moves or is copied, and memory is committed only for the blocks in use.
@@ -22,7 +22,7 @@ from __future__ import annotations
 
 import torch
 
-BLOCK_TOKENS = 65536  # rows mapped per growth step (the reference's bank block)
+BLOCK_TOKENS = 32768  # rows mapped per growth step (4 MB per head at 8 bits, 2 MB at 4 bits)
 
 
 def _driver():
@@ -87,8 +87,10 @@ class ReservedCodes:
         self._access = acc
 
     def grow(self, rows: int) -> None:
-        """Backs rows [0, rows) (rounded up to whole blocks) of every head;
-        new rows are zeroed."""
+        """Backs rows [0, rows) (rounded up to whole blocks) of every head.
+        New rows are not cleared: every row is written (quantize-on-append)
+        before attention reads it, and the kernels mask the rows of a
+        partly filled 4-row group by position, never by their contents."""
         cu = _driver()
         need = -(-rows // BLOCK_TOKENS) * BLOCK_TOKENS
         if need > self.capacity:
@@ -106,8 +108,6 @@ class ReservedCodes:
                 self._handles.append((va, self.block_bytes, handle))
                 _ok(cu.cuMemSetAccess(va, self.block_bytes, [self._access], 1), "cuMemSetAccess")
             self.rows += BLOCK_TOKENS
-            blk = self.view()[:, b * BLOCK_TOKENS:(b + 1) * BLOCK_TOKENS]
-            blk.zero_()
 
     def view(self) -> torch.Tensor:
         """int32 [heads, rows, words] over the backed rows (head stride =

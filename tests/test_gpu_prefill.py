@@ -1,8 +1,8 @@
 """The tensor-core prefill projection (rec_prefill_gemm, tcgen05) against an
-fp64 GEMM of the dequantized int4 weights.  The weights are dequantized to
-bf16 before the MMA (~2^-9 relative per weight) and Y is rounded to bf16, so
-the bound is a relative L2 error of 4e-3 per row (measured ~1.6e-3 for
-random inputs) and no element off by more than 2% of its row's RMS."""
+fp64 GEMM of the dequantized int4 weights.  Each dequantized weight enters
+the MMAs as two bf16 parts (~16 significant bits) and Y is rounded to bf16,
+so the bound is a relative L2 error of 4e-3 per row and no element off by
+more than 2% of its row's RMS."""
 import ctypes as C
 
 import numpy as np
@@ -62,11 +62,12 @@ def test_prefill_moe_matches_fp64(cuda, T, k, E, H, I):
     against an fp64 restatement with the same bf16 rounding points: g, u and
     d rounded to bf16, act = bf16(bf16(g * bf16(sigmoid g)) * u), the mix in
     rank order with a bf16 rounding after each add, then the residual.  The
-    weights are compared as the kernel uses them (dequantized, then bf16);
-    the remaining difference is fp32 vs fp64 accumulation, which flips a
-    bf16 rounding now and then: per token a relative L2 error below 2e-3,
-    no output off by more than 2^-5 (the outputs are O(1)), fewer than 1% of
-    them off at all.  The last expert gets no token."""
+    kernel multiplies each dequantized weight as w_hi + w_lo (two bf16
+    parts, ~16 significant bits), so the reference uses the dequantized
+    weights unrounded; the remaining difference is fp32 vs fp64 accumulation,
+    which flips a bf16 rounding now and then: per token a relative L2 error
+    below 2e-3, no output off by more than 2^-5 (the outputs are O(1)), fewer
+    than 1% of them off at all.  The last expert gets no token."""
     from rec_b200._lib import check, lib
 
     sd = 0
@@ -75,7 +76,7 @@ def test_prefill_moe_matches_fp64(cuda, T, k, E, H, I):
     def qmat(rows, cols):
         w = (0.02 * rng.standard_normal((rows, cols))).astype(np.float32)
         c, s, b = oracle.quantize(w, 4, sd)
-        wd = _bf(oracle.dequantize(c, s, b, 4, sd).reshape(rows, cols))
+        wd = oracle.dequantize(c, s, b, 4, sd).reshape(rows, cols).astype(np.float64)
         return (c.reshape(rows, -1), s.reshape(rows, -1), b.reshape(rows, -1)), wd
 
     (gq, gw), (uq, uw), (dq, dw) = qmat(E * I, H), qmat(E * I, H), qmat(E * H, I)
