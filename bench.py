@@ -62,6 +62,9 @@ def parse():
     p.add_argument("--config1", action="store_true",
                    help="config 1: one decoder layer (64 experts top-8, 1,024-token 8-bit cache) per decode step")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-config4", action="store_true",
+                   help="skip the config-4 measurement (258,048 tokens, 4-bit cache) that follows the main one")
+    p.add_argument("--config4-steps", type=int, default=32)
     p.add_argument("--profile-phases", action="store_true",
                    help="also record the persistent kernel's phase timeline (printed to stderr)")
     return p.parse_args()
@@ -163,7 +166,7 @@ def run_rec(args):
         lo, hi = (plan.token_base, min(plan.token_end, ctx0 - 1)) if plan else (0, ctx0 - 1)
         if hi > lo:
             kv.fill_random(hi - lo, seed=2)  # positions [lo, hi) of this rank's cache
-    sess = DecodeSession(weights, kv, plan=plan)
+    sess = DecodeSession(weights, kv, plan=plan, shard_schedule="graph" if (plan and fill) else "mega")
     if not fill:
         # prefill: the prompt through the decode step
         sess.prefill(prompt[:-1])
@@ -374,6 +377,14 @@ def run_rec(args):
            "positions": [e2e_start + 8, e2e_start + 8 + produced]}
 
 
+    # ---- config 4 (the same model at 258,048 tokens, 4-bit cache): one GPU
+    # at N = 1; at N > 1 one session split over all ranks (experts
+    # expert-parallel, KV split along the sequence, exchanges over NVLink)
+    config4 = None
+    if not args.no_config4 and not sharded and ctx0 <= 4096:
+        del sess, kv, engine, storage
+        torch.cuda.empty_cache()
+        config4 = measure_config4(args, weights, world, rank, barrier)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -404,8 +415,76 @@ def run_rec(args):
         "phases_us": phases,
         "cpu_baseline": cpu,
         "parity": parity,
+        ("config4_1gpu" if world == 1 else "config4_sharded"): config4,
     }
     print(json.dumps(out), flush=True)
+
+
+def measure_config4(args, weights3, world, rank, barrier):
+    """Config 4: greedy decode at 258,048 tokens with a 4-bit cache of
+    quantized synthetic K, V ~ N(0, 1) (the reference's chunked prefill of a
+    252K prompt is not on this path).  N = 1: one GPU, the schedule the
+    session picks there (the CUDA graph of standalone kernels).  N > 1: one
+    session split over the ranks on the sharded graph schedule: rank r holds
+    experts [r E/N, (r+1) E/N) and a contiguous range of 16,384-token
+    super-chunks; the attention partials and the expert outputs cross NVLink
+    as peer stores into each rank's exchange buffer.  Timed with CUDA events
+    over `--config4-steps` steps, max over ranks."""
+    from dataclasses import replace
+
+    import torch
+    import torch.distributed as dist
+
+    from rec_b200 import shard
+    from rec_b200._lib import check, lib
+    from rec_b200.model import CONFIG4, KVCache, generate_weights
+    from rec_b200.session import DecodeSession
+
+    ctx, K, W = 258048, args.config4_steps, 3
+    cap = (ctx + W + K + 255) // 256 * 256
+    plan = shard.plan(world, rank, CONFIG4.n_experts, cap) if world > 1 else None
+    if plan is None:
+        weights = replace(weights3, cfg=CONFIG4)  # the same tensors; only the cache format differs
+        kv = KVCache.allocate(CONFIG4, cap)
+        kv.fill_random(ctx, seed=2)
+        sess = DecodeSession(weights, kv)
+        schedule = {0: "persistent kernel", 1: "graph", 2: "split"}[lib().rec_schedule_for(sess.ctx, ctx)]
+    else:
+        weights = generate_weights(CONFIG4, seed=0, device="cuda", expert_range=(plan.expert_lo, plan.expert_hi))
+        kv = KVCache.allocate(CONFIG4, plan.local_capacity)
+        lo, hi = plan.token_base, min(plan.token_end, ctx)
+        if hi > lo:
+            kv.fill_random(hi - lo, seed=2)
+        sess = DecodeSession(weights, kv, plan=plan, shard_schedule="graph")
+        schedule = f"sharded graph over {world} GPUs"
+    stream = torch.cuda.current_stream()
+
+    def run(n, token, position):
+        done = 0
+        while done < n:
+            c = min(PACKET, n - done)
+            check(lib().rec_decode_greedy(sess.ctx, token if done == 0 else -1, position + done, c, None, 0,
+                                          sess.ids.data_ptr(), sess.produced.data_ptr(), stream.cuda_stream))
+            done += c
+
+    run(W, 1000, ctx)
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    run(K, -1, ctx + W)
+    b.record(stream)
+    barrier()
+    sess.check_status()
+    t = torch.tensor([a.elapsed_time(b) / 1e3], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dt = float(t.item())
+    ids = sess.ids[: min(K, PACKET)].tolist()
+    del sess, kv
+    torch.cuda.empty_cache()
+    return {"tokens_per_s": round(K / dt, 2), "ms_per_step": round(dt / K * 1e3, 3), "n_gpus": world,
+            "context": ctx, "kv_bits": 4, "steps": K, "schedule": schedule,
+            "cache": "synthetic K, V ~ N(0,1) quantized", "first_ids": ids[:8]}
 
 
 def host_threads() -> int:

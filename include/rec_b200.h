@@ -208,6 +208,10 @@ typedef struct RecShard {
   int32_t super_lo, super_hi;
   int32_t capacity_total;  /* global context capacity (positions), multiple of 256 */
   void* exchange[8];       /* rank q's exchange buffer as mapped in this process */
+  int32_t schedule;        /* 0: the persistent kernel; 1: the graph of standalone kernels
+                              (attention on each rank's KV with the standalone kernel, the
+                              super-chunk and expert-output exchanges as separate kernels);
+                              fixed for the session's lifetime */
 } RecShard;
 REC_API int rec_set_shard(RecCtx* ctx, const RecShard* shard);
 REC_API size_t rec_exchange_bytes(const RecCtx* ctx);

@@ -105,3 +105,105 @@ def expert_mix(down: np.ndarray, weights: np.ndarray) -> np.ndarray:
         t = rbf(down[r] * rbf(np.float32(weights[r])))
         m = t if m is None else rbf(t + m)
     return m
+
+
+# ---------------------------------------------------------------- whole model
+# The native MLX decoder (recursive-oss/rec engine/src/rec_mlx/model.py) in
+# float64 with the reference's bf16 rounding points: every projection output,
+# the RoPE'd q / k, the attention output (model.py:108-139), the residual
+# adds (model.py:269-271), the router logit (mixed_bits.py:32-38), the SwiGLU
+# activation and the rank-order expert mix (mixed_bits.py:42-54), the logits.
+# Quantized tensors are dequantized exactly (float32 affine, as MLX does).
+# Used to bound the canonical fixed-point order (oracle/rec_oracle.c, and so
+# the GPU) against the reference's semantics at layer and model scale.
+
+def _dq(qt, sd: int, rows=None) -> np.ndarray:
+    w, s, b = (qt.w, qt.s, qt.b) if rows is None else (qt.w[rows], qt.s[rows], qt.b[rows])
+    return dequantize(np.asarray(w, np.uint32), np.asarray(s, np.uint16), np.asarray(b, np.uint16), 4,
+                      sd).astype(np.float64)
+
+
+def _bfv(u16) -> np.ndarray:
+    return bf16_to_f32(np.asarray(u16, np.uint16)).astype(np.float64)
+
+
+def rmsnorm_f(x: np.ndarray, w_bf16, eps: float) -> np.ndarray:
+    """rmsnorm on bf16-valued floats; returns bf16-valued float64."""
+    x = np.asarray(x, np.float64)
+    inv = 1.0 / np.sqrt(np.mean(x * x) + eps)
+    return rbf(_bfv(w_bf16) * rbf((x * inv).astype(np.float32))).astype(np.float64)
+
+
+class SemanticKV:
+    """Quantized cache of one layer held by the semantic model: codes /
+    scales / biases like the oracle's (model.py:45-82 quantize-on-append)."""
+
+    def __init__(self, layer_arrays: dict, bits: int):
+        self.L = {n: np.array(a, copy=True) for n, a in layer_arrays.items()}
+        self.bits = bits
+
+    def append(self, pos: int, k_bf16v: np.ndarray, v_bf16v: np.ndarray) -> None:
+        from . import quantize
+
+        for name, x in (("k", k_bf16v), ("v", v_bf16v)):
+            c, s, b = quantize(np.asarray(x, np.float32)[:, None, :], self.bits, 1)
+            self.L[f"{name}_codes"][:, pos] = c[:, 0]
+            self.L[f"{name}_scales"][:, pos] = s[:, 0]
+            self.L[f"{name}_biases"][:, pos] = b[:, 0]
+
+    def dequant(self, name: str, upto: int) -> np.ndarray:
+        L = self.L
+        return dequantize(L[f"{name}_codes"][:, :upto], L[f"{name}_scales"][:, :upto], L[f"{name}_biases"][:, :upto],
+                          self.bits, 1).astype(np.float64)
+
+
+def layer_step(cfg, L, kv: SemanticKV, h: np.ndarray, pos: int, sd: int) -> np.ndarray:
+    """One decoder layer (model.py:258-271) for the token at `pos`; h is the
+    bf16-valued residual; returns the new residual (bf16-valued float64)."""
+    from . import f32_to_bf16
+
+    hq, hkv = cfg.n_q_heads, cfg.n_kv_heads
+    xn = rmsnorm_f(h, L.input_norm, cfg.rms_eps)
+    q = rbf(_dq(L.q, sd) @ xn).reshape(hq, 128)
+    k = rbf(_dq(L.k, sd) @ xn).reshape(hkv, 128)
+    v = rbf(_dq(L.v, sd) @ xn).reshape(hkv, 128)
+    if L.q_norm is not None:
+        q = np.stack([rmsnorm_f(r, L.q_norm, cfg.rms_eps) for r in q])
+        k = np.stack([rmsnorm_f(r, L.k_norm, cfg.rms_eps) for r in k])
+    q = rbf(rope(q, pos, cfg.rope_theta))
+    k = rbf(rope(k, pos, cfg.rope_theta))
+    kv.append(pos, k, v)
+    K, V = kv.dequant("k", pos + 1), kv.dequant("v", pos + 1)
+    sinks = None if L.sinks is None else np.asarray(L.sinks, np.uint16)
+    att = rbf(attention(f32_to_bf16(q.astype(np.float32)), K, V, sinks=sinks, bf16_probs=True)).reshape(-1)
+    h = rbf(h + rbf(_dq(L.o, sd) @ att.astype(np.float64))).astype(np.float64)
+    xn2 = rmsnorm_f(h, L.post_norm, cfg.rms_eps)
+    logits = rbf(_bfv(L.router).reshape(cfg.n_experts, -1) @ xn2).astype(np.float64)
+    bias = None if L.expert_bias is None else np.asarray(L.expert_bias, np.float64)
+    ids, wts = route(logits, cfg.top_k, cfg.router_mode, bias)
+    I, H = cfg.moe_inter, cfg.hidden
+    downs = []
+    for e in ids:
+        g = rbf(_dq(L.gate, sd, slice(int(e) * I, (int(e) + 1) * I)) @ xn2)
+        u = rbf(_dq(L.up, sd, slice(int(e) * I, (int(e) + 1) * I)) @ xn2)
+        act = silu_mul(g, u).astype(np.float64)
+        downs.append(rbf(_dq(L.down, sd, slice(int(e) * H, (int(e) + 1) * H)) @ act))
+    mix = expert_mix(np.stack(downs).astype(np.float32), np.asarray(wts, np.float32))
+    return rbf(h + mix.astype(np.float64)).astype(np.float64)
+
+
+def model_step(m, kvs: list, token: int, pos: int):
+    """Embedding -> every layer -> final norm -> lm_head (model.py:318-327).
+    Returns (logits float64 [V], trace float64 [L + 1, H])."""
+    import torch
+
+    cfg = m.cfg
+    sd = 0 if cfg.scale_dtype == torch.float16 else 1
+    h = rbf(_dq(m.embed, sd, slice(token, token + 1))[0]).astype(np.float64)
+    trace = [h]
+    for L, kv in zip(m.layers, kvs):
+        h = layer_step(cfg, L, kv, h, pos, sd)
+        trace.append(h)
+    xf = rmsnorm_f(h, m.final_norm, cfg.rms_eps)
+    logits = rbf(_dq(m.lm_head, sd) @ xf).astype(np.float64)
+    return logits, np.stack(trace)

@@ -100,4 +100,5 @@ class RecShard(C.Structure):
         ("super_hi", C.c_int32),
         ("capacity_total", C.c_int32),
         ("exchange", C.c_void_p * 8),
+        ("schedule", C.c_int32),
     ]

@@ -47,7 +47,13 @@ struct AttnArgs {
   int n_super_max;
   int* status;
   int pdl;
+  // a session split over ranks: this rank's cache holds positions from
+  // token_base on, and it computes the items of super-chunks [super_lo,
+  // super_hi) (one GPU: token_base 0, super_lo 0, super_hi kAttAllSupers)
+  int token_base;
+  int super_lo, super_hi;
 };
+constexpr int kAttAllSupers = 1 << 30;
 
 // Item partial slots per head: one per block covers every item size.
 __host__ __device__ inline int items_cap(int capacity) { return capacity / kAttBlock; }
@@ -243,7 +249,7 @@ __device__ __forceinline__ void issue_block(AttnSmem<BITS>& sm, int s, const Att
   constexpr int RW = AttnStage<BITS>::ROW_WORDS;
   const int n = min(kAttBlock, T - b * kAttBlock);
   const int n4 = (n + 3) & ~3;
-  const size_t slot = size_t(g) * a.capacity + size_t(b) * kAttBlock;
+  const size_t slot = size_t(g) * a.capacity + size_t(b) * kAttBlock - size_t(a.token_base);
   const uint32_t cb = uint32_t(n4) * RW * 4, sbytes = uint32_t(n4) * 4;
   mbar_expect_tx(&sm.bar[s], 2 * cb + 4 * sbytes);
   bulk_g2s(sm.st[s].kc, a.k_codes + slot * RW, cb, &sm.bar[s]);
@@ -276,25 +282,30 @@ __global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnAr
   grid_launch_dependents();
   const int p = *a.position;
   const int T = p + 1;
-  if (p < 0 || p >= a.capacity) {
+  if (p < 0 || (a.super_hi >= kAttAllSupers && p >= a.capacity)) {
     if (blockIdx.x == 0 && threadIdx.x == 0) report(a.status, kStatusBadPosition);
     return;
   }
   const int nblk = (T + kAttBlock - 1) / kAttBlock;
   const int nbi = item_blocks(nblk);
   const int n_items = (nblk + nbi - 1) / nbi;
-  const int items = n_items * a.hkv;
+  const int per_super = super_items(nblk);
+  // this rank's items: those of super-chunks [super_lo, super_hi)
+  const int i_lo = min(a.super_lo, (n_items + per_super - 1) / per_super) * per_super;
+  const int i_hi = a.super_hi >= (n_items + per_super - 1) / per_super ? n_items : a.super_hi * per_super;
+  const int items = max(0, i_hi - i_lo) * a.hkv;
+  const int item0 = a.token_base / (kAttBlock * nbi);  // local index of the first item held here
   const float* cs = a.rope + size_t(p) * 128;
   const int icap = items_cap(a.capacity);
   uint32_t phase = 0;  // bit s: parity of stage s
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
-    const int g = it % a.hkv, item = it / a.hkv;
+    const int g = it % a.hkv, item = i_lo + it / a.hkv;
     const int b0 = item * nbi, b1 = min(b0 + nbi, nblk);
     if (threadIdx.x == 0) issue_block<BITS>(sm, 0, a, g, b0, T);
     if (sm.sc.qg != g) prep_q_heads<BITS>(a.qkv, g, cs, a.q_norm, a.eps, sm.sc, warp);
     const bool has_new = p >= b0 * kAttBlock && p < b1 * kAttBlock;
     if (has_new) {
-      const size_t slot = size_t(g) * a.capacity + size_t(p);
+      const size_t slot = size_t(g) * a.capacity + size_t(p - a.token_base);
       prep_new_kv<BITS>(a.qkv, a.hq, a.hkv, g, cs, a.k_norm, a.eps, sm.sc, warp, a.k_codes + slot * RW,
                         a.v_codes + slot * RW, a.k_scales + slot * 2, a.k_biases + slot * 2, a.v_scales + slot * 2,
                         a.v_biases + slot * 2);
@@ -326,7 +337,8 @@ __global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnAr
       }
       return;
     }
-    warps_fold_store(st, warp, sm.sc, CtaSync{}, a.partials + (size_t(g * kHeadsPerKv) * icap + item) * kPartialFloats,
+    warps_fold_store(st, warp, sm.sc, CtaSync{},
+                     a.partials + (size_t(g * kHeadsPerKv) * icap + (item - item0)) * kPartialFloats,
                      size_t(icap) * kPartialFloats);
     __syncthreads();
   }

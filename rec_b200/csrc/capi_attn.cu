@@ -162,6 +162,7 @@ REC_API int rec_attn_decode(const void* qkv_dev, int32_t n_q_heads, int32_t n_kv
   a.v_scales = static_cast<uint16_t*>(kv->v_scales);
   a.v_biases = static_cast<uint16_t*>(kv->v_biases);
   a.capacity = capacity;
+  a.super_hi = kAttAllSupers;
   a.hq = n_q_heads;
   a.hkv = n_kv_heads;
   a.rope = rope_dev;

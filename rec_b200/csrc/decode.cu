@@ -16,6 +16,7 @@
 #include <cstdlib>
 
 #include "attn.cuh"
+#include "attn_shard.cuh"
 #include "capi_common.h"
 #include "mega.cuh"
 #include "moe.cuh"
@@ -37,6 +38,7 @@ enum Ctrl : int {
   kCtlEos = 8,       // 8 slots
   kCtlRecorded = 16, // 64 slots: ids produced by the current packet
   kCtlSampled = 80,  // 1: a sampled packet; the sampler feeds the next token back
+  kCtlSeq = 81,      // steps completed since the workspace was set (exchange parity of sharded graph steps)
   kCtlInts = 96,
 };
 constexpr int kMaxPacket = 64;
@@ -87,6 +89,7 @@ __global__ void __launch_bounds__(256) k_embed(int* ctl, QMatDev emb, int H, int
 // End of a step: record the argmax, stop after EOS, advance the position.
 __global__ void k_step_end(int* ctl) {
   grid_wait();
+  if (threadIdx.x == 0) ctl[kCtlSeq] += 1;
   if (threadIdx.x == 0) {
     const int t = ctl[kCtlArgmax];
     const int step = ctl[kCtlStep];
@@ -145,6 +148,7 @@ struct RecCtx {
   int block_begin = 0, block_end = 1 << 30;
   // one session over several GPUs (rec_set_shard)
   int world = 1, rank = 0, e_lo = 0, e_hi = 0, super_lo = 0, super_hi = 0, cap_total = 0;
+  bool shard_graph = false;  // a split session on the graph schedule (RecShard.schedule), fixed for its lifetime
   uint8_t* xch[kMaxWorld] = {};
   unsigned layer_seq = 0;  // layer steps run so far (exchange parity)
   uint8_t* ws = nullptr;
@@ -249,10 +253,10 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
   const int grid = c->grid;
   cudaError_t e = cudaSuccess;
   int* status = c->ctl + kCtlStatus;
-  if (kind == kKEmbed)
+  if (kind == kKEmbed)  // a split session checks the position against the whole context
     return launch(k_embed<SD>, 1, 256, 0, st, false, c->ctl, QMatDev{(const uint32_t*)c->g.embed.w,
-                  (const uint16_t*)c->g.embed.scales, (const uint16_t*)c->g.embed.biases}, H, d.vocab, c->capacity,
-                  c->token_base, c->h, c->trace);
+                  (const uint16_t*)c->g.embed.scales, (const uint16_t*)c->g.embed.biases}, H, d.vocab,
+                  c->world > 1 ? c->cap_total : c->capacity, c->world > 1 ? 0 : c->token_base, c->h, c->trace);
   if (kind == kKStepEnd) return launch(k_step_end, 1, 32, 0, st, pdl, c->ctl);
   if (kind != kKHead) {
     const RecLayerWeights& L = c->layers[li];
@@ -288,6 +292,9 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
       a.v_scales = (uint16_t*)kv.v_scales;
       a.v_biases = (uint16_t*)kv.v_biases;
       a.capacity = c->capacity;
+      a.token_base = c->world > 1 ? c->token_base : 0;
+      a.super_lo = c->world > 1 ? c->super_lo : 0;
+      a.super_hi = c->world > 1 ? c->super_hi : kAttAllSupers;
       a.hq = d.n_q_heads;
       a.hkv = d.n_kv_heads;
       a.rope = c->rope;
@@ -307,6 +314,33 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
       if (kind == kKAttn)
         return d.kv_bits == 4 ? launch(k_attn_partial<4>, agrid, kAttWarps * 32, sizeof(AttnSmem<4>), st, pdl, a)
                               : launch(k_attn_partial<8>, agrid, kAttWarps * 32, sizeof(AttnSmem<8>), st, pdl, a);
+      if (c->world > 1) {
+        // this rank's super-chunks to every rank, then the in-order merge
+        AttnXchArgs x = {};
+        x.partials = c->partials;
+        x.capacity = c->capacity;
+        x.token_base = c->token_base;
+        x.super_lo = c->super_lo;
+        x.super_hi = c->super_hi;
+        x.position = c->ctl + kCtlPosition;
+        x.seq = c->ctl + kCtlSeq;
+        x.layer = li;
+        x.n_layers = d.n_layers;
+        x.world = c->world;
+        x.rank = c->rank;
+        x.hq = d.n_q_heads;
+        for (int q = 0; q < kMaxWorld; ++q) x.xch[q] = c->xch[q];
+        x.xl = xch_layout(d.n_q_heads, (c->cap_total + kSuperTokens - 1) / kSuperTokens, H);
+        x.sinks = a.sinks;
+        x.out = c->attn;
+        x.status = status;
+        const int local = std::max(1, c->super_hi - c->super_lo);
+        k_attn_combine_xch<<<dim3(d.n_q_heads, local), 32, 0, st>>>(x);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        k_attn_final_xch<<<d.n_q_heads, 32, 0, st>>>(x);
+        return cudaGetLastError();
+      }
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(d.n_q_heads, std::max(1, c->n_super_max));
       cfg.blockDim = dim3(32);
@@ -364,8 +398,8 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
       a.ids = c->ids;
       a.k = d.top_k;
       a.I = d.moe_inter;
-      a.expert_lo = 0;
-      a.expert_hi = d.n_experts;
+      a.expert_lo = c->world > 1 ? c->e_lo : 0;
+      a.expert_hi = c->world > 1 ? c->e_hi : d.n_experts;
       a.act = c->act;
       a.status = status;
       a.pdl = pdl;
@@ -381,10 +415,17 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
       a.wts = c->wts;
       a.k = d.top_k;
       a.H = H;
-      a.expert_lo = 0;
-      a.expert_hi = d.n_experts;
+      a.expert_lo = c->world > 1 ? c->e_lo : 0;
+      a.expert_hi = c->world > 1 ? c->e_hi : d.n_experts;
       a.h = c->h;
       a.trace_row = c->trace + size_t(li + 1) * H;
+      a.world = c->world;
+      a.rank = c->rank;
+      a.layer = li;
+      a.n_layers = d.n_layers;
+      a.seq = c->ctl + kCtlSeq;
+      for (int q = 0; q < kMaxWorld; ++q) a.xch[q] = c->xch[q];
+      if (c->world > 1) a.xl = xch_layout(d.n_q_heads, (c->cap_total + kSuperTokens - 1) / kSuperTokens, H);
       a.status = status;
       a.pdl = pdl;
       const int dgrid = std::max(grid, H / (2 * DownSmem<768>::RMAX / 2));
@@ -514,6 +555,9 @@ REC_API int rec_set_shard(RecCtx* c, const RecShard* sh) {
   c->super_lo = s.super_lo;
   c->super_hi = s.super_hi;
   c->cap_total = s.capacity_total;
+  REC_CHECK_ARG(s.schedule == 0 || s.schedule == 1, "RecShard.schedule must be 0 or 1");
+  if (c->shard_graph != (s.schedule == 1)) drop_graph(c);
+  c->shard_graph = s.world > 1 && s.schedule == 1;
   c->token_base = s.super_lo * kSuperTokens;
   bool all = true;
   for (int q = 0; q < kMaxWorld; ++q) {
@@ -704,7 +748,8 @@ static int schedule_for(const RecCtx* c, int position) {
   const char* sched = std::getenv("REC_SCHEDULE");
   if (sched && std::strcmp(sched, "graph") == 0) return kSchedGraph;
   if (c->d.n_experts > kMegaMaxExperts) return kSchedGraph;
-  if ((sched && std::strcmp(sched, "mega") == 0) || c->world > 1) return kSchedMega;
+  if (c->world > 1) return c->shard_graph ? kSchedGraph : kSchedMega;
+  if (sched && std::strcmp(sched, "mega") == 0) return kSchedMega;
   if (sched && std::strcmp(sched, "split") == 0) return kSchedSplit;
   const double bytes = double(position + 1) * double(c->d.n_kv_heads) * (c->d.kv_bits == 4 ? 144.0 : 272.0);
   return bytes < kMegaAttnBytes ? kSchedMega : kSchedGraph;
@@ -722,7 +767,8 @@ static int check_ready(RecCtx* c) {
     return REC_ESTATE;
   }
   if (c->world > 1) {
-    REC_CHECK_ARG(mega_for(c, 0), "a session split over ranks runs on the persistent kernel only (no REC_SCHEDULE=graph, n_experts <= %d)", kMegaMaxExperts);
+    REC_CHECK_ARG(c->shard_graph || c->d.n_experts <= kMegaMaxExperts,
+                  "a split session on the persistent kernel needs n_experts <= %d", kMegaMaxExperts);
     for (int q = 0; q < c->world; ++q)
       if (!c->xch[q]) {
         set_error("rec_set_shard: exchange buffer of rank %d not set", q);

@@ -31,9 +31,11 @@
 #pragma once
 #include "attn.cuh"
 #include "moe.cuh"
+#include "xch.cuh"
 
 namespace rec {
 
+static_assert(kXchMaxTopK == kMaxTopK, "exchange slots must cover the top-k");
 constexpr int kMegaCons = 8;                        // consumer warps
 constexpr int kMegaThreads = 32 * (kMegaCons + 1);  // + producer warp
 constexpr int kSlotBytes = 36864;
@@ -65,47 +67,6 @@ struct MegaLayer {
   uint16_t* v_scales;
   uint16_t* v_biases;
 };
-
-// Exchange buffer of one rank (identical layout on every rank); two copies
-// of everything, selected by the parity of the global layer-step counter.
-constexpr int kMaxWorld = 8;
-// Waits on other GPUs: ranks launch independently, so allow more host jitter
-// than for waits inside one GPU (still bounded: a few seconds).
-constexpr uint32_t kPeerSpinLimit = kSpinLimit * 8;
-constexpr int kMaxGrid = 1024;
-struct XchLayout {
-  size_t head_cnt;  // unsigned [2][Hq]: super-chunk partials received per head
-  size_t xcnt;      // unsigned [2][kMaxGrid]: expert-output contributions received per CTA
-  size_t supers;    // float [2][Hq][n_super][132]
-  size_t xd;        // bf16 [2][kMaxTopK][H]: per-slot expert outputs
-  size_t total;
-  int hq, n_super, H;
-};
-inline __host__ __device__ size_t xch_align(size_t x) { return (x + 255) / 256 * 256; }
-inline __host__ __device__ XchLayout xch_layout(int hq, int n_super, int H) {
-  XchLayout x;
-  x.hq = hq;
-  x.n_super = n_super;
-  x.H = H;
-  x.head_cnt = 0;
-  x.xcnt = xch_align(x.head_cnt + size_t(2) * hq * 4);
-  x.supers = xch_align(x.xcnt + size_t(2) * kMaxGrid * 4);
-  x.xd = xch_align(x.supers + size_t(2) * hq * n_super * kPartialFloats * 4);
-  x.total = xch_align(x.xd + size_t(2) * kMaxTopK * H * 2);
-  return x;
-}
-__device__ __forceinline__ unsigned* xch_head_cnt(uint8_t* b, const XchLayout& x, int par, int h) {
-  return reinterpret_cast<unsigned*>(b + x.head_cnt) + par * x.hq + h;
-}
-__device__ __forceinline__ unsigned* xch_xcnt(uint8_t* b, const XchLayout& x, int par, int cta) {
-  return reinterpret_cast<unsigned*>(b + x.xcnt) + par * kMaxGrid + cta;
-}
-__device__ __forceinline__ float* xch_super(uint8_t* b, const XchLayout& x, int par, int h, int s) {
-  return reinterpret_cast<float*>(b + x.supers) + ((size_t(par) * x.hq + h) * x.n_super + s) * kPartialFloats;
-}
-__device__ __forceinline__ uint16_t* xch_xd(uint8_t* b, const XchLayout& x, int par, int slot) {
-  return reinterpret_cast<uint16_t*>(b + x.xd) + (size_t(par) * kMaxTopK + slot) * x.H;
-}
 
 struct MegaArgs {
   const MegaLayer* layers;

@@ -8,6 +8,7 @@
 // megakernel.py:944-969 + mixed_bits.py:32-54 (bf16 logits, bf16 mix).
 #pragma once
 #include "gemv.cuh"
+#include "xch.cuh"
 
 namespace rec {
 
@@ -330,6 +331,13 @@ struct DownArgs {
   uint16_t* dout;          // expert-parallel mode: bf16 [k, H] expert outputs (local ranks only)
   int* status;
   int pdl;
+  // a session split over ranks (world > 1): the local experts' outputs go
+  // into every rank's exchange buffer, then each CTA mixes its rows of all k
+  // slots in rank order once every rank has delivered them
+  int world, rank, layer, n_layers;
+  const int* seq;          // steps completed (device counter): exchange parity
+  uint8_t* xch[kMaxWorld];
+  XchLayout xl;
 };
 
 template <int I>
@@ -426,6 +434,53 @@ __global__ void __launch_bounds__(kThreads, 1) k_down(const DownArgs a) {
       const int rr = t / n, i = t % n;
       if (local(rr)) a.dout[rr * a.H + i0 + i] = to_bf(sm.d[rr][i]);
     }
+    return;
+  }
+  if (a.world > 1) {
+    // rows [i0, i1) of the local slots to every rank (this one included),
+    // a system-scope fence, one counter step per rank for this CTA's rows;
+    // then wait (bounded) for all ranks' rows and mix them from this rank's
+    // buffer, the single-GPU mix order
+    const int par = int((unsigned(*a.seq) * unsigned(a.n_layers) + unsigned(a.layer)) & 1u);
+    for (int q = 0; q < a.world; ++q)
+      for (int t = threadIdx.x; t < a.k * n; t += kThreads) {
+        const int rr = t / n, i = t % n;
+        if (local(rr)) xch_xd(a.xch[q], a.xl, par, rr)[i0 + i] = to_bf(sm.d[rr][i]);
+      }
+    __threadfence_system();
+    __syncthreads();
+    __shared__ int xok;
+    unsigned* cnt = xch_xcnt(a.xch[a.rank], a.xl, par, blockIdx.x);
+    if (threadIdx.x == 0) {
+      for (int q = 0; q < a.world; ++q) atomicAdd_system(xch_xcnt(a.xch[q], a.xl, par, blockIdx.x), 1u);
+      int ok = 1;
+      uint32_t spins = 0;
+      while (ld_acquire_sys_u32(cnt) < unsigned(a.world)) {
+        if (++spins > kPeerSpinLimit) {
+          report(a.status, kStatusCounterTimeout);
+          ok = 0;
+          break;
+        }
+      }
+      xok = ok;
+    }
+    __syncthreads();
+    if (!xok) return;
+    const uint8_t* own = a.xch[a.rank];
+    for (int i = threadIdx.x; i < n; i += kThreads) {
+      float m = 0.0f;
+      for (int rr = 0; rr < a.k; ++rr) {
+        const float d = bf(__ldcg(reinterpret_cast<const unsigned short*>(
+            xch_xd(const_cast<uint8_t*>(own), a.xl, par, rr) + i0 + i)));
+        const float t = __fadd_rn(rbf(__fmul_rn(d, rbf(a.wts[rr]))), 0.0f);
+        m = rr == 0 ? t : rbf(__fadd_rn(t, m));
+      }
+      const uint16_t hn = to_bf(__fadd_rn(bf(a.h[i0 + i]), m));
+      a.h[i0 + i] = hn;
+      if (a.trace_row) a.trace_row[i0 + i] = hn;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(cnt) = 0u;
     return;
   }
   for (int i = threadIdx.x; i < n; i += kThreads) {

@@ -17,7 +17,13 @@ class DecodeSession:
     GPUs: `weights` hold the plan's experts, `kv` its local capacity, and every
     rank must make the same calls in the same order."""
 
-    def __init__(self, weights: ModelWeights, kv: KVCache, plan=None, group=None):
+    def __init__(self, weights: ModelWeights, kv: KVCache, plan=None, group=None, shard_schedule: str = "mega"):
+        """shard_schedule (split sessions): "mega" runs the persistent kernel
+        with the exchanges inside it; "graph" runs the CUDA graph of
+        standalone kernels (attention on this rank's KV with the standalone
+        kernel, the exchanges as separate kernels).  Fixed for the session."""
+        if shard_schedule not in ("mega", "graph"):
+            raise ValueError("shard_schedule must be 'mega' or 'graph'")
         self.weights = weights
         self.kv = kv
         self.cfg = weights.cfg
@@ -29,6 +35,7 @@ class DecodeSession:
         if plan is not None:
             self._shard = abi.RecShard(plan.world, plan.rank, plan.expert_lo, plan.expert_hi, plan.super_lo,
                                        plan.super_hi, plan.capacity)
+            self._shard.schedule = 1 if shard_schedule == "graph" else 0
             check(lib().rec_set_shard(self.ctx, C.byref(self._shard)), "rec_set_shard")
         self._layers = weights.rec_layers()
         self._global = weights.rec_global()

@@ -1,6 +1,9 @@
-"""One decode session split over two GPUs (expert parallelism + split-KV),
-through the C ABI: every rank's logits must equal the single-GPU oracle's bit
-for bit, with the context held on one rank or split over both."""
+"""One decode session split over 2 or 4 GPUs (expert parallelism + split-KV),
+through the C ABI, on both split schedules (the persistent kernel with the
+exchanges inside it, and the CUDA graph of standalone kernels with the
+exchanges as separate kernels): every rank's logits must equal the
+single-GPU oracle's bit for bit, with the context held on one rank, split
+over the ranks, and long enough for 4-block attention items."""
 import os
 from datetime import timedelta
 
@@ -14,10 +17,11 @@ from rec_b200.model import ModelConfig
 
 CFG = ModelConfig(name="mgpu", n_layers=2, n_q_heads=32, n_kv_heads=4, n_experts=16, top_k=4, moe_inter=512,
                   vocab=4096, kv_bits=4, flags=abi.REC_FLAG_SINKS)
-CAP = 2 * shard.SUPER_TOKENS
-CASES = {"context_on_rank0": 300, "context_split": shard.SUPER_TOKENS + 300}
+CAP = 4 * shard.SUPER_TOKENS
+CASES = {"context_on_rank0": 300, "context_split": shard.SUPER_TOKENS + 300,
+         "long_items": 3 * shard.SUPER_TOKENS + 300}
 STEPS = 4
-WORLD = 2
+SCHEDULES = ("mega", "graph")
 
 
 def _global_kv(cfg, T, seed):
@@ -47,7 +51,7 @@ def _to_dev(a, dtype):
     return torch.from_numpy(a).cuda().view(dtype)
 
 
-def _worker(rank, port, q):
+def _worker(rank, world, port, q):
     import torch.distributed as dist
 
     from rec_b200.model import KVCache, generate_weights
@@ -56,12 +60,12 @@ def _worker(rank, port, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=timedelta(seconds=120),
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
     try:
         results = {}
-        for name, T in CASES.items():
-            plan = shard.plan(WORLD, rank, CFG.n_experts, CAP)
+        for (name, T), sched in [(c, s) for c in CASES.items() for s in SCHEDULES]:
+            plan = shard.plan(world, rank, CFG.n_experts, CAP)
             w = generate_weights(CFG, seed=3, device="cuda", expert_range=(plan.expert_lo, plan.expert_hi))
             kv = KVCache.allocate(CFG, plan.local_capacity)
             glob = _global_kv(CFG, T, 11)
@@ -69,7 +73,7 @@ def _worker(rank, port, q):
             for d, h in zip(kv.layers, glob):
                 for n, t in d.items():
                     t[:, : hi - lo].copy_(_to_dev(h[n][:, lo:hi], t.dtype))
-            sess = DecodeSession(w, kv, plan=plan)
+            sess = DecodeSession(w, kv, plan=plan, shard_schedule=sched)
             tok, outs = 5, []
             for i in range(STEPS):
                 logits, _ = sess.step(tok, T + i)
@@ -80,7 +84,7 @@ def _worker(rank, port, q):
             torch.cuda.synchronize()
             dist.barrier()
             del sess
-            results[name] = outs
+            results[(name, sched)] = outs
         q.put((rank, results))
     except Exception as exc:
         q.put((rank, repr(exc)))
@@ -90,23 +94,24 @@ def _worker(rank, port, q):
 
 
 @pytest.mark.gpu
-def test_two_gpu_session_matches_single_gpu_oracle(cuda):
+@pytest.mark.parametrize("world", [2, 4])
+def test_split_session_matches_single_gpu_oracle(cuda, world):
     import torch.multiprocessing as mp
 
     from oracle.host import HostKV, HostModel
     from rec_b200.model import generate_weights
 
-    if torch.cuda.device_count() < WORLD:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 29533, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, world, 29533 + world, q)) for r in range(world)]
     for p in procs:
         p.start()
-    got = dict(q.get(timeout=600) for _ in range(WORLD))
+    got = dict(q.get(timeout=900) for _ in range(world))
     for p in procs:
         p.join(timeout=120)
-    for r in range(WORLD):
+    for r in range(world):
         assert not isinstance(got[r], str), got[r]
         assert procs[r].exitcode == 0
     w = generate_weights(CFG, seed=3, device="cuda")
@@ -119,6 +124,7 @@ def test_two_gpu_session_matches_single_gpu_oracle(cuda):
         tok = 5
         for i in range(STEPS):
             want, _ = host.step(hkv, tok, T + i, want_trace=False)
-            for r in range(WORLD):
-                assert np.array_equal(got[r][name][i], want), (name, i, r)
+            for r in range(world):
+                for sched in SCHEDULES:
+                    assert np.array_equal(got[r][(name, sched)][i], want), (name, sched, i, r)
             tok = oracle.argmax_bf16(want)
