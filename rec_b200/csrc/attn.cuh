@@ -210,7 +210,9 @@ __device__ __forceinline__ void warps_fold_store(WarpState& st, int warp, AttnSc
 
 // This warp's tile (tile `warp`) of one block held in the given K / V tiles
 // (n tokens of the block valid; new_row >= 0: that row is the new token).
-template <int BITS>
+// SPLIT: full tiles take the unmasked instance of tile_fold (same results);
+// the persistent kernel keeps one instance for its instruction footprint.
+template <int BITS, bool SPLIT = false>
 __device__ __forceinline__ void block_tiles(uint32_t* kc, uint16_t* ks, uint16_t* kb, uint32_t* vc, uint16_t* vs,
                                             uint16_t* vb, int n, int new_row, const AttnScratch& sc, int warp,
                                             WarpState& st) {
@@ -219,8 +221,12 @@ __device__ __forceinline__ void block_tiles(uint32_t* kc, uint16_t* ks, uint16_t
   const int nvalid = min(kAttTile, n - t0);
   if (nvalid <= 0) return;
   if (new_row >= t0 && new_row < t0 + kAttTile) patch_row<BITS>(kc, ks, kb, vc, vs, vb, new_row, sc);
-  tile_fold<BITS>(kc + t0 * RW, ks + 2 * t0, kb + 2 * t0, vc + t0 * RW, vs + 2 * t0, vb + 2 * t0, nvalid, sc.qf,
-                  st);
+  if (SPLIT && nvalid == kAttTile)
+    tile_fold<BITS, true>(kc + t0 * RW, ks + 2 * t0, kb + 2 * t0, vc + t0 * RW, vs + 2 * t0, vb + 2 * t0, nvalid,
+                          sc.qf, st);
+  else
+    tile_fold<BITS, false>(kc + t0 * RW, ks + 2 * t0, kb + 2 * t0, vc + t0 * RW, vs + 2 * t0, vb + 2 * t0, nvalid,
+                           sc.qf, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -324,7 +330,7 @@ __global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnAr
       const int n = min(kAttBlock, T - b * kAttBlock);
       const int new_row = (has_new && p / kAttBlock == b) ? p - b * kAttBlock : -1;
       AttnStage<BITS>& S = sm.st[s];
-      block_tiles<BITS>(S.kc, S.ks, S.kb, S.vc, S.vs, S.vb, n, new_row, sm.sc, warp, st);
+      block_tiles<BITS, true>(S.kc, S.ks, S.kb, S.vc, S.vs, S.vb, n, new_row, sm.sc, warp, st);
       // the tile may have been patched through the generic proxy, and the
       // next bulk copy into this stage must not overtake this block's reads
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -341,7 +341,8 @@ __device__ __forceinline__ float tile_max(const float (&v)[8]) {
   return fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
 }
 
-// One tile of 32 tokens (rows of the K and V tiles in shared memory, row
+// One tile of 32 tokens (FULL: all 32 valid, the masks compile away; rows of
+// the K and V tiles in shared memory, row
 // stride RW words; scales/biases [token][2], 8-byte aligned) for the 8 q
 // heads, folded into the warp state (canonical order):
 //   s_t = score of token t (0..nvalid-1), -inf beyond;
@@ -351,7 +352,7 @@ __device__ __forceinline__ float tile_max(const float (&v)[8]) {
 //     F = min(14 - exponent(max|w| (1 + 2^-7)), 100); wq_t = rint(w_t 2^F)
 //     (|wq| <= 32514: signed byte limbs);
 //     acc_d' = fma(acc_d, alpha, fma(float(sum_t wq_t code_td), 2^-F, tile_sum(x))).
-template <int BITS>
+template <int BITS, bool FULL = false>
 __device__ __forceinline__ void tile_fold(const uint32_t* kc, const uint16_t* ks, const uint16_t* kb,
                                           const uint32_t* vc, const uint16_t* vs, const uint16_t* vb, int nvalid,
                                           const QFrags& qf, WarpState& st) {
@@ -410,7 +411,7 @@ __device__ __forceinline__ void tile_fold(const uint32_t* kc, const uint16_t* ks
         float u = __fmaf_rn(b0, meta.x, __fmul_rn(s0, float(D0)));
         u = __fmaf_rn(s1, float(D1), u);
         u = __fmaf_rn(b1, meta.y, u);
-        p[2 * nt + j] = t + j < nvalid ? rbf(__fmul_rn(u, meta.z)) : -INFINITY;
+        p[2 * nt + j] = (FULL || t + j < nvalid) ? rbf(__fmul_rn(u, meta.z)) : -INFINITY;
       }
     }
     const float mt = tile_max(p);
@@ -441,7 +442,7 @@ __device__ __forceinline__ void tile_fold(const uint32_t* kc, const uint16_t* ks
         const uint32_t sw = j ? vsp[nt].y : vsp[nt].x, bw = j ? vbp[nt].y : vbp[nt].x;
         const float sc = __uint_as_float(g ? (sw & 0xFFFF0000u) : (sw << 16));
         const float bi = __uint_as_float(g ? (bw & 0xFFFF0000u) : (bw << 16));
-        const bool ok = 8 * nt + 2 * tq + j < nvalid;
+        const bool ok = FULL || 8 * nt + 2 * tq + j < nvalid;
         w[v] = ok ? __fmul_rn(p[v], sc) : 0.0f;
         x[v] = ok ? __fmul_rn(p[v], bi) : 0.0f;
         mx = fmaxf(mx, fabsf(w[v]));
