@@ -153,9 +153,6 @@ __device__ __forceinline__ void cons_sync() { asm volatile("bar.sync %0, %1;" ::
 struct ConsSync {
   __device__ void operator()() const { cons_sync(); }
 };
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 // Data written by other CTAs during this launch is read through L2 only
 // (L1 is not coherent across SMs inside one kernel).
@@ -248,7 +245,12 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 // builds): each site costs instructions in code that runs once per layer.
 __device__ __forceinline__ void stamp(const MegaArgs& a, int step, int layer, int slot) {
 #ifdef REC_LAYER_STAMPS
-  if (a.prof2 && step == 0 && layer == a.prof_layer) a.prof2[blockIdx.x * 64 + slot] = globaltimer();
+  if (a.prof2 && step == 0 && layer == a.prof_layer) {
+    unsigned long long t;
+    // the memory clobber keeps the site between the loads and stores around it
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) :: "memory");
+    a.prof2[blockIdx.x * 64 + slot] = t;
+  }
 #endif
 }
 // Adds v to a per-CTA diagnostic slot of the same layer profile.
@@ -282,6 +284,12 @@ __device__ __forceinline__ unsigned route_flag(const MegaArgs& a, int step, int 
 __device__ __forceinline__ bool aborted(const MegaArgs& a) {
   return *reinterpret_cast<volatile unsigned*>(a.gbar + 1) != 0;
 }
+// Waits that poll shared memory look at the abort word (a global load, one
+// L2 round trip) every 8th time round only, so that the load seldom delays
+// the moment the wait sees its own condition.
+__device__ __forceinline__ bool aborted_every8(const MegaArgs& a, uint32_t spins) {
+  return (spins & 7u) == 7u && aborted(a);
+}
 __device__ __forceinline__ void set_abort(const MegaArgs& a, int code) {
   report(a.ctl + 0, code);
   atomicExch(a.gbar + 1, 1u);
@@ -304,8 +312,13 @@ __device__ __forceinline__ bool grid_barrier(const MegaArgs& a, unsigned seq, un
     const unsigned target = gridDim.x * (seq + 1);
     int ok = 1;
     uint32_t spins = 0;
-    while (ld_acquire(a.gbar) < target) {
-      if (aborted(a)) { ok = 0; break; }
+    while (true) {
+      // the abort word's load is issued first and overlaps the count's
+      // acquire load: one L2 round trip per poll.  A CTA that leaves while
+      // another raises the abort stops at its next wait (every wait reads it).
+      const bool ab = aborted(a);
+      if (ld_acquire(a.gbar) >= target) break;
+      if (ab) { ok = 0; break; }
       if (++spins > a.bar_spin_limit) {
         set_abort(a, kStatusCounterTimeout);
         ok = 0;
@@ -313,7 +326,7 @@ __device__ __forceinline__ bool grid_barrier(const MegaArgs& a, unsigned seq, un
       }
     }
     if (a.prof && idx != kNoStamp) a.prof[(size_t(idx) * gridDim.x + blockIdx.x) * 2 + 1] = globaltimer();
-    ok_flag = ok && !aborted(a);
+    ok_flag = ok;
   }
   cons_sync();
   return ok_flag != 0;
@@ -343,7 +356,7 @@ struct Producer {
       const uint32_t par = ((chunk / kSlots) - 1) & 1;
       uint32_t spins = 0;
       while (!mbar_try_wait(&sm.empty[slot], par)) {
-        if (aborted(a)) { ok = false; return nullptr; }
+        if (aborted_every8(a, spins)) { ok = false; return nullptr; }
         if (++spins > kSpinLimit) {
           set_abort(a, kStatusBulkTimeout);
           ok = false;
@@ -351,6 +364,12 @@ struct Producer {
         }
       }
     }
+#ifdef REC_LAYER_STAMPS
+    if (acq_stamp >= 0) {
+      stamp_cur(acq_stamp);
+      acq_stamp = -1;
+    }
+#endif
     return sm.ring[slot];
   }
   __device__ void gemv_chunk(const QMatDev& m, int K, int row0, int n) {
@@ -469,7 +488,7 @@ struct Producer {
     uint32_t spins = 0;
     while (sm.merge_seq < target) {
       __nanosleep(32);
-      if (aborted(a)) { ok = false; return; }
+      if (aborted_every8(a, spins)) { ok = false; return; }
       if (++spins > kSpinLimit * 64) {
         set_abort(a, kStatusCounterTimeout);
         ok = false;
@@ -484,6 +503,7 @@ struct Producer {
   // The merge phases of one layer's attention (the consumers' merge_phase
   // and final_phase take the same chunks in the same order).
   int cur_step = 0, cur_layer = 0;  // for the diagnostics stamps
+  int acq_stamp = -1;                // diagnostics: stamp slot of the next slot acquisition
   __device__ void stamp_cur(int slot) { stamp(a, cur_step, cur_layer, slot); }
   __device__ void merge_chunks(const AttnPlan& AP, int step, int l) {
     if (short_merge(a, AP)) return;
@@ -532,6 +552,7 @@ struct Producer {
     const unsigned valid = pending;
     uint32_t spins = 0;
     while (true) {
+      const bool ab = aborted(a);  // in flight with the logit loads
       unsigned long long v[J];
 #pragma unroll
       for (int j = 0; j < J; ++j) v[j] = ((pending >> j) & 1u) ? ld_relaxed64(buf + lane + 32 * j) : 0ull;
@@ -542,7 +563,7 @@ struct Producer {
           pending &= ~(1u << j);
         }
       if (__all_sync(0xffffffffu, pending == 0)) break;
-      if (__any_sync(0xffffffffu, aborted(a))) return false;
+      if (__any_sync(0xffffffffu, ab)) return false;
       if (++spins > kSpinLimit * 4) {
         if (lane == 0) set_abort(a, kStatusCounterTimeout);
         return false;
@@ -577,6 +598,7 @@ struct Producer {
       }
     }
     __syncwarp();
+    if (lane == 0) stamp(a, step, l, 49);
     unsigned key[J];  // this lane's keys in registers for the k rounds (0 = absent or taken)
 #pragma unroll
     for (int j = 0; j < J; ++j) key[j] = ((valid >> j) & 1u) ? sm.route_k[lane + 32 * j] : 0u;
@@ -691,6 +713,11 @@ struct Producer {
           split_range(nl * a.I / 2, gridDim.x, blockIdx.x, g0, g1);
           g0 *= 2;
           g1 *= 2;
+#ifdef REC_LAYER_STAMPS
+          cur_step = step;
+          cur_layer = l;
+          acq_stamp = 50;
+#endif
           for (int u = g0; u < g1 && ok;) {
             const int j = u / a.I, i0 = u % a.I;
             const int n = min(kGPairs, g1 - u), nA = min(n, a.I - i0);
@@ -745,7 +772,7 @@ struct Consumers {
     const uint32_t par = (chunk / kSlots) & 1;
     uint32_t spins = 0;
     while (!mbar_try_wait(&sm.full[slot], par)) {
-      if (aborted(a)) { ok = false; break; }
+      if (aborted_every8(a, spins)) { ok = false; break; }
       if (++spins > kSpinLimit) {
         set_abort(a, kStatusBulkTimeout);  // every CTA leaves at its next grid barrier
         ok = false;
@@ -828,8 +855,9 @@ struct Consumers {
     cons_sync();
   }
   // Loads x into sm.xn and returns its fixed-point scale.
-  __device__ FixScale load_x(const uint16_t* src, int n) {
+  __device__ FixScale load_x(const uint16_t* src, int n, int step_ = -1, int layer_ = -1) {
     load_vec(sm.xn, src, n);
+    if (warp == 0 && lane == 0) stamp(a, step_, layer_, 48);
     return fix_scale_from_max(block_maxabs(sm.xn, n, threadIdx.x - 32, kMegaCons * 32, sm.red, kBarCons));
   }
 
@@ -1136,8 +1164,10 @@ struct Consumers {
       unsigned* c = xch_xcnt(own, a.xl, par, blockIdx.x);
       bool ok = true;
       uint32_t spins = 0;
-      while (ld_acquire_sys(c) < unsigned(a.world - 1)) {
-        if (aborted(a)) { ok = false; break; }
+      while (true) {
+        const bool ab = aborted(a);
+        if (ld_acquire_sys(c) >= unsigned(a.world - 1)) break;
+        if (ab) { ok = false; break; }
         if (++spins > kPeerSpinLimit) {
           set_abort(a, kStatusCounterTimeout);
           ok = false;
@@ -1175,8 +1205,10 @@ struct Consumers {
       uint32_t spins = 0;
       bool ok = true;
       if (lane == 0) {
-        while (ld_acquire_sys(cnt) < unsigned(P.n_super)) {
-          if (aborted(a)) { ok = false; break; }
+        while (true) {
+          const bool ab = aborted(a);
+          if (ld_acquire_sys(cnt) >= unsigned(P.n_super)) break;
+          if (ab) { ok = false; break; }
           if (++spins > kPeerSpinLimit) {
             set_abort(a, kStatusCounterTimeout);
             ok = false;
@@ -1245,7 +1277,7 @@ struct Consumers {
       int ok = 1;
       uint32_t spins = 0;
       while (sm.route_seq < seq) {
-        if (aborted(a)) { ok = 0; break; }
+        if (aborted_every8(a, spins)) { ok = 0; break; }
         if (++spins > kSpinLimit * 4) {
           set_abort(a, kStatusCounterTimeout);
           ok = 0;
@@ -1356,7 +1388,7 @@ struct Consumers {
         // ---- O
         {
           if (warp == 0 && lane == 0) stamp(a, step, l, 40);
-          const FixScale fo = load_x(a.attn, a.hq * 128);
+          const FixScale fo = load_x(a.attn, a.hq * 128, step, l);
           if (warp == 0 && lane == 0) stamp(a, step, l, 41);
           GroupX gx[1];
           if (a.hq * 128 == 4096) {
