@@ -6,9 +6,9 @@
 // 256 tokens each) and computes their item partials with k_attn_partial.
 //   k_attn_combine_xch: one warp per (q head, local super-chunk) folds the
 //     super-chunk's items in order, stores the partial into every rank's
-//     exchange buffer with plain peer stores (NVLink), fences at system
-//     scope and raises each rank's per-head counter with a system-scope
-//     atomic;
+//     exchange buffer with plain peer stores (NVLink); after a warp barrier
+//     lane 0 fences at system scope and raises each rank's per-head counter
+//     with a system-scope atomic;
 //   k_attn_final_xch: one warp per q head waits (bounded) until its counter
 //     holds every super-chunk of the context, folds [sink] and the
 //     super-chunks in order -- the single-GPU combine, so every rank's output
@@ -39,6 +39,7 @@ struct AttnXchArgs {
   const uint16_t* sinks;  // bf16 [Hq] or null
   uint16_t* out;          // bf16 [Hq * 128]
   int* status;
+  int pdl;                // launched as a programmatic dependent of the previous kernel
 };
 
 __device__ __forceinline__ int xch_layer_parity(const AttnXchArgs& a) {
@@ -61,6 +62,8 @@ __device__ __forceinline__ AttnCounts attn_counts(int T) {
 
 __global__ void __launch_bounds__(32) k_attn_combine_xch(const AttnXchArgs a) {
   const int lane = threadIdx.x;
+  if (a.pdl) grid_wait();  // the item partials of k_attn_partial
+  grid_launch_dependents();
   const AttnCounts C = attn_counts(*a.position + 1);
   const int h = blockIdx.x, s = a.super_lo + blockIdx.y;
   if (s >= min(a.super_hi, C.n_super)) return;
@@ -71,14 +74,19 @@ __global__ void __launch_bounds__(32) k_attn_combine_xch(const AttnXchArgs a) {
                 min((s + 1) * C.per_super, C.n_items) - item0);
   const int par = xch_layer_parity(a);
   for (int q = 0; q < a.world; ++q) store_partial(xch_super(a.xch[q], a.xl, par, h, s), P);
-  __threadfence_system();
   __syncwarp();
-  if (lane == 0)
+  if (lane == 0) {
+    __threadfence_system();  // cumulative over the warp's stores (ordered by the warp barrier)
     for (int q = 0; q < a.world; ++q) atomicAdd_system(xch_head_cnt(a.xch[q], a.xl, par, h), 1u);
+  }
 }
 
 __global__ void __launch_bounds__(32) k_attn_final_xch(const AttnXchArgs a) {
   const int lane = threadIdx.x, h = blockIdx.x;
+  // the wait covers this rank's k_attn_combine_xch (its stores and counter
+  // raises); the peers' arrive through the counters
+  if (a.pdl) grid_wait();
+  grid_launch_dependents();
   const AttnCounts C = attn_counts(*a.position + 1);
   const int par = xch_layer_parity(a);
   uint8_t* own = a.xch[a.rank];

@@ -112,13 +112,13 @@ __global__ void k_step_end(int* ctl) {
 
 // --- launch helper ----------------------------------------------------------------
 template <typename Kern, typename... Args>
-cudaError_t launch(Kern kern, int grid, int block, size_t smem, cudaStream_t st, bool pdl, Args... args) {
+cudaError_t launch(Kern kern, dim3 grid, int block, size_t smem, cudaStream_t st, bool pdl, Args... args) {
   if (smem > 48 * 1024) {
     cudaError_t e = set_smem_limit(reinterpret_cast<const void*>(kern), smem);
     if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = grid;
   cfg.blockDim = dim3(block);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -334,12 +334,11 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
         x.sinks = a.sinks;
         x.out = c->attn;
         x.status = status;
+        x.pdl = pdl;
         const int local = std::max(1, c->super_hi - c->super_lo);
-        k_attn_combine_xch<<<dim3(d.n_q_heads, local), 32, 0, st>>>(x);
-        e = cudaGetLastError();
+        e = launch(k_attn_combine_xch, dim3(d.n_q_heads, local), 32, 0, st, pdl, x);
         if (e != cudaSuccess) return e;
-        k_attn_final_xch<<<d.n_q_heads, 32, 0, st>>>(x);
-        return cudaGetLastError();
+        return launch(k_attn_final_xch, dim3(d.n_q_heads), 32, 0, st, pdl, x);
       }
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(d.n_q_heads, std::max(1, c->n_super_max));

@@ -1092,10 +1092,11 @@ struct Consumers {
         // publish the super-chunk to every rank; each merges them itself
         const int par = xch_parity(a, step_, layer_);
         for (int q = 0; q < a.world; ++q) store_partial(xch_super(a.xch[q], a.xl, par, h, s), S);
-        __threadfence_system();
         __syncwarp();
-        if (lane == 0)
+        if (lane == 0) {
+          __threadfence_system();  // cumulative over the warp's stores (ordered by the warp barrier)
           for (int q = 0; q < a.world; ++q) atomicAdd_system(xch_head_cnt(a.xch[q], a.xl, par, h), 1u);
+        }
       } else if (P.n_super == 1) {
         Partial4 F = sink_partial(L, h);
         merge_into(F, S);
@@ -1148,17 +1149,19 @@ struct Consumers {
     const int t = threadIdx.x - 32, nt = kMegaCons * 32;
     const int nl = sm.n_loc;
     uint8_t* own = a.xch[a.rank];
+    const int n2 = n / 2;  // rows as bf16 pairs (n and P.o0 are even)
     for (int q = 0; q < a.world; ++q) {
       if (q == a.rank) continue;
-      for (int idx = t; idx < nl * n; idx += nt) {
-        const int j = idx / n, i = idx - j * n;
+      for (int idx = t; idx < nl * n2; idx += nt) {
+        const int j = idx / n2, i = 2 * (idx - j * n2);
         const int rr = sm.loc[j];
-        xch_xd(a.xch[q], a.xl, par, rr)[P.o0 + i] = to_bf(sm.dsm[rr][i]);
+        *reinterpret_cast<uint32_t*>(xch_xd(a.xch[q], a.xl, par, rr) + P.o0 + i) =
+            uint32_t(to_bf(sm.dsm[rr][i])) | (uint32_t(to_bf(sm.dsm[rr][i + 1])) << 16);
       }
     }
-    __threadfence_system();
     cons_sync();
     if (t == 0) {
+      __threadfence_system();  // cumulative over the consumers' stores (ordered by the barrier)
       for (int q = 0; q < a.world; ++q)
         if (q != a.rank) atomicAdd_system(xch_xcnt(a.xch[q], a.xl, par, blockIdx.x), 1u);
       unsigned* c = xch_xcnt(own, a.xl, par, blockIdx.x);

@@ -437,21 +437,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_down(const DownArgs a) {
     return;
   }
   if (a.world > 1) {
-    // rows [i0, i1) of the local slots to every rank (this one included),
-    // a system-scope fence, one counter step per rank for this CTA's rows;
-    // then wait (bounded) for all ranks' rows and mix them from this rank's
-    // buffer, the single-GPU mix order
+    // rows [i0, i1) of the local slots to every rank (this one included) as
+    // bf16 pairs (n and i0 are even); after the CTA barrier one thread fences
+    // at system scope (cumulative over the CTA's stores) and raises each
+    // rank's counter for this CTA's rows; then wait (bounded) for all ranks'
+    // rows and mix them from this rank's buffer, the single-GPU mix order
     const int par = int((unsigned(*a.seq) * unsigned(a.n_layers) + unsigned(a.layer)) & 1u);
+    const int n2 = n / 2;
     for (int q = 0; q < a.world; ++q)
-      for (int t = threadIdx.x; t < a.k * n; t += kThreads) {
-        const int rr = t / n, i = t % n;
-        if (local(rr)) xch_xd(a.xch[q], a.xl, par, rr)[i0 + i] = to_bf(sm.d[rr][i]);
+      for (int t = threadIdx.x; t < a.k * n2; t += kThreads) {
+        const int rr = t / n2, i = 2 * (t % n2);
+        if (local(rr))
+          *reinterpret_cast<uint32_t*>(xch_xd(a.xch[q], a.xl, par, rr) + i0 + i) =
+              uint32_t(to_bf(sm.d[rr][i])) | (uint32_t(to_bf(sm.d[rr][i + 1])) << 16);
       }
-    __threadfence_system();
     __syncthreads();
     __shared__ int xok;
     unsigned* cnt = xch_xcnt(a.xch[a.rank], a.xl, par, blockIdx.x);
     if (threadIdx.x == 0) {
+      __threadfence_system();
       for (int q = 0; q < a.world; ++q) atomicAdd_system(xch_xcnt(a.xch[q], a.xl, par, blockIdx.x), 1u);
       int ok = 1;
       uint32_t spins = 0;
