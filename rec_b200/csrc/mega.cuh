@@ -1338,7 +1338,7 @@ struct Consumers {
           const FixScale fq = norm(l == 0 ? sm.h0 : a.h, L.input_norm, l == 0);
           GroupX gx[1];
           share_limbs(sm.xn, 32, fq);
-          load_limbs(sm.xn, sm.gX, 32, lane, gx[0]);
+          load_limbs(sm.xn, sm.gX, 32, lane, gx[0], lane_half(lane));
           const int qrows[3] = {a.hq * 128, a.hkv * 128, a.hkv * 128};
           for (int r = P.q0; r < P.q1;) {
             int m = 0, base = 0;
@@ -1396,7 +1396,7 @@ struct Consumers {
           GroupX gx[1];
           if (a.hq * 128 == 4096) {
             share_limbs(sm.xn, 64, fo);
-            load_limbs(sm.xn, sm.gX, 64, KCfg<4096>::group(warp & 1, lane, 0), gx[0]);
+            load_limbs(sm.xn, sm.gX, 64, KCfg<4096>::group(warp & 1, lane, 0), gx[0], lane_half(lane));
             for (int r = P.o0; r < P.o1; r += kORows) {
               const int n = min(kORows, P.o1 - r);
               const uint8_t* st = take();
@@ -1405,7 +1405,7 @@ struct Consumers {
             }
           } else {
             share_limbs(sm.xn, 32, fo);
-            load_limbs(sm.xn, sm.gX, 32, lane, gx[0]);
+            load_limbs(sm.xn, sm.gX, 32, lane, gx[0], lane_half(lane));
             for (int r = P.o0; r < P.o1; r += kORows) {
               const int n = min(kORows, P.o1 - r);
               const uint8_t* st = take();
@@ -1459,7 +1459,7 @@ struct Consumers {
         {
           GroupX gx[1];
           share_limbs(sm.xn, 32, fr);
-          load_limbs(sm.xn, sm.gX, 32, lane, gx[0]);
+          load_limbs(sm.xn, sm.gX, 32, lane, gx[0], lane_half(lane));
           int g0, g1;
           split_range(sm.n_loc * a.I / 2, gridDim.x, blockIdx.x, g0, g1);
           g0 *= 2;
@@ -1480,20 +1480,13 @@ struct Consumers {
               lane_rows_partial<2048, 2, 4>(st, sbase, bbase, rows, 0, lane, gx, v, a.sd);
 #pragma unroll
               for (int q = 0; q < 4; ++q) v[q] = __fmul_rn(bfly_sum(v[q]), fr.down);
-              if (lane == 0) {
-                // pair u + q: selection slot loc[(u + q) / I], row (u + q) % I
-                if (va) {
-                  const float gg = rbf(v[0]), uu = rbf(v[1]);
-                  const int gu = u + pa;
-                  a.act[sm.loc[gu / a.I] * a.I + gu % a.I] =
-                      to_bf(__fmul_rn(rbf(__fmul_rn(gg, rbf(rsigmoid(gg)))), uu));
-                }
-                if (vc) {
-                  const float gg = rbf(v[2]), uu = rbf(v[3]);
-                  const int gu = u + pc;
-                  a.act[sm.loc[gu / a.I] * a.I + gu % a.I] =
-                      to_bf(__fmul_rn(rbf(__fmul_rn(gg, rbf(rsigmoid(gg)))), uu));
-                }
+              // pair u + q: selection slot loc[(u + q) / I], row (u + q) % I;
+              // lanes 0 and 1 finish pairs pa and pc side by side
+              if (lane < 2 && (lane == 0 ? va : vc)) {
+                const float gg = rbf(lane == 0 ? v[0] : v[2]), uu = rbf(lane == 0 ? v[1] : v[3]);
+                const int gu = u + (lane == 0 ? pa : pc);
+                a.act[sm.loc[gu / a.I] * a.I + gu % a.I] =
+                    to_bf(__fmul_rn(rbf(__fmul_rn(gg, rbf(rsigmoid(gg)))), uu));
               }
             }
             release();
@@ -1581,7 +1574,7 @@ struct Consumers {
       {
         GroupX gx[1];
         share_limbs(sm.xn, 32, fh);
-        load_limbs(sm.xn, sm.gX, 32, lane, gx[0]);
+        load_limbs(sm.xn, sm.gX, 32, lane, gx[0], lane_half(lane));
         best = -INFINITY;
         best_i = 0x7fffffff;
         int v0, v1;

@@ -283,17 +283,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gateup(const GateUpArgs a) {
         lane_rows_partial<K, SD, 4>(wbase, sbase, bbase, rows, 0, lane, gx, v);
 #pragma unroll
         for (int q = 0; q < 4; ++q) v[q] = __fmul_rn(bfly_sum(v[q]), fs.down);
-        if (lane == 0) {
-          if (va) {
-            const float g = rbf(v[0]), u = rbf(v[1]);
-            const float sig = rbf(rsigmoid(g));
-            a.act[r * a.I + i0 + pa] = to_bf(__fmul_rn(rbf(__fmul_rn(g, sig)), u));
-          }
-          if (vc) {
-            const float g = rbf(v[2]), u = rbf(v[3]);
-            const float sig = rbf(rsigmoid(g));
-            a.act[r * a.I + i0 + pc] = to_bf(__fmul_rn(rbf(__fmul_rn(g, sig)), u));
-          }
+        // lanes 0 and 1 finish pairs pa and pc side by side (the sums are
+        // on every lane after the butterflies)
+        if (lane < 2 && (lane == 0 ? va : vc)) {
+          const float g = rbf(lane == 0 ? v[0] : v[2]), u = rbf(lane == 0 ? v[1] : v[3]);
+          const float sig = rbf(rsigmoid(g));
+          a.act[r * a.I + i0 + (lane == 0 ? pa : pc)] = to_bf(__fmul_rn(rbf(__fmul_rn(g, sig)), u));
         }
       }
     }

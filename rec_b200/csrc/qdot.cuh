@@ -94,17 +94,27 @@ __device__ __forceinline__ float warp_maxabs(const uint16_t* x, int n) {
 
 // A lane's prepared group of x: per word w of the group, byte-packed limbs
 // matching the even nibbles (0,2,4,6) and odd nibbles (1,3,5,7) of the
-// weight word.
+// weight word.  Lanes with bit 2 set (wide rows, see lane_half) hold the
+// group's two 16-byte halves in swapped order (words 4..7, then 0..3), like
+// the weight words they read; the dot product is an exact integer sum, so
+// the order does not change it.
 struct GroupX {
   uint32_t hi_e[8], hi_o[8], lo_e[8], lo_o[8];
   float X;  // float(sum of xi over the group), exact
 };
 
-__device__ __forceinline__ void prep_group(const uint16_t* xg, FixScale fs, GroupX& gx) {
+// Which half of its 32-byte group a lane of a wide row (32 lanes per row,
+// lane l owning group l) reads first: lanes 0-3 of each quarter-warp the
+// low half, lanes 4-7 the high half, so that the quarter-warp's 128-bit
+// shared loads cover all 32 banks (the plain order puts lanes l and l + 4
+// on the same banks).
+__device__ __forceinline__ int lane_half(int l) { return (l >> 2) & 1; }
+
+__device__ __forceinline__ void prep_group(const uint16_t* xg, FixScale fs, GroupX& gx, int sw = 0) {
   int sum = 0;
 #pragma unroll
   for (int w = 0; w < 8; ++w) {
-    const uint4 u = *reinterpret_cast<const uint4*>(xg + 8 * w);
+    const uint4 u = *reinterpret_cast<const uint4*>(xg + 8 * (w ^ (4 * sw)));
     const uint32_t us[4] = {u.x, u.y, u.z, u.w};
     int xi[8];
 #pragma unroll
@@ -156,7 +166,8 @@ template <int K>
 __device__ __forceinline__ void prep_lane_x(const uint16_t* x, FixScale fs, int seg, int l,
                                             GroupX (&gx)[KCfg<K>::GPL]) {
 #pragma unroll
-  for (int m = 0; m < KCfg<K>::GPL; ++m) prep_group(x + KCfg<K>::group(seg, l, m) * 64, fs, gx[m]);
+  for (int m = 0; m < KCfg<K>::GPL; ++m)
+    prep_group(x + KCfg<K>::group(seg, l, m) * 64, fs, gx[m], KCfg<K>::wide ? lane_half(l) : 0);
 }
 
 // Fixed-point limbs of n_groups groups of 64 bf16 values at x (shared
@@ -251,11 +262,12 @@ __device__ __forceinline__ void prep_limbs_to(const uint16_t* x, uint16_t* out, 
 }
 
 // A lane's prepared group g from the shared limbs of prep_limbs_inplace.
-__device__ __forceinline__ void load_limbs(const uint16_t* x, const float* X, int n_groups, int g, GroupX& gx) {
+__device__ __forceinline__ void load_limbs(const uint16_t* x, const float* X, int n_groups, int g, GroupX& gx,
+                                           int sw = 0) {
   const uint4* L = reinterpret_cast<const uint4*>(x);
   uint4 c[8];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) c[k] = L[k * n_groups + g];
+  for (int k = 0; k < 8; ++k) c[k] = L[(k ^ sw) * n_groups + g];  // sw: halves swapped (lane_half)
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
     gx.hi_e[4 * k] = c[k].x; gx.hi_e[4 * k + 1] = c[k].y; gx.hi_e[4 * k + 2] = c[k].z; gx.hi_e[4 * k + 3] = c[k].w;
@@ -279,14 +291,17 @@ __device__ __forceinline__ void lane_rows_partial(const uint8_t* wbase, const ui
 #pragma unroll
   for (int i = 0; i < ILP; ++i) acc[i] = 0.0f;
 #pragma unroll
+  // wide rows: the halves in the lane's order (lane_half); gx matches it
+  const int h0 = KCfg<K>::wide ? 16 * lane_half(l) : 0;
+#pragma unroll
   for (int m = 0; m < KCfg<K>::GPL; ++m) {
     const int g = KCfg<K>::group(seg, l, m);
     uint4 w[ILP][2];
 #pragma unroll
     for (int i = 0; i < ILP; ++i) {
       const uint8_t* p = wbase + rows[i] * KCfg<K>::ROW_BYTES + g * 32;
-      w[i][0] = lds128(p);
-      w[i][1] = lds128(p + 16);
+      w[i][0] = lds128(p + h0);
+      w[i][1] = lds128(p + (16 - h0));
     }
     int D[ILP];
 #pragma unroll
