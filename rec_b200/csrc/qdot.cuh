@@ -290,7 +290,6 @@ __device__ __forceinline__ void lane_rows_partial(const uint8_t* wbase, const ui
   float acc[ILP];
 #pragma unroll
   for (int i = 0; i < ILP; ++i) acc[i] = 0.0f;
-#pragma unroll
   // wide rows: the halves in the lane's order (lane_half); gx matches it
   const int h0 = KCfg<K>::wide ? 16 * lane_half(l) : 0;
 #pragma unroll
