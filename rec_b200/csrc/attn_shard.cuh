@@ -8,12 +8,13 @@
 //     super-chunk's items in order, stores the partial into every rank's
 //     exchange buffer with plain peer stores (NVLink); after a warp barrier
 //     lane 0 fences at system scope and raises each rank's per-head counter
-//     with a system-scope atomic;
-//   k_attn_final_xch: one warp per q head waits (bounded) until its counter
-//     holds every super-chunk of the context, folds [sink] and the
-//     super-chunks in order -- the single-GPU combine, so every rank's output
-//     equals the one-GPU output bit for bit -- writes the output and resets
-//     the counter.
+//     with a system-scope atomic.  The warp of (head h, first local slot)
+//     then waits (bounded) until its own counter holds every super-chunk of
+//     the context, folds [sink] and the super-chunks in order -- the
+//     single-GPU combine, so every rank's output equals the one-GPU output
+//     bit for bit -- writes the output and resets the counter.  Every CTA of
+//     the grid is resident while it waits (32 x local-slot one-warp CTAs),
+//     and the next kernel launches only after each of them has started.
 // The exchange slots alternate between two copies by the parity of the
 // global layer step (steps completed, a device counter, times n_layers plus
 // the layer), so a rank one layer ahead never overwrites data a peer is
@@ -66,29 +67,24 @@ __global__ void __launch_bounds__(32) k_attn_combine_xch(const AttnXchArgs a) {
   grid_launch_dependents();
   const AttnCounts C = attn_counts(*a.position + 1);
   const int h = blockIdx.x, s = a.super_lo + blockIdx.y;
-  if (s >= min(a.super_hi, C.n_super)) return;
-  const int item0 = a.token_base / (kAttBlock * C.nbi);
-  const int icap = items_cap(a.capacity);
-  Partial4 P = empty_partial();
-  fold_partials(P, a.partials + size_t(h) * icap * kPartialFloats, s * C.per_super - item0,
-                min((s + 1) * C.per_super, C.n_items) - item0);
   const int par = xch_layer_parity(a);
-  for (int q = 0; q < a.world; ++q) store_partial(xch_super(a.xch[q], a.xl, par, h, s), P);
-  __syncwarp();
-  if (lane == 0) {
-    __threadfence_system();  // cumulative over the warp's stores (ordered by the warp barrier)
-    for (int q = 0; q < a.world; ++q) atomicAdd_system(xch_head_cnt(a.xch[q], a.xl, par, h), 1u);
+  if (s < min(a.super_hi, C.n_super)) {
+    const int item0 = a.token_base / (kAttBlock * C.nbi);
+    const int icap = items_cap(a.capacity);
+    Partial4 P = empty_partial();
+    fold_partials(P, a.partials + size_t(h) * icap * kPartialFloats, s * C.per_super - item0,
+                  min((s + 1) * C.per_super, C.n_items) - item0);
+    for (int q = 0; q < a.world; ++q) store_partial(xch_super(a.xch[q], a.xl, par, h, s), P);
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_system();  // cumulative over the warp's stores (ordered by the warp barrier)
+      for (int q = 0; q < a.world; ++q) atomicAdd_system(xch_head_cnt(a.xch[q], a.xl, par, h), 1u);
+    }
   }
-}
-
-__global__ void __launch_bounds__(32) k_attn_final_xch(const AttnXchArgs a) {
-  const int lane = threadIdx.x, h = blockIdx.x;
-  // the wait covers this rank's k_attn_combine_xch (its stores and counter
-  // raises); the peers' arrive through the counters
-  if (a.pdl) grid_wait();
-  grid_launch_dependents();
-  const AttnCounts C = attn_counts(*a.position + 1);
-  const int par = xch_layer_parity(a);
+  if (blockIdx.y != 0) return;
+  // CTA (h, 0) of every rank (present even when the rank holds no
+  // super-chunk of this context yet): wait for every super-chunk of head h,
+  // then the single-GPU combine
   uint8_t* own = a.xch[a.rank];
   unsigned* cnt = xch_head_cnt(own, a.xl, par, h);
   int ok = 1;

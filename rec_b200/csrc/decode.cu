@@ -340,9 +340,7 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
         x.status = status;
         x.pdl = pdl;
         const int local = std::max(1, c->super_hi - c->super_lo);
-        e = launch(k_attn_combine_xch, dim3(d.n_q_heads, local), 32, 0, st, pdl, x);
-        if (e != cudaSuccess) return e;
-        return launch(k_attn_final_xch, dim3(d.n_q_heads), 32, 0, st, pdl, x);
+        return launch(k_attn_combine_xch, dim3(d.n_q_heads, local), 32, 0, st, pdl, x);
       }
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(d.n_q_heads, std::max(1, c->n_super_max));
