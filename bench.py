@@ -67,6 +67,9 @@ def parse():
     p.add_argument("--config4-steps", type=int, default=32)
     p.add_argument("--profile-phases", action="store_true",
                    help="also record the persistent kernel's phase timeline (printed to stderr)")
+    p.add_argument("--layer-stamps", type=int, default=None, metavar="LAYER",
+                   help="diagnostics: in-layer stamps of the persistent kernel at config 3, 1K context, for "
+                        "one layer (needs a library built with REC_LAYER_STAMPS=1)")
     return p.parse_args()
 
 
@@ -890,6 +893,68 @@ def run_config1(args):
           flush=True)
 
 
+# Stamp slots of the persistent kernel's diagnostic build (mega.cuh stamp()):
+# consumer warp 0 of each CTA unless marked (producer).
+STAMP_SLOTS = {
+    11: "A start (after the Q barrier)", 12: "A item start", 19: "A queries + new K/V row ready",
+    29: "A first KV block taken", 16: "A tiles folded", 17: "A tiles done", 18: "A item partial stored",
+    13: "A item done", 31: "A output of a head group written (its last CTA)", 24: "(producer) KV blocks issued",
+    40: "O start (after the A barrier)", 48: "O input loaded", 41: "O fixed-point scale ready", 42: "O rows done",
+    43: "R start (after the O barrier)", 44: "R norm done", 45: "R router row done", 0: "G wait for the selection",
+    14: "(producer) router logits landed", 49: "(producer) softmax / sigmoid done",
+    15: "(producer) selection published", 20: "(producer) routing returned", 1: "G selection seen",
+    50: "(producer) first G slot acquired", 21: "(producer) G chunk 1 issued", 22: "(producer) G chunk 2 issued",
+    23: "(producer) G chunk 3+ issued", 2: "G chunk 1 taken", 3: "G chunk 1 done", 4: "G chunk 2 taken",
+    5: "G chunk 2 done", 6: "G chunk 3 taken", 7: "G chunk 3 done", 10: "G done", 39: "D start (after the G barrier)",
+    33: "D limbs ready", 34: "D first chunk taken", 46: "D chunk 1 done", 47: "D chunk 2 done", 35: "D rows done",
+    36: "D mix + residual done",
+}
+
+
+def run_layer_stamps(args):
+    """Diagnostics: globaltimer stamps inside one layer of the persistent
+    kernel (config 3, 8-bit cache of 1,024 quantized synthetic tokens, step
+    0 of a one-token launch), per slot over the CTAs that record it: count,
+    min, median, max in µs after the earliest A-start stamp."""
+    import ctypes as C
+    import numpy as np
+    import torch
+
+    from rec_b200._lib import check, lib
+    from rec_b200.model import CONFIG3, KVCache, generate_weights
+    from rec_b200.session import DecodeSession
+
+    torch.cuda.set_device(0)
+    cfg, ctx, layer = CONFIG3, 1024, args.layer_stamps
+    w = generate_weights(cfg, seed=0, device="cuda")
+    kv = KVCache.allocate(cfg, (ctx + 300 + 255) // 256 * 256)
+    kv.fill_random(ctx, seed=2)
+    sess = DecodeSession(w, kv)
+    sess.greedy(5, ctx, 8)
+    n_cta = torch.cuda.get_device_properties(0).multi_processor_count
+    buf = torch.zeros(n_cta * 64, dtype=torch.int64, device="cuda")
+    check(lib().rec_set_layer_profile(sess.ctx, C.c_void_p(buf.data_ptr()), layer))
+    sess.greedy(-1, 0, 1)
+    torch.cuda.synchronize()
+    check(lib().rec_set_layer_profile(sess.ctx, None, 0))
+    s = buf.view(n_cta, 64).cpu().numpy().astype(np.int64)
+    if not (s > 0).any():
+        print(json.dumps({"layer_stamps": None, "note": "library built without REC_LAYER_STAMPS"}))
+        return
+    ref = s[:, 11][s[:, 11] > 0].min() if (s[:, 11] > 0).any() else s[s > 0].min()
+    rows = []
+    for k in range(64):
+        v = s[:, k]
+        v = v[v > 0]
+        if v.size:
+            r = (v - ref) / 1e3
+            rows.append({"slot": k, "what": STAMP_SLOTS.get(k, "?"), "ctas": int(v.size),
+                         "min_us": round(float(r.min()), 2), "median_us": round(float(np.median(r)), 2),
+                         "max_us": round(float(r.max()), 2)})
+    rows.sort(key=lambda x: x["median_us"])
+    print(json.dumps({"layer_stamps": {"layer": layer, "context": ctx, "kv_bits": cfg.kv_bits, "slots": rows}}))
+
+
 def main():
     args = parse()
     if args.config1:
@@ -898,6 +963,8 @@ def main():
         run_sample_head(args)
     elif args.prefill:
         run_prefill(args)
+    elif args.layer_stamps is not None:
+        run_layer_stamps(args)
     elif args.attn_sweep:
         run_attn_sweep(args)
     elif args.impl == "reference":
