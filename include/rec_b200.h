@@ -54,6 +54,18 @@ enum { REC_SCALE_FP16 = 0, REC_SCALE_BF16 = 1 };
 enum { REC_ROUTER_SOFTMAX = 0, REC_ROUTER_SIGMOID = 1 };
 /* Model flags. */
 enum { REC_FLAG_SINKS = 1, REC_FLAG_QK_NORM = 2 };
+/* Layer kinds (RecLayerWeights.kind bits), the reference Flint model's layer
+ * options (engine/src/rec_mlx/model.py:14-37,155-163,216-271):
+ *   REC_LAYER_DENSE    the FFN is a dense SwiGLU MLP of dense_inter rows
+ *                      (`mlp_only_layers`, model.py:216-224,262-266) instead of
+ *                      the routed experts; gate/up/down hold its matrices;
+ *   REC_LAYER_NO_ROPE  no rotary embedding of q and k (`no_rope_layer_indices`,
+ *                      the "global" layers, model.py:158-163,196-198);
+ *   REC_LAYER_SLIDING  attention over the last sliding_window positions only
+ *                      (`layer_types` "sliding_attention", model.py:281-313).
+ * A model that uses any of them, or a shared expert, runs on the graph
+ * schedule of separate kernels. */
+enum { REC_LAYER_DENSE = 1, REC_LAYER_NO_ROPE = 2, REC_LAYER_SLIDING = 4 };
 
 /* Model shape (reference ModelArgs, engine/src/rec_mlx/model.py:14-37). */
 typedef struct RecModelDesc {
@@ -73,6 +85,16 @@ typedef struct RecModelDesc {
   int32_t flags;       /* REC_FLAG_* */
   float rms_eps;
   float rope_theta;
+  /* Flint layer options (0 = off).  shared_inter: rows of the always-on
+   * shared SwiGLU expert of every MoE layer (256, 512, 768 or 1024), added to
+   * the routed mix as mlp = bf16(mix + shared) before the residual
+   * (model.py:243,254; megakernel.py:955-958).  dense_inter: rows of the
+   * dense MLP of REC_LAYER_DENSE layers (2048, 4096 or 6144).  sliding_window:
+   * positions a REC_LAYER_SLIDING layer attends, the current one included
+   * (the reference's window is 513). */
+  int32_t shared_inter;
+  int32_t dense_inter;
+  int32_t sliding_window;
 } RecModelDesc;
 
 /* int4 g64 affine matrix in MLX layout: codes uint32[N, K/8], scales and
@@ -93,6 +115,11 @@ typedef struct RecLayerWeights {
   const void* sinks;      /* bf16 [Hq] or NULL */
   const void* q_norm;     /* bf16 [D] or NULL */
   const void* k_norm;     /* bf16 [D] or NULL */
+  int32_t kind;           /* REC_LAYER_* bits (0: routed experts, RoPE, full attention) */
+  /* the shared expert of an MoE layer when shared_inter > 0: [Is, H], [Is, H],
+   * [H, Is]; otherwise unused.  A REC_LAYER_DENSE layer has no router: its
+   * gate/up/down are [Id, H], [Id, H], [H, Id] and router may be NULL. */
+  RecQMat shared_gate, shared_up, shared_down;
 } RecLayerWeights;
 
 typedef struct RecGlobalWeights {

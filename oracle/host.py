@@ -47,12 +47,17 @@ class HostModel:
         def opt(t):
             return None if t is None else keep(_np(t))
 
+        def qopt(qt):
+            return abi.RecQMat() if qt is None else q(qt)
+
         layers = []
         for L in weights.layers:
             layers.append(abi.RecLayerWeights(
                 input_norm=keep(_np(L.input_norm)), post_norm=keep(_np(L.post_norm)), q=q(L.q), k=q(L.k),
-                v=q(L.v), o=q(L.o), router=keep(_np(L.router)), expert_bias=opt(L.expert_bias), gate=q(L.gate),
-                up=q(L.up), down=q(L.down), sinks=opt(L.sinks), q_norm=opt(L.q_norm), k_norm=opt(L.k_norm)))
+                v=q(L.v), o=q(L.o), router=opt(L.router), expert_bias=opt(L.expert_bias), gate=q(L.gate),
+                up=q(L.up), down=q(L.down), sinks=opt(L.sinks), q_norm=opt(L.q_norm), k_norm=opt(L.k_norm),
+                kind=getattr(L, "kind", 0), shared_gate=qopt(getattr(L, "shared_gate", None)),
+                shared_up=qopt(getattr(L, "shared_up", None)), shared_down=qopt(getattr(L, "shared_down", None))))
         self.layers = (abi.RecLayerWeights * len(layers))(*layers)
         self.glob = abi.RecGlobalWeights(embed=q(weights.embed), final_norm=keep(_np(weights.final_norm)),
                                          lm_head=q(weights.lm_head))

@@ -500,15 +500,16 @@ static float tile_sum(const float* x) {
   return (S[0] + S[1]) + (S[2] + S[3]);
 }
 
-/* Folds the tile of one q head over tokens [t0, t0+32) ∩ [0, T) into the
- * running state st (attn_core.cuh tile_fold):
+/* Folds the tile of one q head over tokens [t0, t0+32) ∩ [lo, T) into the
+ * running state st (attn_core.cuh tile_fold; lo > 0: the first position of a
+ * sliding window; a tile with no such token leaves st unchanged):
  *   m' = max(m, max score); alpha = aexp(m - m'); p_j = aexp(s_j - m') (0 beyond T);
  *   l' = fma(l, alpha, tile_sum(p));
  *   per V group (64 dims): w_j = p_j * scale_j, x_j = p_j * bias_j (0 beyond T);
  *      F = min(14 - exponent(max|w| * (1 + 2^-7)), 100); wq_j = rint(w_j * 2^F);
  *      acc_d' = fma(acc_d, alpha, fma(float(sum_j wq_j * code_jd), 2^-F, tile_sum(x))). */
 static void att_tile(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bits, int t0, int T, int base,
-                     Partial* st) {
+                     int lo, Partial* st) {
   int words = 128 * bits / 32;
   const uint32_t* KC = (const uint32_t*)kv->k_codes;
   const uint32_t* VC = (const uint32_t*)kv->v_codes;
@@ -516,12 +517,13 @@ static void att_tile(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bit
   const uint16_t *VS = (const uint16_t*)kv->v_scales, *VB = (const uint16_t*)kv->v_biases;
   int nvalid = T - t0;
   if (nvalid > ATT_TILE) nvalid = ATT_TILE;
-  if (nvalid <= 0) return;
+  const int first = lo > t0 ? lo - t0 : 0;
+  if (nvalid <= first) return;
   float s[ATT_TILE], p[ATT_TILE];
   float mt = NEG_INF;
   for (int j = 0; j < ATT_TILE; ++j) {
     int64_t slot = (int64_t)g * C + t0 - base + j;
-    s[j] = j < nvalid ? att_score(Q, KC + slot * words, KS + slot * 2, KB + slot * 2, bits) : NEG_INF;
+    s[j] = j >= first && j < nvalid ? att_score(Q, KC + slot * words, KS + slot * 2, KB + slot * 2, bits) : NEG_INF;
     mt = fmaxf(mt, s[j]);
   }
   const float mn = fmaxf(st->m, mt);
@@ -533,8 +535,8 @@ static void att_tile(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bit
     float mx = 0.0f;
     for (int j = 0; j < ATT_TILE; ++j) {
       int64_t slot = (int64_t)g * C + t0 - base + j;
-      w[j] = j < nvalid ? p[j] * bf(VS[slot * 2 + gr]) : 0.0f;
-      x[j] = j < nvalid ? p[j] * bf(VB[slot * 2 + gr]) : 0.0f;
+      w[j] = j >= first && j < nvalid ? p[j] * bf(VS[slot * 2 + gr]) : 0.0f;
+      x[j] = j >= first && j < nvalid ? p[j] * bf(VB[slot * 2 + gr]) : 0.0f;
       mx = fmaxf(mx, fabsf(w[j]));
     }
     int E = (int)((f2u(mx * 1.0078125f) >> 23) & 0xFF) - 127;
@@ -546,7 +548,7 @@ static void att_tile(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bit
     const float B = tile_sum(x);
     for (int d = 64 * gr; d < 64 * gr + 64; ++d) {
       int32_t acc = 0;
-      for (int j = 0; j < nvalid; ++j) {
+      for (int j = first; j < nvalid; ++j) {
         int64_t slot = (int64_t)g * C + t0 - base + j;
         acc += wq[j] * (int32_t)kv_code(VC + slot * words, bits, d);
       }
@@ -560,7 +562,7 @@ static void att_tile(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bit
  * warp w folds tiles 8b + w of the item's blocks in order into its running
  * state; the eight warp states are folded as a tree ((w0 w1)(w2 w3))((w4 w5)(w6 w7)). */
 static void att_item(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bits, int it, int T, int base,
-                     Partial* out) {
+                     int lo, Partial* out) {
   const int nbi = att_item_blocks((T + ATT_BLOCK - 1) / ATT_BLOCK);
   Partial st[ATT_WARPS];
   for (int w = 0; w < ATT_WARPS; ++w) {
@@ -568,7 +570,7 @@ static void att_item(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bit
     for (int b = it * nbi; b < (it + 1) * nbi; ++b) {
       int t0 = b * ATT_BLOCK + w * ATT_TILE;
       if (t0 >= T) break;
-      att_tile(Q, kv, g, C, bits, t0, T, base, &st[w]);
+      att_tile(Q, kv, g, C, bits, t0, T, base, lo, &st[w]);
     }
   }
   for (int step = 1; step < ATT_WARPS; step *= 2)
@@ -581,8 +583,8 @@ static void att_item(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bit
  * supers[h * (s_hi - s_lo) + s - s_lo] = items of super s (64 blocks) merged
  * in order.  The cache holds tokens from `base` on (token t in slot t - base
  * of each head's C rows): a rank of a split session passes its own slice. */
-ORC_API void orc_attention_supers_shard(const uint16_t* q, const RecKVLayer* kv, int Hq, int Hkv, int C, int bits,
-                                        int T, int base, int s_lo, int s_hi, Partial* supers) {
+static void attention_supers(const uint16_t* q, const RecKVLayer* kv, int Hq, int Hkv, int C, int bits, int T,
+                             int base, int lo, int s_lo, int s_hi, Partial* supers) {
   int nblocks = (T + ATT_BLOCK - 1) / ATT_BLOCK;
   int nbi = att_item_blocks(nblocks), per_super = ATT_SUPER / nbi;
   int nitems = (nblocks + nbi - 1) / nbi;
@@ -597,11 +599,24 @@ ORC_API void orc_attention_supers_shard(const uint16_t* q, const RecKVLayer* kv,
       p_empty(S);
       for (int it = s * per_super; it < (s + 1) * per_super && it < nitems; ++it) {
         Partial P;
-        att_item(&Q, kv, g, C, bits, it, T, base, &P);
+        att_item(&Q, kv, g, C, bits, it, T, base, lo, &P);
         p_merge(S, &P);
       }
     }
   }
+}
+
+ORC_API void orc_attention_supers_shard(const uint16_t* q, const RecKVLayer* kv, int Hq, int Hkv, int C, int bits,
+                                        int T, int base, int s_lo, int s_hi, Partial* supers) {
+  attention_supers(q, kv, Hq, Hkv, C, bits, T, base, 0, s_lo, s_hi, supers);
+}
+
+/* A sliding-window layer: tokens [lo, T) only, lo = max(0, T - window)
+ * (attn.cuh window_start); items below lo stay empty. */
+ORC_API void orc_attention_supers_window(const uint16_t* q, const RecKVLayer* kv, int Hq, int Hkv, int C, int bits,
+                                         int T, int window, Partial* supers, int n_super) {
+  const int lo = window > 0 && T > window ? T - window : 0;
+  attention_supers(q, kv, Hq, Hkv, C, bits, T, 0, lo, 0, n_super, supers);
 }
 
 /* Super-chunk partials of every q head over tokens [0, T) of one layer's
@@ -721,6 +736,23 @@ ORC_API void orc_mix(const uint16_t* down, int H, const float* w, int k, uint16_
   for (int i = 0; i < H; ++i) out[i] = to_bf(mix_elem(down + i, H, w, k));
 }
 
+/* SwiGLU MLP of one matrix triple on normalised x (a dense layer, or the
+ * shared expert): out = down(bf16(bf16(g*sig)*u)), I rows
+ * (model.py:216-224; the dense down is one GEMV of K = I). */
+static void mlp(const RecQMat* gm, const RecQMat* um, const RecQMat* dm, int sd, int H, int I, const uint16_t* xn,
+                uint16_t* out) {
+  uint16_t* g = (uint16_t*)malloc(sizeof(uint16_t) * I);
+  uint16_t* u = (uint16_t*)malloc(sizeof(uint16_t) * I);
+  uint16_t* act = (uint16_t*)malloc(sizeof(uint16_t) * I);
+  gemv(gm, sd, 0, I, H, xn, NULL, g);
+  gemv(um, sd, 0, I, H, xn, NULL, u);
+  for (int i = 0; i < I; ++i) act[i] = swiglu(bf(g[i]), bf(u[i]));
+  gemv(dm, sd, 0, H, I, act, NULL, out);
+  free(g);
+  free(u);
+  free(act);
+}
+
 /* MoE FFN on normalised x: writes the bf16 mix (without residual). */
 static void moe_ffn(const RecModelDesc* md, const RecLayerWeights* L, const uint16_t* xn,
                     const int32_t* ids, const float* w, uint16_t* mix, uint16_t* act_out,
@@ -745,6 +777,13 @@ static void moe_ffn(const RecModelDesc* md, const RecLayerWeights* L, const uint
   free(u);
 }
 
+/* The FFN block of one layer on the residual h -> h_out:
+ *   dense layer (REC_LAYER_DENSE): h + bf16 MLP output;
+ *   MoE layer: router, experts, bf16 mix in rank order; with a shared expert
+ *   (md->shared_inter > 0) mlp = bf16(mix + shared) (megakernel.py:955-958);
+ *   h_out = bf16(h + mlp).
+ * ids / w / act / down describe the routed experts (untouched for a dense
+ * layer). */
 ORC_API void orc_moe(const RecModelDesc* md, const RecLayerWeights* L, const uint16_t* h,
                      int32_t* ids, float* w, uint16_t* act, uint16_t* down, uint16_t* h_out) {
   int H = md->hidden, E = md->n_experts;
@@ -752,9 +791,19 @@ ORC_API void orc_moe(const RecModelDesc* md, const RecLayerWeights* L, const uin
   float* logits = (float*)malloc(sizeof(float) * E);
   uint16_t* mix = (uint16_t*)malloc(sizeof(uint16_t) * H);
   rmsnorm(h, (const uint16_t*)L->post_norm, H, md->rms_eps, xn);
-  orc_router_logits((const uint16_t*)L->router, xn, E, H, logits);
-  orc_route(logits, E, md->top_k, md->router_mode, (const float*)L->expert_bias, ids, w);
-  moe_ffn(md, L, xn, ids, w, mix, act, down);
+  if (L->kind & REC_LAYER_DENSE) {
+    mlp(&L->gate, &L->up, &L->down, md->scale_dtype, H, md->dense_inter, xn, mix);
+  } else {
+    orc_router_logits((const uint16_t*)L->router, xn, E, H, logits);
+    orc_route(logits, E, md->top_k, md->router_mode, (const float*)L->expert_bias, ids, w);
+    moe_ffn(md, L, xn, ids, w, mix, act, down);
+    if (md->shared_inter > 0) {
+      uint16_t* sh = (uint16_t*)malloc(sizeof(uint16_t) * H);
+      mlp(&L->shared_gate, &L->shared_up, &L->shared_down, md->scale_dtype, H, md->shared_inter, xn, sh);
+      for (int i = 0; i < H; ++i) mix[i] = to_bf(bf(mix[i]) + bf(sh[i]));
+      free(sh);
+    }
+  }
   for (int i = 0; i < H; ++i) h_out[i] = to_bf(bf(h[i]) + bf(mix[i]));
   free(xn);
   free(logits);
@@ -1077,16 +1126,18 @@ ORC_API int orc_decode_step(const RecModelDesc* md, const RecLayerWeights* layer
     uint16_t* q = qkv;
     uint16_t* k = qkv + Hq * D;
     uint16_t* v = qkv + (Hq + Hkv) * D;
+    const int rope = !(L->kind & REC_LAYER_NO_ROPE); /* NoPE ("global") layers skip RoPE */
     for (int hh = 0; hh < Hq; ++hh) {
       if ((md->flags & REC_FLAG_QK_NORM) && L->q_norm) head_norm(q + hh * D, (const uint16_t*)L->q_norm, md->rms_eps);
-      rope_head(q + hh * D, cs);
+      if (rope) rope_head(q + hh * D, cs);
     }
     for (int g = 0; g < Hkv; ++g) {
       if ((md->flags & REC_FLAG_QK_NORM) && L->k_norm) head_norm(k + g * D, (const uint16_t*)L->k_norm, md->rms_eps);
-      rope_head(k + g * D, cs);
+      if (rope) rope_head(k + g * D, cs);
     }
     kv_store(&kv[li], Hkv, C, md->kv_bits, pos, k, v);
-    orc_attention_supers(q, &kv[li], Hq, Hkv, C, md->kv_bits, T, supers, n_super);
+    orc_attention_supers_window(q, &kv[li], Hq, Hkv, C, md->kv_bits, T,
+                                (L->kind & REC_LAYER_SLIDING) ? md->sliding_window : 0, supers, n_super);
     orc_attention_final(supers, Hq, n_super,
                         (md->flags & REC_FLAG_SINKS) ? (const uint16_t*)L->sinks : NULL, att);
     gemv(&L->o, sd, 0, H, Hq * D, att, NULL, o);

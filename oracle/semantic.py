@@ -157,11 +157,24 @@ class SemanticKV:
                           self.bits, 1).astype(np.float64)
 
 
+def mlp(gate, up, down, sd: int, xn: np.ndarray) -> np.ndarray:
+    """SwiGLU MLP (model.py:216-224): bf16 gate / up projections, the
+    activation's rounding points, bf16 down projection."""
+    g = rbf(_dq(gate, sd) @ xn)
+    u = rbf(_dq(up, sd) @ xn)
+    return rbf(_dq(down, sd) @ silu_mul(g, u).astype(np.float64))
+
+
 def layer_step(cfg, L, kv: SemanticKV, h: np.ndarray, pos: int, sd: int) -> np.ndarray:
     """One decoder layer (model.py:258-271) for the token at `pos`; h is the
-    bf16-valued residual; returns the new residual (bf16-valued float64)."""
+    bf16-valued residual; returns the new residual (bf16-valued float64).
+    Layer options (getattr(L, "kind")): a dense MLP instead of the experts
+    (model.py:262-266), no RoPE (model.py:158-163,196-198), attention over the
+    last sliding_window positions (model.py:302-313); a shared expert added
+    to the routed mix as bf16(mix + shared) (model.py:243,254)."""
     from . import f32_to_bf16
 
+    kind = getattr(L, "kind", 0)
     hq, hkv = cfg.n_q_heads, cfg.n_kv_heads
     xn = rmsnorm_f(h, L.input_norm, cfg.rms_eps)
     q = rbf(_dq(L.q, sd) @ xn).reshape(hq, 128)
@@ -170,14 +183,20 @@ def layer_step(cfg, L, kv: SemanticKV, h: np.ndarray, pos: int, sd: int) -> np.n
     if L.q_norm is not None:
         q = np.stack([rmsnorm_f(r, L.q_norm, cfg.rms_eps) for r in q])
         k = np.stack([rmsnorm_f(r, L.k_norm, cfg.rms_eps) for r in k])
-    q = rbf(rope(q, pos, cfg.rope_theta))
-    k = rbf(rope(k, pos, cfg.rope_theta))
+    if not kind & 2:  # REC_LAYER_NO_ROPE
+        q = rbf(rope(q, pos, cfg.rope_theta))
+        k = rbf(rope(k, pos, cfg.rope_theta))
     kv.append(pos, k, v)
     K, V = kv.dequant("k", pos + 1), kv.dequant("v", pos + 1)
+    if kind & 4:  # REC_LAYER_SLIDING: the last sliding_window positions
+        lo = max(0, pos + 1 - cfg.sliding_window)
+        K, V = K[:, lo:], V[:, lo:]
     sinks = None if L.sinks is None else np.asarray(L.sinks, np.uint16)
     att = rbf(attention(f32_to_bf16(q.astype(np.float32)), K, V, sinks=sinks, bf16_probs=True)).reshape(-1)
     h = rbf(h + rbf(_dq(L.o, sd) @ att.astype(np.float64))).astype(np.float64)
     xn2 = rmsnorm_f(h, L.post_norm, cfg.rms_eps)
+    if kind & 1:  # REC_LAYER_DENSE
+        return rbf(h + mlp(L.gate, L.up, L.down, sd, xn2).astype(np.float64)).astype(np.float64)
     logits = rbf(_bfv(L.router).reshape(cfg.n_experts, -1) @ xn2).astype(np.float64)
     bias = None if L.expert_bias is None else np.asarray(L.expert_bias, np.float64)
     ids, wts = route(logits, cfg.top_k, cfg.router_mode, bias)
@@ -189,6 +208,8 @@ def layer_step(cfg, L, kv: SemanticKV, h: np.ndarray, pos: int, sd: int) -> np.n
         act = silu_mul(g, u).astype(np.float64)
         downs.append(rbf(_dq(L.down, sd, slice(int(e) * H, (int(e) + 1) * H)) @ act))
     mix = expert_mix(np.stack(downs).astype(np.float32), np.asarray(wts, np.float32))
+    if getattr(cfg, "shared_inter", 0):
+        mix = rbf(mix + mlp(L.shared_gate, L.shared_up, L.shared_down, sd, xn2))
     return rbf(h + mix.astype(np.float64)).astype(np.float64)
 
 

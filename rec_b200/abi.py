@@ -19,6 +19,10 @@ REC_ROUTER_SOFTMAX = 0
 REC_ROUTER_SIGMOID = 1
 REC_FLAG_SINKS = 1
 REC_FLAG_QK_NORM = 2
+# layer kinds (RecLayerWeights.kind bits)
+REC_LAYER_DENSE = 1
+REC_LAYER_NO_ROPE = 2
+REC_LAYER_SLIDING = 4
 
 
 class RecModelDesc(C.Structure):
@@ -39,6 +43,9 @@ class RecModelDesc(C.Structure):
         ("flags", C.c_int32),
         ("rms_eps", C.c_float),
         ("rope_theta", C.c_float),
+        ("shared_inter", C.c_int32),
+        ("dense_inter", C.c_int32),
+        ("sliding_window", C.c_int32),
     ]
 
 
@@ -62,6 +69,10 @@ class RecLayerWeights(C.Structure):
         ("sinks", C.c_void_p),
         ("q_norm", C.c_void_p),
         ("k_norm", C.c_void_p),
+        ("kind", C.c_int32),
+        ("shared_gate", RecQMat),
+        ("shared_up", RecQMat),
+        ("shared_down", RecQMat),
     ]
 
 

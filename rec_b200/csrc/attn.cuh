@@ -34,7 +34,7 @@ struct AttnArgs {
   uint16_t* v_biases;
   int capacity;            // C, multiple of 256
   int hq, hkv;
-  const float* rope;       // [positions, 128] cos | sin, row = absolute position
+  const float* rope;       // [positions, 128] cos | sin, row = absolute position; null: no RoPE (NoPE layer)
   const uint16_t* q_norm;  // bf16 [128] or null
   const uint16_t* k_norm;
   float eps;
@@ -52,8 +52,13 @@ struct AttnArgs {
   // super_hi) (one GPU: token_base 0, super_lo 0, super_hi kAttAllSupers)
   int token_base;
   int super_lo, super_hi;
+  // > 0: a sliding-window layer attends positions [max(0, p - window + 1), p]
+  int window;
 };
 constexpr int kAttAllSupers = 1 << 30;
+
+// First attended position of a step at position p (sliding window or 0).
+__host__ __device__ inline int window_start(int p, int window) { return window > 0 && p + 1 > window ? p + 1 - window : 0; }
 
 // Item partial slots per head: one per block covers every item size.
 __host__ __device__ inline int items_cap(int capacity) { return capacity / kAttBlock; }
@@ -209,24 +214,27 @@ __device__ __forceinline__ void warps_fold_store(WarpState& st, int warp, AttnSc
 }
 
 // This warp's tile (tile `warp`) of one block held in the given K / V tiles
-// (n tokens of the block valid; new_row >= 0: that row is the new token).
+// (rows [first, n) of the block valid: first > 0 only in the block where a
+// sliding window starts; new_row >= 0: that row is the new token).  A tile
+// with no valid row leaves the state unchanged.
 // SPLIT: full tiles take the unmasked instance of tile_fold (same results);
 // the persistent kernel keeps one instance for its instruction footprint.
 template <int BITS, bool SPLIT = false>
 __device__ __forceinline__ void block_tiles(uint32_t* kc, uint16_t* ks, uint16_t* kb, uint32_t* vc, uint16_t* vs,
                                             uint16_t* vb, int n, int new_row, const AttnScratch& sc, int warp,
-                                            WarpState& st) {
+                                            WarpState& st, int first = 0) {
   constexpr int RW = 128 * BITS / 32;
   const int t0 = warp * kAttTile;
   const int nvalid = min(kAttTile, n - t0);
-  if (nvalid <= 0) return;
+  const int tfirst = max(0, first - t0);
+  if (nvalid <= tfirst) return;
   if (new_row >= t0 && new_row < t0 + kAttTile) patch_row<BITS>(kc, ks, kb, vc, vs, vb, new_row, sc);
-  if (SPLIT && nvalid == kAttTile)
+  if (SPLIT && nvalid == kAttTile && tfirst == 0)
     tile_fold<BITS, true>(kc + t0 * RW, ks + 2 * t0, kb + 2 * t0, vc + t0 * RW, vs + 2 * t0, vb + 2 * t0, nvalid,
                           sc.qf, st);
   else
     tile_fold<BITS, false>(kc + t0 * RW, ks + 2 * t0, kb + 2 * t0, vc + t0 * RW, vs + 2 * t0, vb + 2 * t0, nvalid,
-                           sc.qf, st);
+                           sc.qf, st, tfirst);
 }
 
 // ---------------------------------------------------------------------------
@@ -297,11 +305,15 @@ __global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnAr
   const int n_items = (nblk + nbi - 1) / nbi;
   const int per_super = super_items(nblk);
   // this rank's items: those of super-chunks [super_lo, super_hi)
-  const int i_lo = min(a.super_lo, (n_items + per_super - 1) / per_super) * per_super;
+  // a sliding window skips the items below its first position (their
+  // partials are never read)
+  const int lo = window_start(p, a.window);
+  const int i_first = lo / (kAttBlock * nbi);
+  const int i_lo = max(i_first, min(a.super_lo, (n_items + per_super - 1) / per_super) * per_super);
   const int i_hi = a.super_hi >= (n_items + per_super - 1) / per_super ? n_items : a.super_hi * per_super;
   const int items = max(0, i_hi - i_lo) * a.hkv;
   const int item0 = a.token_base / (kAttBlock * nbi);  // local index of the first item held here
-  const float* cs = a.rope + size_t(p) * 128;
+  const float* cs = a.rope ? a.rope + size_t(p) * 128 : nullptr;
   const int icap = items_cap(a.capacity);
   uint32_t phase = 0;  // bit s: parity of stage s
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
@@ -330,7 +342,7 @@ __global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnAr
       const int n = min(kAttBlock, T - b * kAttBlock);
       const int new_row = (has_new && p / kAttBlock == b) ? p - b * kAttBlock : -1;
       AttnStage<BITS>& S = sm.st[s];
-      block_tiles<BITS, true>(S.kc, S.ks, S.kb, S.vc, S.vs, S.vb, n, new_row, sm.sc, warp, st);
+      block_tiles<BITS, true>(S.kc, S.ks, S.kb, S.vc, S.vs, S.vb, n, new_row, sm.sc, warp, st, lo - b * kAttBlock);
       // the tile may have been patched through the generic proxy, and the
       // next bulk copy into this stage must not overtake this block's reads
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -362,11 +374,12 @@ static __global__ void __launch_bounds__(32) k_attn_combine(const AttnArgs a) {
   const int nbi = item_blocks(nblk), per_super = super_items(nblk);
   const int n_items = (nblk + nbi - 1) / nbi;
   const int n_super = (n_items + per_super - 1) / per_super;
+  const int i_first = window_start(p, a.window) / (kAttBlock * nbi);  // items below a sliding window are empty
   const int h = blockIdx.x;
   const int icap = items_cap(a.capacity);
   for (int s = blockIdx.y; s < n_super; s += gridDim.y) {
     Partial4 P = empty_partial();
-    fold_partials(P, a.partials + size_t(h) * icap * kPartialFloats, s * per_super,
+    fold_partials(P, a.partials + size_t(h) * icap * kPartialFloats, max(s * per_super, i_first),
                   min((s + 1) * per_super, n_items));
     float* dst = a.supers + (size_t(h) * a.n_super_max + s) * kPartialFloats;
     if (lane == 0) {

@@ -123,8 +123,10 @@ __device__ __forceinline__ void head_norm4(float (&x)[4], const uint16_t* w, flo
 
 // RoPE of a 128-dim head held by a warp (lane l: dims 4l..4l+3), through a
 // 128-float shared scratch.  Pairs (i, i+64): lo' = bf16(fma(lo, c, -hi*s)),
-// hi' = bf16(fma(lo, s, hi*c)).
+// hi' = bf16(fma(lo, s, hi*c)).  cs == nullptr: a layer without rotary
+// embedding (x unchanged).
 __device__ __forceinline__ void rope4(float (&x)[4], const float* cs, float* scratch) {
+  if (!cs) return;
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int j = 0; j < 4; ++j) scratch[4 * lane + j] = x[j];
@@ -345,7 +347,8 @@ __device__ __forceinline__ float tile_max(const float (&v)[8]) {
 // the K and V tiles in shared memory, row
 // stride RW words; scales/biases [token][2], 8-byte aligned) for the 8 q
 // heads, folded into the warp state (canonical order):
-//   s_t = score of token t (0..nvalid-1), -inf beyond;
+//   s_t = score of token t (first..nvalid-1), -inf outside (first > 0: the
+//   start of a sliding window inside the tile);
 //   m' = max(m, max_t s_t); alpha = aexp(m - m'); p_t = aexp(s_t - m');
 //   l' = fma(l, alpha, tile_sum(p));
 //   per V group: w_t = p_t scale_t, x_t = p_t bias_t (0 beyond nvalid);
@@ -355,7 +358,7 @@ __device__ __forceinline__ float tile_max(const float (&v)[8]) {
 template <int BITS, bool FULL = false>
 __device__ __forceinline__ void tile_fold(const uint32_t* kc, const uint16_t* ks, const uint16_t* kb,
                                           const uint32_t* vc, const uint16_t* vs, const uint16_t* vb, int nvalid,
-                                          const QFrags& qf, WarpState& st) {
+                                          const QFrags& qf, WarpState& st, int first = 0) {
   constexpr int RW = 128 * BITS / 32;
   constexpr uint32_t M4 = 0x0F0F0F0Fu;
   const int lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
@@ -411,7 +414,7 @@ __device__ __forceinline__ void tile_fold(const uint32_t* kc, const uint16_t* ks
         float u = __fmaf_rn(b0, meta.x, __fmul_rn(s0, float(D0)));
         u = __fmaf_rn(s1, float(D1), u);
         u = __fmaf_rn(b1, meta.y, u);
-        p[2 * nt + j] = (FULL || t + j < nvalid) ? rbf(__fmul_rn(u, meta.z)) : -INFINITY;
+        p[2 * nt + j] = (FULL || (t + j >= first && t + j < nvalid)) ? rbf(__fmul_rn(u, meta.z)) : -INFINITY;
       }
     }
     const float mt = tile_max(p);
@@ -442,7 +445,8 @@ __device__ __forceinline__ void tile_fold(const uint32_t* kc, const uint16_t* ks
         const uint32_t sw = j ? vsp[nt].y : vsp[nt].x, bw = j ? vbp[nt].y : vbp[nt].x;
         const float sc = __uint_as_float(g ? (sw & 0xFFFF0000u) : (sw << 16));
         const float bi = __uint_as_float(g ? (bw & 0xFFFF0000u) : (bw << 16));
-        const bool ok = FULL || 8 * nt + 2 * tq + j < nvalid;
+        const int tt = 8 * nt + 2 * tq + j;
+        const bool ok = FULL || (tt >= first && tt < nvalid);
         w[v] = ok ? __fmul_rn(p[v], sc) : 0.0f;
         x[v] = ok ? __fmul_rn(p[v], bi) : 0.0f;
         mx = fmaxf(mx, fabsf(w[v]));

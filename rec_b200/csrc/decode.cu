@@ -159,6 +159,12 @@ struct RecCtx {
   unsigned* counters = nullptr;
   uint16_t *h = nullptr, *qkv = nullptr, *attn = nullptr, *xn = nullptr, *act = nullptr, *logits = nullptr,
            *trace = nullptr;
+  // Flint layer options (a shared expert, dense-MLP / NoPE / sliding layers):
+  // the model runs on the graph schedule
+  bool flint = false;
+  uint16_t *act_shared = nullptr, *d_shared = nullptr;  // shared expert activations and output
+  int* one_id = nullptr;     // device constant {0}: the single "expert" of a dense MLP or shared expert
+  float* one_wt = nullptr;   // device constant {1.0f}
   float *router_logits = nullptr, *wts = nullptr, *cand_val = nullptr, *partials = nullptr, *supers = nullptr,
         *rope = nullptr;
   int *ids = nullptr, *cand_idx = nullptr;
@@ -199,7 +205,7 @@ struct Layout {
 
 enum Region {
   rCtl, rCounters, rMegaCnt, rRouterLL, rH, rQkv, rAttn, rXn, rAct, rLogits, rTrace, rRouter, rIds, rWts, rCandV, rCandI,
-  rPartials, rSupers, rMegaLayers, rRope, rCount
+  rPartials, rSupers, rMegaLayers, rRope, rFlint, rCount
 };
 
 // Positions the RoPE table covers: the local cache, or the whole context when
@@ -221,7 +227,8 @@ Layout layout_of(const RecCtx* c) {
   sz[rQkv] = size_t(d.n_q_heads + 2 * d.n_kv_heads) * 128 * 2;
   sz[rAttn] = size_t(d.n_q_heads) * 128 * 2;
   sz[rXn] = size_t(d.hidden) * 2;
-  sz[rAct] = size_t(d.top_k) * d.moe_inter * 2;
+  // routed activations, then the shared expert's; a dense MLP's in the same space
+  sz[rAct] = std::max(size_t(d.top_k) * d.moe_inter + size_t(d.shared_inter), size_t(d.dense_inter)) * 2;
   sz[rLogits] = size_t(d.vocab) * 2;
   sz[rTrace] = size_t(d.n_layers + 1) * d.hidden * 2;
   sz[rRouter] = size_t(d.n_experts) * 4;
@@ -232,6 +239,7 @@ Layout layout_of(const RecCtx* c) {
   sz[rPartials] = size_t(d.n_q_heads) * nblk * kPartialFloats * 4;
   sz[rSupers] = size_t(d.n_q_heads) * nsup * kPartialFloats * 4;
   sz[rRope] = size_t(rope_rows(c)) * 128 * 4;
+  sz[rFlint] = size_t(d.hidden) * 2 + 16;  // shared expert output bf16 [H], then {0} and {1.0f}
   Layout L;
   size_t o = 0;
   for (int i = 0; i < rCount; ++i) {
@@ -242,9 +250,14 @@ Layout layout_of(const RecCtx* c) {
   return L;
 }
 
-// Kernels of one decode step, in launch order (per layer: kKQkv..kKDown).
+// Kernels of one decode step, in launch order (per layer: kKQkv..kKDown; a
+// layer with a shared expert runs kKSharedGateUp and kKSharedDown between
+// kKGateUp and kKDown).
 enum KernelKind { kKEmbed = 0, kKQkv, kKAttn, kKCombine, kKOproj, kKRouter, kKGateUp, kKDown, kKHead, kKStepEnd,
-                  kKCount };
+                  kKCount, kKSharedGateUp = kKCount, kKSharedDown, kKAll };
+
+bool layer_dense(const RecCtx* c, int li) { return (c->layers[li].kind & REC_LAYER_DENSE) != 0; }
+bool layer_shared(const RecCtx* c, int li) { return c->d.shared_inter > 0 && !layer_dense(c, li); }
 
 template <int SD>
 cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool pdl) {
@@ -301,7 +314,8 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
       a.super_hi = c->world > 1 ? c->super_hi : kAttAllSupers;
       a.hq = d.n_q_heads;
       a.hkv = d.n_kv_heads;
-      a.rope = c->rope;
+      a.rope = (L.kind & REC_LAYER_NO_ROPE) ? nullptr : c->rope;
+      a.window = (L.kind & REC_LAYER_SLIDING) ? d.sliding_window : 0;
       a.q_norm = (d.flags & REC_FLAG_QK_NORM) ? (const uint16_t*)L.q_norm : nullptr;
       a.k_norm = (d.flags & REC_FLAG_QK_NORM) ? (const uint16_t*)L.k_norm : nullptr;
       a.eps = d.rms_eps;
@@ -388,28 +402,88 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
       a.counter = c->counters + 1;
       a.status = status;
       a.pdl = pdl;
+      if (layer_dense(c, li)) {  // a dense MLP: the post-attention norm only
+        a.norm_only = 1;
+        return launch(k_router<2048>, 1, kThreads, sizeof(RouterSmem<2048>), st, pdl, a);
+      }
       e = launch(k_router<2048>, (d.n_experts + kWarps - 1) / kWarps, kThreads, sizeof(RouterSmem<2048>), st, pdl, a);
       return e;
     }
-    case kKGateUp: {  // experts gate/up + SwiGLU
+    case kKGateUp:         // experts gate/up + SwiGLU (a dense layer: its MLP as one "expert")
+    case kKSharedGateUp: {  // the shared expert's gate/up + SwiGLU
+      const bool one = kind == kKSharedGateUp || layer_dense(c, li);
+      const RecQMat& G = kind == kKSharedGateUp ? L.shared_gate : L.gate;
+      const RecQMat& U = kind == kKSharedGateUp ? L.shared_up : L.up;
       GateUpArgs a = {};
-      a.gate = {(const uint32_t*)L.gate.w, (const uint16_t*)L.gate.scales, (const uint16_t*)L.gate.biases};
-      a.up = {(const uint32_t*)L.up.w, (const uint16_t*)L.up.scales, (const uint16_t*)L.up.biases};
+      a.gate = {(const uint32_t*)G.w, (const uint16_t*)G.scales, (const uint16_t*)G.biases};
+      a.up = {(const uint32_t*)U.w, (const uint16_t*)U.scales, (const uint16_t*)U.biases};
       a.xn = c->xn;
-      a.ids = c->ids;
-      a.k = d.top_k;
-      a.I = d.moe_inter;
-      a.expert_lo = c->world > 1 ? c->e_lo : 0;
-      a.expert_hi = c->world > 1 ? c->e_hi : d.n_experts;
-      a.act = c->act;
+      a.ids = one ? c->one_id : c->ids;
+      a.k = one ? 1 : d.top_k;
+      a.I = kind == kKSharedGateUp ? d.shared_inter : (layer_dense(c, li) ? d.dense_inter : d.moe_inter);
+      a.expert_lo = c->world > 1 && !one ? c->e_lo : 0;
+      a.expert_hi = one ? 1 : (c->world > 1 ? c->e_hi : d.n_experts);
+      a.act = kind == kKSharedGateUp ? c->act_shared : c->act;
       a.status = status;
       a.pdl = pdl;
       constexpr int RSP = 16;
       e = launch(k_gateup<SD, RSP, 3>, grid2, kThreads, sizeof(GateUpSmem<RSP, 3>), st, pdl, a);
       return e;
     }
-    case kKDown: {  // experts down + bf16 mix + residual
+    case kKSharedDown: {  // the shared expert's down projection into d_shared
       DownArgs a = {};
+      a.down = {(const uint32_t*)L.shared_down.w, (const uint16_t*)L.shared_down.scales,
+                (const uint16_t*)L.shared_down.biases};
+      a.act = c->act_shared;
+      a.ids = c->one_id;
+      a.wts = c->one_wt;
+      a.k = 1;
+      a.H = H;
+      a.expert_lo = 0;
+      a.expert_hi = 1;
+      a.h = c->h;
+      a.dout = c->d_shared;
+      a.world = 1;
+      a.status = status;
+      a.pdl = pdl;
+      const int dgrid = std::max(grid, H / (2 * DownSmem<768>::RMAX / 2));
+      switch (d.shared_inter) {
+        case 256: return launch(k_down<256, SD>, dgrid, kThreads, sizeof(DownSmem<256>), st, pdl, a);
+        case 512: return launch(k_down<512, SD>, dgrid, kThreads, sizeof(DownSmem<512>), st, pdl, a);
+        case 768: return launch(k_down<768, SD>, dgrid, kThreads, sizeof(DownSmem<768>), st, pdl, a);
+        case 1024: return launch(k_down<1024, SD>, dgrid, kThreads, sizeof(DownSmem<1024>), st, pdl, a);
+        default: return cudaErrorInvalidValue;
+      }
+    }
+    case kKDown: {  // experts down + bf16 mix + residual
+      if (layer_dense(c, li)) {  // a dense MLP's down projection + residual (the trace row too)
+        GemvArgs g = {};
+        g.mat[0] = {(const uint32_t*)L.down.w, (const uint16_t*)L.down.scales, (const uint16_t*)L.down.biases};
+        g.rows[0] = H;
+        g.total_rows = H;
+        g.x = c->act;
+        g.resid = c->h;
+        g.trace_out = c->trace + size_t(li + 1) * H;
+        g.status = status;
+        g.pdl = pdl;
+        switch (d.dense_inter) {
+          case 2048: {
+            using Kd = GemvSmem<2048, gemv_rs<2048>(), 3>;
+            return launch(k_gemv<2048, SD, gemv_rs<2048>(), 3, kEpiResidual>, grid, kThreads, sizeof(Kd), st, pdl, g);
+          }
+          case 4096: {
+            using Kd = GemvSmem<4096, gemv_rs<4096>(), 3>;
+            return launch(k_gemv<4096, SD, gemv_rs<4096>(), 3, kEpiResidual>, grid, kThreads, sizeof(Kd), st, pdl, g);
+          }
+          case 6144: {
+            using Kd = GemvSmem<6144, gemv_rs<6144>(), 3>;
+            return launch(k_gemv<6144, SD, gemv_rs<6144>(), 3, kEpiResidual>, grid, kThreads, sizeof(Kd), st, pdl, g);
+          }
+          default: return cudaErrorInvalidValue;
+        }
+      }
+      DownArgs a = {};
+      a.shared_out = layer_shared(c, li) ? c->d_shared : nullptr;
       a.down = {(const uint32_t*)L.down.w, (const uint16_t*)L.down.scales, (const uint16_t*)L.down.biases};
       a.act = c->act;
       a.ids = c->ids;
@@ -464,18 +538,35 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
   }
 }
 
+// The FFN kernels of layer li from the router on (the shared expert's two
+// kernels between the routed gate/up and the routed down + mix).
 template <int SD>
-cudaError_t enqueue_step_sd(RecCtx* c, cudaStream_t st) {
+cudaError_t enqueue_ffn_sd(RecCtx* c, int li, cudaStream_t st, bool pdl) {
+  cudaError_t e = enqueue_kernel_sd<SD>(c, kKRouter, li, st, pdl);
+  if (e == cudaSuccess) e = enqueue_kernel_sd<SD>(c, kKGateUp, li, st, pdl);
+  if (e == cudaSuccess && layer_shared(c, li)) e = enqueue_kernel_sd<SD>(c, kKSharedGateUp, li, st, pdl);
+  if (e == cudaSuccess && layer_shared(c, li)) e = enqueue_kernel_sd<SD>(c, kKSharedDown, li, st, pdl);
+  if (e == cudaSuccess) e = enqueue_kernel_sd<SD>(c, kKDown, li, st, pdl);
+  return e;
+}
+
+// One step through the first n_layers layers (all of them in the captured
+// graph; fewer for a partial-depth call), the lm_head and the step end.
+template <int SD>
+cudaError_t enqueue_step_sd(RecCtx* c, cudaStream_t st, int n_layers) {
   cudaError_t e = enqueue_kernel_sd<SD>(c, kKEmbed, 0, st, false);
-  for (int li = 0; li < c->d.n_layers && e == cudaSuccess; ++li)
-    for (int k = kKQkv; k <= kKDown && e == cudaSuccess; ++k) e = enqueue_kernel_sd<SD>(c, k, li, st, true);
+  for (int li = 0; li < n_layers && e == cudaSuccess; ++li) {
+    for (int k = kKQkv; k <= kKOproj && e == cudaSuccess; ++k) e = enqueue_kernel_sd<SD>(c, k, li, st, true);
+    if (e == cudaSuccess) e = enqueue_ffn_sd<SD>(c, li, st, true);
+  }
   if (e == cudaSuccess) e = enqueue_kernel_sd<SD>(c, kKHead, 0, st, true);
   if (e == cudaSuccess) e = enqueue_kernel_sd<SD>(c, kKStepEnd, 0, st, true);
   return e;
 }
 
-cudaError_t enqueue_step(RecCtx* c, cudaStream_t st) {
-  return c->d.scale_dtype == REC_SCALE_FP16 ? enqueue_step_sd<0>(c, st) : enqueue_step_sd<1>(c, st);
+cudaError_t enqueue_step(RecCtx* c, cudaStream_t st, int n_layers) {
+  return c->d.scale_dtype == REC_SCALE_FP16 ? enqueue_step_sd<0>(c, st, n_layers)
+                                            : enqueue_step_sd<1>(c, st, n_layers);
 }
 
 int ensure_graph(RecCtx* c) {
@@ -483,7 +574,7 @@ int ensure_graph(RecCtx* c) {
   if (!c->cap_stream) REC_CHECK_CUDA(cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking));
   cudaGraph_t graph = nullptr;
   REC_CHECK_CUDA(cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal));
-  cudaError_t e = enqueue_step(c, c->cap_stream);
+  cudaError_t e = enqueue_step(c, c->cap_stream, c->d.n_layers);
   cudaError_t e2 = cudaStreamEndCapture(c->cap_stream, &graph);
   if (e != cudaSuccess || e2 != cudaSuccess) {
     if (graph) cudaGraphDestroy(graph);
@@ -531,8 +622,15 @@ REC_API int rec_create(const RecModelDesc* desc, RecCtx** out) {
   REC_CHECK_ARG(d.kv_bits == 4 || d.kv_bits == 8, "kv_bits must be 4 or 8");
   REC_CHECK_ARG(d.router_mode == REC_ROUTER_SOFTMAX || d.router_mode == REC_ROUTER_SIGMOID, "bad router mode");
   REC_CHECK_ARG(d.n_layers >= 1 && d.n_layers <= kMaxLayers, "n_layers must be in 1..%d", kMaxLayers);
+  REC_CHECK_ARG(d.shared_inter == 0 || d.shared_inter == 256 || d.shared_inter == 512 || d.shared_inter == 768 ||
+                    d.shared_inter == 1024,
+                "shared_inter must be 0, 256, 512, 768 or 1024");
+  REC_CHECK_ARG(d.dense_inter == 0 || d.dense_inter == 2048 || d.dense_inter == 4096 || d.dense_inter == 6144,
+                "dense_inter must be 0, 2048, 4096 or 6144");
+  REC_CHECK_ARG(d.sliding_window >= 0, "sliding_window must be >= 0");
   RecCtx* c = new RecCtx();
   c->d = d;
+  c->flint = d.shared_inter > 0;
   c->grid = sm_count();
   *out = c;
   return REC_OK;
@@ -542,6 +640,8 @@ REC_API int rec_set_shard(RecCtx* c, const RecShard* sh) {
   REC_CHECK_ARG(c && sh, "rec_set_shard: null argument");
   const RecShard& s = *sh;
   REC_CHECK_ARG(s.world >= 1 && s.world <= kMaxWorld, "world size must be 1..%d", kMaxWorld);
+  REC_CHECK_ARG(s.world == 1 || !c->flint, "a model with layer options (shared expert, dense / NoPE / sliding "
+                "layers) runs on one GPU");
   REC_CHECK_ARG(s.rank >= 0 && s.rank < s.world, "rank outside the world");
   REC_CHECK_ARG(c->grid <= kMaxGrid, "too many SMs for the exchange layout");
   REC_CHECK_ARG(s.capacity_total > 0 && s.capacity_total % kAttBlock == 0,
@@ -589,12 +689,25 @@ REC_API void rec_destroy(RecCtx* ctx) {
 REC_API int rec_set_weights(RecCtx* c, const RecLayerWeights* layers, int32_t n_layers, const RecGlobalWeights* g) {
   REC_CHECK_ARG(c && layers && g, "rec_set_weights: null argument");
   REC_CHECK_ARG(n_layers == c->d.n_layers, "expected %d layers, got %d", c->d.n_layers, n_layers);
+  bool flint = c->d.shared_inter > 0;
   for (int i = 0; i < n_layers; ++i) {
     const RecLayerWeights& L = layers[i];
-    REC_CHECK_ARG(L.input_norm && L.post_norm && L.router, "layer %d: missing norm/router weights", i);
+    const bool dense = (L.kind & REC_LAYER_DENSE) != 0;
+    REC_CHECK_ARG((L.kind & ~(REC_LAYER_DENSE | REC_LAYER_NO_ROPE | REC_LAYER_SLIDING)) == 0,
+                  "layer %d: unknown kind bits 0x%x", i, L.kind);
+    REC_CHECK_ARG(!dense || c->d.dense_inter > 0, "layer %d: a dense-MLP layer needs dense_inter", i);
+    REC_CHECK_ARG(!(L.kind & REC_LAYER_SLIDING) || c->d.sliding_window > 0,
+                  "layer %d: a sliding-window layer needs sliding_window", i);
+    REC_CHECK_ARG(c->world == 1 || L.kind == 0, "layer %d: layer options need an unsharded session", i);
+    flint = flint || L.kind != 0;
+    REC_CHECK_ARG(L.input_norm && L.post_norm && (dense || L.router), "layer %d: missing norm/router weights", i);
     REC_CHECK_ARG(valid_qmat(L.q) && valid_qmat(L.k) && valid_qmat(L.v) && valid_qmat(L.o) && valid_qmat(L.gate) &&
                       valid_qmat(L.up) && valid_qmat(L.down),
                   "layer %d: quantized matrices must be non-null and 16-byte aligned", i);
+    REC_CHECK_ARG(dense || c->d.shared_inter == 0 ||
+                      (valid_qmat(L.shared_gate) && valid_qmat(L.shared_up) && valid_qmat(L.shared_down)),
+                  "layer %d: shared-expert matrices must be non-null and 16-byte aligned", i);
+    if (dense) continue;
     REC_CHECK_ARG(aligned16(L.router), "layer %d: router must be 16-byte aligned", i);
     REC_CHECK_ARG(c->d.router_mode != REC_ROUTER_SIGMOID || L.expert_bias, "layer %d: sigmoid router needs a bias", i);
     REC_CHECK_ARG(!(c->d.flags & REC_FLAG_SINKS) || L.sinks, "layer %d: sinks enabled but missing", i);
@@ -604,6 +717,7 @@ REC_API int rec_set_weights(RecCtx* c, const RecLayerWeights* layers, int32_t n_
   c->layers.assign(layers, layers + n_layers);
   c->g = *g;
   c->has_weights = true;
+  c->flint = flint;
   drop_graph(c);
   return REC_OK;
 }
@@ -698,6 +812,14 @@ REC_API int rec_set_workspace(RecCtx* c, void* ws, size_t bytes) {
   c->rope = reinterpret_cast<float*>(b + L.off[rRope]);
   c->mega_cnt = reinterpret_cast<unsigned*>(b + L.off[rMegaCnt]);
   c->mega_layers = reinterpret_cast<MegaLayer*>(b + L.off[rMegaLayers]);
+  c->act_shared = c->act + size_t(c->d.top_k) * c->d.moe_inter;
+  c->d_shared = reinterpret_cast<uint16_t*>(b + L.off[rFlint]);
+  c->one_id = reinterpret_cast<int*>(b + L.off[rFlint] + size_t(c->d.hidden) * 2);
+  c->one_wt = reinterpret_cast<float*>(c->one_id + 1);
+  {
+    const int one[2] = {0, 0x3f800000};  // {0, 1.0f}
+    REC_CHECK_CUDA(cudaMemcpy(c->one_id, one, sizeof(one), cudaMemcpyHostToDevice));
+  }
   // control block and counters start at zero
   REC_CHECK_CUDA(cudaMemset(b, 0, L.off[rH]));
   // layer table of the persistent kernel
@@ -746,6 +868,7 @@ REC_API int rec_set_workspace(RecCtx* c, void* ws, size_t bytes) {
 // ranks always runs on the persistent kernel.
 constexpr double kMegaAttnBytes = 24.0 * 1024 * 1024;
 static int schedule_for(const RecCtx* c, int position) {
+  if (c->flint) return kSchedGraph;  // layer options exist on the graph schedule only
   const char* sched = std::getenv("REC_SCHEDULE");
   if (sched && std::strcmp(sched, "graph") == 0) return kSchedGraph;
   if (c->d.n_experts > kMegaMaxExperts) return kSchedGraph;
@@ -943,7 +1066,8 @@ REC_API int rec_decode_layers(RecCtx* c, int32_t token, int32_t position, int32_
   REC_CHECK_ARG(layer_count >= 1 && layer_count <= c->d.n_layers, "layer_count %d outside 1..%d", layer_count,
                 c->d.n_layers);
   if (layer_count == c->d.n_layers) return rec_decode_step(c, token, position, logits_dev, trace_dev, stream);
-  REC_CHECK_ARG(c->d.n_experts <= kMegaMaxExperts, "a partial-depth step needs at most %d experts", kMegaMaxExperts);
+  REC_CHECK_ARG(c->flint || c->d.n_experts <= kMegaMaxExperts, "a partial-depth step needs at most %d experts",
+                kMegaMaxExperts);
   if (position < 0 || position >= position_limit(c)) {
     set_error("position %d outside the KV capacity", position);
     return REC_ELIMIT;
@@ -952,13 +1076,20 @@ REC_API int rec_decode_layers(RecCtx* c, int32_t token, int32_t position, int32_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   k_set_step<<<1, 32, 0, st>>>(c->ctl, token, position, 0, make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0), 0);
   REC_CHECK_CUDA(cudaGetLastError());
-  // the persistent kernel with a shorter layer loop (its H phase follows the
-  // last layer run)
-  c->sched = kSchedMega;
-  c->layers_run = layer_count;
-  const cudaError_t e = launch_mega(c, 1, st);
-  c->layers_run = 0;
-  REC_CHECK_CUDA(e);
+  if (c->flint) {
+    // layer options: the graph schedule's kernels for the first layers,
+    // launched directly (the captured graph runs every layer)
+    c->sched = kSchedGraph;
+    REC_CHECK_CUDA(enqueue_step(c, st, layer_count));
+  } else {
+    // the persistent kernel with a shorter layer loop (its H phase follows
+    // the last layer run)
+    c->sched = kSchedMega;
+    c->layers_run = layer_count;
+    const cudaError_t e = launch_mega(c, 1, st);
+    c->layers_run = 0;
+    REC_CHECK_CUDA(e);
+  }
   if (logits_dev)
     REC_CHECK_CUDA(cudaMemcpyAsync(logits_dev, c->logits, size_t(c->d.vocab) * 2, cudaMemcpyDeviceToDevice, st));
   if (trace_dev)
@@ -1016,6 +1147,8 @@ REC_API int rec_prefill_chunk(RecCtx* c, const int32_t* tokens_dev, int32_t posi
   const RecModelDesc& d = c->d;
   REC_CHECK_ARG(tokens_dev && workspace, "rec_prefill_chunk: null pointer");
   REC_CHECK_ARG(c->world == 1, "rec_prefill_chunk: an unsharded session only");
+  REC_CHECK_ARG(!c->flint, "rec_prefill_chunk: layer options (shared expert, dense / NoPE / sliding layers) are "
+                "prefilled by decode steps");
   REC_CHECK_ARG(d.hidden == 2048 && d.moe_inter % 256 == 0, "rec_prefill_chunk: hidden 2048 and I a multiple of 256");
   REC_CHECK_ARG(t >= 1 && t <= 16384, "rec_prefill_chunk: %d tokens outside 1..16384", t);
   if (position < 0 || int64_t(position) + t > position_limit(c)) {
@@ -1189,10 +1322,11 @@ REC_API int32_t rec_schedule_for(const RecCtx* c, int32_t position) {
 REC_API int rec_launch_kernel(RecCtx* c, int32_t kind, int32_t layer, void* stream) {
   int rc = check_ready(c);
   if (rc) return rc;
-  REC_CHECK_ARG(kind >= 0 && kind < kKCount, "unknown kernel kind %d", kind);
+  REC_CHECK_ARG(kind >= 0 && kind < kKAll, "unknown kernel kind %d", kind);
   rc = ensure_graph(c);
   if (rc) return rc;
   REC_CHECK_ARG(layer >= 0 && layer < c->d.n_layers, "layer %d out of range", layer);
+  REC_CHECK_ARG(kind < kKCount || layer_shared(c, layer), "layer %d has no shared expert", layer);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = c->d.scale_dtype == REC_SCALE_FP16 ? enqueue_kernel_sd<0>(c, kind, layer, st, false)
                                                      : enqueue_kernel_sd<1>(c, kind, layer, st, false);
@@ -1210,11 +1344,8 @@ REC_API int rec_router_moe(RecCtx* c, int32_t layer, void* h_dev, int32_t* ids_d
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t hb = size_t(c->d.hidden) * 2;
   REC_CHECK_CUDA(cudaMemcpyAsync(c->h, h_dev, hb, cudaMemcpyDeviceToDevice, st));
-  for (int k = kKRouter; k <= kKDown; ++k) {
-    cudaError_t e = c->d.scale_dtype == REC_SCALE_FP16 ? enqueue_kernel_sd<0>(c, k, layer, st, false)
-                                                       : enqueue_kernel_sd<1>(c, k, layer, st, false);
-    REC_CHECK_CUDA(e);
-  }
+  REC_CHECK_CUDA(c->d.scale_dtype == REC_SCALE_FP16 ? enqueue_ffn_sd<0>(c, layer, st, false)
+                                                    : enqueue_ffn_sd<1>(c, layer, st, false));
   REC_CHECK_CUDA(cudaMemcpyAsync(h_dev, c->h, hb, cudaMemcpyDeviceToDevice, st));
   if (ids_dev)
     REC_CHECK_CUDA(cudaMemcpyAsync(ids_dev, c->ids, size_t(c->d.top_k) * 4, cudaMemcpyDeviceToDevice, st));

@@ -57,6 +57,7 @@ struct GemvArgs {
   float eps;
   uint16_t* out;           // bf16 rows (kEpiStore, kEpiArgmax)
   uint16_t* resid;         // bf16 residual updated in place (kEpiResidual)
+  uint16_t* trace_out;     // kEpiResidual: also a copy of the updated rows (a layer's trace row), or null
   float* cand_val;         // kEpiArgmax: per-CTA best value
   int* cand_idx;           //             per-CTA best index
   unsigned* counter;       //             CTA arrival counter (reset by the last CTA)
@@ -98,7 +99,8 @@ struct StageCursor {
 // Rows computed together by one warp (independent dependency chains).
 template <int K>
 constexpr int gemv_ilp() { return KCfg<K>::wide ? 4 : 1; }
-// Stage rows: one full pass of the CTA over its row slots.
+// Stage rows: one full pass of the CTA over its row slots (K = 6144: two
+// teams of three warps; the other two warps only wait on the stages).
 template <int K>
 constexpr int gemv_rs() {
   return (kWarps / (KCfg<K>::wide ? KCfg<K>::SEG : 1)) * (32 / KCfg<K>::T) * gemv_ilp<K>();
@@ -151,8 +153,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   // narrow K, 8 rows per warp with 4 lanes each.
   constexpr int SEG = C::SEG;
   constexpr int TEAM = C::wide ? SEG : 1;
-  static_assert(kWarps % TEAM == 0, "teams must tile the CTA");
   constexpr int TEAMS = kWarps / TEAM;
+  static_assert(TEAMS >= 1, "a row needs at most 8 warps");
   constexpr int ROWS_PER_WARP = 32 / C::T;
   const int seg = C::wide ? warp % TEAM : 0;
   const int team = warp / TEAM;
@@ -178,7 +180,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
       // Row slots are walked uniformly by whole warps so that shuffles see
       // every lane; slots past the stage's rows compute nothing.
       constexpr int SLOTS = TEAMS * ROWS_PER_WARP;  // rows per sub-pass
-      for (int rb = 0; rb < nrows; rb += SLOTS * ILP) {
+      // warps outside the teams (kWarps % TEAM of them) compute nothing
+      for (int rb = 0; team < TEAMS && rb < nrows; rb += SLOTS * ILP) {
         int rows[ILP];
         bool valid[ILP];
 #pragma unroll
@@ -228,7 +231,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
             if constexpr (EPI == kEpiStore) {
               a.out[grow] = to_bf(v[i]);
             } else if constexpr (EPI == kEpiResidual) {
-              a.resid[grow] = to_bf(__fadd_rn(res[i], rbf(v[i])));
+              const uint16_t hn = to_bf(__fadd_rn(res[i], rbf(v[i])));
+              a.resid[grow] = hn;
+              if (a.trace_out) a.trace_out[grow] = hn;
             } else {
               uint16_t o = to_bf(v[i]);
               a.out[grow] = o;

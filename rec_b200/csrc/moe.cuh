@@ -30,6 +30,7 @@ struct RouterArgs {
   unsigned* counter;
   int* status;
   int pdl;
+  int norm_only;           // a dense-MLP layer: only the RMSNorm into xn_out (one CTA), no routing
 };
 
 template <int H>
@@ -69,6 +70,7 @@ __global__ void __launch_bounds__(kThreads) k_router(const RouterArgs a) {
   if (blockIdx.x == 0)
     for (int i = threadIdx.x * 8; i < H; i += kThreads * 8)
       *reinterpret_cast<uint4*>(a.xn_out + i) = *reinterpret_cast<const uint4*>(sm.xn + i);
+  if (a.norm_only) return;
   if (e < a.E) {
     float acc = 0.0f;
 #pragma unroll
@@ -324,6 +326,10 @@ struct DownArgs {
   uint16_t* h;             // residual (mix mode)
   uint16_t* trace_row;     // bf16 [H] copy of the new residual, or null
   uint16_t* dout;          // expert-parallel mode: bf16 [k, H] expert outputs (local ranks only)
+  // the shared expert's output bf16 [H] (Flint MoE layers), or null: added to
+  // the routed mix as mlp = bf16(mix + shared) before the residual
+  // (megakernel.py:955-958)
+  const uint16_t* shared_out;
   int* status;
   int pdl;
   // a session split over ranks (world > 1): the local experts' outputs go
@@ -348,7 +354,7 @@ struct DownSmem {
 // Mix mode (single device): every CTA owns output rows [i0, i1) and computes
 // them for all k experts (warp r = rank r), then mixes in rank order:
 // m = bf16(d_0*bf16(w_0)) + 0; m = bf16(bf16(d_r*bf16(w_r)) + 0 + m);
-// h = bf16(h + m).
+// with a shared expert m = bf16(m + shared); h = bf16(h + m).
 template <int I, int SD>
 __global__ void __launch_bounds__(kThreads, 1) k_down(const DownArgs a) {
   using S = DownSmem<I>;
@@ -488,6 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_down(const DownArgs a) {
       const float t = __fadd_rn(rbf(__fmul_rn(sm.d[rr][i], rbf(a.wts[rr]))), 0.0f);
       m = rr == 0 ? t : rbf(__fadd_rn(t, m));
     }
+    if (a.shared_out) m = rbf(__fadd_rn(m, bf(a.shared_out[i0 + i])));
     const uint16_t hn = to_bf(__fadd_rn(bf(a.h[i0 + i]), m));
     a.h[i0 + i] = hn;
     if (a.trace_row) a.trace_row[i0 + i] = hn;

@@ -215,7 +215,10 @@ class QATSession:
                 raise PrefillCancelled()
             self.prompt_cache.checkpoint()
             part = tokens[begin:begin + chunk]
-            if self.prefill_mode == "chunked":
+            # the tensor-core chunk path covers the routed-expert layers; a model
+            # with Flint layer options (shared expert, dense / NoPE / sliding
+            # layers) is prefilled by its decode step
+            if self.prefill_mode == "chunked" and not self.engine.cfg.has_layer_options:
                 out = self.engine._guard(state, lambda: sess.prefill_chunk(part, begin))
             else:
                 for i, t in enumerate(part):

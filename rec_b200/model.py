@@ -36,6 +36,28 @@ class ModelConfig:
     flags: int = 0
     rms_eps: float = 1e-6
     rope_theta: float = 1e6
+    # Flint layer options (reference ModelArgs, model.py:14-37): an always-on
+    # shared expert of shared_inter rows in every MoE layer; dense SwiGLU MLP
+    # layers (`mlp_only_layers`) of dense_inter rows; layers without RoPE
+    # (`no_rope_layer_indices`); sliding-window layers (`layer_types`) that
+    # attend the last sliding_window positions.  Any of them puts the model
+    # on the graph schedule.
+    shared_inter: int = 0
+    dense_layers: tuple = ()
+    dense_inter: int = 0
+    no_rope_layers: tuple = ()
+    sliding_layers: tuple = ()
+    sliding_window: int = 0
+
+    def layer_kind(self, i: int) -> int:
+        """REC_LAYER_* bits of layer i."""
+        return ((abi.REC_LAYER_DENSE if i in self.dense_layers else 0)
+                | (abi.REC_LAYER_NO_ROPE if i in self.no_rope_layers else 0)
+                | (abi.REC_LAYER_SLIDING if i in self.sliding_layers else 0))
+
+    @property
+    def has_layer_options(self) -> bool:
+        return bool(self.shared_inter or self.dense_layers or self.no_rope_layers or self.sliding_layers)
 
     def desc(self) -> abi.RecModelDesc:
         return abi.RecModelDesc(
@@ -44,16 +66,21 @@ class ModelConfig:
             vocab=self.vocab, group_size=64,
             scale_dtype=abi.REC_SCALE_FP16 if self.scale_dtype == torch.float16 else abi.REC_SCALE_BF16,
             kv_bits=self.kv_bits, router_mode=self.router_mode, flags=self.flags, rms_eps=self.rms_eps,
-            rope_theta=self.rope_theta)
+            rope_theta=self.rope_theta, shared_inter=self.shared_inter,
+            dense_inter=self.dense_inter if self.dense_layers else 0,
+            sliding_window=self.sliding_window if self.sliding_layers else 0)
 
     def weight_bytes_per_token(self) -> int:
         """Algorithmic bytes streamed per decode step (weights only)."""
         g = 0.5 + 4 / 64  # int4 codes + fp16/bf16 scale and bias per 64
         h, d = self.hidden, self.head_dim
         attn = (self.n_q_heads + 2 * self.n_kv_heads) * d * h + h * self.n_q_heads * d
-        experts = self.top_k * 3 * self.moe_inter * h
-        per_layer = (attn + experts) * g + self.n_experts * h * 2 + 2 * h * 2
-        return int(self.n_layers * per_layer + self.vocab * h * g + h * 2 + h * g)
+        experts = (self.top_k * self.moe_inter + self.shared_inter) * 3 * h
+        moe_layer = (attn + experts) * g + self.n_experts * h * 2 + 2 * h * 2
+        dense_layer = (attn + 3 * self.dense_inter * h) * g + 2 * h * 2
+        n_dense = len(self.dense_layers)
+        total = (self.n_layers - n_dense) * moe_layer + n_dense * dense_layer
+        return int(total + self.vocab * h * g + h * 2 + h * g)
 
     def kv_bytes_per_token(self, context: int) -> int:
         per = 2 * self.n_kv_heads * (self.head_dim * self.kv_bits // 8 + 2 * 2 * self.head_dim // 64)
@@ -66,6 +93,14 @@ CONFIG3 = ModelConfig(name="config3_flint_shaped_48L_128E", n_layers=48, n_exper
 CONFIG4 = replace(CONFIG3, name="config4_252k_4bit_kv", kv_bits=4)
 # small shapes for parity tests (same kernels, fewer layers/experts/vocab)
 TINY = ModelConfig(name="tiny", n_layers=2, n_experts=16, top_k=4, vocab=4096, kv_bits=8)
+# the reference Flint model's layer structure at test size (model.py:14-37,
+# 155-163,216-271): sigmoid + bias router with top-6, a shared expert, dense
+# MLP in layer 0, a NoPE ("global") layer between RoPE'd sliding-window layers,
+# attention sinks and q/k head norms, bf16 scales
+TINY_FLINT = ModelConfig(name="tiny_flint", n_layers=3, n_experts=16, top_k=6, moe_inter=512, vocab=4096,
+                         kv_bits=8, scale_dtype=torch.bfloat16, router_mode=abi.REC_ROUTER_SIGMOID,
+                         flags=abi.REC_FLAG_SINKS | abi.REC_FLAG_QK_NORM, shared_inter=1024, dense_layers=(0,),
+                         dense_inter=6144, no_rope_layers=(1,), sliding_layers=(0, 2), sliding_window=300)
 
 
 def _quantize(w: torch.Tensor, bits: int, scale_dtype: torch.dtype):
@@ -114,16 +149,24 @@ class LayerWeights:
     sinks: torch.Tensor | None = None
     q_norm: torch.Tensor | None = None
     k_norm: torch.Tensor | None = None
+    kind: int = 0                       # REC_LAYER_* bits
+    shared_gate: QTensor | None = None  # the shared expert (MoE layers of a model with shared_inter)
+    shared_up: QTensor | None = None
+    shared_down: QTensor | None = None
 
     def rec(self) -> abi.RecLayerWeights:
         def p(t):
             return None if t is None else t.data_ptr()
 
+        def qm(t):
+            return t.rec() if t is not None else abi.RecQMat()
+
         return abi.RecLayerWeights(
             input_norm=p(self.input_norm), post_norm=p(self.post_norm), q=self.q.rec(), k=self.k.rec(),
             v=self.v.rec(), o=self.o.rec(), router=p(self.router), expert_bias=p(self.expert_bias),
             gate=self.gate.rec(), up=self.up.rec(), down=self.down.rec(), sinks=p(self.sinks),
-            q_norm=p(self.q_norm), k_norm=p(self.k_norm))
+            q_norm=p(self.q_norm), k_norm=p(self.k_norm), kind=self.kind, shared_gate=qm(self.shared_gate),
+            shared_up=qm(self.shared_up), shared_down=qm(self.shared_down))
 
 
 @dataclass
@@ -172,15 +215,32 @@ def generate_weights(cfg: ModelConfig, seed: int = 0, device: str | torch.device
                 parts.append(_quantize(w, 4, sd))
         return QTensor(*(torch.cat([p[i] for p in parts]) for i in range(3)))
 
+    if cfg.has_layer_options and expert_range is not None and expert_range != (0, cfg.n_experts):
+        raise ValueError("layer options run on one GPU (no expert parallelism)")
     layers = []
-    for _ in range(cfg.n_layers):
+    for i in range(cfg.n_layers):
+        kind = cfg.layer_kind(i)
+        common = dict(input_norm=_norm_weight(gen, h, device), post_norm=_norm_weight(gen, h, device),
+                      q=qmat(cfg.n_q_heads * d, h), k=qmat(cfg.n_kv_heads * d, h), v=qmat(cfg.n_kv_heads * d, h),
+                      o=qmat(h, cfg.n_q_heads * d))
+        if kind & abi.REC_LAYER_DENSE:  # a dense SwiGLU MLP (model.py:216-224), no router
+            I = cfg.dense_inter
+            L = LayerWeights(**common, router=None, gate=qmat(I, h), up=qmat(I, h), down=qmat(h, I), kind=kind)
+            if cfg.flags & abi.REC_FLAG_SINKS:
+                L.sinks = torch.randn(cfg.n_q_heads, generator=gen, device=device).to(torch.bfloat16)
+            if cfg.flags & abi.REC_FLAG_QK_NORM:
+                L.q_norm = _norm_weight(gen, d, device)
+                L.k_norm = _norm_weight(gen, d, device)
+            layers.append(L)
+            continue
         L = LayerWeights(
-            input_norm=_norm_weight(gen, h, device),
-            post_norm=_norm_weight(gen, h, device),
-            q=qmat(cfg.n_q_heads * d, h), k=qmat(cfg.n_kv_heads * d, h), v=qmat(cfg.n_kv_heads * d, h),
-            o=qmat(h, cfg.n_q_heads * d),
+            **common,
             router=_normal(gen, (cfg.n_experts, h), 0.02, device).to(torch.bfloat16),
-            gate=experts(cfg.moe_inter, h), up=experts(cfg.moe_inter, h), down=experts(h, cfg.moe_inter))
+            gate=experts(cfg.moe_inter, h), up=experts(cfg.moe_inter, h), down=experts(h, cfg.moe_inter),
+            kind=kind)
+        if cfg.shared_inter:  # the always-on shared expert (model.py:243,254)
+            Is = cfg.shared_inter
+            L.shared_gate, L.shared_up, L.shared_down = qmat(Is, h), qmat(Is, h), qmat(h, Is)
         if cfg.router_mode == abi.REC_ROUTER_SIGMOID:
             L.expert_bias = (0.05 * torch.randn(cfg.n_experts, generator=gen, device=device)).float()
         if cfg.flags & abi.REC_FLAG_SINKS:

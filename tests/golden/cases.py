@@ -31,7 +31,13 @@ GOLDEN_A = ModelConfig(name="golden_a", n_layers=2, n_q_heads=16, n_kv_heads=2, 
 GOLDEN_B = replace(GOLDEN_A, name="golden_b", n_q_heads=32, n_kv_heads=4, n_experts=16, top_k=6, moe_inter=512,
                    kv_bits=4, scale_dtype=torch.bfloat16, router_mode=abi.REC_ROUTER_SIGMOID,
                    flags=abi.REC_FLAG_SINKS | abi.REC_FLAG_QK_NORM)
-DECODE_CASES = {"decode_a": (GOLDEN_A, 101), "decode_b": (GOLDEN_B, 202)}
+# the reference Flint model's layer options (model.py:14-37,155-163,216-271):
+# a dense SwiGLU MLP in layer 0 (one 6,144-row matrix triple), a shared expert
+# in the MoE layers, a NoPE layer between two sliding-window layers whose
+# 40-position window starts inside block 1 (block 0 skipped, a tile cut)
+GOLDEN_FLINT = replace(GOLDEN_B, name="golden_flint", n_layers=3, shared_inter=256, dense_layers=(0,),
+                       dense_inter=6144, no_rope_layers=(1,), sliding_layers=(0, 2), sliding_window=40)
+DECODE_CASES = {"decode_a": (GOLDEN_A, 101), "decode_b": (GOLDEN_B, 202), "decode_flint": (GOLDEN_FLINT, 303)}
 
 CAPACITY = 512
 CONTEXT = 300      # cached positions before decoding (a ragged second block)
@@ -62,20 +68,36 @@ def _bf(rng, shape, std, mean=0.0):
 
 def host_model(cfg: ModelConfig, seed: int) -> SimpleNamespace:
     """Weights of `cfg` in host memory: linear weights N(0, 0.02) rounded to
-    bf16 then int4 g64; router bf16 N(0, 0.02); embedding rows N(0, 1)."""
+    bf16 then int4 g64; router bf16 N(0, 0.02); embedding rows N(0, 1).  A
+    dense-MLP layer draws its matrix triple (dense_inter rows) instead of the
+    router and experts; a shared expert is drawn after a MoE layer's experts."""
     rng = np.random.default_rng(seed)
     h, d, sd = cfg.hidden, cfg.head_dim, _sd(cfg)
     layers = []
-    for _ in range(cfg.n_layers):
-        L = SimpleNamespace(
+    for i in range(cfg.n_layers):
+        kind = cfg.layer_kind(i)
+        common = dict(
             input_norm=_bf(rng, h, 0.1, 1.0), post_norm=_bf(rng, h, 0.1, 1.0),
             q=_q(rng, cfg.n_q_heads * d, h, sd), k=_q(rng, cfg.n_kv_heads * d, h, sd),
-            v=_q(rng, cfg.n_kv_heads * d, h, sd), o=_q(rng, h, cfg.n_q_heads * d, sd),
-            router=_bf(rng, (cfg.n_experts, h), 0.02),
-            gate=_q(rng, cfg.n_experts * cfg.moe_inter, h, sd), up=_q(rng, cfg.n_experts * cfg.moe_inter, h, sd),
-            down=_q(rng, cfg.n_experts * h, cfg.moe_inter, sd),
-            expert_bias=None, sinks=None, q_norm=None, k_norm=None)
-        if cfg.router_mode == abi.REC_ROUTER_SIGMOID:
+            v=_q(rng, cfg.n_kv_heads * d, h, sd), o=_q(rng, h, cfg.n_q_heads * d, sd))
+        if kind & abi.REC_LAYER_DENSE:
+            I = cfg.dense_inter
+            L = SimpleNamespace(**common, router=None, gate=_q(rng, I, h, sd), up=_q(rng, I, h, sd),
+                                down=_q(rng, h, I, sd), expert_bias=None, sinks=None, q_norm=None, k_norm=None,
+                                kind=kind, shared_gate=None, shared_up=None, shared_down=None)
+        else:
+            L = SimpleNamespace(
+                **common,
+                router=_bf(rng, (cfg.n_experts, h), 0.02),
+                gate=_q(rng, cfg.n_experts * cfg.moe_inter, h, sd),
+                up=_q(rng, cfg.n_experts * cfg.moe_inter, h, sd),
+                down=_q(rng, cfg.n_experts * h, cfg.moe_inter, sd),
+                expert_bias=None, sinks=None, q_norm=None, k_norm=None, kind=kind, shared_gate=None,
+                shared_up=None, shared_down=None)
+            if cfg.shared_inter:
+                Is = cfg.shared_inter
+                L.shared_gate, L.shared_up, L.shared_down = _q(rng, Is, h, sd), _q(rng, Is, h, sd), _q(rng, h, Is, sd)
+        if cfg.router_mode == abi.REC_ROUTER_SIGMOID and not kind & abi.REC_LAYER_DENSE:
             L.expert_bias = (0.05 * rng.standard_normal(cfg.n_experts, dtype=np.float32)).astype(np.float32)
         if cfg.flags & abi.REC_FLAG_SINKS:
             L.sinks = _bf(rng, cfg.n_q_heads, 1.0)
@@ -90,7 +112,9 @@ def host_model(cfg: ModelConfig, seed: int) -> SimpleNamespace:
 def model_sha(m) -> str:
     parts = [m.embed.w, m.lm_head.w, m.final_norm]
     for L in m.layers:
-        parts += [L.q.w, L.q.s, L.o.w, L.gate.w, L.down.b, L.router, L.input_norm]
+        parts += [L.q.w, L.q.s, L.o.w, L.gate.w, L.down.b] + ([] if L.router is None else [L.router]) + [L.input_norm]
+        if getattr(L, "shared_gate", None) is not None:
+            parts += [L.shared_gate.w, L.shared_down.b]
     return sha(*parts)
 
 

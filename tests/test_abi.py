@@ -45,7 +45,8 @@ def test_constants_match_header():
     text = HEADER.read_text()
     for name in ("REC_OK", "REC_EINVAL", "REC_ECUDA", "REC_ESTATE", "REC_ELIMIT", "REC_DEV_BULK_TIMEOUT",
                  "REC_DEV_COUNTER_TIMEOUT", "REC_DEV_BAD_TOKEN", "REC_DEV_BAD_POSITION", "REC_SCALE_FP16",
-                 "REC_SCALE_BF16", "REC_ROUTER_SOFTMAX", "REC_ROUTER_SIGMOID", "REC_FLAG_SINKS", "REC_FLAG_QK_NORM"):
+                 "REC_SCALE_BF16", "REC_ROUTER_SOFTMAX", "REC_ROUTER_SIGMOID", "REC_FLAG_SINKS", "REC_FLAG_QK_NORM",
+                 "REC_LAYER_DENSE", "REC_LAYER_NO_ROPE", "REC_LAYER_SLIDING"):
         m = re.search(rf"\b{name}\s*=\s*(-?\d+)", text)
         assert m, name
         assert int(m.group(1)) == getattr(abi, name), name
@@ -53,9 +54,10 @@ def test_constants_match_header():
 
 def test_struct_sizes():
     p = C.sizeof(C.c_void_p)
-    assert C.sizeof(abi.RecModelDesc) == 16 * 4
+    assert C.sizeof(abi.RecModelDesc) == 19 * 4
     assert C.sizeof(abi.RecQMat) == 3 * p
-    assert C.sizeof(abi.RecLayerWeights) == (2 + 4 * 3 + 2 + 3 * 3 + 3) * p
+    # pointers, then the int32 kind (padded to a pointer) and the shared expert
+    assert C.sizeof(abi.RecLayerWeights) == (2 + 4 * 3 + 2 + 3 * 3 + 3 + 1 + 3 * 3) * p
     assert C.sizeof(abi.RecGlobalWeights) == (3 + 1 + 3) * p
     assert C.sizeof(abi.RecKVLayer) == 6 * p
 
@@ -101,5 +103,35 @@ def test_schedule_rule_needs_no_device(monkeypatch):
     c512 = ctx(8, n_experts=512)
     assert lib.rec_schedule_for(c512, 10) == 1
     assert lib.rec_schedule_for(None, 10) == -1
-    for c in (c4, c8, c512):
+    # a model with a shared expert (a Flint layer option) runs on the graph
+    desc = abi.RecModelDesc(hidden=2048, n_layers=2, n_q_heads=32, n_kv_heads=4, head_dim=128, n_experts=16,
+                            top_k=4, moe_inter=768, vocab=4096, group_size=64, kv_bits=8, shared_inter=1024)
+    cs = C.c_void_p()
+    assert lib.rec_create(C.byref(desc), C.byref(cs)) == abi.REC_OK, _lib.last_error()
+    monkeypatch.setenv("REC_SCHEDULE", "mega")
+    assert lib.rec_schedule_for(cs, 10) == 1
+    monkeypatch.delenv("REC_SCHEDULE")
+    for c in (c4, c8, c512, cs):
         lib.rec_destroy(c)
+
+
+def test_flint_options_are_checked_without_a_device():
+    """Shared expert, dense-MLP and sliding-window sizes outside the kernels'
+    shapes are refused at rec_create."""
+    lib = _lib_or_skip()
+
+    def create(**kw):
+        base = dict(hidden=2048, n_layers=2, n_q_heads=32, n_kv_heads=4, head_dim=128, n_experts=16, top_k=4,
+                    moe_inter=768, vocab=4096, group_size=64, kv_bits=8)
+        base.update(kw)
+        desc = abi.RecModelDesc(**base)
+        out = C.c_void_p()
+        rc = lib.rec_create(C.byref(desc), C.byref(out))
+        if rc == abi.REC_OK:
+            lib.rec_destroy(out)
+        return rc
+
+    assert create(shared_inter=1024, dense_inter=6144, sliding_window=513) == abi.REC_OK
+    assert create(shared_inter=300) == abi.REC_EINVAL
+    assert create(dense_inter=3000) == abi.REC_EINVAL
+    assert create(sliding_window=-1) == abi.REC_EINVAL

@@ -74,10 +74,15 @@ def _device_weights(m, dev):
     def bf(a):
         return None if a is None else _dev(a, dev).view(torch.bfloat16)
 
+    def qo(t):
+        return None if t is None else q(t)
+
     layers = [LayerWeights(input_norm=bf(L.input_norm), post_norm=bf(L.post_norm), q=q(L.q), k=q(L.k), v=q(L.v),
                            o=q(L.o), router=bf(L.router), gate=q(L.gate), up=q(L.up), down=q(L.down),
                            expert_bias=None if L.expert_bias is None else _dev(L.expert_bias, dev),
-                           sinks=bf(L.sinks), q_norm=bf(L.q_norm), k_norm=bf(L.k_norm)) for L in m.layers]
+                           sinks=bf(L.sinks), q_norm=bf(L.q_norm), k_norm=bf(L.k_norm), kind=L.kind,
+                           shared_gate=qo(L.shared_gate), shared_up=qo(L.shared_up), shared_down=qo(L.shared_down))
+              for L in m.layers]
     return ModelWeights(m.cfg, layers, q(m.embed), bf(m.final_norm), q(m.lm_head))
 
 

@@ -27,9 +27,11 @@ from types import SimpleNamespace
 
 import numpy as np
 import pytest
+import torch
 
 import oracle
 from oracle import semantic as S
+from rec_b200 import abi
 from rec_b200.model import CONFIG1_LAYER, TINY
 from tests.golden.cases import host_model
 
@@ -134,18 +136,29 @@ def _teacher_forced(cfg, seed, spikes):
         out = []
         for li in range(cfg.n_layers):
             kv = S.SemanticKV(base[li], cfg.kv_bits)
-            h_out = S.layer_step(cfg, m.layers[li], kv, oracle.bf16_to_f32(tr[li]).astype(np.float64), CTX, 0)
+            sd = 0 if cfg.scale_dtype == torch.float16 else 1
+            h_out = S.layer_step(cfg, m.layers[li], kv, oracle.bf16_to_f32(tr[li]).astype(np.float64), CTX, sd)
             out.append(S.rel_l2(oracle.bf16_to_f32(tr[li + 1]), h_out))
         return out
     finally:
         S.attention = orig
 
 
-@pytest.mark.parametrize("name", ["config1_layer", "four_layers", "four_layers_near_one_hot"])
+# the Flint layer options at the kernels' shapes: a dense 6,144-row MLP, a
+# shared expert, a NoPE layer, sliding windows of 300 positions over the
+# 1,024-token cache (sigmoid + bias router, sinks, q/k norms, bf16 scales)
+FLINT4 = replace(TINY, name="flint4", n_layers=4, top_k=6, moe_inter=512, scale_dtype=torch.bfloat16,
+                 router_mode=abi.REC_ROUTER_SIGMOID, flags=abi.REC_FLAG_SINKS | abi.REC_FLAG_QK_NORM,
+                 shared_inter=1024, dense_layers=(0,), dense_inter=6144, no_rope_layers=(1, 3),
+                 sliding_layers=(0, 2), sliding_window=300)
+
+
+@pytest.mark.parametrize("name", ["config1_layer", "four_layers", "four_layers_near_one_hot", "flint_options"])
 def test_layers_against_semantics(name):
     cfg, seed, spikes = {"config1_layer": (CONFIG1_LAYER, 71, 0),
                          "four_layers": (replace(TINY, n_layers=4), 81, 0),
-                         "four_layers_near_one_hot": (replace(TINY, n_layers=4), 81, 3)}[name]
+                         "four_layers_near_one_hot": (replace(TINY, n_layers=4), 81, 3),
+                         "flint_options": (FLINT4, 91, 0)}[name]
     errs = _teacher_forced(cfg, seed, spikes)
     print(name, [f"{e:.2e}" for e in errs])
     assert max(errs) < LAYER_TOL, errs
