@@ -402,8 +402,10 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
       a.counter = c->counters + 1;
       a.status = status;
       a.pdl = pdl;
-      if (layer_dense(c, li)) {  // a dense MLP: the post-attention norm only
+      if (layer_dense(c, li)) {  // a dense MLP: the post-attention norm only (no router rows to read)
         a.norm_only = 1;
+        a.w = nullptr;
+        a.E = 0;
         return launch(k_router<2048>, 1, kThreads, sizeof(RouterSmem<2048>), st, pdl, a);
       }
       e = launch(k_router<2048>, (d.n_experts + kWarps - 1) / kWarps, kThreads, sizeof(RouterSmem<2048>), st, pdl, a);
