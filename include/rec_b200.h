@@ -80,7 +80,10 @@ typedef struct RecModelDesc {
   int32_t vocab;       /* V */
   int32_t group_size;  /* 64 */
   int32_t scale_dtype; /* REC_SCALE_* of the int4 weights */
-  int32_t kv_bits;     /* 4 or 8 (KV scales/biases are bf16) */
+  int32_t kv_bits;     /* 4 or 8 (KV scales/biases are bf16); 16: bf16 K / V rows,
+                        * the reference megakernel's kv_format "bf16" (graph
+                        * schedule; RecKVLayer codes = bf16 [Hkv, C, 128], no
+                        * scales or biases) */
   int32_t router_mode; /* REC_ROUTER_* */
   int32_t flags;       /* REC_FLAG_* */
   float rms_eps;

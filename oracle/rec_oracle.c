@@ -386,6 +386,14 @@ static void head_norm(uint16_t* x, const uint16_t* w, float eps) {
 /* ------------------------------------------------- KV quantized append */
 static void kv_store(const RecKVLayer* kv, int Hkv, int C, int bits, int pos, const uint16_t* k,
                      const uint16_t* v) {
+  if (bits == 16) { /* bf16 rows, stored as they are */
+    for (int g = 0; g < Hkv; ++g) {
+      int64_t slot = (int64_t)g * C + pos;
+      memcpy((uint16_t*)kv->k_codes + slot * 128, k + g * 128, 256);
+      memcpy((uint16_t*)kv->v_codes + slot * 128, v + g * 128, 256);
+    }
+    return;
+  }
   int words = 128 * bits / 32;
   for (int g = 0; g < Hkv; ++g)
     for (int half = 0; half < 2; ++half) {
@@ -450,12 +458,14 @@ typedef struct {
   int32_t qi[128];
   float QS[2];
   float down;
+  float qf[128]; /* bf16 cache: qs = fp32(q) / sqrt(128) in fp32, unrounded */
 } QPrep;
 
 static void prep_query(const uint16_t* q, QPrep* Q) {
   float qs[128], mx = 0.0f;
   for (int d = 0; d < 128; ++d) {
-    qs[d] = rbf(bf(q[d]) * 0.0883883476483184405f);
+    Q->qf[d] = bf(q[d]) * 0.0883883476483184405f;
+    qs[d] = rbf(Q->qf[d]);
     float a = fabsf(qs[d]);
     mx = a > mx ? a : mx;
   }
@@ -508,8 +518,53 @@ static float tile_sum(const float* x) {
  *   per V group (64 dims): w_j = p_j * scale_j, x_j = p_j * bias_j (0 beyond T);
  *      F = min(14 - exponent(max|w| * (1 + 2^-7)), 100); wq_j = rint(w_j * 2^F);
  *      acc_d' = fma(acc_d, alpha, fma(float(sum_j wq_j * code_jd), 2^-F, tile_sum(x))). */
+/* The tile over a bf16 cache (attn_bf16.cuh tile_fold_bf16): the score of
+ * tile row r sums its 32 four-dim chunks from chunk r on, (c + r) mod 32, in
+ * fp32 fused multiply-adds (no bf16 rounding); l adds the butterfly sum of p
+ * over the 32 rows; acc_d = fma(acc_d, alpha, PV_d), PV_d a fused
+ * multiply-add chain over the valid rows in order. */
+static void att_tile_bf16(const QPrep* Q, const RecKVLayer* kv, int g, int C, int t0, int T, int base, int lo,
+                          Partial* st) {
+  const uint16_t* K = (const uint16_t*)kv->k_codes;
+  const uint16_t* V = (const uint16_t*)kv->v_codes;
+  int nvalid = T - t0;
+  if (nvalid > ATT_TILE) nvalid = ATT_TILE;
+  const int first = lo > t0 ? lo - t0 : 0;
+  if (nvalid <= first) return;
+  float s[ATT_TILE], p[ATT_TILE];
+  float mt = NEG_INF;
+  for (int r = 0; r < ATT_TILE; ++r) {
+    s[r] = NEG_INF;
+    if (r < first || r >= nvalid) continue;
+    const uint16_t* krow = K + ((int64_t)g * C + t0 - base + r) * 128;
+    float a = 0.0f;
+    for (int c = 0; c < 32; ++c) {
+      const int cc = (c + r) & 31;
+      for (int i = 0; i < 4; ++i) a = fmaf(Q->qf[4 * cc + i], bf(krow[4 * cc + i]), a);
+    }
+    s[r] = a;
+    mt = fmaxf(mt, a);
+  }
+  const float mn = fmaxf(st->m, mt);
+  const float alpha = aexp(st->m - mn);
+  float v[32];
+  for (int r = 0; r < ATT_TILE; ++r) v[r] = p[r] = (r >= first && r < nvalid) ? aexp(s[r] - mn) : 0.0f;
+  bfly(v, 32);
+  st->l = fmaf(st->l, alpha, v[0]);
+  for (int d = 0; d < 128; ++d) {
+    float pv = 0.0f;
+    for (int r = first; r < nvalid; ++r) pv = fmaf(p[r], bf(V[((int64_t)g * C + t0 - base + r) * 128 + d]), pv);
+    st->acc[d] = fmaf(st->acc[d], alpha, pv);
+  }
+  st->m = mn;
+}
+
 static void att_tile(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bits, int t0, int T, int base,
                      int lo, Partial* st) {
+  if (bits == 16) {
+    att_tile_bf16(Q, kv, g, C, t0, T, base, lo, st);
+    return;
+  }
   int words = 128 * bits / 32;
   const uint32_t* KC = (const uint32_t*)kv->k_codes;
   const uint32_t* VC = (const uint32_t*)kv->v_codes;

@@ -45,21 +45,28 @@ def rope(x: np.ndarray, pos: int, theta: float) -> np.ndarray:
     return np.concatenate([a * c - b * s, a * s + b * c], axis=1).astype(np.float32)
 
 
-def attention(q_bf16: np.ndarray, k: np.ndarray, v: np.ndarray, sinks=None, bf16_probs: bool = True) -> np.ndarray:
+def attention(q_bf16: np.ndarray, k: np.ndarray, v: np.ndarray, sinks=None, bf16_probs: bool = True,
+              bf16_kv: bool = False) -> np.ndarray:
     """quantized_attention_with_sinks (model.py:108-139) for one query token.
     q: [Hq, 128] bf16 (post-RoPE); k, v: dequantised float [Hkv, T, 128].
     Scores are rounded to bf16 (the quantized matmul returns bf16), softmax in
     fp32 over [scores, sink], probabilities rounded to bf16 before P*V
     (bf16_probs=False keeps them in float64: the exact softmax of the bf16
-    scores)."""
+    scores).  bf16_kv: the reference megakernel's bf16 cache
+    (megakernel.py:619-693): the scaled query stays fp32 and the scores are
+    not rounded."""
     hq = q_bf16.shape[0]
     hkv = k.shape[0]
     rep = hq // hkv
-    qs = rbf(bf16_to_f32(q_bf16) * np.float32(1.0 / np.sqrt(128.0)))
+    qs = bf16_to_f32(q_bf16) * np.float32(1.0 / np.sqrt(128.0))
+    if not bf16_kv:
+        qs = rbf(qs)
     out = np.zeros((hq, 128), np.float32)
     for h in range(hq):
         g = h // rep
-        sc = rbf((k[g].astype(np.float64) @ qs[h].astype(np.float64)).astype(np.float32)).astype(np.float64)
+        sc = k[g].astype(np.float64) @ qs[h].astype(np.float64)
+        if not bf16_kv:
+            sc = rbf(sc.astype(np.float32)).astype(np.float64)
         sink = [] if sinks is None else [float(bf16_to_f32(np.array([sinks[h]], np.uint16))[0])]
         allv = np.concatenate([sc, sink])
         p = np.exp(allv - allv.max())
@@ -143,9 +150,12 @@ class SemanticKV:
         self.bits = bits
 
     def append(self, pos: int, k_bf16v: np.ndarray, v_bf16v: np.ndarray) -> None:
-        from . import quantize
+        from . import f32_to_bf16, quantize
 
         for name, x in (("k", k_bf16v), ("v", v_bf16v)):
+            if self.bits == 16:  # a bf16 cache keeps the rows as they are
+                self.L[f"{name}_codes"].view(np.uint16)[:, pos] = f32_to_bf16(np.asarray(x, np.float32))
+                continue
             c, s, b = quantize(np.asarray(x, np.float32)[:, None, :], self.bits, 1)
             self.L[f"{name}_codes"][:, pos] = c[:, 0]
             self.L[f"{name}_scales"][:, pos] = s[:, 0]
@@ -153,6 +163,8 @@ class SemanticKV:
 
     def dequant(self, name: str, upto: int) -> np.ndarray:
         L = self.L
+        if self.bits == 16:
+            return bf16_to_f32(L[f"{name}_codes"].view(np.uint16)[:, :upto]).astype(np.float64)
         return dequantize(L[f"{name}_codes"][:, :upto], L[f"{name}_scales"][:, :upto], L[f"{name}_biases"][:, :upto],
                           self.bits, 1).astype(np.float64)
 
@@ -192,7 +204,8 @@ def layer_step(cfg, L, kv: SemanticKV, h: np.ndarray, pos: int, sd: int) -> np.n
         lo = max(0, pos + 1 - cfg.sliding_window)
         K, V = K[:, lo:], V[:, lo:]
     sinks = None if L.sinks is None else np.asarray(L.sinks, np.uint16)
-    att = rbf(attention(f32_to_bf16(q.astype(np.float32)), K, V, sinks=sinks, bf16_probs=True)).reshape(-1)
+    att = rbf(attention(f32_to_bf16(q.astype(np.float32)), K, V, sinks=sinks, bf16_probs=True,
+                        bf16_kv=cfg.kv_bits == 16)).reshape(-1)
     h = rbf(h + rbf(_dq(L.o, sd) @ att.astype(np.float64))).astype(np.float64)
     xn2 = rmsnorm_f(h, L.post_norm, cfg.rms_eps)
     if kind & 1:  # REC_LAYER_DENSE

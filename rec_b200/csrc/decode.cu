@@ -16,6 +16,7 @@
 #include <cstdlib>
 
 #include "attn.cuh"
+#include "attn_bf16.cuh"
 #include "attn_shard.cuh"
 #include "capi_common.h"
 #include "mega.cuh"
@@ -329,6 +330,8 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
       a.status = status;
       a.pdl = pdl;
       const int agrid = sm_count() * (d.kv_bits == 4 ? 2 : 1);  // 4-bit stages fit two CTAs per SM
+      if (kind == kKAttn && d.kv_bits == 16)  // a bf16 cache: one block of K and V rows per CTA
+        return launch(k_attn_partial_bf16, sm_count(), kAttWarps * 32, sizeof(AttnBfSmem), st, pdl, a);
       if (kind == kKAttn)
         return d.kv_bits == 4 ? launch(k_attn_partial<4>, agrid, kAttWarps * 32, sizeof(AttnSmem<4>), st, pdl, a)
                               : launch(k_attn_partial<8>, agrid, kAttWarps * 32, sizeof(AttnSmem<8>), st, pdl, a);
@@ -621,7 +624,7 @@ REC_API int rec_create(const RecModelDesc* desc, RecCtx** out) {
   REC_CHECK_ARG(d.vocab > 0 && d.vocab % 2 == 0, "vocab must be even");
   REC_CHECK_ARG(d.group_size == 64, "group_size must be 64");
   REC_CHECK_ARG(d.scale_dtype == REC_SCALE_FP16 || d.scale_dtype == REC_SCALE_BF16, "bad scale dtype");
-  REC_CHECK_ARG(d.kv_bits == 4 || d.kv_bits == 8, "kv_bits must be 4 or 8");
+  REC_CHECK_ARG(d.kv_bits == 4 || d.kv_bits == 8 || d.kv_bits == 16, "kv_bits must be 4, 8 or 16");
   REC_CHECK_ARG(d.router_mode == REC_ROUTER_SOFTMAX || d.router_mode == REC_ROUTER_SIGMOID, "bad router mode");
   REC_CHECK_ARG(d.n_layers >= 1 && d.n_layers <= kMaxLayers, "n_layers must be in 1..%d", kMaxLayers);
   REC_CHECK_ARG(d.shared_inter == 0 || d.shared_inter == 256 || d.shared_inter == 512 || d.shared_inter == 768 ||
@@ -632,7 +635,7 @@ REC_API int rec_create(const RecModelDesc* desc, RecCtx** out) {
   REC_CHECK_ARG(d.sliding_window >= 0, "sliding_window must be >= 0");
   RecCtx* c = new RecCtx();
   c->d = d;
-  c->flint = d.shared_inter > 0;
+  c->flint = d.shared_inter > 0 || d.kv_bits == 16;  // a bf16 cache too: graph schedule only
   c->grid = sm_count();
   *out = c;
   return REC_OK;
@@ -691,7 +694,7 @@ REC_API void rec_destroy(RecCtx* ctx) {
 REC_API int rec_set_weights(RecCtx* c, const RecLayerWeights* layers, int32_t n_layers, const RecGlobalWeights* g) {
   REC_CHECK_ARG(c && layers && g, "rec_set_weights: null argument");
   REC_CHECK_ARG(n_layers == c->d.n_layers, "expected %d layers, got %d", c->d.n_layers, n_layers);
-  bool flint = c->d.shared_inter > 0;
+  bool flint = c->d.shared_inter > 0 || c->d.kv_bits == 16;
   for (int i = 0; i < n_layers; ++i) {
     const RecLayerWeights& L = layers[i];
     const bool dense = (L.kind & REC_LAYER_DENSE) != 0;
@@ -730,6 +733,11 @@ REC_API int rec_set_kv(RecCtx* c, const RecKVLayer* layers, int32_t n_layers, in
   REC_CHECK_ARG(capacity > 0 && capacity % kAttBlock == 0, "capacity must be a positive multiple of %d", kAttBlock);
   for (int i = 0; i < n_layers; ++i) {
     const RecKVLayer& k = layers[i];
+    if (c->d.kv_bits == 16) {  // bf16 rows; no scales or biases
+      REC_CHECK_ARG(k.k_codes && k.v_codes && aligned16(k.k_codes) && aligned16(k.v_codes),
+                    "KV layer %d: bf16 K / V buffers must be non-null and 16-byte aligned", i);
+      continue;
+    }
     REC_CHECK_ARG(k.k_codes && k.k_scales && k.k_biases && k.v_codes && k.v_scales && k.v_biases &&
                       aligned16(k.k_codes) && aligned16(k.v_codes) && aligned16(k.k_scales) &&
                       aligned16(k.k_biases) && aligned16(k.v_scales) && aligned16(k.v_biases),

@@ -57,7 +57,10 @@ class ModelConfig:
 
     @property
     def has_layer_options(self) -> bool:
-        return bool(self.shared_inter or self.dense_layers or self.no_rope_layers or self.sliding_layers)
+        """Options that put the model on the graph schedule (and its prefill
+        on the decode step): the Flint layer options and a bf16 cache."""
+        return bool(self.shared_inter or self.dense_layers or self.no_rope_layers or self.sliding_layers
+                    or self.kv_bits == 16)
 
     def desc(self) -> abi.RecModelDesc:
         return abi.RecModelDesc(
@@ -83,7 +86,8 @@ class ModelConfig:
         return int(total + self.vocab * h * g + h * 2 + h * g)
 
     def kv_bytes_per_token(self, context: int) -> int:
-        per = 2 * self.n_kv_heads * (self.head_dim * self.kv_bits // 8 + 2 * 2 * self.head_dim // 64)
+        scales = 2 * 2 * self.head_dim // 64 if self.kv_bits < 16 else 0  # a bf16 cache has none
+        per = 2 * self.n_kv_heads * (self.head_dim * self.kv_bits // 8 + scales)
         return self.n_layers * per * context
 
 
@@ -356,6 +360,9 @@ class KVCache:
                     p1 = min(upto, p0 + chunk)
                     x = torch.randn(self.cfg.n_kv_heads, p1 - p0, 128, generator=gen, device=dev)
                     x = x.to(torch.bfloat16).float()
+                    if self.cfg.kv_bits == 16:  # bf16 rows (a pair per 32-bit word)
+                        L[f"{kv}_codes"][:, p0:p1] = x.to(torch.bfloat16).view(torch.int16).view(torch.int32)
+                        continue
                     c, s, b = quantize_affine(x, self.cfg.kv_bits, torch.bfloat16)
                     L[f"{kv}_codes"][:, p0:p1] = c
                     L[f"{kv}_scales"][:, p0:p1] = s

@@ -37,7 +37,10 @@ GOLDEN_B = replace(GOLDEN_A, name="golden_b", n_q_heads=32, n_kv_heads=4, n_expe
 # 40-position window starts inside block 1 (block 0 skipped, a tile cut)
 GOLDEN_FLINT = replace(GOLDEN_B, name="golden_flint", n_layers=3, shared_inter=256, dense_layers=(0,),
                        dense_inter=6144, no_rope_layers=(1,), sliding_layers=(0, 2), sliding_window=40)
-DECODE_CASES = {"decode_a": (GOLDEN_A, 101), "decode_b": (GOLDEN_B, 202), "decode_flint": (GOLDEN_FLINT, 303)}
+# a bf16 cache (the reference megakernel's kv_format "bf16")
+GOLDEN_BF16 = replace(GOLDEN_A, name="golden_bf16", kv_bits=16)
+DECODE_CASES = {"decode_a": (GOLDEN_A, 101), "decode_b": (GOLDEN_B, 202), "decode_flint": (GOLDEN_FLINT, 303),
+                "decode_bf16": (GOLDEN_BF16, 404)}
 
 CAPACITY = 512
 CONTEXT = 300      # cached positions before decoding (a ragged second block)
@@ -126,6 +129,9 @@ def fill_kv(hkv, cfg: ModelConfig, seed: int) -> None:
         for name in ("k", "v"):
             x = oracle.bf16_to_f32(oracle.f32_to_bf16(
                 rng.standard_normal((cfg.n_kv_heads, CONTEXT, 128), dtype=np.float32)))
+            if cfg.kv_bits == 16:  # bf16 rows as they are
+                L[f"{name}_codes"].view(np.uint16)[:, :CONTEXT] = oracle.f32_to_bf16(x)
+                continue
             c, s, b = oracle.quantize(x, cfg.kv_bits, 1)
             L[f"{name}_codes"][:, :CONTEXT] = c
             L[f"{name}_scales"][:, :CONTEXT] = s

@@ -2,7 +2,9 @@
 oracle through the C ABI: an always-on shared expert (model.py:243,254), a
 dense SwiGLU MLP layer of 6,144 rows (model.py:216-224, `mlp_only_layers`),
 a NoPE layer (model.py:158-163) and sliding-window layers (model.py:302-313),
-with the sigmoid + bias router, sinks, q/k head norms and bf16 scales.
+with the sigmoid + bias router, sinks, q/k head norms and bf16 scales; and
+the bf16 KV cache of the reference megakernel (kv_format "bf16",
+megakernel.py:619-693), with and without those options.
 
 Caches are filled with quantized synthetic K, V up to the decode position, so
 that the window starts past the first work item (600 tokens: window start in
@@ -16,7 +18,7 @@ import torch
 
 import oracle
 from oracle.host import HostKV, HostModel, _np
-from rec_b200.model import TINY_FLINT, KVCache, generate_weights
+from rec_b200.model import TINY, TINY_FLINT, KVCache, generate_weights
 from rec_b200.session import DecodeSession
 
 pytestmark = pytest.mark.gpu
@@ -43,9 +45,14 @@ def _compare_rows(kv, hkv, lo, hi):
             assert np.array_equal(_np(d[name])[:, lo:hi], h[name][:, lo:hi]), (li, name)
 
 
+VARIANTS = {"flint_kv8": TINY_FLINT, "flint_bf16_kv": replace(TINY_FLINT, kv_bits=16),
+            "tiny_bf16_kv": replace(TINY, kv_bits=16)}
+
+
+@pytest.mark.parametrize("variant", list(VARIANTS))
 @pytest.mark.parametrize("context", [600, 17000])
-def test_flint_decode_steps_bitexact(cuda, context):
-    cfg = TINY_FLINT
+def test_flint_decode_steps_bitexact(cuda, variant, context):
+    cfg = VARIANTS[variant]
     cap = (context + 8 + 255) // 256 * 256
     _, kv, sess, host, hkv = _setup(cfg, cap, context, seed=41)
     rng = np.random.default_rng(43)
@@ -61,10 +68,11 @@ def test_flint_decode_steps_bitexact(cuda, context):
     _compare_rows(kv, hkv, context, context + 3)
 
 
-def test_flint_greedy_packet_and_partial_depth(cuda):
+@pytest.mark.parametrize("variant", ["flint_kv8", "flint_bf16_kv"])
+def test_flint_greedy_packet_and_partial_depth(cuda, variant):
     """A 12-token greedy packet on the device equals the oracle's chain; a
     partial-depth step (the dense and the NoPE layer) equals the oracle's."""
-    cfg = TINY_FLINT
+    cfg = VARIANTS[variant]
     context = 600
     _, kv, sess, host, hkv = _setup(cfg, 1024, context, seed=51)
     ids = sess.greedy(17, context, 12)
@@ -134,13 +142,15 @@ def test_flint_ffn_entry_bitexact(cuda, layer):
     assert np.array_equal(_u16(h_dev), want)
 
 
-def test_flint_engine_prefill_and_block(cuda):
+@pytest.mark.parametrize("kv_bits", [8, 16])
+def test_flint_engine_prefill_and_block(cuda, kv_bits):
     """Through the reference-facing API: QATSession.prefill (a model with
     layer options is prefilled by its decode step) and ResidentSampler.block
     at temperature 0 equal the oracle's chain."""
     from rec_b200.engine import build_decoder
 
-    cfg = replace(TINY_FLINT, sliding_window=24)  # the window moves within the short prompt
+    # the window moves within the short prompt
+    cfg = replace(TINY_FLINT, sliding_window=24, kv_bits=kv_bits)
     w = generate_weights(cfg, seed=71, device="cuda")
     engine, sampler = build_decoder(w)
     prompt = [int(t) for t in np.random.default_rng(73).integers(0, cfg.vocab, 40)]

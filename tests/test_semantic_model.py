@@ -55,6 +55,9 @@ def _kv(cfg, seed, spikes=0):
             if name == "k" and spikes:
                 idx = rng.choice(CTX, spikes, replace=False)
                 x[:, idx] *= 12.0
+            if cfg.kv_bits == 16:  # a bf16 cache holds the rows as they are
+                L[f"{name}_codes"].view(np.uint16)[:, :CTX] = oracle.f32_to_bf16(x)
+                continue
             x = oracle.bf16_to_f32(oracle.f32_to_bf16(x))
             c, s, b = oracle.quantize(x, cfg.kv_bits, 1)
             L[f"{name}_codes"][:, :CTX] = c
@@ -131,7 +134,7 @@ def _teacher_forced(cfg, seed, spikes):
     base = [{n: a.copy() for n, a in L.items()} for L in hkv.layers]
     _, tr = HostModel(m).step(hkv, 7, CTX)
     orig = S.attention
-    S.attention = lambda q, k, v, sinks=None, bf16_probs=True: orig(q, k, v, sinks, False)
+    S.attention = lambda q, k, v, sinks=None, bf16_probs=True, **kw: orig(q, k, v, sinks, False, **kw)
     try:
         out = []
         for li in range(cfg.n_layers):
@@ -153,12 +156,14 @@ FLINT4 = replace(TINY, name="flint4", n_layers=4, top_k=6, moe_inter=512, scale_
                  sliding_layers=(0, 2), sliding_window=300)
 
 
-@pytest.mark.parametrize("name", ["config1_layer", "four_layers", "four_layers_near_one_hot", "flint_options"])
+@pytest.mark.parametrize("name", ["config1_layer", "four_layers", "four_layers_near_one_hot", "flint_options",
+                                  "flint_bf16_kv"])
 def test_layers_against_semantics(name):
     cfg, seed, spikes = {"config1_layer": (CONFIG1_LAYER, 71, 0),
                          "four_layers": (replace(TINY, n_layers=4), 81, 0),
                          "four_layers_near_one_hot": (replace(TINY, n_layers=4), 81, 3),
-                         "flint_options": (FLINT4, 91, 0)}[name]
+                         "flint_options": (FLINT4, 91, 0),
+                         "flint_bf16_kv": (replace(FLINT4, kv_bits=16), 93, 0)}[name]
     errs = _teacher_forced(cfg, seed, spikes)
     print(name, [f"{e:.2e}" for e in errs])
     assert max(errs) < LAYER_TOL, errs

@@ -94,6 +94,11 @@ def test_noalloc_other_shapes(cuda, k, sd):
         torch.cuda.synchronize()
         assert torch.equal(y.view(torch.int16), y_ref.view(torch.int16)), f"rep {rep}"
         assert int(token.item()) == _first_argmax(y_ref), f"rep {rep}"
+        # and directly against the CPU oracle's GEMV of the same inputs
+        import oracle
+        from oracle.host import _np
+
+        assert np.array_equal(_np(y), oracle.gemv(_np(w), _np(s), _np(b), _np(x), sd)), f"rep {rep} (oracle)"
 
 
 def test_noalloc_rejects_rows_beyond_scratch():
