@@ -45,8 +45,9 @@ def parse():
     p.add_argument("--warmup", type=int, default=16)
     p.add_argument("--impl", choices=["rec", "reference"], default="rec")
     p.add_argument("--context", type=int, default=1024)
-    p.add_argument("--kv-bits", type=int, default=8, choices=[4, 8],
-                   help="8: config 3 (the default workload); 4: the config-4 cache format")
+    p.add_argument("--kv-bits", type=int, default=8, choices=[4, 8, 16],
+                   help="8: config 3 (the default workload); 4: the config-4 cache format; 16: a bf16 cache "
+                        "(the reference megakernel's kv_format, graph schedule)")
     p.add_argument("--attn-sweep", action="store_true",
                    help="config 2: time the attention kernels alone over --contexts (4-bit cache unless --kv-bits 8)")
     p.add_argument("--contexts", default="1024,8192,32768,131072,258048")
@@ -153,7 +154,8 @@ def run_rec(args):
 
     from rec_b200 import shard
 
-    cfg = CONFIG3 if args.kv_bits == 8 else replace(CONFIG3, name="config4_252k_4bit_kv", kv_bits=args.kv_bits)
+    cfg = CONFIG3 if args.kv_bits == 8 else replace(
+        CONFIG3, name="config4_252k_4bit_kv" if args.kv_bits == 4 else "config3_bf16_kv", kv_bits=args.kv_bits)
     W, K = max(3, args.warmup), args.steps
     ctx0 = args.context
     capacity = (ctx0 + W + 2 * K + 64 + 255) // 256 * 256
@@ -268,7 +270,7 @@ def run_rec(args):
     g64 = 0.5 + 4 / 64
     kernel_bytes = {
         "qkv": (cfg.n_q_heads + 2 * cfg.n_kv_heads) * 128 * H * g64 + H * 2 * 2,
-        "attn_partial": kv.nbytes() / cfg.n_layers * pos / capacity,
+        "attn_partial": cfg.kv_bytes_per_token(pos) / cfg.n_layers,  # K, V (and scales) of the attended tokens
         "o_proj": H * cfg.n_q_heads * 128 * g64 + H * 2 * 2,
         "router": cfg.n_experts * H * 2 + H * 2 * 2,
         "experts_gate_up": k * 2 * I * H * g64 + H * 2 + k * I * 2,

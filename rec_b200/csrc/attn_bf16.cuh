@@ -26,24 +26,36 @@
 
 namespace rec {
 
+// A block's 256 rows in four 64-row quarters, one per warp pair: pair q
+// (warps 2q, 2q+1) folds tiles 2q, 2q+1 of every block from its own quarter
+// slot, and the pairs stream their quarters independently (one pair's copy
+// overlaps another pair's math).
+constexpr int kBfQuarter = 64;
 struct AttnBfSmem {
-  alignas(128) uint16_t k[kAttBlock * 128];  // one block of K rows
-  alignas(128) uint16_t v[kAttBlock * 128];  // and of V rows
-  alignas(16) float q[kHeadsPerKv][128];     // scaled queries of the kv head's 8 heads
-  float p[kAttWarps][kHeadsPerKv][33];       // per warp: softmax weights [head][row] (padded)
-  alignas(16) uint16_t knew[128], vnew[128]; // the new token's K (normed, RoPE'd) and V
-  AttnScratch sc;                            // query preparation scratch and the warp-state tree fold
-  uint64_t bar[2];                           // K, V copies
+  alignas(128) uint16_t k[4][kBfQuarter * 128];  // per pair: K rows of its quarter
+  alignas(128) uint16_t v[4][kBfQuarter * 128];  // and V rows
+  alignas(16) float q[kHeadsPerKv][128];         // scaled queries of the kv head's 8 heads
+  alignas(16) float p[kAttWarps][kAttTile][kHeadsPerKv];  // per warp: softmax weights [row][head]
+  alignas(16) uint16_t knew[128], vnew[128];     // the new token's K (normed, RoPE'd) and V
+  AttnScratch sc;                                // query preparation scratch and the warp-state tree fold
+  uint64_t bar[4];                               // per pair: its quarter's K and V copies
+  int issued[4];                                 // per pair: a copy of the current block is in flight
+  int failed;                                    // a bounded wait ran out
 };
 
-// Bulk copies of the K (which = 0) or V (1) rows of block b of kv head g.
-__device__ __forceinline__ void issue_bf16_rows(AttnBfSmem& sm, int which, const AttnArgs& a, int g, int b, int T) {
-  const int n = min(kAttBlock, T - b * kAttBlock);
-  const size_t row = size_t(g) * a.capacity + size_t(b) * kAttBlock - size_t(a.token_base);
+// Rows [r0, r0 + 64) of a kv head that some attended position needs (below
+// T, and the quarter reaches the window start lo): the count copied (0: none).
+__device__ __forceinline__ int bf16_quarter_rows(int r0, int T, int lo) {
+  const int n = min(kBfQuarter, T - r0);
+  return (n > 0 && r0 + kBfQuarter > lo) ? n : 0;
+}
+__device__ __forceinline__ void issue_bf16_quarter(AttnBfSmem& sm, int pair, const AttnArgs& a, int g, int r0,
+                                                   int n) {
+  const size_t row = size_t(g) * a.capacity + size_t(r0) - size_t(a.token_base);
   const uint32_t bytes = uint32_t(n) * 256u;
-  mbar_expect_tx(&sm.bar[which], bytes);
-  const uint32_t* src = which ? a.v_codes : a.k_codes;
-  bulk_g2s(which ? sm.v : sm.k, reinterpret_cast<const uint8_t*>(src) + row * 256u, bytes, &sm.bar[which]);
+  mbar_expect_tx(&sm.bar[pair], 2 * bytes);
+  bulk_g2s(sm.k[pair], reinterpret_cast<const uint8_t*>(a.k_codes) + row * 256u, bytes, &sm.bar[pair]);
+  bulk_g2s(sm.v[pair], reinterpret_cast<const uint8_t*>(a.v_codes) + row * 256u, bytes, &sm.bar[pair]);
 }
 
 // Warp w: query of head 8g + w (norm, RoPE, scale) into sm.q[w].
@@ -83,19 +95,21 @@ __device__ __forceinline__ void prep_new_bf16(const AttnArgs& a, AttnBfSmem& sm,
 }
 
 // Per-warp running state of the bf16 tile: m, l of all 8 heads in every lane;
-// acc in the WarpState layout (lane 4gq + tq: head gq, dims state_dim(i, tq)).
+// acc[4h + j] = head h, dim 4 lane + j (each V element is converted once and
+// used for the 8 heads).
 struct BfState {
   float m[kHeadsPerKv], l[kHeadsPerKv];
   float acc[32];
 };
 
-// The tile (rows [32 warp, 32 warp + 32) of the block; rows [first, nvalid)
-// of it valid) folded into st.
-__device__ __forceinline__ void tile_fold_bf16(const AttnBfSmem& sm, float (&p_sm)[kHeadsPerKv][33], int warp,
-                                               int first, int nvalid, BfState& st) {
-  const int lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
+// The tile whose 32 K / V rows start at kt / vt (rows [first, nvalid) of it
+// valid) folded into st.
+__device__ __forceinline__ void tile_fold_bf16(const uint16_t* kt, const uint16_t* vt, const float (&q)[8][128],
+                                               float (&p_sm)[kAttTile][kHeadsPerKv], int first, int nvalid,
+                                               BfState& st) {
+  const int lane = threadIdx.x & 31;
   // ---- scores: lane = row
-  const uint16_t* krow = sm.k + (warp * kAttTile + lane) * 128;
+  const uint16_t* krow = kt + lane * 128;
   float s[kHeadsPerKv];
 #pragma unroll
   for (int h = 0; h < kHeadsPerKv; ++h) s[h] = 0.0f;
@@ -107,7 +121,7 @@ __device__ __forceinline__ void tile_fold_bf16(const AttnBfSmem& sm, float (&p_s
     const float k2 = __uint_as_float(kk.y << 16), k3 = __uint_as_float(kk.y & 0xFFFF0000u);
 #pragma unroll
     for (int h = 0; h < kHeadsPerKv; ++h) {
-      const float4 qq = *reinterpret_cast<const float4*>(&sm.q[h][4 * cc]);
+      const float4 qq = *reinterpret_cast<const float4*>(&q[h][4 * cc]);
       s[h] = __fmaf_rn(qq.x, k0, s[h]);
       s[h] = __fmaf_rn(qq.y, k1, s[h]);
       s[h] = __fmaf_rn(qq.z, k2, s[h]);
@@ -116,60 +130,59 @@ __device__ __forceinline__ void tile_fold_bf16(const AttnBfSmem& sm, float (&p_s
   }
   // ---- softmax per head (all lanes keep every head's m, l)
   const bool valid = lane >= first && lane < nvalid;
-  float alpha[kHeadsPerKv];
+  float alpha[kHeadsPerKv], pr[kHeadsPerKv];
 #pragma unroll
   for (int h = 0; h < kHeadsPerKv; ++h) {
     const float sh = valid ? s[h] : -INFINITY;
     const float mn = fmaxf(st.m[h], bfly_max(sh));
     alpha[h] = aexp(__fsub_rn(st.m[h], mn));
-    const float p = valid ? aexp(__fsub_rn(sh, mn)) : 0.0f;
-    st.l[h] = __fmaf_rn(st.l[h], alpha[h], bfly_sum(p));
+    pr[h] = valid ? aexp(__fsub_rn(sh, mn)) : 0.0f;
+    st.l[h] = __fmaf_rn(st.l[h], alpha[h], bfly_sum(pr[h]));
     st.m[h] = mn;
-    p_sm[h][lane] = p;
   }
+  *reinterpret_cast<float4*>(&p_sm[lane][0]) = make_float4(pr[0], pr[1], pr[2], pr[3]);
+  *reinterpret_cast<float4*>(&p_sm[lane][4]) = make_float4(pr[4], pr[5], pr[6], pr[7]);
   __syncwarp();
-  // ---- P.V: lane (gq, tq), head gq, dims state_dim(i, tq)
-  float a_h = alpha[0], pv[32];
-#pragma unroll
-  for (int h = 1; h < kHeadsPerKv; ++h) a_h = gq == h ? alpha[h] : a_h;
+  // ---- P.V: lane l, dims 4l..4l+3 of every head (rows in order)
+  float pv[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) pv[i] = 0.0f;
   for (int r = first; r < nvalid; ++r) {
-    const float pr = p_sm[gq][r];
-    const uint16_t* vrow = sm.v + (warp * kAttTile + r) * 128 + 16 * tq;
-    uint32_t w[16];
-    {
-      const uint4 a0 = *reinterpret_cast<const uint4*>(vrow);
-      const uint4 a1 = *reinterpret_cast<const uint4*>(vrow + 8);
-      const uint4 b0 = *reinterpret_cast<const uint4*>(vrow + 64);
-      const uint4 b1 = *reinterpret_cast<const uint4*>(vrow + 72);
-      w[0] = a0.x; w[1] = a0.y; w[2] = a0.z; w[3] = a0.w; w[4] = a1.x; w[5] = a1.y; w[6] = a1.z; w[7] = a1.w;
-      w[8] = b0.x; w[9] = b0.y; w[10] = b0.z; w[11] = b0.w; w[12] = b1.x; w[13] = b1.y; w[14] = b1.z; w[15] = b1.w;
-    }
+    const float4 pa = *reinterpret_cast<const float4*>(&p_sm[r][0]);
+    const float4 pb = *reinterpret_cast<const float4*>(&p_sm[r][4]);
+    const uint2 vv = *reinterpret_cast<const uint2*>(vt + r * 128 + 4 * lane);
+    const float v[4] = {__uint_as_float(vv.x << 16), __uint_as_float(vv.x & 0xFFFF0000u),
+                        __uint_as_float(vv.y << 16), __uint_as_float(vv.y & 0xFFFF0000u)};
+    const float ph[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      pv[2 * j] = __fmaf_rn(pr, __uint_as_float(w[j] << 16), pv[2 * j]);
-      pv[2 * j + 1] = __fmaf_rn(pr, __uint_as_float(w[j] & 0xFFFF0000u), pv[2 * j + 1]);
-    }
+    for (int h = 0; h < kHeadsPerKv; ++h)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) pv[4 * h + j] = __fmaf_rn(ph[h], v[j], pv[4 * h + j]);
   }
 #pragma unroll
-  for (int i = 0; i < 32; ++i) st.acc[i] = __fmaf_rn(st.acc[i], a_h, pv[i]);
+  for (int h = 0; h < kHeadsPerKv; ++h)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) st.acc[4 * h + j] = __fmaf_rn(st.acc[4 * h + j], alpha[h], pv[4 * h + j]);
   __syncwarp();  // p_sm is rewritten by the next tile
 }
 
-// Item partials over a bf16 cache.  Persistent grid, one CTA per SM (a block
-// of K and V rows takes 128 KB); item it = (kv head it % Hkv, item
-// i_first + it / Hkv).  Each block is copied, patched with the new row and
-// folded; the CTAs of the grid keep HBM busy between them.
+// Item partials over a bf16 cache.  Persistent grid, one CTA per SM (the
+// four quarter slots take 128 KB); item it = (kv head it % Hkv, item
+// i_first + it / Hkv).  Each warp pair waits for its quarter of a block,
+// patches the new row into it, folds its two tiles and issues its quarter of
+// the next block; the pairs meet only at the item's start and end.
 static __global__ void __launch_bounds__(kAttWarps * 32, 1) k_attn_partial_bf16(const AttnArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnBfSmem& sm = *reinterpret_cast<AttnBfSmem*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pair = warp >> 1, half = warp & 1;
+  const bool leader = half == 0 && lane == 0;
+  volatile int* failed = &sm.failed;
   if (threadIdx.x == 0) {
-    mbar_init(&sm.bar[0], 1);
-    mbar_init(&sm.bar[1], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&sm.bar[i], 1);
     fence_barrier_init();
     sm.sc.qg = -1;
+    sm.failed = 0;
   }
   __syncthreads();
   if (a.pdl) grid_wait();
@@ -188,13 +201,15 @@ static __global__ void __launch_bounds__(kAttWarps * 32, 1) k_attn_partial_bf16(
   const int items = max(0, n_items - i_first) * a.hkv;
   const float* cs = a.rope ? a.rope + size_t(p) * 128 : nullptr;
   const int icap = items_cap(a.capacity);
-  uint32_t phase = 0;  // bit 0: K barrier parity, bit 1: V
+  uint32_t phase = 0;  // parity of this pair's barrier
+  bool ok = true;      // this thread's waits all completed
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
     const int g = it % a.hkv, item = i_first + it / a.hkv;
     const int b0 = item * nbi, b1 = min(b0 + nbi, nblk);
-    if (threadIdx.x == 0) {
-      issue_bf16_rows(sm, 0, a, g, b0, T);
-      issue_bf16_rows(sm, 1, a, g, b0, T);
+    if (leader) {
+      const int r0 = b0 * kAttBlock + kBfQuarter * pair, n = bf16_quarter_rows(r0, T, lo);
+      if (n && !*failed) issue_bf16_quarter(sm, pair, a, g, r0, n);
+      sm.issued[pair] = n && !*failed;
     }
     if (sm.sc.qg != g) prep_q_bf16(a, sm, g, cs, warp);
     const bool has_new = p >= b0 * kAttBlock && p < b1 * kAttBlock;
@@ -209,43 +224,55 @@ static __global__ void __launch_bounds__(kAttWarps * 32, 1) k_attn_partial_bf16(
     }
 #pragma unroll
     for (int i = 0; i < 32; ++i) st.acc[i] = 0.0f;
-    bool ok = true;
     for (int b = b0; b < b1; ++b) {
-      const int n = min(kAttBlock, T - b * kAttBlock);
-      const int t0 = warp * kAttTile;
-      const int nvalid = min(kAttTile, n - t0), first = max(0, lo - b * kAttBlock - t0);
-      const bool tile = nvalid > first;
-      const int new_row = (has_new && p / kAttBlock == b) ? p - b * kAttBlock : -1;
-      const bool mine = new_row >= t0 && new_row < t0 + kAttTile;
-      ok = mbar_wait(&sm.bar[0], phase & 1u) && ok;
-      phase ^= 1u;
-      if (!__syncthreads_and(ok)) break;
-      if (mine) *reinterpret_cast<uint2*>(sm.k + new_row * 128 + 4 * lane) =
-          *reinterpret_cast<const uint2*>(sm.knew + 4 * lane);
-      ok = mbar_wait(&sm.bar[1], (phase >> 1) & 1u) && ok;
-      phase ^= 2u;
-      if (!__syncthreads_and(ok)) break;
-      if (mine) *reinterpret_cast<uint2*>(sm.v + new_row * 128 + 4 * lane) =
-          *reinterpret_cast<const uint2*>(sm.vnew + 4 * lane);
-      __syncwarp();
-      if (tile) tile_fold_bf16(sm, sm.p[warp], warp, first, nvalid, st);
-      // both buffers are read; the next block's copies may overwrite them
+      const int r0 = b * kAttBlock + kBfQuarter * pair;
+      const int n = bf16_quarter_rows(r0, T, lo);
+      // every copy this pair issued is waited for (bounded), whatever the
+      // other pairs do; after a failure no further copy is issued
+      const bool issued = sm.issued[pair] != 0;
+      if (issued) {
+        if (mbar_wait(&sm.bar[pair], phase)) {
+          phase ^= 1u;
+        } else {
+          ok = false;
+          *failed = 1;
+        }
+      }
+      const int t0 = kAttTile * half;  // this warp's tile inside the quarter
+      const int nvalid = min(kAttTile, n - t0), first = max(0, lo - r0 - t0);
+      uint16_t* kt = sm.k[pair] + t0 * 128;
+      uint16_t* vt = sm.v[pair] + t0 * 128;
+      const int new_row = p - r0 - t0;  // the new token's row in this tile, if it is there
+      const bool go = __all_sync(0xffffffffu, issued && ok && !*failed);  // uniform over the warp
+      if (go && nvalid > first) {
+        if (has_new && new_row >= 0 && new_row < kAttTile) {
+          *reinterpret_cast<uint2*>(kt + new_row * 128 + 4 * lane) = *reinterpret_cast<const uint2*>(sm.knew + 4 * lane);
+          *reinterpret_cast<uint2*>(vt + new_row * 128 + 4 * lane) = *reinterpret_cast<const uint2*>(sm.vnew + 4 * lane);
+          __syncwarp();
+        }
+        tile_fold_bf16(kt, vt, sm.q, sm.p[warp], first, nvalid, st);
+      }
+      // both warps of the pair are done with the slot (the generic-proxy
+      // patch and the reads come before the next bulk copy into it)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncthreads();
-      if (threadIdx.x == 0 && b + 1 < b1) {
-        issue_bf16_rows(sm, 0, a, g, b + 1, T);
-        issue_bf16_rows(sm, 1, a, g, b + 1, T);
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + pair), "r"(64));
+      if (leader && b + 1 < b1) {
+        const int n1 = bf16_quarter_rows(r0 + kAttBlock, T, lo);
+        const bool go1 = n1 && !*failed;
+        if (go1) issue_bf16_quarter(sm, pair, a, g, r0 + kAttBlock, n1);
+        sm.issued[pair] = go1;
       }
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + pair), "r"(64));  // issued[pair] seen by the pair
     }
-    if (!ok) {
-      if (threadIdx.x == 0) {
-        report(a.status, kStatusBulkTimeout);
-        for (int s = 0; s < 2; ++s) mbar_wait(&sm.bar[s], (phase >> s) & 1u);
-      }
+    if (__syncthreads_or(!ok)) {
+      if (!ok) mbar_wait(&sm.bar[pair], phase);  // the copy that did not land (bounded)
+      if (threadIdx.x == 0) report(a.status, kStatusBulkTimeout);
       return;
     }
+    // to the WarpState layout (lane 4gq + tq: head gq, dims state_dim(i, tq))
+    // through this warp's 4 KB of the K slots (every copy has been consumed)
     WarpState ws;
-    const int gq = lane >> 2;
+    const int gq = lane >> 2, tq = lane & 3;
     ws.m = st.m[0];
     ws.l = st.l[0];
 #pragma unroll
@@ -253,9 +280,18 @@ static __global__ void __launch_bounds__(kAttWarps * 32, 1) k_attn_partial_bf16(
       ws.m = gq == h ? st.m[h] : ws.m;
       ws.l = gq == h ? st.l[h] : ws.l;
     }
+    float(*tr)[128] = reinterpret_cast<float(*)[128]>(&sm.k[0][0]) + warp * kHeadsPerKv;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) ws.acc[i] = st.acc[i];
-    __syncthreads();  // the fold scratch overlays the query-preparation buffers
+    for (int h = 0; h < kHeadsPerKv; ++h)
+      *reinterpret_cast<float4*>(&tr[h][4 * lane]) =
+          make_float4(st.acc[4 * h], st.acc[4 * h + 1], st.acc[4 * h + 2], st.acc[4 * h + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) ws.acc[i] = tr[gq][state_dim(i, tq)];
+    // the next item's copies into the K slots come after these generic-proxy accesses
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    // (the barrier above ends every warp's tiles: the fold scratch overlays
+    // the query-preparation buffers)
     warps_fold_store(ws, warp, sm.sc, CtaSync{}, a.partials + (size_t(g * kHeadsPerKv) * icap + item) * kPartialFloats,
                      size_t(icap) * kPartialFloats);
     __syncthreads();
