@@ -389,7 +389,11 @@ def run_rec(args):
     if not args.no_config4 and not sharded and ctx0 <= 4096:
         del sess, kv, engine, storage
         torch.cuda.empty_cache()
-        config4 = measure_config4(args, weights, world, rank, barrier)
+        try:
+            config4 = measure_config4(args, weights, world, rank, barrier)
+        except Exception as exc:  # the config-3 measurement above stands; the line records what failed
+            config4 = {"error": f"{type(exc).__name__}: {exc}"[:400]}
+            print(f"config-4 measurement failed: {exc}", file=sys.stderr, flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -98,6 +98,10 @@ typedef struct RecModelDesc {
   int32_t shared_inter;
   int32_t dense_inter;
   int32_t sliding_window;
+  /* bits of the embedding's affine g64 codes: 4 (0 means 4) or 8 (the
+   * production checkpoint's embedding, mixed_bits.py:25-30;
+   * graph schedule) */
+  int32_t embed_bits;
 } RecModelDesc;
 
 /* int4 g64 affine matrix in MLX layout: codes uint32[N, K/8], scales and
@@ -126,7 +130,7 @@ typedef struct RecLayerWeights {
 } RecLayerWeights;
 
 typedef struct RecGlobalWeights {
-  RecQMat embed;          /* int4 [V, H] */
+  RecQMat embed;          /* int4 [V, H] (int8 with embed_bits = 8: codes uint32[V, H/4]) */
   const void* final_norm; /* bf16 [H] */
   RecQMat lm_head;        /* int4 [V, H] */
 } RecGlobalWeights;

@@ -336,12 +336,12 @@ ORC_API void orc_gemv_int4(const uint32_t* w, const uint16_t* s, const uint16_t*
 }
 
 /* --------------------------------------------------------- embedding */
-static void embed(const RecQMat* m, int sd, int H, int token, uint16_t* h) {
-  const uint32_t* W = (const uint32_t*)m->w + (int64_t)token * (H / 8);
+static void embed(const RecQMat* m, int sd, int H, int token, int bits, uint16_t* h) {
+  const uint32_t* W = (const uint32_t*)m->w + (int64_t)token * (H * bits / 32);
   const uint16_t* S = (const uint16_t*)m->scales + (int64_t)token * (H / 64);
   const uint16_t* B = (const uint16_t*)m->biases + (int64_t)token * (H / 64);
   for (int i = 0; i < H; ++i) {
-    float q = (float)((W[i / 8] >> (4 * (i % 8))) & 15u);
+    float q = bits == 8 ? (float)((W[i / 4] >> (8 * (i % 4))) & 255u) : (float)((W[i / 8] >> (4 * (i % 8))) & 15u);
     h[i] = to_bf(fmaf(sbv(S[i / 64], sd), q, sbv(B[i / 64], sd)));
   }
 }
@@ -1170,7 +1170,7 @@ ORC_API int orc_decode_step(const RecModelDesc* md, const RecLayerWeights* layer
   int n_super = (T + ATT_BLOCK * ATT_SUPER - 1) / (ATT_BLOCK * ATT_SUPER);
   Partial* supers = (Partial*)malloc(sizeof(Partial) * Hq * n_super);
 
-  embed(&gw->embed, sd, H, token, h);
+  embed(&gw->embed, sd, H, token, md->embed_bits == 8 ? 8 : 4, h);
   if (trace) memcpy(trace, h, sizeof(uint16_t) * H);
   for (int li = 0; li < md->n_layers; ++li) {
     const RecLayerWeights* L = &layers[li];

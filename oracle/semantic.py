@@ -233,7 +233,10 @@ def model_step(m, kvs: list, token: int, pos: int):
 
     cfg = m.cfg
     sd = 0 if cfg.scale_dtype == torch.float16 else 1
-    h = rbf(_dq(m.embed, sd, slice(token, token + 1))[0]).astype(np.float64)
+    eb = getattr(cfg, "embed_bits", 4)
+    E = m.embed
+    h = rbf(dequantize(np.asarray(E.w[token:token + 1], np.uint32), np.asarray(E.s[token:token + 1], np.uint16),
+                       np.asarray(E.b[token:token + 1], np.uint16), eb, sd)[0].astype(np.float64)).astype(np.float64)
     trace = [h]
     for L, kv in zip(m.layers, kvs):
         h = layer_step(cfg, L, kv, h, pos, sd)

@@ -46,6 +46,7 @@ class RecModelDesc(C.Structure):
         ("shared_inter", C.c_int32),
         ("dense_inter", C.c_int32),
         ("sliding_window", C.c_int32),
+        ("embed_bits", C.c_int32),
     ]
 
 

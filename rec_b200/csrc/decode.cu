@@ -63,11 +63,12 @@ __global__ void k_set_step(int* ctl, int token, int position, int n_eos, const i
   }
 }
 
-// Embedding row (int4 g64): h = bf16(fma(scale, q, bias)).  Also the first
-// trace row.  Reference megakernel.py:850-860.
+// Embedding row (int4 or int8 g64): h = bf16(fma(scale, q, bias)).  Also the
+// first trace row.  Reference megakernel.py:850-860 (int4), mixed_bits.py:25-30
+// (the production checkpoint's int8 codes).
 template <int SD>
 __global__ void __launch_bounds__(256) k_embed(int* ctl, QMatDev emb, int H, int V, int capacity, int token_base,
-                                               uint16_t* h, uint16_t* trace) {
+                                               uint16_t* h, uint16_t* trace, int bits) {
   int tok = ctl[kCtlToken];
   const int pos = ctl[kCtlPosition];
   if (tok < 0 || tok >= V) {
@@ -76,9 +77,9 @@ __global__ void __launch_bounds__(256) k_embed(int* ctl, QMatDev emb, int H, int
   }
   if ((pos < 0 || pos - token_base >= capacity) && threadIdx.x == 0) report(ctl + kCtlStatus, kStatusBadPosition);
   grid_launch_dependents();
-  const uint32_t* w = emb.w + size_t(tok) * (H / 8);
+  const uint32_t* w = emb.w + size_t(tok) * (H * bits / 32);
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    const float q = float((w[i >> 3] >> (4 * (i & 7))) & 15u);
+    const float q = bits == 8 ? float((w[i >> 2] >> (8 * (i & 3))) & 255u) : float((w[i >> 3] >> (4 * (i & 7))) & 15u);
     const float s = sb<SD>(emb.s[size_t(tok) * (H / 64) + (i >> 6)]);
     const float b = sb<SD>(emb.b[size_t(tok) * (H / 64) + (i >> 6)]);
     const uint16_t v = to_bf(__fmaf_rn(s, q, b));
@@ -274,7 +275,8 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
   if (kind == kKEmbed)  // a split session checks the position against the whole context
     return launch(k_embed<SD>, 1, 256, 0, st, false, c->ctl, QMatDev{(const uint32_t*)c->g.embed.w,
                   (const uint16_t*)c->g.embed.scales, (const uint16_t*)c->g.embed.biases}, H, d.vocab,
-                  c->world > 1 ? c->cap_total : c->capacity, c->world > 1 ? 0 : c->token_base, c->h, c->trace);
+                  c->world > 1 ? c->cap_total : c->capacity, c->world > 1 ? 0 : c->token_base, c->h, c->trace,
+                  d.embed_bits == 8 ? 8 : 4);
   if (kind == kKStepEnd) return launch(k_step_end, 1, 32, 0, st, pdl, c->ctl);
   if (kind != kKHead) {
     const RecLayerWeights& L = c->layers[li];
@@ -633,9 +635,11 @@ REC_API int rec_create(const RecModelDesc* desc, RecCtx** out) {
   REC_CHECK_ARG(d.dense_inter == 0 || d.dense_inter == 2048 || d.dense_inter == 4096 || d.dense_inter == 6144,
                 "dense_inter must be 0, 2048, 4096 or 6144");
   REC_CHECK_ARG(d.sliding_window >= 0, "sliding_window must be >= 0");
+  REC_CHECK_ARG(d.embed_bits == 0 || d.embed_bits == 4 || d.embed_bits == 8, "embed_bits must be 4 or 8");
   RecCtx* c = new RecCtx();
   c->d = d;
-  c->flint = d.shared_inter > 0 || d.kv_bits == 16;  // a bf16 cache too: graph schedule only
+  // a bf16 cache and an int8 embedding too: graph schedule only
+  c->flint = d.shared_inter > 0 || d.kv_bits == 16 || d.embed_bits == 8;
   c->grid = sm_count();
   *out = c;
   return REC_OK;
@@ -694,7 +698,7 @@ REC_API void rec_destroy(RecCtx* ctx) {
 REC_API int rec_set_weights(RecCtx* c, const RecLayerWeights* layers, int32_t n_layers, const RecGlobalWeights* g) {
   REC_CHECK_ARG(c && layers && g, "rec_set_weights: null argument");
   REC_CHECK_ARG(n_layers == c->d.n_layers, "expected %d layers, got %d", c->d.n_layers, n_layers);
-  bool flint = c->d.shared_inter > 0 || c->d.kv_bits == 16;
+  bool flint = c->d.shared_inter > 0 || c->d.kv_bits == 16 || c->d.embed_bits == 8;
   for (int i = 0; i < n_layers; ++i) {
     const RecLayerWeights& L = layers[i];
     const bool dense = (L.kind & REC_LAYER_DENSE) != 0;

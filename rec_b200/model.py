@@ -48,6 +48,7 @@ class ModelConfig:
     no_rope_layers: tuple = ()
     sliding_layers: tuple = ()
     sliding_window: int = 0
+    embed_bits: int = 4  # 8: the production checkpoint's int8 embedding
 
     def layer_kind(self, i: int) -> int:
         """REC_LAYER_* bits of layer i."""
@@ -60,7 +61,7 @@ class ModelConfig:
         """Options that put the model on the graph schedule (and its prefill
         on the decode step): the Flint layer options and a bf16 cache."""
         return bool(self.shared_inter or self.dense_layers or self.no_rope_layers or self.sliding_layers
-                    or self.kv_bits == 16)
+                    or self.kv_bits == 16 or self.embed_bits == 8)
 
     def desc(self) -> abi.RecModelDesc:
         return abi.RecModelDesc(
@@ -71,7 +72,7 @@ class ModelConfig:
             kv_bits=self.kv_bits, router_mode=self.router_mode, flags=self.flags, rms_eps=self.rms_eps,
             rope_theta=self.rope_theta, shared_inter=self.shared_inter,
             dense_inter=self.dense_inter if self.dense_layers else 0,
-            sliding_window=self.sliding_window if self.sliding_layers else 0)
+            sliding_window=self.sliding_window if self.sliding_layers else 0, embed_bits=self.embed_bits)
 
     def weight_bytes_per_token(self) -> int:
         """Algorithmic bytes streamed per decode step (weights only)."""
@@ -104,7 +105,8 @@ TINY = ModelConfig(name="tiny", n_layers=2, n_experts=16, top_k=4, vocab=4096, k
 TINY_FLINT = ModelConfig(name="tiny_flint", n_layers=3, n_experts=16, top_k=6, moe_inter=512, vocab=4096,
                          kv_bits=8, scale_dtype=torch.bfloat16, router_mode=abi.REC_ROUTER_SIGMOID,
                          flags=abi.REC_FLAG_SINKS | abi.REC_FLAG_QK_NORM, shared_inter=1024, dense_layers=(0,),
-                         dense_inter=6144, no_rope_layers=(1,), sliding_layers=(0, 2), sliding_window=300)
+                         dense_inter=6144, no_rope_layers=(1,), sliding_layers=(0, 2), sliding_window=300,
+                         embed_bits=8)
 
 
 def _quantize(w: torch.Tensor, bits: int, scale_dtype: torch.dtype):
@@ -253,7 +255,7 @@ def generate_weights(cfg: ModelConfig, seed: int = 0, device: str | torch.device
             L.q_norm = _norm_weight(gen, d, device)
             L.k_norm = _norm_weight(gen, d, device)
         layers.append(L)
-    embed = qmat(cfg.vocab, h, std=1.0)
+    embed = QTensor(*_quantize(_normal(gen, (cfg.vocab, h), 1.0, device), cfg.embed_bits, sd))
     final_norm = _norm_weight(gen, h, device)
     lm_head = qmat(cfg.vocab, h)
     return ModelWeights(cfg, layers, embed, final_norm, lm_head, expert_range=(lo, hi))

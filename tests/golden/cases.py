@@ -36,7 +36,8 @@ GOLDEN_B = replace(GOLDEN_A, name="golden_b", n_q_heads=32, n_kv_heads=4, n_expe
 # in the MoE layers, a NoPE layer between two sliding-window layers whose
 # 40-position window starts inside block 1 (block 0 skipped, a tile cut)
 GOLDEN_FLINT = replace(GOLDEN_B, name="golden_flint", n_layers=3, shared_inter=256, dense_layers=(0,),
-                       dense_inter=6144, no_rope_layers=(1,), sliding_layers=(0, 2), sliding_window=40)
+                       dense_inter=6144, no_rope_layers=(1,), sliding_layers=(0, 2), sliding_window=40,
+                       embed_bits=8)
 # a bf16 cache (the reference megakernel's kv_format "bf16")
 GOLDEN_BF16 = replace(GOLDEN_A, name="golden_bf16", kv_bits=16)
 DECODE_CASES = {"decode_a": (GOLDEN_A, 101), "decode_b": (GOLDEN_B, 202), "decode_flint": (GOLDEN_FLINT, 303),
@@ -108,7 +109,10 @@ def host_model(cfg: ModelConfig, seed: int) -> SimpleNamespace:
             L.q_norm = _bf(rng, d, 0.1, 1.0)
             L.k_norm = _bf(rng, d, 0.1, 1.0)
         layers.append(L)
-    return SimpleNamespace(cfg=cfg, layers=layers, embed=_q(rng, cfg.vocab, h, sd, std=1.0),
+    eb = cfg.embed_bits
+    w_emb = oracle.bf16_to_f32(oracle.f32_to_bf16(rng.standard_normal((cfg.vocab, h), dtype=np.float32)))
+    c, s, b = oracle.quantize(w_emb, eb, sd)
+    return SimpleNamespace(cfg=cfg, layers=layers, embed=SimpleNamespace(w=c, s=s, b=b),
                            final_norm=_bf(rng, h, 0.1, 1.0), lm_head=_q(rng, cfg.vocab, h, sd))
 
 
