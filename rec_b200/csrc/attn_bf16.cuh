@@ -147,6 +147,7 @@ __device__ __forceinline__ void tile_fold_bf16(const uint16_t* kt, const uint16_
   float pv[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) pv[i] = 0.0f;
+#pragma unroll 4
   for (int r = first; r < nvalid; ++r) {
     const float4 pa = *reinterpret_cast<const float4*>(&p_sm[r][0]);
     const float4 pb = *reinterpret_cast<const float4*>(&p_sm[r][4]);
