@@ -102,6 +102,11 @@ typedef struct RecModelDesc {
    * production checkpoint's embedding, mixed_bits.py:25-30;
    * graph schedule) */
   int32_t embed_bits;
+  /* bits of the V codes when they differ from the K codes' (kv_bits): 0
+   * (same), 4 or 8 -- the reference's MixedQuantizedKVCache keeps K at 8 and
+   * V at 4 bits (model.py:35-37,40-82); a mixed cache runs on the graph
+   * schedule, V codes uint32[Hkv, C, 128*kv_value_bits/32] */
+  int32_t kv_value_bits;
 } RecModelDesc;
 
 /* int4 g64 affine matrix in MLX layout: codes uint32[N, K/8], scales and

@@ -92,14 +92,15 @@ class HostModel:
 
 class HostKV:
     def __init__(self, cfg, capacity: int):
-        words = 128 * cfg.kv_bits // 32
+        vbits = getattr(cfg, "kv_value_bits", 0) or cfg.kv_bits
+        words = {"k": 128 * cfg.kv_bits // 32, "v": 128 * vbits // 32}
         self.capacity = capacity
         self.layers = []
         recs = []
         for _ in range(cfg.n_layers):
             L = {}
             for kv in ("k", "v"):
-                L[f"{kv}_codes"] = np.zeros((cfg.n_kv_heads, capacity, words), np.uint32)
+                L[f"{kv}_codes"] = np.zeros((cfg.n_kv_heads, capacity, words[kv]), np.uint32)
                 L[f"{kv}_scales"] = np.zeros((cfg.n_kv_heads, capacity, 2), np.uint16)
                 L[f"{kv}_biases"] = np.zeros((cfg.n_kv_heads, capacity, 2), np.uint16)
             self.layers.append(L)

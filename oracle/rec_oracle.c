@@ -384,7 +384,9 @@ static void head_norm(uint16_t* x, const uint16_t* w, float eps) {
 }
 
 /* ------------------------------------------------- KV quantized append */
-static void kv_store(const RecKVLayer* kv, int Hkv, int C, int bits, int pos, const uint16_t* k,
+/* K codes `bits` wide, V codes `vbits` wide (the reference's mixed cache keeps
+ * K at 8 and V at 4 bits, model.py:35-37,40-82). */
+static void kv_store(const RecKVLayer* kv, int Hkv, int C, int bits, int vbits, int pos, const uint16_t* k,
                      const uint16_t* v) {
   if (bits == 16) { /* bf16 rows, stored as they are */
     for (int g = 0; g < Hkv; ++g) {
@@ -394,7 +396,7 @@ static void kv_store(const RecKVLayer* kv, int Hkv, int C, int bits, int pos, co
     }
     return;
   }
-  int words = 128 * bits / 32;
+  int words = 128 * bits / 32, vwords = 128 * vbits / 32;
   for (int g = 0; g < Hkv; ++g)
     for (int half = 0; half < 2; ++half) {
       int64_t slot = (int64_t)g * C + pos;
@@ -405,13 +407,13 @@ static void kv_store(const RecKVLayer* kv, int Hkv, int C, int bits, int pos, co
       }
       quant_group(wk, bits, REC_SCALE_BF16, (uint32_t*)kv->k_codes + slot * words + half * (words / 2),
                   (uint16_t*)kv->k_scales + slot * 2 + half, (uint16_t*)kv->k_biases + slot * 2 + half);
-      quant_group(wv, bits, REC_SCALE_BF16, (uint32_t*)kv->v_codes + slot * words + half * (words / 2),
+      quant_group(wv, vbits, REC_SCALE_BF16, (uint32_t*)kv->v_codes + slot * vwords + half * (vwords / 2),
                   (uint16_t*)kv->v_scales + slot * 2 + half, (uint16_t*)kv->v_biases + slot * 2 + half);
     }
 }
 ORC_API void orc_kv_store(const RecKVLayer* kv, int Hkv, int C, int bits, int pos, const uint16_t* k,
                           const uint16_t* v) {
-  kv_store(kv, Hkv, C, bits, pos, k, v);
+  kv_store(kv, Hkv, C, bits, bits, pos, k, v);
 }
 
 /* ---------------------------------------------------------- attention */
@@ -559,13 +561,13 @@ static void att_tile_bf16(const QPrep* Q, const RecKVLayer* kv, int g, int C, in
   st->m = mn;
 }
 
-static void att_tile(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bits, int t0, int T, int base,
-                     int lo, Partial* st) {
+static void att_tile(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bits, int vbits, int t0, int T,
+                     int base, int lo, Partial* st) {
   if (bits == 16) {
     att_tile_bf16(Q, kv, g, C, t0, T, base, lo, st);
     return;
   }
-  int words = 128 * bits / 32;
+  int words = 128 * bits / 32, vwords = 128 * vbits / 32;
   const uint32_t* KC = (const uint32_t*)kv->k_codes;
   const uint32_t* VC = (const uint32_t*)kv->v_codes;
   const uint16_t *KS = (const uint16_t*)kv->k_scales, *KB = (const uint16_t*)kv->k_biases;
@@ -605,7 +607,7 @@ static void att_tile(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bit
       int32_t acc = 0;
       for (int j = first; j < nvalid; ++j) {
         int64_t slot = (int64_t)g * C + t0 - base + j;
-        acc += wq[j] * (int32_t)kv_code(VC + slot * words, bits, d);
+        acc += wq[j] * (int32_t)kv_code(VC + slot * vwords, vbits, d);
       }
       st->acc[d] = fmaf(st->acc[d], alpha, fmaf((float)acc, down, B));
     }
@@ -616,8 +618,8 @@ static void att_tile(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bit
 /* Partial of one q head over item it (blocks [nbi*it, nbi*it+nbi) ∩ blocks < T):
  * warp w folds tiles 8b + w of the item's blocks in order into its running
  * state; the eight warp states are folded as a tree ((w0 w1)(w2 w3))((w4 w5)(w6 w7)). */
-static void att_item(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bits, int it, int T, int base,
-                     int lo, Partial* out) {
+static void att_item(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bits, int vbits, int it, int T,
+                     int base, int lo, Partial* out) {
   const int nbi = att_item_blocks((T + ATT_BLOCK - 1) / ATT_BLOCK);
   Partial st[ATT_WARPS];
   for (int w = 0; w < ATT_WARPS; ++w) {
@@ -625,7 +627,7 @@ static void att_item(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bit
     for (int b = it * nbi; b < (it + 1) * nbi; ++b) {
       int t0 = b * ATT_BLOCK + w * ATT_TILE;
       if (t0 >= T) break;
-      att_tile(Q, kv, g, C, bits, t0, T, base, lo, &st[w]);
+      att_tile(Q, kv, g, C, bits, vbits, t0, T, base, lo, &st[w]);
     }
   }
   for (int step = 1; step < ATT_WARPS; step *= 2)
@@ -638,8 +640,8 @@ static void att_item(const QPrep* Q, const RecKVLayer* kv, int g, int C, int bit
  * supers[h * (s_hi - s_lo) + s - s_lo] = items of super s (64 blocks) merged
  * in order.  The cache holds tokens from `base` on (token t in slot t - base
  * of each head's C rows): a rank of a split session passes its own slice. */
-static void attention_supers(const uint16_t* q, const RecKVLayer* kv, int Hq, int Hkv, int C, int bits, int T,
-                             int base, int lo, int s_lo, int s_hi, Partial* supers) {
+static void attention_supers(const uint16_t* q, const RecKVLayer* kv, int Hq, int Hkv, int C, int bits, int vbits,
+                             int T, int base, int lo, int s_lo, int s_hi, Partial* supers) {
   int nblocks = (T + ATT_BLOCK - 1) / ATT_BLOCK;
   int nbi = att_item_blocks(nblocks), per_super = ATT_SUPER / nbi;
   int nitems = (nblocks + nbi - 1) / nbi;
@@ -654,7 +656,7 @@ static void attention_supers(const uint16_t* q, const RecKVLayer* kv, int Hq, in
       p_empty(S);
       for (int it = s * per_super; it < (s + 1) * per_super && it < nitems; ++it) {
         Partial P;
-        att_item(&Q, kv, g, C, bits, it, T, base, lo, &P);
+        att_item(&Q, kv, g, C, bits, vbits, it, T, base, lo, &P);
         p_merge(S, &P);
       }
     }
@@ -663,7 +665,7 @@ static void attention_supers(const uint16_t* q, const RecKVLayer* kv, int Hq, in
 
 ORC_API void orc_attention_supers_shard(const uint16_t* q, const RecKVLayer* kv, int Hq, int Hkv, int C, int bits,
                                         int T, int base, int s_lo, int s_hi, Partial* supers) {
-  attention_supers(q, kv, Hq, Hkv, C, bits, T, base, 0, s_lo, s_hi, supers);
+  attention_supers(q, kv, Hq, Hkv, C, bits, bits, T, base, 0, s_lo, s_hi, supers);
 }
 
 /* A sliding-window layer: tokens [lo, T) only, lo = max(0, T - window)
@@ -671,7 +673,14 @@ ORC_API void orc_attention_supers_shard(const uint16_t* q, const RecKVLayer* kv,
 ORC_API void orc_attention_supers_window(const uint16_t* q, const RecKVLayer* kv, int Hq, int Hkv, int C, int bits,
                                          int T, int window, Partial* supers, int n_super) {
   const int lo = window > 0 && T > window ? T - window : 0;
-  attention_supers(q, kv, Hq, Hkv, C, bits, T, 0, lo, 0, n_super, supers);
+  attention_supers(q, kv, Hq, Hkv, C, bits, bits, T, 0, lo, 0, n_super, supers);
+}
+
+/* The same with V codes vbits wide (a mixed cache). */
+ORC_API void orc_attention_supers_kv(const uint16_t* q, const RecKVLayer* kv, int Hq, int Hkv, int C, int bits,
+                                     int vbits, int T, int window, Partial* supers, int n_super) {
+  const int lo = window > 0 && T > window ? T - window : 0;
+  attention_supers(q, kv, Hq, Hkv, C, bits, vbits, T, 0, lo, 0, n_super, supers);
 }
 
 /* Super-chunk partials of every q head over tokens [0, T) of one layer's
@@ -1190,8 +1199,9 @@ ORC_API int orc_decode_step(const RecModelDesc* md, const RecLayerWeights* layer
       if ((md->flags & REC_FLAG_QK_NORM) && L->k_norm) head_norm(k + g * D, (const uint16_t*)L->k_norm, md->rms_eps);
       if (rope) rope_head(k + g * D, cs);
     }
-    kv_store(&kv[li], Hkv, C, md->kv_bits, pos, k, v);
-    orc_attention_supers_window(q, &kv[li], Hq, Hkv, C, md->kv_bits, T,
+    const int vbits = md->kv_value_bits ? md->kv_value_bits : md->kv_bits;
+    kv_store(&kv[li], Hkv, C, md->kv_bits, vbits, pos, k, v);
+    orc_attention_supers_kv(q, &kv[li], Hq, Hkv, C, md->kv_bits, vbits, T,
                                 (L->kind & REC_LAYER_SLIDING) ? md->sliding_window : 0, supers, n_super);
     orc_attention_final(supers, Hq, n_super,
                         (md->flags & REC_FLAG_SINKS) ? (const uint16_t*)L->sinks : NULL, att);

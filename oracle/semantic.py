@@ -145,9 +145,10 @@ class SemanticKV:
     """Quantized cache of one layer held by the semantic model: codes /
     scales / biases like the oracle's (model.py:45-82 quantize-on-append)."""
 
-    def __init__(self, layer_arrays: dict, bits: int):
+    def __init__(self, layer_arrays: dict, bits: int, vbits: int | None = None):
         self.L = {n: np.array(a, copy=True) for n, a in layer_arrays.items()}
         self.bits = bits
+        self.vbits = vbits or bits  # V codes' width (the reference's mixed cache: K 8, V 4)
 
     def append(self, pos: int, k_bf16v: np.ndarray, v_bf16v: np.ndarray) -> None:
         from . import f32_to_bf16, quantize
@@ -156,7 +157,7 @@ class SemanticKV:
             if self.bits == 16:  # a bf16 cache keeps the rows as they are
                 self.L[f"{name}_codes"].view(np.uint16)[:, pos] = f32_to_bf16(np.asarray(x, np.float32))
                 continue
-            c, s, b = quantize(np.asarray(x, np.float32)[:, None, :], self.bits, 1)
+            c, s, b = quantize(np.asarray(x, np.float32)[:, None, :], self.bits if name == "k" else self.vbits, 1)
             self.L[f"{name}_codes"][:, pos] = c[:, 0]
             self.L[f"{name}_scales"][:, pos] = s[:, 0]
             self.L[f"{name}_biases"][:, pos] = b[:, 0]
@@ -166,7 +167,7 @@ class SemanticKV:
         if self.bits == 16:
             return bf16_to_f32(L[f"{name}_codes"].view(np.uint16)[:, :upto]).astype(np.float64)
         return dequantize(L[f"{name}_codes"][:, :upto], L[f"{name}_scales"][:, :upto], L[f"{name}_biases"][:, :upto],
-                          self.bits, 1).astype(np.float64)
+                          self.bits if name == "k" else self.vbits, 1).astype(np.float64)
 
 
 def mlp(gate, up, down, sd: int, xn: np.ndarray) -> np.ndarray:

@@ -47,6 +47,7 @@ class RecModelDesc(C.Structure):
         ("dense_inter", C.c_int32),
         ("sliding_window", C.c_int32),
         ("embed_bits", C.c_int32),
+        ("kv_value_bits", C.c_int32),
     ]
 
 

@@ -93,9 +93,9 @@ __device__ __forceinline__ void prep_q_heads(const uint16_t* qkv, int g, const f
 }
 
 // The new token's K and V of kv head g, RoPE'd (K) and quantized into the
-// patch rows; warps 0,1 = K groups, 2,3 = V groups.  With g_* non-null the
-// rows are also stored into the cache.
-template <int BITS>
+// patch rows; warps 0,1 = K groups, 2,3 = V groups (K codes BITS wide, V
+// codes VBITS wide).  With g_* non-null the rows are also stored into the cache.
+template <int BITS, int VBITS = BITS>
 __device__ __forceinline__ void prep_new_kv(const uint16_t* qkv, int hq_total, int hkv, int g, const float* cs,
                                             const uint16_t* k_norm, float eps, AttnScratch& sc, int warp,
                                             uint32_t* g_kc, uint32_t* g_vc, uint16_t* g_ks, uint16_t* g_kb,
@@ -117,9 +117,10 @@ __device__ __forceinline__ void prep_new_kv(const uint16_t* qkv, int hq_total, i
   for (int j = 0; j < 4; ++j) tmp[4 * lane + j] = kv4[j];
   __syncwarp();
   const float v0 = tmp[64 * grp + 2 * lane], v1 = tmp[64 * grp + 2 * lane + 1];
-  const QGroupParams qp = warp_group_params(v0, v1, BITS);
-  const uint32_t word = warp_pack(quant_code(v0, qp, BITS), quant_code(v1, qp, BITS), BITS);
-  constexpr int GW = 64 * BITS / 32;
+  const int bits = is_k ? BITS : VBITS;
+  const QGroupParams qp = warp_group_params(v0, v1, bits);
+  const uint32_t word = warp_pack(quant_code(v0, qp, bits), quant_code(v1, qp, bits), bits);
+  const int GW = 64 * bits / 32;
   uint32_t* prow = (is_k ? sc.kpatch : sc.vpatch) + grp * GW;
   if (lane < GW) prow[lane] = word;
   const uint16_t scb = to_bf(qp.scale), bib = to_bf(qp.bias);
@@ -139,15 +140,14 @@ __device__ __forceinline__ void prep_new_kv(const uint16_t* qkv, int hq_total, i
 }
 
 // One warp copies the patch rows into row `row` of a K / V tile pair.
-template <int BITS>
+template <int BITS, int VBITS = BITS>
 __device__ __forceinline__ void patch_row(uint32_t* kc, uint16_t* ks, uint16_t* kb, uint32_t* vc, uint16_t* vs,
                                           uint16_t* vb, int row, const AttnScratch& sc) {
   constexpr int RW = 128 * BITS / 32;
+  constexpr int RWV = 128 * VBITS / 32;
   const int lane = threadIdx.x & 31;
-  if (lane < RW) {
-    kc[row * RW + lane] = sc.kpatch[lane];
-    vc[row * RW + lane] = sc.vpatch[lane];
-  }
+  if (lane < RW) kc[row * RW + lane] = sc.kpatch[lane];
+  if (lane < RWV) vc[row * RWV + lane] = sc.vpatch[lane];
   if (lane < 2) {
     ks[row * 2 + lane] = sc.kps[lane];
     kb[row * 2 + lane] = sc.kpb[lane];
@@ -219,55 +219,59 @@ __device__ __forceinline__ void warps_fold_store(WarpState& st, int warp, AttnSc
 // with no valid row leaves the state unchanged.
 // SPLIT: full tiles take the unmasked instance of tile_fold (same results);
 // the persistent kernel keeps one instance for its instruction footprint.
-template <int BITS, bool SPLIT = false>
+template <int BITS, bool SPLIT = false, int VBITS = BITS>
 __device__ __forceinline__ void block_tiles(uint32_t* kc, uint16_t* ks, uint16_t* kb, uint32_t* vc, uint16_t* vs,
                                             uint16_t* vb, int n, int new_row, const AttnScratch& sc, int warp,
                                             WarpState& st, int first = 0) {
   constexpr int RW = 128 * BITS / 32;
+  constexpr int RWV = 128 * VBITS / 32;
   const int t0 = warp * kAttTile;
   const int nvalid = min(kAttTile, n - t0);
   const int tfirst = max(0, first - t0);
   if (nvalid <= tfirst) return;
-  if (new_row >= t0 && new_row < t0 + kAttTile) patch_row<BITS>(kc, ks, kb, vc, vs, vb, new_row, sc);
+  if (new_row >= t0 && new_row < t0 + kAttTile) patch_row<BITS, VBITS>(kc, ks, kb, vc, vs, vb, new_row, sc);
   if (SPLIT && nvalid == kAttTile && tfirst == 0)
-    tile_fold<BITS, true>(kc + t0 * RW, ks + 2 * t0, kb + 2 * t0, vc + t0 * RW, vs + 2 * t0, vb + 2 * t0, nvalid,
-                          sc.qf, st);
+    tile_fold<BITS, true, VBITS>(kc + t0 * RW, ks + 2 * t0, kb + 2 * t0, vc + t0 * RWV, vs + 2 * t0, vb + 2 * t0,
+                                 nvalid, sc.qf, st);
   else
-    tile_fold<BITS, false>(kc + t0 * RW, ks + 2 * t0, kb + 2 * t0, vc + t0 * RW, vs + 2 * t0, vb + 2 * t0, nvalid,
-                           sc.qf, st, tfirst);
+    tile_fold<BITS, false, VBITS>(kc + t0 * RW, ks + 2 * t0, kb + 2 * t0, vc + t0 * RWV, vs + 2 * t0, vb + 2 * t0,
+                                  nvalid, sc.qf, st, tfirst);
 }
 
 // ---------------------------------------------------------------------------
 // Standalone kernels (the graph schedule)
 // ---------------------------------------------------------------------------
-template <int BITS>
+template <int BITS, int VBITS = BITS>
 struct AttnStage {
-  static constexpr int ROW_WORDS = 128 * BITS / 32;
+  static constexpr int ROW_WORDS = 128 * BITS / 32;    // K
+  static constexpr int VROW_WORDS = 128 * VBITS / 32;  // V
   alignas(128) uint32_t kc[kAttBlock * ROW_WORDS];
-  alignas(128) uint32_t vc[kAttBlock * ROW_WORDS];
+  alignas(128) uint32_t vc[kAttBlock * VROW_WORDS];
   alignas(16) uint16_t ks[kAttBlock * 2];
   alignas(16) uint16_t kb[kAttBlock * 2];
   alignas(16) uint16_t vs[kAttBlock * 2];
   alignas(16) uint16_t vb[kAttBlock * 2];
 };
-template <int BITS>
+template <int BITS, int VBITS = BITS>
 struct AttnSmem {
-  AttnStage<BITS> st[2];
+  AttnStage<BITS, VBITS> st[2];
   AttnScratch sc;
   uint64_t bar[2];
 };
 
 // Bulk copies of block b (global index) of kv head g into stage s.
-template <int BITS>
-__device__ __forceinline__ void issue_block(AttnSmem<BITS>& sm, int s, const AttnArgs& a, int g, int b, int T) {
-  constexpr int RW = AttnStage<BITS>::ROW_WORDS;
+template <int BITS, int VBITS = BITS>
+__device__ __forceinline__ void issue_block(AttnSmem<BITS, VBITS>& sm, int s, const AttnArgs& a, int g, int b,
+                                            int T) {
+  constexpr int RW = AttnStage<BITS, VBITS>::ROW_WORDS;
+  constexpr int RWV = AttnStage<BITS, VBITS>::VROW_WORDS;
   const int n = min(kAttBlock, T - b * kAttBlock);
   const int n4 = (n + 3) & ~3;
   const size_t slot = size_t(g) * a.capacity + size_t(b) * kAttBlock - size_t(a.token_base);
-  const uint32_t cb = uint32_t(n4) * RW * 4, sbytes = uint32_t(n4) * 4;
-  mbar_expect_tx(&sm.bar[s], 2 * cb + 4 * sbytes);
+  const uint32_t cb = uint32_t(n4) * RW * 4, cbv = uint32_t(n4) * RWV * 4, sbytes = uint32_t(n4) * 4;
+  mbar_expect_tx(&sm.bar[s], cb + cbv + 4 * sbytes);
   bulk_g2s(sm.st[s].kc, a.k_codes + slot * RW, cb, &sm.bar[s]);
-  bulk_g2s(sm.st[s].vc, a.v_codes + slot * RW, cb, &sm.bar[s]);
+  bulk_g2s(sm.st[s].vc, a.v_codes + slot * RWV, cbv, &sm.bar[s]);
   bulk_g2s(sm.st[s].ks, a.k_scales + slot * 2, sbytes, &sm.bar[s]);
   bulk_g2s(sm.st[s].kb, a.k_biases + slot * 2, sbytes, &sm.bar[s]);
   bulk_g2s(sm.st[s].vs, a.v_scales + slot * 2, sbytes, &sm.bar[s]);
@@ -279,11 +283,12 @@ struct CtaSync {
 };
 
 // Item partials.  Persistent grid; item it = (kv head it % Hkv, item it / Hkv).
-template <int BITS>
+template <int BITS, int VBITS = BITS>
 __global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnArgs a) {
-  constexpr int RW = AttnStage<BITS>::ROW_WORDS;
+  constexpr int RW = AttnStage<BITS, VBITS>::ROW_WORDS;
+  constexpr int RWV = AttnStage<BITS, VBITS>::VROW_WORDS;
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  AttnSmem<BITS>& sm = *reinterpret_cast<AttnSmem<BITS>*>(smem_raw);
+  AttnSmem<BITS, VBITS>& sm = *reinterpret_cast<AttnSmem<BITS, VBITS>*>(smem_raw);
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     mbar_init(&sm.bar[0], 1);
@@ -319,14 +324,14 @@ __global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnAr
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
     const int g = it % a.hkv, item = i_lo + it / a.hkv;
     const int b0 = item * nbi, b1 = min(b0 + nbi, nblk);
-    if (threadIdx.x == 0) issue_block<BITS>(sm, 0, a, g, b0, T);
+    if (threadIdx.x == 0) issue_block<BITS, VBITS>(sm, 0, a, g, b0, T);
     if (sm.sc.qg != g) prep_q_heads<BITS>(a.qkv, g, cs, a.q_norm, a.eps, sm.sc, warp);
     const bool has_new = p >= b0 * kAttBlock && p < b1 * kAttBlock;
     if (has_new) {
       const size_t slot = size_t(g) * a.capacity + size_t(p - a.token_base);
-      prep_new_kv<BITS>(a.qkv, a.hq, a.hkv, g, cs, a.k_norm, a.eps, sm.sc, warp, a.k_codes + slot * RW,
-                        a.v_codes + slot * RW, a.k_scales + slot * 2, a.k_biases + slot * 2, a.v_scales + slot * 2,
-                        a.v_biases + slot * 2);
+      prep_new_kv<BITS, VBITS>(a.qkv, a.hq, a.hkv, g, cs, a.k_norm, a.eps, sm.sc, warp, a.k_codes + slot * RW,
+                               a.v_codes + slot * RWV, a.k_scales + slot * 2, a.k_biases + slot * 2,
+                               a.v_scales + slot * 2, a.v_biases + slot * 2);
     }
     __syncthreads();
     if (threadIdx.x == 0) sm.sc.qg = g;
@@ -335,14 +340,15 @@ __global__ void __launch_bounds__(kAttWarps * 32, 2) k_attn_partial(const AttnAr
     bool ok = true;
     for (int b = b0; b < b1; ++b) {
       const int s = (b - b0) & 1;
-      if (threadIdx.x == 0 && b + 1 < b1) issue_block<BITS>(sm, s ^ 1, a, g, b + 1, T);
+      if (threadIdx.x == 0 && b + 1 < b1) issue_block<BITS, VBITS>(sm, s ^ 1, a, g, b + 1, T);
       ok = mbar_wait(&sm.bar[s], (phase >> s) & 1u) && ok;
       phase ^= 1u << s;
       if (!__syncthreads_and(ok)) break;
       const int n = min(kAttBlock, T - b * kAttBlock);
       const int new_row = (has_new && p / kAttBlock == b) ? p - b * kAttBlock : -1;
-      AttnStage<BITS>& S = sm.st[s];
-      block_tiles<BITS, true>(S.kc, S.ks, S.kb, S.vc, S.vs, S.vb, n, new_row, sm.sc, warp, st, lo - b * kAttBlock);
+      AttnStage<BITS, VBITS>& S = sm.st[s];
+      block_tiles<BITS, true, VBITS>(S.kc, S.ks, S.kb, S.vc, S.vs, S.vb, n, new_row, sm.sc, warp, st,
+                                     lo - b * kAttBlock);
       // the tile may have been patched through the generic proxy, and the
       // next bulk copy into this stage must not overtake this block's reads
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -355,11 +355,14 @@ __device__ __forceinline__ float tile_max(const float (&v)[8]) {
 //     F = min(14 - exponent(max|w| (1 + 2^-7)), 100); wq_t = rint(w_t 2^F)
 //     (|wq| <= 32514: signed byte limbs);
 //     acc_d' = fma(acc_d, alpha, fma(float(sum_t wq_t code_td), 2^-F, tile_sum(x))).
-template <int BITS, bool FULL = false>
+// BITS: the K codes' width; VBITS: the V codes' (the reference's mixed cache
+// keeps K at 8 and V at 4 bits, model.py:35-37,40-82).
+template <int BITS, bool FULL = false, int VBITS = BITS>
 __device__ __forceinline__ void tile_fold(const uint32_t* kc, const uint16_t* ks, const uint16_t* kb,
                                           const uint32_t* vc, const uint16_t* vs, const uint16_t* vb, int nvalid,
                                           const QFrags& qf, WarpState& st, int first = 0) {
   constexpr int RW = 128 * BITS / 32;
+  constexpr int RWV = 128 * VBITS / 32;
   constexpr uint32_t M4 = 0x0F0F0F0Fu;
   const int lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
   // ---- scores: C[group][nt]
@@ -479,13 +482,13 @@ __device__ __forceinline__ void tile_fold(const uint32_t* kc, const uint16_t* ks
     for (int side = 0; side < 2; ++side) {
       const int tb = 16 * side + 2 * tq;
       const int rows[4] = {tb, tb + 1, tb + 8, tb + 9};
-      if constexpr (BITS == 4) {
+      if constexpr (VBITS == 4) {
         // odd tq reads each row pair in swapped order: the four threads of a
         // column then hit two rows of each parity (two bank halves)
         const int odd = tq & 1;
         uint32_t wv[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) wv[i] = vc[(tb + 8 * (i >> 1) + ((i & 1) ^ odd)) * RW + 8 * g + gq];
+        for (int i = 0; i < 4; ++i) wv[i] = vc[(tb + 8 * (i >> 1) + ((i & 1) ^ odd)) * RWV + 8 * g + gq];
         uint32_t r[4];
         transpose4s(wv[0], wv[1], wv[2], wv[3], odd ? 0x1504u : 0x5140u, odd ? 0x3726u : 0x7362u, r[0], r[1], r[2],
                     r[3]);
@@ -497,7 +500,7 @@ __device__ __forceinline__ void tile_fold(const uint32_t* kc, const uint16_t* ks
       } else {
         uint2 wv[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) wv[i] = *reinterpret_cast<const uint2*>(vc + rows[i] * RW + 16 * g + 2 * gq);
+        for (int i = 0; i < 4; ++i) wv[i] = *reinterpret_cast<const uint2*>(vc + rows[i] * RWV + 16 * g + 2 * gq);
         transpose4(wv[0].x, wv[1].x, wv[2].x, wv[3].x, bt[side][0], bt[side][1], bt[side][2], bt[side][3]);
         transpose4(wv[0].y, wv[1].y, wv[2].y, wv[3].y, bt[side][4], bt[side][5], bt[side][6], bt[side][7]);
       }

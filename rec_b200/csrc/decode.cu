@@ -334,6 +334,11 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
       const int agrid = sm_count() * (d.kv_bits == 4 ? 2 : 1);  // 4-bit stages fit two CTAs per SM
       if (kind == kKAttn && d.kv_bits == 16)  // a bf16 cache: one block of K and V rows per CTA
         return launch(k_attn_partial_bf16, sm_count(), kAttWarps * 32, sizeof(AttnBfSmem), st, pdl, a);
+      const int vbits = d.kv_value_bits ? d.kv_value_bits : d.kv_bits;
+      if (kind == kKAttn && vbits != d.kv_bits)  // a mixed cache (K and V codes of different widths)
+        return d.kv_bits == 8
+                   ? launch(k_attn_partial<8, 4>, sm_count(), kAttWarps * 32, sizeof(AttnSmem<8, 4>), st, pdl, a)
+                   : launch(k_attn_partial<4, 8>, sm_count(), kAttWarps * 32, sizeof(AttnSmem<4, 8>), st, pdl, a);
       if (kind == kKAttn)
         return d.kv_bits == 4 ? launch(k_attn_partial<4>, agrid, kAttWarps * 32, sizeof(AttnSmem<4>), st, pdl, a)
                               : launch(k_attn_partial<8>, agrid, kAttWarps * 32, sizeof(AttnSmem<8>), st, pdl, a);
@@ -636,10 +641,14 @@ REC_API int rec_create(const RecModelDesc* desc, RecCtx** out) {
                 "dense_inter must be 0, 2048, 4096 or 6144");
   REC_CHECK_ARG(d.sliding_window >= 0, "sliding_window must be >= 0");
   REC_CHECK_ARG(d.embed_bits == 0 || d.embed_bits == 4 || d.embed_bits == 8, "embed_bits must be 4 or 8");
+  REC_CHECK_ARG(d.kv_value_bits == 0 || d.kv_value_bits == d.kv_bits ||
+                    (d.kv_bits != 16 && (d.kv_value_bits == 4 || d.kv_value_bits == 8)),
+                "kv_value_bits must be 0 or, with 4- or 8-bit K codes, 4 or 8");
   RecCtx* c = new RecCtx();
   c->d = d;
-  // a bf16 cache and an int8 embedding too: graph schedule only
-  c->flint = d.shared_inter > 0 || d.kv_bits == 16 || d.embed_bits == 8;
+  // a bf16 or mixed cache and an int8 embedding too: graph schedule only
+  c->flint = d.shared_inter > 0 || d.kv_bits == 16 || d.embed_bits == 8 ||
+             (d.kv_value_bits != 0 && d.kv_value_bits != d.kv_bits);
   c->grid = sm_count();
   *out = c;
   return REC_OK;
@@ -698,7 +707,7 @@ REC_API void rec_destroy(RecCtx* ctx) {
 REC_API int rec_set_weights(RecCtx* c, const RecLayerWeights* layers, int32_t n_layers, const RecGlobalWeights* g) {
   REC_CHECK_ARG(c && layers && g, "rec_set_weights: null argument");
   REC_CHECK_ARG(n_layers == c->d.n_layers, "expected %d layers, got %d", c->d.n_layers, n_layers);
-  bool flint = c->d.shared_inter > 0 || c->d.kv_bits == 16 || c->d.embed_bits == 8;
+  bool flint = c->flint;
   for (int i = 0; i < n_layers; ++i) {
     const RecLayerWeights& L = layers[i];
     const bool dense = (L.kind & REC_LAYER_DENSE) != 0;

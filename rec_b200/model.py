@@ -49,6 +49,7 @@ class ModelConfig:
     sliding_layers: tuple = ()
     sliding_window: int = 0
     embed_bits: int = 4  # 8: the production checkpoint's int8 embedding
+    kv_value_bits: int = 0  # V codes' width when it differs from kv_bits (the reference's K8 / V4 cache)
 
     def layer_kind(self, i: int) -> int:
         """REC_LAYER_* bits of layer i."""
@@ -61,7 +62,12 @@ class ModelConfig:
         """Options that put the model on the graph schedule (and its prefill
         on the decode step): the Flint layer options and a bf16 cache."""
         return bool(self.shared_inter or self.dense_layers or self.no_rope_layers or self.sliding_layers
-                    or self.kv_bits == 16 or self.embed_bits == 8)
+                    or self.kv_bits == 16 or self.embed_bits == 8 or self.v_bits != self.kv_bits)
+
+    @property
+    def v_bits(self) -> int:
+        """Bits of the V codes (kv_bits unless the cache is mixed)."""
+        return self.kv_value_bits or self.kv_bits
 
     def desc(self) -> abi.RecModelDesc:
         return abi.RecModelDesc(
@@ -72,7 +78,8 @@ class ModelConfig:
             kv_bits=self.kv_bits, router_mode=self.router_mode, flags=self.flags, rms_eps=self.rms_eps,
             rope_theta=self.rope_theta, shared_inter=self.shared_inter,
             dense_inter=self.dense_inter if self.dense_layers else 0,
-            sliding_window=self.sliding_window if self.sliding_layers else 0, embed_bits=self.embed_bits)
+            sliding_window=self.sliding_window if self.sliding_layers else 0, embed_bits=self.embed_bits,
+            kv_value_bits=self.kv_value_bits)
 
     def weight_bytes_per_token(self) -> int:
         """Algorithmic bytes streamed per decode step (weights only)."""
@@ -88,7 +95,7 @@ class ModelConfig:
 
     def kv_bytes_per_token(self, context: int) -> int:
         scales = 2 * 2 * self.head_dim // 64 if self.kv_bits < 16 else 0  # a bf16 cache has none
-        per = 2 * self.n_kv_heads * (self.head_dim * self.kv_bits // 8 + scales)
+        per = self.n_kv_heads * (self.head_dim * (self.kv_bits + self.v_bits) // 8 + 2 * scales)
         return self.n_layers * per * context
 
 
@@ -284,11 +291,11 @@ class KVCache:
         for `rows`; scales and biases allocated for the full capacity."""
         from .vmm import ReservedCodes
 
-        words = 128 * cfg.kv_bits // 32
+        words = {"k_codes": 128 * cfg.kv_bits // 32, "v_codes": 128 * cfg.v_bits // 32}
         dev = torch.device(device)
         layers, reserved = [], []
         for _ in range(cfg.n_layers):
-            R = {n: ReservedCodes(cfg.n_kv_heads, capacity, words, dev) for n in ("k_codes", "v_codes")}
+            R = {n: ReservedCodes(cfg.n_kv_heads, capacity, words[n], dev) for n in ("k_codes", "v_codes")}
             L = {}
             for kv in ("k", "v"):
                 L[f"{kv}_codes"] = None
@@ -318,12 +325,12 @@ class KVCache:
     def allocate(cls, cfg: ModelConfig, capacity: int, device="cuda") -> "KVCache":
         if capacity % 256:
             raise ValueError("KV capacity must be a multiple of 256")
-        words = 128 * cfg.kv_bits // 32
+        words = {"k": 128 * cfg.kv_bits // 32, "v": 128 * cfg.v_bits // 32}
         layers = []
         for _ in range(cfg.n_layers):
             L = {}
             for kv in ("k", "v"):
-                L[f"{kv}_codes"] = torch.zeros(cfg.n_kv_heads, capacity, words, dtype=torch.int32, device=device)
+                L[f"{kv}_codes"] = torch.zeros(cfg.n_kv_heads, capacity, words[kv], dtype=torch.int32, device=device)
                 L[f"{kv}_scales"] = torch.zeros(cfg.n_kv_heads, capacity, 2, dtype=torch.bfloat16, device=device)
                 L[f"{kv}_biases"] = torch.zeros(cfg.n_kv_heads, capacity, 2, dtype=torch.bfloat16, device=device)
             layers.append(L)
@@ -365,7 +372,7 @@ class KVCache:
                     if self.cfg.kv_bits == 16:  # bf16 rows (a pair per 32-bit word)
                         L[f"{kv}_codes"][:, p0:p1] = x.to(torch.bfloat16).view(torch.int16).view(torch.int32)
                         continue
-                    c, s, b = quantize_affine(x, self.cfg.kv_bits, torch.bfloat16)
+                    c, s, b = quantize_affine(x, self.cfg.kv_bits if kv == "k" else self.cfg.v_bits, torch.bfloat16)
                     L[f"{kv}_codes"][:, p0:p1] = c
                     L[f"{kv}_scales"][:, p0:p1] = s
                     L[f"{kv}_biases"][:, p0:p1] = b

@@ -40,8 +40,10 @@ GOLDEN_FLINT = replace(GOLDEN_B, name="golden_flint", n_layers=3, shared_inter=2
                        embed_bits=8)
 # a bf16 cache (the reference megakernel's kv_format "bf16")
 GOLDEN_BF16 = replace(GOLDEN_A, name="golden_bf16", kv_bits=16)
+# the reference's mixed cache (K 8-bit, V 4-bit; model.py:35-37,40-82)
+GOLDEN_MIXED = replace(GOLDEN_B, name="golden_mixed", kv_bits=8, kv_value_bits=4)
 DECODE_CASES = {"decode_a": (GOLDEN_A, 101), "decode_b": (GOLDEN_B, 202), "decode_flint": (GOLDEN_FLINT, 303),
-                "decode_bf16": (GOLDEN_BF16, 404)}
+                "decode_bf16": (GOLDEN_BF16, 404), "decode_mixed": (GOLDEN_MIXED, 505)}
 
 CAPACITY = 512
 CONTEXT = 300      # cached positions before decoding (a ragged second block)
@@ -136,7 +138,7 @@ def fill_kv(hkv, cfg: ModelConfig, seed: int) -> None:
             if cfg.kv_bits == 16:  # bf16 rows as they are
                 L[f"{name}_codes"].view(np.uint16)[:, :CONTEXT] = oracle.f32_to_bf16(x)
                 continue
-            c, s, b = oracle.quantize(x, cfg.kv_bits, 1)
+            c, s, b = oracle.quantize(x, cfg.kv_bits if name == "k" else cfg.v_bits, 1)
             L[f"{name}_codes"][:, :CONTEXT] = c
             L[f"{name}_scales"][:, :CONTEXT] = s
             L[f"{name}_biases"][:, :CONTEXT] = b

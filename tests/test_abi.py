@@ -54,7 +54,7 @@ def test_constants_match_header():
 
 def test_struct_sizes():
     p = C.sizeof(C.c_void_p)
-    assert C.sizeof(abi.RecModelDesc) == 20 * 4
+    assert C.sizeof(abi.RecModelDesc) == 21 * 4
     assert C.sizeof(abi.RecQMat) == 3 * p
     # pointers, then the int32 kind (padded to a pointer) and the shared expert
     assert C.sizeof(abi.RecLayerWeights) == (2 + 4 * 3 + 2 + 3 * 3 + 3 + 1 + 3 * 3) * p
@@ -137,3 +137,5 @@ def test_flint_options_are_checked_without_a_device():
     assert create(sliding_window=-1) == abi.REC_EINVAL
     assert create(embed_bits=8) == abi.REC_OK
     assert create(embed_bits=3) == abi.REC_EINVAL
+    assert create(kv_value_bits=4) == abi.REC_OK  # K 8-bit, V 4-bit: the reference's mixed cache
+    assert create(kv_bits=16, kv_value_bits=4) == abi.REC_EINVAL

@@ -4,7 +4,8 @@ dense SwiGLU MLP layer of 6,144 rows (model.py:216-224, `mlp_only_layers`),
 a NoPE layer (model.py:158-163) and sliding-window layers (model.py:302-313),
 with the sigmoid + bias router, sinks, q/k head norms and bf16 scales; and
 the bf16 KV cache of the reference megakernel (kv_format "bf16",
-megakernel.py:619-693), with and without those options.
+megakernel.py:619-693) and the native path's mixed cache (K 8-bit, V 4-bit,
+model.py:35-37,40-82), with and without those options.
 
 Caches are filled with quantized synthetic K, V up to the decode position, so
 that the window starts past the first work item (600 tokens: window start in
@@ -46,7 +47,10 @@ def _compare_rows(kv, hkv, lo, hi):
 
 
 VARIANTS = {"flint_kv8": TINY_FLINT, "flint_bf16_kv": replace(TINY_FLINT, kv_bits=16),
-            "tiny_bf16_kv": replace(TINY, kv_bits=16)}
+            "tiny_bf16_kv": replace(TINY, kv_bits=16),
+            # the reference's mixed cache (K 8-bit, V 4-bit), and the other mix
+            "flint_k8_v4": replace(TINY_FLINT, kv_value_bits=4),
+            "tiny_k4_v8": replace(TINY, kv_bits=4, kv_value_bits=8)}
 
 
 @pytest.mark.parametrize("variant", list(VARIANTS))
@@ -142,15 +146,15 @@ def test_flint_ffn_entry_bitexact(cuda, layer):
     assert np.array_equal(_u16(h_dev), want)
 
 
-@pytest.mark.parametrize("kv_bits", [8, 16])
-def test_flint_engine_prefill_and_block(cuda, kv_bits):
+@pytest.mark.parametrize("kv_bits,kv_value_bits", [(8, 0), (16, 0), (8, 4)])
+def test_flint_engine_prefill_and_block(cuda, kv_bits, kv_value_bits):
     """Through the reference-facing API: QATSession.prefill (a model with
     layer options is prefilled by its decode step) and ResidentSampler.block
     at temperature 0 equal the oracle's chain."""
     from rec_b200.engine import build_decoder
 
     # the window moves within the short prompt
-    cfg = replace(TINY_FLINT, sliding_window=24, kv_bits=kv_bits)
+    cfg = replace(TINY_FLINT, sliding_window=24, kv_bits=kv_bits, kv_value_bits=kv_value_bits)
     w = generate_weights(cfg, seed=71, device="cuda")
     engine, sampler = build_decoder(w)
     prompt = [int(t) for t in np.random.default_rng(73).integers(0, cfg.vocab, 40)]

@@ -59,7 +59,7 @@ def _kv(cfg, seed, spikes=0):
                 L[f"{name}_codes"].view(np.uint16)[:, :CTX] = oracle.f32_to_bf16(x)
                 continue
             x = oracle.bf16_to_f32(oracle.f32_to_bf16(x))
-            c, s, b = oracle.quantize(x, cfg.kv_bits, 1)
+            c, s, b = oracle.quantize(x, cfg.kv_bits if name == "k" else cfg.v_bits, 1)
             L[f"{name}_codes"][:, :CTX] = c
             L[f"{name}_scales"][:, :CTX] = s
             L[f"{name}_biases"][:, :CTX] = b
@@ -138,7 +138,7 @@ def _teacher_forced(cfg, seed, spikes):
     try:
         out = []
         for li in range(cfg.n_layers):
-            kv = S.SemanticKV(base[li], cfg.kv_bits)
+            kv = S.SemanticKV(base[li], cfg.kv_bits, cfg.v_bits)
             sd = 0 if cfg.scale_dtype == torch.float16 else 1
             h_out = S.layer_step(cfg, m.layers[li], kv, oracle.bf16_to_f32(tr[li]).astype(np.float64), CTX, sd)
             out.append(S.rel_l2(oracle.bf16_to_f32(tr[li + 1]), h_out))
@@ -157,13 +157,14 @@ FLINT4 = replace(TINY, name="flint4", n_layers=4, top_k=6, moe_inter=512, scale_
 
 
 @pytest.mark.parametrize("name", ["config1_layer", "four_layers", "four_layers_near_one_hot", "flint_options",
-                                  "flint_bf16_kv"])
+                                  "flint_bf16_kv", "mixed_kv"])
 def test_layers_against_semantics(name):
     cfg, seed, spikes = {"config1_layer": (CONFIG1_LAYER, 71, 0),
                          "four_layers": (replace(TINY, n_layers=4), 81, 0),
                          "four_layers_near_one_hot": (replace(TINY, n_layers=4), 81, 3),
                          "flint_options": (FLINT4, 91, 0),
-                         "flint_bf16_kv": (replace(FLINT4, kv_bits=16), 93, 0)}[name]
+                         "flint_bf16_kv": (replace(FLINT4, kv_bits=16), 93, 0),
+                         "mixed_kv": (replace(FLINT4, kv_bits=8, kv_value_bits=4), 95, 0)}[name]
     errs = _teacher_forced(cfg, seed, spikes)
     print(name, [f"{e:.2e}" for e in errs])
     assert max(errs) < LAYER_TOL, errs
