@@ -60,6 +60,11 @@ def parse():
     p.add_argument("--shard", action="store_true",
                    help="with N GPUs: one session split over the GPUs (expert parallelism + split-KV, the "
                         "config-4 partitioning) instead of N independent sessions (config 3 replicas)")
+    p.add_argument("--flint", action="store_true",
+                   help="the reference's Flint model shape at full size (49 layers, 256 experts top-6, shared "
+                        "expert, dense layers, sliding windows, bf16 cache) over --flint-contexts, beside the "
+                        "reference's published M4 Pro decode rates")
+    p.add_argument("--flint-contexts", default="1024,32768,131072,258048")
     p.add_argument("--config1", action="store_true",
                    help="config 1: one decoder layer (64 experts top-8, 1,024-token 8-bit cache) per decode step")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -843,6 +848,80 @@ def run_sample_head(args):
                       "rows": rows}), flush=True)
 
 
+# The reference's published decode rates for its Flint model (batch 1, 1,024
+# output tokens, prefill excluded) on an Apple M4 Pro, from the README's
+# throughput chart.
+FLINT_M4_PRO = {1024: 131.2, 2048: 128.3, 4096: 123.0, 8192: 113.7, 16384: 99.0, 32768: 82.4, 65536: 61.7,
+                131072: 39.1, 258048: 22.6}
+
+
+def run_flint(args):
+    """The reference's Flint model shape at full size (rec_b200.model.FLINT:
+    49 layers, dense MLP layers 0-1, 256 experts top-6 + shared expert,
+    sliding-window and global layers, bf16 cache, int8 embedding), random-init
+    weights, the cache of every layer filled with synthetic K, V ~ N(0, 1)
+    (bf16) up to each context; greedy decode on the graph schedule in
+    device-side packets, CUDA events over K steps.  Algorithmic bytes per
+    token: the weights a step reads (the selected experts, the shared expert,
+    the dense MLPs, the router rows, the lm_head) + K and V of the attended
+    positions (global layers: the context; sliding layers: 513)."""
+    import torch
+
+    from rec_b200._lib import check, lib
+    from rec_b200.model import FLINT, KVCache, generate_weights
+    from rec_b200.session import DecodeSession
+
+    torch.cuda.set_device(0)
+    cfg = FLINT
+    W, K = max(3, args.warmup), min(args.steps, 128)
+    w = generate_weights(cfg, seed=0, device="cuda")
+    peak, kind = measured_peaks()
+    stream = torch.cuda.current_stream()
+    n_global = len(cfg.no_rope_layers)
+    rows = []
+    for ctx in [int(c) for c in args.flint_contexts.split(",")]:
+        cap = (ctx + W + K + 8 + 255) // 256 * 256
+        kv = KVCache.allocate(cfg, cap)
+        kv.fill_random(ctx, seed=2)
+        sess = DecodeSession(w, kv)
+
+        def run(n, token, position):
+            done = 0
+            while done < n:
+                c = min(PACKET, n - done)
+                check(lib().rec_decode_greedy(sess.ctx, token if done == 0 else -1, position + done, c, None, 0,
+                                              sess.ids.data_ptr(), sess.produced.data_ptr(), stream.cuda_stream))
+                done += c
+
+        run(W, 1000, ctx)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        run(K, -1, ctx + W)
+        b.record(stream)
+        torch.cuda.synchronize()
+        sess.check_status()
+        dt = a.elapsed_time(b) / 1e3
+        mid = ctx + W + K // 2
+        per_pos = cfg.n_kv_heads * 2 * 256  # K and V rows, bf16
+        kv_b = per_pos * (n_global * mid + (cfg.n_layers - n_global) * min(mid, cfg.sliding_window))
+        tok_b = cfg.weight_bytes_per_token() + kv_b
+        rows.append({"context": ctx, "tokens_per_s": round(K / dt, 2), "ms_per_step": round(dt / K * 1e3, 3),
+                     "bytes_per_step": int(tok_b), "GBps": round(tok_b / (dt / K) / 1e9, 1),
+                     "frac_of_peak": round(tok_b / (dt / K) / 1e9 / peak, 4),
+                     "reference_m4_pro_tokens_per_s": FLINT_M4_PRO.get(ctx)})
+        del sess, kv
+        torch.cuda.empty_cache()
+    print(json.dumps({"workload": "flint_full_shape_decode", "model": cfg.name, "steps": K, "warmup": W,
+                      "data": "synthetic: random-init weights of the Flint shape; caches of K, V ~ N(0, 1) in bf16",
+                      "assumed": "one global (NoPE, full-attention) layer in four (layers 3, 7, ..., 47); the "
+                                 "checkpoint's layer_types are not in the reference",
+                      "schedule": "graph (Flint layer options)", "peak_GBps": peak, "peak_source": kind,
+                      "reference_note": "the reference's rates are its published Apple M4 Pro figures for the real "
+                                        "Flint checkpoint (BASELINE.md), not a run on this box",
+                      "rows": rows}), flush=True)
+
+
 def run_config1(args):
     """Config 1: decode steps of one decoder layer (hidden 2048, GQA 32/4 x
     128, 64 experts top-8 with I 768, int4 g64 weights, 1,024-token 8-bit
@@ -965,6 +1044,8 @@ def main():
     args = parse()
     if args.config1:
         run_config1(args)
+    elif args.flint:
+        run_flint(args)
     elif args.sample_head:
         run_sample_head(args)
     elif args.prefill:

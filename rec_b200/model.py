@@ -114,6 +114,21 @@ TINY_FLINT = ModelConfig(name="tiny_flint", n_layers=3, n_experts=16, top_k=6, m
                          flags=abi.REC_FLAG_SINKS | abi.REC_FLAG_QK_NORM, shared_inter=1024, dense_layers=(0,),
                          dense_inter=6144, no_rope_layers=(1,), sliding_layers=(0, 2), sliding_window=300,
                          embed_bits=8)
+# The reference's Flint checkpoint at full size (model.py:14-37; megakernel.py:
+# 992-1004 asserts 49 layers, hidden 2048, 32/4 heads x 128, 256 experts
+# top-6, window 513, vocab 150,144): dense MLP layers 0-1 (I 6,144), shared
+# expert 1,024, routed I 512, sigmoid + bias router, sinks, q/k norms, int8
+# embedding, bf16 scales, the production megakernel's bf16 cache, RoPE theta
+# 10,000.  Which layers are global (NoPE, full attention) comes from the
+# checkpoint's config, which the reference does not ship: one in four is
+# assumed here (layers 3, 7, ..., 47), the rest slide over 513 positions.
+_FLINT_GLOBAL = tuple(range(3, 49, 4))
+FLINT = ModelConfig(name="flint_full_shape", n_layers=49, n_experts=256, top_k=6, moe_inter=512, vocab=150144,
+                    kv_bits=16, scale_dtype=torch.bfloat16, router_mode=abi.REC_ROUTER_SIGMOID,
+                    flags=abi.REC_FLAG_SINKS | abi.REC_FLAG_QK_NORM, shared_inter=1024, dense_layers=(0, 1),
+                    dense_inter=6144, no_rope_layers=_FLINT_GLOBAL,
+                    sliding_layers=tuple(i for i in range(49) if i not in _FLINT_GLOBAL), sliding_window=513,
+                    embed_bits=8, rope_theta=10000.0)
 
 
 def _quantize(w: torch.Tensor, bits: int, scale_dtype: torch.dtype):
