@@ -253,8 +253,9 @@ Layout layout_of(const RecCtx* c) {
 }
 
 // Kernels of one decode step, in launch order (per layer: kKQkv..kKDown; a
-// layer with a shared expert runs kKSharedGateUp and kKSharedDown between
-// kKGateUp and kKDown).
+// layer with a shared expert runs kKSharedDown between kKGateUp, which also
+// takes the shared expert's gate/up pairs, and kKDown; kKSharedGateUp runs
+// those pairs alone, for timing).
 enum KernelKind { kKEmbed = 0, kKQkv, kKAttn, kKCombine, kKOproj, kKRouter, kKGateUp, kKDown, kKHead, kKStepEnd,
                   kKCount, kKSharedGateUp = kKCount, kKSharedDown, kKAll };
 
@@ -421,8 +422,9 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
       e = launch(k_router<2048>, (d.n_experts + kWarps - 1) / kWarps, kThreads, sizeof(RouterSmem<2048>), st, pdl, a);
       return e;
     }
-    case kKGateUp:         // experts gate/up + SwiGLU (a dense layer: its MLP as one "expert")
-    case kKSharedGateUp: {  // the shared expert's gate/up + SwiGLU
+    case kKGateUp:         // experts gate/up + SwiGLU (a dense layer: its MLP as one "expert"; a
+                           // shared expert's pairs follow the routed ones in the same launch)
+    case kKSharedGateUp: {  // the shared expert's gate/up alone (diagnostics: rec_launch_kernel)
       const bool one = kind == kKSharedGateUp || layer_dense(c, li);
       const RecQMat& G = kind == kKSharedGateUp ? L.shared_gate : L.gate;
       const RecQMat& U = kind == kKSharedGateUp ? L.shared_up : L.up;
@@ -436,6 +438,13 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
       a.expert_lo = c->world > 1 && !one ? c->e_lo : 0;
       a.expert_hi = one ? 1 : (c->world > 1 ? c->e_hi : d.n_experts);
       a.act = kind == kKSharedGateUp ? c->act_shared : c->act;
+      if (kind == kKGateUp && layer_shared(c, li)) {  // act_shared = act + k * I: rank k of the same units
+        a.sgate = {(const uint32_t*)L.shared_gate.w, (const uint16_t*)L.shared_gate.scales,
+                   (const uint16_t*)L.shared_gate.biases};
+        a.sup = {(const uint32_t*)L.shared_up.w, (const uint16_t*)L.shared_up.scales,
+                 (const uint16_t*)L.shared_up.biases};
+        a.Is = d.shared_inter;
+      }
       a.status = status;
       a.pdl = pdl;
       constexpr int RSP = 16;
@@ -550,13 +559,13 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
   }
 }
 
-// The FFN kernels of layer li from the router on (the shared expert's two
-// kernels between the routed gate/up and the routed down + mix).
+// The FFN kernels of layer li from the router on (a shared expert's gate/up
+// pairs ride in the routed gate/up launch; its down projection runs between
+// that and the routed down + mix).
 template <int SD>
 cudaError_t enqueue_ffn_sd(RecCtx* c, int li, cudaStream_t st, bool pdl) {
   cudaError_t e = enqueue_kernel_sd<SD>(c, kKRouter, li, st, pdl);
   if (e == cudaSuccess) e = enqueue_kernel_sd<SD>(c, kKGateUp, li, st, pdl);
-  if (e == cudaSuccess && layer_shared(c, li)) e = enqueue_kernel_sd<SD>(c, kKSharedGateUp, li, st, pdl);
   if (e == cudaSuccess && layer_shared(c, li)) e = enqueue_kernel_sd<SD>(c, kKSharedDown, li, st, pdl);
   if (e == cudaSuccess) e = enqueue_kernel_sd<SD>(c, kKDown, li, st, pdl);
   return e;

@@ -168,7 +168,11 @@ struct GateUpArgs {
   const int* ids;          // [k]
   int k, I;
   int expert_lo, expert_hi;  // experts computed here (expert parallelism)
-  uint16_t* act;           // bf16 [k, I]
+  uint16_t* act;           // bf16 [k, I] (then the shared expert's [Is])
+  // an always-on shared expert (Is > 0): its Is gate/up pairs follow the
+  // routed ones as "rank k", from these matrices
+  QMatDev sgate, sup;
+  int Is;
   int* status;
   int pdl;
 };
@@ -183,35 +187,46 @@ struct GateUpSmem {
 };
 
 // Row pairs (gate row i, up row i) of expert rank r form work units
-// u = r*I + i; a stage holds up to RSP consecutive pairs of one rank.
+// u = r*I + i; a stage holds up to RSP consecutive pairs of one rank.  A
+// shared expert's pairs follow as rank k: u = k*I + i, i < Is.
 struct PairCursor {
-  int cur, end, I, rsp;
+  int cur, end, I, rsp, kI, Is;
   __device__ bool next(int& r, int& i0, int& n) {
     if (cur >= end) return false;
-    r = cur / I;
-    i0 = cur % I;
-    n = min(min(rsp, end - cur), I - i0);
+    if (cur < kI) {
+      r = cur / I;
+      i0 = cur % I;
+      n = min(min(rsp, end - cur), I - i0);
+    } else {
+      r = kI / I;
+      i0 = cur - kI;
+      n = min(min(rsp, end - cur), Is - i0);
+    }
     cur += n;
     return true;
   }
 };
 
+// expert < 0: the shared expert (rows i0.. of its own matrices).
 template <int RSP>
 __device__ __forceinline__ void issue_pairs(uint8_t* stage, uint64_t* bar, const GateUpArgs& a, int expert, int i0,
                                             int n) {
   using L = StageLayout<2048, 2 * RSP>;
   constexpr int RB = KCfg<2048>::ROW_BYTES, G = KCfg<2048>::GROUPS;
-  const size_t row = size_t(expert) * a.I + i0;
+  const bool sh = expert < 0;
+  const QMatDev& gm = sh ? a.sgate : a.gate;
+  const QMatDev& um = sh ? a.sup : a.up;
+  const size_t row = sh ? size_t(i0) : size_t(expert) * a.I + i0;
   const uint32_t wb = uint32_t(n) * RB, sbytes = uint32_t(n) * G * 2;
   mbar_expect_tx(bar, 2 * wb + 4 * sbytes);
-  bulk_g2s(stage, reinterpret_cast<const uint8_t*>(a.gate.w) + row * RB, wb, bar);
-  bulk_g2s(stage + RSP * RB, reinterpret_cast<const uint8_t*>(a.up.w) + row * RB, wb, bar);
+  bulk_g2s(stage, reinterpret_cast<const uint8_t*>(gm.w) + row * RB, wb, bar);
+  bulk_g2s(stage + RSP * RB, reinterpret_cast<const uint8_t*>(um.w) + row * RB, wb, bar);
   uint8_t* s = stage + L::W_BYTES;
   uint8_t* b = stage + L::W_BYTES + L::S_BYTES;
-  bulk_g2s(s, a.gate.s + row * G, sbytes, bar);
-  bulk_g2s(s + RSP * G * 2, a.up.s + row * G, sbytes, bar);
-  bulk_g2s(b, a.gate.b + row * G, sbytes, bar);
-  bulk_g2s(b + RSP * G * 2, a.up.b + row * G, sbytes, bar);
+  bulk_g2s(s, gm.s + row * G, sbytes, bar);
+  bulk_g2s(s + RSP * G * 2, um.s + row * G, sbytes, bar);
+  bulk_g2s(b, gm.b + row * G, sbytes, bar);
+  bulk_g2s(b + RSP * G * 2, um.b + row * G, sbytes, bar);
 }
 
 template <int SD, int RSP, int NS>
@@ -231,16 +246,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_gateup(const GateUpArgs a) {
   grid_launch_dependents();
 
   int u0, u1;
-  split_range(a.k * a.I / 2, gridDim.x, blockIdx.x, u0, u1);
+  const int kI = a.k * a.I;
+  split_range((kI + a.Is) / 2, gridDim.x, blockIdx.x, u0, u1);
   u0 *= 2;
   u1 *= 2;
-  PairCursor prod{u0, u1, a.I, RSP}, cons{u0, u1, a.I, RSP};
+  PairCursor prod{u0, u1, a.I, RSP, kI, a.Is}, cons{u0, u1, a.I, RSP, kI, a.Is};
   // Slot s completes one barrier phase per issued (local) stage; both sides
   // track the parity per slot, and `outstanding` (thread 0) the slots with a
   // copy in flight.
   uint32_t phase_bits = 0, outstanding = 0;
-  auto expert_of = [&](int r) { return a.ids[r]; };
-  auto local = [&](int r) { const int e = expert_of(r); return e >= a.expert_lo && e < a.expert_hi; };
+  // rank k is the shared expert (expert_of -1 - expert_lo: issue_pairs takes it by its sign)
+  auto expert_of = [&](int r) { return r < a.k ? a.ids[r] : -1 + a.expert_lo; };
+  auto local = [&](int r) {
+    if (r >= a.k) return true;
+    const int e = expert_of(r);
+    return e >= a.expert_lo && e < a.expert_hi;
+  };
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       int r, i0, n;
