@@ -261,6 +261,23 @@ enum KernelKind { kKEmbed = 0, kKQkv, kKAttn, kKCombine, kKOproj, kKRouter, kKGa
 
 bool layer_dense(const RecCtx* c, int li) { return (c->layers[li].kind & REC_LAYER_DENSE) != 0; }
 bool layer_shared(const RecCtx* c, int li) { return c->d.shared_inter > 0 && !layer_dense(c, li); }
+// The routed k_down computes the shared expert's down rows itself (one warp
+// beside the k routed ones): k < 8 and a shared intermediate it is built for.
+bool shared_down_fused(const RecCtx* c, int li) {
+  return layer_shared(c, li) && c->d.top_k < kMaxTopK && (c->d.shared_inter == 512 || c->d.shared_inter == 1024);
+}
+
+// The routed down + mix kernel for intermediate I, with the shared expert's
+// down rows fused when is > 0.
+template <int SD, int I>
+cudaError_t launch_down(const DownArgs& a, int dgrid, int is, cudaStream_t st, bool pdl) {
+  switch (is) {
+    case 0: return launch(k_down<I, SD>, dgrid, kThreads, sizeof(DownSmem<I>), st, pdl, a);
+    case 512: return launch(k_down<I, SD, 512>, dgrid, kThreads, down_smem_bytes<I, 512>(), st, pdl, a);
+    case 1024: return launch(k_down<I, SD, 1024>, dgrid, kThreads, down_smem_bytes<I, 1024>(), st, pdl, a);
+    default: return cudaErrorInvalidValue;
+  }
+}
 
 template <int SD>
 cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool pdl) {
@@ -504,7 +521,12 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
         }
       }
       DownArgs a = {};
-      a.shared_out = layer_shared(c, li) ? c->d_shared : nullptr;
+      const bool fused = shared_down_fused(c, li);
+      a.shared_out = layer_shared(c, li) && !fused ? c->d_shared : nullptr;
+      if (fused)
+        a.sdown = {(const uint32_t*)L.shared_down.w, (const uint16_t*)L.shared_down.scales,
+                   (const uint16_t*)L.shared_down.biases};
+      const int is = fused ? d.shared_inter : 0;
       a.down = {(const uint32_t*)L.down.w, (const uint16_t*)L.down.scales, (const uint16_t*)L.down.biases};
       a.act = c->act;
       a.ids = c->ids;
@@ -526,13 +548,12 @@ cudaError_t enqueue_kernel_sd(RecCtx* c, int kind, int li, cudaStream_t st, bool
       a.pdl = pdl;
       const int dgrid = std::max(grid, H / (2 * DownSmem<768>::RMAX / 2));
       switch (d.moe_inter) {
-        case 256: e = launch(k_down<256, SD>, dgrid, kThreads, sizeof(DownSmem<256>), st, pdl, a); break;
-        case 512: e = launch(k_down<512, SD>, dgrid, kThreads, sizeof(DownSmem<512>), st, pdl, a); break;
-        case 768: e = launch(k_down<768, SD>, dgrid, kThreads, sizeof(DownSmem<768>), st, pdl, a); break;
-        case 1024: e = launch(k_down<1024, SD>, dgrid, kThreads, sizeof(DownSmem<1024>), st, pdl, a); break;
+        case 256: return launch_down<SD, 256>(a, dgrid, is, st, pdl);
+        case 512: return launch_down<SD, 512>(a, dgrid, is, st, pdl);
+        case 768: return launch_down<SD, 768>(a, dgrid, is, st, pdl);
+        case 1024: return launch_down<SD, 1024>(a, dgrid, is, st, pdl);
         default: return cudaErrorInvalidValue;
       }
-      return e;
     }
     default:
       return cudaErrorInvalidValue;
@@ -566,7 +587,8 @@ template <int SD>
 cudaError_t enqueue_ffn_sd(RecCtx* c, int li, cudaStream_t st, bool pdl) {
   cudaError_t e = enqueue_kernel_sd<SD>(c, kKRouter, li, st, pdl);
   if (e == cudaSuccess) e = enqueue_kernel_sd<SD>(c, kKGateUp, li, st, pdl);
-  if (e == cudaSuccess && layer_shared(c, li)) e = enqueue_kernel_sd<SD>(c, kKSharedDown, li, st, pdl);
+  if (e == cudaSuccess && layer_shared(c, li) && !shared_down_fused(c, li))
+    e = enqueue_kernel_sd<SD>(c, kKSharedDown, li, st, pdl);
   if (e == cudaSuccess) e = enqueue_kernel_sd<SD>(c, kKDown, li, st, pdl);
   return e;
 }

@@ -351,6 +351,9 @@ struct DownArgs {
   // the routed mix as mlp = bf16(mix + shared) before the residual
   // (megakernel.py:955-958)
   const uint16_t* shared_out;
+  // or computed here (k_down<I, SD, IS> with IS > 0): the shared expert's down
+  // matrix [H, IS]; its activations follow the routed ones in act (k * I on)
+  QMatDev sdown;
   int* status;
   int pdl;
   // a session split over ranks (world > 1): the local experts' outputs go
@@ -371,12 +374,56 @@ struct DownSmem {
   float d[kMaxTopK][RMAX];
   uint64_t bar;
 };
+// The shared expert's part (k_down<I, SD, IS>), after DownSmem<I> in shared memory.
+template <int IS>
+struct DownSharedSmem {
+  using L = StageLayout<IS, DownSmem<256>::RMAX>;
+  alignas(128) uint8_t stage[L::BYTES];
+  alignas(16) uint16_t act[IS];
+  float d[DownSmem<256>::RMAX];
+};
+template <int I, int IS>
+constexpr size_t down_smem_bytes() {
+  return IS ? (sizeof(DownSmem<I>) + 127) / 128 * 128 + sizeof(DownSharedSmem<IS ? IS : 256>) : sizeof(DownSmem<I>);
+}
+
+// One warp: rows [0, n) of a stage of K-wide down rows (8 rows per pass, 4
+// lanes per row) against activations x, into d[row] = bf16(row dot).
+template <int K, int SD, int RMAX>
+__device__ __forceinline__ void down_rows(const uint8_t* st, const uint16_t* x, int n, float* d) {
+  using C = KCfg<K>;
+  const int lane = threadIdx.x & 31;
+  const FixScale fs = fix_scale_from_max(warp_maxabs(x, K));
+  GroupX gx[C::GPL];
+  const int sub = lane >> 2, l = lane & 3;
+  prep_lane_x<K>(x, fs, 0, l, gx);
+  for (int rb = 0; rb < n; rb += 16) {
+    int rows[2];
+    bool valid[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int rr = rb + 8 * q + sub;
+      valid[q] = rr < n;
+      rows[q] = valid[q] ? rr : 0;
+    }
+    float v[2];
+    lane_rows_partial<K, SD, 2>(stage_wrow<K, RMAX>(st, 0), stage_srow<K, RMAX>(st, 0), stage_brow<K, RMAX>(st, 0),
+                                rows, 0, l, gx, v);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      v[q] = bfly_sum<4>(valid[q] ? v[q] : 0.0f);
+      if (valid[q] && l == 0) d[rows[q]] = rbf(__fmul_rn(v[q], fs.down));
+    }
+  }
+}
 
 // Mix mode (single device): every CTA owns output rows [i0, i1) and computes
 // them for all k experts (warp r = rank r), then mixes in rank order:
 // m = bf16(d_0*bf16(w_0)) + 0; m = bf16(bf16(d_r*bf16(w_r)) + 0 + m);
-// with a shared expert m = bf16(m + shared); h = bf16(h + m).
-template <int I, int SD>
+// with a shared expert m = bf16(m + shared); h = bf16(h + m).  IS > 0: the
+// shared expert's down rows (K = IS) are computed here by warp k (k < 8),
+// from a.sdown and the activations at act + k * I.
+template <int I, int SD, int IS = 0>
 __global__ void __launch_bounds__(kThreads, 1) k_down(const DownArgs a) {
   using S = DownSmem<I>;
   using L = typename S::L;
@@ -384,6 +431,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_down(const DownArgs a) {
   static_assert(!C::wide, "down projection expects a narrow K");
   extern __shared__ __align__(128) uint8_t smem_raw[];
   S& sm = *reinterpret_cast<S*>(smem_raw);
+  using SS = DownSharedSmem<IS ? IS : 256>;
+  using CS = KCfg<IS ? IS : 256>;
+  SS& ss = *reinterpret_cast<SS*>(smem_raw + (sizeof(S) + 127) / 128 * 128);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int i0, i1;
   split_range(a.H / 2, gridDim.x, blockIdx.x, i0, i1);
@@ -402,7 +452,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_down(const DownArgs a) {
     uint32_t total = 0;
     for (int r = 0; r < a.k; ++r)
       if (local(r)) total += uint32_t(n) * (C::ROW_BYTES + 2 * C::GROUPS * 2);
+    if constexpr (IS > 0) total += uint32_t(n) * (CS::ROW_BYTES + 2 * CS::GROUPS * 2);
     mbar_expect_tx(&sm.bar, total);
+    if constexpr (IS > 0) {
+      using LS = typename SS::L;
+      const size_t row = size_t(i0);
+      bulk_g2s(ss.stage, reinterpret_cast<const uint8_t*>(a.sdown.w) + row * CS::ROW_BYTES, n * CS::ROW_BYTES,
+               &sm.bar);
+      bulk_g2s(ss.stage + LS::W_BYTES, a.sdown.s + row * CS::GROUPS, n * CS::GROUPS * 2, &sm.bar);
+      bulk_g2s(ss.stage + LS::W_BYTES + LS::S_BYTES, a.sdown.b + row * CS::GROUPS, n * CS::GROUPS * 2, &sm.bar);
+    }
     for (int r = 0; r < a.k; ++r) {
       if (!local(r)) continue;
       const size_t row = size_t(a.ids[r] - a.expert_lo) * a.H + i0;
@@ -415,6 +474,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_down(const DownArgs a) {
   grid_launch_dependents();
   for (int i = threadIdx.x * 8; i < a.k * I; i += kThreads * 8)
     *reinterpret_cast<uint4*>(&sm.act[0][0] + i) = ldg128(a.act + i);
+  if constexpr (IS > 0)
+    for (int i = threadIdx.x * 8; i < IS; i += kThreads * 8)
+      *reinterpret_cast<uint4*>(ss.act + i) = ldg128(a.act + a.k * I + i);
   __syncthreads();
   bool ok = n == 0 || mbar_wait(&sm.bar, 0);
   if (!__syncthreads_and(ok)) {
@@ -425,31 +487,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_down(const DownArgs a) {
     return;
   }
   const int r = warp;
-  if (r < a.k && local(r)) {
-    const FixScale fs = fix_scale_from_max(warp_maxabs(sm.act[r], I));
-    GroupX gx[C::GPL];
-    const int sub = lane >> 2, l = lane & 3;  // 8 rows per pass, 4 lanes per row
-    prep_lane_x<I>(sm.act[r], fs, 0, l, gx);
-    const uint8_t* st = sm.stage[r];
-    for (int rb = 0; rb < n; rb += 16) {
-      int rows[2];
-      bool valid[2];
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const int rr = rb + 8 * q + sub;
-        valid[q] = rr < n;
-        rows[q] = valid[q] ? rr : 0;
-      }
-      float v[2];
-      lane_rows_partial<I, SD, 2>(stage_wrow<I, S::RMAX>(st, 0), stage_srow<I, S::RMAX>(st, 0),
-                                  stage_brow<I, S::RMAX>(st, 0), rows, 0, l, gx, v);
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        v[q] = bfly_sum<4>(valid[q] ? v[q] : 0.0f);
-        if (valid[q] && l == 0) sm.d[r][rows[q]] = rbf(__fmul_rn(v[q], fs.down));
-      }
-    }
-  }
+  if (r < a.k && local(r)) down_rows<I, SD, S::RMAX>(sm.stage[r], sm.act[r], n, sm.d[r]);
+  if constexpr (IS > 0)
+    if (r == a.k) down_rows<IS, SD, S::RMAX>(ss.stage, ss.act, n, ss.d);
   __syncthreads();
   if (a.dout) {
     for (int t = threadIdx.x; t < a.k * n; t += kThreads) {
@@ -516,6 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_down(const DownArgs a) {
       m = rr == 0 ? t : rbf(__fadd_rn(t, m));
     }
     if (a.shared_out) m = rbf(__fadd_rn(m, bf(a.shared_out[i0 + i])));
+    if constexpr (IS > 0) m = rbf(__fadd_rn(m, ss.d[i]));
     const uint16_t hn = to_bf(__fadd_rn(bf(a.h[i0 + i]), m));
     a.h[i0 + i] = hn;
     if (a.trace_row) a.trace_row[i0 + i] = hn;
