@@ -639,6 +639,14 @@ void drop_graph(RecCtx* c) {
   c->step_exec = nullptr;
 }
 
+// Options of the model description that put it on the graph schedule: a
+// shared expert, a bf16 or mixed cache, an int8 embedding (layer kinds add to
+// them at rec_set_weights).
+bool desc_options(const RecModelDesc& d) {
+  return d.shared_inter > 0 || d.kv_bits == 16 || d.embed_bits == 8 ||
+         (d.kv_value_bits != 0 && d.kv_value_bits != d.kv_bits);
+}
+
 bool valid_qmat(const RecQMat& m) {
   return m.w && m.scales && m.biases && aligned16(m.w) && aligned16(m.scales) && aligned16(m.biases);
 }
@@ -677,9 +685,7 @@ REC_API int rec_create(const RecModelDesc* desc, RecCtx** out) {
                 "kv_value_bits must be 0 or, with 4- or 8-bit K codes, 4 or 8");
   RecCtx* c = new RecCtx();
   c->d = d;
-  // a bf16 or mixed cache and an int8 embedding too: graph schedule only
-  c->flint = d.shared_inter > 0 || d.kv_bits == 16 || d.embed_bits == 8 ||
-             (d.kv_value_bits != 0 && d.kv_value_bits != d.kv_bits);
+  c->flint = desc_options(d);
   c->grid = sm_count();
   *out = c;
   return REC_OK;
@@ -738,7 +744,7 @@ REC_API void rec_destroy(RecCtx* ctx) {
 REC_API int rec_set_weights(RecCtx* c, const RecLayerWeights* layers, int32_t n_layers, const RecGlobalWeights* g) {
   REC_CHECK_ARG(c && layers && g, "rec_set_weights: null argument");
   REC_CHECK_ARG(n_layers == c->d.n_layers, "expected %d layers, got %d", c->d.n_layers, n_layers);
-  bool flint = c->flint;
+  bool flint = desc_options(c->d);  // and any layer kind below
   for (int i = 0; i < n_layers; ++i) {
     const RecLayerWeights& L = layers[i];
     const bool dense = (L.kind & REC_LAYER_DENSE) != 0;
