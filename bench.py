@@ -896,9 +896,11 @@ def run_flint(args):
         run(W, 1000, ctx)
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("timed")
         a.record(stream)
         run(K, -1, ctx + W)
         b.record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         sess.check_status()
         dt = a.elapsed_time(b) / 1e3
