@@ -131,6 +131,68 @@ FLINT = ModelConfig(name="flint_full_shape", n_layers=49, n_experts=256, top_k=6
                     embed_bits=8, rope_theta=10000.0)
 
 
+# The reference's ModelArgs defaults (engine/src/rec_mlx/model.py:14-37).
+_REFERENCE_ARGS = dict(hidden_size=2048, intermediate_size=6144, moe_intermediate_size=512,
+                       shared_expert_intermediate_size=1024, num_hidden_layers=49, num_attention_heads=32,
+                       num_key_value_heads=4, head_dim=128, num_experts=256, num_experts_per_tok=6,
+                       vocab_size=150144, rms_norm_eps=1e-6, rope_theta=10000.0, sliding_window=513,
+                       layer_types=[], no_rope_layer_indices=[], mlp_only_layers=[0, 1],
+                       tie_word_embeddings=False, kv_key_bits=8, kv_value_bits=4, kv_group_size=64)
+
+
+def config_from_reference(config: dict, *, kv_format: str = "bf16", name: str = "from_reference") -> ModelConfig:
+    """The ModelConfig of a reference checkpoint's config.json (the
+    reference's ModelArgs fields, engine/src/rec_mlx/model.py:14-37; absent
+    keys take its defaults).  The Flint decoder always has the sigmoid + bias
+    router (model.py:245-254), a shared expert (model.py:243), attention sinks
+    and q/k head norms (model.py:155-163), bf16 scales and biases.
+
+    kv_format: "bf16" (the production engine's cache, checkpoint.py:7) or
+    "native" (MLX's MixedQuantizedKVCache with kv_key_bits / kv_value_bits,
+    model.py:35-37).  `mlx_export.embedding_bits` gives the embedding's code
+    width (8 in the production export, checkpoint.py:26-28).  Raises
+    ValueError for what these kernels do not take: tied embeddings, routed
+    experts other than int4, quantization other than int4 group 64, KV
+    groups other than 64, unknown layer types."""
+    a = dict(_REFERENCE_ARGS)
+    a.update({k: v for k, v in config.items() if k in _REFERENCE_ARGS})
+    n = int(a["num_hidden_layers"])
+    if a["tie_word_embeddings"]:
+        raise ValueError("tied embeddings are not supported: the lm_head is its own int4 matrix")
+    q = config.get("quantization", {"group_size": 64, "bits": 4})
+    if q.get("group_size") != 64 or q.get("bits") != 4:
+        raise ValueError("expected int4 group-64 quantization")
+    export = config.get("mlx_export", {})
+    if export.get("routed_expert_bits", 4) != 4 or export.get("bits", 4) != 4:
+        raise ValueError("routed experts and projections must be int4")
+    embed_bits = int(export.get("embedding_bits", 4))
+    if a["kv_group_size"] != 64:
+        raise ValueError("the KV cache is quantized in groups of 64")
+    types = list(a["layer_types"]) or ["full_attention"] * n
+    if len(types) != n or not set(types) <= {"full_attention", "sliding_attention"}:
+        raise ValueError("layer_types must name 'full_attention' or 'sliding_attention' for every layer")
+    if kv_format == "bf16":
+        kv_bits, kv_value_bits = 16, 0
+    elif kv_format == "native":
+        kv_bits = int(a["kv_key_bits"])
+        kv_value_bits = int(a["kv_value_bits"]) if int(a["kv_value_bits"]) != kv_bits else 0
+    else:
+        raise ValueError("kv_format must be 'bf16' or 'native'")
+    dense = tuple(int(i) for i in a["mlp_only_layers"])
+    return ModelConfig(
+        name=name, hidden=int(a["hidden_size"]), n_layers=n, n_q_heads=int(a["num_attention_heads"]),
+        n_kv_heads=int(a["num_key_value_heads"]), head_dim=int(a["head_dim"]), n_experts=int(a["num_experts"]),
+        top_k=int(a["num_experts_per_tok"]), moe_inter=int(a["moe_intermediate_size"]),
+        vocab=int(a["vocab_size"]), scale_dtype=torch.bfloat16, kv_bits=kv_bits, kv_value_bits=kv_value_bits,
+        router_mode=abi.REC_ROUTER_SIGMOID, flags=abi.REC_FLAG_SINKS | abi.REC_FLAG_QK_NORM,
+        rms_eps=float(a["rms_norm_eps"]), rope_theta=float(a["rope_theta"]),
+        shared_inter=int(a["shared_expert_intermediate_size"]), dense_layers=dense,
+        dense_inter=int(a["intermediate_size"]) if dense else 0,
+        no_rope_layers=tuple(int(i) for i in a["no_rope_layer_indices"]),
+        sliding_layers=tuple(i for i, t in enumerate(types) if t == "sliding_attention"),
+        sliding_window=int(a["sliding_window"]), embed_bits=embed_bits)
+
+
 def _quantize(w: torch.Tensor, bits: int, scale_dtype: torch.dtype):
     if w.is_cuda:
         from .ops import quantize_affine

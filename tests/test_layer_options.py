@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 
 from rec_b200 import _lib, abi
-from rec_b200.model import FLINT, TINY_FLINT
+from rec_b200.model import FLINT, TINY_FLINT, config_from_reference
 
 
 def test_flint_config_is_the_reference_shape():
@@ -115,3 +115,42 @@ def test_dense_layer_needs_dense_inter(built):
     h = _Host()
     rc, msg = _set(cfg, _layers(cfg, h, kind_override=(0, abi.REC_LAYER_DENSE)), h)
     assert rc == abi.REC_EINVAL and "dense" in msg
+
+
+def _flint_config_json():
+    """A config.json of the reference's shape (ModelArgs fields and the export
+    keys checkpoint.py checks), with FLINT's assumed global layers."""
+    glob = list(FLINT.no_rope_layers)
+    return {"model_type": "flint", "num_hidden_layers": 49, "vocab_size": 150144, "mlp_only_layers": [0, 1],
+            "layer_types": ["full_attention" if i in glob else "sliding_attention" for i in range(49)],
+            "no_rope_layer_indices": glob, "sliding_window": 513, "rope_theta": 10000.0,
+            "quantization": {"group_size": 64, "bits": 4},
+            "mlx_export": {"bits": 4, "routed_expert_bits": 4, "embedding_bits": 8}}
+
+
+def test_config_from_reference_is_the_flint_shape():
+    got = config_from_reference(_flint_config_json(), name=FLINT.name)
+    assert got == FLINT
+    native = config_from_reference(_flint_config_json(), kv_format="native")
+    assert (native.kv_bits, native.kv_value_bits, native.v_bits) == (8, 4, 4)
+
+
+def test_config_from_reference_refuses_what_the_kernels_do_not_take():
+    base = _flint_config_json()
+    for change in ({"tie_word_embeddings": True}, {"kv_group_size": 32},
+                   {"mlx_export": {"bits": 4, "routed_expert_bits": 3, "embedding_bits": 8}},
+                   {"quantization": {"group_size": 32, "bits": 4}},
+                   {"layer_types": ["chunked_attention"] * 49}):
+        with pytest.raises(ValueError):
+            config_from_reference({**base, **change})
+    with pytest.raises(ValueError):
+        config_from_reference(base, kv_format="fp8")
+
+
+def test_config_from_reference_creates_a_session(built):
+    lib = _lib.lib()
+    for fmt in ("bf16", "native"):
+        desc = config_from_reference(_flint_config_json(), kv_format=fmt).desc()
+        ctx = C.c_void_p()
+        assert lib.rec_create(C.byref(desc), C.byref(ctx)) == abi.REC_OK, _lib.last_error()
+        lib.rec_destroy(ctx)
