@@ -128,3 +128,36 @@ def test_checkpoint_extra_tensor_is_refused(tmp_path):
     save_file(t, str(shard))
     with pytest.raises(ValueError, match="not part of the model"):
         load_reference_checkpoint(tmp_path, cfg, device="cpu")
+
+
+@pytest.mark.gpu
+def test_gpu_checkpoint_decodes_the_golden_case(cuda, tmp_path):
+    """The golden Flint case written as a reference checkpoint, loaded onto
+    the device and decoded through the C ABI, reproduces the frozen fixture."""
+    import oracle
+    from oracle.host import HostKV
+    from rec_b200.model import KVCache
+    from rec_b200.session import DecodeSession
+
+    cfg, seed = cases.DECODE_CASES["decode_flint"]
+    want = cases.load("decode_flint")
+    m = cases.host_model(cfg, seed)
+    _write(m, cfg, tmp_path, True)
+    weights = load_reference_checkpoint(tmp_path, cfg, device="cuda")
+    hkv = HostKV(cfg, cases.CAPACITY)
+    cases.fill_kv(hkv, cfg, seed + 1)
+    kv = KVCache.allocate(cfg, cases.CAPACITY)
+    for d, h in zip(kv.layers, hkv.layers):
+        for n in d:
+            d[n].copy_(torch.from_numpy(h[n].view(np.int32) if h[n].dtype == np.uint32 else h[n].view(np.int16))
+                       .to("cuda").view(d[n].dtype))
+    sess = DecodeSession(weights, kv)
+    token, ids = cases.START_TOKEN, []
+    for i in range(cases.STEPS):
+        logits, _ = sess.step(token, cases.CONTEXT + i)
+        lg = _u16(logits.cpu())
+        assert cases.sha(lg) == str(want["logits_sha"][i]), f"step {i}"
+        token = oracle.argmax_bf16(lg)
+        ids.append(token)
+    sess.check_status()
+    assert ids == want["ids"].tolist()
