@@ -278,3 +278,15 @@ def build_decoder(model: ModelWeights, *, optimized: bool = True, eos_tokens=())
     """(engine, resident_sampler) for a model, as kernels.build_decoder."""
     engine = FullModel(model)
     return engine, (ResidentSampler(engine, eos_tokens) if optimized else None)
+
+
+def build_decoder_from_checkpoint(directory, *, kv_format: str = "bf16", optimized: bool = True, eos_tokens=(),
+                                  device="cuda"):
+    """build_decoder for a reference checkpoint directory (config.json +
+    model-*.safetensors, engine/src/rec_mlx/checkpoint.py:5-31): the weights
+    through rec_b200.checkpoint.load_reference_checkpoint (kv_format "bf16"
+    as the production engine, or "native" for MLX's K8/V4 cache)."""
+    from .checkpoint import load_reference_checkpoint
+
+    weights = load_reference_checkpoint(directory, kv_format=kv_format, device=device)
+    return build_decoder(weights, optimized=optimized, eos_tokens=eos_tokens)
