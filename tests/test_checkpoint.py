@@ -161,3 +161,28 @@ def test_gpu_checkpoint_decodes_the_golden_case(cuda, tmp_path):
         ids.append(token)
     sess.check_status()
     assert ids == want["ids"].tolist()
+
+
+def test_checkpoint_config_json_gives_the_model(tmp_path):
+    """Without an explicit ModelConfig the loader reads config.json (the
+    reference's ModelArgs keys, kv_format "native": MLX's quantized cache)
+    and arrives at the golden Flint case's configuration."""
+    from dataclasses import replace
+
+    cfg, seed = cases.DECODE_CASES["decode_flint"]
+    m = cases.host_model(cfg, seed)
+    _write(m, cfg, tmp_path, False)
+    (tmp_path / "config.json").write_text(json.dumps({
+        "model_type": "flint", "hidden_size": cfg.hidden, "num_hidden_layers": cfg.n_layers,
+        "num_attention_heads": cfg.n_q_heads, "num_key_value_heads": cfg.n_kv_heads, "head_dim": cfg.head_dim,
+        "num_experts": cfg.n_experts, "num_experts_per_tok": cfg.top_k, "moe_intermediate_size": cfg.moe_inter,
+        "shared_expert_intermediate_size": cfg.shared_inter, "intermediate_size": cfg.dense_inter,
+        "mlp_only_layers": list(cfg.dense_layers), "no_rope_layer_indices": list(cfg.no_rope_layers),
+        "layer_types": ["sliding_attention" if i in cfg.sliding_layers else "full_attention"
+                        for i in range(cfg.n_layers)],
+        "sliding_window": cfg.sliding_window, "vocab_size": cfg.vocab, "rms_norm_eps": cfg.rms_eps,
+        "rope_theta": cfg.rope_theta, "kv_key_bits": cfg.kv_bits, "kv_value_bits": cfg.kv_bits,
+        "kv_group_size": 64, "tie_word_embeddings": False, "quantization": {"group_size": 64, "bits": 4},
+        "mlx_export": {"bits": 4, "routed_expert_bits": 4, "embedding_bits": cfg.embed_bits}}))
+    w = load_reference_checkpoint(tmp_path, kv_format="native", device="cpu")
+    assert replace(w.cfg, name=cfg.name) == cfg
