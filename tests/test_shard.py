@@ -110,8 +110,11 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_two_rank_exchange_matches_single_rank():
-    world, port = 2, 29511
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_rank_exchange_matches_single_rank(world):
+    """2, 4 and 8 gloo ranks (with 3 super-chunks of context, 4 and 8 ranks
+    include ranks that hold none of the cache, as at 8 GPUs for config 4)."""
+    port = 29511 + world
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
