@@ -485,5 +485,10 @@ REC_API int rec_attn_decode(const void* qkv_dev, int32_t n_q_heads, int32_t n_kv
 REC_API int rec_quantize_affine(const float* w_dev, int64_t n_groups, int32_t bits,
                                 int32_t scale_dtype, void* codes_dev, void* scales_dev,
                                 void* biases_dev, void* stream);
+/* The SiLU table: out_dev bf16[65536], entry i = bf16(bf16(g * bf16(sigmoid(g)))
+ * * 1) for the gate g whose bf16 bits are i — the decode path's gate/up
+ * epilogue with u = 1.  Replaces the engine's `silu` table
+ * (megakernel.py:1110-1112: swiglu over every bf16 gate, up = 1). */
+REC_API int rec_silu_table(void* out_dev, void* stream);
 
 #endif /* REC_B200_H */

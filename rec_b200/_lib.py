@@ -63,6 +63,7 @@ _SIGNATURES = {
                                   C.c_void_p]),
     "rec_quantize_affine": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                                       C.c_void_p, C.c_void_p]),
+    "rec_silu_table": (C.c_int, [C.c_void_p, C.c_void_p]),
     "rec_create": (C.c_int, [C.POINTER(abi.RecModelDesc), C.POINTER(C.c_void_p)]),
     "rec_destroy": (None, [C.c_void_p]),
     "rec_set_weights": (C.c_int, [C.c_void_p, C.POINTER(abi.RecLayerWeights), C.c_int32,

@@ -122,3 +122,19 @@ REC_API int rec_quantize_affine(const float* w_dev, int64_t n_groups, int32_t bi
   REC_CHECK_CUDA(cudaGetLastError());
   return REC_OK;
 }
+
+// The SiLU table: entry i = bf16(bf16(g * bf16(sigmoid(g))) * 1) for the gate
+// g whose bf16 bits are i, the decode path's gate/up epilogue with u = 1.
+__global__ void k_silu_table(uint16_t* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // grid covers exactly 65,536
+  const float gg = bf(uint16_t(i));
+  out[i] = to_bf(__fmul_rn(rbf(__fmul_rn(gg, rbf(rsigmoid(gg)))), 1.0f));
+}
+
+REC_API int rec_silu_table(void* out_dev, void* stream) {
+  REC_CHECK_ARG(out_dev, "rec_silu_table: null pointer");
+  REC_CHECK_ARG((reinterpret_cast<uintptr_t>(out_dev) & 1u) == 0, "rec_silu_table: output must be 2-byte aligned");
+  k_silu_table<<<65536 / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint16_t*>(out_dev));
+  REC_CHECK_CUDA(cudaGetLastError());
+  return REC_OK;
+}

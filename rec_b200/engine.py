@@ -16,14 +16,98 @@ hold 1..8 tokens.
 from __future__ import annotations
 
 import time
+from dataclasses import dataclass, fields
 
 import torch
 
+from . import abi
 from ._lib import RecError
-from .model import KVCache, ModelWeights
+from .model import KVCache, ModelConfig, ModelWeights, QTensor
 from .session import DecodeSession
 
 WIDTH = 8  # resident packet size (sampling.py:8)
+GROUP_LAYERS = 4  # layers per weight group (the reference packs one bank per four layers)
+
+
+@dataclass(frozen=True)
+class DeviceProfile:
+    """The engine's device (reference kernels/device.py:4-13): `chip` is the
+    CUDA device name, `architecture` its compute capability; `workers` the
+    SM count the persistent schedule spreads over."""
+
+    chip: str
+    architecture: str
+    workers: int
+    prefill_chunk_size: int
+
+
+def layer_metadata(cfg: ModelConfig) -> list[list[int]]:
+    """The engine's layer table, one row of 64 per layer and a last row for
+    the globals, with the reference's column meaning
+    (kernels/megakernel.py:1008-1088).  Column 0 is the layer's group of four
+    (the reference's weight bank), 1 is 1 when the layer attends over the
+    whole context (not a sliding-window layer), 2 is 1 when it routes
+    experts.  Each quantized matrix takes five columns — the byte offsets of
+    its codes, scales and biases within the bank, then its rows (per expert)
+    and columns — at 10 (q), 15 (k), 20 (v), 25 (o), 30 (gate), 35 (up), 40
+    (down) and, for the shared expert, 45 / 50 / 55; the last row holds the
+    embedding at 10 and lm_head at 30.  Here every weight is its own device
+    tensor rather than a slice of a packed bank, so the offset columns (3-9,
+    the first three of each matrix, 60) hold 0."""
+    H, d = cfg.hidden, cfg.head_dim
+    rows = []
+
+    def linear(row, base, n, k):
+        row[base + 3:base + 5] = [n, k]
+
+    for i in range(cfg.n_layers):
+        kind = cfg.layer_kind(i)
+        row = [0] * 64
+        moe = not kind & abi.REC_LAYER_DENSE
+        row[0:3] = [i // GROUP_LAYERS, int(not kind & abi.REC_LAYER_SLIDING), int(moe)]
+        linear(row, 10, cfg.n_q_heads * d, H)
+        linear(row, 15, cfg.n_kv_heads * d, H)
+        linear(row, 20, cfg.n_kv_heads * d, H)
+        linear(row, 25, H, cfg.n_q_heads * d)
+        inter = cfg.moe_inter if moe else cfg.dense_inter
+        linear(row, 30, inter, H)
+        linear(row, 35, inter, H)
+        linear(row, 40, H, inter)
+        if moe and cfg.shared_inter:
+            linear(row, 45, cfg.shared_inter, H)
+            linear(row, 50, cfg.shared_inter, H)
+            linear(row, 55, H, cfg.shared_inter)
+        rows.append(row)
+    last = [0] * 64
+    last[0] = (cfg.n_layers - 1) // GROUP_LAYERS
+    linear(last, 10, cfg.vocab, H)
+    linear(last, 30, cfg.vocab, H)
+    rows.append(last)
+    return rows
+
+
+def weight_banks(weights: ModelWeights) -> list[tuple]:
+    """The device tensors of each group of four layers, in the layer
+    fields' order (a quantized matrix as codes, scales, biases), the last
+    group followed by the embedding, the final norm and lm_head — the
+    reference's thirteen weight banks (kernels/megakernel.py:1011-1108),
+    held as separate tensors instead of one packed buffer per group."""
+    def flat(obj):
+        out = []
+        for f in fields(obj):
+            v = getattr(obj, f.name)
+            if isinstance(v, QTensor):
+                out += [v.w, v.s, v.b]
+            elif isinstance(v, torch.Tensor):
+                out.append(v)
+        return out
+
+    banks = []
+    for first in range(0, len(weights.layers), GROUP_LAYERS):
+        banks.append([t for L in weights.layers[first:first + GROUP_LAYERS] for t in flat(L)])
+    banks[-1] += [weights.embed.w, weights.embed.s, weights.embed.b, weights.final_norm,
+                  weights.lm_head.w, weights.lm_head.s, weights.lm_head.b]
+    return [tuple(b) for b in banks]
 
 
 class KVStorage:
@@ -92,6 +176,23 @@ class KVStorage:
     def nbytes(self) -> int:
         return self.cache.nbytes() if self.cache is not None else 0
 
+    @property
+    def banks(self) -> list[tuple]:
+        """Each layer's cache tensors (codes, scales, biases of K and V), the
+        counterpart of the reference's KV banks (cache.py:68)."""
+        return [tuple(layer.values()) for layer in self.cache.layers]
+
+    @property
+    def metadata(self) -> list[list[int]]:
+        """The engine's layer table with columns 61-62 set as the
+        reference's storage sets them (cache.py:53-66): the layer's element
+        offset in its bank (0: each layer is its own tensor) and its rows (the
+        cache's head stride; a sliding layer reads only its window of them)."""
+        rows = layer_metadata(self.weights.cfg)
+        for row in rows[:-1]:
+            row[61:63] = [0, self.cache.capacity]
+        return rows
+
 
 class FullModel:
     """B200 decode engine for one model (one GPU)."""
@@ -102,9 +203,20 @@ class FullModel:
         self.cfg = weights.cfg
         self.device = torch.device(device)
         self.prefill_chunk_size = prefill_chunk_size
-        self.device_profile = torch.cuda.get_device_name(self.device) if torch.cuda.is_available() else None
-        self.workers = torch.cuda.get_device_properties(self.device).multi_processor_count
+        props = torch.cuda.get_device_properties(self.device)
+        self.workers = props.multi_processor_count
+        self.device_profile = DeviceProfile(props.name, f"sm_{props.major}{props.minor}", self.workers,
+                                            prefill_chunk_size)
         self.schedule = {"workers": self.workers, "graph": "per-token CUDA graph, programmatic dependent launch"}
+        self.metadata = layer_metadata(self.cfg)
+        self.banks = weight_banks(weights)
+        # bf16[65536]: the SiLU of every bf16 gate (megakernel.py:1110-1112)
+        self.silu = torch.empty(65536, dtype=torch.bfloat16, device=self.device)
+        from . import _lib
+
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().rec_silu_table(self.silu.data_ptr(),
+                                                 torch.cuda.current_stream(self.device).cuda_stream))
 
     # -- state ---------------------------------------------------------------
     def prefill_state(self, capacity, *, limit=None, storage=None):
@@ -112,7 +224,7 @@ class FullModel:
             storage = KVStorage(self.weights, capacity, self.device, limit=limit)
         else:
             storage.grow(capacity)
-        return {"usable": True, "kv": storage, "metadata": None, "position": 0, "initial": 0,
+        return {"usable": True, "kv": storage, "metadata": storage.metadata, "position": 0, "initial": 0,
                 "capacity": storage.capacity, "limit": capacity if limit is None else limit,
                 "growth_count": 0, "growth_seconds": 0.0}
 
@@ -126,6 +238,7 @@ class FullModel:
             started = time.perf_counter()
             state["kv"].grow(required)
             state["capacity"] = state["kv"].capacity
+            state["metadata"] = state["kv"].metadata
             state["growth_count"] += 1
             state["growth_seconds"] += time.perf_counter() - started
 

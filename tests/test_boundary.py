@@ -5,6 +5,10 @@
   report[id] - logsumexp(report), report = penalised, masked logits / T;
 - FullModel.forward(state, token, layer_count) at partial depth
   (megakernel.py:824,861,1224-1233,1272);
+- the engine attributes the reference's callers read: `metadata` (the
+  layer table, megakernel.py:1008-1088, read by engine.py:326 and
+  kernels/activation_optimization.py:20-25), `banks`, `silu`
+  (megakernel.py:1110-1112) and `device_profile.chip` (engine.py:244);
 - the failure contract (megakernel.py:137-159,1264-1268,1326-1331;
   sampling.py:77-78): a bounded device wait that runs out gives
   RuntimeError("GPU synchronization failed ...") and state["usable"] = False,
@@ -267,3 +271,57 @@ def test_gpu_limits_and_packet_size(cuda):
     state = engine.prefill_state(256, limit=4)
     with pytest.raises(ValueError, match="Decode context limit exhausted"):
         sampler.block(state, 1, 5, 0, temperature=0)
+
+
+def test_layer_metadata_is_the_reference_table():
+    """The Flint shape's table: 50 rows; column 1 marks the global layers
+    (the rows engine.py:326 leaves out of its sliding bytes), column 2 the
+    47 routed layers, whose gate / up / shared gate / shared up shapes are
+    the tuple the reference's activation guard asserts
+    (kernels/activation_optimization.py:20-25)."""
+    from rec_b200.engine import layer_metadata
+    from rec_b200.model import FLINT
+
+    rows = layer_metadata(FLINT)
+    assert len(rows) == 50 and all(len(r) == 64 for r in rows)
+    assert [i for i, r in enumerate(rows[:49]) if r[1]] == sorted(FLINT.no_rope_layers)
+    routed = [r for r in rows[:49] if r[2]]
+    assert len(routed) == 47 and not rows[0][2] and not rows[1][2]
+    assert all(tuple(r[i] for i in (33, 34, 38, 39, 48, 49, 53, 54))
+               == (512, 2048, 512, 2048, 1024, 2048, 1024, 2048) for r in routed)
+    assert tuple(rows[0][i] for i in (33, 34, 43, 44)) == (6144, 2048, 2048, 6144)
+    assert tuple(rows[5][i] for i in (13, 14, 18, 19, 28, 29)) == (4096, 2048, 512, 2048, 2048, 4096)
+    assert [r[0] for r in rows[:49]] == [i // 4 for i in range(49)] and rows[49][0] == 12
+    assert tuple(rows[49][i] for i in (13, 14, 33, 34)) == (150144, 2048, 150144, 2048)
+
+
+@pytest.mark.gpu
+def test_gpu_engine_attributes(cuda):
+    """engine.silu is the SiLU of every bf16 gate (bit-exact against the
+    oracle's SwiGLU with up = 1; NaN gates give NaN); engine.banks holds
+    every weight tensor once, in groups of four layers; the state's table
+    carries the cache rows in columns 61-62; device_profile.chip names the
+    device, so the reference's M4-Max test is false."""
+    from rec_b200.engine import layer_metadata
+
+    w, engine, _ = _tiny_engine(seed=3)
+    silu = engine.silu.view(torch.int16).cpu().numpy().view(np.uint16)
+    want = np.array([oracle.swiglu(g, 0x3F80) for g in range(65536)], np.uint16)
+    got_f, want_f = oracle.bf16_to_f32(silu), oracle.bf16_to_f32(want)
+    both_nan = np.isnan(got_f) & np.isnan(want_f)
+    assert np.array_equal(silu[~both_nan], want[~both_nan])
+    assert np.array_equal(np.isnan(got_f), np.isnan(want_f))
+
+    assert len(engine.banks) == -(-len(w.layers) // 4)
+    ptrs = [t.data_ptr() for bank in engine.banks for t in bank]
+    assert len(ptrs) == len(set(ptrs))
+    assert {w.embed.w.data_ptr(), w.lm_head.w.data_ptr(), w.final_norm.data_ptr(),
+            w.layers[0].q.w.data_ptr(), w.layers[-1].down.b.data_ptr()} <= set(ptrs)
+    assert engine.metadata == layer_metadata(w.cfg)
+
+    state = engine.prefill_state(256)
+    cap = state["kv"].cache.capacity
+    assert all(r[61:63] == [0, cap] for r in state["metadata"][:-1])
+    assert len(state["kv"].banks) == w.cfg.n_layers
+    assert engine.device_profile.chip == torch.cuda.get_device_name()
+    assert engine.device_profile.architecture.startswith("sm_") and engine.device_profile.chip != "M4 Max"
