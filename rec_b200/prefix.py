@@ -5,10 +5,10 @@ the logits after the last of them, and checkpoints taken before each prefill
 chunk.  `select_prefix` keeps the longest reusable part for a new prompt:
 the whole cache when the new prompt extends it, else the latest checkpoint
 at or below the common prefix (prefix.py:83-118).  The reference's
-checkpoints also copy the sliding-window rings; the decoder here has no
-sliding layers (every layer attends to the full cache, whose rows past a
-position are simply rewritten), so a checkpoint is a position and its
-logits.
+checkpoints also copy the sliding-window rings; here a sliding-window layer
+keeps every row like the others and reads only its window, so no row is
+ever overwritten by a later position, and a checkpoint is a position and
+its logits.
 """
 from __future__ import annotations
 
@@ -16,6 +16,17 @@ import logging
 from dataclasses import dataclass, field
 
 from .errors import PrefillCancelled  # noqa: F401  (re-exported, as the reference's module does)
+
+
+@dataclass
+class LayerCache:
+    """One layer's cache tensors (codes, scales and biases of K and V)."""
+
+    tensors: dict
+
+    @property
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self.tensors.values())
 
 
 @dataclass
@@ -49,6 +60,13 @@ class PromptCache:
             return
         self.checkpoints = self.checkpoints[-1:]
         self.checkpoints.append(Checkpoint(len(self.tokens), self.logits))
+
+    @property
+    def layers(self) -> list["LayerCache"]:
+        """One view per layer of the cache the prompt's K/V sit in, each with
+        its `nbytes` (the reference's per-layer caches, prefix.py:22-27,
+        whose sliding layers' bytes engine.py:323-329 sums)."""
+        return [LayerCache(tensors) for tensors in self.storage.cache.layers]
 
     @property
     def checkpoint_bytes(self) -> int:

@@ -323,5 +323,8 @@ def test_gpu_engine_attributes(cuda):
     cap = state["kv"].cache.capacity
     assert all(r[61:63] == [0, cap] for r in state["metadata"][:-1])
     assert len(state["kv"].banks) == w.cfg.n_layers
+    from rec_b200.prefix import PromptCache
+
+    assert sum(L.nbytes for L in PromptCache([], state["kv"]).layers) == state["kv"].nbytes
     assert engine.device_profile.chip == torch.cuda.get_device_name()
     assert engine.device_profile.architecture.startswith("sm_") and engine.device_profile.chip != "M4 Max"

@@ -54,6 +54,24 @@ def test_checkpoint_keeps_two():
     assert len(c.tokens) == 12 and f.storage is c.storage
 
 
+
+def test_layers_sum_sliding_bytes_as_the_reference_engine():
+    """engine.py:323-329 sums `cache.nbytes` over the prompt cache's layers
+    whose metadata row has column 1 clear (the sliding-window layers)."""
+    from types import SimpleNamespace
+
+    from rec_b200.engine import layer_metadata
+    from rec_b200.model import TINY_FLINT
+
+    layers = [{"k_codes": torch.zeros(4, 16 * (i + 1), dtype=torch.int32),
+               "k_scales": torch.zeros(4, 2, dtype=torch.bfloat16)} for i in range(TINY_FLINT.n_layers)]
+    c = PromptCache([1, 2], storage=SimpleNamespace(cache=SimpleNamespace(layers=layers)))
+    sliding = sum(cache.nbytes for row, cache in zip(layer_metadata(TINY_FLINT)[:3], c.layers, strict=True)
+                  if not row[1])
+    assert [L.nbytes for L in c.layers] == [4 * 16 * 4 + 16, 4 * 32 * 4 + 16, 4 * 48 * 4 + 16]
+    assert sliding == c.layers[0].nbytes + c.layers[2].nbytes  # TINY_FLINT's sliding layers are 0 and 2
+
+
 @pytest.mark.gpu
 def test_gpu_prefill_with_prefix_bitexact(cuda):
     from rec_b200.engine import build_decoder
