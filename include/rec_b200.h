@@ -423,6 +423,18 @@ REC_API size_t rec_prefill_workspace_bytes(const RecCtx* ctx, int32_t t);
  * kernels/m4_max_prefill.py:49-144). */
 REC_API int rec_prefill_chunk(RecCtx* ctx, const int32_t* tokens_dev, int32_t position, int32_t t, void* logits_dev,
                               void* workspace, size_t workspace_bytes, void* stream);
+/* rec_prefill_chunk over layers [layer_begin, layer_end) only, so that a
+ * caller can stop between layers: the range starting at 0 embeds tokens_dev
+ * (which later ranges may pass as NULL), the chunk's hidden states stay in
+ * the workspace between ranges (the same workspace, the same t and
+ * position), and the range ending at the last layer writes the logits.
+ * Layer ranges that cover 0 .. n_layers in order give the same bits as one
+ * rec_prefill_chunk.  Replaces the per-layer stop poll of the reference's
+ * prefill (quantized.py:129-133 with interrupt_between_layers;
+ * model.py:309-314). */
+REC_API int rec_prefill_chunk_layers(RecCtx* ctx, const int32_t* tokens_dev, int32_t position, int32_t t,
+                                     int32_t layer_begin, int32_t layer_end, void* logits_dev, void* workspace,
+                                     size_t workspace_bytes, void* stream);
 /* The causal attention step of rec_prefill_chunk alone: q_dev bf16 [t,
  * n_q_heads, 128] (RoPE'd, not scaled) at positions [position, position + t)
  * attends over cache rows 0 .. its own position (the chunk's rows already

@@ -32,6 +32,8 @@ _SIGNATURES = {
     "rec_prefill_workspace_bytes": (C.c_size_t, [C.c_void_p, C.c_int32]),
     "rec_prefill_chunk": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_size_t,
                                     C.c_void_p]),
+    "rec_prefill_chunk_layers": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                           C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "rec_set_kv_rows": (C.c_int, [C.c_void_p, C.c_int32]),
     "rec_decode_layers": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
                                     C.c_void_p]),

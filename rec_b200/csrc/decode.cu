@@ -1200,12 +1200,15 @@ REC_API size_t rec_prefill_workspace_bytes(const RecCtx* c, int32_t t) {
   return prefill_layout(c->d, t).total;
 }
 
-REC_API int rec_prefill_chunk(RecCtx* c, const int32_t* tokens_dev, int32_t position, int32_t t, void* logits_dev,
-                              void* workspace, size_t workspace_bytes, void* stream) {
+REC_API int rec_prefill_chunk_layers(RecCtx* c, const int32_t* tokens_dev, int32_t position, int32_t t,
+                                     int32_t layer_begin, int32_t layer_end, void* logits_dev, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
   int rc = check_ready(c);
   if (rc) return rc;
   const RecModelDesc& d = c->d;
-  REC_CHECK_ARG(tokens_dev && workspace, "rec_prefill_chunk: null pointer");
+  REC_CHECK_ARG(workspace && (tokens_dev || layer_begin > 0), "rec_prefill_chunk: null pointer");
+  REC_CHECK_ARG(layer_begin >= 0 && layer_begin < layer_end && layer_end <= d.n_layers,
+                "rec_prefill_chunk: layers [%d, %d) outside [0, %d)", layer_begin, layer_end, d.n_layers);
   REC_CHECK_ARG(c->world == 1, "rec_prefill_chunk: an unsharded session only");
   REC_CHECK_ARG(!c->flint, "rec_prefill_chunk: layer options (shared expert, dense / NoPE / sliding layers) are "
                 "prefilled by decode steps");
@@ -1234,9 +1237,11 @@ REC_API int rec_prefill_chunk(RecCtx* c, const int32_t* tokens_dev, int32_t posi
   const int H = d.hidden, Q = d.n_q_heads * 128, KV = d.n_kv_heads * 128;
   const QMatDev emb = {(const uint32_t*)c->g.embed.w, (const uint16_t*)c->g.embed.scales,
                        (const uint16_t*)c->g.embed.biases};
-  REC_CHECK_CUDA(pf_embed(emb, sd == REC_SCALE_BF16 ? 1 : 0, tokens_dev, t, H, d.vocab, h, status, st));
+  // the chunk's hidden states stay in the workspace between layer ranges
+  if (layer_begin == 0)
+    REC_CHECK_CUDA(pf_embed(emb, sd == REC_SCALE_BF16 ? 1 : 0, tokens_dev, t, H, d.vocab, h, status, st));
   const bool qk = (d.flags & REC_FLAG_QK_NORM) != 0, sinks = (d.flags & REC_FLAG_SINKS) != 0;
-  for (int l = 0; l < d.n_layers; ++l) {
+  for (int l = layer_begin; l < layer_end; ++l) {
     const RecLayerWeights& W = c->layers[l];
     REC_CHECK_CUDA(pf_rmsnorm(h, (const uint16_t*)W.input_norm, t, d.rms_eps, xn, st));
     if ((rc = rec_prefill_gemm(&W.q, sd, Q, H, xn, t, q, status, st))) return rc;
@@ -1258,10 +1263,17 @@ REC_API int rec_prefill_chunk(RecCtx* c, const int32_t* tokens_dev, int32_t posi
                               h, w + L.moe, L.moe_bytes, status, st)))
       return rc;
   }
-  if (logits_dev)
+  if (logits_dev && layer_end == d.n_layers)
     return rec_gemv_int4(&c->g.lm_head, sd, d.vocab, H, h + size_t(t - 1) * H, c->g.final_norm, d.rms_eps, logits_dev,
                          st);
   return REC_OK;
+}
+
+REC_API int rec_prefill_chunk(RecCtx* c, const int32_t* tokens_dev, int32_t position, int32_t t, void* logits_dev,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  if (!c) return check_ready(c);
+  return rec_prefill_chunk_layers(c, tokens_dev, position, t, 0, c->d.n_layers, logits_dev, workspace,
+                                  workspace_bytes, stream);
 }
 
 REC_API int rec_prefill_attention(const void* q_dev, int32_t n_q_heads, int32_t n_kv_heads, const RecKVLayer* kv,

@@ -307,7 +307,11 @@ class QATSession:
         `prompt_cache` of an earlier session: its K/V rows for the common
         prompt prefix are reused in place (prefix.py:83-118), and only the
         rest of the prompt runs.  `should_stop` is polled before each chunk
-        (PrefillCancelled)."""
+        (PrefillCancelled); with interrupt_between_layers also before each
+        layer of a chunk, each layer finished on the device before the next
+        poll (model.py:309-314) — through rec_prefill_chunk_layers, with the
+        same bits as the whole chunk — and on the decode-step path before
+        each token."""
         from .errors import PrefillCancelled
         from .prefix import PromptCache, select_prefix
 
@@ -332,9 +336,20 @@ class QATSession:
             # with Flint layer options (shared expert, dense / NoPE / sliding
             # layers) is prefilled by its decode step
             if self.prefill_mode == "chunked" and not self.engine.cfg.has_layer_options:
-                out = self.engine._guard(state, lambda: sess.prefill_chunk(part, begin))
+                if interrupt_between_layers:
+                    n = self.engine.cfg.n_layers
+                    for layer in range(n):
+                        if layer and should_stop():
+                            raise PrefillCancelled()
+                        out = self.engine._guard(state, lambda: sess.prefill_chunk(
+                            part, begin, want_logits=layer == n - 1, layers=(layer, layer + 1)))
+                        self.engine._guard(state, sess.check_status)
+                else:
+                    out = self.engine._guard(state, lambda: sess.prefill_chunk(part, begin))
             else:
                 for i, t in enumerate(part):
+                    if i and interrupt_between_layers and should_stop():
+                        raise PrefillCancelled()
                     out, _ = sess.step(t, begin + i, want_logits=i == len(part) - 1)
             self.engine._guard(state, sess.check_status)
             logits = out.clone()

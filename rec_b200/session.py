@@ -127,22 +127,33 @@ class DecodeSession:
             self.step(int(t), start + i, want_logits=False)
         self.check_status()
 
-    def prefill_chunk(self, tokens, start: int, want_logits: bool = True):
+    def prefill_chunk(self, tokens, start: int, want_logits: bool = True, layers: tuple[int, int] | None = None):
         """One prompt chunk at positions start.. through rec_prefill_chunk
         (tensor-core projections and experts, causal attention over the
         quantized cache); returns the last token's logits (bf16 [V]) or None.
-        Results are independent of how a prompt is cut into chunks."""
+        Results are independent of how a prompt is cut into chunks.
+        `layers` = (begin, end) runs only those layers
+        (rec_prefill_chunk_layers): the ranges of one chunk are called in
+        order with the same tokens and start, and the logits come with the
+        range that ends at the last layer."""
         t = len(tokens)
         dev = self.workspace.device
         nbytes = int(lib().rec_prefill_workspace_bytes(self.ctx, t))
         ws = getattr(self, "_pf_ws", None)
         if ws is None or ws.numel() < nbytes + 256:
+            if layers is not None and layers[0] > 0:
+                raise ValueError("a layer range after the first needs the workspace of its chunk")
             ws = self._pf_ws = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
         base = (ws.data_ptr() + 255) // 256 * 256
         tok = torch.tensor([int(x) for x in tokens], dtype=torch.int32, device=dev)
-        check(lib().rec_prefill_chunk(self.ctx, C.c_void_p(tok.data_ptr()), int(start), t,
-                                      C.c_void_p(self.logits.data_ptr()) if want_logits else None, C.c_void_p(base),
-                                      nbytes, self._stream()), "rec_prefill_chunk")
+        out = C.c_void_p(self.logits.data_ptr()) if want_logits else None
+        if layers is None:
+            check(lib().rec_prefill_chunk(self.ctx, C.c_void_p(tok.data_ptr()), int(start), t, out, C.c_void_p(base),
+                                          nbytes, self._stream()), "rec_prefill_chunk")
+        else:
+            check(lib().rec_prefill_chunk_layers(self.ctx, C.c_void_p(tok.data_ptr()), int(start), t, int(layers[0]),
+                                                 int(layers[1]), out, C.c_void_p(base), nbytes, self._stream()),
+                  "rec_prefill_chunk_layers")
         self._pf_tokens = tok  # alive until the stream has read it
         return self.logits if want_logits else None
 

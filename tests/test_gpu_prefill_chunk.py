@@ -121,6 +121,32 @@ def test_chunked_prefill_against_decode_path(tiny, n_tokens):
     assert torch.isfinite(nxt.float()).all()
 
 
+def test_prefill_interrupt_between_layers(tiny):
+    """interrupt_between_layers (quantized.py:129-133, model.py:309-314): the
+    chunks run layer by layer through rec_prefill_chunk_layers give the same
+    bits as whole chunks; a stop requested between two layers of a chunk
+    raises PrefillCancelled, and a later prefill is unaffected."""
+    from rec_b200.errors import PrefillCancelled
+
+    w, engine = tiny
+    tokens = np.random.default_rng(5).integers(0, w.cfg.vocab, 300).tolist()
+    _, whole = _prefill(engine, tokens, "chunked", 256)
+    s = engine.make_session(max_new_tokens=16)
+    by_layer = s.prefill(tokens, interrupt_between_layers=True)
+    assert torch.equal(by_layer.view(torch.int16), whole.view(torch.int16))
+    polls = []
+
+    def stop():  # poll 1: before chunk 0; poll 2: between its layers 0 and 1
+        polls.append(1)
+        return len(polls) == 2
+
+    with pytest.raises(PrefillCancelled):
+        engine.make_session(max_new_tokens=16).prefill(tokens, should_stop=stop, interrupt_between_layers=True)
+    assert len(polls) == 2
+    _, again = _prefill(engine, tokens, "chunked", 256)
+    assert torch.equal(again.view(torch.int16), whole.view(torch.int16))
+
+
 def test_chunked_prefill_without_attention_is_close(cuda):
     """One layer with the O projection zeroed (attention cannot reach the
     residual): the chunk's hidden state is within the per-operation bound of
