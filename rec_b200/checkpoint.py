@@ -46,10 +46,14 @@ def _load_tensors(directory: Path) -> dict:
 def load_reference_checkpoint(directory, cfg: ModelConfig | None = None, *, kv_format: str = "bf16",
                               device="cuda") -> ModelWeights:
     """ModelWeights of the checkpoint in `directory` on `device`.  cfg
-    defaults to config_from_reference(config.json, kv_format=...)."""
+    defaults to config_from_reference(config.json, kv_format=...); the
+    model's end ids are config.json's `eos_token_id` (an id or a list, as
+    quantized.py:77 keeps them)."""
     directory = Path(directory)
+    config_path = directory / "config.json"
+    config = json.loads(config_path.read_text()) if cfg is None or config_path.exists() else {}
     if cfg is None:
-        cfg = config_from_reference(json.loads((directory / "config.json").read_text()), kv_format=kv_format)
+        cfg = config_from_reference(config, kv_format=kv_format)
     t = _load_tensors(directory)
     dev = torch.device(device)
     used = set()
@@ -118,4 +122,6 @@ def load_reference_checkpoint(directory, cfg: ModelConfig | None = None, *, kv_f
     extra = sorted(set(t) - used)
     if extra:  # strict, as the reference loads (quantized.py:42)
         raise ValueError(f"{len(extra)} checkpoint tensors are not part of the model, e.g. {extra[0]}")
-    return ModelWeights(cfg, layers, embed, final_norm, lm_head, expert_range=(0, cfg.n_experts))
+    eos = config.get("eos_token_id", ())
+    eos = (eos,) if isinstance(eos, int) else tuple(int(e) for e in eos or ())
+    return ModelWeights(cfg, layers, embed, final_norm, lm_head, expert_range=(0, cfg.n_experts), eos_tokens=eos)

@@ -290,7 +290,7 @@ class QATSession:
     through the decode step token by token instead (the cache then holds
     exactly what decoding would have written)."""
 
-    context_limit = 262144
+    context_limit = ModelWeights.context_limit
 
     def __init__(self, engine: FullModel, max_new_tokens: int, prefill_mode: str = "chunked"):
         if prefill_mode not in ("chunked", "decode"):
@@ -317,7 +317,7 @@ class QATSession:
 
         tokens = [int(t) for t in tokens]
         limit = len(tokens) + self.maximum
-        if limit > self.context_limit:
+        if limit > self.engine.model.context_limit:
             raise ValueError("prompt plus output allowance exceeds the context limit")
         prefix, self.common_prefix_tokens = select_prefix(prefix, tokens)
         self.cached_tokens = 0 if prefix is None else len(prefix.tokens)
@@ -369,11 +369,13 @@ class QATSession:
 
 class ResidentSampler:
     """Packets of up to 8 tokens decoded with the next token fed back on the
-    device (reference sampling.py:62-169, resident_block.py:12-88)."""
+    device (reference sampling.py:62-169, resident_block.py:12-88).  The
+    packet stops after one of `eos_tokens`, by default the model's own end
+    ids (engine.model.eos_tokens, as sampling.py:22,99-105 reads them)."""
 
     def __init__(self, engine: FullModel, eos_tokens=()):
         self.engine = engine
-        self.eos_tokens = list(eos_tokens)
+        self.eos_tokens = list(eos_tokens) if eos_tokens else list(getattr(engine.model, "eos_tokens", ()))
 
     def block(self, state, token, count, seed, *, temperature=1.0, top_p=1.0, top_k=0, presence_penalty=0.0,
               grammar=None, logprobs=None):

@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import ctypes as C
 from dataclasses import dataclass, field, replace
+from typing import ClassVar
 
 import torch
 
@@ -268,6 +269,8 @@ class ModelWeights:
     lm_head: QTensor
     expert_range: tuple[int, int] = (0, 0)  # experts held (expert parallelism)
     _keep: list = field(default_factory=list)
+    eos_tokens: tuple = ()  # the model's end ids (config.json eos_token_id; quantized.py:77)
+    context_limit: ClassVar[int] = 262144  # positions a session may reach (quantized.py:17)
 
     def rec_layers(self):
         arr = (abi.RecLayerWeights * len(self.layers))(*[L.rec() for L in self.layers])

@@ -65,7 +65,7 @@ def _write(m, cfg, directory, byte_codes: bool):
     half = len(names) // 2  # two shards
     save_file({n: t[n].contiguous() for n in names[:half]}, str(directory / "model-00001-of-00002.safetensors"))
     save_file({n: t[n].contiguous() for n in names[half:]}, str(directory / "model-00002-of-00002.safetensors"))
-    (directory / "config.json").write_text(json.dumps({"model_type": "flint"}))
+    (directory / "config.json").write_text(json.dumps({"model_type": "flint", "eos_token_id": 3}))
 
 
 def _u16(x):
@@ -99,6 +99,7 @@ def test_checkpoint_round_trip(tmp_path, byte_codes):
     same_q(w.embed, m.embed)
     same_q(w.lm_head, m.lm_head)
     assert np.array_equal(_u16(w.final_norm), m.final_norm)
+    assert w.eos_tokens == (3,)  # config.json's eos_token_id, an id or a list (quantized.py:77)
 
 
 def test_checkpoint_missing_tensor_is_named(tmp_path):
@@ -183,6 +184,8 @@ def test_checkpoint_config_json_gives_the_model(tmp_path):
         "sliding_window": cfg.sliding_window, "vocab_size": cfg.vocab, "rms_norm_eps": cfg.rms_eps,
         "rope_theta": cfg.rope_theta, "kv_key_bits": cfg.kv_bits, "kv_value_bits": cfg.kv_bits,
         "kv_group_size": 64, "tie_word_embeddings": False, "quantization": {"group_size": 64, "bits": 4},
-        "mlx_export": {"bits": 4, "routed_expert_bits": 4, "embedding_bits": cfg.embed_bits}}))
+        "mlx_export": {"bits": 4, "routed_expert_bits": 4, "embedding_bits": cfg.embed_bits},
+        "eos_token_id": [5, 7]}))
     w = load_reference_checkpoint(tmp_path, kv_format="native", device="cpu")
     assert replace(w.cfg, name=cfg.name) == cfg
+    assert w.eos_tokens == (5, 7) and w.context_limit == 262144
