@@ -187,11 +187,15 @@ class KVStorage:
         """The engine's layer table with columns 61-62 set as the
         reference's storage sets them (cache.py:53-66): the layer's element
         offset in its bank (0: each layer is its own tensor) and its rows (the
-        cache's head stride; a sliding layer reads only its window of them)."""
-        rows = layer_metadata(self.weights.cfg)
-        for row in rows[:-1]:
-            row[61:63] = [0, self.cache.capacity]
-        return rows
+        cache's head stride; a sliding layer reads only its window of them).
+        The same object until the cache moves into a larger reservation."""
+        cached = getattr(self, "_metadata", None)
+        if cached is None or cached[0] is not self.cache:
+            rows = layer_metadata(self.weights.cfg)
+            for row in rows[:-1]:
+                row[61:63] = [0, self.cache.capacity]
+            cached = self._metadata = (self.cache, rows)
+        return cached[1]
 
 
 class FullModel:

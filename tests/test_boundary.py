@@ -295,6 +295,40 @@ def test_layer_metadata_is_the_reference_table():
     assert tuple(rows[49][i] for i in (13, 14, 33, 34)) == (150144, 2048, 150144, 2048)
 
 
+def test_state_growth_and_limit_on_the_host():
+    """prefill_state / ensure_capacity over a given storage, the contract of
+    the reference's shared-KV test (engine/tests/test_shared_kv.py:64-80):
+    the state keeps the storage and its table, a packet past the capacity
+    grows that storage once and counts it, the limit gives ValueError and an
+    unusable state raises "invalidated"."""
+    from rec_b200.engine import FullModel
+
+    block = 65536
+
+    class Storage:
+        def __init__(self):
+            self.capacity, self.metadata, self.grown = 17, [[0] * 64], []
+
+        def grow(self, count):
+            self.grown.append(count)
+            self.capacity = max(self.capacity, -(-count // block) * block)
+
+    storage = Storage()
+    state = FullModel.prefill_state(None, 17, limit=block + 8, storage=storage)
+    state["position"] = block - 4
+    FullModel.ensure_capacity(None, state, 8)
+    assert state["kv"] is storage and state["metadata"] is storage.metadata
+    assert state["capacity"] == 2 * block and state["growth_count"] == 1 and state["growth_seconds"] >= 0
+    FullModel.ensure_capacity(None, state, 8)  # within the capacity: no growth
+    assert state["growth_count"] == 1
+    state["position"] = block + 7
+    with pytest.raises(ValueError, match="Decode context limit exhausted"):
+        FullModel.ensure_capacity(None, state, 2)
+    state["usable"] = False
+    with pytest.raises(RuntimeError, match="invalidated"):
+        FullModel.ensure_capacity(None, state, 1)
+
+
 @pytest.mark.gpu
 def test_gpu_engine_attributes(cuda):
     """engine.silu is the SiLU of every bf16 gate (bit-exact against the
@@ -322,6 +356,7 @@ def test_gpu_engine_attributes(cuda):
     state = engine.prefill_state(256)
     cap = state["kv"].cache.capacity
     assert all(r[61:63] == [0, cap] for r in state["metadata"][:-1])
+    assert state["metadata"] is state["kv"].metadata
     assert len(state["kv"].banks) == w.cfg.n_layers
     from rec_b200.prefix import PromptCache
 
