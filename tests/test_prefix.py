@@ -107,3 +107,70 @@ def test_gpu_prefill_with_prefix_bitexact(cuda):
         want_logits, want_next = fresh(prompt)
         assert torch.equal(logits.view(torch.int16), want_logits.view(torch.int16))
         assert nxt == want_next
+
+
+class _FakeSession:
+    """Stands in for the device session: a chunk's 'logits' are its last
+    token, and every call is recorded."""
+
+    def __init__(self):
+        self.calls = []
+
+    def prefill_chunk(self, part, begin, want_logits=True, layers=None):
+        self.calls.append((tuple(part), begin, layers, want_logits))
+        return torch.tensor([float(part[-1])])
+
+    def check_status(self):
+        pass
+
+
+def _fake_engine(n_layers=3, chunk=2):
+    from types import SimpleNamespace
+
+    sess = _FakeSession()
+    storage = SimpleNamespace(capacity=64)
+    engine = SimpleNamespace(
+        prefill_chunk_size=chunk, cfg=SimpleNamespace(has_layer_options=False, n_layers=n_layers),
+        model=SimpleNamespace(context_limit=32), _session=lambda state: sess, _guard=lambda state, fn: fn(),
+        prefill_state=lambda capacity, limit=None, storage=None, _kv=storage: {"kv": _kv})
+    return engine, sess
+
+
+def test_cancelled_prefill_keeps_the_last_completed_chunk():
+    """The reference's test_prefix_rollback.py:65-85 on this QATSession: a
+    stop before the second chunk leaves the first chunk's tokens and logits
+    in the prompt cache, which a later prompt reuses."""
+    from rec_b200.engine import QATSession
+    from rec_b200.errors import PrefillCancelled
+
+    engine, sess = _fake_engine()
+    session = QATSession(engine, 1)
+    checks = iter([False, True])
+    with pytest.raises(PrefillCancelled):
+        session.prefill([1, 2, 3, 4], should_stop=lambda: next(checks))
+    assert session.prompt_cache.tokens == [1, 2] and session.prompt_cache.logits.item() == 2
+    restored, common = select_prefix(session.prompt_cache, [1, 2, 5])
+    assert common == 2 and restored is session.prompt_cache
+    assert sess.calls == [((1, 2), 0, None, True)]
+
+
+def test_interrupt_between_layers_polls_before_each_layer():
+    """interrupt_between_layers (quantized.py:129-133, model.py:309-314):
+    each chunk runs as one call per layer, the logits with the last layer; a
+    stop before a later layer of the first chunk cancels with no chunk
+    completed."""
+    from rec_b200.engine import QATSession
+    from rec_b200.errors import PrefillCancelled
+
+    engine, sess = _fake_engine(n_layers=3)
+    logits = QATSession(engine, 1).prefill([1, 2, 3], interrupt_between_layers=True)
+    assert logits.item() == 3
+    assert sess.calls == [((1, 2), 0, (0, 1), False), ((1, 2), 0, (1, 2), False), ((1, 2), 0, (2, 3), True),
+                          ((3,), 2, (0, 1), False), ((3,), 2, (1, 2), False), ((3,), 2, (2, 3), True)]
+    engine, sess = _fake_engine(n_layers=3)
+    polls = []
+    session = QATSession(engine, 1)
+    with pytest.raises(PrefillCancelled):
+        session.prefill([1, 2, 3], should_stop=lambda: polls.append(1) or len(polls) == 3,
+                        interrupt_between_layers=True)
+    assert [c[2] for c in sess.calls] == [(0, 1), (1, 2)] and session.prompt_cache.tokens == []
