@@ -295,6 +295,33 @@ def test_layer_metadata_is_the_reference_table():
     assert tuple(rows[49][i] for i in (13, 14, 33, 34)) == (150144, 2048, 150144, 2048)
 
 
+def test_weight_banks_group_four_layers():
+    """engine.banks: each group of four layers' tensors once, in the layer
+    fields' order (codes, scales, biases per matrix), the last group
+    followed by the embedding, the final norm and lm_head (the reference's
+    thirteen banks for 49 layers, megakernel.py:1011-1108)."""
+    from rec_b200.engine import weight_banks
+    from rec_b200.model import LayerWeights, ModelWeights, QTensor, TINY
+
+    def t():
+        return torch.zeros(2)
+
+    def q():
+        return QTensor(t(), t(), t())
+
+    layers = [LayerWeights(input_norm=t(), post_norm=t(), q=q(), k=q(), v=q(), o=q(), router=t(), gate=q(), up=q(),
+                           down=q(), expert_bias=t(), sinks=None, q_norm=None, k_norm=None) for _ in range(9)]
+    w = ModelWeights(TINY, layers, q(), t(), q())
+    banks = weight_banks(w)
+    per_layer = 2 + 7 * 3 + 2  # norms, seven matrices, router and bias
+    assert [len(b) for b in banks] == [4 * per_layer, 4 * per_layer, per_layer + 7]
+    ids = [id(x) for b in banks for x in b]
+    assert len(ids) == len(set(ids)) == 9 * per_layer + 7
+    assert banks[0][0] is layers[0].input_norm and banks[0][2] is layers[0].q.w and banks[1][0] is layers[4].input_norm
+    tail = (w.embed.w, w.embed.s, w.embed.b, w.final_norm, w.lm_head.w, w.lm_head.s, w.lm_head.b)
+    assert all(a is b for a, b in zip(banks[-1][-7:], tail, strict=True))
+
+
 def test_state_growth_and_limit_on_the_host():
     """prefill_state / ensure_capacity over a given storage, the contract of
     the reference's shared-KV test (engine/tests/test_shared_kv.py:64-80):
