@@ -293,6 +293,12 @@ def test_layer_metadata_is_the_reference_table():
     assert tuple(rows[5][i] for i in (13, 14, 18, 19, 28, 29)) == (4096, 2048, 512, 2048, 2048, 4096)
     assert [r[0] for r in rows[:49]] == [i // 4 for i in range(49)] and rows[49][0] == 12
     assert tuple(rows[49][i] for i in (13, 14, 33, 34)) == (150144, 2048, 150144, 2048)
+    # config 3: every layer global and routed, no shared expert
+    from rec_b200.model import ModelConfig
+
+    c3 = layer_metadata(ModelConfig(name="config3", n_experts=128, top_k=8, moe_inter=768, vocab=151936))
+    assert len(c3) == 49 and all(r[1] == 1 and r[2] == 1 for r in c3[:48])
+    assert all(tuple(r[i] for i in (33, 34, 43, 44, 48)) == (768, 2048, 2048, 768, 0) for r in c3[:48])
 
 
 def test_weight_banks_group_four_layers():
